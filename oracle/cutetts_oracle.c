@@ -34,15 +34,30 @@ void orc_linear(const float* x, int S, int I, const float* W, const float* b, in
                 float* y) {
   long ops = (long)S * I * O;
   int nth = ops >= 1000000 ? g_nth : 1;
+  const int nblk = (O + 7) / 8;
+  /* eight output rows per task, each with its own sequential FMA chain
+   * (the gemv8 panel shape); per-output arithmetic is unchanged. */
 #pragma omp parallel for schedule(static) num_threads(nth)
-  for (int o = 0; o < O; o++) {
-    const float* wr = W + (size_t)o * I;
-    float bo = b ? b[o] : 0.0f;
+  for (int blk = 0; blk < nblk; blk++) {
+    const int o0 = blk * 8, nr = O - o0 < 8 ? O - o0 : 8;
+    const float* wr[8];
+    for (int r = 0; r < 8; r++) wr[r] = W + (size_t)(o0 + (r < nr ? r : 0)) * I;
     for (int s = 0; s < S; s++) {
       const float* xr = x + (size_t)s * I;
-      float acc = bo;
-      for (int i = 0; i < I; i++) acc = fmaf(wr[i], xr[i], acc);
-      y[(size_t)s * O + o] = acc;
+      float acc[8];
+      for (int r = 0; r < 8; r++) acc[r] = (b && r < nr) ? b[o0 + r] : 0.0f;
+      for (int i = 0; i < I; i++) {
+        const float xv = xr[i];
+        acc[0] = fmaf(wr[0][i], xv, acc[0]);
+        acc[1] = fmaf(wr[1][i], xv, acc[1]);
+        acc[2] = fmaf(wr[2][i], xv, acc[2]);
+        acc[3] = fmaf(wr[3][i], xv, acc[3]);
+        acc[4] = fmaf(wr[4][i], xv, acc[4]);
+        acc[5] = fmaf(wr[5][i], xv, acc[5]);
+        acc[6] = fmaf(wr[6][i], xv, acc[6]);
+        acc[7] = fmaf(wr[7][i], xv, acc[7]);
+      }
+      for (int r = 0; r < nr; r++) y[(size_t)s * O + o0 + r] = acc[r];
     }
   }
 }

@@ -1,0 +1,690 @@
+// api_dit.cu -- C ABI: the DiT flow head (dit.rs / diffusion_head.py) and
+// the per-frame engine (bin/cutetts.rs:429-523 loop body) captured as one
+// CUDA graph per frame.
+#include <cstdio>
+
+#include "api_common.h"
+#include "model.h"
+
+using namespace ctts;
+
+namespace {
+
+int dit_ws_ensure(ctts_dit* d, int rows, int steps) {
+  DitWs& w = d->ws;
+  if (w.rows >= rows && w.steps >= steps) return CTTS_OK;
+  rows = std::max(rows, w.rows);
+  steps = std::max(steps, w.steps);
+  cudaDeviceSynchronize();
+  w.arena.~DevArena();
+  new (&w.arena) DevArena();
+  const ctts_dit_config& c = d->cfg;
+  const int H = c.hidden, P = c.patch, S = 1 + 2 * P, L = c.latent;
+  const int qkvw = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim, qd = c.n_heads * c.head_dim;
+  w.seq = w.arena.alloc<float>((size_t)rows * S * H);
+  w.qkv = w.arena.alloc<float>((size_t)rows * S * qkvw);
+  w.att = w.arena.alloc<float>((size_t)rows * S * qd);
+  w.act = w.arena.alloc<float>((size_t)rows * S * c.ffn);
+  w.mu = w.arena.alloc<float>((size_t)rows * H);
+  w.ad = w.arena.alloc<float>((size_t)rows * c.n_layers * 6 * H);
+  w.condh = w.arena.alloc<float>((size_t)rows * P * H);
+  w.temb = w.arena.alloc<float>((size_t)steps * H);
+  w.dtemb = w.arena.alloc<float>(H);
+  w.stemb = w.arena.alloc<float>(H);
+  w.tmp = w.arena.alloc<float>((size_t)(steps + 2) * H);
+  w.se = w.arena.alloc<float>((size_t)(steps + 2) * H);
+  w.tv = w.arena.alloc<float>(TGrid::kMax);
+  w.x = w.arena.alloc<float>((size_t)rows * P * L);
+  w.v = w.arena.alloc<float>((size_t)rows * P * L);
+  w.z = w.arena.alloc<float>((size_t)rows * c.cond_dim);
+  w.cond = w.arena.alloc<float>((size_t)rows * P * L);
+  w.spk = w.arena.alloc<float>((size_t)rows * std::max(c.spk_dim, 1));
+  w.hbuf = w.arena.alloc<float>((size_t)2 * H);
+  if (!w.seq || !w.qkv || !w.att || !w.act || !w.ad || !w.x || !w.spk || !w.hbuf)
+    return set_error(CTTS_ERR_NOMEM, "DiT workspace allocation failed");
+  w.rows = rows;
+  w.steps = steps;
+  return CTTS_OK;
+}
+
+struct DitRun {
+  int R = 0;                 // rows (utterance-branches)
+  const float* z = nullptr;  // [R, cond_dim]
+  const float* cond = nullptr;  // [R, P*L]
+  const float* spk = nullptr;   // [R, spk_dim] or null (plain residual path)
+  int zero_adaln_from = -1;     // rows >= this get zero AdaLN (CFG uncond branch)
+  float* x = nullptr;           // latent being integrated [X, P*L]
+  int x_rows = 0;               // rows of x (R, or R/2 for CFG where both halves read x)
+  int steps = 0;
+  const float* times = nullptr;  // host: t per step
+  const float* dts = nullptr;    // host: dt per step (Euler / CFG modes)
+  int mode = 0;                  // 0 euler, 1 predict (single v -> out), 2 cfg
+  float cfg = 0.0f;
+  float cfg_w = 0.0f;            // cfg_strength embedding input (distill)
+  float step_dt = 0.0f;          // step-size embedding input (distill)
+  float* out = nullptr;          // predict: v [R, P*L]
+};
+
+// Enqueues one DiT sample / predict on stream s.  All pointers device.
+int dit_enqueue(ctts_dit* d, const DitRun& r, cudaStream_t s, int* launches) {
+  const ctts_dit_config& c = d->cfg;
+  DitWs& w = d->ws;
+  const int H = c.hidden, P = c.patch, S = 1 + 2 * P, L = c.latent, PL = P * L;
+  const int qd = c.n_heads * c.head_dim, qkvw = qd + 2 * c.n_kv_heads * c.head_dim;
+  const int F = c.ffn, R = r.R, NL = c.n_layers;
+  const long adld = (long)NL * 6 * H;
+  const int bf = d->bf16;
+  int nl = 0;
+  auto lin = [&](LinearArgs a) -> int {
+    a.w_bf16 = bf;
+    cudaError_t e = launch_linear(a, s);
+    if (e != cudaSuccess) return set_error(CTTS_ERR_CUDA, std::string("linear: ") + cudaGetErrorString(e));
+    nl++;
+    return CTTS_OK;
+  };
+#define RUN(x)                      \
+  do {                              \
+    int _rc = (x);                  \
+    if (_rc != CTTS_OK) return _rc; \
+  } while (0)
+
+  // ---- once per sample (sample_prologue, dit.rs:756-772)
+  TGrid g;
+  g.n = r.steps + 1 + (d->st1_w ? 1 : 0);
+  CTTS_REQ(g.n <= TGrid::kMax, CTTS_ERR_ARG, "too many Euler steps");
+  for (int i = 0; i < r.steps; i++) g.t[i] = r.times[i];
+  g.t[r.steps] = 0.0f;  // delta_time_mlp input (legacy dt = 0)
+  if (d->st1_w) g.t[r.steps + 1] = r.step_dt;
+  CTTS_CK(launch_fill_tv(w.tv, g, s)); nl++;
+  CTTS_CK(launch_sin_emb(w.tv, g.n, H, w.se, s)); nl++;
+  {
+    LinearArgs a; a.x = w.se; a.x_ld = H; a.M = r.steps; a.K = H; a.N = H; a.w = d->t1_w;
+    a.bias = d->t1_b; a.act = 1; a.y = w.tmp; a.y_ld = H; RUN(lin(a));
+    LinearArgs b; b.x = w.tmp; b.x_ld = H; b.M = r.steps; b.K = H; b.N = H; b.w = d->t2_w;
+    b.bias = d->t2_b; b.y = w.temb; b.y_ld = H; RUN(lin(b));
+    LinearArgs c1; c1.x = w.se + (size_t)r.steps * H; c1.x_ld = H; c1.M = 1; c1.K = H; c1.N = H;
+    c1.w = d->dt1_w; c1.bias = d->dt1_b; c1.act = 1; c1.y = w.tmp + (size_t)r.steps * H; c1.y_ld = H;
+    RUN(lin(c1));
+    LinearArgs c2; c2.x = w.tmp + (size_t)r.steps * H; c2.x_ld = H; c2.M = 1; c2.K = H; c2.N = H;
+    c2.w = d->dt2_w; c2.bias = d->dt2_b; c2.y = w.dtemb; c2.y_ld = H; RUN(lin(c2));
+  }
+  // mu = mu_proj(z) (+ cfg_strength) (+ step_size)   diffusion_head.py:601-627
+  if (d->mu_w) {
+    LinearArgs a; a.x = r.z; a.x_ld = c.cond_dim; a.M = R; a.K = c.cond_dim; a.N = H; a.w = d->mu_w;
+    a.bias = d->mu_b; a.y = w.mu; a.y_ld = H; RUN(lin(a));
+  } else {
+    CTTS_CK(cudaMemcpyAsync(w.mu, r.z, sizeof(float) * R * H, cudaMemcpyDeviceToDevice, s));
+  }
+  if (d->cfg2_w) {
+    // silu(cfg0 * cfg_w/5) on the host (a [H,1] x scalar product), then cfg2.
+    LinearArgs a; a.x = w.hbuf; a.x_ld = H; a.M = 1; a.K = H; a.N = H; a.w = d->cfg2_w;
+    a.y = w.hbuf + H; a.y_ld = H; RUN(lin(a));
+    CTTS_CK(launch_add_rows(w.mu, R, H, w.hbuf + H, s)); nl++;
+  }
+  if (d->st1_w) {
+    LinearArgs a; a.x = w.se + (size_t)(r.steps + 1) * H; a.x_ld = H; a.M = 1; a.K = H; a.N = H;
+    a.w = d->st1_w; a.bias = d->st1_b; a.act = 1; a.y = w.tmp + (size_t)(r.steps + 1) * H; a.y_ld = H;
+    RUN(lin(a));
+    LinearArgs b; b.x = w.tmp + (size_t)(r.steps + 1) * H; b.x_ld = H; b.M = 1; b.K = H; b.N = H;
+    b.w = d->st2_w; b.bias = d->st2_b; b.y = w.stemb; b.y_ld = H; RUN(lin(b));
+    CTTS_CK(launch_add_rows(w.mu, R, H, w.stemb, s)); nl++;
+  }
+  const bool use_ad = c.adaln && r.spk;
+  if (use_ad) {
+    int rows = r.zero_adaln_from >= 0 ? r.zero_adaln_from : R;
+    LinearArgs a; a.x = r.spk; a.x_ld = c.spk_dim; a.M = rows; a.K = c.spk_dim; a.N = (int)adld;
+    a.w = d->adaln; a.y = w.ad; a.y_ld = adld; RUN(lin(a));
+    if (rows < R) CTTS_CK(cudaMemsetAsync(w.ad + (size_t)rows * adld, 0, sizeof(float) * (R - rows) * adld, s));
+  }
+  {  // cond_proj(cond) rows [R*P, L]
+    LinearArgs a; a.x = r.cond; a.x_ld = L; a.M = R * P; a.K = L; a.N = H; a.w = d->cond_w;
+    a.bias = d->cond_b; a.y = w.condh; a.y_ld = H; RUN(lin(a));
+  }
+
+  // ---- Euler steps (predict_cached, dit.rs:775-814)
+  const int xrows = r.x_rows;
+  for (int st = 0; st < r.steps; st++) {
+    {  // in_proj(x) -> seq rows 1+P.. ; rows of x repeat for CFG's second half
+      LinearArgs a; a.x = r.x; a.x_ld = L; a.x_div = xrows * P; a.x_ld_outer = 0;
+      a.M = R * P; a.K = L; a.N = H; a.w = d->in_w; a.bias = d->in_b;
+      a.y = w.seq + (size_t)(1 + P) * H; a.y_ld = H; a.y_div = P; a.y_ld_outer = (long)S * H;
+      RUN(lin(a));
+    }
+    CTTS_CK(launch_dit_seq_fill(w.seq, w.mu, w.temb + (size_t)st * H, w.dtemb, w.condh, R, P, H, s)); nl++;
+    for (int l = 0; l < NL; l++) {
+      const DitLayer& Ly = d->layers[l];
+      const float* ad = use_ad ? w.ad + (size_t)l * 6 * H : nullptr;
+      LinearArgs q; q.x = w.seq; q.x_ld = H; q.M = R * S; q.K = H; q.N = qkvw; q.w = Ly.wqkv;
+      q.y = w.qkv; q.y_ld = qkvw; q.norm_w = Ly.norm1; q.eps = c.rms_eps;
+      if (ad) { q.mod = ad; q.mod_ld = adld; q.mod_div = S; q.mod_shift = 0; q.mod_scale = H; }
+      RUN(lin(q));
+      CTTS_CK(launch_dit_attn(w.qkv, R, S, c.n_heads, c.n_kv_heads, c.head_dim, d->inv_freq, w.att, s)); nl++;
+      LinearArgs o; o.x = w.att; o.x_ld = qd; o.M = R * S; o.K = qd; o.N = H; o.w = Ly.wo;
+      o.y = w.seq; o.y_ld = H; o.res = w.seq;
+      if (ad) { o.gate = ad; o.gate_ld = adld; o.gate_div = S; o.gate_off = 2 * H; }
+      RUN(lin(o));
+      LinearArgs gu; gu.x = w.seq; gu.x_ld = H; gu.M = R * S; gu.K = H; gu.N = F; gu.w = Ly.wgu;
+      gu.y = w.act; gu.y_ld = F; gu.act = 2; gu.norm_w = Ly.norm2; gu.eps = c.rms_eps;
+      if (ad) { gu.mod = ad; gu.mod_ld = adld; gu.mod_div = S; gu.mod_shift = 3 * H; gu.mod_scale = 4 * H; }
+      RUN(lin(gu));
+      LinearArgs dn; dn.x = w.act; dn.x_ld = F; dn.M = R * S; dn.K = F; dn.N = H; dn.w = Ly.wd;
+      dn.y = w.seq; dn.y_ld = H; dn.res = w.seq;
+      if (ad) { dn.gate = ad; dn.gate_ld = adld; dn.gate_div = S; dn.gate_off = 5 * H; }
+      RUN(lin(dn));
+    }
+    // final norm + out_proj on the x rows (+ Euler update)
+    LinearArgs f; f.x = w.seq + (size_t)(1 + P) * H; f.x_ld = H; f.x_div = P; f.x_ld_outer = (long)S * H;
+    f.M = R * P; f.K = H; f.N = L; f.w = d->out_w; f.bias = d->out_b; f.norm_w = d->final_norm;
+    f.eps = c.rms_eps;
+    const float dt = r.mode == 1 ? 0.0f : r.dts[st];
+    if (r.mode == 0) {
+      f.y = r.x; f.y_ld = L; f.res = r.x; f.scale = dt;
+      RUN(lin(f));
+    } else if (r.mode == 1) {
+      f.y = r.out; f.y_ld = L;
+      RUN(lin(f));
+    } else {
+      f.y = w.v; f.y_ld = L;
+      RUN(lin(f));
+      CTTS_CK(launch_cfg_euler(r.x, w.v, xrows * PL, r.cfg, dt, s)); nl++;
+    }
+  }
+#undef RUN
+  if (launches) *launches += nl;
+  return CTTS_OK;
+}
+
+int dit_check(ctts_dit* d) {
+  CTTS_REQ(d, CTTS_ERR_ARG, "null handle");
+  if (d->slots.missing())
+    return set_error(CTTS_ERR_STATE, "DiT weights missing: " + d->slots.first_missing());
+  return CTTS_OK;
+}
+
+// host-side cfg-strength hidden: silu(cfg0[:,0] * cfg_w / 5) (dit.rs:657-662)
+int dit_upload_cfg_hidden(ctts_dit* d, float cfg_w, cudaStream_t s) {
+  if (!d->cfg2_w) return CTTS_OK;
+  const int H = d->cfg.hidden;
+  std::vector<float> w0(H), h(H);
+  CTTS_CK(cudaMemcpy(w0.data(), d->cfg0_w, H * 4, cudaMemcpyDeviceToHost));
+  const float wn = cfg_w / 5.0f;
+  for (int i = 0; i < H; i++) {
+    float v = fmaf(w0[i], wn, 0.0f);
+    h[i] = v / (1.0f + expf(-v));
+  }
+  CTTS_CK(cudaMemcpyAsync(d->ws.hbuf, h.data(), H * 4, cudaMemcpyHostToDevice, s));
+  CTTS_CK(cudaStreamSynchronize(s));
+  return CTTS_OK;
+}
+
+}  // namespace
+
+// ----------------------------------------------------------------- create
+
+extern "C" int ctts_dit_create(const ctts_dit_config* cfg, int device, ctts_dit** out) {
+  CTTS_REQ(cfg && out, CTTS_ERR_ARG, "null argument");
+  const ctts_dit_config& c = *cfg;
+  CTTS_REQ(c.latent > 0 && c.hidden > 0 && c.n_heads > 0 && c.n_kv_heads > 0 && c.head_dim > 0 &&
+               c.ffn > 0 && c.n_layers > 0 && c.patch > 0 && c.cond_dim > 0,
+           CTTS_ERR_ARG, "non-positive dimension");
+  CTTS_REQ(1 + 2 * c.patch <= 5, CTTS_ERR_ARG, "patch must be 1 or 2");
+  CTTS_REQ(c.n_heads % c.n_kv_heads == 0, CTTS_ERR_ARG, "n_heads % n_kv_heads != 0");
+  CTTS_REQ(c.head_dim % 64 == 0 && c.head_dim <= 128, CTTS_ERR_ARG, "head_dim must be 64 or 128");
+  CTTS_REQ(c.hidden % 8 == 0 && c.ffn % 8 == 0 && c.latent % 8 == 0 && c.cond_dim % 8 == 0 &&
+               (!c.adaln || c.spk_dim % 8 == 0),
+           CTTS_ERR_ARG, "dimensions must be multiples of 8");
+  CTTS_REQ(c.weight_dtype == CTTS_F32 || c.weight_dtype == CTTS_BF16, CTTS_ERR_ARG, "bad weight dtype");
+  CTTS_CK(cudaSetDevice(device));
+  auto* d = new ctts_dit();
+  d->cfg = c;
+  d->device = device;
+  d->bf16 = c.weight_dtype == CTTS_BF16;
+  d->slots.model_bf16 = d->bf16;
+  cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
+  const int H = c.hidden, L = c.latent, F = c.ffn, hd = c.head_dim;
+  const int qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
+  const size_t es = d->bf16 ? 2 : 4;
+  DevArena& A = d->arena;
+  auto W = [&](size_t n) -> void* { return A.alloc<uint8_t>(n * es); };
+  auto lin = [&](const std::string& name, void** w, float** b, int o, int i, bool bias, bool opt) {
+    *w = W((size_t)o * i);
+    d->slots.add(name + ".weight", *w, {o, i}, true, opt);
+    if (bias) {
+      *b = A.alloc<float>(o);
+      d->slots.add(name + ".bias", *b, {o}, false, opt);
+    }
+  };
+  lin("in_proj", &d->in_w, &d->in_b, H, L, true, false);
+  lin("cond_proj", &d->cond_w, &d->cond_b, H, L, true, false);
+  if (c.cond_dim != H) lin("mu_proj", &d->mu_w, &d->mu_b, H, c.cond_dim, true, false);
+  lin("out_proj", &d->out_w, &d->out_b, L, H, true, false);
+  lin("time_mlp.linear_1", &d->t1_w, &d->t1_b, H, H, true, false);
+  lin("time_mlp.linear_2", &d->t2_w, &d->t2_b, H, H, true, false);
+  lin("delta_time_mlp.linear_1", &d->dt1_w, &d->dt1_b, H, H, true, false);
+  lin("delta_time_mlp.linear_2", &d->dt2_w, &d->dt2_b, H, H, true, false);
+  if (c.step_emb) {
+    lin("step_size_embedding.linear_1", &d->st1_w, &d->st1_b, H, H, true, false);
+    lin("step_size_embedding.linear_2", &d->st2_w, &d->st2_b, H, H, true, false);
+  }
+  if (c.cfg_emb) {
+    d->cfg0_w = A.alloc<float>(H);
+    d->slots.add("cfg_strength_embedding.0.weight", d->cfg0_w, {H, 1}, false);
+    d->cfg2_w = W((size_t)H * H);
+    d->slots.add("cfg_strength_embedding.2.weight", d->cfg2_w, {H, H}, true);
+  }
+  if (c.adaln) d->adaln = W((size_t)c.n_layers * 6 * H * c.spk_dim);
+  d->layers.resize(c.n_layers);
+  for (int i = 0; i < c.n_layers; i++) {
+    DitLayer& Ly = d->layers[i];
+    std::string p = "decoder.layers." + std::to_string(i) + ".";
+    Ly.norm1 = A.alloc<float>(H);
+    Ly.norm2 = A.alloc<float>(H);
+    Ly.wqkv = W((size_t)(qd + 2 * kvd) * H);
+    Ly.wo = W((size_t)H * qd);
+    Ly.wgu = W((size_t)2 * F * H);
+    Ly.wd = W((size_t)H * F);
+    char* qkv = reinterpret_cast<char*>(Ly.wqkv);
+    char* gu = reinterpret_cast<char*>(Ly.wgu);
+    d->slots.add(p + "input_layernorm.weight", Ly.norm1, {H}, false);
+    d->slots.add(p + "post_attention_layernorm.weight", Ly.norm2, {H}, false);
+    d->slots.add(p + "self_attn.q_proj.weight", qkv, {qd, H}, true);
+    d->slots.add(p + "self_attn.k_proj.weight", qkv + (size_t)qd * H * es, {kvd, H}, true);
+    d->slots.add(p + "self_attn.v_proj.weight", qkv + (size_t)(qd + kvd) * H * es, {kvd, H}, true);
+    d->slots.add(p + "self_attn.o_proj.weight", Ly.wo, {H, qd}, true);
+    d->slots.add(p + "mlp.gate_proj.weight", gu, {F, H}, true);
+    d->slots.add(p + "mlp.up_proj.weight", gu + (size_t)F * H * es, {F, H}, true);
+    d->slots.add(p + "mlp.down_proj.weight", Ly.wd, {H, F}, true);
+    if (c.adaln)
+      d->slots.add(p + "speaker_adaln.weight",
+                   reinterpret_cast<char*>(d->adaln) + (size_t)i * 6 * H * c.spk_dim * es,
+                   {6 * H, c.spk_dim}, true);
+  }
+  d->final_norm = A.alloc<float>(H);
+  d->slots.add("decoder.norm.weight", d->final_norm, {H}, false);
+  std::vector<float> inv = rope_inv_freq(hd, c.rope_theta);
+  d->inv_freq = A.alloc<float>(hd / 2);
+  if (!d->final_norm || !d->inv_freq ||
+      cudaMemcpy(d->inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+    delete d;
+    return set_error(CTTS_ERR_NOMEM, "device allocation failed");
+  }
+  *out = d;
+  return CTTS_OK;
+}
+
+extern "C" int ctts_dit_set_tensor(ctts_dit* d, const char* name, const void* host, int dtype,
+                                   const int64_t* shape, int ndim) {
+  CTTS_REQ(d, CTTS_ERR_ARG, "null handle");
+  CTTS_CK(cudaSetDevice(d->device));
+  return slot_set(d->slots, name, host, dtype, shape, ndim);
+}
+
+extern "C" int ctts_dit_load(ctts_dit* d, const char* path, const char* prefix) {
+  CTTS_REQ(d, CTTS_ERR_ARG, "null handle");
+  return load_safetensors(path, prefix, [&](const char* n, const void* p, int dt, const int64_t* s, int nd) {
+    return ctts_dit_set_tensor(d, n, p, dt, s, nd);
+  });
+}
+
+extern "C" int ctts_dit_missing(const ctts_dit* d) { return d ? d->slots.missing() : -1; }
+
+extern "C" void ctts_dit_free(ctts_dit* d) {
+  if (!d) return;
+  cudaSetDevice(d->device);
+  cudaStreamSynchronize(d->stream);
+  cudaStreamDestroy(d->stream);
+  delete d;
+}
+
+extern "C" int ctts_sway_timesteps(int steps, float coeff, float* out) {
+  CTTS_REQ(steps > 0 && out, CTTS_ERR_ARG, "bad argument");
+  const float ub = 2.0f / (3.14159265358979f - 2.0f);
+  CTTS_REQ(coeff >= -1.0f && coeff <= ub, CTTS_ERR_ARG, "sway coefficient outside [-1, 2/(pi-2)]");
+  for (int s = 0; s <= steps; s++) {
+    float u = (float)s / (float)steps;
+    out[s] = u + coeff * (cosf(0.5f * 3.14159265358979f * u) - 1.0f + u);
+  }
+  return CTTS_OK;
+}
+
+// ------------------------------------------------------------- sampling
+
+namespace {
+
+int copy_in(float* dst, const float* src, size_t n) {
+  CTTS_CK(cudaMemcpy(dst, src, n * 4, cudaMemcpyHostToDevice));
+  return CTTS_OK;
+}
+
+}  // namespace
+
+extern "C" int ctts_dit_euler_sample_dev(ctts_dit* d, int batch, const float* x0_dev, const float* z_dev,
+                                         const float* cond_dev, const float* spk_dev, int steps,
+                                         float cfg_w, float* x_out_dev, void* stream) {
+  int rc = dit_check(d);
+  if (rc) return rc;
+  CTTS_REQ(batch > 0 && steps > 0 && x0_dev && z_dev && cond_dev && x_out_dev, CTTS_ERR_ARG, "bad argument");
+  CTTS_CK(cudaSetDevice(d->device));
+  rc = dit_ws_ensure(d, batch, steps);
+  if (rc) return rc;
+  cudaStream_t s = as_stream(stream, d->stream);
+  rc = dit_upload_cfg_hidden(d, cfg_w, s);
+  if (rc) return rc;
+  const int PL = d->cfg.patch * d->cfg.latent;
+  if (x_out_dev != x0_dev)
+    CTTS_CK(cudaMemcpyAsync(x_out_dev, x0_dev, sizeof(float) * batch * PL, cudaMemcpyDeviceToDevice, s));
+  // euler_sample (dit.rs:819-842): t_s = s*dt, x += v*dt, dt = 1/steps
+  std::vector<float> times(steps), dts(steps);
+  const float dt = 1.0f / (float)steps;
+  for (int i = 0; i < steps; i++) {
+    times[i] = (float)i * dt;
+    dts[i] = dt;
+  }
+  DitRun r;
+  r.R = batch; r.z = z_dev; r.cond = cond_dev; r.spk = spk_dev; r.x = x_out_dev; r.x_rows = batch;
+  r.steps = steps; r.times = times.data(); r.dts = dts.data(); r.mode = 0; r.cfg_w = cfg_w;
+  r.step_dt = dt;
+  return dit_enqueue(d, r, s, nullptr);
+}
+
+extern "C" int ctts_dit_euler_sample(ctts_dit* d, int batch, const float* x0, const float* z,
+                                     const float* cond, const float* spk, int steps, float cfg_w,
+                                     float* x_out) {
+  int rc = dit_check(d);
+  if (rc) return rc;
+  CTTS_REQ(batch > 0 && steps > 0 && x0 && z && cond && x_out, CTTS_ERR_ARG, "bad argument");
+  CTTS_CK(cudaSetDevice(d->device));
+  rc = dit_ws_ensure(d, batch, steps);
+  if (rc) return rc;
+  DitWs& w = d->ws;
+  const int PL = d->cfg.patch * d->cfg.latent;
+  if ((rc = copy_in(w.x, x0, (size_t)batch * PL))) return rc;
+  if ((rc = copy_in(w.z, z, (size_t)batch * d->cfg.cond_dim))) return rc;
+  if ((rc = copy_in(w.cond, cond, (size_t)batch * PL))) return rc;
+  if (spk && (rc = copy_in(w.spk, spk, (size_t)batch * d->cfg.spk_dim))) return rc;
+  rc = ctts_dit_euler_sample_dev(d, batch, w.x, w.z, w.cond, spk ? w.spk : nullptr, steps, cfg_w, w.x,
+                                 d->stream);
+  if (rc) return rc;
+  CTTS_CK(cudaStreamSynchronize(d->stream));
+  CTTS_CK(cudaMemcpy(x_out, w.x, sizeof(float) * batch * PL, cudaMemcpyDeviceToHost));
+  return CTTS_OK;
+}
+
+extern "C" int ctts_dit_predict(ctts_dit* d, int batch, const float* x, float t, const float* z,
+                                const float* cond, float dt, const float* spk, float cfg_w, float* v) {
+  int rc = dit_check(d);
+  if (rc) return rc;
+  CTTS_REQ(batch > 0 && x && z && cond && v, CTTS_ERR_ARG, "bad argument");
+  CTTS_CK(cudaSetDevice(d->device));
+  rc = dit_ws_ensure(d, batch, 1);
+  if (rc) return rc;
+  DitWs& w = d->ws;
+  const int PL = d->cfg.patch * d->cfg.latent;
+  if ((rc = copy_in(w.x, x, (size_t)batch * PL))) return rc;
+  if ((rc = copy_in(w.z, z, (size_t)batch * d->cfg.cond_dim))) return rc;
+  if ((rc = copy_in(w.cond, cond, (size_t)batch * PL))) return rc;
+  if (spk && (rc = copy_in(w.spk, spk, (size_t)batch * d->cfg.spk_dim))) return rc;
+  rc = dit_upload_cfg_hidden(d, cfg_w, d->stream);
+  if (rc) return rc;
+  float times[1] = {t};
+  DitRun r;
+  r.R = batch; r.z = w.z; r.cond = w.cond; r.spk = spk ? w.spk : nullptr; r.x = w.x; r.x_rows = batch;
+  r.steps = 1; r.times = times; r.mode = 1; r.out = w.v; r.cfg_w = cfg_w; r.step_dt = dt;
+  rc = dit_enqueue(d, r, d->stream, nullptr);
+  if (rc) return rc;
+  CTTS_CK(cudaStreamSynchronize(d->stream));
+  CTTS_CK(cudaMemcpy(v, w.v, sizeof(float) * batch * PL, cudaMemcpyDeviceToHost));
+  return CTTS_OK;
+}
+
+extern "C" int ctts_dit_euler_sample_cfg(ctts_dit* d, int batch, const float* x0, const float* z_c,
+                                         const float* z_u, const float* cond, const float* uncond,
+                                         const float* spk, int steps, float coeff, float cfg,
+                                         float* x_out) {
+  int rc = dit_check(d);
+  if (rc) return rc;
+  CTTS_REQ(batch > 0 && steps > 0 && x0 && z_c && z_u && cond && uncond && x_out, CTTS_ERR_ARG,
+           "bad argument");
+  CTTS_CK(cudaSetDevice(d->device));
+  rc = dit_ws_ensure(d, 2 * batch, steps);
+  if (rc) return rc;
+  DitWs& w = d->ws;
+  const int PL = d->cfg.patch * d->cfg.latent, CD = d->cfg.cond_dim;
+  if ((rc = copy_in(w.x, x0, (size_t)batch * PL))) return rc;
+  if ((rc = copy_in(w.z, z_c, (size_t)batch * CD))) return rc;
+  if ((rc = copy_in(w.z + (size_t)batch * CD, z_u, (size_t)batch * CD))) return rc;
+  if ((rc = copy_in(w.cond, cond, (size_t)batch * PL))) return rc;
+  if ((rc = copy_in(w.cond + (size_t)batch * PL, uncond, (size_t)batch * PL))) return rc;
+  if (spk) {
+    if ((rc = copy_in(w.spk, spk, (size_t)batch * d->cfg.spk_dim))) return rc;
+  }
+  rc = dit_upload_cfg_hidden(d, cfg, d->stream);
+  if (rc) return rc;
+  std::vector<float> times(steps + 1), dts(steps);
+  rc = ctts_sway_timesteps(steps, coeff, times.data());
+  if (rc) return rc;
+  for (int i = 0; i < steps; i++) dts[i] = times[i + 1] - times[i];
+  DitRun r;
+  r.R = 2 * batch; r.z = w.z; r.cond = w.cond; r.spk = spk ? w.spk : nullptr;
+  r.zero_adaln_from = spk ? batch : -1;
+  r.x = w.x; r.x_rows = batch; r.steps = steps; r.times = times.data(); r.dts = dts.data();
+  r.mode = 2; r.cfg = cfg;
+  r.cfg_w = cfg; r.step_dt = 1.0f / (float)steps;
+  rc = dit_enqueue(d, r, d->stream, nullptr);
+  if (rc) return rc;
+  CTTS_CK(cudaStreamSynchronize(d->stream));
+  CTTS_CK(cudaMemcpy(x_out, w.x, sizeof(float) * batch * PL, cudaMemcpyDeviceToHost));
+  return CTTS_OK;
+}
+
+// ------------------------------------------------------------------ engine
+
+namespace {
+
+int engine_enqueue(ctts_engine* e, cudaStream_t s, int* launches) {
+  ctts_lm* lm = e->lm;
+  ctts_dit* d = e->dit;
+  const int B = e->cfg.batch, H = lm->cfg.hidden;
+  const int PL = d->cfg.patch * d->cfg.latent;
+  int nl = 0;
+  CTTS_CK(cudaMemcpyAsync(e->x, e->noise, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
+  {  // stop logits (e2e.rs:83-92)
+    LinearArgs a; a.x = e->z; a.x_ld = H; a.M = B; a.K = H; a.N = 2; a.w = e->stop_w;
+    a.bias = e->stop_b; a.y = e->stop; a.y_ld = 2;
+    CTTS_CK(launch_linear(a, s)); nl++;
+  }
+  const int steps = e->cfg.euler_steps;
+  std::vector<float> times(steps), dts(steps);
+  const float dt = 1.0f / (float)steps;
+  for (int i = 0; i < steps; i++) {
+    times[i] = (float)i * dt;
+    dts[i] = dt;
+  }
+  DitRun r;
+  r.R = B; r.z = e->z; r.cond = e->cond; r.spk = d->cfg.adaln ? e->z : nullptr;
+  r.x = e->x; r.x_rows = B; r.steps = steps; r.times = times.data(); r.dts = dts.data(); r.mode = 0;
+  r.step_dt = dt;
+  int rc = dit_enqueue(d, r, s, &nl);
+  if (rc) return rc;
+  CTTS_CK(launch_affine(e->x, B * PL, e->cfg.latent_scale, e->cfg.latent_bias, e->lat, s)); nl++;
+  CTTS_CK(cudaMemcpyAsync(e->cond, e->x, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
+  {  // feedback projection straight into the LM residual stream
+    LinearArgs a; a.x = e->x; a.x_ld = PL; a.M = B; a.K = PL; a.N = H; a.w = e->proj_w;
+    a.bias = e->proj_b; a.y = e->kv->h; a.y_ld = H;
+    CTTS_CK(launch_linear(a, s)); nl++;
+  }
+  rc = lm_forward_rows(lm, e->kv, B, -1, 0, e->z, s, &nl);
+  if (rc) return rc;
+  if (launches) *launches = nl;
+  return CTTS_OK;
+}
+
+}  // namespace
+
+extern "C" int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_config* cfg,
+                                  ctts_engine** out) {
+  CTTS_REQ(lm && dit && cfg && out, CTTS_ERR_ARG, "null argument");
+  CTTS_REQ(lm->device == dit->device, CTTS_ERR_ARG, "LM and DiT on different devices");
+  CTTS_REQ(dit->cfg.cond_dim == lm->cfg.hidden, CTTS_ERR_ARG, "DiT cond_dim must equal LM hidden");
+  CTTS_REQ(!dit->cfg.adaln || dit->cfg.spk_dim == lm->cfg.hidden, CTTS_ERR_ARG,
+           "AdaLN conditioning width must equal LM hidden");
+  CTTS_REQ(cfg->batch > 0 && cfg->capacity > 0 && cfg->euler_steps > 0, CTTS_ERR_ARG, "bad config");
+  CTTS_REQ(cfg->latent_scale != 0.0f, CTTS_ERR_ARG, "latent_scale must be non-zero");
+  int rc = lm_check_ready(lm);
+  if (rc) return rc;
+  rc = dit_check(dit);
+  if (rc) return rc;
+  CTTS_REQ(!dit->cfg.cfg_emb, CTTS_ERR_ARG, "engine runs the single-branch head (no cfg embedding)");
+  CTTS_CK(cudaSetDevice(lm->device));
+  auto* e = new ctts_engine();
+  e->lm = lm;
+  e->dit = dit;
+  e->cfg = *cfg;
+  rc = ctts_kv_alloc(lm, cfg->batch, cfg->capacity, &e->kv);
+  if (rc) {
+    delete e;
+    return rc;
+  }
+  rc = dit_ws_ensure(dit, cfg->batch, cfg->euler_steps);
+  if (rc) {
+    ctts_kv_free(e->kv);
+    delete e;
+    return rc;
+  }
+  cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+  const int B = cfg->batch, H = lm->cfg.hidden, PL = dit->cfg.patch * dit->cfg.latent;
+  DevArena& A = e->arena;
+  e->stop_w = A.alloc<float>(2 * H);
+  e->stop_b = A.alloc<float>(2);
+  e->proj_w = A.alloc<float>((size_t)H * PL);
+  e->proj_b = A.alloc<float>(H);
+  e->z = A.alloc<float>((size_t)B * H);
+  e->x = A.alloc<float>((size_t)B * PL);
+  e->cond = A.alloc<float>((size_t)B * PL);
+  e->lat = A.alloc<float>((size_t)B * PL);
+  e->stop = A.alloc<float>((size_t)B * 2);
+  e->noise = A.alloc<float>((size_t)B * PL);
+  if (cudaMallocHost(&e->h_noise, sizeof(float) * B * PL) != cudaSuccess ||
+      cudaMallocHost(&e->h_lat, sizeof(float) * B * PL) != cudaSuccess ||
+      cudaMallocHost(&e->h_stop, sizeof(float) * B * 2) != cudaSuccess || !e->noise) {
+    ctts_engine_free(e);
+    return set_error(CTTS_ERR_NOMEM, "engine buffers");
+  }
+  e->prefilled.assign(B, false);
+  *out = e;
+  return CTTS_OK;
+}
+
+extern "C" int ctts_engine_set_heads(ctts_engine* e, const float* stop_w, const float* stop_b,
+                                     const float* proj_w, const float* proj_b) {
+  CTTS_REQ(e && stop_w && stop_b && proj_w && proj_b, CTTS_ERR_ARG, "null argument");
+  CTTS_CK(cudaSetDevice(e->lm->device));
+  const int H = e->lm->cfg.hidden, PL = e->dit->cfg.patch * e->dit->cfg.latent;
+  CTTS_CK(cudaMemcpy(e->stop_w, stop_w, sizeof(float) * 2 * H, cudaMemcpyHostToDevice));
+  CTTS_CK(cudaMemcpy(e->stop_b, stop_b, sizeof(float) * 2, cudaMemcpyHostToDevice));
+  CTTS_CK(cudaMemcpy(e->proj_w, proj_w, sizeof(float) * H * PL, cudaMemcpyHostToDevice));
+  CTTS_CK(cudaMemcpy(e->proj_b, proj_b, sizeof(float) * H, cudaMemcpyHostToDevice));
+  e->heads_set = true;
+  return CTTS_OK;
+}
+
+extern "C" int ctts_engine_prefill(ctts_engine* e, int b, const float* x, int T, const float* cond0) {
+  CTTS_REQ(e && x && cond0, CTTS_ERR_ARG, "null argument");
+  CTTS_REQ(b >= 0 && b < e->cfg.batch && T > 0, CTTS_ERR_ARG, "bad utterance index or length");
+  CTTS_REQ(e->steps_done == 0, CTTS_ERR_STATE, "prefill after the first frame step");
+  CTTS_CK(cudaSetDevice(e->lm->device));
+  ctts_kv* kv = e->kv;
+  const int H = e->lm->cfg.hidden, PL = e->dit->cfg.patch * e->dit->cfg.latent;
+  CTTS_REQ(T <= kv->ws_rows, CTTS_ERR_RANGE, "prefill length outside workspace");
+  CTTS_CK(cudaMemcpy(kv->xin, x, sizeof(float) * T * H, cudaMemcpyHostToDevice));
+  int rc = ctts_lm_prefill_dev(e->lm, kv, b, kv->xin, T, kv->xout, e->stream);
+  if (rc) return rc;
+  CTTS_CK(cudaMemcpyAsync(e->z + (size_t)b * H, kv->xout + (size_t)(T - 1) * H, sizeof(float) * H,
+                          cudaMemcpyDeviceToDevice, e->stream));
+  CTTS_CK(cudaMemcpyAsync(e->cond + (size_t)b * PL, cond0, sizeof(float) * PL, cudaMemcpyHostToDevice,
+                          e->stream));
+  CTTS_CK(cudaStreamSynchronize(e->stream));
+  e->prefilled[b] = true;
+  return CTTS_OK;
+}
+
+extern "C" int ctts_engine_step_dev(ctts_engine* e, const float* noise_dev, float* latents_dev,
+                                    float* stop_dev, void* stream) {
+  CTTS_REQ(e && noise_dev, CTTS_ERR_ARG, "null argument");
+  CTTS_REQ(e->heads_set, CTTS_ERR_STATE, "engine heads not set");
+  for (int b = 0; b < e->cfg.batch; b++) {
+    CTTS_REQ(e->prefilled[b], CTTS_ERR_STATE, "utterance " + std::to_string(b) + " not prefilled");
+    CTTS_REQ(e->kv->pos_host[b] < e->kv->cap, CTTS_ERR_RANGE, "KV cache full");
+  }
+  CTTS_CK(cudaSetDevice(e->lm->device));
+  cudaStream_t s = as_stream(stream, e->stream);
+  const int B = e->cfg.batch, PL = e->dit->cfg.patch * e->dit->cfg.latent;
+  if (noise_dev != e->noise)
+    CTTS_CK(cudaMemcpyAsync(e->noise, noise_dev, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
+  if (!e->cfg.use_graph || e->steps_done == 0) {
+    // first frame runs eagerly (sets kernel attributes outside any capture)
+    int rc = engine_enqueue(e, s, &e->launches);
+    if (rc) return rc;
+  } else {
+    if (!e->exec) {
+      CTTS_CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+      int n = 0;
+      int rc = engine_enqueue(e, s, &n);
+      cudaGraph_t g = nullptr;
+      cudaError_t ce = cudaStreamEndCapture(s, &g);
+      if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+      }
+      CTTS_CK(ce);
+      e->graph = g;
+      CTTS_CK(cudaGraphInstantiate(&e->exec, g, 0));
+    }
+    CTTS_CK(cudaGraphLaunch(e->exec, s));
+  }
+  for (int b = 0; b < B; b++) e->kv->pos_host[b]++;
+  e->steps_done++;
+  if (latents_dev && latents_dev != e->lat)
+    CTTS_CK(cudaMemcpyAsync(latents_dev, e->lat, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
+  if (stop_dev && stop_dev != e->stop)
+    CTTS_CK(cudaMemcpyAsync(stop_dev, e->stop, sizeof(float) * B * 2, cudaMemcpyDeviceToDevice, s));
+  return CTTS_OK;
+}
+
+extern "C" int ctts_engine_step(ctts_engine* e, const float* noise, float* latents_out, float* stop_out) {
+  CTTS_REQ(e && noise && latents_out, CTTS_ERR_ARG, "null argument");
+  CTTS_CK(cudaSetDevice(e->lm->device));
+  const int B = e->cfg.batch, PL = e->dit->cfg.patch * e->dit->cfg.latent;
+  memcpy(e->h_noise, noise, sizeof(float) * B * PL);
+  CTTS_CK(cudaMemcpyAsync(e->noise, e->h_noise, sizeof(float) * B * PL, cudaMemcpyHostToDevice, e->stream));
+  int rc = ctts_engine_step_dev(e, e->noise, e->lat, e->stop, e->stream);
+  if (rc) return rc;
+  CTTS_CK(cudaMemcpyAsync(e->h_lat, e->lat, sizeof(float) * B * PL, cudaMemcpyDeviceToHost, e->stream));
+  if (stop_out)
+    CTTS_CK(cudaMemcpyAsync(e->h_stop, e->stop, sizeof(float) * B * 2, cudaMemcpyDeviceToHost, e->stream));
+  CTTS_CK(cudaStreamSynchronize(e->stream));
+  int err = 0;
+  CTTS_CK(cudaMemcpy(&err, e->kv->err, sizeof(int), cudaMemcpyDeviceToHost));
+  CTTS_REQ(err == 0, CTTS_ERR_RANGE, "device reported a KV position outside capacity");
+  memcpy(latents_out, e->h_lat, sizeof(float) * B * PL);
+  if (stop_out) memcpy(stop_out, e->h_stop, sizeof(float) * B * 2);
+  return CTTS_OK;
+}
+
+extern "C" int ctts_engine_launches_per_step(const ctts_engine* e) { return e ? e->launches : -1; }
+
+extern "C" void* ctts_engine_stream(const ctts_engine* e) { return e ? (void*)e->stream : nullptr; }
+
+extern "C" void ctts_engine_free(ctts_engine* e) {
+  if (!e) return;
+  cudaSetDevice(e->lm->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  if (e->exec) cudaGraphExecDestroy(e->exec);
+  if (e->graph) cudaGraphDestroy(e->graph);
+  if (e->h_noise) cudaFreeHost(e->h_noise);
+  if (e->h_lat) cudaFreeHost(e->h_lat);
+  if (e->h_stop) cudaFreeHost(e->h_stop);
+  if (e->kv) ctts_kv_free(e->kv);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+}

@@ -1,0 +1,229 @@
+// linear.cu -- skinny linear layers on CUDA cores (the decode GEMV path).
+//
+// Replaces the reference's packed-panel GEMV / small-T SGEMM
+// (rust-codec/src/qwen.rs:177-221 linear_gemv, simd.rs:333-387 gemv8,
+// gemm.rs:149-221 sgemm_small_t, dit.rs:184-206 linear_rows).  At decode the
+// contraction has 1..8 activation rows per weight row, so it is bound by
+// streaming W from HBM (or L2): each warp owns RPW weight rows and reads
+// them with 16-byte non-allocating loads, the activation tile (up to 8 rows,
+// RMSNorm / AdaLN-modulate prologue already applied) sits in shared memory
+// and is broadcast to every lane, partial sums are reduced with warp
+// shuffles.  The epilogue fuses bias, SiLU / SwiGLU, residual add, AdaLN
+// gated residual and the Euler update (y += dt * v).
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ctts {
+
+namespace {
+
+constexpr int kWarps = 4;
+
+template <bool BF16>
+struct WVec;
+template <>
+struct WVec<false> {
+  static constexpr int N = 4;
+  static CTTS_DEV void load(const void* base, size_t off, float* v) {
+    float4 t = ld_stream_f4(reinterpret_cast<const float*>(base) + off);
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+  }
+};
+template <>
+struct WVec<true> {
+  static constexpr int N = 8;
+  static CTTS_DEV void load(const void* base, size_t off, float* v) {
+    uint4 t = ld_stream_u4(reinterpret_cast<const uint16_t*>(base) + off);
+    v[0] = bf_lo(t.x); v[1] = bf_hi(t.x); v[2] = bf_lo(t.y); v[3] = bf_hi(t.y);
+    v[4] = bf_lo(t.z); v[5] = bf_hi(t.z); v[6] = bf_lo(t.w); v[7] = bf_hi(t.w);
+  }
+};
+
+CTTS_DEV const float* row_in(const float* base, int m, int div, long ld, long ld_outer) {
+  return base + (long)(m / div) * ld_outer + (long)(m % div) * ld;
+}
+
+template <bool BF16, int MT, int RPW, bool SWIGLU>
+__global__ void __launch_bounds__(kWarps * 32) linear_rows_kernel(const LinearArgs a) {
+  extern __shared__ __align__(16) float xs[];  // [MT][K]
+  constexpr int VEC = WVec<BF16>::N;
+  const int K = a.K;
+  const int m0 = blockIdx.y * MT;
+  const int mt = min(MT, a.M - m0);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+  grid_dep_wait();
+  // ---- prologue: stage the activation tile (RMSNorm + modulate)
+  for (int r = warp; r < MT; r += kWarps) {
+    float* dst = xs + r * K;
+    if (r >= mt) {
+      for (int k = lane; k < K; k += 32) dst[k] = 0.0f;
+      continue;
+    }
+    const int m = m0 + r;
+    const float* xr = row_in(a.x, m, a.x_div, a.x_ld, a.x_ld_outer);
+    float inv = 1.0f;
+    if (a.norm_w) {
+      float ss = 0.0f;
+      for (int k = lane; k < K; k += 32) ss = fmaf(xr[k], xr[k], ss);
+      ss = warp_sum(ss);
+      inv = 1.0f / sqrtf(ss / (float)K + a.eps);
+    }
+    const float* md = a.mod ? a.mod + (long)(m / a.mod_div) * a.mod_ld : nullptr;
+    for (int k = lane; k < K; k += 32) {
+      float v = xr[k];
+      if (a.norm_w) v = v * inv * a.norm_w[k];
+      if (md) v = v * (1.0f + md[a.mod_scale + k]) + md[a.mod_shift + k];
+      dst[k] = v;
+    }
+  }
+  __syncthreads();
+
+  const int n0 = (blockIdx.x * kWarps + warp) * RPW;
+  if (n0 >= a.N) return;
+
+  float acc[RPW][MT];
+  float acc2[SWIGLU ? RPW : 1][MT];
+#pragma unroll
+  for (int r = 0; r < RPW; r++)
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+      acc[r][m] = 0.0f;
+      if (SWIGLU) acc2[r][m] = 0.0f;
+    }
+
+  int nr[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; r++) nr[r] = min(n0 + r, a.N - 1);
+
+#pragma unroll 2
+  for (int k = lane * VEC; k < K; k += 32 * VEC) {
+    float wv[RPW][VEC];
+    float wu[SWIGLU ? RPW : 1][VEC];
+#pragma unroll
+    for (int r = 0; r < RPW; r++) {
+      WVec<BF16>::load(a.w, (size_t)nr[r] * K + k, wv[r]);
+      if (SWIGLU) WVec<BF16>::load(a.w, (size_t)(nr[r] + a.N) * K + k, wu[r]);
+    }
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+      float xv[VEC];
+#pragma unroll
+      for (int v4 = 0; v4 < VEC; v4 += 4) {
+        float4 t = *reinterpret_cast<const float4*>(xs + m * K + k + v4);
+        xv[v4] = t.x; xv[v4 + 1] = t.y; xv[v4 + 2] = t.z; xv[v4 + 3] = t.w;
+      }
+#pragma unroll
+      for (int r = 0; r < RPW; r++)
+#pragma unroll
+        for (int v = 0; v < VEC; v++) {
+          acc[r][m] = fmaf(wv[r][v], xv[v], acc[r][m]);
+          if (SWIGLU) acc2[r][m] = fmaf(wu[r][v], xv[v], acc2[r][m]);
+        }
+    }
+  }
+
+#pragma unroll
+  for (int r = 0; r < RPW; r++)
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+      acc[r][m] = warp_sum(acc[r][m]);
+      if (SWIGLU) acc2[r][m] = warp_sum(acc2[r][m]);
+    }
+
+#pragma unroll
+  for (int r = 0; r < RPW; r++) {
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+      if (((r * MT + m) & 31) != lane) continue;
+      const int n = n0 + r, mm = m0 + m;
+      if (n >= a.N || m >= mt) continue;
+      float val = acc[r][m] + (a.bias ? a.bias[n] : 0.0f);
+      if (SWIGLU) {
+        float u = acc2[r][m] + (a.bias ? a.bias[a.N + n] : 0.0f);
+        val = silu(val) * u;
+      } else if (a.act == 1) {
+        val = silu(val);
+      }
+      float coef = a.gate ? 1.0f + a.gate[(long)(mm / a.gate_div) * a.gate_ld + a.gate_off + n]
+                          : a.scale;
+      float* yr = const_cast<float*>(row_in(a.y, mm, a.y_div, a.y_ld, a.y_ld_outer));
+      float out = coef * val;
+      if (a.res) out = row_in(a.res, mm, a.y_div, a.y_ld, a.y_ld_outer)[n] + out;
+      yr[n] = out;
+    }
+  }
+}
+
+template <bool BF16, int MT, int RPW, bool SWIGLU>
+cudaError_t launch_t(const LinearArgs& a, cudaStream_t s) {
+  auto kern = linear_rows_kernel<BF16, MT, RPW, SWIGLU>;
+  size_t smem = (size_t)MT * a.K * sizeof(float);
+  static int configured = 0;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         200 * 1024);
+    if (e != cudaSuccess) return e;
+    configured = 1;
+  }
+  dim3 grid((a.N + kWarps * RPW - 1) / (kWarps * RPW), (a.M + MT - 1) / MT);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+int pick_mt(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
+
+int pick_rpw(const LinearArgs& a, int mt) {
+  int gy = (a.M + mt - 1) / mt;
+  for (int rpw : {4, 2}) {
+    long ctas = (long)((a.N + kWarps * rpw - 1) / (kWarps * rpw)) * gy;
+    if (ctas >= 2 * 148) return rpw;
+  }
+  return 1;
+}
+
+template <bool BF16, bool SW>
+cudaError_t dispatch_mt(const LinearArgs& a, cudaStream_t s) {
+  int mt = pick_mt(a.M);
+  int rpw = pick_rpw(a, mt);
+#define CTTS_L(MT_)                                                     \
+  if (mt == MT_) {                                                      \
+    if (rpw == 4) return launch_t<BF16, MT_, 4, SW>(a, s);              \
+    if (rpw == 2) return launch_t<BF16, MT_, 2, SW>(a, s);              \
+    return launch_t<BF16, MT_, 1, SW>(a, s);                            \
+  }
+  CTTS_L(1) CTTS_L(2) CTTS_L(4) CTTS_L(8)
+#undef CTTS_L
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+int linear_grid_ctas(const LinearArgs& a) {
+  int mt = pick_mt(a.M);
+  int rpw = pick_rpw(a, mt);
+  return ((a.N + kWarps * rpw - 1) / (kWarps * rpw)) * ((a.M + mt - 1) / mt);
+}
+
+cudaError_t launch_linear(const LinearArgs& a, cudaStream_t s) {
+  if (a.M <= 0 || a.N <= 0) return cudaSuccess;
+  const int vec = a.w_bf16 ? 8 : 4;
+  if (a.K <= 0 || a.K % vec != 0 || (size_t)8 * a.K * sizeof(float) > 200 * 1024)
+    return cudaErrorInvalidValue;
+  const bool sw = a.act == 2;
+  if (a.w_bf16) return sw ? dispatch_mt<true, true>(a, s) : dispatch_mt<true, false>(a, s);
+  return sw ? dispatch_mt<false, true>(a, s) : dispatch_mt<false, false>(a, s);
+}
+
+}  // namespace ctts

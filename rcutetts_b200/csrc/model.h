@@ -1,0 +1,140 @@
+// model.h -- the objects behind the C ABI handles.
+#pragma once
+
+#include <algorithm>
+#include <vector>
+
+#include "api_common.h"
+
+// LM stack (replaces QwenW, qwen.rs:26-44).  Weights of a layer are fused
+// into wide matrices at load: [q;k;v] -> wqkv, [gate;up] -> wgu, so one
+// pass over the activations feeds all of them.
+struct LMLayer {
+  float *norm1 = nullptr, *norm2 = nullptr, *qn = nullptr, *kn = nullptr;
+  void *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wd = nullptr;
+};
+
+struct ctts_lm {
+  ctts_lm_config cfg{};
+  int device = 0;
+  int bf16 = 0;
+  cudaStream_t stream = nullptr;
+  ctts::DevArena arena;
+  ctts::SlotTable slots;
+  void* embed = nullptr;
+  std::vector<LMLayer> layers;
+  float* final_norm = nullptr;
+  float* inv_freq = nullptr;
+};
+
+// Batched KV cache (replaces QwenCache, qwen.rs:139-149) plus the decode /
+// prefill workspace sized for this batch.  Layout per layer:
+// [batch][kv_head][capacity][head_dim] in the model weight dtype.
+struct ctts_kv {
+  const ctts_lm* lm = nullptr;
+  int batch = 0, cap = 0, nsplit = 0, ws_rows = 0;
+  size_t layer_elems = 0;
+  ctts::DevArena arena;
+  void *k = nullptr, *v = nullptr;
+  int* pos = nullptr;  // device positions (= cache lengths)
+  int* err = nullptr;
+  std::vector<int> pos_host;
+  float *h = nullptr, *qkv = nullptr, *qrot = nullptr, *att = nullptr, *act = nullptr,
+        *part = nullptr, *xin = nullptr, *xout = nullptr;
+};
+
+// DiT head (replaces DitW, dit.rs:27-68).
+struct DitLayer {
+  float *norm1 = nullptr, *norm2 = nullptr;
+  void *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wd = nullptr;
+};
+
+struct DitWs {  // workspace for `rows` utterance-branches
+  int rows = 0, steps = 0;
+  ctts::DevArena arena;
+  float *seq = nullptr, *qkv = nullptr, *att = nullptr, *act = nullptr, *mu = nullptr,
+        *ad = nullptr, *condh = nullptr, *temb = nullptr, *dtemb = nullptr, *tmp = nullptr,
+        *se = nullptr, *tv = nullptr, *x = nullptr, *v = nullptr, *z = nullptr,
+        *cond = nullptr, *spk = nullptr, *hbuf = nullptr, *stemb = nullptr;
+};
+
+struct ctts_dit {
+  ctts_dit_config cfg{};
+  int device = 0;
+  int bf16 = 0;
+  cudaStream_t stream = nullptr;
+  ctts::DevArena arena;
+  ctts::SlotTable slots;
+  void *in_w = nullptr, *cond_w = nullptr, *mu_w = nullptr, *out_w = nullptr;
+  void *t1_w = nullptr, *t2_w = nullptr, *dt1_w = nullptr, *dt2_w = nullptr;
+  void *st1_w = nullptr, *st2_w = nullptr;
+  float *in_b = nullptr, *cond_b = nullptr, *mu_b = nullptr, *out_b = nullptr;
+  float *t1_b = nullptr, *t2_b = nullptr, *dt1_b = nullptr, *dt2_b = nullptr;
+  float *st1_b = nullptr, *st2_b = nullptr;
+  float* cfg0_w = nullptr;  // [H,1] float32 (applied on the host: scalar input)
+  void* cfg2_w = nullptr;
+  void* adaln = nullptr;  // [n_layers*6H, spk_dim]
+  std::vector<DitLayer> layers;
+  float* final_norm = nullptr;
+  float* inv_freq = nullptr;
+  DitWs ws;
+};
+
+struct ctts_engine {
+  ctts_lm* lm = nullptr;
+  ctts_dit* dit = nullptr;
+  ctts_kv* kv = nullptr;
+  ctts_engine_config cfg{};
+  cudaStream_t stream = nullptr;
+  ctts::DevArena arena;
+  float *stop_w = nullptr, *stop_b = nullptr, *proj_w = nullptr, *proj_b = nullptr;
+  float *z = nullptr, *x = nullptr, *cond = nullptr, *lat = nullptr, *stop = nullptr,
+        *fb = nullptr, *noise = nullptr;
+  float *h_noise = nullptr, *h_lat = nullptr, *h_stop = nullptr;  // pinned staging
+  bool heads_set = false;
+  std::vector<bool> prefilled;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int steps_done = 0;
+  int launches = 0;
+};
+
+// VAE decoder (replaces DecoderW, weights.rs:34-44).
+struct VaeRes {
+  float *a0 = nullptr, *b0 = nullptr, *a1 = nullptr, *b1 = nullptr;
+  void *w0 = nullptr, *w1 = nullptr;
+};
+struct VaeStage {
+  int cin = 0, cout = 0, stride = 0;
+  float *alpha = nullptr, *tb = nullptr;
+  void* tw = nullptr;  // repacked [stride][cout][cin*2]
+  VaeRes res[3];
+};
+struct ctts_vae {
+  ctts_vae_config cfg{};
+  int device = 0;
+  int bf16 = 0;
+  cudaStream_t stream = nullptr;
+  ctts::DevArena arena;
+  ctts::SlotTable slots;
+  void *front_w = nullptr, *front_pw_w = nullptr;
+  float *front_b = nullptr, *front_pw_b = nullptr;
+  std::vector<VaeStage> stages;
+  float *final_alpha = nullptr, *final_b = nullptr;
+  void* final_w = nullptr;
+  int hop = 1;
+  // workspace
+  size_t ws_elems = 0;
+  float *buf[3] = {nullptr, nullptr, nullptr};
+  ctts::DevArena ws_arena;
+  float *lat_dev = nullptr, *wav_dev = nullptr;
+  size_t io_lat = 0, io_wav = 0;
+};
+
+namespace ctts {
+int lm_forward_rows(ctts_lm* lm, ctts_kv* kv, int rows, int prefill_b, int pos0, float* out,
+                    cudaStream_t s, int* launches);
+int lm_check_ready(const ctts_lm* lm);
+int lm_decode_dev(ctts_lm* lm, ctts_kv* kv, const float* x_dev, float* out_dev, cudaStream_t s,
+                  int* launches);
+}  // namespace ctts

@@ -1,0 +1,150 @@
+// vae.cu -- causal Conv1d / ConvTranspose1d (+ fused Snake) for the VAE
+// decoder (audio_vae.py:43-62,73-79; rust-codec/src/conv.rs, snake.rs,
+// decode.rs).
+//
+// Both convolutions run as an implicit GEMM on CUDA cores:
+//   y[o, t] = bias[o] + sum_{c, j} W[o, c*k + j] * snake(x[c, t + j*dil - left])
+// The Snake activation of the *input* is applied while the activation tile
+// is staged into shared memory (the reference runs it as a separate pass,
+// snake.rs:26-36), the residual add and the final tanh are applied in the
+// epilogue.  A transposed conv with kernel 2s and stride s is s such
+// convolutions with k = 2, dilation 1, left pad 1 on repacked weights, each
+// writing every s-th output sample (the two-GEMM decomposition of
+// decode.rs:39-80 / weights.rs:133-147).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ctts {
+
+namespace {
+
+constexpr int TO = 64;   // output channels per CTA
+constexpr int TT = 64;   // output positions per CTA
+constexpr int TK = 16;   // reduction chunk
+
+template <bool BF>
+CTTS_DEV float ldw(const void* w, size_t i) {
+  if (BF) return bf2f(reinterpret_cast<const uint16_t*>(w)[i]);
+  return reinterpret_cast<const float*>(w)[i];
+}
+
+CTTS_DEV float snake1(float v, float a) {
+  float s = sinf(v * a);
+  return v + (1.0f / (a + 1e-9f)) * s * s;
+}
+
+// grid (ceil(Tc/TT), ceil(Cout/TO), B*nphase); 256 threads, 4x4 outputs each.
+// Tc = computed positions per phase; output sample = t*ostride + phase.
+template <bool BF>
+__global__ void __launch_bounds__(256) conv_kernel(const ConvArgs a, int Tc, int ostride,
+                                                   int nphase, long wphase) {
+  __shared__ __align__(16) float Ws[TK][TO];
+  __shared__ __align__(16) float Xs[TK][TT];
+  grid_dep_wait();
+  const int b = blockIdx.z / nphase, ph = blockIdx.z % nphase;
+  const int o0 = blockIdx.y * TO, t0 = blockIdx.x * TT;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int k = a.k, KK = a.Cin * k;
+  const void* w = BF ? (const void*)(reinterpret_cast<const uint16_t*>(a.w) + ph * wphase)
+                     : (const void*)(reinterpret_cast<const float*>(a.w) + ph * wphase);
+  const float* xb = a.x + (size_t)b * a.Cin * a.Tin;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+
+  for (int kc = 0; kc < KK; kc += TK) {
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      int idx = tid + e * 256;        // 0..1023
+      int kk = idx & (TK - 1), oo = idx >> 4;
+      int o = o0 + oo, kidx = kc + kk;
+      Ws[kk][oo] = (o < a.Cout && kidx < KK) ? ldw<BF>(w, (size_t)o * KK + kidx) : 0.0f;
+      int tt = idx & (TT - 1), kk2 = idx >> 6;
+      int kidx2 = kc + kk2;
+      float v = 0.0f;
+      if (kidx2 < KK && t0 + tt < Tc) {
+        int c = kidx2 / k, j = kidx2 % k;
+        int src = t0 + tt + j * a.dil - a.left;
+        if (src >= 0 && src < a.Tin) {
+          v = xb[(size_t)c * a.Tin + src];
+          if (a.snake_alpha) v = snake1(v, a.snake_alpha[c]);
+        }
+      }
+      Xs[kk2][tt] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < TK; kk++) {
+      float4 wv = *reinterpret_cast<const float4*>(&Ws[kk][ty * 4]);
+      float4 xv = *reinterpret_cast<const float4*>(&Xs[kk][tx * 4]);
+      float wr[4] = {wv.x, wv.y, wv.z, wv.w}, xr[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = fmaf(wr[i], xr[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    int o = o0 + ty * 4 + i;
+    if (o >= a.Cout) continue;
+    float bo = a.bias ? a.bias[o] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      int t = t0 + tx * 4 + j;
+      if (t >= Tc) continue;
+      size_t oi = ((size_t)b * a.Cout + o) * a.Tout + (size_t)t * ostride + ph;
+      float v = acc[i][j] + bo;
+      if (a.res) v += a.res[oi];
+      if (a.tanh_out) v = tanhf(v);
+      a.y[oi] = v;
+    }
+  }
+}
+
+__global__ void snake_kernel(const float* x, int C, int T, const float* alpha, float* y,
+                             size_t n) {
+  grid_dep_wait();
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int c = (int)((i / T) % C);
+  y[i] = snake1(x[i], alpha[c]);
+}
+
+}  // namespace
+
+cudaError_t launch_conv1d(const ConvArgs& a, cudaStream_t s) {
+  if (a.Tout != a.Tin) return cudaErrorInvalidValue;
+  dim3 grid((a.Tout + TT - 1) / TT, (a.Cout + TO - 1) / TO, a.B);
+  if (a.w_bf16)
+    conv_kernel<true><<<grid, 256, 0, s>>>(a, a.Tout, 1, 1, 0);
+  else
+    conv_kernel<false><<<grid, 256, 0, s>>>(a, a.Tout, 1, 1, 0);
+  return cudaGetLastError();
+}
+
+// a.w: repacked [stride][Cout][Cin*2] (tap 0 <- x[i-1], tap 1 <- x[i]);
+// a.k must be 2, a.dil 1, a.left 1; Tout = Tin * stride.
+cudaError_t launch_conv_transpose(const ConvArgs& a, cudaStream_t s) {
+  if (a.k != 2 || a.Tout != a.Tin * a.stride) return cudaErrorInvalidValue;
+  dim3 grid((a.Tin + TT - 1) / TT, (a.Cout + TO - 1) / TO, a.B * a.stride);
+  long wphase = (long)a.Cout * a.Cin * 2;
+  if (a.w_bf16)
+    conv_kernel<true><<<grid, 256, 0, s>>>(a, a.Tin, a.stride, a.stride, wphase);
+  else
+    conv_kernel<false><<<grid, 256, 0, s>>>(a, a.Tin, a.stride, a.stride, wphase);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_snake(const float* x, int B, int C, int T, const float* alpha, float* y,
+                         cudaStream_t s) {
+  size_t n = (size_t)B * C * T;
+  if (!n) return cudaSuccess;
+  snake_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, C, T, alpha, y, n);
+  return cudaGetLastError();
+}
+
+}  // namespace ctts

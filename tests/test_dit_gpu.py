@@ -1,0 +1,83 @@
+"""DiT flow head on the GPU against the torch-made golden vectors
+(AudioDiTHead at the config[2] shape) and the oracle."""
+import numpy as np
+import pytest
+
+from conftest import cosine, rel_err
+from helpers import bf16_weights, dit_model, rnd
+from oracle import oracle as orc
+from rcutetts_b200.config import DiTConfig
+
+pytestmark = pytest.mark.gpu
+
+
+def test_predict_and_euler_config2(golden):
+    g = golden("dit_c2.npz")
+    cfg = DiTConfig()
+    m, w = dit_model(cfg, seed=12)
+    v = m.predict(g["x0"], float(g["t"]), g["z"], g["cond"], spk=g["z"])
+    for b in range(2):
+        assert rel_err(v[b], g["predict_out"][b]) < 1e-4
+    x = m.euler_sample(g["x0"], g["z"], g["cond"], g["z"], 10)
+    for b in range(2):
+        assert rel_err(x[b], g["euler10_out"][b]) < 1e-4
+        assert cosine(x[b], g["euler10_out"][b]) >= 0.9999
+
+
+def test_plain_predict_and_cfg(golden):
+    g, gc = golden("dit_plain.npz"), golden("dit_c2.npz")
+    cfg = DiTConfig(adaln=False, n_layers=2)
+    m, w = dit_model(cfg, seed=13)
+    v = m.predict(gc["x0"], 0.7, gc["z"], gc["cond"])
+    assert rel_err(v, g["predict_out"]) < 1e-4
+    x = m.euler_sample_cfg(gc["x0"], gc["z"], g["z_uncond"], gc["cond"], g["uncond"], None, 10, -0.8, 2.0)
+    assert rel_err(x, g["cfg_out"]) < 1e-4
+
+
+def test_cfg_with_adaln_vs_oracle():
+    """CFG with AdaLN: the uncond branch feeds zero AdaLN rows (dit.rs:878-887)."""
+    cfg = DiTConfig(n_layers=2)
+    m, w = dit_model(cfg, seed=14)
+    o = orc.DiT(cfg, w)
+    x0, zc, zu = rnd(1, (2, 64)), rnd(2, (2, 768)), rnd(3, (2, 768))
+    c, u, spk = rnd(4, (2, 64)), rnd(5, (2, 64)), rnd(6, (2, 768))
+    x = m.euler_sample_cfg(x0, zc, zu, c, u, spk, 6, -0.8, 2.0)
+    for b in range(2):
+        ref = o.euler_sample_cfg(x0[b], zc[b], zu[b], c[b], u[b], spk[b], 6, -0.8, 2.0)
+        assert rel_err(x[b], ref) < 1e-4
+
+
+def test_bf16_vs_oracle():
+    cfg = DiTConfig()
+    m, w = dit_model(cfg, seed=15, dtype="bf16")
+    o = orc.DiT(cfg, bf16_weights(w))
+    x0, z, c = rnd(7, (3, 64)), rnd(8, (3, 768)), rnd(9, (3, 64))
+    x = m.euler_sample(x0, z, c, z, 10)
+    for b in range(3):
+        ref = o.euler_sample(x0[b], z[b], c[b], z[b], 10)
+        assert cosine(x[b], ref) >= 0.999
+        assert rel_err(x[b], ref) < 1e-3
+
+
+def test_batch_matches_single():
+    cfg = DiTConfig()
+    m, _ = dit_model(cfg, seed=16)
+    x0, z, c = rnd(10, (5, 64)), rnd(11, (5, 768)), rnd(12, (5, 64))
+    xb = m.euler_sample(x0, z, c, z, 4)
+    for b in range(5):
+        xs = m.euler_sample(x0[b:b + 1], z[b:b + 1], c[b:b + 1], z[b:b + 1], 4)
+        assert rel_err(xs[0], xb[b]) < 1e-6
+
+
+def test_distill_embeddings_vs_oracle():
+    """Step-size and cfg-strength embeddings (distill checkpoint layout,
+    diffusion_head.py:451-542) with hidden == cond_dim (mu_proj Identity)."""
+    cfg = DiTConfig(hidden=256, cond_dim=256, spk_dim=128, n_heads=4, n_kv_heads=2, ffn=512,
+                    n_layers=2, patch=2, step_emb=True, cfg_emb=True)
+    m, w = dit_model(cfg, seed=17)
+    o = orc.DiT(cfg, w)
+    x0, z, c, spk = rnd(13, (2, 128)), rnd(14, (2, 256)), rnd(15, (2, 128)), rnd(16, (2, 128))
+    x = m.euler_sample(x0, z, c, spk, 4, cfg_w=2.0)
+    for b in range(2):
+        ref = o.euler_sample(x0[b], z[b], c[b], spk[b], 4, cfg_w=2.0)
+        assert rel_err(x[b], ref) < 1e-4

@@ -1,0 +1,103 @@
+"""The per-frame engine (stop head -> DiT Euler sample -> latent out ->
+feedback projection -> LM decode step, one CUDA graph per frame) against
+the oracle's AR loop on identical seeded inputs (noise passed in)."""
+import numpy as np
+import pytest
+
+from conftest import cosine, rel_err
+from helpers import bf16_weights, rnd
+from oracle import oracle as orc
+from rcutetts_b200 import synth
+from rcutetts_b200.config import DiTConfig, LMConfig
+
+pytestmark = pytest.mark.gpu
+
+
+def build(lcfg, dcfg, seed, dtype, batch, capacity, use_graph=True):
+    from rcutetts_b200.model import DitW, FrameEngine, QwenW
+
+    lw = synth.lm_weights(lcfg, seed=seed, with_embed=True)
+    dw = synth.dit_weights(dcfg, seed=seed + 10)
+    hw = synth.frame_weights(lcfg.hidden, dcfg.latent, seed=seed + 20)
+    lm = QwenW(lcfg, dtype).set_weights(lw)
+    dit = DitW(dcfg, dtype).set_weights(dw)
+    eng = FrameEngine(lm, dit, hw, batch=batch, capacity=capacity, euler_steps=10, use_graph=use_graph)
+    return eng, (lm, dit), lw, dw, hw
+
+
+def prefix_rows(lw, hw, ids, prompt):
+    """[embed(text ids); latent_proj(prompt latents)] -- the config[2] prefix."""
+    emb = orc.embed_lookup(lw["embed_tokens.weight"], ids)
+    pr = orc.linear(prompt, hw["latent_proj.weight"], hw["latent_proj.bias"])
+    return np.concatenate([emb, pr], 0)
+
+
+def test_b1_fp32_frames_vs_oracle():
+    lcfg, dcfg = LMConfig(), DiTConfig()
+    eng, keep, lw, dw, hw = build(lcfg, dcfg, seed=2, dtype="f32", batch=1, capacity=256)
+    rng = np.random.default_rng(2)
+    ids = rng.integers(0, lcfg.vocab, 40)
+    prompt = rng.standard_normal((150, 64), dtype=np.float32)
+    noise = rng.standard_normal((5, 64), dtype=np.float32)
+    pre = prefix_rows(lw, hw, ids, prompt)
+    eng.prefill(0, pre, prompt[-1])
+    lats, stops = [], []
+    for f in range(5):
+        lat, st = eng.step(noise[f:f + 1])
+        lats.append(lat[0])
+        stops.append(st[0])
+    ref_lat, ref_stop, _ = orc.generate(orc.LM(lcfg, lw), orc.DiT(dcfg, dw), hw, pre, noise, prompt[-1], 10)
+    for f in range(5):
+        assert rel_err(lats[f], ref_lat[f]) < 1e-4, f
+        assert cosine(lats[f], ref_lat[f]) >= 0.9999, f
+        assert rel_err(stops[f], ref_stop[f]) < 1e-4, f
+    assert eng.launches_per_step > 0
+
+
+def test_graph_replay_matches_eager():
+    lcfg, dcfg = LMConfig(n_layers=2), DiTConfig(n_layers=2)
+    outs = []
+    for use_graph in (True, False):
+        eng, keep, lw, dw, hw = build(lcfg, dcfg, seed=3, dtype="f32", batch=2, capacity=64,
+                                      use_graph=use_graph)
+        for b in range(2):
+            eng.prefill(b, rnd(30 + b, (7 + 3 * b, lcfg.hidden)), rnd(40 + b, (64,)))
+        noise = rnd(50, (4, 2, 64))
+        outs.append(np.stack([eng.step(noise[f])[0] for f in range(4)]))
+        del eng
+    assert np.array_equal(outs[0], outs[1])
+
+
+def test_batched_bf16_ragged_vs_oracle():
+    """config[3] in miniature: bf16 weights, ragged prefixes, batch 3."""
+    lcfg, dcfg = LMConfig(n_layers=4), DiTConfig()
+    eng, keep, lw, dw, hw = build(lcfg, dcfg, seed=4, dtype="bf16", batch=3, capacity=96)
+    rng = np.random.default_rng(4)
+    lens = [20, 33, 27]
+    pres, conds = [], []
+    lwb, dwb, hwb = bf16_weights(lw), bf16_weights(dw), hw
+    for b in range(3):
+        ids = rng.integers(0, lcfg.vocab, lens[b])
+        prompt = rng.standard_normal((12, 64), dtype=np.float32)
+        # the device embeds with its bf16 table: build the prefix from the same rounded table
+        pres.append(prefix_rows(lwb, hw, ids, prompt))
+        conds.append(prompt[-1])
+        eng.prefill(b, pres[-1], conds[-1])
+    noise = rng.standard_normal((4, 3, 64), dtype=np.float32)
+    lat = np.stack([eng.step(noise[f])[0] for f in range(4)])
+    lm_o, dit_o = orc.LM(lcfg, lwb), orc.DiT(dcfg, dwb)
+    for b in range(3):
+        ref, _, _ = orc.generate(lm_o, dit_o, hwb, pres[b], noise[:, b, :], conds[b], 10)
+        for f in range(4):
+            assert cosine(lat[f, b], ref[f]) >= 0.999, (b, f)
+
+
+def test_step_requires_prefill():
+    from rcutetts_b200._lib import ERR_STATE, CttsError
+
+    lcfg, dcfg = LMConfig(n_layers=1), DiTConfig(n_layers=1)
+    eng, keep, lw, dw, hw = build(lcfg, dcfg, seed=5, dtype="f32", batch=2, capacity=16)
+    eng.prefill(0, rnd(1, (3, lcfg.hidden)), rnd(2, (64,)))
+    with pytest.raises(CttsError) as e:
+        eng.step(rnd(3, (2, 64)))
+    assert e.value.code == ERR_STATE
