@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <array>
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -16,6 +17,7 @@
 #include "../../include/cutetts_b200.h"
 #include "kernels.cuh"
 #include "safetensors.h"
+#include "tc_linear.cuh"
 
 namespace ctts {
 
@@ -114,15 +116,95 @@ inline void host_to_f32(const void* src, int dtype, size_t n, std::vector<float>
   }
 }
 
+constexpr int kXformNone = 0;
+constexpr int kXformTranspose = 1;      // VAE ConvTranspose repack (api_vae.cu)
+constexpr int kXformRowInterleave = 2;  // 64-row groups at a 128-row pitch (t_b = row length)
+
 // Upload float32 host data into a slot (converting to the model dtype).
+// kXformRowInterleave places rows [64g, 64g+64) of the tensor at rows
+// [128g, 128g+64) of the destination: the gate/up tile interleave the
+// SwiGLU linears read.
 inline int upload_f32(const Slot& s, const float* data, size_t n, int model_bf16) {
-  if (s.weight && model_bf16) {
-    std::vector<uint16_t> b(n);
+  const bool bf = s.weight && model_bf16;
+  const size_t es = bf ? 2 : 4;
+  std::vector<uint16_t> b;
+  const void* src = data;
+  if (bf) {
+    b.resize(n);
     for (size_t i = 0; i < n; i++) b[i] = host_f2bf(data[i]);
-    CTTS_CK(cudaMemcpy(s.dst, b.data(), n * 2, cudaMemcpyHostToDevice));
-  } else {
-    CTTS_CK(cudaMemcpy(s.dst, data, n * 4, cudaMemcpyHostToDevice));
+    src = b.data();
   }
+  if (s.transform == kXformRowInterleave) {
+    const size_t row = (size_t)s.t_b * es, rows = n / (size_t)s.t_b;
+    if (rows % 64) return set_error(CTTS_ERR_ARG, "interleaved tensor rows must be a multiple of 64");
+    CTTS_CK(cudaMemcpy2D(s.dst, 128 * row, src, 64 * row, 64 * row, rows / 64, cudaMemcpyHostToDevice));
+  } else {
+    CTTS_CK(cudaMemcpy(s.dst, src, n * es, cudaMemcpyHostToDevice));
+  }
+  return CTTS_OK;
+}
+
+// Device scratch for the split-K tensor-core linears.
+struct TcScratch {
+  float* part = nullptr;
+  size_t part_floats = 0;
+  int* counters = nullptr;
+  int ncounters = 0;
+  int* err = nullptr;
+};
+
+// Scratch floats the widest of `shapes` (M, N, K triples) needs.
+inline size_t tc_scratch_need(const std::vector<std::array<int, 3>>& shapes, int max_splitk,
+                              int* counters) {
+  size_t need = 0;
+  int cnt = 0;
+  for (auto& sh : shapes) {
+    TcPlan p = tc_plan(sh[0], sh[1], sh[2], tc_num_sms(), max_splitk);
+    need = std::max(need, tc_scratch_floats(p));
+    cnt = std::max(cnt, p.ntiles * p.mtiles);
+  }
+  if (counters) *counters = cnt;
+  return need;
+}
+
+inline int tc_alloc(DevArena& arena, TcScratch* sc, const std::vector<std::array<int, 3>>& shapes,
+                    int* err) {
+  int cnt = 0;
+  size_t need = tc_scratch_need(shapes, 64, &cnt);
+  sc->part = arena.alloc<float>(std::max<size_t>(need, 1));
+  sc->part_floats = need;
+  sc->counters = arena.alloc<int>(std::max(cnt, 1));
+  sc->ncounters = cnt;
+  sc->err = err;
+  if (!sc->part || !sc->counters) return set_error(CTTS_ERR_NOMEM, "tensor-core scratch allocation failed");
+  return CTTS_OK;
+}
+
+// Y = epi(X[M,K] . W[N,K]^T) on the tensor cores; falls back to fewer K
+// splits (down to 1) when the scratch is too small for the planned split.
+inline int tc_run(const TcScratch& sc, const uint16_t* x, int M, int K, const void* w, int N,
+                  const TcArgs& epi, cudaStream_t s, int* nl) {
+  TcCall c;
+  c.x = x;
+  c.w = reinterpret_cast<const uint16_t*>(w);
+  c.M = M;
+  c.N = N;
+  c.K = K;
+  c.epi = epi;
+  c.part = sc.part;
+  c.part_floats = sc.part_floats;
+  c.counters = sc.counters;
+  c.counter_count = sc.ncounters;
+  c.err = sc.err;
+  c.max_splitk = M > 256 ? 1 : 64;
+  while (c.max_splitk > 1) {
+    TcPlan p = tc_plan(M, N, K, tc_num_sms(), c.max_splitk);
+    if (tc_scratch_floats(p) <= sc.part_floats && p.ntiles * p.mtiles <= sc.ncounters) break;
+    c.max_splitk = std::max(1, p.splitk / 2);
+  }
+  cudaError_t e = launch_tc_linear(c, s);
+  if (e != cudaSuccess) return set_error(CTTS_ERR_CUDA, std::string("tc_linear: ") + cudaGetErrorString(e));
+  if (nl) *nl += tc_plan(M, N, K, tc_num_sms(), c.max_splitk).mtiles;
   return CTTS_OK;
 }
 

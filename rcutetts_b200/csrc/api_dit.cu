@@ -40,8 +40,21 @@ int dit_ws_ensure(ctts_dit* d, int rows, int steps) {
   w.cond = w.arena.alloc<float>((size_t)rows * P * L);
   w.spk = w.arena.alloc<float>((size_t)rows * std::max(c.spk_dim, 1));
   w.hbuf = w.arena.alloc<float>((size_t)2 * H);
-  if (!w.seq || !w.qkv || !w.att || !w.act || !w.ad || !w.x || !w.spk || !w.hbuf)
+  w.err = w.arena.alloc<int>(1);
+  if (!w.seq || !w.qkv || !w.att || !w.act || !w.ad || !w.x || !w.spk || !w.hbuf || !w.err)
     return set_error(CTTS_ERR_NOMEM, "DiT workspace allocation failed");
+  if (d->bf16) {
+    const int SR = rows * S;
+    w.xb = w.arena.alloc<uint16_t>((size_t)SR * std::max(std::max(H, c.spk_dim), c.ffn));
+    w.attb = w.arena.alloc<uint16_t>((size_t)SR * qd);
+    w.actb = w.arena.alloc<uint16_t>((size_t)SR * c.ffn);
+    std::vector<std::array<int, 3>> shapes = {
+        {SR, qkvw, H}, {SR, H, qd}, {SR, 2 * c.ffn, H}, {SR, H, c.ffn},
+        {rows, c.n_layers * 6 * H, std::max(c.spk_dim, 64)}};
+    int rc = tc_alloc(w.arena, &w.tc, shapes, w.err);
+    if (rc) return rc;
+    if (!w.xb || !w.attb || !w.actb) return set_error(CTTS_ERR_NOMEM, "DiT workspace allocation failed");
+  }
   w.rows = rows;
   w.steps = steps;
   return CTTS_OK;
@@ -130,10 +143,20 @@ int dit_enqueue(ctts_dit* d, const DitRun& r, cudaStream_t s, int* launches) {
     CTTS_CK(launch_add_rows(w.mu, R, H, w.stemb, s)); nl++;
   }
   const bool use_ad = c.adaln && r.spk;
+  // bf16 weights with >= 16 rows: the tensor-core linears (tc_linear.cu)
+  const bool tc = bf && R * S >= 16;
   if (use_ad) {
     int rows = r.zero_adaln_from >= 0 ? r.zero_adaln_from : R;
-    LinearArgs a; a.x = r.spk; a.x_ld = c.spk_dim; a.M = rows; a.K = c.spk_dim; a.N = (int)adld;
-    a.w = d->adaln; a.y = w.ad; a.y_ld = adld; RUN(lin(a));
+    if (bf && rows >= 16 && c.spk_dim % 64 == 0) {
+      PrepArgs pa; pa.x = r.spk; pa.x_ld = c.spk_dim; pa.y = w.xb; pa.y_ld = c.spk_dim; pa.M = rows;
+      pa.K = c.spk_dim;
+      CTTS_CK(launch_prep_bf16(pa, s)); nl++;
+      TcArgs e; e.y = w.ad; e.y_ld = adld;
+      RUN(tc_run(w.tc, w.xb, rows, c.spk_dim, d->adaln, (int)adld, e, s, &nl));
+    } else {
+      LinearArgs a; a.x = r.spk; a.x_ld = c.spk_dim; a.M = rows; a.K = c.spk_dim; a.N = (int)adld;
+      a.w = d->adaln; a.y = w.ad; a.y_ld = adld; RUN(lin(a));
+    }
     if (rows < R) CTTS_CK(cudaMemsetAsync(w.ad + (size_t)rows * adld, 0, sizeof(float) * (R - rows) * adld, s));
   }
   {  // cond_proj(cond) rows [R*P, L]
@@ -154,11 +177,36 @@ int dit_enqueue(ctts_dit* d, const DitRun& r, cudaStream_t s, int* launches) {
     for (int l = 0; l < NL; l++) {
       const DitLayer& Ly = d->layers[l];
       const float* ad = use_ad ? w.ad + (size_t)l * 6 * H : nullptr;
+      if (tc) {
+        const int SR = R * S;
+        PrepArgs pq; pq.x = w.seq; pq.x_ld = H; pq.y = w.xb; pq.y_ld = H; pq.M = SR; pq.K = H;
+        pq.norm_w = Ly.norm1; pq.eps = c.rms_eps;
+        if (ad) { pq.mod = ad; pq.mod_ld = adld; pq.mod_div = S; pq.mod_shift = 0; pq.mod_scale = H; }
+        CTTS_CK(launch_prep_bf16(pq, s)); nl++;
+        TcArgs eq; eq.y = w.qkv; eq.y_ld = qkvw;
+        RUN(tc_run(w.tc, w.xb, SR, H, Ly.wqkv, qkvw, eq, s, &nl));
+        CTTS_CK(launch_dit_attn(w.qkv, R, S, c.n_heads, c.n_kv_heads, c.head_dim, d->inv_freq, nullptr,
+                                w.attb, s)); nl++;
+        TcArgs eo; eo.y = w.seq; eo.y_ld = H; eo.res = w.seq;
+        if (ad) { eo.gate = ad; eo.gate_ld = adld; eo.gate_div = S; eo.gate_off = 2 * H; }
+        RUN(tc_run(w.tc, w.attb, SR, qd, Ly.wo, H, eo, s, &nl));
+        PrepArgs pg; pg.x = w.seq; pg.x_ld = H; pg.y = w.xb; pg.y_ld = H; pg.M = SR; pg.K = H;
+        pg.norm_w = Ly.norm2; pg.eps = c.rms_eps;
+        if (ad) { pg.mod = ad; pg.mod_ld = adld; pg.mod_div = S; pg.mod_shift = 3 * H; pg.mod_scale = 4 * H; }
+        CTTS_CK(launch_prep_bf16(pg, s)); nl++;
+        TcArgs eg; eg.act = 2; eg.yb = w.actb; eg.y_ld = F;
+        RUN(tc_run(w.tc, w.xb, SR, H, Ly.wgu, 2 * F, eg, s, &nl));
+        TcArgs ed; ed.y = w.seq; ed.y_ld = H; ed.res = w.seq;
+        if (ad) { ed.gate = ad; ed.gate_ld = adld; ed.gate_div = S; ed.gate_off = 5 * H; }
+        RUN(tc_run(w.tc, w.actb, SR, F, Ly.wd, H, ed, s, &nl));
+        continue;
+      }
       LinearArgs q; q.x = w.seq; q.x_ld = H; q.M = R * S; q.K = H; q.N = qkvw; q.w = Ly.wqkv;
       q.y = w.qkv; q.y_ld = qkvw; q.norm_w = Ly.norm1; q.eps = c.rms_eps;
       if (ad) { q.mod = ad; q.mod_ld = adld; q.mod_div = S; q.mod_shift = 0; q.mod_scale = H; }
       RUN(lin(q));
-      CTTS_CK(launch_dit_attn(w.qkv, R, S, c.n_heads, c.n_kv_heads, c.head_dim, d->inv_freq, w.att, s)); nl++;
+      CTTS_CK(launch_dit_attn(w.qkv, R, S, c.n_heads, c.n_kv_heads, c.head_dim, d->inv_freq, w.att, nullptr,
+                              s)); nl++;
       LinearArgs o; o.x = w.att; o.x_ld = qd; o.M = R * S; o.K = qd; o.N = H; o.w = Ly.wo;
       o.y = w.seq; o.y_ld = H; o.res = w.seq;
       if (ad) { o.gate = ad; o.gate_ld = adld; o.gate_div = S; o.gate_off = 2 * H; }
@@ -230,9 +278,9 @@ extern "C" int ctts_dit_create(const ctts_dit_config* cfg, int device, ctts_dit*
   CTTS_REQ(1 + 2 * c.patch <= 5, CTTS_ERR_ARG, "patch must be 1 or 2");
   CTTS_REQ(c.n_heads % c.n_kv_heads == 0, CTTS_ERR_ARG, "n_heads % n_kv_heads != 0");
   CTTS_REQ(c.head_dim % 64 == 0 && c.head_dim <= 128, CTTS_ERR_ARG, "head_dim must be 64 or 128");
-  CTTS_REQ(c.hidden % 8 == 0 && c.ffn % 8 == 0 && c.latent % 8 == 0 && c.cond_dim % 8 == 0 &&
+  CTTS_REQ(c.hidden % 64 == 0 && c.ffn % 64 == 0 && c.latent % 8 == 0 && c.cond_dim % 8 == 0 &&
                (!c.adaln || c.spk_dim % 8 == 0),
-           CTTS_ERR_ARG, "dimensions must be multiples of 8");
+           CTTS_ERR_ARG, "hidden/ffn must be multiples of 64, latent/cond/spk of 8");
   CTTS_REQ(c.weight_dtype == CTTS_F32 || c.weight_dtype == CTTS_BF16, CTTS_ERR_ARG, "bad weight dtype");
   CTTS_CK(cudaSetDevice(device));
   auto* d = new ctts_dit();
@@ -292,7 +340,12 @@ extern "C" int ctts_dit_create(const ctts_dit_config* cfg, int device, ctts_dit*
     d->slots.add(p + "self_attn.v_proj.weight", qkv + (size_t)(qd + kvd) * H * es, {kvd, H}, true);
     d->slots.add(p + "self_attn.o_proj.weight", Ly.wo, {H, qd}, true);
     d->slots.add(p + "mlp.gate_proj.weight", gu, {F, H}, true);
-    d->slots.add(p + "mlp.up_proj.weight", gu + (size_t)F * H * es, {F, H}, true);
+    d->slots.add(p + "mlp.up_proj.weight", gu + (size_t)64 * H * es, {F, H}, true);
+    for (const char* nm : {"mlp.gate_proj.weight", "mlp.up_proj.weight"}) {
+      Slot& sl = d->slots.slots[p + nm];
+      sl.transform = kXformRowInterleave;
+      sl.t_b = H;
+    }
     d->slots.add(p + "mlp.down_proj.weight", Ly.wd, {H, F}, true);
     if (c.adaln)
       d->slots.add(p + "speaker_adaln.weight",
@@ -665,7 +718,8 @@ extern "C" int ctts_engine_step(ctts_engine* e, const float* noise, float* laten
   CTTS_CK(cudaStreamSynchronize(e->stream));
   int err = 0;
   CTTS_CK(cudaMemcpy(&err, e->kv->err, sizeof(int), cudaMemcpyDeviceToHost));
-  CTTS_REQ(err == 0, CTTS_ERR_RANGE, "device reported a KV position outside capacity");
+  CTTS_REQ(err != 1, CTTS_ERR_RANGE, "device reported a KV position outside capacity");
+  CTTS_REQ(err == 0, CTTS_ERR_TIMEOUT, "a tensor-core linear gave up waiting on its pipeline");
   memcpy(latents_out, e->h_lat, sizeof(float) * B * PL);
   if (stop_out) memcpy(stop_out, e->h_stop, sizeof(float) * B * 2);
   return CTTS_OK;

@@ -56,7 +56,7 @@ extern "C" int ctts_lm_create(const ctts_lm_config* cfg, int device, ctts_lm** o
   CTTS_REQ(c.n_heads % c.n_kv_heads == 0 && c.n_heads / c.n_kv_heads <= 8, CTTS_ERR_ARG,
            "n_heads must be a multiple of n_kv_heads (group <= 8)");
   CTTS_REQ(c.head_dim % 64 == 0 && c.head_dim <= 128, CTTS_ERR_ARG, "head_dim must be 64 or 128");
-  CTTS_REQ(c.hidden % 8 == 0 && c.ffn % 8 == 0, CTTS_ERR_ARG, "hidden and ffn must be multiples of 8");
+  CTTS_REQ(c.hidden % 64 == 0 && c.ffn % 64 == 0, CTTS_ERR_ARG, "hidden and ffn must be multiples of 64");
   CTTS_REQ(c.weight_dtype == CTTS_F32 || c.weight_dtype == CTTS_BF16, CTTS_ERR_ARG, "bad weight dtype");
   CTTS_CK(cudaSetDevice(device));
   auto* lm = new ctts_lm();
@@ -99,7 +99,12 @@ extern "C" int ctts_lm_create(const ctts_lm_config* cfg, int device, ctts_lm** o
     lm->slots.add(p + "self_attn.v_proj.weight", qkv + (size_t)(qd + kvd) * H * es, {kvd, H}, true);
     lm->slots.add(p + "self_attn.o_proj.weight", L.wo, {H, qd}, true);
     lm->slots.add(p + "mlp.gate_proj.weight", gu, {F, H}, true);
-    lm->slots.add(p + "mlp.up_proj.weight", gu + (size_t)F * H * es, {F, H}, true);
+    lm->slots.add(p + "mlp.up_proj.weight", gu + (size_t)64 * H * es, {F, H}, true);
+    for (const char* nm : {"mlp.gate_proj.weight", "mlp.up_proj.weight"}) {
+      Slot& sl = lm->slots.slots[p + nm];
+      sl.transform = kXformRowInterleave;
+      sl.t_b = H;
+    }
     lm->slots.add(p + "mlp.down_proj.weight", L.wd, {H, F}, true);
   }
   std::vector<float> inv = rope_inv_freq(hd, c.rope_theta);
@@ -173,6 +178,21 @@ extern "C" int ctts_kv_alloc(const ctts_lm* lm, int batch, int capacity, ctts_kv
     delete kv;
     return set_error(CTTS_ERR_NOMEM, "KV cache allocation failed");
   }
+  if (lm->bf16) {
+    kv->xb = kv->arena.alloc<uint16_t>((size_t)rows * std::max(H, qd));
+    kv->attb = kv->arena.alloc<uint16_t>((size_t)rows * qd);
+    kv->actb = kv->arena.alloc<uint16_t>((size_t)rows * c.ffn);
+    const int qkvw = qd + 2 * kvd;
+    std::vector<std::array<int, 3>> shapes;
+    for (int m : {batch, std::min(rows, 256)})
+      for (auto nk : {std::array<int, 2>{qkvw, H}, {H, qd}, {2 * c.ffn, H}, {H, c.ffn}})
+        shapes.push_back({m, nk[0], nk[1]});
+    int rc = tc_alloc(kv->arena, &kv->tc, shapes, kv->err);
+    if (rc != CTTS_OK || !kv->xb || !kv->attb || !kv->actb) {
+      delete kv;
+      return rc != CTTS_OK ? rc : set_error(CTTS_ERR_NOMEM, "KV workspace allocation failed");
+    }
+  }
   *out = kv;
   return CTTS_OK;
 }
@@ -221,13 +241,26 @@ int lm_forward_rows(ctts_lm* lm, ctts_kv* kv, int rows, int prefill_b, int pos0,
   const int qkvw = qd + 2 * kvd, F = c.ffn;
   const size_t es = lm->bf16 ? 2 : 4;
   int nl = 0;
+  // bf16 weights with >= 16 rows: the tensor-core linears (tc_linear.cu);
+  // otherwise the CUDA-core skinny linears (linear.cu).
+  const bool tc = lm->bf16 && rows >= 16;
   for (int l = 0; l < c.n_layers; l++) {
     const LMLayer& L = lm->layers[l];
-    LinearArgs q;
-    q.x = kv->h; q.x_ld = H; q.M = rows; q.K = H; q.N = qkvw;
-    q.w = L.wqkv; q.w_bf16 = lm->bf16; q.y = kv->qkv; q.y_ld = qkvw;
-    q.norm_w = L.norm1; q.eps = c.rms_eps;
-    CTTS_CK(launch_linear(q, s)); nl++;
+    if (tc) {
+      PrepArgs pa;
+      pa.x = kv->h; pa.x_ld = H; pa.y = kv->xb; pa.y_ld = H; pa.M = rows; pa.K = H;
+      pa.norm_w = L.norm1; pa.eps = c.rms_eps;
+      CTTS_CK(launch_prep_bf16(pa, s)); nl++;
+      TcArgs e; e.y = kv->qkv; e.y_ld = qkvw;
+      int rc = tc_run(kv->tc, kv->xb, rows, H, L.wqkv, qkvw, e, s, &nl);
+      if (rc) return rc;
+    } else {
+      LinearArgs q;
+      q.x = kv->h; q.x_ld = H; q.M = rows; q.K = H; q.N = qkvw;
+      q.w = L.wqkv; q.w_bf16 = lm->bf16; q.y = kv->qkv; q.y_ld = qkvw;
+      q.norm_w = L.norm1; q.eps = c.rms_eps;
+      CTTS_CK(launch_linear(q, s)); nl++;
+    }
 
     AttnArgs a;
     a.qkv = kv->qkv; a.rows = rows; a.prefill_b = prefill_b; a.pos0 = pos0; a.pos = kv->pos;
@@ -239,11 +272,29 @@ int lm_forward_rows(ctts_lm* lm, ctts_kv* kv, int rows, int prefill_b, int pos0,
     a.kv_bf16 = lm->bf16; a.cap = kv->cap; a.batch = kv->batch;
     a.qrot = kv->qrot; a.out = kv->att; a.part = kv->part; a.nsplit = kv->nsplit; a.chunk = 128;
     a.err = kv->err;
+    if (tc) a.out_b = kv->attb;
     CTTS_CK(launch_qk_rope_append(a, s)); nl++;
     if (prefill_b >= 0) {
       CTTS_CK(launch_attn_prefill(a, s)); nl++;
     } else {
       CTTS_CK(launch_attn_decode(a, s)); nl += 2;
+    }
+
+    if (tc) {
+      TcArgs e; e.y = kv->h; e.y_ld = H; e.res = kv->h;
+      int rc = tc_run(kv->tc, kv->attb, rows, qd, L.wo, H, e, s, &nl);
+      if (rc) return rc;
+      PrepArgs pa;
+      pa.x = kv->h; pa.x_ld = H; pa.y = kv->xb; pa.y_ld = H; pa.M = rows; pa.K = H;
+      pa.norm_w = L.norm2; pa.eps = c.rms_eps;
+      CTTS_CK(launch_prep_bf16(pa, s)); nl++;
+      TcArgs g; g.act = 2; g.yb = kv->actb; g.y_ld = F;
+      rc = tc_run(kv->tc, kv->xb, rows, H, L.wgu, 2 * F, g, s, &nl);
+      if (rc) return rc;
+      TcArgs d; d.y = kv->h; d.y_ld = H; d.res = kv->h;
+      rc = tc_run(kv->tc, kv->actb, rows, F, L.wd, H, d, s, &nl);
+      if (rc) return rc;
+      continue;
     }
 
     LinearArgs o;
@@ -342,7 +393,8 @@ extern "C" int ctts_lm_decode_step(ctts_lm* lm, ctts_kv* kv, const float* x, flo
   CTTS_CK(cudaStreamSynchronize(lm->stream));
   int err = 0;
   CTTS_CK(cudaMemcpy(&err, kv->err, sizeof(int), cudaMemcpyDeviceToHost));
-  CTTS_REQ(err == 0, CTTS_ERR_RANGE, "device reported a KV position outside capacity");
+  CTTS_REQ(err != 1, CTTS_ERR_RANGE, "device reported a KV position outside capacity");
+  CTTS_REQ(err == 0, CTTS_ERR_TIMEOUT, "a tensor-core linear gave up waiting on its pipeline");
   CTTS_CK(cudaMemcpy(out, kv->xout, n * 4, cudaMemcpyDeviceToHost));
   return CTTS_OK;
 }
@@ -375,15 +427,70 @@ extern "C" int ctts_lm_embed_lookup(ctts_lm* lm, const int64_t* ids, int n, floa
 
 // -------------------------------------------------------------- op level
 
+namespace {
+
+// Per-device workspace of the op-level tensor-core linear (bf16 operand +
+// split-K scratch), grown on demand.
+struct OpTcWs {
+  size_t xb_elems = 0, part = 0;
+  int counters = 0;
+  DevArena* arena = nullptr;
+  uint16_t* xb = nullptr;
+  TcScratch tc;
+  int* err = nullptr;
+};
+
+int op_tc_ws(int M, int N, int K, OpTcWs** out) {
+  static thread_local std::unordered_map<int, OpTcWs> wss;
+  int dev = 0;
+  CTTS_CK(cudaGetDevice(&dev));
+  OpTcWs& w = wss[dev];
+  int cnt = 0;
+  size_t need = tc_scratch_need({{M, N, K}}, 64, &cnt);
+  if (!w.arena || (size_t)M * K > w.xb_elems || need > w.part || cnt > w.counters) {
+    CTTS_CK(cudaDeviceSynchronize());
+    delete w.arena;
+    w.arena = new DevArena();
+    w.xb_elems = std::max((size_t)M * K, w.xb_elems);
+    w.part = std::max(need, w.part);
+    w.counters = std::max(cnt, w.counters);
+    w.xb = w.arena->alloc<uint16_t>(w.xb_elems);
+    w.err = w.arena->alloc<int>(1);
+    w.tc.part = w.arena->alloc<float>(std::max<size_t>(w.part, 1));
+    w.tc.part_floats = w.part;
+    w.tc.counters = w.arena->alloc<int>(std::max(w.counters, 1));
+    w.tc.ncounters = w.counters;
+    w.tc.err = w.err;
+    if (!w.xb || !w.tc.part || !w.tc.counters) return set_error(CTTS_ERR_NOMEM, "op workspace");
+  }
+  *out = &w;
+  return CTTS_OK;
+}
+
+}  // namespace
+
 extern "C" int ctts_op_linear(const float* x, int M, int K, const void* w, int w_dtype, int N,
                               const float* norm_w, float eps, const float* res, float* y,
                               void* stream) {
   CTTS_REQ(x && w && y && M >= 0 && K > 0 && N > 0, CTTS_ERR_ARG, "bad argument");
   CTTS_REQ(K % (w_dtype == CTTS_BF16 ? 8 : 4) == 0, CTTS_ERR_ARG, "K must be a multiple of 4 (f32) / 8 (bf16)");
+  cudaStream_t s = as_stream(stream, 0);
+  if (w_dtype == CTTS_BF16 && M >= 16 && K % 64 == 0) {
+    // bf16 weights and a batch of rows: tcgen05 tensor cores, the activation
+    // is normalized and rounded to bf16 first
+    OpTcWs* ws = nullptr;
+    int rc = op_tc_ws(M, N, K, &ws);
+    if (rc) return rc;
+    PrepArgs pa;
+    pa.x = x; pa.x_ld = K; pa.y = ws->xb; pa.y_ld = K; pa.M = M; pa.K = K; pa.norm_w = norm_w; pa.eps = eps;
+    CTTS_CK(launch_prep_bf16(pa, s));
+    TcArgs e; e.y = y; e.y_ld = N; e.res = res;
+    return tc_run(ws->tc, ws->xb, M, K, w, N, e, s, nullptr);
+  }
   LinearArgs a;
   a.x = x; a.x_ld = K; a.M = M; a.K = K; a.N = N; a.w = w; a.w_bf16 = w_dtype == CTTS_BF16;
   a.y = y; a.y_ld = N; a.norm_w = norm_w; a.eps = eps; a.res = res;
-  CTTS_CK(launch_linear(a, as_stream(stream, 0)));
+  CTTS_CK(launch_linear(a, s));
   return CTTS_OK;
 }
 

@@ -251,7 +251,11 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
     L = fmaf(ps[1], w, L);
     acc = fmaf(ps[2 + d], w, acc);
   }
-  a.out[(size_t)b * a.nq * hd + h * hd + d] = acc / L;
+  const size_t o = (size_t)b * a.nq * hd + h * hd + d;
+  if (a.out_b)
+    a.out_b[o] = f2bf(acc / L);
+  else
+    a.out[o] = acc / L;
 }
 
 // causal prefill attention: grid (T, nq), 128 threads, dyn smem n floats
@@ -304,7 +308,11 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnArgs a) {
   __syncthreads();
   if (pp == 0) {
     for (int p2 = 1; p2 < parts; p2++) acc += accs[p2 * hd + d];
-    a.out[(size_t)i * nq * hd + h * hd + d] = acc / L;
+    const size_t o = (size_t)i * nq * hd + h * hd + d;
+    if (a.out_b)
+      a.out_b[o] = f2bf(acc / L);
+    else
+      a.out[o] = acc / L;
   }
 }
 

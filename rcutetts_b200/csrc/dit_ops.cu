@@ -21,7 +21,7 @@ constexpr int kPer = 4;  // head_dim <= 128
 
 __global__ void __launch_bounds__(32) dit_attn_kernel(const float* qkv, int S, int nq, int nkv,
                                                       int hd, const float* inv_freq,
-                                                      float* out) {
+                                                      float* out, uint16_t* out_b) {
   grid_dep_wait();
   const int b = blockIdx.x, h = blockIdx.y, lane = threadIdx.x;
   const int G = nq / nkv, kh = h / G;
@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(32) dit_attn_kernel(const float* qkv, int S, i
       l += sc[j2];
     }
     const float inv = 1.0f / l;
-    float* orow = out + (size_t)(b * S + i) * nq * hd + h * hd;
+    const size_t obase = (size_t)(b * S + i) * nq * hd + h * hd;
 #pragma unroll
     for (int j = 0; j < kPer; j++) {
       if (j >= per) break;
@@ -89,7 +89,10 @@ __global__ void __launch_bounds__(32) dit_attn_kernel(const float* qkv, int S, i
         if (j2 >= S) break;
         acc = fmaf(sc[j2] * inv, v[j2][j], acc);
       }
-      orow[lane + 32 * j] = acc;
+      if (out_b)
+        out_b[obase + lane + 32 * j] = f2bf(acc);
+      else
+        out[obase + lane + 32 * j] = acc;
     }
   }
 }
@@ -158,9 +161,9 @@ cudaError_t launch_add_rows(float* x, int R, int H, const float* v, cudaStream_t
 }
 
 cudaError_t launch_dit_attn(const float* qkv, int B, int S, int nq, int nkv, int hd,
-                            const float* inv_freq, float* out, cudaStream_t s) {
+                            const float* inv_freq, float* out, uint16_t* out_b, cudaStream_t s) {
   if (S > kMaxS || hd % 64 != 0 || hd > 32 * kPer || nq % nkv) return cudaErrorInvalidValue;
-  dit_attn_kernel<<<dim3(B, nq), 32, 0, s>>>(qkv, S, nq, nkv, hd, inv_freq, out);
+  dit_attn_kernel<<<dim3(B, nq), 32, 0, s>>>(qkv, S, nq, nkv, hd, inv_freq, out, out_b);
   return cudaGetLastError();
 }
 

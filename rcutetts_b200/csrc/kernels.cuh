@@ -10,17 +10,19 @@ namespace ctts {
 // y[m, n] = epi( sum_k pro(x)[m, k] * W[n, k] )
 // Row addressing (x, y and res): row m lives at
 //   base + (m / div) * ld_outer + (m % div) * ld
-// so a linear can read or write every S-th token of a packed sequence.
+// so a linear can read or write every S-th token of a packed sequence.  The
+// default div (kNoDiv) makes it plain row-major: base + m * ld.
+constexpr int kNoDiv = 1 << 30;
 struct LinearArgs {
   const float* x = nullptr;
   long x_ld = 0, x_ld_outer = 0;
-  int x_div = 1;
+  int x_div = kNoDiv;
   const void* w = nullptr;  // [N (2N for swiglu), K], f32 or bf16 bits
   int w_bf16 = 0;
   const float* bias = nullptr;  // [N (2N)] or null
   float* y = nullptr;
   long y_ld = 0, y_ld_outer = 0;
-  int y_div = 1;
+  int y_div = kNoDiv;
   int M = 0, N = 0, K = 0;
   // prologue: RMSNorm (norm_w != null) then AdaLN modulate (mod != null):
   //   v = v * (1 + mod[b*mod_ld + mod_scale + k]) + mod[b*mod_ld + mod_shift + k], b = m / mod_div
@@ -31,7 +33,7 @@ struct LinearArgs {
   int mod_div = 1, mod_shift = 0, mod_scale = 0;
   // epilogue: val = act(acc + bias); y = (res ? res[m,n] : 0) + coef * val
   //   coef = gate ? 1 + gate[(m / gate_div) * gate_ld + gate_off + n] : scale
-  int act = 0;  // 0 none, 1 silu, 2 swiglu (W rows [0,N) gate, [N,2N) up)
+  int act = 0;  // 0 none, 1 silu, 2 swiglu (W rows in 128-row groups: 64 gate, 64 up)
   const float* res = nullptr;
   const float* gate = nullptr;
   long gate_ld = 0;
@@ -41,6 +43,22 @@ struct LinearArgs {
 };
 
 cudaError_t launch_linear(const LinearArgs& a, cudaStream_t s);
+
+// bf16 activation operand for the tensor-core linears:
+// y[m, k] = bf16( RMSNorm(x[m]) (norm_w != null) then AdaLN modulate (mod != null) )
+struct PrepArgs {
+  const float* x = nullptr;
+  long x_ld = 0;
+  uint16_t* y = nullptr;
+  long y_ld = 0;
+  int M = 0, K = 0;
+  const float* norm_w = nullptr;
+  float eps = 1e-6f;
+  const float* mod = nullptr;
+  long mod_ld = 0;
+  int mod_div = 1, mod_shift = 0, mod_scale = 0;
+};
+cudaError_t launch_prep_bf16(const PrepArgs& a, cudaStream_t s);
 // Number of CTAs launch_linear would use (for reporting).
 int linear_grid_ctas(const LinearArgs& a);
 
@@ -63,7 +81,8 @@ struct AttnArgs {
   int cap = 0;
   int batch = 0;
   float* qrot = nullptr;  // [rows, nq*hd] rotated queries
-  float* out = nullptr;   // [rows, nq*hd] attention output
+  float* out = nullptr;   // [rows, nq*hd] attention output (fp32) ...
+  uint16_t* out_b = nullptr;  // ... or bf16 when set
   float* part = nullptr;  // split partials [batch][nq][nsplit][hd+2]
   int nsplit = 0, chunk = 0;
   int* err = nullptr;     // device error flag (capacity overflow)
@@ -87,7 +106,7 @@ cudaError_t launch_swiglu(const float* gu, int M, int F, float* out, cudaStream_
 // attention over each utterance's S-token sequence (bidirectional, RoPE
 // positions 0..S-1): qkv [B*S, (nq + 2nkv)*hd] -> out [B*S, nq*hd]
 cudaError_t launch_dit_attn(const float* qkv, int B, int S, int nq, int nkv, int hd,
-                            const float* inv_freq, float* out, cudaStream_t s);
+                            const float* inv_freq, float* out, uint16_t* out_b, cudaStream_t s);
 // rows r: out[r, :] = SinusoidalPosEmb(t[r]) (dim H)
 cudaError_t launch_sin_emb(const float* t, int rows, int H, float* out, cudaStream_t s);
 // seq[b, 0, :] = mu[b] + temb + dtemb ; seq[b, 1..P, :] = condh[b*P..]

@@ -94,9 +94,14 @@ __global__ void __launch_bounds__(kWarps * 32) linear_rows_kernel(const LinearAr
       if (SWIGLU) acc2[r][m] = 0.0f;
     }
 
+  // SwiGLU weights are stored tile-interleaved (64 gate rows, then the 64
+  // matching up rows): gate row n sits at (n/64)*128 + n%64, up at +64.
   int nr[RPW];
 #pragma unroll
-  for (int r = 0; r < RPW; r++) nr[r] = min(n0 + r, a.N - 1);
+  for (int r = 0; r < RPW; r++) {
+    const int n = min(n0 + r, a.N - 1);
+    nr[r] = SWIGLU ? (n >> 6) * 128 + (n & 63) : n;
+  }
 
 #pragma unroll 2
   for (int k = lane * VEC; k < K; k += 32 * VEC) {
@@ -105,7 +110,7 @@ __global__ void __launch_bounds__(kWarps * 32) linear_rows_kernel(const LinearAr
 #pragma unroll
     for (int r = 0; r < RPW; r++) {
       WVec<BF16>::load(a.w, (size_t)nr[r] * K + k, wv[r]);
-      if (SWIGLU) WVec<BF16>::load(a.w, (size_t)(nr[r] + a.N) * K + k, wu[r]);
+      if (SWIGLU) WVec<BF16>::load(a.w, (size_t)(nr[r] + 64) * K + k, wu[r]);
     }
 #pragma unroll
     for (int m = 0; m < MT; m++) {
@@ -140,9 +145,9 @@ __global__ void __launch_bounds__(kWarps * 32) linear_rows_kernel(const LinearAr
       if (((r * MT + m) & 31) != lane) continue;
       const int n = n0 + r, mm = m0 + m;
       if (n >= a.N || m >= mt) continue;
-      float val = acc[r][m] + (a.bias ? a.bias[n] : 0.0f);
+      float val = acc[r][m] + (a.bias ? a.bias[SWIGLU ? nr[r] : n] : 0.0f);
       if (SWIGLU) {
-        float u = acc2[r][m] + (a.bias ? a.bias[a.N + n] : 0.0f);
+        float u = acc2[r][m] + (a.bias ? a.bias[nr[r] + 64] : 0.0f);
         val = silu(val) * u;
       } else if (a.act == 1) {
         val = silu(val);
@@ -154,6 +159,30 @@ __global__ void __launch_bounds__(kWarps * 32) linear_rows_kernel(const LinearAr
       if (a.res) out = row_in(a.res, mm, a.y_div, a.y_ld, a.y_ld_outer)[n] + out;
       yr[n] = out;
     }
+  }
+}
+
+// One warp per row: y = bf16( modulate( RMSNorm(x) ) ), the tensor-core
+// path's activation operand.
+__global__ void __launch_bounds__(128) prep_bf16_kernel(const PrepArgs a) {
+  grid_dep_wait();
+  const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= a.M) return;
+  const float* xr = a.x + (long)row * a.x_ld;
+  float inv = 1.0f;
+  if (a.norm_w) {
+    float ss = 0.0f;
+    for (int k = lane; k < a.K; k += 32) ss = fmaf(xr[k], xr[k], ss);
+    ss = warp_sum(ss);
+    inv = 1.0f / sqrtf(ss / (float)a.K + a.eps);
+  }
+  const float* md = a.mod ? a.mod + (long)(row / a.mod_div) * a.mod_ld : nullptr;
+  uint16_t* yr = a.y + (long)row * a.y_ld;
+  for (int k = lane; k < a.K; k += 32) {
+    float v = xr[k];
+    if (a.norm_w) v = v * inv * a.norm_w[k];
+    if (md) v = v * (1.0f + md[a.mod_scale + k]) + md[a.mod_shift + k];
+    yr[k] = f2bf(v);
   }
 }
 
@@ -214,6 +243,12 @@ int linear_grid_ctas(const LinearArgs& a) {
   int mt = pick_mt(a.M);
   int rpw = pick_rpw(a, mt);
   return ((a.N + kWarps * rpw - 1) / (kWarps * rpw)) * ((a.M + mt - 1) / mt);
+}
+
+cudaError_t launch_prep_bf16(const PrepArgs& a, cudaStream_t s) {
+  if (a.M <= 0) return cudaSuccess;
+  prep_bf16_kernel<<<(a.M + 3) / 4, 128, 0, s>>>(a);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_linear(const LinearArgs& a, cudaStream_t s) {

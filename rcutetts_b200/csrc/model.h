@@ -41,6 +41,9 @@ struct ctts_kv {
   std::vector<int> pos_host;
   float *h = nullptr, *qkv = nullptr, *qrot = nullptr, *att = nullptr, *act = nullptr,
         *part = nullptr, *xin = nullptr, *xout = nullptr;
+  // tensor-core path (bf16 models, >= 16 rows): bf16 operands + split-K scratch
+  uint16_t *xb = nullptr, *attb = nullptr, *actb = nullptr;
+  ctts::TcScratch tc;
 };
 
 // DiT head (replaces DitW, dit.rs:27-68).
@@ -56,6 +59,9 @@ struct DitWs {  // workspace for `rows` utterance-branches
         *ad = nullptr, *condh = nullptr, *temb = nullptr, *dtemb = nullptr, *tmp = nullptr,
         *se = nullptr, *tv = nullptr, *x = nullptr, *v = nullptr, *z = nullptr,
         *cond = nullptr, *spk = nullptr, *hbuf = nullptr, *stemb = nullptr;
+  uint16_t *xb = nullptr, *attb = nullptr, *actb = nullptr;
+  ctts::TcScratch tc;
+  int* err = nullptr;
 };
 
 struct ctts_dit {

@@ -1,0 +1,434 @@
+// tc_linear.cu -- bf16 linear layers on the 5th-generation tensor cores
+// (tcgen05.mma with the accumulator in TMEM, operands staged by TMA).
+//
+// Replaces the packed SGEMM for batched decode (gemm.rs:45-291 sgemm_bias,
+// simd.rs:256-270 micro_8x8) when weights are bf16 and the batch has >= 16
+// rows.  Swap-AB: the weight matrix W[N, K] is the MMA's A operand (128
+// weight rows per CTA on the MMA M side) and the activations X[M, K] the B
+// operand (the batch on the MMA N side, 16..256), so D[n, m] = sum_k W[n,k]
+// X[m,k] lives in TMEM with one weight row per TMEM lane.
+//
+// Pipeline per CTA (128 threads): thread 0 issues TMA loads of 64-wide K
+// blocks of W and X into an S-stage shared-memory ring (128-byte swizzle),
+// thread 32 issues four K=16 MMAs per block and commits each stage back to
+// the producer, then all four warps read the accumulator with tcgen05.ld
+// (warp w owns TMEM lanes 32w..32w+31).  The K range is split over
+// `splitk` CTAs per 128-row tile when the tile count alone cannot fill the
+// GPU; partial tiles go to a scratch buffer and the last CTA of a tile (an
+// atomic ticket) sums them in split order -- deterministic -- and runs the
+// epilogue: bias, SwiGLU (tile rows 0..63 gate, 64..127 up), AdaLN gate,
+// residual, fp32 or bf16 output.
+//
+// Every wait on an mbarrier is bounded; on timeout the CTA records an error
+// code, skips the rest of its work, releases its TMEM and returns.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "tc_linear.cuh"
+
+namespace ctts {
+
+namespace {
+
+constexpr int kBK = 64;            // K elements per stage (128 bytes of bf16)
+constexpr int kTileN = 128;        // weight rows per CTA (MMA M)
+constexpr uint32_t kWaitLimit = 1u << 24;
+
+CTTS_DEV uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+CTTS_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+CTTS_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+// Bounded wait for the phase with the given parity; false on timeout.
+CTTS_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  for (uint32_t it = 0; it < kWaitLimit; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+CTTS_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// UMMA shared-memory matrix descriptor, K-major operand, 128-byte swizzle:
+// rows of 128 bytes, 8-row groups 1024 bytes apart (SBO), LBO unused (1),
+// version 1 (sm_100), layout type 2 (SWIZZLE_128B).
+CTTS_DEV uint64_t umma_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
+// Instruction descriptor: D f32, A/B bf16, both K-major, M = 128, N = nmma.
+CTTS_DEV uint32_t umma_idesc(int nmma) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(nmma >> 3) << 17) |
+         ((uint32_t)(kTileN >> 4) << 24);
+}
+
+CTTS_DEV void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+CTTS_DEV void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+CTTS_DEV void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Epilogue of one output element; `val` = accumulated sum (+bias applied
+// here).  n is the W row (for swiglu: the gate row), col the output column.
+CTTS_DEV void store_out(const TcArgs& a, int m, int col, float val) {
+  float coef = a.gate ? 1.0f + a.gate[(long)(m / a.gate_div) * a.gate_ld + a.gate_off + col] : a.scale;
+  float out = coef * val;
+  if (a.res) out += a.res[(long)m * a.y_ld + col];
+  if (a.yb)
+    a.yb[(long)m * a.y_ld + col] = f2bf(out);
+  else
+    a.y[(long)m * a.y_ld + col] = out;
+}
+
+__global__ void __launch_bounds__(128, 1)
+    tc_linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                     const TcArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzled tiles
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = a.stages;
+  const int bbytes = a.MT * 128;
+  const size_t stage_bytes = 16384 + (size_t)bbytes;
+  // barriers sit after both the stage ring and the epilogue exchange area
+  const size_t xch_bytes = (size_t)128 * (a.MT + 1) * 4;
+  const size_t region = (size_t)S * stage_bytes > xch_bytes ? (size_t)S * stage_bytes : xch_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ((region + 15) & ~size_t(15)));
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* done = bars + 2 * S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 1);
+  int* flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int n0 = tile * kTileN;
+  const int kb0 = (int)(((long)split * a.kblocks) / a.splitk);
+  const int kb1 = (int)(((long)(split + 1) * a.kblocks) / a.splitk);
+  const int nk = kb1 - kb0;
+  const uint32_t ncols = a.tmem_cols;
+
+  if (tid == 0) {
+    for (int s = 0; s < S; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(ncols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  // inputs of this kernel may be produced by the previous launch
+  grid_dep_wait();
+
+  bool ok = true;
+  if (tid == 0) {  // ---- TMA producer
+    for (int i = 0; i < nk && ok; i++) {
+      const int s = i % S;
+      if (i >= S) ok = mbar_wait(&empty[s], ((i / S) - 1) & 1);
+      if (!ok) break;
+      uint8_t* sa = smem + (size_t)s * stage_bytes;
+      mbar_expect_tx(&full[s], (uint32_t)stage_bytes);
+      tma_load_2d(sa, &tmW, (kb0 + i) * kBK, n0, &full[s]);
+      tma_load_2d(sa + 16384, &tmX, (kb0 + i) * kBK, a.m0, &full[s]);
+    }
+  } else if (tid == 32) {  // ---- MMA issuer
+    const uint32_t idesc = umma_idesc(a.MT);
+    for (int i = 0; i < nk && ok; i++) {
+      const int s = i % S;
+      ok = mbar_wait(&full[s], (i / S) & 1);
+      if (!ok) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t sa = smem_u32(smem + (size_t)s * stage_bytes);
+      const uint32_t sb = sa + 16384;
+#pragma unroll
+      for (int kk = 0; kk < kBK / 16; kk++)
+        umma_bf16(tmem, umma_desc(sa + kk * 32), umma_desc(sb + kk * 32), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+      umma_commit(&empty[s]);
+    }
+    if (ok) umma_commit(done);
+  }
+  if (!ok) atomicExch(flag, 1);
+  __syncwarp();
+
+  // ---- epilogue: every warp waits for the accumulator
+  bool have = mbar_wait(done, 0);
+  if (!have) atomicExch(flag, 1);
+  __syncthreads();
+  const bool failed = *flag != 0;
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+
+  const int r = warp * 32 + lane;  // TMEM lane = W row within the tile
+  const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+  const int mcount = min(a.MT, a.M - a.m0);
+  if (!failed) {
+    if (a.splitk == 1) {
+      float* xch = reinterpret_cast<float*>(smem);  // pipeline buffers are free now
+      const int xs = a.MT + 1;
+      for (int c0 = 0; c0 < a.MT; c0 += 16) {
+        float v[16];
+        tmem_ld16(tl + c0, v);
+        if (a.act == 2) {
+          if (r >= 64)
+#pragma unroll
+            for (int j = 0; j < 16; j++) xch[(r - 64) * xs + c0 + j] = v[j];
+          else
+#pragma unroll
+            for (int j = 0; j < 16; j++) xch[(64 + r) * xs + c0 + j] = v[j];
+        } else {
+          const int n = n0 + r;
+          if (n < a.N) {
+            const float b = a.bias ? a.bias[n] : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+              const int m = c0 + j;
+              if (m < mcount) store_out(a, a.m0 + m, n, v[j] + b);
+            }
+          }
+        }
+      }
+      if (a.act == 2) {
+        __syncthreads();
+        // thread r < 64 owns output column tile*64 + r: gate row n0 + r, up row n0 + 64 + r
+        if (r < 64) {
+          const int col = tile * 64 + r;
+          const float bg = a.bias ? a.bias[n0 + r] : 0.0f, bu = a.bias ? a.bias[n0 + 64 + r] : 0.0f;
+          for (int m = 0; m < mcount; m++) {
+            const float g = xch[(64 + r) * xs + m] + bg, u = xch[r * xs + m] + bu;
+            store_out(a, a.m0 + m, col, silu(g) * u);
+          }
+        }
+      }
+    } else {
+      // partial tile -> scratch [tile][split][MT][128]
+      float* part = a.part + (((size_t)tile * a.splitk + split) * a.MT) * kTileN;
+      for (int c0 = 0; c0 < a.MT; c0 += 16) {
+        float v[16];
+        tmem_ld16(tl + c0, v);
+#pragma unroll
+        for (int j = 0; j < 16; j++) __stcg(&part[(size_t)(c0 + j) * kTileN + r], v[j]);
+      }
+      __threadfence();
+      __syncthreads();
+      __shared__ int last;
+      if (tid == 0) last = atomicAdd(&a.counters[tile], 1) == a.splitk - 1;
+      __syncthreads();
+      if (last) {
+        __threadfence();
+        const float* pt = a.part + ((size_t)tile * a.splitk * a.MT) * kTileN;
+        const size_t sstride = (size_t)a.MT * kTileN;
+        if (a.act == 2) {
+          if (r < 64) {
+            const int col = tile * 64 + r;
+            const float bg = a.bias ? a.bias[n0 + r] : 0.0f, bu = a.bias ? a.bias[n0 + 64 + r] : 0.0f;
+            for (int m = 0; m < mcount; m++) {
+              float g = 0.0f, u = 0.0f;
+              for (int s = 0; s < a.splitk; s++) {
+                g += __ldcg(&pt[s * sstride + (size_t)m * kTileN + r]);
+                u += __ldcg(&pt[s * sstride + (size_t)m * kTileN + 64 + r]);
+              }
+              store_out(a, a.m0 + m, col, silu(g + bg) * (u + bu));
+            }
+          }
+        } else {
+          const int n = n0 + r;
+          if (n < a.N) {
+            const float b = a.bias ? a.bias[n] : 0.0f;
+            for (int m = 0; m < mcount; m++) {
+              float acc = 0.0f;
+              for (int s = 0; s < a.splitk; s++) acc += __ldcg(&pt[s * sstride + (size_t)m * kTileN + r]);
+              store_out(a, a.m0 + m, n, acc + b);
+            }
+          }
+        }
+        if (tid == 0) a.counters[tile] = 0;  // ready for the next launch
+      }
+    }
+  } else if (tid == 0 && a.err) {
+    atomicExch(a.err, 2);
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
+}
+
+// ---------------------------------------------------------- host helpers
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2D bf16 tensor [rows, cols] (cols contiguous), box [box_rows, 64], SW128.
+bool make_map(CUtensorMap* m, const void* base, int rows, int cols, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+int tc_num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+TcPlan tc_plan(int M, int N, int K, int num_sms, int max_splitk) {
+  TcPlan p;
+  p.MT = ((std::min(M, 256) + 15) / 16) * 16;
+  p.mtiles = (M + p.MT - 1) / p.MT;
+  p.ntiles = (N + kTileN - 1) / kTileN;
+  p.kblocks = K / kBK;
+  const int ctas_per_split = p.ntiles * p.mtiles;
+  int sk = (2 * num_sms + ctas_per_split - 1) / ctas_per_split;
+  sk = std::min(sk, std::max(1, p.kblocks / 2));
+  p.splitk = std::max(1, std::min(std::min(sk, p.kblocks), max_splitk));
+  const int kb_per = (p.kblocks + p.splitk - 1) / p.splitk;
+  const size_t stage = 16384 + (size_t)p.MT * 128;
+  const size_t budget = 200 * 1024;
+  p.stages = std::max(1, std::min(kb_per, (int)(budget / stage)));
+  p.stages = std::min(p.stages, 8);
+  size_t pipe = (size_t)p.stages * stage;
+  size_t xch = (size_t)128 * (p.MT + 1) * 4;
+  p.smem = ((std::max(pipe, xch) + 15) & ~size_t(15)) + 1024 /*align*/ + 8 * (2 * p.stages + 1) + 16;
+  int cols = 32;
+  while (cols < p.MT) cols <<= 1;
+  p.tmem_cols = cols;
+  return p;
+}
+
+size_t tc_scratch_floats(const TcPlan& p) {
+  return p.splitk > 1 ? (size_t)p.ntiles * p.splitk * p.MT * kTileN * p.mtiles : 0;
+}
+
+cudaError_t launch_tc_linear(const TcCall& c, cudaStream_t s) {
+  if (c.K % kBK != 0 || c.M <= 0 || c.N <= 0) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(c.w) & 15) || (reinterpret_cast<uintptr_t>(c.x) & 15))
+    return cudaErrorInvalidValue;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(tc_linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  TcPlan p = tc_plan(c.M, c.N, c.K, tc_num_sms(), c.max_splitk);
+  if (p.splitk > 1 && (!c.part || !c.counters || c.part_floats < tc_scratch_floats(p) ||
+                       c.counter_count < p.ntiles * p.mtiles))
+    return cudaErrorInvalidValue;
+  CUtensorMap tmW, tmX;
+  if (!make_map(&tmW, c.w, c.N, c.K, kTileN)) return cudaErrorInvalidValue;
+  if (!make_map(&tmX, c.x, c.M, c.K, p.MT)) return cudaErrorInvalidValue;
+  for (int mt = 0; mt < p.mtiles; mt++) {
+    TcArgs a = c.epi;
+    a.M = c.M;
+    a.N = c.N;
+    a.m0 = mt * p.MT;
+    a.MT = p.MT;
+    a.kblocks = p.kblocks;
+    a.splitk = p.splitk;
+    a.stages = p.stages;
+    a.tmem_cols = p.tmem_cols;
+    a.part = c.part + (size_t)mt * p.ntiles * p.splitk * p.MT * kTileN;
+    a.counters = c.counters + mt * p.ntiles;
+    a.err = c.err;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.ntiles, p.splitk, 1);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = c.pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, tc_linear_kernel, tmW, tmX, a);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace ctts

@@ -81,3 +81,17 @@ def test_distill_embeddings_vs_oracle():
     for b in range(2):
         ref = o.euler_sample(x0[b], z[b], c[b], spk[b], 4, cfg_w=2.0)
         assert rel_err(x[b], ref) < 1e-4
+
+
+def test_bf16_tensor_core_batch_vs_oracle():
+    """48 sequence rows (16 utterances x 3 tokens): tcgen05 linears incl. the
+    AdaLN projection, gated residual epilogues and the SwiGLU tile pairing."""
+    cfg = DiTConfig()
+    m, w = dit_model(cfg, seed=18, dtype="bf16")
+    o = orc.DiT(cfg, bf16_weights(w))
+    B = 16
+    x0, z, c = rnd(20, (B, 64)), rnd(21, (B, 768)), rnd(22, (B, 64))
+    x = m.euler_sample(x0, z, c, z, 10)
+    for b in range(B):
+        ref = o.euler_sample(x0[b], z[b], c[b], z[b], 10)
+        assert cosine(x[b], ref) >= 0.999, b

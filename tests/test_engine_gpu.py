@@ -101,3 +101,27 @@ def test_step_requires_prefill():
     with pytest.raises(CttsError) as e:
         eng.step(rnd(3, (2, 64)))
     assert e.value.code == ERR_STATE
+
+
+def test_batched_bf16_tensor_core_path_vs_oracle():
+    """16 utterances: the LM decode step and the DiT linears run on the
+    tcgen05 tensor cores (>= 16 rows); prefill rows too."""
+    lcfg, dcfg = LMConfig(n_layers=2), DiTConfig(n_layers=2)
+    B = 16
+    eng, keep, lw, dw, hw = build(lcfg, dcfg, seed=6, dtype="bf16", batch=B, capacity=64)
+    rng = np.random.default_rng(6)
+    lwb, dwb = bf16_weights(lw), bf16_weights(dw)
+    pres, conds = [], []
+    for b in range(B):
+        ids = rng.integers(0, lcfg.vocab, 10 + (7 * b) % 23)
+        prompt = rng.standard_normal((6, 64), dtype=np.float32)
+        pres.append(prefix_rows(lwb, hw, ids, prompt))
+        conds.append(prompt[-1])
+        eng.prefill(b, pres[-1], conds[-1])
+    noise = rng.standard_normal((3, B, 64), dtype=np.float32)
+    lat = np.stack([eng.step(noise[f])[0] for f in range(3)])
+    lm_o, dit_o = orc.LM(lcfg, lwb), orc.DiT(dcfg, dwb)
+    for b in range(B):
+        ref, _, _ = orc.generate(lm_o, dit_o, hw, pres[b], noise[:, b, :], conds[b], 10)
+        for f in range(3):
+            assert cosine(lat[f, b], ref[f]) >= 0.999, (b, f)

@@ -158,3 +158,23 @@ def test_safetensors_loader(tmp_path):
     a = prefill(m2, x, QwenCache(m2, 1, 8))
     b = prefill(m3, x, QwenCache(m3, 1, 8))
     assert np.array_equal(a, b)
+
+
+def test_tensor_core_decode_batch16():
+    """Batched decode with 16 utterances uses the tcgen05 linears."""
+    from rcutetts_b200.model import QwenCache, decode_step, prefill
+
+    cfg = LMConfig(n_layers=2)
+    m, w = lm_model(cfg, seed=10, dtype="bf16")
+    wo = bf16_weights(w)
+    B = 16
+    cache = QwenCache(m, batch=B, capacity=48)
+    pre = [rnd(100 + b, (3 + b, cfg.hidden)) for b in range(B)]
+    for b in range(B):
+        prefill(m, pre[b], cache, b)
+    dec = rnd(200, (3, B, cfg.hidden))
+    outs = [decode_step(m, dec[s], cache) for s in range(3)]
+    for b in range(B):
+        ref = run_oracle(cfg, wo, pre[b], dec[:, b, :], capacity=48)[3 + b:]
+        for s in range(3):
+            assert cosine(outs[s][b], ref[s]) >= 0.999, (b, s)

@@ -6,7 +6,7 @@ import ctypes as C
 import numpy as np
 import pytest
 
-from conftest import rel_err
+from conftest import cosine, rel_err
 from helpers import rnd
 from oracle import oracle as orc
 from rcutetts_b200 import synth
@@ -46,7 +46,13 @@ def test_linear_rmsnorm_residual(M, KN, dtype):
     assert rc == 0
     torch.cuda.synchronize()
     ref = orc.linear(orc.rms_norm(x, g, 1e-6), W) + res
-    assert rel_err(y.cpu().numpy(), ref) < 1e-4
+    got = y.cpu().numpy()
+    if dtype == "bf16" and M >= 16:
+        # tensor-core path: activations rounded to bf16 for the MMA
+        assert cosine(got - res, ref - res) >= 0.9999
+        assert rel_err(got, ref) < 1e-2
+    else:
+        assert rel_err(got, ref) < 1e-4
 
 
 def test_rope_positions_0_4095():
