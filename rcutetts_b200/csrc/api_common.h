@@ -23,11 +23,15 @@ namespace ctts {
 
 int set_error(int code, const std::string& msg);
 
+// On failure the runtime's last-error slot is cleared too, so a
+// non-sticky error cannot resurface in a later, unrelated launch check.
 #define CTTS_CK(call)                                                                   \
   do {                                                                                  \
     cudaError_t _e = (call);                                                            \
-    if (_e != cudaSuccess)                                                              \
+    if (_e != cudaSuccess) {                                                            \
+      (void)cudaGetLastError();                                                         \
       return ::ctts::set_error(CTTS_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(_e)); \
+    }                                                                                   \
   } while (0)
 
 #define CTTS_REQ(cond, code, msg)                       \
@@ -59,7 +63,9 @@ struct DevArena {
   T* alloc(size_t n) {
     void* p = nullptr;
     if (cudaMalloc(&p, n * sizeof(T) + 16) != cudaSuccess) return nullptr;
+    // zeroed before any stream (blocking or not) can touch it
     cudaMemset(p, 0, n * sizeof(T) + 16);
+    cudaStreamSynchronize(cudaStreamLegacy);
     ptrs.push_back(p);
     return reinterpret_cast<T*>(p);
   }
@@ -141,6 +147,9 @@ inline int upload_f32(const Slot& s, const float* data, size_t n, int model_bf16
   } else {
     CTTS_CK(cudaMemcpy(s.dst, src, n * es, cudaMemcpyHostToDevice));
   }
+  // a pageable-source copy may return before its DMA lands; the handle's
+  // kernels run on non-blocking streams, so wait for it here
+  CTTS_CK(cudaStreamSynchronize(cudaStreamLegacy));
   return CTTS_OK;
 }
 
@@ -203,7 +212,10 @@ inline int tc_run(const TcScratch& sc, const uint16_t* x, int M, int K, const vo
     c.max_splitk = std::max(1, p.splitk / 2);
   }
   cudaError_t e = launch_tc_linear(c, s);
-  if (e != cudaSuccess) return set_error(CTTS_ERR_CUDA, std::string("tc_linear: ") + cudaGetErrorString(e));
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return set_error(CTTS_ERR_CUDA, std::string("tc_linear: ") + cudaGetErrorString(e));
+  }
   if (nl) *nl += tc_plan(M, N, K, tc_num_sms(), c.max_splitk).mtiles;
   return CTTS_OK;
 }

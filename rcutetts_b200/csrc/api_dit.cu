@@ -91,7 +91,10 @@ int dit_enqueue(ctts_dit* d, const DitRun& r, cudaStream_t s, int* launches) {
   auto lin = [&](LinearArgs a) -> int {
     a.w_bf16 = bf;
     cudaError_t e = launch_linear(a, s);
-    if (e != cudaSuccess) return set_error(CTTS_ERR_CUDA, std::string("linear: ") + cudaGetErrorString(e));
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      return set_error(CTTS_ERR_CUDA, std::string("linear: ") + cudaGetErrorString(e));
+    }
     nl++;
     return CTTS_OK;
   };
@@ -357,7 +360,8 @@ extern "C" int ctts_dit_create(const ctts_dit_config* cfg, int device, ctts_dit*
   std::vector<float> inv = rope_inv_freq(hd, c.rope_theta);
   d->inv_freq = A.alloc<float>(hd / 2);
   if (!d->final_norm || !d->inv_freq ||
-      cudaMemcpy(d->inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+      cudaMemcpy(d->inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaStreamSynchronize(cudaStreamLegacy) != cudaSuccess) {
     delete d;
     return set_error(CTTS_ERR_NOMEM, "device allocation failed");
   }
@@ -404,8 +408,9 @@ extern "C" int ctts_sway_timesteps(int steps, float coeff, float* out) {
 
 namespace {
 
-int copy_in(float* dst, const float* src, size_t n) {
-  CTTS_CK(cudaMemcpy(dst, src, n * 4, cudaMemcpyHostToDevice));
+// host -> device, ordered before the kernels later enqueued on `s`
+int copy_in(float* dst, const float* src, size_t n, cudaStream_t s) {
+  CTTS_CK(cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyHostToDevice, s));
   return CTTS_OK;
 }
 
@@ -451,10 +456,10 @@ extern "C" int ctts_dit_euler_sample(ctts_dit* d, int batch, const float* x0, co
   if (rc) return rc;
   DitWs& w = d->ws;
   const int PL = d->cfg.patch * d->cfg.latent;
-  if ((rc = copy_in(w.x, x0, (size_t)batch * PL))) return rc;
-  if ((rc = copy_in(w.z, z, (size_t)batch * d->cfg.cond_dim))) return rc;
-  if ((rc = copy_in(w.cond, cond, (size_t)batch * PL))) return rc;
-  if (spk && (rc = copy_in(w.spk, spk, (size_t)batch * d->cfg.spk_dim))) return rc;
+  if ((rc = copy_in(w.x, x0, (size_t)batch * PL, d->stream))) return rc;
+  if ((rc = copy_in(w.z, z, (size_t)batch * d->cfg.cond_dim, d->stream))) return rc;
+  if ((rc = copy_in(w.cond, cond, (size_t)batch * PL, d->stream))) return rc;
+  if (spk && (rc = copy_in(w.spk, spk, (size_t)batch * d->cfg.spk_dim, d->stream))) return rc;
   rc = ctts_dit_euler_sample_dev(d, batch, w.x, w.z, w.cond, spk ? w.spk : nullptr, steps, cfg_w, w.x,
                                  d->stream);
   if (rc) return rc;
@@ -473,10 +478,10 @@ extern "C" int ctts_dit_predict(ctts_dit* d, int batch, const float* x, float t,
   if (rc) return rc;
   DitWs& w = d->ws;
   const int PL = d->cfg.patch * d->cfg.latent;
-  if ((rc = copy_in(w.x, x, (size_t)batch * PL))) return rc;
-  if ((rc = copy_in(w.z, z, (size_t)batch * d->cfg.cond_dim))) return rc;
-  if ((rc = copy_in(w.cond, cond, (size_t)batch * PL))) return rc;
-  if (spk && (rc = copy_in(w.spk, spk, (size_t)batch * d->cfg.spk_dim))) return rc;
+  if ((rc = copy_in(w.x, x, (size_t)batch * PL, d->stream))) return rc;
+  if ((rc = copy_in(w.z, z, (size_t)batch * d->cfg.cond_dim, d->stream))) return rc;
+  if ((rc = copy_in(w.cond, cond, (size_t)batch * PL, d->stream))) return rc;
+  if (spk && (rc = copy_in(w.spk, spk, (size_t)batch * d->cfg.spk_dim, d->stream))) return rc;
   rc = dit_upload_cfg_hidden(d, cfg_w, d->stream);
   if (rc) return rc;
   float times[1] = {t};
@@ -503,13 +508,13 @@ extern "C" int ctts_dit_euler_sample_cfg(ctts_dit* d, int batch, const float* x0
   if (rc) return rc;
   DitWs& w = d->ws;
   const int PL = d->cfg.patch * d->cfg.latent, CD = d->cfg.cond_dim;
-  if ((rc = copy_in(w.x, x0, (size_t)batch * PL))) return rc;
-  if ((rc = copy_in(w.z, z_c, (size_t)batch * CD))) return rc;
-  if ((rc = copy_in(w.z + (size_t)batch * CD, z_u, (size_t)batch * CD))) return rc;
-  if ((rc = copy_in(w.cond, cond, (size_t)batch * PL))) return rc;
-  if ((rc = copy_in(w.cond + (size_t)batch * PL, uncond, (size_t)batch * PL))) return rc;
+  if ((rc = copy_in(w.x, x0, (size_t)batch * PL, d->stream))) return rc;
+  if ((rc = copy_in(w.z, z_c, (size_t)batch * CD, d->stream))) return rc;
+  if ((rc = copy_in(w.z + (size_t)batch * CD, z_u, (size_t)batch * CD, d->stream))) return rc;
+  if ((rc = copy_in(w.cond, cond, (size_t)batch * PL, d->stream))) return rc;
+  if ((rc = copy_in(w.cond + (size_t)batch * PL, uncond, (size_t)batch * PL, d->stream))) return rc;
   if (spk) {
-    if ((rc = copy_in(w.spk, spk, (size_t)batch * d->cfg.spk_dim))) return rc;
+    if ((rc = copy_in(w.spk, spk, (size_t)batch * d->cfg.spk_dim, d->stream))) return rc;
   }
   rc = dit_upload_cfg_hidden(d, cfg, d->stream);
   if (rc) return rc;
@@ -637,6 +642,7 @@ extern "C" int ctts_engine_set_heads(ctts_engine* e, const float* stop_w, const 
   CTTS_CK(cudaMemcpy(e->stop_b, stop_b, sizeof(float) * 2, cudaMemcpyHostToDevice));
   CTTS_CK(cudaMemcpy(e->proj_w, proj_w, sizeof(float) * H * PL, cudaMemcpyHostToDevice));
   CTTS_CK(cudaMemcpy(e->proj_b, proj_b, sizeof(float) * H, cudaMemcpyHostToDevice));
+  CTTS_CK(cudaStreamSynchronize(cudaStreamLegacy));
   e->heads_set = true;
   return CTTS_OK;
 }
@@ -649,7 +655,7 @@ extern "C" int ctts_engine_prefill(ctts_engine* e, int b, const float* x, int T,
   ctts_kv* kv = e->kv;
   const int H = e->lm->cfg.hidden, PL = e->dit->cfg.patch * e->dit->cfg.latent;
   CTTS_REQ(T <= kv->ws_rows, CTTS_ERR_RANGE, "prefill length outside workspace");
-  CTTS_CK(cudaMemcpy(kv->xin, x, sizeof(float) * T * H, cudaMemcpyHostToDevice));
+  CTTS_CK(cudaMemcpyAsync(kv->xin, x, sizeof(float) * T * H, cudaMemcpyHostToDevice, e->stream));
   int rc = ctts_lm_prefill_dev(e->lm, kv, b, kv->xin, T, kv->xout, e->stream);
   if (rc) return rc;
   CTTS_CK(cudaMemcpyAsync(e->z + (size_t)b * H, kv->xout + (size_t)(T - 1) * H, sizeof(float) * H,

@@ -110,7 +110,8 @@ extern "C" int ctts_lm_create(const ctts_lm_config* cfg, int device, ctts_lm** o
   std::vector<float> inv = rope_inv_freq(hd, c.rope_theta);
   lm->inv_freq = lm->arena.alloc<float>(hd / 2);
   if (!lm->embed || !lm->final_norm || !lm->inv_freq ||
-      cudaMemcpy(lm->inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+      cudaMemcpy(lm->inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaStreamSynchronize(cudaStreamLegacy) != cudaSuccess) {
     delete lm;
     return set_error(CTTS_ERR_NOMEM, "device allocation failed");
   }
@@ -200,8 +201,9 @@ extern "C" int ctts_kv_alloc(const ctts_lm* lm, int batch, int capacity, ctts_kv
 extern "C" int ctts_kv_reset(ctts_kv* kv) {
   CTTS_REQ(kv, CTTS_ERR_ARG, "null handle");
   CTTS_CK(cudaSetDevice(kv->lm->device));
-  CTTS_CK(cudaMemset(kv->pos, 0, sizeof(int) * kv->batch));
-  CTTS_CK(cudaMemset(kv->err, 0, sizeof(int)));
+  CTTS_CK(cudaMemsetAsync(kv->pos, 0, sizeof(int) * kv->batch, kv->lm->stream));
+  CTTS_CK(cudaMemsetAsync(kv->err, 0, sizeof(int), kv->lm->stream));
+  CTTS_CK(cudaStreamSynchronize(kv->lm->stream));
   std::fill(kv->pos_host.begin(), kv->pos_host.end(), 0);
   return CTTS_OK;
 }
@@ -216,7 +218,8 @@ extern "C" int ctts_kv_set_len(ctts_kv* kv, int b, int len) {
   CTTS_REQ(len >= 0 && len <= kv->cap, CTTS_ERR_RANGE, "length outside [0, capacity]");
   CTTS_CK(cudaSetDevice(kv->lm->device));
   kv->pos_host[b] = len;
-  CTTS_CK(cudaMemcpy(kv->pos + b, &len, sizeof(int), cudaMemcpyHostToDevice));
+  CTTS_CK(cudaMemcpyAsync(kv->pos + b, &len, sizeof(int), cudaMemcpyHostToDevice, kv->lm->stream));
+  CTTS_CK(cudaStreamSynchronize(kv->lm->stream));
   return CTTS_OK;
 }
 
@@ -368,7 +371,8 @@ extern "C" int ctts_lm_prefill(ctts_lm* lm, ctts_kv* kv, int b, const float* x, 
   CTTS_REQ(T > 0 && T <= kv->ws_rows, CTTS_ERR_RANGE, "prefill length outside workspace");
   CTTS_CK(cudaSetDevice(lm->device));
   const size_t n = (size_t)T * lm->cfg.hidden;
-  CTTS_CK(cudaMemcpy(kv->xin, x, n * 4, cudaMemcpyHostToDevice));
+  // stream-ordered with the kernels that consume it
+  CTTS_CK(cudaMemcpyAsync(kv->xin, x, n * 4, cudaMemcpyHostToDevice, lm->stream));
   int rc = ctts_lm_prefill_dev(lm, kv, b, kv->xin, T, kv->xout, nullptr);
   if (rc != CTTS_OK) return rc;
   CTTS_CK(cudaMemcpy(out, kv->xout, n * 4, cudaMemcpyDeviceToHost));
@@ -387,7 +391,7 @@ extern "C" int ctts_lm_decode_step(ctts_lm* lm, ctts_kv* kv, const float* x, flo
   CTTS_REQ(lm && kv && x && out, CTTS_ERR_ARG, "null argument");
   CTTS_CK(cudaSetDevice(lm->device));
   const size_t n = (size_t)kv->batch * lm->cfg.hidden;
-  CTTS_CK(cudaMemcpy(kv->xin, x, n * 4, cudaMemcpyHostToDevice));
+  CTTS_CK(cudaMemcpyAsync(kv->xin, x, n * 4, cudaMemcpyHostToDevice, lm->stream));
   int rc = ctts_lm_decode_step_dev(lm, kv, kv->xin, kv->xout, nullptr);
   if (rc != CTTS_OK) return rc;
   CTTS_CK(cudaStreamSynchronize(lm->stream));
@@ -415,7 +419,7 @@ extern "C" int ctts_lm_embed_lookup(ctts_lm* lm, const int64_t* ids, int n, floa
     cudaFree(d_ids);
     return set_error(CTTS_ERR_NOMEM, "embed scratch");
   }
-  cudaError_t e = cudaMemcpy(d_ids, ids, n * 8, cudaMemcpyHostToDevice);
+  cudaError_t e = cudaMemcpyAsync(d_ids, ids, n * 8, cudaMemcpyHostToDevice, lm->stream);
   if (e == cudaSuccess) e = launch_embed_gather(lm->embed, lm->bf16, lm->cfg.vocab, H, d_ids, n, d_out, nullptr, lm->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(lm->stream);
   if (e == cudaSuccess) e = cudaMemcpy(out, d_out, (size_t)n * H * 4, cudaMemcpyDeviceToHost);
@@ -508,6 +512,7 @@ extern "C" int ctts_op_rope(float* x, int M, int heads, int head_dim, const int*
     std::vector<float> h = rope_inv_freq(head_dim, theta);
     CTTS_CK(cudaMalloc(&inv, h.size() * 4));
     CTTS_CK(cudaMemcpy(inv, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
+    CTTS_CK(cudaStreamSynchronize(cudaStreamLegacy));
   }
   CTTS_CK(launch_rope_inplace(x, M, heads, head_dim, pos, inv, as_stream(stream, 0)));
   return CTTS_OK;

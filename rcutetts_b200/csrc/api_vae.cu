@@ -284,7 +284,7 @@ extern "C" int ctts_vae_decode_batch(ctts_vae* v, int batch, const float* latent
     v->io_lat = nl;
     v->io_wav = nw;
   }
-  CTTS_CK(cudaMemcpy(v->lat_dev, latent, nl * 4, cudaMemcpyHostToDevice));
+  CTTS_CK(cudaMemcpyAsync(v->lat_dev, latent, nl * 4, cudaMemcpyHostToDevice, v->stream));
   int rc = ctts_vae_decode_batch_dev(v, batch, v->lat_dev, T, v->wav_dev, v->stream);
   if (rc) return rc;
   CTTS_CK(cudaStreamSynchronize(v->stream));

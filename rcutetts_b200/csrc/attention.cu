@@ -36,7 +36,7 @@ CTTS_DEV void st_kv(void* base, size_t i, float v) {
 // one warp per (row, head); grid (rows, ceil((nq + 2nkv)/4)), 128 threads
 template <bool BF>
 __global__ void __launch_bounds__(128) qk_rope_append_kernel(const AttnArgs a) {
-  grid_dep_wait();
+  grid_dep_enter();
   const int row = blockIdx.x;
   const int head = blockIdx.y * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(128) qk_rope_append_kernel(const AttnArgs a) {
 // (b, q head, split): [m, l, acc[hd]].
 template <bool BF>
 __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
-  grid_dep_wait();
+  grid_dep_enter();
   const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
   const int hd = a.hd, nq = a.nq, nkv = a.nkv;
   const int G = nq / nkv;
@@ -149,6 +149,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
 #pragma unroll
     for (int g = 0; g < kMaxG; g++) s[g] = 0.0f;
     const size_t kr = kvbase + (size_t)j * hd;
+#pragma unroll 8
     for (int d = 0; d < hd; d += 8) {
       float kv[8];
       if (BF) {
@@ -205,12 +206,23 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
 #pragma unroll
   for (int g = 0; g < kMaxG; g++) acc[g] = 0.0f;
   if (pp < parts) {
-    for (int jj = r0 + pp; jj < r1; jj += parts) {
-      float vv = ld_kv<BF>(a.vcache, kvbase + (size_t)jj * hd + d);
+    // eight V rows in flight per iteration
+    for (int j0 = r0 + pp; j0 < r1; j0 += 8 * parts) {
+      float vv[8];
 #pragma unroll
-      for (int g = 0; g < kMaxG; g++) {
-        if (g >= G) break;
-        acc[g] = fmaf(sc[g][jj - r0], vv, acc[g]);
+      for (int u = 0; u < 8; u++) {
+        const int jj = j0 + u * parts;
+        vv[u] = jj < r1 ? ld_kv<BF>(a.vcache, kvbase + (size_t)jj * hd + d) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int jj = j0 + u * parts;
+        if (jj >= r1) break;
+#pragma unroll
+        for (int g = 0; g < kMaxG; g++) {
+          if (g >= G) break;
+          acc[g] = fmaf(sc[g][jj - r0], vv[u], acc[g]);
+        }
       }
     }
   }
@@ -237,7 +249,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
 
 // grid (batch, nq), hd threads
 __global__ void attn_combine_kernel(const AttnArgs a) {
-  grid_dep_wait();
+  grid_dep_enter();
   const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const int hd = a.hd;
   const float* p = a.part + ((size_t)b * a.nq + h) * a.nsplit * (hd + 2);
@@ -262,7 +274,7 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
 template <bool BF>
 __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnArgs a) {
   extern __shared__ float ps[];
-  grid_dep_wait();
+  grid_dep_enter();
   const int i = blockIdx.x, h = blockIdx.y;
   const int hd = a.hd, nq = a.nq, G = nq / a.nkv, kh = h / G;
   const int b = a.prefill_b;
@@ -317,7 +329,7 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnArgs a) {
 }
 
 __global__ void advance_pos_kernel(int* pos, int batch) {
-  grid_dep_wait();
+  grid_dep_enter();
   int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < batch) pos[b] += 1;
 }
@@ -325,11 +337,25 @@ __global__ void advance_pos_kernel(int* pos, int batch) {
 // one warp per row
 __global__ void rmsnorm_rows_kernel(const float* x, int M, int K, const float* w, float eps,
                                     float* y) {
-  grid_dep_wait();
+  grid_dep_enter();
   int row = blockIdx.x * 4 + (threadIdx.x >> 5);
   int lane = threadIdx.x & 31;
   if (row >= M) return;
   const float* xr = x + (size_t)row * K;
+  if ((K & 127) == 0 && K <= 2048) {
+    float4 v[16];
+    const float ss = warp_load_row<16>(xr, K, v);
+    const float inv = 1.0f / sqrtf(ss / (float)K + eps);
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      if (i >= (K >> 7)) break;
+      const int k = lane * 4 + 128 * i;
+      float4 o = make_float4(v[i].x * inv * w[k], v[i].y * inv * w[k + 1], v[i].z * inv * w[k + 2],
+                             v[i].w * inv * w[k + 3]);
+      *reinterpret_cast<float4*>(y + (size_t)row * K + k) = o;
+    }
+    return;
+  }
   float ss = 0.0f;
   for (int k = lane; k < K; k += 32) ss = fmaf(xr[k], xr[k], ss);
   ss = warp_sum(ss);
@@ -340,6 +366,7 @@ __global__ void rmsnorm_rows_kernel(const float* x, int M, int K, const float* w
 template <bool BF>
 __global__ void embed_gather_kernel(const void* table, int vocab, int H, const int64_t* ids,
                                     int n, float* out, int* bad) {
+  grid_dep_enter();
   int r = blockIdx.x;
   if (r >= n) return;
   int64_t id = ids[r];
@@ -354,6 +381,7 @@ __global__ void embed_gather_kernel(const void* table, int vocab, int H, const i
 
 __global__ void rope_inplace_kernel(float* x, int M, int heads, int hd, const int* pos,
                                     const float* inv_freq) {
+  grid_dep_enter();
   int m = blockIdx.x, h = blockIdx.y;
   int half = hd / 2;
   float* v = x + ((size_t)m * heads + h) * hd;
@@ -368,6 +396,7 @@ __global__ void rope_inplace_kernel(float* x, int M, int heads, int hd, const in
 }
 
 __global__ void swiglu_kernel(const float* gu, int M, int F, float* out) {
+  grid_dep_enter();
   size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (size_t)M * F) return;
   size_t m = i / F, f = i % F;
@@ -381,9 +410,9 @@ cudaError_t launch_qk_rope_append(const AttnArgs& a, cudaStream_t s) {
   if (a.hd % 64 != 0 || a.hd > kMaxHd) return cudaErrorInvalidValue;
   dim3 grid(a.rows, (a.nq + 2 * a.nkv + 3) / 4);
   if (a.kv_bf16)
-    qk_rope_append_kernel<true><<<grid, 128, 0, s>>>(a);
+    CTTS_LK(launch_k(qk_rope_append_kernel<true>, dim3(grid), dim3(128), 0, s, a));
   else
-    qk_rope_append_kernel<false><<<grid, 128, 0, s>>>(a);
+    CTTS_LK(launch_k(qk_rope_append_kernel<false>, dim3(grid), dim3(128), 0, s, a));
   return cudaGetLastError();
 }
 
@@ -393,12 +422,12 @@ cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t s) {
     return cudaErrorInvalidValue;
   dim3 grid(a.nsplit, a.nkv, a.batch);
   if (a.kv_bf16)
-    attn_decode_kernel<true><<<grid, 128, 0, s>>>(a);
+    CTTS_LK(launch_k(attn_decode_kernel<true>, dim3(grid), dim3(128), 0, s, a));
   else
-    attn_decode_kernel<false><<<grid, 128, 0, s>>>(a);
+    CTTS_LK(launch_k(attn_decode_kernel<false>, dim3(grid), dim3(128), 0, s, a));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  attn_combine_kernel<<<dim3(a.batch, a.nq), a.hd, 0, s>>>(a);
+  CTTS_LK(launch_k(attn_combine_kernel, dim3(a.batch, a.nq), dim3(a.hd), 0, s, a));
   return cudaGetLastError();
 }
 
@@ -408,20 +437,20 @@ cudaError_t launch_attn_prefill(const AttnArgs& a, cudaStream_t s) {
   if (smem > 48 * 1024) return cudaErrorInvalidValue;
   dim3 grid(a.rows, a.nq);
   if (a.kv_bf16)
-    attn_prefill_kernel<true><<<grid, 128, smem, s>>>(a);
+    CTTS_LK(launch_k(attn_prefill_kernel<true>, dim3(grid), dim3(128), smem, s, a));
   else
-    attn_prefill_kernel<false><<<grid, 128, smem, s>>>(a);
+    CTTS_LK(launch_k(attn_prefill_kernel<false>, dim3(grid), dim3(128), smem, s, a));
   return cudaGetLastError();
 }
 
 cudaError_t launch_advance_pos(int* pos, int batch, cudaStream_t s) {
-  advance_pos_kernel<<<(batch + 127) / 128, 128, 0, s>>>(pos, batch);
+  CTTS_LK(launch_k(advance_pos_kernel, dim3((batch + 127) / 128), dim3(128), 0, s, pos, batch));
   return cudaGetLastError();
 }
 
 cudaError_t launch_rmsnorm_rows(const float* x, int M, int K, const float* w, float eps,
                                 float* y, cudaStream_t s) {
-  rmsnorm_rows_kernel<<<(M + 3) / 4, 128, 0, s>>>(x, M, K, w, eps, y);
+  CTTS_LK(launch_k(rmsnorm_rows_kernel, dim3((M + 3) / 4), dim3(128), 0, s, x, M, K, w, eps, y));
   return cudaGetLastError();
 }
 
@@ -430,23 +459,23 @@ cudaError_t launch_embed_gather(const void* table, int table_bf16, int vocab, in
                                 cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   if (table_bf16)
-    embed_gather_kernel<true><<<n, 256, 0, s>>>(table, vocab, H, ids, n, out, bad);
+    CTTS_LK(launch_k(embed_gather_kernel<true>, dim3(n), dim3(256), 0, s, table, vocab, H, ids, n, out, bad));
   else
-    embed_gather_kernel<false><<<n, 256, 0, s>>>(table, vocab, H, ids, n, out, bad);
+    CTTS_LK(launch_k(embed_gather_kernel<false>, dim3(n), dim3(256), 0, s, table, vocab, H, ids, n, out, bad));
   return cudaGetLastError();
 }
 
 cudaError_t launch_rope_inplace(float* x, int M, int heads, int hd, const int* pos,
                                 const float* inv_freq, cudaStream_t s) {
   if (M <= 0) return cudaSuccess;
-  rope_inplace_kernel<<<dim3(M, heads), 64, 0, s>>>(x, M, heads, hd, pos, inv_freq);
+  CTTS_LK(launch_k(rope_inplace_kernel, dim3(M, heads), dim3(64), 0, s, x, M, heads, hd, pos, inv_freq));
   return cudaGetLastError();
 }
 
 cudaError_t launch_swiglu(const float* gu, int M, int F, float* out, cudaStream_t s) {
   size_t n = (size_t)M * F;
   if (n == 0) return cudaSuccess;
-  swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(gu, M, F, out);
+  CTTS_LK(launch_k(swiglu_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, gu, M, F, out));
   return cudaGetLastError();
 }
 

@@ -22,7 +22,7 @@ constexpr int kPer = 4;  // head_dim <= 128
 __global__ void __launch_bounds__(32) dit_attn_kernel(const float* qkv, int S, int nq, int nkv,
                                                       int hd, const float* inv_freq,
                                                       float* out, uint16_t* out_b) {
-  grid_dep_wait();
+  grid_dep_enter();
   const int b = blockIdx.x, h = blockIdx.y, lane = threadIdx.x;
   const int G = nq / nkv, kh = h / G;
   const int width = (nq + 2 * nkv) * hd;
@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(32) dit_attn_kernel(const float* qkv, int S, i
 }
 
 __global__ void sin_emb_kernel(const float* t, int H, float e, float* out) {
-  grid_dep_wait();
+  grid_dep_enter();
   const int r = blockIdx.x, half = H / 2;
   const float x = t[r];
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
@@ -111,7 +111,7 @@ __global__ void sin_emb_kernel(const float* t, int H, float e, float* out) {
 
 __global__ void seq_fill_kernel(float* seq, const float* mu, const float* temb,
                                 const float* dtemb, const float* condh, int P, int H) {
-  grid_dep_wait();
+  grid_dep_enter();
   const int b = blockIdx.x, S = 1 + 2 * P;
   float* base = seq + (size_t)b * S * H;
   for (int n = threadIdx.x; n < H; n += blockDim.x) {
@@ -121,13 +121,13 @@ __global__ void seq_fill_kernel(float* seq, const float* mu, const float* temb,
 }
 
 __global__ void affine_kernel(const float* x, int n, float scale, float bias, float* out) {
-  grid_dep_wait();
+  grid_dep_enter();
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) out[i] = x[i] / scale - bias;
 }
 
 __global__ void cfg_euler_kernel(float* x, const float* v2, int n, float cfg, float dt) {
-  grid_dep_wait();
+  grid_dep_enter();
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) {
     float vc = v2[i], vu = v2[n + i];
@@ -136,12 +136,13 @@ __global__ void cfg_euler_kernel(float* x, const float* v2, int n, float cfg, fl
 }
 
 __global__ void fill_tv_kernel(float* tv, TGrid g) {
+  grid_dep_enter();
   int i = threadIdx.x;
   if (i < g.n) tv[i] = g.t[i];
 }
 
 __global__ void add_rows_kernel(float* x, int R, int H, const float* v) {
-  grid_dep_wait();
+  grid_dep_enter();
   int r = blockIdx.x;
   for (int n = threadIdx.x; n < H; n += blockDim.x) x[(size_t)r * H + n] += v[n];
 }
@@ -150,46 +151,46 @@ __global__ void add_rows_kernel(float* x, int R, int H, const float* v) {
 
 cudaError_t launch_fill_tv(float* tv, const TGrid& g, cudaStream_t s) {
   if (g.n > TGrid::kMax) return cudaErrorInvalidValue;
-  fill_tv_kernel<<<1, TGrid::kMax, 0, s>>>(tv, g);
+  CTTS_LK(launch_k(fill_tv_kernel, dim3(1), dim3(TGrid::kMax), 0, s, tv, g));
   return cudaGetLastError();
 }
 
 cudaError_t launch_add_rows(float* x, int R, int H, const float* v, cudaStream_t s) {
   if (R <= 0) return cudaSuccess;
-  add_rows_kernel<<<R, 256, 0, s>>>(x, R, H, v);
+  CTTS_LK(launch_k(add_rows_kernel, dim3(R), dim3(256), 0, s, x, R, H, v));
   return cudaGetLastError();
 }
 
 cudaError_t launch_dit_attn(const float* qkv, int B, int S, int nq, int nkv, int hd,
                             const float* inv_freq, float* out, uint16_t* out_b, cudaStream_t s) {
   if (S > kMaxS || hd % 64 != 0 || hd > 32 * kPer || nq % nkv) return cudaErrorInvalidValue;
-  dit_attn_kernel<<<dim3(B, nq), 32, 0, s>>>(qkv, S, nq, nkv, hd, inv_freq, out, out_b);
+  CTTS_LK(launch_k(dit_attn_kernel, dim3(B, nq), dim3(32), 0, s, qkv, S, nq, nkv, hd, inv_freq, out, out_b));
   return cudaGetLastError();
 }
 
 cudaError_t launch_sin_emb(const float* t, int rows, int H, float* out, cudaStream_t s) {
   const int half = H / 2;
   const float e = (float)(std::log(10000.0) / (double)(half - 1));
-  sin_emb_kernel<<<rows, 256, 0, s>>>(t, H, e, out);
+  CTTS_LK(launch_k(sin_emb_kernel, dim3(rows), dim3(256), 0, s, t, H, e, out));
   return cudaGetLastError();
 }
 
 cudaError_t launch_dit_seq_fill(float* seq, const float* mu, const float* temb,
                                 const float* dtemb, const float* condh, int B, int P, int H,
                                 cudaStream_t s) {
-  seq_fill_kernel<<<B, 256, 0, s>>>(seq, mu, temb, dtemb, condh, P, H);
+  CTTS_LK(launch_k(seq_fill_kernel, dim3(B), dim3(256), 0, s, seq, mu, temb, dtemb, condh, P, H));
   return cudaGetLastError();
 }
 
 cudaError_t launch_affine(const float* x, int n, float scale, float bias, float* out,
                           cudaStream_t s) {
-  affine_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, n, scale, bias, out);
+  CTTS_LK(launch_k(affine_kernel, dim3((n + 255) / 256), dim3(256), 0, s, x, n, scale, bias, out));
   return cudaGetLastError();
 }
 
 cudaError_t launch_cfg_euler(float* x, const float* v2, int n, float cfg, float dt,
                              cudaStream_t s) {
-  cfg_euler_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, v2, n, cfg, dt);
+  CTTS_LK(launch_k(cfg_euler_kernel, dim3((n + 255) / 256), dim3(256), 0, s, x, v2, n, cfg, dt));
   return cudaGetLastError();
 }
 

@@ -11,6 +11,7 @@
 // shuffles.  The epilogue fuses bias, SiLU / SwiGLU, residual add, AdaLN
 // gated residual and the Euler update (y += dt * v).
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -54,7 +55,7 @@ __global__ void __launch_bounds__(kWarps * 32) linear_rows_kernel(const LinearAr
   const int mt = min(MT, a.M - m0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
-  grid_dep_wait();
+  grid_dep_enter();
   // ---- prologue: stage the activation tile (RMSNorm + modulate)
   for (int r = warp; r < MT; r += kWarps) {
     float* dst = xs + r * K;
@@ -64,6 +65,26 @@ __global__ void __launch_bounds__(kWarps * 32) linear_rows_kernel(const LinearAr
     }
     const int m = m0 + r;
     const float* xr = row_in(a.x, m, a.x_div, a.x_ld, a.x_ld_outer);
+    const float* md0 = a.mod ? a.mod + (long)(m / a.mod_div) * a.mod_ld : nullptr;
+    if ((K & 127) == 0 && K <= 2048 && (reinterpret_cast<uintptr_t>(xr) & 15) == 0) {
+      // register-resident row: all loads in flight at once
+      float4 v[16];
+      const float ss = warp_load_row<16>(xr, K, v);
+      const float inv = a.norm_w ? 1.0f / sqrtf(ss / (float)K + a.eps) : 1.0f;
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        if (i >= (K >> 7)) break;
+        const int k = lane * 4 + 128 * i;
+        float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          if (a.norm_w) e[j] = e[j] * inv * a.norm_w[k + j];
+          if (md0) e[j] = e[j] * (1.0f + md0[a.mod_scale + k + j]) + md0[a.mod_shift + k + j];
+        }
+        *reinterpret_cast<float4*>(dst + k) = make_float4(e[0], e[1], e[2], e[3]);
+      }
+      continue;
+    }
     float inv = 1.0f;
     if (a.norm_w) {
       float ss = 0.0f;
@@ -103,7 +124,7 @@ __global__ void __launch_bounds__(kWarps * 32) linear_rows_kernel(const LinearAr
     nr[r] = SWIGLU ? (n >> 6) * 128 + (n & 63) : n;
   }
 
-#pragma unroll 2
+#pragma unroll 4
   for (int k = lane * VEC; k < K; k += 32 * VEC) {
     float wv[RPW][VEC];
     float wu[SWIGLU ? RPW : 1][VEC];
@@ -165,10 +186,34 @@ __global__ void __launch_bounds__(kWarps * 32) linear_rows_kernel(const LinearAr
 // One warp per row: y = bf16( modulate( RMSNorm(x) ) ), the tensor-core
 // path's activation operand.
 __global__ void __launch_bounds__(128) prep_bf16_kernel(const PrepArgs a) {
-  grid_dep_wait();
+  grid_dep_enter();
   const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= a.M) return;
   const float* xr = a.x + (long)row * a.x_ld;
+  const float* md = a.mod ? a.mod + (long)(row / a.mod_div) * a.mod_ld : nullptr;
+  uint16_t* yr = a.y + (long)row * a.y_ld;
+  if ((a.K & 127) == 0 && a.K <= 2048 && (reinterpret_cast<uintptr_t>(xr) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(yr) & 7) == 0) {
+    float4 v[16];
+    const float ss = warp_load_row<16>(xr, a.K, v);
+    const float inv = a.norm_w ? 1.0f / sqrtf(ss / (float)a.K + a.eps) : 1.0f;
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      if (i >= (a.K >> 7)) break;
+      const int k = lane * 4 + 128 * i;
+      float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        if (a.norm_w) e[j] = e[j] * inv * a.norm_w[k + j];
+        if (md) e[j] = e[j] * (1.0f + md[a.mod_scale + k + j]) + md[a.mod_shift + k + j];
+      }
+      uint2 pk;
+      pk.x = (uint32_t)f2bf(e[0]) | ((uint32_t)f2bf(e[1]) << 16);
+      pk.y = (uint32_t)f2bf(e[2]) | ((uint32_t)f2bf(e[3]) << 16);
+      *reinterpret_cast<uint2*>(yr + k) = pk;
+    }
+    return;
+  }
   float inv = 1.0f;
   if (a.norm_w) {
     float ss = 0.0f;
@@ -176,8 +221,6 @@ __global__ void __launch_bounds__(128) prep_bf16_kernel(const PrepArgs a) {
     ss = warp_sum(ss);
     inv = 1.0f / sqrtf(ss / (float)a.K + a.eps);
   }
-  const float* md = a.mod ? a.mod + (long)(row / a.mod_div) * a.mod_ld : nullptr;
-  uint16_t* yr = a.y + (long)row * a.y_ld;
   for (int k = lane; k < a.K; k += 32) {
     float v = xr[k];
     if (a.norm_w) v = v * inv * a.norm_w[k];
@@ -207,7 +250,7 @@ cudaError_t launch_t(const LinearArgs& a, cudaStream_t s) {
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = a.pdl ? 1 : 0;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
@@ -245,9 +288,18 @@ int linear_grid_ctas(const LinearArgs& a) {
   return ((a.N + kWarps * rpw - 1) / (kWarps * rpw)) * ((a.M + mt - 1) / mt);
 }
 
+bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("CTTS_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 cudaError_t launch_prep_bf16(const PrepArgs& a, cudaStream_t s) {
   if (a.M <= 0) return cudaSuccess;
-  prep_bf16_kernel<<<(a.M + 3) / 4, 128, 0, s>>>(a);
+  CTTS_LK(launch_k(prep_bf16_kernel, dim3((a.M + 3) / 4), dim3(128), 0, s, a));
   return cudaGetLastError();
 }
 

@@ -23,6 +23,8 @@
 // code, skips the rest of its work, releases its TMEM and returns.
 #include <cuda.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "tc_linear.cuh"
 
@@ -40,6 +42,12 @@ CTTS_DEV uint32_t smem_u32(const void* p) {
 
 CTTS_DEV void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+// Raise the expected transaction bytes without arriving.
+CTTS_DEV void mbar_add_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
 }
 
 CTTS_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
@@ -118,19 +126,68 @@ CTTS_DEV void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// Epilogue of one output element; `val` = accumulated sum (+bias applied
-// here).  n is the W row (for swiglu: the gate row), col the output column.
-CTTS_DEV void store_out(const TcArgs& a, int m, int col, float val) {
-  float coef = a.gate ? 1.0f + a.gate[(long)(m / a.gate_div) * a.gate_ld + a.gate_off + col] : a.scale;
-  float out = coef * val;
-  if (a.res) out += a.res[(long)m * a.y_ld + col];
-  if (a.yb)
-    a.yb[(long)m * a.y_ld + col] = f2bf(out);
-  else
-    a.y[(long)m * a.y_ld + col] = out;
+CTTS_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-__global__ void __launch_bounds__(128, 1)
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+CTTS_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+CTTS_DEV uint32_t ld_dsmem_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+CTTS_DEV float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// Epilogue of four adjacent output columns col..col+n-1 of row m:
+// y = res + coef * val, coef = 1 + gate (AdaLN) or `scale`.  Vector
+// accesses when the row offset allows, scalar otherwise.
+CTTS_DEV void store_out4(const TcArgs& a, int m, int col, const float* val, int n) {
+  const long yo = (long)m * a.y_ld + col;
+  float out[4];
+  const float* gp = a.gate ? a.gate + (long)(m / a.gate_div) * a.gate_ld + a.gate_off + col : nullptr;
+  const bool vec = n == 4 && (yo % 4 == 0) && (!gp || ((reinterpret_cast<uintptr_t>(gp) & 15) == 0));
+  if (vec) {
+    float4 gv = gp ? *reinterpret_cast<const float4*>(gp) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 rv = a.res ? *reinterpret_cast<const float4*>(a.res + yo) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float gg[4] = {gv.x, gv.y, gv.z, gv.w}, rr[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) out[j] = rr[j] + (gp ? 1.0f + gg[j] : a.scale) * val[j];
+    if (a.yb) {
+      uint2 pk;
+      pk.x = (uint32_t)f2bf(out[0]) | ((uint32_t)f2bf(out[1]) << 16);
+      pk.y = (uint32_t)f2bf(out[2]) | ((uint32_t)f2bf(out[3]) << 16);
+      *reinterpret_cast<uint2*>(a.yb + yo) = pk;
+    } else {
+      *reinterpret_cast<float4*>(a.y + yo) = make_float4(out[0], out[1], out[2], out[3]);
+    }
+    return;
+  }
+  for (int j = 0; j < n; j++) {
+    float o = (gp ? 1.0f + gp[j] : a.scale) * val[j];
+    if (a.res) o += a.res[yo + j];
+    if (a.yb)
+      a.yb[yo + j] = f2bf(o);
+    else
+      a.y[yo + j] = o;
+  }
+}
+
+__global__ void __launch_bounds__(128)
     tc_linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                      const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -140,7 +197,7 @@ __global__ void __launch_bounds__(128, 1)
   const int bbytes = a.MT * 128;
   const size_t stage_bytes = 16384 + (size_t)bbytes;
   // barriers sit after both the stage ring and the epilogue exchange area
-  const size_t xch_bytes = (size_t)128 * (a.MT + 1) * 4;
+  const size_t xch_bytes = (size_t)a.MT * kTileN * 4;  // fp32 partial tile (phase 1)
   const size_t region = (size_t)S * stage_bytes > xch_bytes ? (size_t)S * stage_bytes : xch_bytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ((region + 15) & ~size_t(15)));
   uint64_t* full = bars;
@@ -176,18 +233,33 @@ __global__ void __launch_bounds__(128, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  // inputs of this kernel may be produced by the previous launch
+  // Weights do not depend on the previous kernel: their first stages are
+  // fetched before waiting on it (programmatic dependent launch), the
+  // activation tiles only after.
+  const int pre = nk < S ? nk : S;
+  if (tid == 0) {
+    for (int i = 0; i < pre; i++) {
+      uint8_t* sa = smem + (size_t)i * stage_bytes;
+      mbar_add_tx(&full[i], 16384u);
+      tma_load_2d(sa, &tmW, (kb0 + i) * kBK, n0, &full[i]);
+    }
+  }
   grid_dep_wait();
+  grid_dep_launch();
 
   bool ok = true;
   if (tid == 0) {  // ---- TMA producer
     for (int i = 0; i < nk && ok; i++) {
       const int s = i % S;
-      if (i >= S) ok = mbar_wait(&empty[s], ((i / S) - 1) & 1);
-      if (!ok) break;
       uint8_t* sa = smem + (size_t)s * stage_bytes;
-      mbar_expect_tx(&full[s], (uint32_t)stage_bytes);
-      tma_load_2d(sa, &tmW, (kb0 + i) * kBK, n0, &full[s]);
+      if (i >= S) {
+        ok = mbar_wait(&empty[s], ((i / S) - 1) & 1);
+        if (!ok) break;
+        mbar_expect_tx(&full[s], (uint32_t)stage_bytes);
+        tma_load_2d(sa, &tmW, (kb0 + i) * kBK, n0, &full[s]);
+      } else {
+        mbar_expect_tx(&full[s], (uint32_t)(stage_bytes - 16384));
+      }
       tma_load_2d(sa + 16384, &tmX, (kb0 + i) * kBK, a.m0, &full[s]);
     }
   } else if (tid == 32) {  // ---- MMA issuer
@@ -219,92 +291,75 @@ __global__ void __launch_bounds__(128, 1)
   const int r = warp * 32 + lane;  // TMEM lane = W row within the tile
   const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
   const int mcount = min(a.MT, a.M - a.m0);
+  // ---- phase 1: accumulator -> this CTA's partial tile in shared memory
+  // (the stage ring is free once every MMA has completed): part[m][128].
+  float* part = reinterpret_cast<float*>(smem);
   if (!failed) {
-    if (a.splitk == 1) {
-      float* xch = reinterpret_cast<float*>(smem);  // pipeline buffers are free now
-      const int xs = a.MT + 1;
-      for (int c0 = 0; c0 < a.MT; c0 += 16) {
-        float v[16];
-        tmem_ld16(tl + c0, v);
-        if (a.act == 2) {
-          if (r >= 64)
+    for (int c0 = 0; c0 < a.MT; c0 += 16) {
+      float v[16];
+      tmem_ld16(tl + c0, v);
 #pragma unroll
-            for (int j = 0; j < 16; j++) xch[(r - 64) * xs + c0 + j] = v[j];
-          else
+      for (int j = 0; j < 16; j++) part[(c0 + j) * kTileN + r] = v[j];
+    }
+  }
+  // every split of this tile (one cluster) has its partial in shared memory
+  cluster_sync();
+
+  // ---- phase 2: CTA `split` reduces rows [m_lo, m_hi) of the tile over all
+  // splits, in split order (deterministic), reading peers over DSMEM, and
+  // runs the epilogue on float4 column groups.
+  bool any_failed = failed;
+  for (int s0 = 0; s0 < a.splitk; s0++)  // a failed peer leaves a garbage partial
+    any_failed |= ld_dsmem_u32(mapa_shared(smem_u32(flag), (uint32_t)s0)) != 0;
+  if (!any_failed) {
+    const int rows_per = (mcount + a.splitk - 1) / a.splitk;
+    const int m_lo = split * rows_per, m_hi = min(mcount, m_lo + rows_per);
+    const bool sw = a.act == 2;
+    const int groups = sw ? 16 : 32;
+    const uint32_t my_base = smem_u32(part);
+    for (int u = tid; u < (m_hi - m_lo) * groups; u += 128) {
+      const int m = m_lo + u / groups, c = (u % groups) * 4;
+      const uint32_t off = (uint32_t)(m * kTileN + c) * 4u;
+      float g[4] = {0.f, 0.f, 0.f, 0.f}, up[4] = {0.f, 0.f, 0.f, 0.f};
+      // all split loads in flight first, then the in-order sum
+      float4 tg[8], tu[8];
 #pragma unroll
-            for (int j = 0; j < 16; j++) xch[(64 + r) * xs + c0 + j] = v[j];
-        } else {
-          const int n = n0 + r;
-          if (n < a.N) {
-            const float b = a.bias ? a.bias[n] : 0.0f;
-#pragma unroll
-            for (int j = 0; j < 16; j++) {
-              const int m = c0 + j;
-              if (m < mcount) store_out(a, a.m0 + m, n, v[j] + b);
-            }
-          }
+      for (int s0 = 0; s0 < 8; s0++) {
+        if (s0 < a.splitk) {
+          const uint32_t remote = mapa_shared(my_base + off, (uint32_t)s0);
+          tg[s0] = ld_dsmem_f4(remote);
+          if (sw) tu[s0] = ld_dsmem_f4(remote + 64u * 4u);
         }
       }
-      if (a.act == 2) {
-        __syncthreads();
-        // thread r < 64 owns output column tile*64 + r: gate row n0 + r, up row n0 + 64 + r
-        if (r < 64) {
-          const int col = tile * 64 + r;
-          const float bg = a.bias ? a.bias[n0 + r] : 0.0f, bu = a.bias ? a.bias[n0 + 64 + r] : 0.0f;
-          for (int m = 0; m < mcount; m++) {
-            const float g = xch[(64 + r) * xs + m] + bg, u = xch[r * xs + m] + bu;
-            store_out(a, a.m0 + m, col, silu(g) * u);
-          }
-        }
-      }
-    } else {
-      // partial tile -> scratch [tile][split][MT][128]
-      float* part = a.part + (((size_t)tile * a.splitk + split) * a.MT) * kTileN;
-      for (int c0 = 0; c0 < a.MT; c0 += 16) {
-        float v[16];
-        tmem_ld16(tl + c0, v);
 #pragma unroll
-        for (int j = 0; j < 16; j++) __stcg(&part[(size_t)(c0 + j) * kTileN + r], v[j]);
-      }
-      __threadfence();
-      __syncthreads();
-      __shared__ int last;
-      if (tid == 0) last = atomicAdd(&a.counters[tile], 1) == a.splitk - 1;
-      __syncthreads();
-      if (last) {
-        __threadfence();
-        const float* pt = a.part + ((size_t)tile * a.splitk * a.MT) * kTileN;
-        const size_t sstride = (size_t)a.MT * kTileN;
-        if (a.act == 2) {
-          if (r < 64) {
-            const int col = tile * 64 + r;
-            const float bg = a.bias ? a.bias[n0 + r] : 0.0f, bu = a.bias ? a.bias[n0 + 64 + r] : 0.0f;
-            for (int m = 0; m < mcount; m++) {
-              float g = 0.0f, u = 0.0f;
-              for (int s = 0; s < a.splitk; s++) {
-                g += __ldcg(&pt[s * sstride + (size_t)m * kTileN + r]);
-                u += __ldcg(&pt[s * sstride + (size_t)m * kTileN + 64 + r]);
-              }
-              store_out(a, a.m0 + m, col, silu(g + bg) * (u + bu));
-            }
-          }
-        } else {
-          const int n = n0 + r;
-          if (n < a.N) {
-            const float b = a.bias ? a.bias[n] : 0.0f;
-            for (int m = 0; m < mcount; m++) {
-              float acc = 0.0f;
-              for (int s = 0; s < a.splitk; s++) acc += __ldcg(&pt[s * sstride + (size_t)m * kTileN + r]);
-              store_out(a, a.m0 + m, n, acc + b);
-            }
-          }
+      for (int s0 = 0; s0 < 8; s0++) {
+        if (s0 < a.splitk) {
+          g[0] += tg[s0].x; g[1] += tg[s0].y; g[2] += tg[s0].z; g[3] += tg[s0].w;
+          if (sw) { up[0] += tu[s0].x; up[1] += tu[s0].y; up[2] += tu[s0].z; up[3] += tu[s0].w; }
         }
-        if (tid == 0) a.counters[tile] = 0;  // ready for the next launch
+      }
+      if (sw) {
+        float out[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float bg = a.bias ? a.bias[n0 + c + j] : 0.0f, bu = a.bias ? a.bias[n0 + 64 + c + j] : 0.0f;
+          out[j] = silu(g[j] + bg) * (up[j] + bu);
+        }
+        store_out4(a, a.m0 + m, tile * 64 + c, out, 4);
+      } else {
+        const int nvalid = min(4, a.N - (n0 + c));
+        if (nvalid > 0) {
+#pragma unroll
+          for (int j = 0; j < 4; j++) g[j] += (a.bias && j < nvalid) ? a.bias[n0 + c + j] : 0.0f;
+          store_out4(a, a.m0 + m, n0 + c, g, nvalid);
+        }
       }
     }
   } else if (tid == 0 && a.err) {
     atomicExch(a.err, 2);
   }
+  // no CTA leaves while a peer may still read its shared memory
+  cluster_sync();
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -363,17 +418,24 @@ TcPlan tc_plan(int M, int N, int K, int num_sms, int max_splitk) {
   p.mtiles = (M + p.MT - 1) / p.MT;
   p.ntiles = (N + kTileN - 1) / kTileN;
   p.kblocks = K / kBK;
+  // the K splits of one tile form a thread-block cluster (<= 8, portable);
+  // aim for about one wave of CTAs.  CTTS_TC_MAX_SPLITK caps the split.
+  static int env_cap = -1;
+  if (env_cap < 0) {
+    const char* e = getenv("CTTS_TC_MAX_SPLITK");
+    env_cap = e ? std::max(1, atoi(e)) : 8;
+  }
+  max_splitk = std::min(max_splitk, env_cap);
   const int ctas_per_split = p.ntiles * p.mtiles;
-  int sk = (2 * num_sms + ctas_per_split - 1) / ctas_per_split;
-  sk = std::min(sk, std::max(1, p.kblocks / 2));
-  p.splitk = std::max(1, std::min(std::min(sk, p.kblocks), max_splitk));
+  int sk = std::max(1, num_sms / ctas_per_split);
+  p.splitk = std::max(1, std::min(std::min(std::min(sk, p.kblocks), max_splitk), 8));
   const int kb_per = (p.kblocks + p.splitk - 1) / p.splitk;
   const size_t stage = 16384 + (size_t)p.MT * 128;
   const size_t budget = 200 * 1024;
   p.stages = std::max(1, std::min(kb_per, (int)(budget / stage)));
   p.stages = std::min(p.stages, 8);
   size_t pipe = (size_t)p.stages * stage;
-  size_t xch = (size_t)128 * (p.MT + 1) * 4;
+  size_t xch = (size_t)p.MT * kTileN * 4;
   p.smem = ((std::max(pipe, xch) + 15) & ~size_t(15)) + 1024 /*align*/ + 8 * (2 * p.stages + 1) + 16;
   int cols = 32;
   while (cols < p.MT) cols <<= 1;
@@ -382,26 +444,29 @@ TcPlan tc_plan(int M, int N, int K, int num_sms, int max_splitk) {
 }
 
 size_t tc_scratch_floats(const TcPlan& p) {
-  return p.splitk > 1 ? (size_t)p.ntiles * p.splitk * p.MT * kTileN * p.mtiles : 0;
+  (void)p;
+  return 0;  // split-K partials stay in the cluster's shared memory
 }
 
 cudaError_t launch_tc_linear(const TcCall& c, cudaStream_t s) {
   if (c.K % kBK != 0 || c.M <= 0 || c.N <= 0) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(c.w) & 15) || (reinterpret_cast<uintptr_t>(c.x) & 15))
     return cudaErrorInvalidValue;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(tc_linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
   TcPlan p = tc_plan(c.M, c.N, c.K, tc_num_sms(), c.max_splitk);
-  if (p.splitk > 1 && (!c.part || !c.counters || c.part_floats < tc_scratch_floats(p) ||
-                       c.counter_count < p.ntiles * p.mtiles))
-    return cudaErrorInvalidValue;
+  static size_t configured = 0;  // dynamic smem opt-in so far (static smem is tiny)
+  if (p.smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(tc_linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      return e;
+    }
+    configured = p.smem;
+  }
   CUtensorMap tmW, tmX;
-  if (!make_map(&tmW, c.w, c.N, c.K, kTileN)) return cudaErrorInvalidValue;
-  if (!make_map(&tmX, c.x, c.M, c.K, p.MT)) return cudaErrorInvalidValue;
+  // distinct codes for the tensor-map failures (diagnostics)
+  if (!encode_fn()) return cudaErrorNotSupported;
+  if (!make_map(&tmW, c.w, c.N, c.K, kTileN)) return cudaErrorInvalidPitchValue;
+  if (!make_map(&tmX, c.x, c.M, c.K, p.MT)) return cudaErrorInvalidPitchValue;
   for (int mt = 0; mt < p.mtiles; mt++) {
     TcArgs a = c.epi;
     a.M = c.M;
@@ -412,21 +477,26 @@ cudaError_t launch_tc_linear(const TcCall& c, cudaStream_t s) {
     a.splitk = p.splitk;
     a.stages = p.stages;
     a.tmem_cols = p.tmem_cols;
-    a.part = c.part + (size_t)mt * p.ntiles * p.splitk * p.MT * kTileN;
-    a.counters = c.counters + mt * p.ntiles;
     a.err = c.err;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.ntiles, p.splitk, 1);
     cfg.blockDim = dim3(128);
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = p.splitk;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = c.pdl ? 1 : 0;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, tc_linear_kernel, tmW, tmX, a);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      return e;
+    }
   }
   return cudaSuccess;
 }

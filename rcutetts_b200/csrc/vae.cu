@@ -40,7 +40,7 @@ __global__ void __launch_bounds__(256) conv_kernel(const ConvArgs a, int Tc, int
                                                    int nphase, long wphase) {
   __shared__ __align__(16) float Ws[TK][TO];
   __shared__ __align__(16) float Xs[TK][TT];
-  grid_dep_wait();
+  grid_dep_enter();
   const int b = blockIdx.z / nphase, ph = blockIdx.z % nphase;
   const int o0 = blockIdx.y * TO, t0 = blockIdx.x * TT;
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(256) conv_kernel(const ConvArgs a, int Tc, int
 
 __global__ void snake_kernel(const float* x, int C, int T, const float* alpha, float* y,
                              size_t n) {
-  grid_dep_wait();
+  grid_dep_enter();
   size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   int c = (int)((i / T) % C);
@@ -120,9 +120,9 @@ cudaError_t launch_conv1d(const ConvArgs& a, cudaStream_t s) {
   if (a.Tout != a.Tin) return cudaErrorInvalidValue;
   dim3 grid((a.Tout + TT - 1) / TT, (a.Cout + TO - 1) / TO, a.B);
   if (a.w_bf16)
-    conv_kernel<true><<<grid, 256, 0, s>>>(a, a.Tout, 1, 1, 0);
+    CTTS_LK(launch_k(conv_kernel<true>, dim3(grid), dim3(256), 0, s, a, a.Tout, 1, 1, 0));
   else
-    conv_kernel<false><<<grid, 256, 0, s>>>(a, a.Tout, 1, 1, 0);
+    CTTS_LK(launch_k(conv_kernel<false>, dim3(grid), dim3(256), 0, s, a, a.Tout, 1, 1, 0));
   return cudaGetLastError();
 }
 
@@ -133,9 +133,9 @@ cudaError_t launch_conv_transpose(const ConvArgs& a, cudaStream_t s) {
   dim3 grid((a.Tin + TT - 1) / TT, (a.Cout + TO - 1) / TO, a.B * a.stride);
   long wphase = (long)a.Cout * a.Cin * 2;
   if (a.w_bf16)
-    conv_kernel<true><<<grid, 256, 0, s>>>(a, a.Tin, a.stride, a.stride, wphase);
+    CTTS_LK(launch_k(conv_kernel<true>, dim3(grid), dim3(256), 0, s, a, a.Tin, a.stride, a.stride, wphase));
   else
-    conv_kernel<false><<<grid, 256, 0, s>>>(a, a.Tin, a.stride, a.stride, wphase);
+    CTTS_LK(launch_k(conv_kernel<false>, dim3(grid), dim3(256), 0, s, a, a.Tin, a.stride, a.stride, wphase));
   return cudaGetLastError();
 }
 
@@ -143,7 +143,7 @@ cudaError_t launch_snake(const float* x, int B, int C, int T, const float* alpha
                          cudaStream_t s) {
   size_t n = (size_t)B * C * T;
   if (!n) return cudaSuccess;
-  snake_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, C, T, alpha, y, n);
+  CTTS_LK(launch_k(snake_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, x, C, T, alpha, y, n));
   return cudaGetLastError();
 }
 
