@@ -233,6 +233,23 @@ CTTS_API int cutetts_vae_decode(void* handle, const float* latent64xT, unsigned 
  * bf16 bits). */
 CTTS_API int ctts_op_linear(const float* x, int M, int K, const void* w, int w_dtype, int N,
                    const float* norm_w, float eps, const float* res, float* y, void* stream);
+/* ctts_op_linear without any device allocation.  No counterpart in the
+ * reference (whose CPU kernels allocate host vectors freely): for callers
+ * that cannot call cudaMalloc -- a process whose device heap is owned by
+ * its own pool, or code that must not allocate after set-up (during a
+ * stream capture, or in a serving loop that cannot afford cudaMalloc's
+ * implicit synchronization).  Same arguments and results as ctts_op_linear.
+ * The bf16 tensor-core path (w_dtype CTTS_BF16, M >= 16, K % 64 == 0) keeps
+ * its bf16 activation operand in a static device array of 2^20 elements
+ * (2 MiB, held by every GPU that loads this library until exit) instead of
+ * an allocated buffer; M*K above 2^20 returns CTTS_ERR_RANGE.  The first call
+ * on a device looks the array's device address up (cudaGetSymbolAddress),
+ * so make it before any stream capture.  All calls share the array: calls
+ * that overlap on the GPU (different streams, or threads on one device)
+ * race on it, so serialize them. */
+CTTS_API int ctts_op_linear_noalloc(const float* x, int M, int K, const void* w, int w_dtype, int N,
+                                    const float* norm_w, float eps, const float* res, float* y,
+                                    void* stream);
 /* NeoX RoPE in place on x [M, heads, head_dim] at positions pos[M]. */
 CTTS_API int ctts_op_rope(float* x, int M, int heads, int head_dim, const int* pos, float theta,
                  void* stream);

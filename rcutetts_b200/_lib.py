@@ -93,6 +93,8 @@ SIGNATURES = {
     "cutetts_vae_free": (None, [vp]),
     "cutetts_vae_decode": (C.c_int, [vp, fp, C.c_ulong, fp]),
     "ctts_op_linear": (C.c_int, [vp, C.c_int, C.c_int, vp, C.c_int, C.c_int, vp, C.c_float, vp, vp, vp]),
+    "ctts_op_linear_noalloc": (C.c_int, [vp, C.c_int, C.c_int, vp, C.c_int, C.c_int, vp, C.c_float, vp, vp,
+                                         vp]),
     "ctts_op_rope": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, vp, C.c_float, vp]),
     "ctts_op_swiglu": (C.c_int, [vp, C.c_int, C.c_int, vp, vp]),
     "ctts_op_embed_gather": (C.c_int, [vp, C.c_int, C.c_int, vp, C.c_int, vp, vp, vp]),
