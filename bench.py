@@ -124,6 +124,25 @@ def utterances(n_total: int, seed: int, vocab: int):
             for u in range(n_total)]
 
 
+def shard(n_total: int, rank: int, world: int):
+    """Contiguous utterance shard of this rank (utterances are independent:
+    no collective on the data path)."""
+    per = n_total // world
+    return range(rank * per, (rank + 1) * per)
+
+
+def max_over_ranks(values, world: int, device=None):
+    """Element-wise max of per-rank timings (the slowest rank defines the
+    job's time).  torch.distributed plumbing only."""
+    if world <= 1:
+        return list(values)
+    import torch
+
+    t = torch.tensor(list(values), dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return [float(v) for v in t.cpu()]
+
+
 def prefix_rows(lm, hw, ids, prompt):
     emb = lm.embed_lookup(ids)
     pr = prompt @ hw["latent_proj.weight"].T + hw["latent_proj.bias"]
@@ -154,7 +173,8 @@ def run_ours(args, rank, world, local):
     hbm, bf16_tf, peak_kind = peaks()
     lcfg, dcfg, lw, dw, hw, lm, dit = make_models("bf16", seed=3, device=dev)
     B = B_PER_GPU
-    utts = utterances(B * world, seed=3, vocab=lcfg.vocab)[rank * B:(rank + 1) * B]
+    allu = utterances(B * world, seed=3, vocab=lcfg.vocab)
+    utts = [allu[i] for i in shard(B * world, rank, world)]
     K, W = args.steps, args.warmup
     # timed frames end near the middle of the run unless a start frame is given
     start = args.start_frame if args.start_frame >= 0 else max(0, GEN_FRAMES // 2 - W - K)
@@ -205,10 +225,7 @@ def run_ours(args, rank, world, local):
     x1.record(es)
     torch.cuda.synchronize()
     ms_e2e = x0.elapsed_time(x1)
-    if world > 1:
-        t = torch.tensor([ms, ms_e2e], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, ms_e2e = float(t[0]), float(t[1])
+    ms, ms_e2e = max_over_ranks([ms, ms_e2e], world, device="cuda")
     launches = eng.launches_per_step
     ctx_mean = float(np.mean(ctx0)) + start + W + K / 2
     step_bytes = algorithmic_bytes_per_step(lcfg, dcfg, B, ctx_mean, 2, 2)
@@ -243,12 +260,14 @@ def run_b1(args, dev):
         eng.step_dev(noise[f], lat[f], None)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.profiler.start()
     e0.record(stream)
-    for f in range(W, frames):
+    for f in range(W, W + args.b1_frames):
         eng.step_dev(noise[f], lat[f], None)
     e1.record(stream)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / (frames - W)
+    torch.cuda.profiler.stop()
+    ms = e0.elapsed_time(e1) / args.b1_frames
     ctx_mean = 40 + PROMPT_FRAMES + frames / 2
     step_bytes = algorithmic_bytes_per_step(lcfg, dcfg, 1, ctx_mean, 4, 4)
     hbm, _, kind = peaks()
@@ -265,11 +284,12 @@ def run_b1(args, dev):
 
 
 def dominant_kernel_roofline(lm, dit, lcfg, dcfg, dev):
-    """Average device time of the dominant kernel class, replayed alone with
-    CUDA events: the DiT gate/up linear of the batched step (M = 3*64 rows,
-    K = 512, N = 2*1536, bf16 weights, SwiGLU epilogue), whose weights sit in
-    L2 from the second Euler step on, and the LM gate/up linear (M = 64, K =
-    768, N = 2*2048) that streams from HBM (L2 flushed between launches)."""
+    """Average device time of the dominant kernel class (the tcgen05 bf16
+    linear, tc_linear_kernel), replayed alone through ctts_op_linear with CUDA
+    events on the launching stream: the LM down and gate/up shapes of the
+    batched step (M = 64 rows, bf16 weights streamed from HBM; L2 flushed
+    between launches).  Algorithmic bytes = weights + activation in +
+    output out."""
     import ctypes as C
 
     import torch
@@ -289,6 +309,7 @@ def dominant_kernel_roofline(lm, dit, lcfg, dcfg, dev):
         flush = torch.empty(2 * L2_BYTES // 4, device="cuda")
         st = torch.cuda.current_stream()
         times = []
+        torch.cuda.profiler.start()
         for it in range(23):
             flush.add_(1.0)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -300,13 +321,14 @@ def dominant_kernel_roofline(lm, dit, lcfg, dcfg, dev):
             torch.cuda.synchronize()
             if it >= 3:
                 times.append(e0.elapsed_time(e1))
+        torch.cuda.profiler.stop()
         t = statistics.mean(times) * 1e-3
         algo = N * K * 2 + M * K * 4 + M * N * 4
         out[name] = {"us": round(t * 1e6, 2), "bytes": algo, "gbs": algo / t / 1e9}
     d = out["lm_gate_up"]
     return {"bound": "hbm", "achieved": round(d["gbs"], 1), "peak": hbm, "unit": "GB/s",
             "frac": round(d["gbs"] / hbm, 4), "traffic": None, "of": kind,
-            "kernel": "linear_rows_kernel<bf16> LM gate/up, M=64 K=768 N=2x2048, L2 flushed",
+            "kernel": "tc_linear_kernel (tcgen05, bf16) via ctts_op_linear: LM gate/up shape M=64 K=768 N=4096, L2 flushed",
             "bytes_per_launch": d["bytes"], "us_per_launch": d["us"],
             "others": {k: {"us": v["us"], "gbs": round(v["gbs"], 1)} for k, v in out.items()}}
 
@@ -394,6 +416,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-b1", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--only", default="", choices=["", "c2", "probe"],
+                    help="c2: only the batch-1 fp32 config[2] measurement; probe: only the roofline probe")
+    ap.add_argument("--b1-frames", type=int, default=197, help="timed frames of the batch-1 run (<= 197)")
     ap.add_argument("--start-frame", type=int, default=-1,
                     help="first warm-up frame (default: timed window centred on the run)")
     args = ap.parse_args()
@@ -406,6 +431,16 @@ def main():
         return
     import torch
 
+    if args.only == "probe":
+        torch.cuda.set_device(local)
+        print(json.dumps({"roofline": dominant_kernel_roofline(None, None, None, None, local)}), flush=True)
+        return
+    if args.only == "c2":
+        torch.cuda.set_device(local)
+        out = run_b1(args, local)
+        out.update({"metric": "us per decode step (config[2], batch 1, fp32)", "n_gpus": 1})
+        print(json.dumps(out), flush=True)
+        return
     if world > 1:
         import datetime
 

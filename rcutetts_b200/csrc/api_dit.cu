@@ -169,14 +169,27 @@ int dit_enqueue(ctts_dit* d, const DitRun& r, cudaStream_t s, int* launches) {
 
   // ---- Euler steps (predict_cached, dit.rs:775-814)
   const int xrows = r.x_rows;
+  // Euler mode: the step tail (final norm, out_proj, x += dt*v) and the
+  // next step's head (in_proj, seq fill) run as one kernel per utterance.
+  const bool fused_tail = r.mode == 0 && H % 8 == 0 && L % 8 == 0 && H <= 1024 && L <= 64;
+  DitTailArgs ta;
+  ta.seq = w.seq; ta.x = r.x; ta.R = R; ta.P = P; ta.H = H; ta.L = L;
+  ta.out_w = d->out_w; ta.out_b = d->out_b; ta.in_w = d->in_w; ta.in_b = d->in_b; ta.w_bf16 = bf;
+  ta.final_norm = d->final_norm; ta.eps = c.rms_eps;
+  ta.mu = w.mu; ta.dtemb = w.dtemb; ta.condh = w.condh;
+  if (fused_tail) {
+    DitTailArgs t0 = ta;
+    t0.do_out = 0; t0.fill = 1; t0.temb = w.temb;
+    CTTS_CK(launch_dit_tail(t0, s)); nl++;
+  }
   for (int st = 0; st < r.steps; st++) {
-    {  // in_proj(x) -> seq rows 1+P.. ; rows of x repeat for CFG's second half
+    if (!fused_tail) {  // in_proj(x) -> seq rows 1+P.. ; rows of x repeat for CFG's second half
       LinearArgs a; a.x = r.x; a.x_ld = L; a.x_div = xrows * P; a.x_ld_outer = 0;
       a.M = R * P; a.K = L; a.N = H; a.w = d->in_w; a.bias = d->in_b;
       a.y = w.seq + (size_t)(1 + P) * H; a.y_ld = H; a.y_div = P; a.y_ld_outer = (long)S * H;
       RUN(lin(a));
+      CTTS_CK(launch_dit_seq_fill(w.seq, w.mu, w.temb + (size_t)st * H, w.dtemb, w.condh, R, P, H, s)); nl++;
     }
-    CTTS_CK(launch_dit_seq_fill(w.seq, w.mu, w.temb + (size_t)st * H, w.dtemb, w.condh, R, P, H, s)); nl++;
     for (int l = 0; l < NL; l++) {
       const DitLayer& Ly = d->layers[l];
       const float* ad = use_ad ? w.ad + (size_t)l * 6 * H : nullptr;
@@ -222,6 +235,14 @@ int dit_enqueue(ctts_dit* d, const DitRun& r, cudaStream_t s, int* launches) {
       dn.y = w.seq; dn.y_ld = H; dn.res = w.seq;
       if (ad) { dn.gate = ad; dn.gate_ld = adld; dn.gate_div = S; dn.gate_off = 5 * H; }
       RUN(lin(dn));
+    }
+    if (fused_tail) {
+      DitTailArgs tt = ta;
+      tt.do_out = 1; tt.dt = r.dts[st];
+      tt.fill = st + 1 < r.steps;
+      tt.temb = w.temb + (size_t)(st + 1 < r.steps ? st + 1 : st) * H;
+      CTTS_CK(launch_dit_tail(tt, s)); nl++;
+      continue;
     }
     // final norm + out_proj on the x rows (+ Euler update)
     LinearArgs f; f.x = w.seq + (size_t)(1 + P) * H; f.x_ld = H; f.x_div = P; f.x_ld_outer = (long)S * H;

@@ -147,7 +147,113 @@ __global__ void add_rows_kernel(float* x, int R, int H, const float* v) {
   for (int n = threadIdx.x; n < H; n += blockDim.x) x[(size_t)r * H + n] += v[n];
 }
 
+template <bool BF>
+CTTS_DEV float ldw(const void* w, size_t i) {
+  if (BF) return bf2f(reinterpret_cast<const uint16_t*>(w)[i]);
+  return reinterpret_cast<const float*>(w)[i];
+}
+
+constexpr int kTailThreads = 512;
+
+// Dot product of a weight row (f32 or bf16, 16-byte aligned, n % 8 == 0)
+// with an fp32 vector in shared memory, lane-strided over 8-element groups
+// starting at group g0 with stride gs; every load of the row is issued
+// before the first multiply.
+template <bool BF, int MAXG>
+CTTS_DEV float row_dot(const void* w, size_t off, const float* xs, int n, int g0, int gs) {
+  float v[MAXG][8];
+  const int ng = n >> 3;
+#pragma unroll
+  for (int i = 0; i < MAXG; i++) {
+    const int g = g0 + i * gs;
+    if (g < ng) {
+      if (BF) {
+        uint4 t = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(w) + off + g * 8);
+        v[i][0] = bf_lo(t.x); v[i][1] = bf_hi(t.x); v[i][2] = bf_lo(t.y); v[i][3] = bf_hi(t.y);
+        v[i][4] = bf_lo(t.z); v[i][5] = bf_hi(t.z); v[i][6] = bf_lo(t.w); v[i][7] = bf_hi(t.w);
+      } else {
+        const float* p = reinterpret_cast<const float*>(w) + off + g * 8;
+        float4 t0 = *reinterpret_cast<const float4*>(p), t1 = *reinterpret_cast<const float4*>(p + 4);
+        v[i][0] = t0.x; v[i][1] = t0.y; v[i][2] = t0.z; v[i][3] = t0.w;
+        v[i][4] = t1.x; v[i][5] = t1.y; v[i][6] = t1.z; v[i][7] = t1.w;
+      }
+    }
+  }
+  float acc = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXG; i++) {
+    const int g = g0 + i * gs;
+    if (g < ng)
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc = fmaf(v[i][e], xs[g * 8 + e], acc);
+  }
+  return acc;
+}
+
+// grid R (one CTA per utterance), 512 threads.  Requires H % 8 == 0,
+// L % 8 == 0, H <= 1024, L <= 64 (host-checked).
+template <bool BF>
+__global__ void __launch_bounds__(kTailThreads) dit_tail_kernel(const DitTailArgs a) {
+  extern __shared__ __align__(16) float sm[];  // xn [P][H], xs [P*L]
+  grid_dep_enter();
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NW = kTailThreads / 32;
+  const int P = a.P, H = a.H, L = a.L, S = 1 + 2 * P, PL = P * L;
+  float* xn = sm;
+  float* xs = sm + P * H;
+  __shared__ float red[NW];
+  float* seqb = a.seq + (size_t)b * S * H;
+  float* xb = a.x + (size_t)b * PL;
+  if (a.do_out) {
+    for (int p = 0; p < P; p++) {
+      const float* row = seqb + (size_t)(1 + P + p) * H;
+      const float v0 = tid < H ? row[tid] : 0.0f, v1 = tid + kTailThreads < H ? row[tid + kTailThreads] : 0.0f;
+      float ss = warp_sum(fmaf(v0, v0, v1 * v1));
+      if (lane == 0) red[warp] = ss;
+      __syncthreads();
+      float tot = 0.0f;
+#pragma unroll
+      for (int w = 0; w < NW; w++) tot += red[w];
+      const float inv = 1.0f / sqrtf(tot / (float)H + a.eps);
+      if (tid < H) xn[p * H + tid] = v0 * inv * a.final_norm[tid];
+      if (tid + kTailThreads < H) xn[p * H + tid + kTailThreads] = v1 * inv * a.final_norm[tid + kTailThreads];
+      __syncthreads();
+    }
+    // out_proj: a warp per output, lanes over 8-element groups of H (<= 4 each)
+    for (int o = warp; o < PL; o += NW) {
+      const int p = o / L, l = o % L;
+      float acc = row_dot<BF, 4>(a.out_w, (size_t)l * H, xn + p * H, H, lane, 32);
+      acc = warp_sum(acc);
+      if (lane == 0) xb[o] = xb[o] + a.dt * (acc + (a.out_b ? a.out_b[l] : 0.0f));
+    }
+    __syncthreads();
+  }
+  if (!a.fill) return;
+  for (int i = tid; i < PL; i += kTailThreads) xs[i] = xb[i];
+  __syncthreads();
+  // in_proj: a thread per output row n, the whole weight row (<= 64) in flight
+  for (int n = tid; n < H; n += kTailThreads) {
+    for (int p = 0; p < P; p++) {
+      const float acc = row_dot<BF, 8>(a.in_w, (size_t)n * L, xs + p * L, L, 0, 1);
+      seqb[(size_t)(1 + P + p) * H + n] = acc + (a.in_b ? a.in_b[n] : 0.0f);
+    }
+    seqb[n] = (a.mu[(size_t)b * H + n] + a.temb[n]) + a.dtemb[n];
+    for (int p = 0; p < P; p++) seqb[(size_t)(1 + p) * H + n] = a.condh[((size_t)b * P + p) * H + n];
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_dit_tail(const DitTailArgs& a, cudaStream_t s) {
+  if (a.R <= 0) return cudaSuccess;
+  const size_t smem = ((size_t)a.P * a.H + (size_t)a.P * a.L) * sizeof(float);
+  if (smem > 48 * 1024 || a.H % 8 || a.L % 8 || a.H > 1024 || a.L > 64) return cudaErrorInvalidValue;
+  if (a.w_bf16)
+    CTTS_LK(launch_k(dit_tail_kernel<true>, dim3(a.R), dim3(kTailThreads), smem, s, a));
+  else
+    CTTS_LK(launch_k(dit_tail_kernel<false>, dim3(a.R), dim3(kTailThreads), smem, s, a));
+  return cudaSuccess;
+}
 
 cudaError_t launch_fill_tv(float* tv, const TGrid& g, cudaStream_t s) {
   if (g.n > TGrid::kMax) return cudaErrorInvalidValue;

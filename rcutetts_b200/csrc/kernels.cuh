@@ -125,6 +125,29 @@ struct TGrid {
 cudaError_t launch_fill_tv(float* tv, const TGrid& g, cudaStream_t s);
 // x[r, :] += v[:] for r < R
 cudaError_t launch_add_rows(float* x, int R, int H, const float* v, cudaStream_t s);
+// The tail of one Euler step fused with the head of the next, one CTA per
+// utterance: [final RMSNorm -> out_proj -> x += dt*v] (do_out) then
+// [in_proj(x) -> seq rows 1+P.., seq row 0 = mu + temb + dtemb, rows
+// 1..P = cond_proj(cond)] (fill).
+struct DitTailArgs {
+  float* seq = nullptr;  // [R, S, H]
+  float* x = nullptr;    // [R, P*L] latent, updated in place
+  int R = 0, P = 1, H = 0, L = 0;
+  const void* out_w = nullptr;  // [L, H]
+  const float* out_b = nullptr;
+  const void* in_w = nullptr;   // [H, L]
+  const float* in_b = nullptr;
+  int w_bf16 = 0;
+  const float* final_norm = nullptr;
+  float eps = 1e-6f;
+  float dt = 0.0f;
+  int do_out = 0, fill = 0;
+  const float* mu = nullptr;     // [R, H]
+  const float* temb = nullptr;   // [H] for the step being filled
+  const float* dtemb = nullptr;  // [H]
+  const float* condh = nullptr;  // [R*P, H]
+};
+cudaError_t launch_dit_tail(const DitTailArgs& a, cudaStream_t s);
 // v = vc + cfg*(vc - vu) ; x += v*dt    (vc = v[0:n], vu = v[n:2n])
 cudaError_t launch_cfg_euler(float* x, const float* v2, int n, float cfg, float dt,
                              cudaStream_t s);

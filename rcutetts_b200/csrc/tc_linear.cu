@@ -113,18 +113,16 @@ CTTS_DEV void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
-CTTS_DEV void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
+// 16 consecutive TMEM columns of this thread's lane; no wait (see tmem_wait).
+CTTS_DEV void tmem_ld16_nowait(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
         "=r"(r[15])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
+CTTS_DEV void tmem_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 CTTS_DEV void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
@@ -153,20 +151,34 @@ CTTS_DEV float4 ld_dsmem_f4(uint32_t addr) {
   return v;
 }
 
-// Epilogue of four adjacent output columns col..col+n-1 of row m:
-// y = res + coef * val, coef = 1 + gate (AdaLN) or `scale`.  Vector
-// accesses when the row offset allows, scalar otherwise.
-CTTS_DEV void store_out4(const TcArgs& a, int m, int col, const float* val, int n) {
+// Epilogue of four adjacent output columns of row m, y = res + coef * val
+// (coef = 1 + AdaLN gate, or `scale`), split in two halves so a thread can
+// issue the global loads of several output units before any of their stores.
+struct Epi4 {
+  float g[4], r[4];
+};
+CTTS_DEV void epi_fetch(const TcArgs& a, int m, int col, int n, Epi4& e) {
   const long yo = (long)m * a.y_ld + col;
-  float out[4];
   const float* gp = a.gate ? a.gate + (long)(m / a.gate_div) * a.gate_ld + a.gate_off + col : nullptr;
-  const bool vec = n == 4 && (yo % 4 == 0) && (!gp || ((reinterpret_cast<uintptr_t>(gp) & 15) == 0));
-  if (vec) {
+  if (n == 4 && (yo % 4 == 0) && (!gp || ((reinterpret_cast<uintptr_t>(gp) & 15) == 0))) {
     float4 gv = gp ? *reinterpret_cast<const float4*>(gp) : make_float4(0.f, 0.f, 0.f, 0.f);
     float4 rv = a.res ? *reinterpret_cast<const float4*>(a.res + yo) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float gg[4] = {gv.x, gv.y, gv.z, gv.w}, rr[4] = {rv.x, rv.y, rv.z, rv.w};
+    e.g[0] = gv.x; e.g[1] = gv.y; e.g[2] = gv.z; e.g[3] = gv.w;
+    e.r[0] = rv.x; e.r[1] = rv.y; e.r[2] = rv.z; e.r[3] = rv.w;
+  } else {
 #pragma unroll
-    for (int j = 0; j < 4; j++) out[j] = rr[j] + (gp ? 1.0f + gg[j] : a.scale) * val[j];
+    for (int j = 0; j < 4; j++) {
+      e.g[j] = (gp && j < n) ? gp[j] : 0.0f;
+      e.r[j] = (a.res && j < n) ? a.res[yo + j] : 0.0f;
+    }
+  }
+}
+CTTS_DEV void epi_store(const TcArgs& a, int m, int col, int n, const float* val, const Epi4& e) {
+  const long yo = (long)m * a.y_ld + col;
+  float out[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) out[j] = e.r[j] + (a.gate ? 1.0f + e.g[j] : a.scale) * val[j];
+  if (n == 4 && (yo % 4 == 0)) {
     if (a.yb) {
       uint2 pk;
       pk.x = (uint32_t)f2bf(out[0]) | ((uint32_t)f2bf(out[1]) << 16);
@@ -178,12 +190,10 @@ CTTS_DEV void store_out4(const TcArgs& a, int m, int col, const float* val, int 
     return;
   }
   for (int j = 0; j < n; j++) {
-    float o = (gp ? 1.0f + gp[j] : a.scale) * val[j];
-    if (a.res) o += a.res[yo + j];
     if (a.yb)
-      a.yb[yo + j] = f2bf(o);
+      a.yb[yo + j] = f2bf(out[j]);
     else
-      a.y[yo + j] = o;
+      a.y[yo + j] = out[j];
   }
 }
 
@@ -295,11 +305,18 @@ __global__ void __launch_bounds__(128)
   // (the stage ring is free once every MMA has completed): part[m][128].
   float* part = reinterpret_cast<float*>(smem);
   if (!failed) {
-    for (int c0 = 0; c0 < a.MT; c0 += 16) {
-      float v[16];
-      tmem_ld16(tl + c0, v);
+    // four 16-column loads in flight per wait
+    for (int c0 = 0; c0 < a.MT; c0 += 64) {
+      uint32_t v[4][16];
 #pragma unroll
-      for (int j = 0; j < 16; j++) part[(c0 + j) * kTileN + r] = v[j];
+      for (int q = 0; q < 4; q++)
+        if (c0 + 16 * q < a.MT) tmem_ld16_nowait(tl + c0 + 16 * q, v[q]);
+      tmem_wait();
+#pragma unroll
+      for (int q = 0; q < 4; q++)
+        if (c0 + 16 * q < a.MT)
+#pragma unroll
+          for (int j = 0; j < 16; j++) part[(c0 + 16 * q + j) * kTileN + r] = __uint_as_float(v[q][j]);
     }
   }
   // every split of this tile (one cluster) has its partial in shared memory
@@ -317,42 +334,67 @@ __global__ void __launch_bounds__(128)
     const bool sw = a.act == 2;
     const int groups = sw ? 16 : 32;
     const uint32_t my_base = smem_u32(part);
-    for (int u = tid; u < (m_hi - m_lo) * groups; u += 128) {
-      const int m = m_lo + u / groups, c = (u % groups) * 4;
-      const uint32_t off = (uint32_t)(m * kTileN + c) * 4u;
-      float g[4] = {0.f, 0.f, 0.f, 0.f}, up[4] = {0.f, 0.f, 0.f, 0.f};
-      // all split loads in flight first, then the in-order sum
-      float4 tg[8], tu[8];
+    const int nunits = (m_hi - m_lo) * groups;
+    // kU output units per thread per round: every DSMEM partial of the round
+    // is requested before the first sum, and the epilogue's global loads of
+    // the round are issued before its stores.
+    constexpr int kU = 2;
+    for (int u0 = tid; u0 < nunits; u0 += 128 * kU) {
+      float acc[kU][4], accu[kU][4];
 #pragma unroll
-      for (int s0 = 0; s0 < 8; s0++) {
-        if (s0 < a.splitk) {
-          const uint32_t remote = mapa_shared(my_base + off, (uint32_t)s0);
-          tg[s0] = ld_dsmem_f4(remote);
-          if (sw) tu[s0] = ld_dsmem_f4(remote + 64u * 4u);
+      for (int q = 0; q < kU; q++) {
+        const int u = u0 + q * 128;
+        float4 tg[8], tu[8];
+        const int m = m_lo + u / groups, c = (u % groups) * 4;
+        const uint32_t off = (uint32_t)(m * kTileN + c) * 4u;
+#pragma unroll
+        for (int s0 = 0; s0 < 8; s0++) {
+          if (u < nunits && s0 < a.splitk) {
+            const uint32_t remote = mapa_shared(my_base + off, (uint32_t)s0);
+            tg[s0] = ld_dsmem_f4(remote);
+            if (sw) tu[s0] = ld_dsmem_f4(remote + 64u * 4u);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[q][j] = accu[q][j] = 0.0f;
+#pragma unroll
+        for (int s0 = 0; s0 < 8; s0++) {
+          if (u < nunits && s0 < a.splitk) {
+            acc[q][0] += tg[s0].x; acc[q][1] += tg[s0].y; acc[q][2] += tg[s0].z; acc[q][3] += tg[s0].w;
+            if (sw) {
+              accu[q][0] += tu[s0].x; accu[q][1] += tu[s0].y; accu[q][2] += tu[s0].z; accu[q][3] += tu[s0].w;
+            }
+          }
         }
       }
+      // epilogue: fetch every unit's gate/residual, then compute and store
+      Epi4 ep[kU];
+      int em[kU], ec[kU], en[kU];
 #pragma unroll
-      for (int s0 = 0; s0 < 8; s0++) {
-        if (s0 < a.splitk) {
-          g[0] += tg[s0].x; g[1] += tg[s0].y; g[2] += tg[s0].z; g[3] += tg[s0].w;
-          if (sw) { up[0] += tu[s0].x; up[1] += tu[s0].y; up[2] += tu[s0].z; up[3] += tu[s0].w; }
-        }
+      for (int q = 0; q < kU; q++) {
+        const int u = u0 + q * 128;
+        const int m = m_lo + u / groups, c = (u % groups) * 4;
+        em[q] = a.m0 + m;
+        ec[q] = sw ? tile * 64 + c : n0 + c;
+        en[q] = u < nunits ? (sw ? 4 : max(0, min(4, a.N - (n0 + c)))) : 0;
+        if (en[q] > 0) epi_fetch(a, em[q], ec[q], en[q], ep[q]);
       }
-      if (sw) {
+#pragma unroll
+      for (int q = 0; q < kU; q++) {
+        if (en[q] <= 0) continue;
+        const int u = u0 + q * 128;
+        const int c = (u % groups) * 4;
         float out[4];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-          const float bg = a.bias ? a.bias[n0 + c + j] : 0.0f, bu = a.bias ? a.bias[n0 + 64 + c + j] : 0.0f;
-          out[j] = silu(g[j] + bg) * (up[j] + bu);
+          if (sw) {
+            const float bg = a.bias ? a.bias[n0 + c + j] : 0.0f, bu = a.bias ? a.bias[n0 + 64 + c + j] : 0.0f;
+            out[j] = silu(acc[q][j] + bg) * (accu[q][j] + bu);
+          } else {
+            out[j] = acc[q][j] + ((a.bias && j < en[q]) ? a.bias[n0 + c + j] : 0.0f);
+          }
         }
-        store_out4(a, a.m0 + m, tile * 64 + c, out, 4);
-      } else {
-        const int nvalid = min(4, a.N - (n0 + c));
-        if (nvalid > 0) {
-#pragma unroll
-          for (int j = 0; j < 4; j++) g[j] += (a.bias && j < nvalid) ? a.bias[n0 + c + j] : 0.0f;
-          store_out4(a, a.m0 + m, n0 + c, g, nvalid);
-        }
+        epi_store(a, em[q], ec[q], en[q], out, ep[q]);
       }
     }
   } else if (tid == 0 && a.err) {
