@@ -181,7 +181,7 @@ def run_ours(args, rank, world, local):
     total = start + W + 2 * K + 2
     max_prefix = max(len(ids) for ids, _ in utts) + PROMPT_FRAMES
     cap = max_prefix + max(total, GEN_FRAMES) + 4
-    eng = FrameEngine(lm, dit, hw, batch=B, capacity=cap, euler_steps=10)
+    eng = FrameEngine(lm, dit, hw, batch=B, capacity=cap, euler_steps=10, groups=args.groups)
     ctx0 = []
     for b, (ids, prompt) in enumerate(utts):
         rows = prefix_rows(lm, hw, ids, prompt)
@@ -419,6 +419,8 @@ def main():
     ap.add_argument("--only", default="", choices=["", "c2", "probe"],
                     help="c2: only the batch-1 fp32 config[2] measurement; probe: only the roofline probe")
     ap.add_argument("--b1-frames", type=int, default=197, help="timed frames of the batch-1 run (<= 197)")
+    ap.add_argument("--groups", type=int, default=4,
+                    help="sub-batches of the 64 utterances run as parallel branches of the frame graph")
     ap.add_argument("--start-frame", type=int, default=-1,
                     help="first warm-up frame (default: timed window centred on the run)")
     args = ap.parse_args()
@@ -463,6 +465,7 @@ def main():
         "config": {"workload": "config[3]: batched AR decode, config[2] model, 64 utterances/GPU, "
                                "text U[20,120] + 150 prompt frames, 500 frames each",
                    "global_batch": B * world, "utterances_per_gpu": B, "euler_steps": 10,
+                   "sub_batch_groups": args.groups,
                    "timed_frames": f"{res['start'] + W}..{res['start'] + W + K - 1} of 500",
                    "kv_ctx_mean": round(res["ctx_mean"], 1), "parallelism": f"utterance-sharded x{world}",
                    "l2": "per-step working set (weights+KV) > 126 MB L2; no flush"},

@@ -167,6 +167,7 @@ typedef struct {
   int euler_steps;
   float latent_scale, latent_bias; /* scaled = raw/scale - bias */
   int use_graph;     /* 1: capture the frame step as a CUDA graph */
+  int groups;        /* sub-batches run as parallel graph branches (divides batch; <=0 -> 1) */
 } ctts_engine_config;
 
 CTTS_API int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_config* cfg,

@@ -36,7 +36,8 @@ class DiTConfigC(C.Structure):
 
 class EngineConfigC(C.Structure):
     _fields_ = [("batch", C.c_int), ("capacity", C.c_int), ("euler_steps", C.c_int),
-                ("latent_scale", C.c_float), ("latent_bias", C.c_float), ("use_graph", C.c_int)]
+                ("latent_scale", C.c_float), ("latent_bias", C.c_float), ("use_graph", C.c_int),
+                ("groups", C.c_int)]
 
 
 class VAEConfigC(C.Structure):

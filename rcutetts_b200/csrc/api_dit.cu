@@ -10,8 +10,7 @@ using namespace ctts;
 
 namespace {
 
-int dit_ws_ensure(ctts_dit* d, int rows, int steps) {
-  DitWs& w = d->ws;
+int dit_ws_ensure(ctts_dit* d, DitWs& w, int rows, int steps) {
   if (w.rows >= rows && w.steps >= steps) return CTTS_OK;
   rows = std::max(rows, w.rows);
   steps = std::max(steps, w.steps);
@@ -78,10 +77,10 @@ struct DitRun {
   float* out = nullptr;          // predict: v [R, P*L]
 };
 
-// Enqueues one DiT sample / predict on stream s.  All pointers device.
-int dit_enqueue(ctts_dit* d, const DitRun& r, cudaStream_t s, int* launches) {
+// Enqueues one DiT sample / predict on stream s with workspace w (sized by
+// dit_ws_ensure).  All pointers device.
+int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* launches) {
   const ctts_dit_config& c = d->cfg;
-  DitWs& w = d->ws;
   const int H = c.hidden, P = c.patch, S = 1 + 2 * P, L = c.latent, PL = P * L;
   const int qd = c.n_heads * c.head_dim, qkvw = qd + 2 * c.n_kv_heads * c.head_dim;
   const int F = c.ffn, R = r.R, NL = c.n_layers;
@@ -266,6 +265,14 @@ int dit_enqueue(ctts_dit* d, const DitRun& r, cudaStream_t s, int* launches) {
   return CTTS_OK;
 }
 
+// Reads back the workspace's device error flag after a synchronized run.
+int dit_read_err(const DitWs& w) {
+  int err = 0;
+  CTTS_CK(cudaMemcpy(&err, w.err, sizeof(int), cudaMemcpyDeviceToHost));
+  CTTS_REQ(err == 0, CTTS_ERR_TIMEOUT, "a tensor-core linear gave up waiting on its pipeline");
+  return CTTS_OK;
+}
+
 int dit_check(ctts_dit* d) {
   CTTS_REQ(d, CTTS_ERR_ARG, "null handle");
   if (d->slots.missing())
@@ -444,7 +451,7 @@ extern "C" int ctts_dit_euler_sample_dev(ctts_dit* d, int batch, const float* x0
   if (rc) return rc;
   CTTS_REQ(batch > 0 && steps > 0 && x0_dev && z_dev && cond_dev && x_out_dev, CTTS_ERR_ARG, "bad argument");
   CTTS_CK(cudaSetDevice(d->device));
-  rc = dit_ws_ensure(d, batch, steps);
+  rc = dit_ws_ensure(d, d->ws, batch, steps);
   if (rc) return rc;
   cudaStream_t s = as_stream(stream, d->stream);
   rc = dit_upload_cfg_hidden(d, cfg_w, s);
@@ -463,7 +470,7 @@ extern "C" int ctts_dit_euler_sample_dev(ctts_dit* d, int batch, const float* x0
   r.R = batch; r.z = z_dev; r.cond = cond_dev; r.spk = spk_dev; r.x = x_out_dev; r.x_rows = batch;
   r.steps = steps; r.times = times.data(); r.dts = dts.data(); r.mode = 0; r.cfg_w = cfg_w;
   r.step_dt = dt;
-  return dit_enqueue(d, r, s, nullptr);
+  return dit_enqueue(d, d->ws, r, s, nullptr);
 }
 
 extern "C" int ctts_dit_euler_sample(ctts_dit* d, int batch, const float* x0, const float* z,
@@ -473,7 +480,7 @@ extern "C" int ctts_dit_euler_sample(ctts_dit* d, int batch, const float* x0, co
   if (rc) return rc;
   CTTS_REQ(batch > 0 && steps > 0 && x0 && z && cond && x_out, CTTS_ERR_ARG, "bad argument");
   CTTS_CK(cudaSetDevice(d->device));
-  rc = dit_ws_ensure(d, batch, steps);
+  rc = dit_ws_ensure(d, d->ws, batch, steps);
   if (rc) return rc;
   DitWs& w = d->ws;
   const int PL = d->cfg.patch * d->cfg.latent;
@@ -485,6 +492,7 @@ extern "C" int ctts_dit_euler_sample(ctts_dit* d, int batch, const float* x0, co
                                  d->stream);
   if (rc) return rc;
   CTTS_CK(cudaStreamSynchronize(d->stream));
+  if ((rc = dit_read_err(w))) return rc;
   CTTS_CK(cudaMemcpy(x_out, w.x, sizeof(float) * batch * PL, cudaMemcpyDeviceToHost));
   return CTTS_OK;
 }
@@ -495,7 +503,7 @@ extern "C" int ctts_dit_predict(ctts_dit* d, int batch, const float* x, float t,
   if (rc) return rc;
   CTTS_REQ(batch > 0 && x && z && cond && v, CTTS_ERR_ARG, "bad argument");
   CTTS_CK(cudaSetDevice(d->device));
-  rc = dit_ws_ensure(d, batch, 1);
+  rc = dit_ws_ensure(d, d->ws, batch, 1);
   if (rc) return rc;
   DitWs& w = d->ws;
   const int PL = d->cfg.patch * d->cfg.latent;
@@ -509,9 +517,10 @@ extern "C" int ctts_dit_predict(ctts_dit* d, int batch, const float* x, float t,
   DitRun r;
   r.R = batch; r.z = w.z; r.cond = w.cond; r.spk = spk ? w.spk : nullptr; r.x = w.x; r.x_rows = batch;
   r.steps = 1; r.times = times; r.mode = 1; r.out = w.v; r.cfg_w = cfg_w; r.step_dt = dt;
-  rc = dit_enqueue(d, r, d->stream, nullptr);
+  rc = dit_enqueue(d, d->ws, r, d->stream, nullptr);
   if (rc) return rc;
   CTTS_CK(cudaStreamSynchronize(d->stream));
+  if ((rc = dit_read_err(w))) return rc;
   CTTS_CK(cudaMemcpy(v, w.v, sizeof(float) * batch * PL, cudaMemcpyDeviceToHost));
   return CTTS_OK;
 }
@@ -525,7 +534,7 @@ extern "C" int ctts_dit_euler_sample_cfg(ctts_dit* d, int batch, const float* x0
   CTTS_REQ(batch > 0 && steps > 0 && x0 && z_c && z_u && cond && uncond && x_out, CTTS_ERR_ARG,
            "bad argument");
   CTTS_CK(cudaSetDevice(d->device));
-  rc = dit_ws_ensure(d, 2 * batch, steps);
+  rc = dit_ws_ensure(d, d->ws, 2 * batch, steps);
   if (rc) return rc;
   DitWs& w = d->ws;
   const int PL = d->cfg.patch * d->cfg.latent, CD = d->cfg.cond_dim;
@@ -549,9 +558,10 @@ extern "C" int ctts_dit_euler_sample_cfg(ctts_dit* d, int batch, const float* x0
   r.x = w.x; r.x_rows = batch; r.steps = steps; r.times = times.data(); r.dts = dts.data();
   r.mode = 2; r.cfg = cfg;
   r.cfg_w = cfg; r.step_dt = 1.0f / (float)steps;
-  rc = dit_enqueue(d, r, d->stream, nullptr);
+  rc = dit_enqueue(d, d->ws, r, d->stream, nullptr);
   if (rc) return rc;
   CTTS_CK(cudaStreamSynchronize(d->stream));
+  if ((rc = dit_read_err(w))) return rc;
   CTTS_CK(cudaMemcpy(x_out, w.x, sizeof(float) * batch * PL, cudaMemcpyDeviceToHost));
   return CTTS_OK;
 }
@@ -560,16 +570,25 @@ extern "C" int ctts_dit_euler_sample_cfg(ctts_dit* d, int batch, const float* x0
 
 namespace {
 
-int engine_enqueue(ctts_engine* e, cudaStream_t s, int* launches) {
+// One sub-batch of the engine: its own KV cache, DiT workspace and stream.
+// Sub-batches are independent utterances, so their frame chains run as
+// parallel branches of the frame graph and overlap on the GPU.
+int engine_enqueue_group(ctts_engine* e, EngineGroup& g, cudaStream_t s, int* launches) {
   ctts_lm* lm = e->lm;
   ctts_dit* d = e->dit;
-  const int B = e->cfg.batch, H = lm->cfg.hidden;
+  const int B = g.nb, H = lm->cfg.hidden;
   const int PL = d->cfg.patch * d->cfg.latent;
+  float* z = e->z + (size_t)g.b0 * H;
+  float* x = e->x + (size_t)g.b0 * PL;
+  float* cond = e->cond + (size_t)g.b0 * PL;
+  float* lat = e->lat + (size_t)g.b0 * PL;
+  float* stop = e->stop + (size_t)g.b0 * 2;
+  const float* noise = e->noise + (size_t)g.b0 * PL;
   int nl = 0;
-  CTTS_CK(cudaMemcpyAsync(e->x, e->noise, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
+  CTTS_CK(cudaMemcpyAsync(x, noise, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
   {  // stop logits (e2e.rs:83-92)
-    LinearArgs a; a.x = e->z; a.x_ld = H; a.M = B; a.K = H; a.N = 2; a.w = e->stop_w;
-    a.bias = e->stop_b; a.y = e->stop; a.y_ld = 2;
+    LinearArgs a; a.x = z; a.x_ld = H; a.M = B; a.K = H; a.N = 2; a.w = e->stop_w;
+    a.bias = e->stop_b; a.y = stop; a.y_ld = 2;
     CTTS_CK(launch_linear(a, s)); nl++;
   }
   const int steps = e->cfg.euler_steps;
@@ -580,22 +599,65 @@ int engine_enqueue(ctts_engine* e, cudaStream_t s, int* launches) {
     dts[i] = dt;
   }
   DitRun r;
-  r.R = B; r.z = e->z; r.cond = e->cond; r.spk = d->cfg.adaln ? e->z : nullptr;
-  r.x = e->x; r.x_rows = B; r.steps = steps; r.times = times.data(); r.dts = dts.data(); r.mode = 0;
+  r.R = B; r.z = z; r.cond = cond; r.spk = d->cfg.adaln ? z : nullptr;
+  r.x = x; r.x_rows = B; r.steps = steps; r.times = times.data(); r.dts = dts.data(); r.mode = 0;
   r.step_dt = dt;
-  int rc = dit_enqueue(d, r, s, &nl);
+  int rc = dit_enqueue(d, *g.ws, r, s, &nl);
   if (rc) return rc;
-  CTTS_CK(launch_affine(e->x, B * PL, e->cfg.latent_scale, e->cfg.latent_bias, e->lat, s)); nl++;
-  CTTS_CK(cudaMemcpyAsync(e->cond, e->x, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
+  CTTS_CK(launch_affine(x, B * PL, e->cfg.latent_scale, e->cfg.latent_bias, lat, s)); nl++;
+  CTTS_CK(cudaMemcpyAsync(cond, x, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
   {  // feedback projection straight into the LM residual stream
-    LinearArgs a; a.x = e->x; a.x_ld = PL; a.M = B; a.K = PL; a.N = H; a.w = e->proj_w;
-    a.bias = e->proj_b; a.y = e->kv->h; a.y_ld = H;
+    LinearArgs a; a.x = x; a.x_ld = PL; a.M = B; a.K = PL; a.N = H; a.w = e->proj_w;
+    a.bias = e->proj_b; a.y = g.kv->h; a.y_ld = H;
     CTTS_CK(launch_linear(a, s)); nl++;
   }
-  rc = lm_forward_rows(lm, e->kv, B, -1, 0, e->z, s, &nl);
+  rc = lm_forward_rows(lm, g.kv, B, -1, 0, z, s, &nl);
   if (rc) return rc;
-  if (launches) *launches = nl;
+  if (launches) *launches += nl;
   return CTTS_OK;
+}
+
+int engine_enqueue(ctts_engine* e, cudaStream_t s, int* launches) {
+  int n = 0;
+  if (e->groups.size() == 1) {
+    int rc = engine_enqueue_group(e, e->groups[0], s, &n);
+    if (rc) return rc;
+  } else {
+    // fork: every sub-batch branch waits for the work already on s ...
+    CTTS_CK(cudaEventRecord(e->fork, s));
+    for (auto& g : e->groups) {
+      CTTS_CK(cudaStreamWaitEvent(g.stream, e->fork, 0));
+      int rc = engine_enqueue_group(e, g, g.stream, &n);
+      if (rc) return rc;
+      CTTS_CK(cudaEventRecord(g.done, g.stream));
+    }
+    // ... join: s continues once every branch is done
+    for (auto& g : e->groups) CTTS_CK(cudaStreamWaitEvent(s, g.done, 0));
+  }
+  if (launches) *launches = n;
+  return CTTS_OK;
+}
+
+void engine_destroy(ctts_engine* e) {
+  cudaSetDevice(e->lm->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  for (auto& g : e->groups) {
+    if (g.stream) cudaStreamSynchronize(g.stream);
+  }
+  if (e->exec) cudaGraphExecDestroy(e->exec);
+  if (e->graph) cudaGraphDestroy(e->graph);
+  if (e->h_noise) cudaFreeHost(e->h_noise);
+  if (e->h_lat) cudaFreeHost(e->h_lat);
+  if (e->h_stop) cudaFreeHost(e->h_stop);
+  for (auto& g : e->groups) {
+    if (g.kv) ctts_kv_free(g.kv);
+    delete g.ws;
+    if (g.done) cudaEventDestroy(g.done);
+    if (g.stream) cudaStreamDestroy(g.stream);
+  }
+  if (e->fork) cudaEventDestroy(e->fork);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
 }
 
 }  // namespace
@@ -609,6 +671,8 @@ extern "C" int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_
            "AdaLN conditioning width must equal LM hidden");
   CTTS_REQ(cfg->batch > 0 && cfg->capacity > 0 && cfg->euler_steps > 0, CTTS_ERR_ARG, "bad config");
   CTTS_REQ(cfg->latent_scale != 0.0f, CTTS_ERR_ARG, "latent_scale must be non-zero");
+  const int G = cfg->groups <= 0 ? 1 : cfg->groups;
+  CTTS_REQ(cfg->batch % G == 0, CTTS_ERR_ARG, "batch must be a multiple of groups");
   int rc = lm_check_ready(lm);
   if (rc) return rc;
   rc = dit_check(dit);
@@ -619,18 +683,26 @@ extern "C" int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_
   e->lm = lm;
   e->dit = dit;
   e->cfg = *cfg;
-  rc = ctts_kv_alloc(lm, cfg->batch, cfg->capacity, &e->kv);
-  if (rc) {
-    delete e;
-    return rc;
-  }
-  rc = dit_ws_ensure(dit, cfg->batch, cfg->euler_steps);
-  if (rc) {
-    ctts_kv_free(e->kv);
-    delete e;
-    return rc;
-  }
+  e->cfg.groups = G;
   cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+  cudaEventCreateWithFlags(&e->fork, cudaEventDisableTiming);
+  const int per = cfg->batch / G;
+  e->groups.resize(G);
+  for (int gi = 0; gi < G; gi++) {
+    EngineGroup& g = e->groups[gi];
+    g.b0 = gi * per;
+    g.nb = per;
+    g.ws = new DitWs();
+    cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking);
+    cudaEventCreateWithFlags(&g.done, cudaEventDisableTiming);
+    rc = ctts_kv_alloc(lm, per, cfg->capacity, &g.kv);
+    if (!rc) rc = dit_ws_ensure(dit, *g.ws, per, cfg->euler_steps);
+    if (rc) {
+      engine_destroy(e);
+      return rc;
+    }
+  }
+  e->kv = e->groups[0].kv;
   const int B = cfg->batch, H = lm->cfg.hidden, PL = dit->cfg.patch * dit->cfg.latent;
   DevArena& A = e->arena;
   e->stop_w = A.alloc<float>(2 * H);
@@ -646,7 +718,7 @@ extern "C" int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_
   if (cudaMallocHost(&e->h_noise, sizeof(float) * B * PL) != cudaSuccess ||
       cudaMallocHost(&e->h_lat, sizeof(float) * B * PL) != cudaSuccess ||
       cudaMallocHost(&e->h_stop, sizeof(float) * B * 2) != cudaSuccess || !e->noise) {
-    ctts_engine_free(e);
+    engine_destroy(e);
     return set_error(CTTS_ERR_NOMEM, "engine buffers");
   }
   e->prefilled.assign(B, false);
@@ -673,11 +745,13 @@ extern "C" int ctts_engine_prefill(ctts_engine* e, int b, const float* x, int T,
   CTTS_REQ(b >= 0 && b < e->cfg.batch && T > 0, CTTS_ERR_ARG, "bad utterance index or length");
   CTTS_REQ(e->steps_done == 0, CTTS_ERR_STATE, "prefill after the first frame step");
   CTTS_CK(cudaSetDevice(e->lm->device));
-  ctts_kv* kv = e->kv;
+  EngineGroup& g = e->groups[b / e->groups[0].nb];
+  ctts_kv* kv = g.kv;
+  const int lb = b - g.b0;
   const int H = e->lm->cfg.hidden, PL = e->dit->cfg.patch * e->dit->cfg.latent;
   CTTS_REQ(T <= kv->ws_rows, CTTS_ERR_RANGE, "prefill length outside workspace");
   CTTS_CK(cudaMemcpyAsync(kv->xin, x, sizeof(float) * T * H, cudaMemcpyHostToDevice, e->stream));
-  int rc = ctts_lm_prefill_dev(e->lm, kv, b, kv->xin, T, kv->xout, e->stream);
+  int rc = ctts_lm_prefill_dev(e->lm, kv, lb, kv->xin, T, kv->xout, e->stream);
   if (rc) return rc;
   CTTS_CK(cudaMemcpyAsync(e->z + (size_t)b * H, kv->xout + (size_t)(T - 1) * H, sizeof(float) * H,
                           cudaMemcpyDeviceToDevice, e->stream));
@@ -692,10 +766,10 @@ extern "C" int ctts_engine_step_dev(ctts_engine* e, const float* noise_dev, floa
                                     float* stop_dev, void* stream) {
   CTTS_REQ(e && noise_dev, CTTS_ERR_ARG, "null argument");
   CTTS_REQ(e->heads_set, CTTS_ERR_STATE, "engine heads not set");
-  for (int b = 0; b < e->cfg.batch; b++) {
+  for (int b = 0; b < e->cfg.batch; b++)
     CTTS_REQ(e->prefilled[b], CTTS_ERR_STATE, "utterance " + std::to_string(b) + " not prefilled");
-    CTTS_REQ(e->kv->pos_host[b] < e->kv->cap, CTTS_ERR_RANGE, "KV cache full");
-  }
+  for (auto& g : e->groups)
+    for (int b = 0; b < g.nb; b++) CTTS_REQ(g.kv->pos_host[b] < g.kv->cap, CTTS_ERR_RANGE, "KV cache full");
   CTTS_CK(cudaSetDevice(e->lm->device));
   cudaStream_t s = as_stream(stream, e->stream);
   const int B = e->cfg.batch, PL = e->dit->cfg.patch * e->dit->cfg.latent;
@@ -710,19 +784,20 @@ extern "C" int ctts_engine_step_dev(ctts_engine* e, const float* noise_dev, floa
       CTTS_CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
       int n = 0;
       int rc = engine_enqueue(e, s, &n);
-      cudaGraph_t g = nullptr;
-      cudaError_t ce = cudaStreamEndCapture(s, &g);
+      cudaGraph_t gr = nullptr;
+      cudaError_t ce = cudaStreamEndCapture(s, &gr);
       if (rc) {
-        if (g) cudaGraphDestroy(g);
+        if (gr) cudaGraphDestroy(gr);
         return rc;
       }
       CTTS_CK(ce);
-      e->graph = g;
-      CTTS_CK(cudaGraphInstantiate(&e->exec, g, 0));
+      e->graph = gr;
+      CTTS_CK(cudaGraphInstantiate(&e->exec, gr, 0));
     }
     CTTS_CK(cudaGraphLaunch(e->exec, s));
   }
-  for (int b = 0; b < B; b++) e->kv->pos_host[b]++;
+  for (auto& g : e->groups)
+    for (int b = 0; b < g.nb; b++) g.kv->pos_host[b]++;
   e->steps_done++;
   if (latents_dev && latents_dev != e->lat)
     CTTS_CK(cudaMemcpyAsync(latents_dev, e->lat, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
@@ -743,10 +818,13 @@ extern "C" int ctts_engine_step(ctts_engine* e, const float* noise, float* laten
   if (stop_out)
     CTTS_CK(cudaMemcpyAsync(e->h_stop, e->stop, sizeof(float) * B * 2, cudaMemcpyDeviceToHost, e->stream));
   CTTS_CK(cudaStreamSynchronize(e->stream));
-  int err = 0;
-  CTTS_CK(cudaMemcpy(&err, e->kv->err, sizeof(int), cudaMemcpyDeviceToHost));
-  CTTS_REQ(err != 1, CTTS_ERR_RANGE, "device reported a KV position outside capacity");
-  CTTS_REQ(err == 0, CTTS_ERR_TIMEOUT, "a tensor-core linear gave up waiting on its pipeline");
+  for (auto& g : e->groups) {
+    int err = 0, derr = 0;
+    CTTS_CK(cudaMemcpy(&err, g.kv->err, sizeof(int), cudaMemcpyDeviceToHost));
+    CTTS_CK(cudaMemcpy(&derr, g.ws->err, sizeof(int), cudaMemcpyDeviceToHost));
+    CTTS_REQ(err != 1, CTTS_ERR_RANGE, "device reported a KV position outside capacity");
+    CTTS_REQ(err == 0 && derr == 0, CTTS_ERR_TIMEOUT, "a tensor-core linear gave up waiting on its pipeline");
+  }
   memcpy(latents_out, e->h_lat, sizeof(float) * B * PL);
   if (stop_out) memcpy(stop_out, e->h_stop, sizeof(float) * B * 2);
   return CTTS_OK;
@@ -758,14 +836,5 @@ extern "C" void* ctts_engine_stream(const ctts_engine* e) { return e ? (void*)e-
 
 extern "C" void ctts_engine_free(ctts_engine* e) {
   if (!e) return;
-  cudaSetDevice(e->lm->device);
-  if (e->stream) cudaStreamSynchronize(e->stream);
-  if (e->exec) cudaGraphExecDestroy(e->exec);
-  if (e->graph) cudaGraphDestroy(e->graph);
-  if (e->h_noise) cudaFreeHost(e->h_noise);
-  if (e->h_lat) cudaFreeHost(e->h_lat);
-  if (e->h_stop) cudaFreeHost(e->h_stop);
-  if (e->kv) ctts_kv_free(e->kv);
-  if (e->stream) cudaStreamDestroy(e->stream);
-  delete e;
+  engine_destroy(e);
 }

@@ -86,10 +86,20 @@ struct ctts_dit {
   DitWs ws;
 };
 
+struct EngineGroup {
+  int b0 = 0, nb = 0;          // utterances [b0, b0 + nb)
+  ctts_kv* kv = nullptr;       // their KV cache + LM workspace
+  DitWs* ws = nullptr;         // their DiT workspace (owned)
+  cudaStream_t stream = nullptr;
+  cudaEvent_t done = nullptr;
+};
+
 struct ctts_engine {
   ctts_lm* lm = nullptr;
   ctts_dit* dit = nullptr;
-  ctts_kv* kv = nullptr;
+  ctts_kv* kv = nullptr;  // groups[0].kv
+  std::vector<EngineGroup> groups;
+  cudaEvent_t fork = nullptr;
   ctts_engine_config cfg{};
   cudaStream_t stream = nullptr;
   ctts::DevArena arena;

@@ -255,11 +255,12 @@ class FrameEngine(_Handle):
 
     def __init__(self, lm: QwenW, dit: DitW, heads: dict, batch: int, capacity: int,
                  euler_steps: int = 10, latent_scale: float = 1.0, latent_bias: float = 0.0,
-                 use_graph: bool = True):
+                 use_graph: bool = True, groups: int = 1):
         super().__init__()
         self.lm, self.dit = lm, dit
         self.batch = batch
-        c = _lib.EngineConfigC(batch, capacity, euler_steps, latent_scale, latent_bias, int(use_graph))
+        c = _lib.EngineConfigC(batch, capacity, euler_steps, latent_scale, latent_bias, int(use_graph),
+                               groups)
         check(_lib.load().ctts_engine_create(lm.h, dit.h, C.byref(c), C.byref(self.h)))
         sw, sb = _f(heads["stop_predictor.weight"]), _f(heads["stop_predictor.bias"])
         pw, pb = _f(heads["latent_proj.weight"]), _f(heads["latent_proj.bias"])

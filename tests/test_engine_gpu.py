@@ -125,3 +125,56 @@ def test_batched_bf16_tensor_core_path_vs_oracle():
         ref, _, _ = orc.generate(lm_o, dit_o, hw, pres[b], noise[:, b, :], conds[b], 10)
         for f in range(3):
             assert cosine(lat[f, b], ref[f]) >= 0.999, (b, f)
+
+
+def test_sub_batch_groups_match_single_group():
+    """groups=4 splits 32 utterances into 4 chains of 8 (own KV cache, DiT
+    workspace and stream, parallel graph branches); every utterance's latents
+    match the single-chain engine and the oracle, and graph replay equals
+    eager execution bit for bit."""
+    lcfg, dcfg = LMConfig(n_layers=2), DiTConfig(n_layers=2)
+    B = 32
+    rng = np.random.default_rng(7)
+    lens = [5 + (11 * b) % 29 for b in range(B)]
+    pres = [rnd(100 + b, (lens[b], lcfg.hidden)) for b in range(B)]
+    conds = [rnd(200 + b, (64,)) for b in range(B)]
+    noise = rng.standard_normal((3, B, 64), dtype=np.float32)
+    outs = {}
+    for groups, use_graph in ((1, True), (4, True), (4, False), (2, True)):
+        from rcutetts_b200.model import DitW, FrameEngine, QwenW
+
+        lw = synth.lm_weights(lcfg, seed=8, with_embed=False)
+        dw = synth.dit_weights(dcfg, seed=18)
+        hw = synth.frame_weights(lcfg.hidden, dcfg.latent, seed=28)
+        lm = QwenW(lcfg, "bf16").set_weights(lw)
+        dit = DitW(dcfg, "bf16").set_weights(dw)
+        eng = FrameEngine(lm, dit, hw, batch=B, capacity=64, euler_steps=10, use_graph=use_graph,
+                          groups=groups)
+        for b in range(B):
+            eng.prefill(b, pres[b], conds[b])
+        outs[(groups, use_graph)] = np.stack([eng.step(noise[f])[0] for f in range(3)])
+        del eng
+    assert np.array_equal(outs[(4, True)], outs[(4, False)])
+    for key in ((4, True), (2, True)):
+        for b in range(B):
+            for f in range(3):
+                assert cosine(outs[key][f, b], outs[(1, True)][f, b]) >= 0.9999, (key, b, f)
+    lwb, dwb = bf16_weights(lw), bf16_weights(dw)
+    lm_o, dit_o = orc.LM(lcfg, lwb), orc.DiT(dcfg, dwb)
+    for b in (0, 9, 31):
+        ref, _, _ = orc.generate(lm_o, dit_o, hw, pres[b], noise[:, b, :], conds[b], 10)
+        for f in range(3):
+            assert cosine(outs[(4, True)][f, b], ref[f]) >= 0.999, (b, f)
+
+
+def test_groups_must_divide_batch():
+    from rcutetts_b200._lib import ERR_ARG, CttsError
+    from rcutetts_b200.model import DitW, FrameEngine, QwenW
+
+    lcfg, dcfg = LMConfig(n_layers=1), DiTConfig(n_layers=1)
+    lm = QwenW(lcfg, "f32").set_weights(synth.lm_weights(lcfg, seed=9, with_embed=False))
+    dit = DitW(dcfg, "f32").set_weights(synth.dit_weights(dcfg, seed=19))
+    hw = synth.frame_weights(lcfg.hidden, dcfg.latent, seed=29)
+    with pytest.raises(CttsError) as e:
+        FrameEngine(lm, dit, hw, batch=6, capacity=16, groups=4)
+    assert e.value.code == ERR_ARG
