@@ -419,7 +419,7 @@ def main():
     ap.add_argument("--only", default="", choices=["", "c2", "probe"],
                     help="c2: only the batch-1 fp32 config[2] measurement; probe: only the roofline probe")
     ap.add_argument("--b1-frames", type=int, default=197, help="timed frames of the batch-1 run (<= 197)")
-    ap.add_argument("--groups", type=int, default=4,
+    ap.add_argument("--groups", type=int, default=1,
                     help="sub-batches of the 64 utterances run as parallel branches of the frame graph")
     ap.add_argument("--start-frame", type=int, default=-1,
                     help="first warm-up frame (default: timed window centred on the run)")

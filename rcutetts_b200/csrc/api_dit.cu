@@ -2,6 +2,7 @@
 // the per-frame engine (bin/cutetts.rs:429-523 loop body) captured as one
 // CUDA graph per frame.
 #include <cstdio>
+#include <cstdlib>
 
 #include "api_common.h"
 #include "model.h"
@@ -76,6 +77,46 @@ struct DitRun {
   float step_dt = 0.0f;          // step-size embedding input (distill)
   float* out = nullptr;          // predict: v [R, P*L]
 };
+
+// The cluster-resident Euler loop runs when the head has the shapes it is
+// specialised for, the weights are bf16, 16-CTA clusters fit on the GPU
+// and CTTS_DIT_CLUSTER is not 0.  The first call packs the weights
+// (synchronous; the engine's first frame runs outside graph capture).
+bool dit_cluster_ready(ctts_dit* d, int steps) {
+  using Sh = ctts::DitClusterShape;
+  const ctts_dit_config& c = d->cfg;
+  if (!d->bf16 || c.hidden != Sh::kH || c.ffn != Sh::kF || c.n_heads != Sh::kNH || c.n_kv_heads != Sh::kNH ||
+      c.head_dim != Sh::kHD || c.patch != 1 || c.latent != Sh::kL || c.n_layers > Sh::kMaxNL ||
+      steps > Sh::kMaxSteps)
+    return false;
+  if (d->cl_state == 0) {
+    d->cl_state = -1;
+    const char* env = getenv("CTTS_DIT_CLUSTER");
+    if ((!env || atoi(env) != 0) && ctts::dit_cluster_max_active() > 0) {
+      auto* W = new ctts::DitClusterW();
+      std::vector<const void*> q, o, g, dn;
+      std::vector<const float*> n1, n2;
+      for (const DitLayer& L : d->layers) {
+        q.push_back(L.wqkv);
+        o.push_back(L.wo);
+        g.push_back(L.wgu);
+        dn.push_back(L.wd);
+        n1.push_back(L.norm1);
+        n2.push_back(L.norm2);
+      }
+      if (ctts::dit_cluster_pack(*W, c.n_layers, q.data(), o.data(), g.data(), dn.data(), n1.data(),
+                                 n2.data()) == cudaSuccess) {
+        d->cl = W;
+        d->cl_state = 1;
+      } else {
+        (void)cudaGetLastError();
+        ctts::dit_cluster_free(*W);
+        delete W;
+      }
+    }
+  }
+  return d->cl_state == 1;
+}
 
 // Enqueues one DiT sample / predict on stream s with workspace w (sized by
 // dit_ws_ensure).  All pointers device.
@@ -167,6 +208,19 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
   }
 
   // ---- Euler steps (predict_cached, dit.rs:775-814)
+  if (r.mode == 0 && r.x_rows == R && dit_cluster_ready(d, r.steps)) {
+    ctts::DitClusterArgs ca;
+    ca.R = R; ca.NL = NL; ca.steps = r.steps; ca.adaln = use_ad ? 1 : 0; ca.eps = c.rms_eps;
+    for (int i = 0; i < r.steps; i++) ca.dts[i] = r.dts[i];
+    ca.x = r.x; ca.mu = w.mu; ca.temb = w.temb; ca.dtemb = w.dtemb; ca.condh = w.condh;
+    ca.ad = use_ad ? w.ad : nullptr; ca.norms = d->cl->norms; ca.fnorm = d->final_norm;
+    ca.out_w = static_cast<const uint16_t*>(d->out_w); ca.out_b = d->out_b;
+    ca.in_w = static_cast<const uint16_t*>(d->in_w); ca.in_b = d->in_b; ca.inv_freq = d->inv_freq;
+    ca.err = w.err;
+    CTTS_CK(ctts::launch_dit_cluster(*d->cl, ca, s)); nl++;
+    if (launches) *launches += nl;
+    return CTTS_OK;
+  }
   const int xrows = r.x_rows;
   // Euler mode: the step tail (final norm, out_proj, x += dt*v) and the
   // next step's head (in_proj, seq fill) run as one kernel per utterance.
@@ -418,6 +472,11 @@ extern "C" void ctts_dit_free(ctts_dit* d) {
   cudaSetDevice(d->device);
   cudaStreamSynchronize(d->stream);
   cudaStreamDestroy(d->stream);
+  if (d->cl) {
+    cudaDeviceSynchronize();
+    ctts::dit_cluster_free(*d->cl);
+    delete d->cl;
+  }
   delete d;
 }
 

@@ -1,0 +1,1039 @@
+// dit_cluster.cu -- the whole DiT Euler loop of one frame (every step, every
+// layer, the output/feedback tail) as ONE kernel launch on thread-block
+// clusters of 16 CTAs.
+//
+// Replaces the per-step launch chain of dit.rs:775-814 predict_cached /
+// euler_sample (in_proj + seq fill, per layer RMSNorm+AdaLN -> QKV ->
+// 3-token RoPE attention -> o-proj + gated residual -> RMSNorm+AdaLN ->
+// SwiGLU -> down + gated residual, final norm -> out_proj -> x += dt*v).
+//
+// Layout.  A cluster owns kU = 10 utterances (30 token rows: row 3u+s is
+// token s of utterance u) for the whole frame.  CTA c of the cluster owns
+// hidden columns [32c, 32c+32) of the residual stream (fp32, in shared
+// memory for all steps) and one contiguous weight slice per GEMM: 96 QKV
+// rows (half of head c/2), 32 o-proj rows, 192 gate/up rows (SwiGLU columns
+// [96c, 96c+96)), 32 down rows.  Each GEMM is one tcgen05.mma chain
+// D[128 x N] = A[128 x K] . B[N x K]^T with the activations as A (rows
+// 0..29 valid; the descriptor's 8-row groups beyond the fourth read the
+// following shared memory and land in accumulator lanes that are never
+// read) and the weight slice as B, streamed by TMA through a 2-slot ring
+// that runs ahead of the activations across layers and steps (the weights
+// do not depend on them), the accumulator in TMEM.
+//
+// Exchange.  A operands are stored K-major with the 64-byte swizzle as one
+// contiguous slice per CTA ([32-column atom][row group][8 rows x 64 B]), so
+// each stage ends with the compute warp writing its own slice in place and
+// pushing it to the 15 peers with one bulk copy each
+// (cp.async.bulk shared::cta -> shared::cluster), completing on the peer's
+// mbarrier; row statistics, attention score partials, out_proj partials and
+// the new latent go the same way from small staging buffers.  Every
+// mbarrier is armed with its phase's byte count (arrive.expect_tx) by its
+// waiter right after the previous phase completed, which by the stage order
+// is before any peer can push for that phase; consecutive stages never
+// share an mbarrier.  Stages that feed a GEMM (A barriers, two arrivals:
+// the arm and this CTA's own slice) are waited by the MMA thread, the others
+// (B barriers) by the compute warp.  RMSNorm row sums are reduced from the
+// 16 per-CTA partials in CTA order (deterministic), attention scores from
+// the two half-head partials in order, out_proj over the 16 column slices
+// in order.  AdaLN slices of the next layer are prefetched by bulk copies
+// from global memory into a second buffer.
+//
+// Roles (128 threads): warp 0 = compute (lane = token row; TMEM lanes
+// 0..31), warp 1 = MMA issuer (lane 0) and TMEM owner, warp 2 = TMA
+// producer (lane 0).  Every wait is bounded; on timeout the CTA records an
+// error code, tells its peers to stop, waits (bounded) for its own copies
+// and MMAs in flight, and leaves through a final cluster barrier.
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+#include <vector>
+
+#include "dit_cluster.cuh"
+#include "tc_ptx.cuh"
+
+namespace ctts {
+
+namespace {
+
+using Sh = DitClusterShape;
+constexpr int kC = Sh::kC, kH = Sh::kH, kF = Sh::kF, kHD = Sh::kHD, kL = Sh::kL, kU = Sh::kU;
+constexpr int kRows = 3 * kU;          // 30 token rows per cluster
+constexpr int kGrp = (kRows + 7) / 8;  // 4 groups of 8 rows (32 row slots)
+constexpr int kOwn = kH / kC;          // 32 hidden columns per CTA
+constexpr int kActOwn = kF / kC;       // 96 SwiGLU columns per CTA
+constexpr int kQkvN = 3 * kHD / 2;     // 96: q, k, v of half a head
+constexpr int kGuN = 2 * kActOwn;      // 192: gate + up
+// A operands: K-major, no swizzle, one contiguous slice per CTA: slice =
+// [row group g][8-column core kc][8 rows x 16 bytes], so a CTA's share of an
+// operand is one block it can push to its peers with a single bulk copy.
+constexpr uint32_t kSlice = kGrp * (kOwn / 8) * 128;      // 2 KB: 32 columns
+constexpr uint32_t kActSlice = kGrp * (kActOwn / 8) * 128;  // 6 KB: 96 columns
+constexpr uint32_t kXA = 0;                              // norm outputs, K = 512
+constexpr uint32_t kACT = kXA + kC * kSlice;             // SwiGLU outputs, K = 1536 (attention, K = 512, aliased)
+constexpr uint32_t kRING = kACT + kC * kActSlice;        // weight ring
+constexpr uint32_t kSlotBytes = kGuN * 128;              // 24 KB: one 192-row, 64-wide K block
+constexpr int kSlots = 2;
+constexpr uint32_t kF32 = kRING + kSlots * kSlotBytes;
+constexpr int kSeqLd = kOwn + 1;
+constexpr int kAdLd = 6 * kOwn + 4;  // 196: 16-byte rows, 2-way banks at most
+// fp32 area, float offsets from kF32 (exchange buffers 16-byte aligned)
+constexpr int oSEQ = 0;                          // [32][33] residual stream, own columns
+constexpr int oSSR = 1056;                       // [16][32] row sum-of-squares partials, by source CTA
+constexpr int oSSO = oSSR + kC * 32;             // [32] my partials (push source)
+constexpr int oSCR = oSSO + 32;                  // [2][32][3] attention score partials, by half
+constexpr int oSCO = oSCR + 2 * 32 * 3;          // [32][3] my partials
+constexpr int oVR = oSCO + 32 * 3;               // [16][10][4] out_proj partials of my 4 latent columns, by source
+constexpr int oVRO = oVR + kC * kU * 4;          // [16][10][4] my partials, by owner
+constexpr int oXS = oVRO + kC * kU * 4;          // [16][10][4] latent x, by owner: x[u][4c+i]
+constexpr int oXO = oXS + kC * kU * 4;           // [10][4] my updated latent columns
+constexpr int oXN = oXO + kU * 4;                // [10][32] final-normed x rows, own columns
+constexpr int oMU = oXN + kU * kOwn;             // [10][32] mu
+constexpr int oCH = oMU + kU * kOwn;             // [10][32] cond_proj rows
+constexpr int oDT = oCH + kU * kOwn;             // [32] delta-time embedding
+constexpr int oINB = oDT + kOwn;                 // [32] in_proj bias
+constexpr int oFN = oINB + kOwn;                 // [32] final norm
+constexpr int oOUTB = oFN + kOwn;                // [4] out_proj bias of my latent columns (+4 pad)
+constexpr int oIFQ = oOUTB + 8;                  // [16] RoPE frequencies of my dims
+constexpr int oTEMB = oIFQ + 16;                 // [steps][32] time embeddings
+constexpr int oNRM = oTEMB + Sh::kMaxSteps * kOwn;  // [NL][2][32] norm1, norm2
+__host__ __device__ constexpr int oAD(int NL) { return oNRM + NL * 2 * kOwn; }  // [2][10][196] AdaLN, by layer parity
+__host__ __device__ constexpr int f32_floats(int NL) { return oAD(NL) + 2 * kU * kAdLd; }
+static_assert(oSSR >= 32 * kSeqLd && oSSR % 4 == 0 && oSCR % 4 == 0 && oVR % 4 == 0 && oXS % 4 == 0 &&
+                  oXO % 4 == 0 && oVRO % 4 == 0 && oSSO % 4 == 0 && oSCO % 4 == 0 && oNRM % 4 == 0,
+              "exchange buffers must be 16-byte aligned");
+
+// byte offsets of the bf16 tail tables and the barriers
+struct Lay {
+  uint32_t outw, inw, bar;
+  size_t total;
+};
+__host__ __device__ inline Lay lay(int NL) {
+  Lay L;
+  const uint32_t f32_end = kF32 + (uint32_t)f32_floats(NL) * 4u;
+  L.outw = (f32_end + 15u) & ~15u;          // [32 own cols][64 latent] out_proj slice (transposed)
+  L.inw = L.outw + kOwn * kL * 2;           // [64 latent][32 own cols] in_proj slice (transposed)
+  L.bar = (L.inw + kOwn * kL * 2 + 15u) & ~15u;
+  L.total = (size_t)L.bar + 16 * 8 + 16;    // 16 mbarriers, TMEM slot, abort flag
+  return L;
+}
+
+// mbarrier indices
+constexpr int bFULL = 0, bEMPTY = kSlots, bMMA = 2 * kSlots, bFIN = bMMA + 1, bA = bFIN + 1, bB = bA + 2,
+              bAD = bB + 2;
+
+// Optional stage timeline (build with -DCTTS_DIT_TRACE): CTA 0 records
+// (event, %globaltimer) pairs of its compute warp (row 0) and MMA thread.
+#ifdef CTTS_DIT_TRACE
+__device__ long long g_dit_trace[2][8192];
+__device__ int g_dit_trace_n[2];
+CTTS_DEV void dtrace(int role, int ev, int& n) {
+  if (blockIdx.x != 0) return;
+  long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  if (n < 4095) {
+    g_dit_trace[role][2 * n] = ev;
+    g_dit_trace[role][2 * n + 1] = t;
+    n++;
+    g_dit_trace_n[role] = n;
+  }
+}
+#define DTRACE(role, ev) \
+  if (lane == 0) dtrace(role, ev, tr_n)
+#else
+#define DTRACE(role, ev)
+#endif
+
+// per-GEMM geometry: weight rows of the slice (MMA N), 64-wide K blocks,
+// K blocks per ring slot (one TMA box: the packed weights are pre-tiled as
+// [layer][CTA][K block][N rows][64], so a slot is kbps*N contiguous rows),
+// rows of one layer in the row-major slices
+struct Gemm {
+  int N, nkb, kbps, rows_per_layer;
+};
+CTTS_DEV Gemm gemm(int g) {
+  switch (g) {
+    case 0: return {kQkvN, kH / 64, (int)(kSlotBytes / (kQkvN * 128)), kC * kQkvN};
+    case 1: return {kOwn, kH / 64, 4, kH};
+    case 2: return {kGuN, kH / 64, (int)(kSlotBytes / (kGuN * 128)), kC * kGuN};
+    default: return {kOwn, kF / 64, (int)(kSlotBytes / (kOwn * 128)), kH};
+  }
+}
+// bytes a CTA receives from its 15 peers for the A stage of GEMM g
+CTTS_DEV uint32_t a_bytes(int g) { return (uint32_t)(kC - 1) * (g == 3 ? kActSlice : kSlice); }
+
+// Bytes of B stage b (all senders, self included).  Order: the first fill,
+// then per Euler step [scores, row stats, row stats] per layer, out_proj
+// partials, new x, next fill.
+constexpr uint32_t kSsBytes = kC * 128, kScBytes = 2 * 384, kVrBytes = kC * kU * 16;
+CTTS_DEV uint32_t b_bytes(int b, int NL) {
+  if (b == 0) return kSsBytes;
+  const int per = 3 * NL + 3, rem = (b - 1) % per;
+  if (rem < 3 * NL) return rem % 3 == 0 ? kScBytes : kSsBytes;
+  return rem == 3 * NL + 2 ? kSsBytes : kVrBytes;
+}
+
+// Bounded waits that give up early once this CTA is aborting.
+CTTS_DEV bool wait_cluster(uint32_t bar, uint32_t parity, const volatile uint32_t* abort) {
+  for (uint32_t it = 0; it < kWaitLimit; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((it & 255u) == 255u && *abort) return false;
+  }
+  return false;
+}
+CTTS_DEV bool wait_local(uint32_t bar, uint32_t parity, const volatile uint32_t* abort) {
+  for (uint32_t it = 0; it < kWaitLimit; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((it & 255u) == 255u && *abort) return false;
+  }
+  return false;
+}
+
+// arrive (one of the phase's arrivals) and raise its expected bytes
+CTTS_DEV void arm(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+CTTS_DEV void arrive_local(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// bulk copy of `bytes` from this CTA's shared memory into CTA `rank`'s, at
+// the same offsets, completing on that CTA's mbarrier at `bar`
+CTTS_DEV void push(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar, uint32_t rank) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          mapa_shared(dst, rank)),
+      "r"(src), "r"(bytes), "r"(mapa_shared(bar, rank))
+      : "memory");
+}
+CTTS_DEV void st_rc_u32(uint32_t a, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+CTTS_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+CTTS_DEV void st_u4(uint8_t* p, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+  *reinterpret_cast<uint4*>(p) = make_uint4(x, y, z, w);
+}
+
+// Byte offset of the 16-byte chunk holding columns [8kc, 8kc+8) of row r
+// inside a slice: [32-column atom][8-row group][8 rows x 64 B, 64-byte
+// swizzle (chunk ^= (row >> 1) & 3)], so a 32-column slice is 2 KB and the
+// 16 row groups one M=128 MMA reads are 8 KB of contiguous shared memory.
+CTTS_DEV uint32_t slice_off(int r, int kc) {
+  const int rr = r & 7;
+  return (uint32_t)(kc >> 2) * (kGrp * 512u) + (uint32_t)(r >> 3) * 512u + (uint32_t)rr * 64u +
+         ((uint32_t)((kc & 3) ^ ((rr >> 1) & 3)) << 4);
+}
+
+// UMMA descriptor of a K-major operand with 64-byte swizzle: SBO = 512
+// bytes between 8-row groups, LBO unused (1), version 1, layout type 4.
+CTTS_DEV uint64_t desc_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)(512u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)4u << 61;
+  return d;
+}
+
+CTTS_DEV uint32_t pack_bf(float a, float b) { return (uint32_t)f2bf(a) | ((uint32_t)f2bf(b) << 16); }
+
+__global__ void __launch_bounds__(128, 1)
+    dit_cluster_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmO,
+                       const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmD,
+                       const DitClusterArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int NL = a.NL, steps = a.steps;
+  const Lay LY = lay(NL);
+  const uint32_t sb = smem_u32(smem);
+  float* F = reinterpret_cast<float*>(smem + kF32);
+  const uint32_t fb = sb + kF32;  // byte address of F
+  uint16_t* outw_t = reinterpret_cast<uint16_t*>(smem + LY.outw);
+  uint16_t* inw_t = reinterpret_cast<uint16_t*>(smem + LY.inw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY.bar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + LY.bar + 128);
+  volatile uint32_t* abort = reinterpret_cast<volatile uint32_t*>(smem + LY.bar + 132);
+  auto bar = [&](int i) { return sb + LY.bar + 8u * (uint32_t)i; };
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c = (int)cluster_rank();
+  const int U0 = (int)(blockIdx.x / kC) * kU;
+#ifdef CTTS_DIT_TRACE
+  int tr_n = 0;
+#endif
+  const int nvalid = max(0, min(kU, a.R - U0));
+
+  if (tid == 0) {
+    for (int i = 0; i < kSlots; i++) {
+      mbar_init(&bars[bFULL + i], 1);
+      mbar_init(&bars[bEMPTY + i], 1);
+    }
+    mbar_init(&bars[bMMA], 1);
+    mbar_init(&bars[bFIN], 1);
+    mbar_init(&bars[bAD], 1);
+    // A stages: the MMA thread's arm + this CTA's own slice; B stages: the
+    // compute warp's arm (every sender, itself included, pushes bytes)
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&bars[bA + i], 2);
+      mbar_init(&bars[bB + i], 1);
+    }
+    *abort = 0u;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    arm(bar(bA + 0), a_bytes(0));
+    arm(bar(bA + 1), a_bytes(1));
+    arm(bar(bB + 0), b_bytes(0, NL));
+    arm(bar(bB + 1), b_bytes(1, NL));
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(256));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  // the weights do not depend on earlier kernels: the producer fills the
+  // ring before the programmatic-launch wait
+  const CUtensorMap* maps[4] = {&tmQ, &tmO, &tmG, &tmD};
+  uint32_t pit = 0;  // producer: ring slots filled so far
+  int pst = 0, pl = 0, pg = 0, pkb = 0;  // producer position
+  bool pdone = false;
+  auto produce_one = [&]() {
+    const Gemm G = gemm(pg);
+    const int n = min(G.kbps, G.nkb - pkb);
+    const int slot = (int)(pit % kSlots);
+    const uint32_t dst = sb + kRING + (uint32_t)slot * kSlotBytes;
+    mbar_expect_tx(&bars[bFULL + slot], (uint32_t)(n * G.N * 128));
+    const int y = ((pl * kC + c) * G.nkb + pkb) * G.N;
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(maps[pg])), "r"(0), "r"(y), "r"(bar(bFULL + slot))
+        : "memory");
+    pit++;
+    pkb += n;
+    if (pkb >= G.nkb) {
+      pkb = 0;
+      if (++pg == 4) {
+        pg = 0;
+        if (++pl == NL) {
+          pl = 0;
+          if (++pst == steps) pdone = true;
+        }
+      }
+    }
+  };
+  if (warp == 2 && lane == 0)
+    while (!pdone && pit < (uint32_t)kSlots) produce_one();
+  grid_dep_wait();
+
+  // ---- per-CTA constants (every thread)
+  const int adld = NL * 6 * kH;
+  for (int i = tid; i < kC * kU * 4; i += 128) {  // xs[q][u][i] = x[u][4q + i]
+    const int q = i / (kU * 4), u = (i / 4) % kU, k = 4 * q + (i & 3);
+    F[oXS + i] = (u < nvalid) ? a.x[(size_t)(U0 + u) * kL + k] : 0.0f;
+  }
+  for (int i = tid; i < kU * kOwn; i += 128) {
+    const int u = i / kOwn, j = i % kOwn;
+    const bool ok = u < nvalid;
+    F[oMU + i] = ok ? a.mu[(size_t)(U0 + u) * kH + c * kOwn + j] : 0.0f;
+    F[oCH + i] = ok ? a.condh[(size_t)(U0 + u) * kH + c * kOwn + j] : 0.0f;
+  }
+  for (int i = tid; i < 32 * kSeqLd; i += 128) F[oSEQ + i] = 0.0f;
+  for (int j = tid; j < kOwn; j += 128) {
+    F[oDT + j] = a.dtemb[c * kOwn + j];
+    F[oINB + j] = a.in_b ? a.in_b[c * kOwn + j] : 0.0f;
+    F[oFN + j] = a.fnorm[c * kOwn + j];
+  }
+  if (tid < 4) F[oOUTB + tid] = a.out_b ? a.out_b[4 * c + tid] : 0.0f;
+  if (tid < 16) F[oIFQ + tid] = a.inv_freq[16 * (c & 1) + tid];
+  for (int i = tid; i < steps * kOwn; i += 128) F[oTEMB + i] = a.temb[(size_t)(i / kOwn) * kH + c * kOwn + i % kOwn];
+  for (int i = tid; i < NL * 2 * kOwn; i += 128)
+    F[oNRM + i] = a.norms[(size_t)(i / kOwn) * kH + c * kOwn + i % kOwn];
+  // AdaLN slices of layer 0 in buffer 0; invalid utterances stay zero in both
+  for (int i = tid; i < 2 * kU * kAdLd; i += 128) {
+    const int buf = i / (kU * kAdLd), u = (i / kAdLd) % kU, e = i % kAdLd;
+    float v = 0.0f;
+    if (buf == 0 && a.adaln && u < nvalid && e < 6 * kOwn)
+      v = a.ad[(size_t)(U0 + u) * adld + (size_t)(e / kOwn) * kH + c * kOwn + e % kOwn];
+    F[oAD(NL) + i] = v;
+  }
+  for (int i = tid; i < kOwn * kL; i += 128) {
+    const int j = i / kL, o = i % kL;  // outw_t[j][o] = out_w[o][32c + j]
+    outw_t[i] = a.out_w[(size_t)o * kH + c * kOwn + j];
+    const int ii = i / kOwn, jj = i % kOwn;  // inw_t[i][j] = in_w[32c + j][i]
+    inw_t[i] = a.in_w[(size_t)(c * kOwn + jj) * kL + ii];
+  }
+  // the async proxy (bulk copies into the AdaLN buffers) sees the zeros
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncthreads();
+  grid_dep_launch();
+  // every CTA's barriers exist and are armed before any peer pushes
+  cluster_sync();
+
+  const float eps = a.eps;
+  bool ok = true;
+  auto fail = [&](int code) {
+    if (!*abort) {
+      *abort = 1u;
+      if (a.err) atomicExch(a.err, code);
+      for (int d = 0; d < kC; d++) st_rc_u32(mapa_shared(sb + LY.bar + 132, (uint32_t)d), 1u);
+    }
+  };
+
+  if (warp == 2) {
+    // ================= TMA producer (weights)
+    if (lane == 0) {
+      while (!pdone) {
+        const int slot = (int)(pit % kSlots);
+        if (!wait_local(bar(bEMPTY + slot), ((pit / kSlots) - 1) & 1, abort)) {
+          fail(3);
+          break;
+        }
+        produce_one();
+      }
+      // drain: the last fills of every slot have landed
+      const uint32_t n0 = pit > (uint32_t)kSlots ? pit - kSlots : 0;
+      for (uint32_t i = n0; i < pit; i++) wait_local(bar(bFULL + (int)(i % kSlots)), (i / kSlots) & 1, abort);
+    }
+  } else if (warp == 1) {
+    // ================= MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0, aph = 0;
+      for (int st = 0; st < steps && ok; st++)
+        for (int l = 0; l < NL && ok; l++)
+          for (int g = 0; g < 4 && ok; g++) {
+            const Gemm G = gemm(g);
+            const uint32_t ab = bar(bA + (int)(aph & 1));
+            if (!wait_cluster(ab, (aph >> 1) & 1, abort)) {
+              ok = false;
+              break;
+            }
+            arm(ab, a_bytes((g + 2) & 3));  // this barrier's next stage
+            aph++;
+            DTRACE(1, 5);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t idesc = umma_idesc(G.N);
+            const uint32_t abase = sb + ((g == 0 || g == 2) ? kXA : kACT);
+            for (int kb0 = 0; kb0 < G.nkb && ok; kb0 += G.kbps) {
+              const int slot = (int)(it % kSlots);
+              if (!wait_local(bar(bFULL + slot), (it / kSlots) & 1, abort)) {
+                ok = false;
+                break;
+              }
+              asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+              DTRACE(1, 8);
+              const int n = min(G.kbps, G.nkb - kb0);
+              const uint32_t ws = sb + kRING + (uint32_t)slot * kSlotBytes;
+              for (int q = 0; q < n; q++) {
+                const int kb = kb0 + q;
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                  const int ks = 4 * kb + kk;  // K step of 16
+                  // 16-column K step ks: its 32-column atom, +32 bytes for the odd half
+                  const uint32_t aoff = g == 3 ? (uint32_t)(ks / 6) * kActSlice + (uint32_t)((ks % 6) >> 1) * (kGrp * 512u)
+                                               : (uint32_t)(ks >> 1) * kSlice;
+                  const uint64_t ad = desc_sw64(abase + aoff + (uint32_t)(ks & 1) * 32u);
+                  umma_bf16(tmem, ad, umma_desc(ws + (uint32_t)(q * G.N * 128) + kk * 32), idesc,
+                            (kb | kk) ? 1u : 0u);
+                }
+              }
+              umma_commit(&bars[bEMPTY + slot]);
+              it++;
+            }
+            if (ok) umma_commit(&bars[bMMA]);
+            DTRACE(1, 6);
+          }
+      if (!ok) fail(3);
+      // every MMA this thread issued has completed before TMEM is freed
+      umma_commit(&bars[bFIN]);
+      wait_local(bar(bFIN), 0, abort);
+    }
+  } else if (warp == 0) {
+    // ================= compute warp: lane = token row
+    const int r = lane, u = r / 3, s = r % 3;
+    const bool rv = r < kRows;
+    float* seq = F + oSEQ;
+    float* ssr = F + oSSR;
+    float* scr = F + oSCR;
+    float* vr = F + oVR;
+    float* xs = F + oXS;
+    float* xn = F + oXN;
+    float* nrm = F + oNRM;
+    uint32_t bph = 0, aph = 0, gph = 0;
+    // B stage: every lane's staging writes are visible to the bulk copies,
+    // lanes issue the pushes; then wait and re-arm for two stages later
+    auto pushB = [&](uint32_t src_off, uint32_t dst_off, uint32_t bytes, int ndst, bool pair) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      DTRACE(0, 7);
+      const uint32_t bb = bar(bB + (int)(bph & 1));
+      if (lane < ndst) {
+        const uint32_t d = pair ? (uint32_t)(c ^ lane) : (uint32_t)lane;
+        push(sb + dst_off, sb + src_off, bytes, bb, d);
+      }
+    };
+    auto waitB = [&]() {
+      const uint32_t bb = bar(bB + (int)(bph & 1));
+      if (ok && !wait_cluster(bb, (bph >> 1) & 1, abort)) ok = false;
+      if (lane == 0) arm(bb, b_bytes((int)bph + 2, NL));
+      bph++;
+      __syncwarp();
+      DTRACE(0, 3);
+    };
+    // A stage: this CTA's slice (already written in place) to the 15 peers
+    auto postA = [&](uint32_t slice_addr, uint32_t bytes) {
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      DTRACE(0, 7);
+      const uint32_t ab = bar(bA + (int)(aph & 1));
+      if (lane == 0) arrive_local(ab);
+      if (lane < kC && lane != c) push(slice_addr, slice_addr, bytes, ab, (uint32_t)lane);
+      aph++;
+      __syncwarp();
+      DTRACE(0, 1);
+    };
+    auto wait_mma = [&]() {
+      if (ok && !wait_local(bar(bMMA), gph & 1, abort)) ok = false;
+      gph++;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      DTRACE(0, 4);
+    };
+    // row sum of squares of the own columns -> every CTA's ssr[c]
+    auto ss_push = [&]() {
+      float p = 0.0f;
+#pragma unroll 8
+      for (int j = 0; j < kOwn; j++) p = fmaf(seq[r * kSeqLd + j], seq[r * kSeqLd + j], p);
+      F[oSSO + r] = p;
+      pushB(kF32 + oSSO * 4, kF32 + (oSSR + c * 32) * 4, 128, kC, false);
+      waitB();
+    };
+    auto row_inv = [&]() {
+      float ss = 0.0f;
+#pragma unroll
+      for (int q = 0; q < kC; q++) ss += ssr[q * 32 + r];
+      return 1.0f / sqrtf(ss / (float)kH + eps);
+    };
+    // RMSNorm (+ AdaLN modulate) of the own columns -> my slice of the K=512 operand
+    auto norm_slice = [&](const float* adb, int l, int which) {
+      const float inv = row_inv();
+      const float* nw = nrm + (l * 2 + which) * kOwn;
+      const float* md = adb + min(u, kU - 1) * kAdLd + which * 3 * kOwn;  // shift, scale
+      uint32_t pk[16];
+#pragma unroll
+      for (int j = 0; j < kOwn; j += 2) {
+        float e0 = seq[r * kSeqLd + j] * inv * nw[j], e1 = seq[r * kSeqLd + j + 1] * inv * nw[j + 1];
+        if (a.adaln) {
+          e0 = e0 * (1.0f + md[kOwn + j]) + md[j];
+          e1 = e1 * (1.0f + md[kOwn + j + 1]) + md[j + 1];
+        }
+        pk[j >> 1] = pack_bf(e0, e1);
+      }
+      uint8_t* sl = smem + kXA + c * kSlice;
+#pragma unroll
+      for (int kc = 0; kc < 4; kc++)
+        st_u4(sl + slice_off(r, kc), pk[4 * kc], pk[4 * kc + 1], pk[4 * kc + 2], pk[4 * kc + 3]);
+      postA(sb + kXA + c * kSlice, kSlice);
+    };
+    // gated residual update of the own columns from a 32-column accumulator
+    auto resid = [&](const float* adb, int gate_k) {
+      uint32_t v0[16], v1[16];
+      __syncwarp();
+      tmem_ld16_nowait(tmem, v0);
+      tmem_ld16_nowait(tmem + 16, v1);
+      tmem_wait();
+      if (rv) {
+        const float* gt = adb + u * kAdLd + gate_k * kOwn;
+#pragma unroll
+        for (int j = 0; j < kOwn; j++) {
+          const float val = __uint_as_float(j < 16 ? v0[j] : v1[j - 16]);
+          const float coef = a.adaln ? 1.0f + gt[j] : 1.0f;
+          seq[r * kSeqLd + j] = seq[r * kSeqLd + j] + coef * val;
+        }
+      }
+    };
+    // seq rows of step stn: [mu + temb + dtemb; cond; in_proj(x)] (lane = column)
+    auto fill = [&](int stn) {
+      const int j = lane;
+      float acc[kU];
+#pragma unroll
+      for (int uu = 0; uu < kU; uu++) acc[uu] = 0.0f;
+      // in_proj: the utterances' dot products advance together (independent chains)
+#pragma unroll 4
+      for (int i4 = 0; i4 < kL / 4; i4++) {
+        float w4[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) w4[e] = bf2f(inw_t[(4 * i4 + e) * kOwn + j]);
+#pragma unroll
+        for (int uu = 0; uu < kU; uu++) {
+          const float4 xv = *reinterpret_cast<const float4*>(&xs[(i4 * kU + uu) * 4]);
+          acc[uu] = fmaf(w4[0], xv.x, acc[uu]);
+          acc[uu] = fmaf(w4[1], xv.y, acc[uu]);
+          acc[uu] = fmaf(w4[2], xv.z, acc[uu]);
+          acc[uu] = fmaf(w4[3], xv.w, acc[uu]);
+        }
+      }
+#pragma unroll
+      for (int uu = 0; uu < kU; uu++) {
+        seq[(3 * uu) * kSeqLd + j] = (F[oMU + uu * kOwn + j] + F[oTEMB + stn * kOwn + j]) + F[oDT + j];
+        seq[(3 * uu + 1) * kSeqLd + j] = F[oCH + uu * kOwn + j];
+        seq[(3 * uu + 2) * kSeqLd + j] = acc[uu] + F[oINB + j];
+      }
+      __syncwarp();
+      ss_push();
+    };
+
+    fill(0);
+    for (int st = 0; st < steps && ok; st++) {
+      for (int l = 0; l < NL && ok; l++) {
+        const int LG = st * NL + l;  // layer count so far
+        const float* adb = F + oAD(NL) + (LG & 1) * kU * kAdLd;
+        if (a.adaln) {
+          // this layer's slices (prefetched one layer ago)
+          if (LG > 0 && ok && !wait_local(bar(bAD), (LG - 1) & 1, abort)) ok = false;
+        }
+        // S1: norm1 -> my operand slice -> peers
+        norm_slice(adb, l, 0);
+        if (a.adaln) {
+          // the next layer's AdaLN slices into the other buffer, one 128-byte
+          // copy per (utterance, part)
+          if (LG + 1 < steps * NL) {
+            const int ln = (LG + 1) % NL;
+            const uint32_t dst = fb + (uint32_t)(oAD(NL) + ((LG + 1) & 1) * kU * kAdLd) * 4u;
+            if (lane == 0) arm(bar(bAD), (uint32_t)(nvalid * 6 * 128));
+            __syncwarp();
+            if (lane < nvalid)
+              for (int k = 0; k < 6; k++)
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], 128, [%2];" ::"r"(
+                        dst + (uint32_t)(lane * kAdLd + k * kOwn) * 4u),
+                    "l"((uint64_t)__cvta_generic_to_global(a.ad + (size_t)(U0 + lane) * adld + (size_t)ln * 6 * kH +
+                                                          k * kH + c * kOwn)),
+                    "r"(bar(bAD))
+                    : "memory");
+          }
+        }
+        // S2: QKV accumulator -> RoPE -> half-head score partials -> partner
+        wait_mma();
+        if (!ok) break;
+        float q[32], k[32], v[32];
+        {
+          uint32_t t[6][16];
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 6; i++) tmem_ld16_nowait(tmem + 16 * i, t[i]);
+          tmem_wait();
+#pragma unroll
+          for (int i = 0; i < 32; i++) {
+            q[i] = __uint_as_float(t[i >> 4][i & 15]);
+            k[i] = __uint_as_float(t[2 + (i >> 4)][i & 15]);
+            v[i] = __uint_as_float(t[4 + (i >> 4)][i & 15]);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          float sn, cs;
+          sincosf((float)s * F[oIFQ + j], &sn, &cs);
+          float a1 = q[j], a2 = q[j + 16];
+          q[j] = a1 * cs - a2 * sn;
+          q[j + 16] = a1 * sn + a2 * cs;
+          a1 = k[j];
+          a2 = k[j + 16];
+          k[j] = a1 * cs - a2 * sn;
+          k[j + 16] = a1 * sn + a2 * cs;
+        }
+#pragma unroll
+        for (int jt = 0; jt < 3; jt++) {
+          const int src = min(3 * u + jt, 31);
+          float d = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 32; i++) d = fmaf(q[i], __shfl_sync(0xffffffffu, k[i], src), d);
+          F[oSCO + r * 3 + jt] = d;
+        }
+        pushB(kF32 + oSCO * 4, kF32 + (oSCR + (c & 1) * 96) * 4, 384, 2, true);
+        waitB();
+        if (!ok) break;
+        // S3: softmax over the utterance's 3 tokens, P.V on the own dims -> my attention slice
+        {
+          float sc[3], m = -INFINITY;
+          const float scale = 1.0f / sqrtf((float)kHD);
+#pragma unroll
+          for (int jt = 0; jt < 3; jt++) {
+            sc[jt] = (scr[r * 3 + jt] + scr[96 + r * 3 + jt]) * scale;
+            m = fmaxf(m, sc[jt]);
+          }
+          float lsum = 0.0f;
+#pragma unroll
+          for (int jt = 0; jt < 3; jt++) {
+            sc[jt] = expf(sc[jt] - m);
+            lsum += sc[jt];
+          }
+          const float inv = 1.0f / lsum;
+          float o[32];
+#pragma unroll
+          for (int i = 0; i < 32; i++) o[i] = 0.0f;
+#pragma unroll
+          for (int jt = 0; jt < 3; jt++) {
+            const int src = min(3 * u + jt, 31);
+            const float p = sc[jt] * inv;
+#pragma unroll
+            for (int i = 0; i < 32; i++) o[i] = fmaf(p, __shfl_sync(0xffffffffu, v[i], src), o[i]);
+          }
+          // o-proj weights are column-permuted so this slice is K columns [32c, 32c+32)
+          uint8_t* sl = smem + kACT + c * kSlice;
+#pragma unroll
+          for (int kc = 0; kc < 4; kc++)
+            st_u4(sl + slice_off(r, kc), pack_bf(o[8 * kc], o[8 * kc + 1]), pack_bf(o[8 * kc + 2], o[8 * kc + 3]),
+                  pack_bf(o[8 * kc + 4], o[8 * kc + 5]), pack_bf(o[8 * kc + 6], o[8 * kc + 7]));
+          postA(sb + kACT + c * kSlice, kSlice);
+        }
+        // S4: o-proj accumulator -> gated residual -> row statistics
+        wait_mma();
+        if (!ok) break;
+        resid(adb, 2);
+        ss_push();
+        if (!ok) break;
+        // S5: norm2 -> operand
+        norm_slice(adb, l, 1);
+        // S6: gate/up accumulator -> SwiGLU -> my slice of the K=1536 operand
+        wait_mma();
+        if (!ok) break;
+        {
+          uint8_t* sl = smem + kACT + c * kActSlice;
+#pragma unroll 1
+          for (int t3 = 0; t3 < kActOwn / 32; t3++) {
+            uint32_t gv[32], uv[32];
+            __syncwarp();
+            tmem_ld32_nowait(tmem + 32 * t3, gv);
+            tmem_ld32_nowait(tmem + kActOwn + 32 * t3, uv);
+            tmem_wait();
+#pragma unroll
+            for (int h4 = 0; h4 < 4; h4++) {
+              uint32_t pk[4];
+#pragma unroll
+              for (int e = 0; e < 8; e += 2) {
+                const int i0 = 8 * h4 + e;
+                const float g0 = __uint_as_float(gv[i0]), g1 = __uint_as_float(gv[i0 + 1]);
+                pk[e >> 1] = pack_bf(__fdividef(g0, 1.0f + __expf(-g0)) * __uint_as_float(uv[i0]),
+                                     __fdividef(g1, 1.0f + __expf(-g1)) * __uint_as_float(uv[i0 + 1]));
+              }
+              st_u4(sl + slice_off(r, 4 * t3 + h4), pk[0], pk[1], pk[2], pk[3]);
+            }
+          }
+          postA(sb + kACT + c * kActSlice, kActSlice);
+        }
+        // S7: down accumulator -> gated residual -> row statistics
+        wait_mma();
+        if (!ok) break;
+        resid(adb, 5);
+        ss_push();
+      }
+      if (!ok) break;
+      // T1: final norm of the x rows, out_proj partial over the own columns,
+      // 4 latent columns to each owner CTA
+      if (rv && s == 2) {
+        const float inv = row_inv();
+#pragma unroll 8
+        for (int j = 0; j < kOwn; j++) xn[u * kOwn + j] = seq[r * kSeqLd + j] * inv * F[oFN + j];
+      }
+      __syncwarp();
+      {
+        float a0[kU], a1[kU];
+#pragma unroll
+        for (int uu = 0; uu < kU; uu++) a0[uu] = a1[uu] = 0.0f;
+#pragma unroll 4
+        for (int j = 0; j < kOwn; j++) {
+          const float w0 = bf2f(outw_t[j * kL + lane]), w1 = bf2f(outw_t[j * kL + lane + 32]);
+#pragma unroll
+          for (int uu = 0; uu < kU; uu++) {
+            const float xv = xn[uu * kOwn + j];
+            a0[uu] = fmaf(w0, xv, a0[uu]);
+            a1[uu] = fmaf(w1, xv, a1[uu]);
+          }
+        }
+        // owner of latent column o is CTA o/4; vro[owner][uu][o%4]
+#pragma unroll
+        for (int uu = 0; uu < kU; uu++) {
+          F[oVRO + ((lane >> 2) * kU + uu) * 4 + (lane & 3)] = a0[uu];
+          F[oVRO + (((lane + 32) >> 2) * kU + uu) * 4 + (lane & 3)] = a1[uu];
+        }
+      }
+      {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        const uint32_t bb = bar(bB + (int)(bph & 1));
+        if (lane < kC)
+          push(sb + kF32 + (oVR + c * kU * 4) * 4, sb + kF32 + (oVRO + lane * kU * 4) * 4, kU * 16, bb,
+               (uint32_t)lane);
+      }
+      waitB();
+      if (!ok) break;
+      // T2: my 4 latent columns: reduce the 16 partials in order, Euler update
+      for (int e = lane; e < kU * 4; e += 32) {
+        const int uu = e >> 2, i = e & 3;
+        float acc = 0.0f;
+#pragma unroll
+        for (int q2 = 0; q2 < kC; q2++) acc += vr[(q2 * kU + uu) * 4 + i];
+        const float xnew = xs[(c * kU + uu) * 4 + i] + a.dts[st] * (acc + F[oOUTB + i]);
+        if (st + 1 == steps) {
+          if (uu < nvalid) a.x[(size_t)(U0 + uu) * kL + 4 * c + i] = xnew;
+        } else {
+          F[oXO + e] = xnew;
+        }
+      }
+      if (st + 1 == steps) break;
+      pushB(kF32 + oXO * 4, kF32 + (oXS + c * kU * 4) * 4, kU * 16, kC, false);
+      waitB();
+      if (!ok) break;
+      // T3: the next step's sequence
+      fill(st + 1);
+    }
+    if (!ok) fail(3);
+  }
+
+  __syncwarp();
+  __syncthreads();
+  if (*abort) {
+    // let bulk copies already in flight land before any CTA leaves
+    long long t0, t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    do {
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    } while (t1 - t0 < 200000);
+  }
+  // no CTA leaves while a peer may still write into its shared memory
+  cluster_sync();
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
+}
+
+// dst[row][k] = src[row][perm[k]] (o-proj input columns into CTA order)
+__global__ void permute_cols_kernel(uint16_t* dst, const uint16_t* src, const int* perm, int K) {
+  const size_t row = blockIdx.x;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) dst[row * K + k] = src[row * K + perm[k]];
+}
+
+// Pre-tiling: src [blocks*N rows, K] (row-major slices of N rows) ->
+// dst [blocks][K/64][N][64], one 128-byte row per 8 threads.
+__global__ void tile_kernel(uint16_t* dst, const uint16_t* src, int N, int K) {
+  const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int nkb = K / 64;
+  const size_t row = t >> 3;  // dst row
+  const int part = (int)(t & 7);
+  const size_t blk = row / ((size_t)nkb * N);
+  const int kb = (int)((row / N) % nkb), n = (int)(row % N);
+  const uint4* s = reinterpret_cast<const uint4*>(src + (blk * N + n) * K + kb * 64) + part;
+  reinterpret_cast<uint4*>(dst + row * 64)[part] = *s;
+}
+
+// dst row i (K bf16 elements) = src row idx[i]
+__global__ void gather_rows_kernel(uint16_t* dst, const uint16_t* src, const int* idx, int K) {
+  const int i = blockIdx.x;
+  const uint4* s = reinterpret_cast<const uint4*>(src + (size_t)idx[i] * K);
+  uint4* d = reinterpret_cast<uint4*>(dst + (size_t)i * K);
+  for (int t = threadIdx.x; t < K / 8; t += blockDim.x) d[t] = s[t];
+}
+
+cudaError_t set_attrs(size_t smem) {
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  static size_t configured = 0;
+  if (smem <= configured) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(dit_cluster_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(dit_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return e;
+  }
+  configured = smem;
+  return cudaSuccess;
+}
+
+cudaLaunchConfig_t make_cfg(int nclusters, size_t smem, cudaStream_t s, cudaLaunchAttribute* attr, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kC * nclusters, 1, 1);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kC;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cfg;
+}
+
+}  // namespace
+
+size_t dit_cluster_smem(int NL) { return lay(NL).total + 1024; }
+
+int dit_cluster_max_active() {
+  const size_t smem = dit_cluster_smem(Sh::kMaxNL);
+  if (smem > 227 * 1024) return 0;
+  if (set_attrs(smem) != cudaSuccess) return 0;
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = make_cfg(1, smem, nullptr, attr, false);
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, dit_cluster_kernel, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+cudaError_t dit_cluster_pack(DitClusterW& W, int NL, const void* const* wqkv, const void* const* wo,
+                             const void* const* wgu, const void* const* wd, const float* const* norm1,
+                             const float* const* norm2) {
+  if (NL <= 0 || NL > Sh::kMaxNL) return cudaErrorInvalidValue;
+  W.NL = NL;
+  const size_t nq = (size_t)NL * kC * kQkvN * kH, no = (size_t)NL * kH * kH;
+  const size_t ng = (size_t)NL * kC * kGuN * kH, nd = (size_t)NL * kH * kF;
+  cudaError_t e;
+  if ((e = cudaMalloc(&W.qkv, nq * 2)) != cudaSuccess) return e;
+  if ((e = cudaMalloc(&W.o, no * 2)) != cudaSuccess) return e;
+  if ((e = cudaMalloc(&W.gu, ng * 2)) != cudaSuccess) return e;
+  if ((e = cudaMalloc(&W.dn, nd * 2)) != cudaSuccess) return e;
+  if ((e = cudaMalloc(&W.norms, sizeof(float) * NL * 2 * kH)) != cudaSuccess) return e;
+  // row maps
+  std::vector<int> iq(kC * kQkvN), ig(kC * kGuN), iid(kH);
+  for (int c = 0; c < kC; c++) {
+    const int h = c >> 1, hf = c & 1;
+    for (int i = 0; i < kQkvN; i++) {
+      const int part = i / 32, j = i % 32;
+      const int dim = j < 16 ? 16 * hf + j : 32 + 16 * hf + (j - 16);
+      iq[c * kQkvN + i] = part * kH + h * kHD + dim;
+    }
+    for (int i = 0; i < kGuN; i++) {
+      const int n = kActOwn * c + (i % kActOwn);
+      ig[c * kGuN + i] = (n >> 6) * 128 + (i >= kActOwn ? 64 : 0) + (n & 63);
+    }
+  }
+  for (int i = 0; i < kH; i++) iid[i] = i;
+  std::vector<int> pcol(kH);  // o-proj column 32c + j <- attention dim of CTA c
+  for (int c = 0; c < kC; c++)
+    for (int j = 0; j < kOwn; j++) {
+      const int h = c >> 1, hf = c & 1;
+      pcol[c * kOwn + j] = h * kHD + (j < 16 ? 16 * hf + j : 32 + 16 * hf + (j - 16));
+    }
+  int* didx = nullptr;
+  const size_t nidx = iq.size() + ig.size() + iid.size() + pcol.size();
+  if ((e = cudaMalloc(&didx, nidx * sizeof(int))) != cudaSuccess) return e;
+  std::vector<int> all;
+  all.insert(all.end(), iq.begin(), iq.end());
+  all.insert(all.end(), ig.begin(), ig.end());
+  all.insert(all.end(), iid.begin(), iid.end());
+  all.insert(all.end(), pcol.begin(), pcol.end());
+  e = cudaMemcpy(didx, all.data(), nidx * sizeof(int), cudaMemcpyHostToDevice);
+  const int* dq = didx;
+  const int* dg = didx + iq.size();
+  const int* di = dg + ig.size();
+  const int* dp = di + iid.size();
+  for (int l = 0; l < NL && e == cudaSuccess; l++) {
+    gather_rows_kernel<<<kC * kQkvN, 64>>>(W.qkv + (size_t)l * kC * kQkvN * kH,
+                                           static_cast<const uint16_t*>(wqkv[l]), dq, kH);
+    permute_cols_kernel<<<kH, 128>>>(W.o + (size_t)l * kH * kH, static_cast<const uint16_t*>(wo[l]), dp, kH);
+    gather_rows_kernel<<<kC * kGuN, 64>>>(W.gu + (size_t)l * kC * kGuN * kH,
+                                          static_cast<const uint16_t*>(wgu[l]), dg, kH);
+    gather_rows_kernel<<<kH, 64>>>(W.dn + (size_t)l * kH * kF, static_cast<const uint16_t*>(wd[l]), di, kF);
+    e = cudaGetLastError();
+    if (e == cudaSuccess)
+      e = cudaMemcpy(W.norms + (size_t)(l * 2) * kH, norm1[l], sizeof(float) * kH, cudaMemcpyDeviceToDevice);
+    if (e == cudaSuccess)
+      e = cudaMemcpy(W.norms + (size_t)(l * 2 + 1) * kH, norm2[l], sizeof(float) * kH, cudaMemcpyDeviceToDevice);
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(didx);
+  if (e != cudaSuccess) return e;
+  // pre-tile every packed matrix in place (through a scratch copy)
+  uint16_t* tmp = nullptr;
+  if ((e = cudaMalloc(&tmp, std::max(std::max(nq, no), std::max(ng, nd)) * 2)) != cudaSuccess) return e;
+  struct T {
+    uint16_t* p;
+    size_t n;
+    int N, K;
+  } mats[4] = {{W.qkv, nq, kQkvN, kH}, {W.o, no, kOwn, kH}, {W.gu, ng, kGuN, kH}, {W.dn, nd, kOwn, kF}};
+  for (auto& m : mats) {
+    if (e == cudaSuccess) e = cudaMemcpy(tmp, m.p, m.n * 2, cudaMemcpyDeviceToDevice);
+    if (e == cudaSuccess) {
+      const size_t threads = m.n / 64 * 8;
+      tile_kernel<<<(unsigned)((threads + 255) / 256), 256>>>(m.p, tmp, m.N, m.K);
+      e = cudaGetLastError();
+    }
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(tmp);
+  if (e != cudaSuccess) return e;
+  if (!make_map(&W.tm_qkv, W.qkv, (int)(nq / 64), 64, 2 * kQkvN) || !make_map(&W.tm_o, W.o, (int)(no / 64), 64, 4 * kOwn) ||
+      !make_map(&W.tm_gu, W.gu, (int)(ng / 64), 64, kGuN) || !make_map(&W.tm_dn, W.dn, (int)(nd / 64), 64, 6 * kOwn))
+    return cudaErrorInvalidPitchValue;
+  return cudaSuccess;
+}
+
+void dit_cluster_free(DitClusterW& W) {
+  cudaFree(W.qkv);
+  cudaFree(W.o);
+  cudaFree(W.gu);
+  cudaFree(W.dn);
+  cudaFree(W.norms);
+  W = DitClusterW();
+}
+
+cudaError_t launch_dit_cluster(const DitClusterW& W, const DitClusterArgs& a, cudaStream_t s) {
+  if (a.R <= 0) return cudaSuccess;
+  if (a.NL != W.NL || a.steps <= 0 || a.steps > Sh::kMaxSteps) return cudaErrorInvalidValue;
+  const size_t smem = dit_cluster_smem(a.NL);
+  cudaError_t e = set_attrs(dit_cluster_smem(Sh::kMaxNL));
+  if (e != cudaSuccess) return e;
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = make_cfg((a.R + kU - 1) / kU, smem, s, attr, pdl_enabled());
+  e = cudaLaunchKernelEx(&cfg, dit_cluster_kernel, W.tm_qkv, W.tm_o, W.tm_gu, W.tm_dn, a);
+  if (e != cudaSuccess) (void)cudaGetLastError();
+  return e;
+}
+
+}  // namespace ctts
+
+#ifdef CTTS_DIT_TRACE
+// Copies the recorded timeline out (role 0 compute, 1 MMA) and resets it.
+extern "C" __attribute__((visibility("default"))) int ctts_dit_trace(long long* out0, int* n0, long long* out1,
+                                                                     int* n1) {
+  int n[2];
+  cudaMemcpyFromSymbol(n, ctts::g_dit_trace_n, sizeof(n));
+  cudaMemcpyFromSymbol(out0, ctts::g_dit_trace, sizeof(long long) * 8192, 0);
+  cudaMemcpyFromSymbol(out1, ctts::g_dit_trace, sizeof(long long) * 8192, sizeof(long long) * 8192);
+  *n0 = n[0];
+  *n1 = n[1];
+  n[0] = ctts::dit_cluster_max_active();
+  fprintf(stderr, "dit_cluster_max_active=%d\n", n[0]);
+  int z[2] = {0, 0};
+  return cudaMemcpyToSymbol(ctts::g_dit_trace_n, z, sizeof(z)) == cudaSuccess ? 0 : -2;
+}
+#endif

@@ -5,6 +5,7 @@
 #include <vector>
 
 #include "api_common.h"
+#include "dit_cluster.cuh"
 
 // LM stack (replaces QwenW, qwen.rs:26-44).  Weights of a layer are fused
 // into wide matrices at load: [q;k;v] -> wqkv, [gate;up] -> wgu, so one
@@ -84,6 +85,10 @@ struct ctts_dit {
   float* final_norm = nullptr;
   float* inv_freq = nullptr;
   DitWs ws;
+  // cluster-resident Euler loop (dit_cluster.cu): packed weights, state
+  // 0 = not tried, 1 = ready, -1 = shapes/device unsupported or disabled
+  ctts::DitClusterW* cl = nullptr;
+  int cl_state = 0;
 };
 
 struct EngineGroup {

@@ -27,6 +27,7 @@
 
 #include "common.cuh"
 #include "tc_linear.cuh"
+#include "tc_ptx.cuh"
 
 namespace ctts {
 
@@ -34,123 +35,6 @@ namespace {
 
 constexpr int kBK = 64;            // K elements per stage (128 bytes of bf16)
 constexpr int kTileN = 128;        // weight rows per CTA (MMA M)
-constexpr uint32_t kWaitLimit = 1u << 24;
-
-CTTS_DEV uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-CTTS_DEV void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-// Raise the expected transaction bytes without arriving.
-CTTS_DEV void mbar_add_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-CTTS_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-// Bounded wait for the phase with the given parity; false on timeout.
-CTTS_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  const uint32_t a = smem_u32(bar);
-  for (uint32_t it = 0; it < kWaitLimit; ++it) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-  }
-  return false;
-}
-
-CTTS_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-          "r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// UMMA shared-memory matrix descriptor, K-major operand, 128-byte swizzle:
-// rows of 128 bytes, 8-row groups 1024 bytes apart (SBO), LBO unused (1),
-// version 1 (sm_100), layout type 2 (SWIZZLE_128B).
-CTTS_DEV uint64_t umma_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)1u << 16;
-  d |= (uint64_t)(1024u >> 4) << 32;
-  d |= (uint64_t)1u << 46;
-  d |= (uint64_t)2u << 61;
-  return d;
-}
-
-// Instruction descriptor: D f32, A/B bf16, both K-major, M = 128, N = nmma.
-CTTS_DEV uint32_t umma_idesc(int nmma) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(nmma >> 3) << 17) |
-         ((uint32_t)(kTileN >> 4) << 24);
-}
-
-CTTS_DEV void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-
-CTTS_DEV void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
-
-// 16 consecutive TMEM columns of this thread's lane; no wait (see tmem_wait).
-CTTS_DEV void tmem_ld16_nowait(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-        "=r"(r[15])
-      : "r"(taddr));
-}
-CTTS_DEV void tmem_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-CTTS_DEV void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// Address of the same shared-memory offset in CTA `rank` of this cluster.
-CTTS_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-
-CTTS_DEV uint32_t ld_dsmem_u32(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
-  return v;
-}
-
-CTTS_DEV float4 ld_dsmem_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
-}
-
 // Epilogue of four adjacent output columns of row m, y = res + coef * val
 // (coef = 1 + AdaLN gate, or `scale`), split in two halves so a thread can
 // issue the global loads of several output units before any of their stores.
@@ -410,9 +294,8 @@ __global__ void __launch_bounds__(128)
 
 // ---------------------------------------------------------- host helpers
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+}  // namespace
+
 
 EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
@@ -429,6 +312,7 @@ EncodeTiledFn encode_fn() {
 
 // 2D bf16 tensor [rows, cols] (cols contiguous), box [box_rows, 64], SW128.
 bool make_map(CUtensorMap* m, const void* base, int rows, int cols, int box_rows) {
+  constexpr int kBK = 64;
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -441,7 +325,6 @@ bool make_map(CUtensorMap* m, const void* base, int rows, int cols, int box_rows
   return r == CUDA_SUCCESS;
 }
 
-}  // namespace
 
 int tc_num_sms() {
   static int n = 0;

@@ -178,3 +178,25 @@ def test_groups_must_divide_batch():
     with pytest.raises(CttsError) as e:
         FrameEngine(lm, dit, hw, batch=6, capacity=16, groups=4)
     assert e.value.code == ERR_ARG
+
+
+def test_cluster_dit_path_is_one_launch(monkeypatch):
+    """bf16 engine at the benchmark DiT shape: the whole Euler loop of a
+    frame is one launch (CTTS_DIT_CLUSTER unset) instead of the per-step
+    chain, with the same latents."""
+    lcfg, dcfg = LMConfig(n_layers=1), DiTConfig()
+    B = 16
+    res = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("CTTS_DIT_CLUSTER", flag)
+        eng, keep, lw, dw, hw = build(lcfg, dcfg, seed=11, dtype="bf16", batch=B, capacity=32)
+        for b in range(B):
+            eng.prefill(b, rnd(300 + b, (4 + b % 5, lcfg.hidden)), rnd(400 + b, (64,)))
+        noise = rnd(500, (2, B, 64))
+        lat = np.stack([eng.step(noise[f])[0] for f in range(2)])
+        res[flag] = (lat, eng.launches_per_step)
+        del eng
+    assert res["1"][1] + 200 < res["0"][1], (res["1"][1], res["0"][1])
+    for f in range(2):
+        for b in range(B):
+            assert cosine(res["1"][0][f, b], res["0"][0][f, b]) >= 0.9999, (f, b)
