@@ -164,7 +164,10 @@ extern "C" int ctts_kv_alloc(const ctts_lm* lm, int batch, int capacity, ctts_kv
   kv->pos_host.assign(batch, 0);
   const int rows = std::max(batch, capacity);
   const int H = c.hidden, qd = c.n_heads * c.head_dim, kvd = c.n_kv_heads * c.head_dim;
-  kv->nsplit = (capacity + 127) / 128;
+  // keys per attention split: small batches use short splits so the
+  // decode attention still spreads over many SMs
+  kv->chunk = batch >= 16 ? 128 : 32;
+  kv->nsplit = (capacity + kv->chunk - 1) / kv->chunk;
   kv->ws_rows = rows;
   kv->h = kv->arena.alloc<float>((size_t)rows * H);
   kv->qkv = kv->arena.alloc<float>((size_t)rows * (qd + 2 * kvd));
@@ -172,10 +175,11 @@ extern "C" int ctts_kv_alloc(const ctts_lm* lm, int batch, int capacity, ctts_kv
   kv->att = kv->arena.alloc<float>((size_t)rows * qd);
   kv->act = kv->arena.alloc<float>((size_t)rows * c.ffn);
   kv->part = kv->arena.alloc<float>((size_t)batch * c.n_heads * kv->nsplit * (c.head_dim + 2));
+  kv->cnt = kv->arena.alloc<int>((size_t)batch * c.n_kv_heads);
   kv->xin = kv->arena.alloc<float>((size_t)rows * H);
   kv->xout = kv->arena.alloc<float>((size_t)rows * H);
   if (!kv->k || !kv->v || !kv->pos || !kv->h || !kv->qkv || !kv->qrot || !kv->att || !kv->act ||
-      !kv->part || !kv->xin || !kv->xout) {
+      !kv->part || !kv->cnt || !kv->xin || !kv->xout) {
     delete kv;
     return set_error(CTTS_ERR_NOMEM, "KV cache allocation failed");
   }
@@ -273,14 +277,14 @@ int lm_forward_rows(ctts_lm* lm, ctts_kv* kv, int rows, int prefill_b, int pos0,
     a.kcache = reinterpret_cast<uint8_t*>(kv->k) + (size_t)l * kv->layer_elems * es;
     a.vcache = reinterpret_cast<uint8_t*>(kv->v) + (size_t)l * kv->layer_elems * es;
     a.kv_bf16 = lm->bf16; a.cap = kv->cap; a.batch = kv->batch;
-    a.qrot = kv->qrot; a.out = kv->att; a.part = kv->part; a.nsplit = kv->nsplit; a.chunk = 128;
-    a.err = kv->err;
+    a.qrot = kv->qrot; a.out = kv->att; a.part = kv->part; a.nsplit = kv->nsplit; a.chunk = kv->chunk;
+    a.cnt = kv->cnt; a.err = kv->err;
     if (tc) a.out_b = kv->attb;
-    CTTS_CK(launch_qk_rope_append(a, s)); nl++;
     if (prefill_b >= 0) {
+      CTTS_CK(launch_qk_rope_append(a, s)); nl++;
       CTTS_CK(launch_attn_prefill(a, s)); nl++;
-    } else {
-      CTTS_CK(launch_attn_decode(a, s)); nl += 2;
+    } else {  // norm/RoPE, KV append, attention and split merge in one launch
+      CTTS_CK(launch_attn_decode(a, s)); nl++;
     }
 
     if (tc) {

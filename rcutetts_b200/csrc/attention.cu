@@ -1,13 +1,11 @@
 // attention.cu -- LM attention blocks and small LM ops.
 //
 // qk_rope_append: QK-Norm + NeoX RoPE of the new q/k rows and the KV-cache
-//   append (qwen.rs:323-340 decode, 255-272 prefill).
-// attn_decode: GQA decode attention over each utterance's ragged cache
-//   (qwen.rs:341-362).  Split over the sequence so a batch of one still
-//   fills the GPU: CTA (split, kv_head, utterance) scores its chunk of keys
-//   for all query heads of the group (the K/V rows are read once per group,
-//   not once per query head), then a combine pass merges the splits with
-//   the usual max-rescaled softmax sums.
+//   append for prefill rows (qwen.rs:255-272).
+// attn_step: the whole decode-step attention of a layer in one launch --
+//   query QK-Norm + RoPE, KV append of the new row, GQA attention over each
+//   utterance's ragged cache (qwen.rs:323-362), split over the sequence so
+//   a batch of one still fills the GPU, splits merged by the last CTA.
 // attn_prefill: causal attention of T new rows against the cache
 //   (qwen.rs:273-297).
 #include "common.cuh"
@@ -104,170 +102,284 @@ __global__ void __launch_bounds__(128) qk_rope_append_kernel(const AttnArgs a) {
   }
 }
 
-// grid (nsplit, nkv, batch), 128 threads.  Partial layout per
-// (b, q head, split): [m, l, acc[hd]].
-template <bool BF>
-__global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
-  grid_dep_enter();
-  const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
-  const int hd = a.hd, nq = a.nq, nkv = a.nkv;
-  const int G = nq / nkv;
-  const int tid = threadIdx.x;
-  const int n = min(a.pos[b] + 1, a.cap);  // keys incl. the row appended this step
-  const int r0 = split * a.chunk;
-  const int r1 = min(r0 + a.chunk, n);
-  float* part_base = a.part + (((size_t)b * nq + kh * G) * a.nsplit + split) * (hd + 2);
-  const size_t pstride = (size_t)a.nsplit * (hd + 2);
-
-  __shared__ __align__(16) float qs[kMaxG * kMaxHd];
-  __shared__ float sc[kMaxG][128];
+// Fused decode step of one layer's attention (qwen.rs:323-362): QK-Norm +
+// NeoX RoPE of the step's queries, the KV-cache append of the new key/value
+// row, GQA attention over each utterance's ragged cache and the merge of
+// the sequence splits -- one launch.
+//
+// grid (nsplit, nkv, batch), 128 threads.  CTA (split, kv head, utterance)
+// owns keys [split*chunk, +chunk) of that utterance.  The cached rows of
+// the range are contiguous in the cache ([b][kv head][cap][hd]), so one bulk
+// copy each brings K and V into shared memory, issued before the wait on the
+// previous kernel (they were written frames ago).  The CTA whose range
+// holds the new position also normalises/rotates the new key, rounds it to
+// the cache type and writes it to the cache and to its shared tile.  Every
+// query head of the group is scored against the tile (K/V read once per
+// group), the online-softmax partial [m, l, acc[hd]] goes to global memory,
+// and the last CTA of the (utterance, kv head) -- an atomic ticket --
+// merges the splits in split order (deterministic) and writes the output.
+template <bool BF, int HD>
+__global__ void __launch_bounds__(128) attn_step_kernel(const AttnArgs a) {
+  constexpr int ES = BF ? 2 : 4;
+  constexpr int ROWB = HD * ES;     // bytes of one cache row
+  constexpr int NC = ROWB / 16;     // 16-byte chunks per row
+  constexpr int VPC = 16 / ES;      // values per chunk
+  constexpr int PER = HD / 32;      // values per lane of a head vector
+  constexpr int HP = HD / 2;        // dim pairs
+  constexpr int PARTS = 128 / HP;   // key partitions of the P.V pass
+  extern __shared__ __align__(128) uint8_t kv_smem[];
+  __shared__ __align__(16) float qs[kMaxG][HD];
+  __shared__ float ps[kMaxG][128];
   __shared__ float red[kMaxG][4];
   __shared__ float stat[kMaxG][2];
-  __shared__ __align__(16) float accs[kMaxG][kMaxHd];
+  __shared__ __align__(16) float accs[PARTS][kMaxG][HD];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int s_last;
 
-  if (r0 >= r1) {  // empty split: neutral partial
-    for (int i = tid; i < G * (hd + 2); i += blockDim.x) {
-      int g = i / (hd + 2), c = i % (hd + 2);
-      part_base[g * pstride + c] = c == 0 ? -INFINITY : 0.0f;
-    }
-    return;
-  }
-  const float scale = 1.0f / sqrtf((float)hd);
-  for (int i = tid; i < G * hd; i += blockDim.x) {
-    int g = i / hd, d = i % hd;
-    qs[i] = a.qrot[(size_t)b * nq * hd + (kh * G + g) * hd + d];
-  }
-  __syncthreads();
+  const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nq = a.nq, nkv = a.nkv, G = nq / nkv, chunk = a.chunk;
+  uint8_t* Ks = kv_smem;
+  uint8_t* Vs = kv_smem + (size_t)chunk * ROWB;
+  const uint32_t bar_a = static_cast<uint32_t>(__cvta_generic_to_shared(&bar));
 
-  const size_t kvbase = ((size_t)b * nkv + kh) * a.cap * hd;
-  // phase 1: one thread per key row
-  const int j = r0 + tid;
-  float s[kMaxG];
+  const int pos = a.pos[b];
+  const bool bad = pos < 0 || pos >= a.cap;
+  const int n = bad ? 0 : pos + 1;  // keys incl. the row appended this step
+  const int r0 = split * chunk, r1 = min(r0 + chunk, n);
+  const int nrows = max(0, r1 - r0);
+  const int ncached = max(0, min(r1, pos) - r0);  // rows already in the cache
+  const size_t row0 = ((size_t)b * nkv + kh) * a.cap;  // cache row of key 0
+  // the barrier is initialised before any thread can wait on it or any
+  // copy can complete on it
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_a));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid == 0) {
+    if (ncached > 0) {
+      const uint32_t bytes = (uint32_t)ncached * ROWB;
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_a), "r"(2 * bytes)
+                   : "memory");
+      const uint8_t* ksrc = reinterpret_cast<const uint8_t*>(a.kcache) + (row0 + r0) * ROWB;
+      const uint8_t* vsrc = reinterpret_cast<const uint8_t*>(a.vcache) + (row0 + r0) * ROWB;
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       static_cast<uint32_t>(__cvta_generic_to_shared(Ks))),
+                   "l"(ksrc), "r"(bytes), "r"(bar_a)
+                   : "memory");
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       static_cast<uint32_t>(__cvta_generic_to_shared(Vs))),
+                   "l"(vsrc), "r"(bytes), "r"(bar_a)
+                   : "memory");
+    }
+  }
+  grid_dep_enter();
+  if (bad && split == 0 && tid == 0 && a.err) atomicExch(a.err, 1);
+
+  // ---- queries (and the new key/value row in its split): one warp per job
+  const bool has_new = !bad && pos >= r0 && pos < r1;
+  const int width = (nq + 2 * nkv) * HD;
+  const float* src_row = a.qkv + (size_t)b * width;
+  const int jobs = nrows > 0 ? G + (has_new ? 2 : 0) : 0;
+  for (int job = warp; job < jobs; job += 4) {
+    const bool is_q = job < G, is_v = job == G + 1;
+    const int head = is_q ? kh * G + job : (is_v ? nq + nkv + kh : nq + kh);
+    const float* src = src_row + head * HD;
+    float v[PER];
 #pragma unroll
-  for (int g = 0; g < kMaxG; g++) s[g] = -INFINITY;
-  if (j < r1) {
+    for (int j = 0; j < PER; j++) v[j] = src[lane + 32 * j];
+    if (!is_v) {
+      const float* gn = is_q ? a.qn : a.kn;
+      if (gn) {
+        float ss = 0.0f;
 #pragma unroll
-    for (int g = 0; g < kMaxG; g++) s[g] = 0.0f;
-    const size_t kr = kvbase + (size_t)j * hd;
-#pragma unroll 8
-    for (int d = 0; d < hd; d += 8) {
-      float kv[8];
-      if (BF) {
-        uint4 t = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.kcache) + kr + d);
-        kv[0] = bf_lo(t.x); kv[1] = bf_hi(t.x); kv[2] = bf_lo(t.y); kv[3] = bf_hi(t.y);
-        kv[4] = bf_lo(t.z); kv[5] = bf_hi(t.z); kv[6] = bf_lo(t.w); kv[7] = bf_hi(t.w);
-      } else {
-        const float* kp = reinterpret_cast<const float*>(a.kcache) + kr + d;
-        float4 t0 = *reinterpret_cast<const float4*>(kp);
-        float4 t1 = *reinterpret_cast<const float4*>(kp + 4);
-        kv[0] = t0.x; kv[1] = t0.y; kv[2] = t0.z; kv[3] = t0.w;
-        kv[4] = t1.x; kv[5] = t1.y; kv[6] = t1.z; kv[7] = t1.w;
+        for (int j = 0; j < PER; j++) ss = fmaf(v[j], v[j], ss);
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+#pragma unroll
+        for (int j = 0; j < PER; j++) v[j] = v[j] * inv * gn[lane + 32 * j];
       }
+      // rotate-half: element i pairs with i + HD/2 (same lane, j + PER/2)
 #pragma unroll
-      for (int g = 0; g < kMaxG; g++) {
-        if (g >= G) break;
-        const float* q = qs + g * hd + d;
-#pragma unroll
-        for (int e = 0; e < 8; e++) s[g] = fmaf(q[e], kv[e], s[g]);
+      for (int j = 0; j < PER / 2; j++) {
+        const int i = lane + 32 * j;
+        float sn, cs;
+        sincosf((float)pos * a.inv_freq[i], &sn, &cs);
+        const float x1 = v[j], x2 = v[j + PER / 2];
+        v[j] = x1 * cs - x2 * sn;
+        v[j + PER / 2] = x1 * sn + x2 * cs;
       }
     }
+    if (is_q) {
 #pragma unroll
-    for (int g = 0; g < kMaxG; g++) s[g] *= scale;
-  }
-  // phase 2: max and sum per head
-  const int lane = tid & 31, warp = tid >> 5;
+      for (int j = 0; j < PER; j++) qs[job][lane + 32 * j] = v[j];
+    } else {
+      void* cache = is_v ? a.vcache : a.kcache;
+      uint8_t* tile = (is_v ? Vs : Ks) + (size_t)(pos - r0) * ROWB;
 #pragma unroll
-  for (int g = 0; g < kMaxG; g++) {
-    if (g >= G) break;
-    float m = warp_max(s[g]);
-    if (lane == 0) red[g][warp] = m;
-  }
-  __syncthreads();
-  if (tid < G) {
-    float m = fmaxf(fmaxf(red[tid][0], red[tid][1]), fmaxf(red[tid][2], red[tid][3]));
-    stat[tid][0] = m;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int g = 0; g < kMaxG; g++) {
-    if (g >= G) break;
-    float p = j < r1 ? expf(s[g] - stat[g][0]) : 0.0f;
-    sc[g][tid] = p;
-    float l = warp_sum(p);
-    if (lane == 0) red[g][warp] = l;
-  }
-  __syncthreads();
-  if (tid < G) stat[tid][1] = red[tid][0] + red[tid][1] + red[tid][2] + red[tid][3];
-  __syncthreads();
-  // phase 3: P.V ; thread -> (dim d, row partition)
-  const int parts = blockDim.x / hd;  // 2 for hd=64
-  const int d = tid % hd, pp = tid / hd;
-  float acc[kMaxG];
-#pragma unroll
-  for (int g = 0; g < kMaxG; g++) acc[g] = 0.0f;
-  if (pp < parts) {
-    // eight V rows in flight per iteration
-    for (int j0 = r0 + pp; j0 < r1; j0 += 8 * parts) {
-      float vv[8];
-#pragma unroll
-      for (int u = 0; u < 8; u++) {
-        const int jj = j0 + u * parts;
-        vv[u] = jj < r1 ? ld_kv<BF>(a.vcache, kvbase + (size_t)jj * hd + d) : 0.0f;
-      }
-#pragma unroll
-      for (int u = 0; u < 8; u++) {
-        const int jj = j0 + u * parts;
-        if (jj >= r1) break;
-#pragma unroll
-        for (int g = 0; g < kMaxG; g++) {
-          if (g >= G) break;
-          acc[g] = fmaf(sc[g][jj - r0], vv[u], acc[g]);
+      for (int j = 0; j < PER; j++) {
+        const int d = lane + 32 * j;
+        if constexpr (BF) {
+          const uint16_t hb = f2bf(v[j]);
+          reinterpret_cast<uint16_t*>(cache)[(row0 + pos) * HD + d] = hb;
+          reinterpret_cast<uint16_t*>(tile)[d] = hb;
+        } else {
+          reinterpret_cast<float*>(cache)[(row0 + pos) * HD + d] = v[j];
+          reinterpret_cast<float*>(tile)[d] = v[j];
         }
       }
     }
   }
-  for (int p2 = 1; p2 < parts; p2++) {
-    __syncthreads();
-    if (pp == p2)
-      for (int g = 0; g < G; g++) accs[g][d] = acc[g];
-    __syncthreads();
-    if (pp == 0)
-      for (int g = 0; g < G; g++) acc[g] += accs[g][d];
+  if (ncached > 0) {
+    bool ok = false;
+    for (uint32_t it = 0; it < (1u << 24) && !ok; ++it) {
+      uint32_t done;
+      asm volatile(
+          "{\n\t.reg .pred p;\n\t"
+          "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\t"
+          "selp.u32 %0, 1, 0, p;\n\t}"
+          : "=r"(done)
+          : "r"(bar_a)
+          : "memory");
+      ok = done != 0;
+    }
+    if (!ok && a.err) atomicExch(a.err, 3);
   }
   __syncthreads();
-  if (pp == 0) {
-    for (int g = 0; g < G; g++) {
-      float* pb = part_base + g * pstride;
-      pb[2 + d] = acc[g];
-      if (d == 0) {
-        pb[0] = stat[g][0];
-        pb[1] = stat[g][1];
+
+  if (nrows > 0) {
+    // ---- scores: one key per thread; the 16-byte chunks of a row are
+    // visited in a per-thread rotated order (no bank conflicts)
+    const float scale = 1.0f / sqrtf((float)HD);
+    float sc[kMaxG];
+#pragma unroll
+    for (int g = 0; g < kMaxG; g++) sc[g] = -INFINITY;
+    if (tid < nrows) {
+#pragma unroll
+      for (int g = 0; g < kMaxG; g++) sc[g] = 0.0f;
+      const uint8_t* krow = Ks + (size_t)tid * ROWB;
+#pragma unroll 4
+      for (int cc = 0; cc < NC; cc++) {
+        const int c = (cc + tid) % NC;
+        const uint4 t = *reinterpret_cast<const uint4*>(krow + c * 16);
+        float kv[VPC];
+        if constexpr (BF) {
+          kv[0] = bf_lo(t.x); kv[1] = bf_hi(t.x); kv[2] = bf_lo(t.y); kv[3] = bf_hi(t.y);
+          kv[4] = bf_lo(t.z); kv[5] = bf_hi(t.z); kv[6] = bf_lo(t.w); kv[7] = bf_hi(t.w);
+        } else {
+          kv[0] = __uint_as_float(t.x); kv[1] = __uint_as_float(t.y);
+          kv[2] = __uint_as_float(t.z); kv[3] = __uint_as_float(t.w);
+        }
+#pragma unroll
+        for (int g = 0; g < kMaxG; g++) {
+          if (g >= G) break;
+          const float* q = qs[g] + c * VPC;
+#pragma unroll
+          for (int e = 0; e < VPC; e++) sc[g] = fmaf(q[e], kv[e], sc[g]);
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < kMaxG; g++) sc[g] *= scale;
+    }
+    // ---- softmax statistics of the split
+#pragma unroll
+    for (int g = 0; g < kMaxG; g++) {
+      if (g >= G) break;
+      const float m = warp_max(sc[g]);
+      if (lane == 0) red[g][warp] = m;
+    }
+    __syncthreads();
+    if (tid < G) stat[tid][0] = fmaxf(fmaxf(red[tid][0], red[tid][1]), fmaxf(red[tid][2], red[tid][3]));
+    __syncthreads();
+#pragma unroll
+    for (int g = 0; g < kMaxG; g++) {
+      if (g >= G) break;
+      const float p = tid < nrows ? expf(sc[g] - stat[g][0]) : 0.0f;
+      ps[g][tid] = p;
+      const float l = warp_sum(p);
+      if (lane == 0) red[g][warp] = l;
+    }
+    __syncthreads();
+    if (tid < G) stat[tid][1] = red[tid][0] + red[tid][1] + red[tid][2] + red[tid][3];
+    // ---- P.V: thread -> (dim pair, key partition)
+    const int dp = tid % HP, pp = tid / HP;
+    float acc[kMaxG][2];
+#pragma unroll
+    for (int g = 0; g < kMaxG; g++) acc[g][0] = acc[g][1] = 0.0f;
+    for (int j = pp; j < nrows; j += PARTS) {
+      float v0, v1;
+      if constexpr (BF) {
+        const uint32_t t = reinterpret_cast<const uint32_t*>(Vs + (size_t)j * ROWB)[dp];
+        v0 = bf_lo(t);
+        v1 = bf_hi(t);
+      } else {
+        const float2 t = reinterpret_cast<const float2*>(Vs + (size_t)j * ROWB)[dp];
+        v0 = t.x;
+        v1 = t.y;
+      }
+#pragma unroll
+      for (int g = 0; g < kMaxG; g++) {
+        if (g >= G) break;
+        const float p = ps[g][j];
+        acc[g][0] = fmaf(p, v0, acc[g][0]);
+        acc[g][1] = fmaf(p, v1, acc[g][1]);
       }
     }
+#pragma unroll
+    for (int g = 0; g < kMaxG; g++) {
+      if (g >= G) break;
+      accs[pp][g][2 * dp] = acc[g][0];
+      accs[pp][g][2 * dp + 1] = acc[g][1];
+    }
+    __syncthreads();
+    // ---- partial [m, l, acc[HD]] per query head, partitions summed in order
+    const size_t pstride = (size_t)a.nsplit * (HD + 2);
+    float* pbase = a.part + (((size_t)b * nq + kh * G) * a.nsplit + split) * (HD + 2);
+    for (int i = tid; i < G * HD; i += 128) {
+      const int g = i / HD, d = i % HD;
+      float t = 0.0f;
+#pragma unroll
+      for (int q = 0; q < PARTS; q++) t += accs[q][g][d];
+      pbase[g * pstride + 2 + d] = t;
+    }
+    if (tid < G) {
+      pbase[tid * pstride] = stat[tid][0];
+      pbase[tid * pstride + 1] = stat[tid][1];
+    }
   }
-}
-
-// grid (batch, nq), hd threads
-__global__ void attn_combine_kernel(const AttnArgs a) {
-  grid_dep_enter();
-  const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
-  const int hd = a.hd;
-  const float* p = a.part + ((size_t)b * a.nq + h) * a.nsplit * (hd + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < a.nsplit; s++) M = fmaxf(M, p[s * (hd + 2)]);
-  float L = 0.0f, acc = 0.0f;
-  for (int s = 0; s < a.nsplit; s++) {
-    const float* ps = p + s * (hd + 2);
-    if (ps[0] == -INFINITY) continue;
-    float w = expf(ps[0] - M);
-    L = fmaf(ps[1], w, L);
-    acc = fmaf(ps[2 + d], w, acc);
+  // ---- ticket: the last CTA of (utterance, kv head) merges the splits
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    int* cnt = a.cnt + (size_t)b * nkv + kh;
+    const int t = atomicAdd(cnt, 1);
+    s_last = t == a.nsplit - 1;
+    if (s_last) *cnt = 0;  // ready for the next launch
   }
-  const size_t o = (size_t)b * a.nq * hd + h * hd + d;
-  if (a.out_b)
-    a.out_b[o] = f2bf(acc / L);
-  else
-    a.out[o] = acc / L;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int nsa = (n + chunk - 1) / chunk;  // splits that hold keys
+  for (int i = tid; i < G * HD; i += 128) {
+    const int g = i / HD, d = i % HD, h = kh * G + g;
+    const float* pb = a.part + ((size_t)b * nq + h) * a.nsplit * (HD + 2);
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < nsa; s2++) M = fmaxf(M, __ldcg(pb + (size_t)s2 * (HD + 2)));
+    float L = 0.0f, acc = 0.0f;
+    for (int s2 = 0; s2 < nsa; s2++) {
+      const float* q = pb + (size_t)s2 * (HD + 2);
+      const float w = expf(__ldcg(q) - M);
+      L = fmaf(__ldcg(q + 1), w, L);
+      acc = fmaf(__ldcg(q + 2 + d), w, acc);
+    }
+    const float o = nsa > 0 ? acc / L : 0.0f;
+    const size_t oi = (size_t)b * nq * HD + (size_t)h * HD + d;
+    if (a.out_b)
+      a.out_b[oi] = f2bf(o);
+    else
+      a.out[oi] = o;
+  }
 }
 
 // causal prefill attention: grid (T, nq), 128 threads, dyn smem n floats
@@ -416,19 +528,27 @@ cudaError_t launch_qk_rope_append(const AttnArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+template <bool BF, int HD>
+cudaError_t launch_attn_step_t(const AttnArgs& a, cudaStream_t s) {
+  const size_t smem = (size_t)2 * a.chunk * HD * (BF ? 2 : 4);
+  static size_t configured = 0;
+  if (smem > 48 * 1024 && smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(attn_step_kernel<BF, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  CTTS_LK(launch_k(attn_step_kernel<BF, HD>, dim3(a.nsplit, a.nkv, a.batch), dim3(128), smem, s, a));
+  return cudaGetLastError();
+}
+
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t s) {
   const int G = a.nq / a.nkv;
-  if (G > kMaxG || a.hd % 8 != 0 || a.hd > kMaxHd || a.chunk != 128 || 128 % a.hd != 0)
+  if (G > kMaxG || a.nq % a.nkv != 0 || (a.hd != 64 && a.hd != 128) || a.chunk <= 0 || a.chunk > 128 ||
+      a.chunk % 16 != 0 || a.nsplit * a.chunk < a.cap || a.rows != a.batch || !a.cnt)
     return cudaErrorInvalidValue;
-  dim3 grid(a.nsplit, a.nkv, a.batch);
-  if (a.kv_bf16)
-    CTTS_LK(launch_k(attn_decode_kernel<true>, dim3(grid), dim3(128), 0, s, a));
-  else
-    CTTS_LK(launch_k(attn_decode_kernel<false>, dim3(grid), dim3(128), 0, s, a));
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  CTTS_LK(launch_k(attn_combine_kernel, dim3(a.batch, a.nq), dim3(a.hd), 0, s, a));
-  return cudaGetLastError();
+  if (a.kv_bf16) return a.hd == 64 ? launch_attn_step_t<true, 64>(a, s) : launch_attn_step_t<true, 128>(a, s);
+  return a.hd == 64 ? launch_attn_step_t<false, 64>(a, s) : launch_attn_step_t<false, 128>(a, s);
 }
 
 cudaError_t launch_attn_prefill(const AttnArgs& a, cudaStream_t s) {

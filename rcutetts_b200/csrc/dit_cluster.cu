@@ -93,8 +93,8 @@ constexpr int oDT = oCH + kU * kOwn;             // [32] delta-time embedding
 constexpr int oINB = oDT + kOwn;                 // [32] in_proj bias
 constexpr int oFN = oINB + kOwn;                 // [32] final norm
 constexpr int oOUTB = oFN + kOwn;                // [4] out_proj bias of my latent columns (+4 pad)
-constexpr int oIFQ = oOUTB + 8;                  // [16] RoPE frequencies of my dims
-constexpr int oTEMB = oIFQ + 16;                 // [steps][32] time embeddings
+constexpr int oRCS = oOUTB + 8;                  // [3 positions][cos 16, sin 16] RoPE of my dims
+constexpr int oTEMB = oRCS + 96;                 // [steps][32] time embeddings
 constexpr int oNRM = oTEMB + Sh::kMaxSteps * kOwn;  // [NL][2][32] norm1, norm2
 __host__ __device__ constexpr int oAD(int NL) { return oNRM + NL * 2 * kOwn; }  // [2][10][196] AdaLN, by layer parity
 __host__ __device__ constexpr int f32_floats(int NL) { return oAD(NL) + 2 * kU * kAdLd; }
@@ -367,7 +367,13 @@ __global__ void __launch_bounds__(128, 1)
     F[oFN + j] = a.fnorm[c * kOwn + j];
   }
   if (tid < 4) F[oOUTB + tid] = a.out_b ? a.out_b[4 * c + tid] : 0.0f;
-  if (tid < 16) F[oIFQ + tid] = a.inv_freq[16 * (c & 1) + tid];
+  if (tid < 48) {  // the three token positions' rotations, computed once
+    const int sp = tid / 16, j = tid % 16;
+    float sn, cs;
+    sincosf((float)sp * a.inv_freq[16 * (c & 1) + j], &sn, &cs);
+    F[oRCS + sp * 32 + j] = cs;
+    F[oRCS + sp * 32 + 16 + j] = sn;
+  }
   for (int i = tid; i < steps * kOwn; i += 128) F[oTEMB + i] = a.temb[(size_t)(i / kOwn) * kH + c * kOwn + i % kOwn];
   for (int i = tid; i < NL * 2 * kOwn; i += 128)
     F[oNRM + i] = a.norms[(size_t)(i / kOwn) * kH + c * kOwn + i % kOwn];
@@ -437,6 +443,13 @@ __global__ void __launch_bounds__(128, 1)
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t idesc = umma_idesc(G.N);
             const uint32_t abase = sb + ((g == 0 || g == 2) ? kXA : kACT);
+            // Both operands advance by constant descriptor steps (address >> 4
+            // in the low bits): the A operand's 32-column atoms are 2 KB apart
+            // in column order for every GEMM (one atom per 32-column slice,
+            // three per 96-column slice), so K step ks sits at atom ks / 2,
+            // +32 bytes for odd ks; a weight K block is G.N rows of 128 bytes.
+            uint64_t ad = desc_sw64(abase);
+            const uint64_t bstep = (uint64_t)(G.N * 8);
             for (int kb0 = 0; kb0 < G.nkb && ok; kb0 += G.kbps) {
               const int slot = (int)(it % kSlots);
               if (!wait_local(bar(bFULL + slot), (it / kSlots) & 1, abort)) {
@@ -446,19 +459,14 @@ __global__ void __launch_bounds__(128, 1)
               asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
               DTRACE(1, 8);
               const int n = min(G.kbps, G.nkb - kb0);
-              const uint32_t ws = sb + kRING + (uint32_t)slot * kSlotBytes;
+              uint64_t bd = umma_desc(sb + kRING + (uint32_t)slot * kSlotBytes);
               for (int q = 0; q < n; q++) {
-                const int kb = kb0 + q;
-#pragma unroll
-                for (int kk = 0; kk < 4; kk++) {
-                  const int ks = 4 * kb + kk;  // K step of 16
-                  // 16-column K step ks: its 32-column atom, +32 bytes for the odd half
-                  const uint32_t aoff = g == 3 ? (uint32_t)(ks / 6) * kActSlice + (uint32_t)((ks % 6) >> 1) * (kGrp * 512u)
-                                               : (uint32_t)(ks >> 1) * kSlice;
-                  const uint64_t ad = desc_sw64(abase + aoff + (uint32_t)(ks & 1) * 32u);
-                  umma_bf16(tmem, ad, umma_desc(ws + (uint32_t)(q * G.N * 128) + kk * 32), idesc,
-                            (kb | kk) ? 1u : 0u);
-                }
+                umma_bf16(tmem, ad, bd, idesc, (kb0 | q) ? 1u : 0u);
+                umma_bf16(tmem, ad + 2, bd + 2, idesc, 1u);
+                umma_bf16(tmem, ad + 128, bd + 4, idesc, 1u);
+                umma_bf16(tmem, ad + 130, bd + 6, idesc, 1u);
+                ad += 256;
+                bd += bstep;
               }
               umma_commit(&bars[bEMPTY + slot]);
               it++;
@@ -655,8 +663,7 @@ __global__ void __launch_bounds__(128, 1)
         }
 #pragma unroll
         for (int j = 0; j < 16; j++) {
-          float sn, cs;
-          sincosf((float)s * F[oIFQ + j], &sn, &cs);
+          const float cs = F[oRCS + s * 32 + j], sn = F[oRCS + s * 32 + 16 + j];
           float a1 = q[j], a2 = q[j + 16];
           q[j] = a1 * cs - a2 * sn;
           q[j + 16] = a1 * sn + a2 * cs;

@@ -84,6 +84,7 @@ struct AttnArgs {
   float* out = nullptr;   // [rows, nq*hd] attention output (fp32) ...
   uint16_t* out_b = nullptr;  // ... or bf16 when set
   float* part = nullptr;  // split partials [batch][nq][nsplit][hd+2]
+  int* cnt = nullptr;     // [batch][nkv] split tickets (zero at rest)
   int nsplit = 0, chunk = 0;
   int* err = nullptr;     // device error flag (capacity overflow)
 };

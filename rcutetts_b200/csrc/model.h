@@ -33,7 +33,8 @@ struct ctts_lm {
 // [batch][kv_head][capacity][head_dim] in the model weight dtype.
 struct ctts_kv {
   const ctts_lm* lm = nullptr;
-  int batch = 0, cap = 0, nsplit = 0, ws_rows = 0;
+  int batch = 0, cap = 0, nsplit = 0, chunk = 128, ws_rows = 0;
+  int* cnt = nullptr;  // decode-attention split tickets [batch][n_kv_heads]
   size_t layer_elems = 0;
   ctts::DevArena arena;
   void *k = nullptr, *v = nullptr;
