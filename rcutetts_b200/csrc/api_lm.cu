@@ -184,6 +184,7 @@ extern "C" int ctts_kv_alloc(const ctts_lm* lm, int batch, int capacity, ctts_kv
     return set_error(CTTS_ERR_NOMEM, "KV cache allocation failed");
   }
   if (lm->bf16) {
+    kv->ssp = kv->arena.alloc<float>((size_t)((H + 127) / 128) * rows);
     kv->xb = kv->arena.alloc<uint16_t>((size_t)rows * std::max(H, qd));
     kv->attb = kv->arena.alloc<uint16_t>((size_t)rows * qd);
     kv->actb = kv->arena.alloc<uint16_t>((size_t)rows * c.ffn);
@@ -193,7 +194,7 @@ extern "C" int ctts_kv_alloc(const ctts_lm* lm, int batch, int capacity, ctts_kv
       for (auto nk : {std::array<int, 2>{qkvw, H}, {H, qd}, {2 * c.ffn, H}, {H, c.ffn}})
         shapes.push_back({m, nk[0], nk[1]});
     int rc = tc_alloc(kv->arena, &kv->tc, shapes, kv->err);
-    if (rc != CTTS_OK || !kv->xb || !kv->attb || !kv->actb) {
+    if (rc != CTTS_OK || !kv->xb || !kv->attb || !kv->actb || !kv->ssp) {
       delete kv;
       return rc != CTTS_OK ? rc : set_error(CTTS_ERR_NOMEM, "KV workspace allocation failed");
     }
@@ -251,14 +252,29 @@ int lm_forward_rows(ctts_lm* lm, ctts_kv* kv, int rows, int prefill_b, int pos0,
   // bf16 weights with >= 16 rows: the tensor-core linears (tc_linear.cu);
   // otherwise the CUDA-core skinny linears (linear.cu).
   const bool tc = lm->bf16 && rows >= 16;
+  // Tensor-core path: each residual-writing GEMM (o-proj, down) also writes
+  // the next RMSNorm's operand bf16(h * gain) and per-tile row sums of
+  // squares; the consuming GEMM (QKV, gate/up) applies 1/rms to its
+  // accumulator rows, so only layer 0 needs a separate norm pass.
+  const int nt = (H + 127) / 128;
+  auto fold_in = [&](TcArgs& e) {
+    e.rs_ssp = kv->ssp; e.rs_ld = kv->ws_rows; e.rs_nt = nt; e.rs_k = (float)H; e.rs_eps = c.rms_eps;
+  };
+  auto fold_out = [&](TcArgs& e, const float* gain) {
+    e.yb2 = kv->xb; e.g2 = gain; e.ssp = kv->ssp; e.ssp_ld = kv->ws_rows;
+  };
   for (int l = 0; l < c.n_layers; l++) {
     const LMLayer& L = lm->layers[l];
     if (tc) {
-      PrepArgs pa;
-      pa.x = kv->h; pa.x_ld = H; pa.y = kv->xb; pa.y_ld = H; pa.M = rows; pa.K = H;
-      pa.norm_w = L.norm1; pa.eps = c.rms_eps;
-      CTTS_CK(launch_prep_bf16(pa, s)); nl++;
       TcArgs e; e.y = kv->qkv; e.y_ld = qkvw;
+      if (l == 0) {
+        PrepArgs pa;
+        pa.x = kv->h; pa.x_ld = H; pa.y = kv->xb; pa.y_ld = H; pa.M = rows; pa.K = H;
+        pa.norm_w = L.norm1; pa.eps = c.rms_eps;
+        CTTS_CK(launch_prep_bf16(pa, s)); nl++;
+      } else {
+        fold_in(e);
+      }
       int rc = tc_run(kv->tc, kv->xb, rows, H, L.wqkv, qkvw, e, s, &nl);
       if (rc) return rc;
     } else {
@@ -289,16 +305,15 @@ int lm_forward_rows(ctts_lm* lm, ctts_kv* kv, int rows, int prefill_b, int pos0,
 
     if (tc) {
       TcArgs e; e.y = kv->h; e.y_ld = H; e.res = kv->h;
+      fold_out(e, L.norm2);
       int rc = tc_run(kv->tc, kv->attb, rows, qd, L.wo, H, e, s, &nl);
       if (rc) return rc;
-      PrepArgs pa;
-      pa.x = kv->h; pa.x_ld = H; pa.y = kv->xb; pa.y_ld = H; pa.M = rows; pa.K = H;
-      pa.norm_w = L.norm2; pa.eps = c.rms_eps;
-      CTTS_CK(launch_prep_bf16(pa, s)); nl++;
       TcArgs g; g.act = 2; g.yb = kv->actb; g.y_ld = F;
+      fold_in(g);
       rc = tc_run(kv->tc, kv->xb, rows, H, L.wgu, 2 * F, g, s, &nl);
       if (rc) return rc;
       TcArgs d; d.y = kv->h; d.y_ld = H; d.res = kv->h;
+      if (l + 1 < c.n_layers) fold_out(d, lm->layers[l + 1].norm1);
       rc = tc_run(kv->tc, kv->actb, rows, F, L.wd, H, d, s, &nl);
       if (rc) return rc;
       continue;

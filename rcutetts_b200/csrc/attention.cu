@@ -382,6 +382,278 @@ __global__ void __launch_bounds__(128) attn_step_kernel(const AttnArgs a) {
   }
 }
 
+// Large-batch form of the same decode step: one CTA per (kv head,
+// utterance) walks the utterance's keys in 128-key stages through a
+// two-stage ring of bulk copies (the copy of stage s+2 is issued as soon as
+// stage s is consumed) with an online softmax, so there is no split merge
+// and the grid is one wave.  The new key/value row is kept in shared memory
+// and placed into its stage's tile once that stage's copy has landed.
+// grid (nkv, batch), 256 threads, dynamic smem 2 stages x (K, V) x 128 rows.
+template <bool BF, int HD>
+__global__ void __launch_bounds__(256) attn_loop_kernel(const AttnArgs a) {
+  constexpr int ES = BF ? 2 : 4;
+  constexpr int ROWB = HD * ES;
+  constexpr int NC = ROWB / 16;
+  constexpr int VPC = 16 / ES;
+  constexpr int PER = HD / 32;
+  constexpr int HP = HD / 2;
+  constexpr int C = 128;             // keys per stage
+  constexpr int NT = 256;
+  constexpr int PARTS = NT / HP;     // key partitions of the P.V pass
+  constexpr int NW = NT / 32;
+  extern __shared__ __align__(128) uint8_t kv_smem[];  // [2][K|V][C][ROWB]
+  __shared__ __align__(16) float qs[kMaxG][HD];
+  __shared__ float ps[kMaxG][C];
+  __shared__ float red[kMaxG][NW];
+  __shared__ float mrun[kMaxG], lrun[kMaxG], fac[kMaxG];
+  __shared__ __align__(16) uint8_t newrow[2][ROWB];  // new K, V row in the cache type
+  __shared__ __align__(16) float accs[PARTS][kMaxG][HD];
+  __shared__ __align__(8) uint64_t bars[2];
+
+  const int kh = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nq = a.nq, nkv = a.nkv, G = nq / nkv;
+  const int pos = a.pos[b];
+  const bool bad = pos < 0 || pos >= a.cap;
+  const int n = bad ? 0 : pos + 1;
+  const int nst = (n + C - 1) / C;
+  const size_t row0 = ((size_t)b * nkv + kh) * a.cap;
+  auto tile = [&](int buf, int kv) { return kv_smem + ((size_t)(buf * 2 + kv) * C) * ROWB; };
+  auto bar_a = [&](int i) { return static_cast<uint32_t>(__cvta_generic_to_shared(&bars[i])); };
+  // rows of stage st already in the cache (the new row at `pos` is not)
+  auto cached = [&](int st) { return max(0, min(st * C + C, pos) - st * C); };
+  auto issue = [&](int st) {  // thread 0
+    const int rows = cached(st);
+    if (rows <= 0) return;
+    const int buf = st & 1;
+    const uint32_t bytes = (uint32_t)rows * ROWB;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_a(buf)), "r"(2 * bytes)
+                 : "memory");
+#pragma unroll
+    for (int kv = 0; kv < 2; kv++) {
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(kv ? a.vcache : a.kcache) + (row0 + (size_t)st * C) * ROWB;
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       static_cast<uint32_t>(__cvta_generic_to_shared(tile(buf, kv)))),
+                   "l"(src), "r"(bytes), "r"(bar_a(buf))
+                   : "memory");
+    }
+  };
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_a(0)));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_a(1)));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid == 0 && !bad) {  // cached rows were written frames ago
+    issue(0);
+    if (nst > 1) issue(1);
+  }
+  grid_dep_enter();
+  if (bad && kh == 0 && tid == 0 && a.err) atomicExch(a.err, 1);
+
+  // ---- queries and the new key/value row: one warp per job
+  const int width = (nq + 2 * nkv) * HD;
+  const float* src_row = a.qkv + (size_t)b * width;
+  const int jobs = bad ? 0 : G + 2;
+  for (int job = warp; job < jobs; job += NW) {
+    const bool is_q = job < G, is_v = job == G + 1;
+    const int head = is_q ? kh * G + job : (is_v ? nq + nkv + kh : nq + kh);
+    const float* src = src_row + head * HD;
+    float v[PER];
+#pragma unroll
+    for (int j = 0; j < PER; j++) v[j] = src[lane + 32 * j];
+    if (!is_v) {
+      const float* gn = is_q ? a.qn : a.kn;
+      if (gn) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < PER; j++) ss = fmaf(v[j], v[j], ss);
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+#pragma unroll
+        for (int j = 0; j < PER; j++) v[j] = v[j] * inv * gn[lane + 32 * j];
+      }
+#pragma unroll
+      for (int j = 0; j < PER / 2; j++) {
+        const int i = lane + 32 * j;
+        float sn, cs;
+        sincosf((float)pos * a.inv_freq[i], &sn, &cs);
+        const float x1 = v[j], x2 = v[j + PER / 2];
+        v[j] = x1 * cs - x2 * sn;
+        v[j + PER / 2] = x1 * sn + x2 * cs;
+      }
+    }
+    if (is_q) {
+#pragma unroll
+      for (int j = 0; j < PER; j++) qs[job][lane + 32 * j] = v[j];
+    } else {
+      void* cache = is_v ? a.vcache : a.kcache;
+      uint8_t* nr = newrow[is_v ? 1 : 0];
+#pragma unroll
+      for (int j = 0; j < PER; j++) {
+        const int d = lane + 32 * j;
+        if constexpr (BF) {
+          const uint16_t hb = f2bf(v[j]);
+          reinterpret_cast<uint16_t*>(cache)[(row0 + pos) * HD + d] = hb;
+          reinterpret_cast<uint16_t*>(nr)[d] = hb;
+        } else {
+          reinterpret_cast<float*>(cache)[(row0 + pos) * HD + d] = v[j];
+          reinterpret_cast<float*>(nr)[d] = v[j];
+        }
+      }
+    }
+  }
+  if (tid < kMaxG) {
+    mrun[tid] = -INFINITY;
+    lrun[tid] = 0.0f;
+  }
+  __syncthreads();  // queries, the new row and the running statistics are set
+  const float scale = 1.0f / sqrtf((float)HD);
+  const int dp = tid % HP, pp = tid / HP;
+  float acc[kMaxG][2];
+#pragma unroll
+  for (int g = 0; g < kMaxG; g++) acc[g][0] = acc[g][1] = 0.0f;
+  bool ok = true;
+  for (int st = 0; st < nst; st++) {
+    const int buf = st & 1;
+    const int rows = min(C, n - st * C);
+    if (cached(st) > 0) {
+      bool done = false;
+      for (uint32_t it = 0; it < (1u << 24) && !done; ++it) {
+        uint32_t d;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(d)
+            : "r"(bar_a(buf)), "r"((uint32_t)((st >> 1) & 1))
+            : "memory");
+        done = d != 0;
+      }
+      if (!done) ok = false;
+    }
+    uint8_t* Ks = tile(buf, 0);
+    uint8_t* Vs = tile(buf, 1);
+    if (pos >= st * C && pos < st * C + C && tid < 2 * NC) {  // the new row into its stage
+      const int kv = tid / NC, cch = tid % NC;
+      reinterpret_cast<uint4*>((kv ? Vs : Ks) + (size_t)(pos - st * C) * ROWB)[cch] =
+          reinterpret_cast<const uint4*>(newrow[kv])[cch];
+    }
+    __syncthreads();
+    // scores: two threads per key, each half of the 16-byte chunks
+    const int key = tid >> 1, half = tid & 1;
+    float sc[kMaxG];
+#pragma unroll
+    for (int g = 0; g < kMaxG; g++) sc[g] = 0.0f;
+    if (key < rows) {
+      const uint8_t* krow = Ks + (size_t)key * ROWB;
+#pragma unroll
+      for (int cc = 0; cc < NC / 2; cc++) {
+        const int c = half * (NC / 2) + (cc + key) % (NC / 2);
+        const uint4 t = *reinterpret_cast<const uint4*>(krow + c * 16);
+        float kv[VPC];
+        if constexpr (BF) {
+          kv[0] = bf_lo(t.x); kv[1] = bf_hi(t.x); kv[2] = bf_lo(t.y); kv[3] = bf_hi(t.y);
+          kv[4] = bf_lo(t.z); kv[5] = bf_hi(t.z); kv[6] = bf_lo(t.w); kv[7] = bf_hi(t.w);
+        } else {
+          kv[0] = __uint_as_float(t.x); kv[1] = __uint_as_float(t.y);
+          kv[2] = __uint_as_float(t.z); kv[3] = __uint_as_float(t.w);
+        }
+#pragma unroll
+        for (int g = 0; g < kMaxG; g++) {
+          if (g >= G) break;
+          const float* q = qs[g] + c * VPC;
+#pragma unroll
+          for (int e = 0; e < VPC; e++) sc[g] = fmaf(q[e], kv[e], sc[g]);
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < kMaxG; g++) {
+      if (g >= G) break;
+      sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], 1);
+      sc[g] = key < rows ? sc[g] * scale : -INFINITY;
+      const float m = warp_max(sc[g]);
+      if (lane == 0) red[g][warp] = m;
+    }
+    __syncthreads();
+    if (tid < G) {
+      float m = red[tid][0];
+#pragma unroll
+      for (int w = 1; w < NW; w++) m = fmaxf(m, red[tid][w]);
+      const float mn = fmaxf(mrun[tid], m);
+      fac[tid] = expf(mrun[tid] - mn);  // 0 on the first stage
+      mrun[tid] = mn;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int g = 0; g < kMaxG; g++) {
+      if (g >= G) break;
+      const float p = key < rows ? expf(sc[g] - mrun[g]) : 0.0f;
+      if (half == 0) ps[g][key] = p;
+      const float l = warp_sum(half == 0 ? p : 0.0f);
+      if (lane == 0) red[g][warp] = l;
+    }
+    __syncthreads();
+    if (tid < G) {
+      float l = 0.0f;
+#pragma unroll
+      for (int w = 0; w < NW; w++) l += red[tid][w];
+      lrun[tid] = lrun[tid] * fac[tid] + l;
+    }
+    // P.V of this stage, rescaled running accumulators
+#pragma unroll
+    for (int g = 0; g < kMaxG; g++) {
+      if (g >= G) break;
+      acc[g][0] *= fac[g];
+      acc[g][1] *= fac[g];
+    }
+    for (int j = pp; j < rows; j += PARTS) {
+      float v0, v1;
+      if constexpr (BF) {
+        const uint32_t t = reinterpret_cast<const uint32_t*>(Vs + (size_t)j * ROWB)[dp];
+        v0 = bf_lo(t);
+        v1 = bf_hi(t);
+      } else {
+        const float2 t = reinterpret_cast<const float2*>(Vs + (size_t)j * ROWB)[dp];
+        v0 = t.x;
+        v1 = t.y;
+      }
+#pragma unroll
+      for (int g = 0; g < kMaxG; g++) {
+        if (g >= G) break;
+        const float p = ps[g][j];
+        acc[g][0] = fmaf(p, v0, acc[g][0]);
+        acc[g][1] = fmaf(p, v1, acc[g][1]);
+      }
+    }
+    __syncthreads();  // stage buffer and ps consumed
+    if (tid == 0 && st + 2 < nst) issue(st + 2);
+  }
+  if (!ok && a.err && tid == 0) atomicExch(a.err, 3);
+  if (bad) return;
+  // partitions summed in order
+#pragma unroll
+  for (int g = 0; g < kMaxG; g++) {
+    if (g >= G) break;
+    accs[pp][g][2 * dp] = acc[g][0];
+    accs[pp][g][2 * dp + 1] = acc[g][1];
+  }
+  __syncthreads();
+  for (int i = tid; i < G * HD; i += NT) {
+    const int g = i / HD, d = i % HD, h = kh * G + g;
+    float t = 0.0f;
+#pragma unroll
+    for (int q = 0; q < PARTS; q++) t += accs[q][g][d];
+    const float o = t / lrun[g];
+    const size_t oi = (size_t)b * nq * HD + (size_t)h * HD + d;
+    if (a.out_b)
+      a.out_b[oi] = f2bf(o);
+    else
+      a.out[oi] = o;
+  }
+}
+
 // causal prefill attention: grid (T, nq), 128 threads, dyn smem n floats
 template <bool BF>
 __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnArgs a) {
@@ -542,11 +814,31 @@ cudaError_t launch_attn_step_t(const AttnArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+template <bool BF, int HD>
+cudaError_t launch_attn_loop_t(const AttnArgs& a, cudaStream_t s) {
+  const size_t smem = (size_t)2 * 2 * 128 * HD * (BF ? 2 : 4);
+  static size_t configured = 0;
+  if (smem > 48 * 1024 && smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(attn_loop_kernel<BF, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  CTTS_LK(launch_k(attn_loop_kernel<BF, HD>, dim3(a.nkv, a.batch), dim3(256), smem, s, a));
+  return cudaGetLastError();
+}
+
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t s) {
   const int G = a.nq / a.nkv;
   if (G > kMaxG || a.nq % a.nkv != 0 || (a.hd != 64 && a.hd != 128) || a.chunk <= 0 || a.chunk > 128 ||
       a.chunk % 16 != 0 || a.nsplit * a.chunk < a.cap || a.rows != a.batch || !a.cnt)
     return cudaErrorInvalidValue;
+  // enough (utterance, kv head) pairs to fill the GPU: one CTA per pair
+  // walking all its keys; otherwise split the keys over CTAs
+  if (a.batch * a.nkv >= 128 && (a.kv_bf16 || a.hd == 64)) {
+    if (a.kv_bf16) return a.hd == 64 ? launch_attn_loop_t<true, 64>(a, s) : launch_attn_loop_t<true, 128>(a, s);
+    return a.hd == 64 ? launch_attn_loop_t<false, 64>(a, s) : launch_attn_loop_t<false, 128>(a, s);
+  }
   if (a.kv_bf16) return a.hd == 64 ? launch_attn_step_t<true, 64>(a, s) : launch_attn_step_t<true, 128>(a, s);
   return a.hd == 64 ? launch_attn_step_t<false, 64>(a, s) : launch_attn_step_t<false, 128>(a, s);
 }

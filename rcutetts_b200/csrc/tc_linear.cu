@@ -33,6 +33,27 @@ namespace ctts {
 
 namespace {
 
+// Optional phase timeline (build with -DCTTS_TC_TRACE): thread 0 of the
+// first CTA of the grid records (event, %globaltimer) pairs per launch.
+#ifdef CTTS_TC_TRACE
+__device__ long long g_tc_trace[4096];
+__device__ int g_tc_trace_n;
+CTTS_DEV void tc_trace(int ev) {
+  if (blockIdx.x != 0 || blockIdx.y != 0 || threadIdx.x != 0) return;
+  long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  const int n = g_tc_trace_n;
+  if (n < 2047) {
+    g_tc_trace[2 * n] = ev;
+    g_tc_trace[2 * n + 1] = t;
+    g_tc_trace_n = n + 1;
+  }
+}
+#define TC_TRACE(ev) tc_trace(ev)
+#else
+#define TC_TRACE(ev)
+#endif
+
 constexpr int kBK = 64;            // K elements per stage (128 bytes of bf16)
 constexpr int kTileN = 128;        // weight rows per CTA (MMA M)
 // Epilogue of four adjacent output columns of row m, y = res + coef * val
@@ -57,11 +78,36 @@ CTTS_DEV void epi_fetch(const TcArgs& a, int m, int col, int n, Epi4& e) {
     }
   }
 }
-CTTS_DEV void epi_store(const TcArgs& a, int m, int col, int n, const float* val, const Epi4& e) {
+// The next RMSNorm's gains for four output columns (zero where n < 4).
+CTTS_DEV float4 epi_gains(const TcArgs& a, int col, int n) {
+  if (!a.yb2) return make_float4(0.f, 0.f, 0.f, 0.f);
+  if (n == 4 && (reinterpret_cast<uintptr_t>(a.g2 + col) & 15) == 0) return *reinterpret_cast<const float4*>(a.g2 + col);
+  return make_float4(n > 0 ? a.g2[col] : 0.f, n > 1 ? a.g2[col + 1] : 0.f, n > 2 ? a.g2[col + 2] : 0.f,
+                     n > 3 ? a.g2[col + 3] : 0.f);
+}
+// 1/rms of activation row m from the folded-norm partial sums (1 without).
+CTTS_DEV float epi_rinv(const TcArgs& a, int m) {
+  if (!a.rs_ssp) return 1.0f;
+  float ss = 0.0f;
+  for (int t = 0; t < a.rs_nt; t++) ss += a.rs_ssp[(long)t * a.rs_ld + m];
+  return 1.0f / sqrtf(ss / a.rs_k + a.rs_eps);
+}
+CTTS_DEV void epi_store(const TcArgs& a, int m, int col, int n, const float* val, const Epi4& e, const float4& g,
+                        float* out) {
   const long yo = (long)m * a.y_ld + col;
-  float out[4];
 #pragma unroll
   for (int j = 0; j < 4; j++) out[j] = e.r[j] + (a.gate ? 1.0f + e.g[j] : a.scale) * val[j];
+  if (a.yb2) {  // the next RMSNorm's operand, gain applied, scale folded downstream
+    if (n == 4 && (yo % 4 == 0)) {
+      uint2 pk;
+      pk.x = (uint32_t)f2bf(out[0] * g.x) | ((uint32_t)f2bf(out[1] * g.y) << 16);
+      pk.y = (uint32_t)f2bf(out[2] * g.z) | ((uint32_t)f2bf(out[3] * g.w) << 16);
+      *reinterpret_cast<uint2*>(a.yb2 + yo) = pk;
+    } else {
+      const float gg[4] = {g.x, g.y, g.z, g.w};
+      for (int j = 0; j < n; j++) a.yb2[yo + j] = f2bf(out[j] * gg[j]);
+    }
+  }
   if (n == 4 && (yo % 4 == 0)) {
     if (a.yb) {
       uint2 pk;
@@ -85,6 +131,7 @@ __global__ void __launch_bounds__(128)
     tc_linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                      const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  TC_TRACE(0);
   // 1024-byte alignment for the swizzled tiles
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = a.stages;
@@ -126,6 +173,7 @@ __global__ void __launch_bounds__(128)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
+  TC_TRACE(1);
 
   // Weights do not depend on the previous kernel: their first stages are
   // fetched before waiting on it (programmatic dependent launch), the
@@ -140,6 +188,7 @@ __global__ void __launch_bounds__(128)
   }
   grid_dep_wait();
   grid_dep_launch();
+  TC_TRACE(2);
 
   bool ok = true;
   if (tid == 0) {  // ---- TMA producer
@@ -175,8 +224,42 @@ __global__ void __launch_bounds__(128)
   if (!ok) atomicExch(flag, 1);
   __syncwarp();
 
+  // ---- epilogue operands that do not depend on the accumulator (residual,
+  // AdaLN gate, next-norm gains, folded-norm row scale) of this thread's
+  // first round of output units, fetched while the MMAs run.  Output unit u
+  // of this CTA = row m_lo + u / groups, four columns at (u % groups) * 4.
+  const int mcount = min(a.MT, a.M - a.m0);
+  const int rows_per = (mcount + a.splitk - 1) / a.splitk;
+  const int m_lo = split * rows_per, m_hi = min(mcount, m_lo + rows_per);
+  const bool sw = a.act == 2;
+  const int groups = sw ? 16 : 32;
+  const int nunits = max(0, m_hi - m_lo) * groups;
+  constexpr int kU = 2;
+  auto unit_geom = [&](int u, int& em, int& ec, int& en) {
+    const int m = m_lo + u / groups, c = (u % groups) * 4;
+    em = a.m0 + m;
+    ec = sw ? tile * 64 + c : n0 + c;
+    en = u < nunits ? (sw ? 4 : max(0, min(4, a.N - (n0 + c)))) : 0;
+  };
+  Epi4 pre_ep[kU];
+  float pre_rinv[kU];
+  float4 pre_g[kU];
+#pragma unroll
+  for (int q = 0; q < kU; q++) {
+    int em, ec, en;
+    unit_geom(tid + q * 128, em, ec, en);
+    pre_rinv[q] = 1.0f;
+    pre_g[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (en > 0) {
+      epi_fetch(a, em, ec, en, pre_ep[q]);
+      pre_rinv[q] = epi_rinv(a, em);
+      pre_g[q] = epi_gains(a, ec, en);
+    }
+  }
+
   // ---- epilogue: every warp waits for the accumulator
   bool have = mbar_wait(done, 0);
+  TC_TRACE(3);
   if (!have) atomicExch(flag, 1);
   __syncthreads();
   const bool failed = *flag != 0;
@@ -184,7 +267,6 @@ __global__ void __launch_bounds__(128)
 
   const int r = warp * 32 + lane;  // TMEM lane = W row within the tile
   const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-  const int mcount = min(a.MT, a.M - a.m0);
   // ---- phase 1: accumulator -> this CTA's partial tile in shared memory
   // (the stage ring is free once every MMA has completed): part[m][128].
   float* part = reinterpret_cast<float*>(smem);
@@ -203,26 +285,22 @@ __global__ void __launch_bounds__(128)
           for (int j = 0; j < 16; j++) part[(c0 + 16 * q + j) * kTileN + r] = __uint_as_float(v[q][j]);
     }
   }
+  TC_TRACE(4);
   // every split of this tile (one cluster) has its partial in shared memory
   cluster_sync();
+  TC_TRACE(5);
 
   // ---- phase 2: CTA `split` reduces rows [m_lo, m_hi) of the tile over all
   // splits, in split order (deterministic), reading peers over DSMEM, and
   // runs the epilogue on float4 column groups.
-  bool any_failed = failed;
-  for (int s0 = 0; s0 < a.splitk; s0++)  // a failed peer leaves a garbage partial
-    any_failed |= ld_dsmem_u32(mapa_shared(smem_u32(flag), (uint32_t)s0)) != 0;
+  // a failed peer leaves a garbage partial: lane s reads split s's flag
+  const uint32_t peer_flag = lane < a.splitk ? ld_dsmem_u32(mapa_shared(smem_u32(flag), (uint32_t)lane)) : 0u;
+  const bool any_failed = failed || __any_sync(0xffffffffu, peer_flag != 0u);
   if (!any_failed) {
-    const int rows_per = (mcount + a.splitk - 1) / a.splitk;
-    const int m_lo = split * rows_per, m_hi = min(mcount, m_lo + rows_per);
-    const bool sw = a.act == 2;
-    const int groups = sw ? 16 : 32;
     const uint32_t my_base = smem_u32(part);
-    const int nunits = (m_hi - m_lo) * groups;
     // kU output units per thread per round: every DSMEM partial of the round
     // is requested before the first sum, and the epilogue's global loads of
-    // the round are issued before its stores.
-    constexpr int kU = 2;
+    // the round are issued before its stores (prefetched for round one).
     for (int u0 = tid; u0 < nunits; u0 += 128 * kU) {
       float acc[kU][4], accu[kU][4];
 #pragma unroll
@@ -251,41 +329,59 @@ __global__ void __launch_bounds__(128)
           }
         }
       }
-      // epilogue: fetch every unit's gate/residual, then compute and store
+      // epilogue: fetch every unit's gate/residual (prefetched in round
+      // one), then compute and store
       Epi4 ep[kU];
       int em[kU], ec[kU], en[kU];
+      float rinv[kU];
+      float4 gv[kU];
 #pragma unroll
       for (int q = 0; q < kU; q++) {
-        const int u = u0 + q * 128;
-        const int m = m_lo + u / groups, c = (u % groups) * 4;
-        em[q] = a.m0 + m;
-        ec[q] = sw ? tile * 64 + c : n0 + c;
-        en[q] = u < nunits ? (sw ? 4 : max(0, min(4, a.N - (n0 + c)))) : 0;
-        if (en[q] > 0) epi_fetch(a, em[q], ec[q], en[q], ep[q]);
+        unit_geom(u0 + q * 128, em[q], ec[q], en[q]);
+        if (u0 == tid) {
+          ep[q] = pre_ep[q];
+          rinv[q] = pre_rinv[q];
+          gv[q] = pre_g[q];
+        } else if (en[q] > 0) {
+          epi_fetch(a, em[q], ec[q], en[q], ep[q]);
+          rinv[q] = epi_rinv(a, em[q]);
+          gv[q] = epi_gains(a, ec[q], en[q]);
+        }
       }
 #pragma unroll
       for (int q = 0; q < kU; q++) {
-        if (en[q] <= 0) continue;
         const int u = u0 + q * 128;
         const int c = (u % groups) * 4;
-        float out[4];
+        float sq = 0.0f;
+        if (en[q] > 0) {  // rinv: folded RMSNorm of activation row em[q]
+          float val[4], out[4];
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-          if (sw) {
-            const float bg = a.bias ? a.bias[n0 + c + j] : 0.0f, bu = a.bias ? a.bias[n0 + 64 + c + j] : 0.0f;
-            out[j] = silu(acc[q][j] + bg) * (accu[q][j] + bu);
-          } else {
-            out[j] = acc[q][j] + ((a.bias && j < en[q]) ? a.bias[n0 + c + j] : 0.0f);
+          for (int j = 0; j < 4; j++) {
+            if (sw) {
+              const float bg = a.bias ? a.bias[n0 + c + j] : 0.0f, bu = a.bias ? a.bias[n0 + 64 + c + j] : 0.0f;
+              val[j] = silu(acc[q][j] * rinv[q] + bg) * (accu[q][j] * rinv[q] + bu);
+            } else {
+              val[j] = acc[q][j] * rinv[q] + ((a.bias && j < en[q]) ? a.bias[n0 + c + j] : 0.0f);
+            }
           }
+          epi_store(a, em[q], ec[q], en[q], val, ep[q], gv[q], out);
+          for (int j = 0; j < en[q]; j++) sq = fmaf(out[j], out[j], sq);
         }
-        epi_store(a, em[q], ec[q], en[q], out, ep[q]);
+        // one warp covers one output row of the tile (32 groups of 4
+        // columns): its sum of squares over the tile's columns
+        if (a.ssp) {
+          sq = warp_sum(sq);
+          if (lane == 0 && u < nunits) a.ssp[(long)tile * a.ssp_ld + em[q]] = sq;
+        }
       }
     }
   } else if (tid == 0 && a.err) {
     atomicExch(a.err, 2);
   }
+  TC_TRACE(6);
   // no CTA leaves while a peer may still read its shared memory
   cluster_sync();
+  TC_TRACE(7);
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -375,6 +471,9 @@ size_t tc_scratch_floats(const TcPlan& p) {
 
 cudaError_t launch_tc_linear(const TcCall& c, cudaStream_t s) {
   if (c.K % kBK != 0 || c.M <= 0 || c.N <= 0) return cudaErrorInvalidValue;
+  // row statistics need one warp per output row (no SwiGLU column pairing)
+  if ((c.epi.ssp || c.epi.yb2) && (c.epi.act == 2 || c.epi.yb || !c.epi.y)) return cudaErrorInvalidValue;
+  if (c.epi.yb2 && !c.epi.g2) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(c.w) & 15) || (reinterpret_cast<uintptr_t>(c.x) & 15))
     return cudaErrorInvalidValue;
   TcPlan p = tc_plan(c.M, c.N, c.K, tc_num_sms(), c.max_splitk);
@@ -427,3 +526,13 @@ cudaError_t launch_tc_linear(const TcCall& c, cudaStream_t s) {
 }
 
 }  // namespace ctts
+
+#ifdef CTTS_TC_TRACE
+// Copies the recorded timeline out and resets it.
+extern "C" __attribute__((visibility("default"))) int ctts_tc_trace(long long* out, int* n) {
+  cudaMemcpyFromSymbol(n, ctts::g_tc_trace_n, sizeof(int));
+  cudaMemcpyFromSymbol(out, ctts::g_tc_trace, sizeof(long long) * 4096);
+  int z = 0;
+  return cudaMemcpyToSymbol(ctts::g_tc_trace_n, &z, sizeof(int)) == cudaSuccess ? 0 : -2;
+}
+#endif

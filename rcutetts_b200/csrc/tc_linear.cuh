@@ -23,6 +23,20 @@ struct TcArgs {
   long gate_ld = 0;
   int gate_div = 1, gate_off = 0;
   float scale = 1.0f;           // coef when gate is null
+  // RMSNorm folded into the GEMM: the B operand holds bf16(x * gain) and the
+  // accumulator of row m is scaled by 1/sqrt(sum_t rs_ssp[t*rs_ld + m] / rs_k
+  // + rs_eps), the row's sum of squares given as rs_nt partials.
+  const float* rs_ssp = nullptr;
+  long rs_ld = 0;
+  int rs_nt = 0;
+  float rs_k = 1.0f, rs_eps = 0.0f;
+  // Producer side of that fold (fp32 output, no SwiGLU): also write
+  // yb2 = bf16(out * g2[col]) with leading dimension y_ld, and this tile's
+  // partial sum of squares of each output row to ssp[tile*ssp_ld + m].
+  uint16_t* yb2 = nullptr;
+  const float* g2 = nullptr;
+  float* ssp = nullptr;
+  long ssp_ld = 0;
   float* part = nullptr;        // split-K partial tiles
   int* counters = nullptr;      // per-tile tickets (zero at rest)
   int* err = nullptr;           // device error flag

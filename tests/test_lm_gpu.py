@@ -178,3 +178,32 @@ def test_tensor_core_decode_batch16():
         ref = run_oracle(cfg, wo, pre[b], dec[:, b, :], capacity=48)[3 + b:]
         for s in range(3):
             assert cosine(outs[s][b], ref[s]) >= 0.999, (b, s)
+
+
+@pytest.mark.parametrize("dtype,B", [("bf16", 40), ("f32", 32)])
+def test_large_batch_decode_stage_boundaries(dtype, B):
+    """Enough utterances that the decode attention runs one CTA per
+    (utterance, kv head) walking 128-key stages: ragged contexts that cross
+    stage boundaries, and steps whose new key opens a stage (position 128,
+    256), against the oracle."""
+    from rcutetts_b200.model import QwenCache, decode_step, prefill
+
+    cfg = LMConfig(n_layers=2)
+    m, w = lm_model(cfg, seed=12, dtype=dtype)
+    wo = bf16_weights(w) if dtype == "bf16" else w
+    special = [126, 255, 1, 127, 300, 128, 254]
+    lens = [special[b] if b < len(special) else 1 + (37 * b) % 290 for b in range(B)]
+    cap = 312
+    cache = QwenCache(m, batch=B, capacity=cap)
+    pre = [rnd(300 + b, (lens[b], cfg.hidden)) for b in range(B)]
+    for b in range(B):
+        prefill(m, pre[b], cache, b)
+    dec = rnd(400, (4, B, cfg.hidden))
+    outs = [decode_step(m, dec[s], cache) for s in range(4)]
+    for b in list(range(len(special))) + [B - 1]:
+        ref = run_oracle(cfg, wo, pre[b], dec[:, b, :], capacity=cap)[lens[b]:]
+        for s in range(4):
+            if dtype == "f32":
+                assert rel_err(outs[s][b], ref[s]) < 1e-4, (b, s)
+            else:
+                assert cosine(outs[s][b], ref[s]) >= 0.999, (b, s)
