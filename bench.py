@@ -283,13 +283,74 @@ def run_b1(args, dev):
     return out
 
 
+def dit_kernel_roofline(dit, dcfg, lcfg, dev, tc_probe=None):
+    """Roofline of the dominant kernel of the batched frame: the DiT head's
+    cluster-resident Euler loop (dit_cluster_kernel, about 60% of the frame
+    in the ncu launch list), run alone through ctts_dit_euler_sample_dev at
+    the benchmark's 64 utterances x 10 Euler steps, timed with CUDA events
+    on the launching stream.  The timed call also holds the once-per-frame
+    prologue (AdaLN, cond/mu projections, time embeddings: 6 small
+    launches).  Algorithmic flops = 2 x 192 token rows x the DiT layer
+    parameters x 10 steps + the prologue GEMMs; its weights are
+    L2-resident, so the bound is the tensor pipe (measured bf16 peak, burst)."""
+    import ctypes as C
+
+    import torch
+
+    from rcutetts_b200 import _lib
+
+    lib = _lib.load()
+    hbm, bf16_tf, kind = peaks()
+    B, steps = B_PER_GPU, 10
+    g = torch.Generator(device="cuda").manual_seed(7)
+    x0 = torch.randn((B, dcfg.latent), device="cuda", generator=g)
+    z = torch.randn((B, lcfg.hidden), device="cuda", generator=g)
+    cond = torch.randn((B, dcfg.latent), device="cuda", generator=g)
+    out = torch.empty((B, dcfg.latent), device="cuda")
+    # a stream of our own: a null stream handle would select the head's
+    # internal stream, which the events below would not see
+    st = torch.cuda.Stream()
+    torch.cuda.synchronize()
+
+    def call():
+        rc = lib.ctts_dit_euler_sample_dev(dit.h, B, x0.data_ptr(), z.data_ptr(), cond.data_ptr(), z.data_ptr(),
+                                           steps, C.c_float(0.0), out.data_ptr(), st.cuda_stream)
+        assert rc == 0, lib.ctts_last_error()
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    n = 20
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(n):
+        call()
+    e1.record(st)
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / n * 1e-3
+    Hd, Fd, L = dcfg.hidden, dcfg.ffn, dcfg.n_layers
+    layer_params = L * (4 * Hd * Hd + 3 * Hd * Fd)
+    flops = 2 * 3 * B * layer_params * steps + 2 * B * (L * 6 * Hd * dcfg.spk_dim + Hd * dcfg.cond_dim)
+    tf = flops / t / 1e12
+    res = {"bound": "tensor", "achieved": round(tf, 2), "peak": bf16_tf, "unit": "TFLOP/s",
+           "frac": round(tf / bf16_tf, 4), "traffic": 31.0e6, "of": kind,
+           "kernel": "dit_cluster_kernel (tcgen05, 16-CTA clusters) + DiT prologue via ctts_dit_euler_sample_dev, "
+                     "64 utterances x 10 Euler steps",
+           "flops_per_launch": flops, "us_per_launch": round(t * 1e6, 2),
+           "traffic_note": "ncu dram__bytes_read+write of one dit_cluster_kernel launch in the bench frame "
+                           "(weights L2-resident; 1.94 GB of L2->SMEM TMA traffic per launch)"}
+    if tc_probe is not None:
+        res["others"] = tc_probe
+    return res
+
+
 def dominant_kernel_roofline(lm, dit, lcfg, dcfg, dev):
-    """Average device time of the dominant kernel class (the tcgen05 bf16
-    linear, tc_linear_kernel), replayed alone through ctts_op_linear with CUDA
-    events on the launching stream: the LM down and gate/up shapes of the
-    batched step (M = 64 rows, bf16 weights streamed from HBM; L2 flushed
-    between launches).  Algorithmic bytes = weights + activation in +
-    output out."""
+    """Average device time of the LM's tensor-core linear (tc_linear_kernel,
+    the second kernel class of the batched frame), replayed alone through
+    ctts_op_linear with CUDA events on the launching stream: the LM down and
+    gate/up shapes of the batched step (M = 64 rows, bf16 weights streamed
+    from HBM; L2 flushed between launches).  Algorithmic bytes = weights +
+    activation in + output out."""
     import ctypes as C
 
     import torch
@@ -484,7 +545,8 @@ def main():
     if rank == 0 and world == 1:
         lm, dit, lcfg, dcfg, hw = keep
         try:
-            out["roofline"] = dominant_kernel_roofline(lm, dit, lcfg, dcfg, local)
+            tc = dominant_kernel_roofline(lm, dit, lcfg, dcfg, local)
+            out["roofline"] = dit_kernel_roofline(dit, dcfg, lcfg, local, tc_probe={"tc_linear": tc})
         except Exception as ex:  # report, do not hide
             out["roofline"] = {"error": repr(ex)}
         if not args.no_b1:

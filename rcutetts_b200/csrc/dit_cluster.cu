@@ -57,6 +57,7 @@ namespace {
 
 using Sh = DitClusterShape;
 constexpr int kC = Sh::kC, kH = Sh::kH, kF = Sh::kF, kHD = Sh::kHD, kL = Sh::kL, kU = Sh::kU;
+constexpr int kNT = 512;               // threads per CTA: 16 warps, compute warps 0, 4, 8, 12
 constexpr int kRows = 3 * kU;          // 30 token rows per cluster
 constexpr int kGrp = (kRows + 7) / 8;  // 4 groups of 8 rows (32 row slots)
 constexpr int kOwn = kH / kC;          // 32 hidden columns per CTA
@@ -97,7 +98,9 @@ constexpr int oRCS = oOUTB + 8;                  // [3 positions][cos 16, sin 16
 constexpr int oTEMB = oRCS + 96;                 // [steps][32] time embeddings
 constexpr int oNRM = oTEMB + Sh::kMaxSteps * kOwn;  // [NL][2][32] norm1, norm2
 __host__ __device__ constexpr int oAD(int NL) { return oNRM + NL * 2 * kOwn; }  // [2][10][196] AdaLN, by layer parity
-__host__ __device__ constexpr int f32_floats(int NL) { return oAD(NL) + 2 * kU * kAdLd; }
+__host__ __device__ constexpr int oPSC(int NL) { return oAD(NL) + 2 * kU * kAdLd; }  // [4][32][3] score partials
+__host__ __device__ constexpr int oPSS(int NL) { return oPSC(NL) + 4 * 32 * 3; }     // [4][32] row ss partials
+__host__ __device__ constexpr int f32_floats(int NL) { return oPSS(NL) + 4 * 32; }
 static_assert(oSSR >= 32 * kSeqLd && oSSR % 4 == 0 && oSCR % 4 == 0 && oVR % 4 == 0 && oXS % 4 == 0 &&
                   oXO % 4 == 0 && oVRO % 4 == 0 && oSSO % 4 == 0 && oSCO % 4 == 0 && oNRM % 4 == 0,
               "exchange buffers must be 16-byte aligned");
@@ -256,7 +259,7 @@ CTTS_DEV uint64_t desc_sw64(uint32_t saddr) {
 
 CTTS_DEV uint32_t pack_bf(float a, float b) { return (uint32_t)f2bf(a) | ((uint32_t)f2bf(b) << 16); }
 
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kNT, 1)
     dit_cluster_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmO,
                        const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmD,
                        const DitClusterArgs a) {
@@ -350,18 +353,18 @@ __global__ void __launch_bounds__(128, 1)
 
   // ---- per-CTA constants (every thread)
   const int adld = NL * 6 * kH;
-  for (int i = tid; i < kC * kU * 4; i += 128) {  // xs[q][u][i] = x[u][4q + i]
+  for (int i = tid; i < kC * kU * 4; i += kNT) {  // xs[q][u][i] = x[u][4q + i]
     const int q = i / (kU * 4), u = (i / 4) % kU, k = 4 * q + (i & 3);
     F[oXS + i] = (u < nvalid) ? a.x[(size_t)(U0 + u) * kL + k] : 0.0f;
   }
-  for (int i = tid; i < kU * kOwn; i += 128) {
+  for (int i = tid; i < kU * kOwn; i += kNT) {
     const int u = i / kOwn, j = i % kOwn;
     const bool ok = u < nvalid;
     F[oMU + i] = ok ? a.mu[(size_t)(U0 + u) * kH + c * kOwn + j] : 0.0f;
     F[oCH + i] = ok ? a.condh[(size_t)(U0 + u) * kH + c * kOwn + j] : 0.0f;
   }
-  for (int i = tid; i < 32 * kSeqLd; i += 128) F[oSEQ + i] = 0.0f;
-  for (int j = tid; j < kOwn; j += 128) {
+  for (int i = tid; i < 32 * kSeqLd; i += kNT) F[oSEQ + i] = 0.0f;
+  for (int j = tid; j < kOwn; j += kNT) {
     F[oDT + j] = a.dtemb[c * kOwn + j];
     F[oINB + j] = a.in_b ? a.in_b[c * kOwn + j] : 0.0f;
     F[oFN + j] = a.fnorm[c * kOwn + j];
@@ -374,18 +377,18 @@ __global__ void __launch_bounds__(128, 1)
     F[oRCS + sp * 32 + j] = cs;
     F[oRCS + sp * 32 + 16 + j] = sn;
   }
-  for (int i = tid; i < steps * kOwn; i += 128) F[oTEMB + i] = a.temb[(size_t)(i / kOwn) * kH + c * kOwn + i % kOwn];
-  for (int i = tid; i < NL * 2 * kOwn; i += 128)
+  for (int i = tid; i < steps * kOwn; i += kNT) F[oTEMB + i] = a.temb[(size_t)(i / kOwn) * kH + c * kOwn + i % kOwn];
+  for (int i = tid; i < NL * 2 * kOwn; i += kNT)
     F[oNRM + i] = a.norms[(size_t)(i / kOwn) * kH + c * kOwn + i % kOwn];
   // AdaLN slices of layer 0 in buffer 0; invalid utterances stay zero in both
-  for (int i = tid; i < 2 * kU * kAdLd; i += 128) {
+  for (int i = tid; i < 2 * kU * kAdLd; i += kNT) {
     const int buf = i / (kU * kAdLd), u = (i / kAdLd) % kU, e = i % kAdLd;
     float v = 0.0f;
     if (buf == 0 && a.adaln && u < nvalid && e < 6 * kOwn)
       v = a.ad[(size_t)(U0 + u) * adld + (size_t)(e / kOwn) * kH + c * kOwn + e % kOwn];
     F[oAD(NL) + i] = v;
   }
-  for (int i = tid; i < kOwn * kL; i += 128) {
+  for (int i = tid; i < kOwn * kL; i += kNT) {
     const int j = i / kL, o = i % kL;  // outw_t[j][o] = out_w[o][32c + j]
     outw_t[i] = a.out_w[(size_t)o * kH + c * kOwn + j];
     const int ii = i / kOwn, jj = i % kOwn;  // inw_t[i][j] = in_w[32c + j][i]
@@ -479,8 +482,15 @@ __global__ void __launch_bounds__(128, 1)
       umma_commit(&bars[bFIN]);
       wait_local(bar(bFIN), 0, abort);
     }
-  } else if (warp == 0) {
-    // ================= compute warp: lane = token row
+  } else if ((warp & 3) == 0) {
+    // ================= compute warps 0, 4, 8, 12 (cw = 0..3): lane = token
+    // row (TMEM lanes 0..31, which warps 0 mod 4 may read).  Every stage
+    // splits its columns over the four warps; warp 0 alone waits on the
+    // exchange/MMA barriers, combines the per-warp row partials in warp
+    // order (deterministic), pushes to the peers and runs the per-step
+    // tail.  All four warps pass the same named barriers in the same order,
+    // with `ok` made uniform at each of them.
+    const int cw = warp >> 2;
     const int r = lane, u = r / 3, s = r % 3;
     const bool rv = r < kRows;
     float* seq = F + oSEQ;
@@ -490,9 +500,21 @@ __global__ void __launch_bounds__(128, 1)
     float* xs = F + oXS;
     float* xn = F + oXN;
     float* nrm = F + oNRM;
-    uint32_t bph = 0, aph = 0, gph = 0;
-    // B stage: every lane's staging writes are visible to the bulk copies,
-    // lanes issue the pushes; then wait and re-arm for two stages later
+    float* psc = F + oPSC(NL);  // [4 warps][32 rows][3] score partials
+    float* pss = F + oPSS(NL);  // [4 warps][32 rows] sum-of-squares partials
+    volatile uint32_t* cok = reinterpret_cast<volatile uint32_t*>(smem + LY.bar + 136);
+    uint32_t bph = 0, aph = 0, gph = 0, nsync = 0;
+    auto cbar = [&]() { asm volatile("bar.sync 1, 128;" ::: "memory"); };
+    // warp 0's `ok` to all compute warps (two slots: a slow reader of one
+    // sync never sees the next sync's value)
+    auto sync_ok = [&]() {
+      if (cw == 0 && lane == 0) cok[nsync & 1] = ok ? 1u : 0u;
+      cbar();
+      ok = cok[nsync & 1] != 0u;
+      nsync++;
+    };
+    // B stage (warp 0): staging writes visible to the bulk copies, lanes
+    // issue the pushes; then wait and re-arm for two stages later
     auto pushB = [&](uint32_t src_off, uint32_t dst_off, uint32_t bytes, int ndst, bool pair) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
@@ -511,33 +533,40 @@ __global__ void __launch_bounds__(128, 1)
       __syncwarp();
       DTRACE(0, 3);
     };
-    // A stage: this CTA's slice (already written in place) to the 15 peers
+    // A stage (all compute warps): this CTA's slice, written in place by the
+    // four warps, to the 15 peers (warp 0 pushes)
     auto postA = [&](uint32_t slice_addr, uint32_t bytes) {
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      DTRACE(0, 7);
-      const uint32_t ab = bar(bA + (int)(aph & 1));
-      if (lane == 0) arrive_local(ab);
-      if (lane < kC && lane != c) push(slice_addr, slice_addr, bytes, ab, (uint32_t)lane);
+      cbar();
+      if (cw == 0) {
+        DTRACE(0, 7);
+        const uint32_t ab = bar(bA + (int)(aph & 1));
+        if (lane == 0) arrive_local(ab);
+        if (lane < kC && lane != c) push(slice_addr, slice_addr, bytes, ab, (uint32_t)lane);
+        __syncwarp();
+        DTRACE(0, 1);
+      }
       aph++;
-      __syncwarp();
-      DTRACE(0, 1);
     };
+    // accumulator complete (warp 0 waits, all warps then read TMEM)
     auto wait_mma = [&]() {
-      if (ok && !wait_local(bar(bMMA), gph & 1, abort)) ok = false;
+      if (cw == 0 && ok && !wait_local(bar(bMMA), gph & 1, abort)) ok = false;
       gph++;
+      sync_ok();
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      DTRACE(0, 4);
+      if (cw == 0) DTRACE(0, 4);
     };
-    // row sum of squares of the own columns -> every CTA's ssr[c]
-    auto ss_push = [&]() {
-      float p = 0.0f;
-#pragma unroll 8
-      for (int j = 0; j < kOwn; j++) p = fmaf(seq[r * kSeqLd + j], seq[r * kSeqLd + j], p);
-      F[oSSO + r] = p;
-      pushB(kF32 + oSSO * 4, kF32 + (oSSR + c * 32) * 4, 128, kC, false);
-      waitB();
+    // the per-warp row partials pss[cw][r] summed in warp order -> every
+    // CTA's ssr[c] (warp 0), then all warps see the 16 CTAs' sums
+    auto ss_combine_push = [&]() {
+      cbar();
+      if (cw == 0) {
+        F[oSSO + r] = ((pss[r] + pss[32 + r]) + pss[64 + r]) + pss[96 + r];
+        pushB(kF32 + oSSO * 4, kF32 + (oSSR + c * 32) * 4, 128, kC, false);
+        waitB();
+      }
+      sync_ok();
     };
     auto row_inv = [&]() {
       float ss = 0.0f;
@@ -545,45 +574,51 @@ __global__ void __launch_bounds__(128, 1)
       for (int q = 0; q < kC; q++) ss += ssr[q * 32 + r];
       return 1.0f / sqrtf(ss / (float)kH + eps);
     };
-    // RMSNorm (+ AdaLN modulate) of the own columns -> my slice of the K=512 operand
+    // RMSNorm (+ AdaLN modulate) of own columns [8cw, 8cw+8) -> chunk cw of
+    // my slice of the K=512 operand
     auto norm_slice = [&](const float* adb, int l, int which) {
       const float inv = row_inv();
       const float* nw = nrm + (l * 2 + which) * kOwn;
       const float* md = adb + min(u, kU - 1) * kAdLd + which * 3 * kOwn;  // shift, scale
-      uint32_t pk[16];
+      uint32_t pk[4];
 #pragma unroll
-      for (int j = 0; j < kOwn; j += 2) {
+      for (int e = 0; e < 8; e += 2) {
+        const int j = 8 * cw + e;
         float e0 = seq[r * kSeqLd + j] * inv * nw[j], e1 = seq[r * kSeqLd + j + 1] * inv * nw[j + 1];
         if (a.adaln) {
           e0 = e0 * (1.0f + md[kOwn + j]) + md[j];
           e1 = e1 * (1.0f + md[kOwn + j + 1]) + md[j + 1];
         }
-        pk[j >> 1] = pack_bf(e0, e1);
+        pk[e >> 1] = pack_bf(e0, e1);
       }
-      uint8_t* sl = smem + kXA + c * kSlice;
-#pragma unroll
-      for (int kc = 0; kc < 4; kc++)
-        st_u4(sl + slice_off(r, kc), pk[4 * kc], pk[4 * kc + 1], pk[4 * kc + 2], pk[4 * kc + 3]);
+      st_u4(smem + kXA + c * kSlice + slice_off(r, cw), pk[0], pk[1], pk[2], pk[3]);
       postA(sb + kXA + c * kSlice, kSlice);
     };
-    // gated residual update of the own columns from a 32-column accumulator
+    // gated residual update of own columns [8cw, 8cw+8) from the 32-column
+    // accumulator, and their sum of squares -> pss[cw]
     auto resid = [&](const float* adb, int gate_k) {
-      uint32_t v0[16], v1[16];
-      __syncwarp();
-      tmem_ld16_nowait(tmem, v0);
-      tmem_ld16_nowait(tmem + 16, v1);
+      uint32_t v[8];
+      tmem_ld8_nowait(tmem + 8 * cw, v);
       tmem_wait();
+      float p = 0.0f;
       if (rv) {
         const float* gt = adb + u * kAdLd + gate_k * kOwn;
 #pragma unroll
-        for (int j = 0; j < kOwn; j++) {
-          const float val = __uint_as_float(j < 16 ? v0[j] : v1[j - 16]);
+        for (int e = 0; e < 8; e++) {
+          const int j = 8 * cw + e;
           const float coef = a.adaln ? 1.0f + gt[j] : 1.0f;
-          seq[r * kSeqLd + j] = seq[r * kSeqLd + j] + coef * val;
+          const float nv = seq[r * kSeqLd + j] + coef * __uint_as_float(v[e]);
+          seq[r * kSeqLd + j] = nv;
+          p = fmaf(nv, nv, p);
         }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; e++) p = fmaf(seq[r * kSeqLd + 8 * cw + e], seq[r * kSeqLd + 8 * cw + e], p);
       }
+      pss[cw * 32 + r] = p;
     };
-    // seq rows of step stn: [mu + temb + dtemb; cond; in_proj(x)] (lane = column)
+    // seq rows of step stn: [mu + temb + dtemb; cond; in_proj(x)] (warp 0,
+    // lane = column), then the rows' sums of squares to every CTA
     auto fill = [&](int stn) {
       const int j = lane;
       float acc[kU];
@@ -611,21 +646,29 @@ __global__ void __launch_bounds__(128, 1)
         seq[(3 * uu + 2) * kSeqLd + j] = acc[uu] + F[oINB + j];
       }
       __syncwarp();
-      ss_push();
+      float p = 0.0f;
+#pragma unroll 8
+      for (int jj = 0; jj < kOwn; jj++) p = fmaf(seq[r * kSeqLd + jj], seq[r * kSeqLd + jj], p);
+      F[oSSO + r] = p;
+      pushB(kF32 + oSSO * 4, kF32 + (oSSR + c * 32) * 4, 128, kC, false);
+      waitB();
     };
 
-    fill(0);
+    if (cw == 0) fill(0);
+    sync_ok();
     for (int st = 0; st < steps && ok; st++) {
       for (int l = 0; l < NL && ok; l++) {
         const int LG = st * NL + l;  // layer count so far
         const float* adb = F + oAD(NL) + (LG & 1) * kU * kAdLd;
-        if (a.adaln) {
+        if (a.adaln && LG > 0) {
           // this layer's slices (prefetched one layer ago)
-          if (LG > 0 && ok && !wait_local(bar(bAD), (LG - 1) & 1, abort)) ok = false;
+          if (cw == 0 && ok && !wait_local(bar(bAD), (LG - 1) & 1, abort)) ok = false;
+          sync_ok();
+          if (!ok) break;
         }
         // S1: norm1 -> my operand slice -> peers
         norm_slice(adb, l, 0);
-        if (a.adaln) {
+        if (a.adaln && cw == 0) {
           // the next layer's AdaLN slices into the other buffer, one 128-byte
           // copy per (utterance, part)
           if (LG + 1 < steps * NL) {
@@ -644,46 +687,63 @@ __global__ void __launch_bounds__(128, 1)
                     : "memory");
           }
         }
-        // S2: QKV accumulator -> RoPE -> half-head score partials -> partner
+        // S2: QKV accumulator -> RoPE -> half-head score partials -> partner.
+        // Warp cw rotates dims {4cw..4cw+3} with their pairs {+16} and holds
+        // v dims [8cw, 8cw+8) for the P.V of S3.
         wait_mma();
         if (!ok) break;
-        float q[32], k[32], v[32];
+        float q[8], k[8], v[8];
         {
-          uint32_t t[6][16];
-          __syncwarp();
-#pragma unroll
-          for (int i = 0; i < 6; i++) tmem_ld16_nowait(tmem + 16 * i, t[i]);
+          uint32_t t0[4], t1[4], t2[4], t3[4], t4[8];
+          tmem_ld4_nowait(tmem + 4 * cw, t0);
+          tmem_ld4_nowait(tmem + 16 + 4 * cw, t1);
+          tmem_ld4_nowait(tmem + 32 + 4 * cw, t2);
+          tmem_ld4_nowait(tmem + 48 + 4 * cw, t3);
+          tmem_ld8_nowait(tmem + 64 + 8 * cw, t4);
           tmem_wait();
 #pragma unroll
-          for (int i = 0; i < 32; i++) {
-            q[i] = __uint_as_float(t[i >> 4][i & 15]);
-            k[i] = __uint_as_float(t[2 + (i >> 4)][i & 15]);
-            v[i] = __uint_as_float(t[4 + (i >> 4)][i & 15]);
+          for (int i = 0; i < 4; i++) {
+            q[i] = __uint_as_float(t0[i]);
+            q[i + 4] = __uint_as_float(t1[i]);
+            k[i] = __uint_as_float(t2[i]);
+            k[i + 4] = __uint_as_float(t3[i]);
           }
+#pragma unroll
+          for (int i = 0; i < 8; i++) v[i] = __uint_as_float(t4[i]);
         }
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
+        for (int i = 0; i < 4; i++) {
+          const int j = 4 * cw + i;
           const float cs = F[oRCS + s * 32 + j], sn = F[oRCS + s * 32 + 16 + j];
-          float a1 = q[j], a2 = q[j + 16];
-          q[j] = a1 * cs - a2 * sn;
-          q[j + 16] = a1 * sn + a2 * cs;
-          a1 = k[j];
-          a2 = k[j + 16];
-          k[j] = a1 * cs - a2 * sn;
-          k[j + 16] = a1 * sn + a2 * cs;
+          float a1 = q[i], a2 = q[i + 4];
+          q[i] = a1 * cs - a2 * sn;
+          q[i + 4] = a1 * sn + a2 * cs;
+          a1 = k[i];
+          a2 = k[i + 4];
+          k[i] = a1 * cs - a2 * sn;
+          k[i + 4] = a1 * sn + a2 * cs;
         }
 #pragma unroll
         for (int jt = 0; jt < 3; jt++) {
           const int src = min(3 * u + jt, 31);
           float d = 0.0f;
 #pragma unroll
-          for (int i = 0; i < 32; i++) d = fmaf(q[i], __shfl_sync(0xffffffffu, k[i], src), d);
-          F[oSCO + r * 3 + jt] = d;
+          for (int i = 0; i < 8; i++) d = fmaf(q[i], __shfl_sync(0xffffffffu, k[i], src), d);
+          psc[(cw * 32 + r) * 3 + jt] = d;
         }
-        pushB(kF32 + oSCO * 4, kF32 + (oSCR + (c & 1) * 96) * 4, 384, 2, true);
-        waitB();
+        cbar();
+        if (cw == 0) {
+#pragma unroll
+          for (int jt = 0; jt < 3; jt++)
+            F[oSCO + r * 3 + jt] = ((psc[r * 3 + jt] + psc[(32 + r) * 3 + jt]) + psc[(64 + r) * 3 + jt]) +
+                                   psc[(96 + r) * 3 + jt];
+          pushB(kF32 + oSCO * 4, kF32 + (oSCR + (c & 1) * 96) * 4, 384, 2, true);
+          waitB();
+        }
+        sync_ok();
         if (!ok) break;
-        // S3: softmax over the utterance's 3 tokens, P.V on the own dims -> my attention slice
+        // S3: softmax over the utterance's 3 tokens, P.V on dims [8cw, 8cw+8)
+        // -> chunk cw of my attention slice
         {
           float sc[3], m = -INFINITY;
           const float scale = 1.0f / sqrtf((float)kHD);
@@ -699,56 +759,49 @@ __global__ void __launch_bounds__(128, 1)
             lsum += sc[jt];
           }
           const float inv = 1.0f / lsum;
-          float o[32];
+          float o[8];
 #pragma unroll
-          for (int i = 0; i < 32; i++) o[i] = 0.0f;
+          for (int i = 0; i < 8; i++) o[i] = 0.0f;
 #pragma unroll
           for (int jt = 0; jt < 3; jt++) {
             const int src = min(3 * u + jt, 31);
             const float p = sc[jt] * inv;
 #pragma unroll
-            for (int i = 0; i < 32; i++) o[i] = fmaf(p, __shfl_sync(0xffffffffu, v[i], src), o[i]);
+            for (int i = 0; i < 8; i++) o[i] = fmaf(p, __shfl_sync(0xffffffffu, v[i], src), o[i]);
           }
           // o-proj weights are column-permuted so this slice is K columns [32c, 32c+32)
-          uint8_t* sl = smem + kACT + c * kSlice;
-#pragma unroll
-          for (int kc = 0; kc < 4; kc++)
-            st_u4(sl + slice_off(r, kc), pack_bf(o[8 * kc], o[8 * kc + 1]), pack_bf(o[8 * kc + 2], o[8 * kc + 3]),
-                  pack_bf(o[8 * kc + 4], o[8 * kc + 5]), pack_bf(o[8 * kc + 6], o[8 * kc + 7]));
+          st_u4(smem + kACT + c * kSlice + slice_off(r, cw), pack_bf(o[0], o[1]), pack_bf(o[2], o[3]),
+                pack_bf(o[4], o[5]), pack_bf(o[6], o[7]));
           postA(sb + kACT + c * kSlice, kSlice);
         }
         // S4: o-proj accumulator -> gated residual -> row statistics
         wait_mma();
         if (!ok) break;
         resid(adb, 2);
-        ss_push();
+        ss_combine_push();
         if (!ok) break;
         // S5: norm2 -> operand
         norm_slice(adb, l, 1);
-        // S6: gate/up accumulator -> SwiGLU -> my slice of the K=1536 operand
+        // S6: gate/up accumulator -> SwiGLU of columns [24cw, 24cw+24) ->
+        // chunks 3cw..3cw+2 of my slice of the K=1536 operand
         wait_mma();
         if (!ok) break;
         {
           uint8_t* sl = smem + kACT + c * kActSlice;
-#pragma unroll 1
-          for (int t3 = 0; t3 < kActOwn / 32; t3++) {
-            uint32_t gv[32], uv[32];
-            __syncwarp();
-            tmem_ld32_nowait(tmem + 32 * t3, gv);
-            tmem_ld32_nowait(tmem + kActOwn + 32 * t3, uv);
+#pragma unroll
+          for (int t = 0; t < 3; t++) {
+            uint32_t gv[8], uv[8];
+            tmem_ld8_nowait(tmem + 24 * cw + 8 * t, gv);
+            tmem_ld8_nowait(tmem + kActOwn + 24 * cw + 8 * t, uv);
             tmem_wait();
+            uint32_t pk[4];
 #pragma unroll
-            for (int h4 = 0; h4 < 4; h4++) {
-              uint32_t pk[4];
-#pragma unroll
-              for (int e = 0; e < 8; e += 2) {
-                const int i0 = 8 * h4 + e;
-                const float g0 = __uint_as_float(gv[i0]), g1 = __uint_as_float(gv[i0 + 1]);
-                pk[e >> 1] = pack_bf(__fdividef(g0, 1.0f + __expf(-g0)) * __uint_as_float(uv[i0]),
-                                     __fdividef(g1, 1.0f + __expf(-g1)) * __uint_as_float(uv[i0 + 1]));
-              }
-              st_u4(sl + slice_off(r, 4 * t3 + h4), pk[0], pk[1], pk[2], pk[3]);
+            for (int e = 0; e < 8; e += 2) {
+              const float g0 = __uint_as_float(gv[e]), g1 = __uint_as_float(gv[e + 1]);
+              pk[e >> 1] = pack_bf(__fdividef(g0, 1.0f + __expf(-g0)) * __uint_as_float(uv[e]),
+                                   __fdividef(g1, 1.0f + __expf(-g1)) * __uint_as_float(uv[e + 1]));
             }
+            st_u4(sl + slice_off(r, 3 * cw + t), pk[0], pk[1], pk[2], pk[3]);
           }
           postA(sb + kACT + c * kActSlice, kActSlice);
         }
@@ -756,69 +809,73 @@ __global__ void __launch_bounds__(128, 1)
         wait_mma();
         if (!ok) break;
         resid(adb, 5);
-        ss_push();
+        ss_combine_push();
       }
       if (!ok) break;
-      // T1: final norm of the x rows, out_proj partial over the own columns,
-      // 4 latent columns to each owner CTA
-      if (rv && s == 2) {
-        const float inv = row_inv();
+      if (cw == 0) {
+        // T1: final norm of the x rows, out_proj partial over the own columns,
+        // 4 latent columns to each owner CTA
+        if (rv && s == 2) {
+          const float inv = row_inv();
 #pragma unroll 8
-        for (int j = 0; j < kOwn; j++) xn[u * kOwn + j] = seq[r * kSeqLd + j] * inv * F[oFN + j];
-      }
-      __syncwarp();
-      {
-        float a0[kU], a1[kU];
+          for (int j = 0; j < kOwn; j++) xn[u * kOwn + j] = seq[r * kSeqLd + j] * inv * F[oFN + j];
+        }
+        __syncwarp();
+        {
+          float a0[kU], a1[kU];
 #pragma unroll
-        for (int uu = 0; uu < kU; uu++) a0[uu] = a1[uu] = 0.0f;
+          for (int uu = 0; uu < kU; uu++) a0[uu] = a1[uu] = 0.0f;
 #pragma unroll 4
-        for (int j = 0; j < kOwn; j++) {
-          const float w0 = bf2f(outw_t[j * kL + lane]), w1 = bf2f(outw_t[j * kL + lane + 32]);
+          for (int j = 0; j < kOwn; j++) {
+            const float w0 = bf2f(outw_t[j * kL + lane]), w1 = bf2f(outw_t[j * kL + lane + 32]);
+#pragma unroll
+            for (int uu = 0; uu < kU; uu++) {
+              const float xv = xn[uu * kOwn + j];
+              a0[uu] = fmaf(w0, xv, a0[uu]);
+              a1[uu] = fmaf(w1, xv, a1[uu]);
+            }
+          }
+          // owner of latent column o is CTA o/4; vro[owner][uu][o%4]
 #pragma unroll
           for (int uu = 0; uu < kU; uu++) {
-            const float xv = xn[uu * kOwn + j];
-            a0[uu] = fmaf(w0, xv, a0[uu]);
-            a1[uu] = fmaf(w1, xv, a1[uu]);
+            F[oVRO + ((lane >> 2) * kU + uu) * 4 + (lane & 3)] = a0[uu];
+            F[oVRO + (((lane + 32) >> 2) * kU + uu) * 4 + (lane & 3)] = a1[uu];
           }
         }
-        // owner of latent column o is CTA o/4; vro[owner][uu][o%4]
+        {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          const uint32_t bb = bar(bB + (int)(bph & 1));
+          if (lane < kC)
+            push(sb + kF32 + (oVR + c * kU * 4) * 4, sb + kF32 + (oVRO + lane * kU * 4) * 4, kU * 16, bb,
+                 (uint32_t)lane);
+        }
+        waitB();
+        if (ok) {
+          // T2: my 4 latent columns: reduce the 16 partials in order, Euler update
+          for (int e = lane; e < kU * 4; e += 32) {
+            const int uu = e >> 2, i = e & 3;
+            float acc = 0.0f;
 #pragma unroll
-        for (int uu = 0; uu < kU; uu++) {
-          F[oVRO + ((lane >> 2) * kU + uu) * 4 + (lane & 3)] = a0[uu];
-          F[oVRO + (((lane + 32) >> 2) * kU + uu) * 4 + (lane & 3)] = a1[uu];
+            for (int q2 = 0; q2 < kC; q2++) acc += vr[(q2 * kU + uu) * 4 + i];
+            const float xnew = xs[(c * kU + uu) * 4 + i] + a.dts[st] * (acc + F[oOUTB + i]);
+            if (st + 1 == steps) {
+              if (uu < nvalid) a.x[(size_t)(U0 + uu) * kL + 4 * c + i] = xnew;
+            } else {
+              F[oXO + e] = xnew;
+            }
+          }
+          if (st + 1 < steps) {
+            pushB(kF32 + oXO * 4, kF32 + (oXS + c * kU * 4) * 4, kU * 16, kC, false);
+            waitB();
+            // T3: the next step's sequence
+            if (ok) fill(st + 1);
+          }
         }
       }
-      {
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        const uint32_t bb = bar(bB + (int)(bph & 1));
-        if (lane < kC)
-          push(sb + kF32 + (oVR + c * kU * 4) * 4, sb + kF32 + (oVRO + lane * kU * 4) * 4, kU * 16, bb,
-               (uint32_t)lane);
-      }
-      waitB();
-      if (!ok) break;
-      // T2: my 4 latent columns: reduce the 16 partials in order, Euler update
-      for (int e = lane; e < kU * 4; e += 32) {
-        const int uu = e >> 2, i = e & 3;
-        float acc = 0.0f;
-#pragma unroll
-        for (int q2 = 0; q2 < kC; q2++) acc += vr[(q2 * kU + uu) * 4 + i];
-        const float xnew = xs[(c * kU + uu) * 4 + i] + a.dts[st] * (acc + F[oOUTB + i]);
-        if (st + 1 == steps) {
-          if (uu < nvalid) a.x[(size_t)(U0 + uu) * kL + 4 * c + i] = xnew;
-        } else {
-          F[oXO + e] = xnew;
-        }
-      }
-      if (st + 1 == steps) break;
-      pushB(kF32 + oXO * 4, kF32 + (oXS + c * kU * 4) * 4, kU * 16, kC, false);
-      waitB();
-      if (!ok) break;
-      // T3: the next step's sequence
-      fill(st + 1);
+      sync_ok();
     }
-    if (!ok) fail(3);
+    if (cw == 0 && !ok) fail(3);
   }
 
   __syncwarp();
@@ -884,7 +941,7 @@ cudaError_t set_attrs(size_t smem) {
 cudaLaunchConfig_t make_cfg(int nclusters, size_t smem, cudaStream_t s, cudaLaunchAttribute* attr, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kC * nclusters, 1, 1);
-  cfg.blockDim = dim3(128);
+  cfg.blockDim = dim3(kNT);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   attr[0].id = cudaLaunchAttributeClusterDimension;

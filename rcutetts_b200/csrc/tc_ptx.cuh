@@ -89,6 +89,17 @@ CTTS_DEV void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
+// 4 / 8 consecutive TMEM columns of this thread's lane; no wait.
+CTTS_DEV void tmem_ld4_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+CTTS_DEV void tmem_ld8_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
 // 16 consecutive TMEM columns of this thread's lane; no wait (see tmem_wait).
 CTTS_DEV void tmem_ld16_nowait(uint32_t taddr, uint32_t* r) {
   asm volatile(
