@@ -41,7 +41,8 @@ int dit_ws_ensure(ctts_dit* d, DitWs& w, int rows, int steps) {
   w.spk = w.arena.alloc<float>((size_t)rows * std::max(c.spk_dim, 1));
   w.hbuf = w.arena.alloc<float>((size_t)2 * H);
   w.err = w.arena.alloc<int>(1);
-  if (!w.seq || !w.qkv || !w.att || !w.act || !w.ad || !w.x || !w.spk || !w.hbuf || !w.err)
+  w.gbar = w.arena.alloc<unsigned>((size_t)dit_grid_counters(c.n_layers, steps));
+  if (!w.seq || !w.qkv || !w.att || !w.act || !w.ad || !w.x || !w.spk || !w.hbuf || !w.err || !w.gbar)
     return set_error(CTTS_ERR_NOMEM, "DiT workspace allocation failed");
   if (d->bf16) {
     const int SR = rows * S;
@@ -208,6 +209,32 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
   }
 
   // ---- Euler steps (predict_cached, dit.rs:775-814)
+  // small batches with fp32 weights: the whole loop as one grid-persistent
+  // launch (dit_grid.cu) unless CTTS_DIT_GRID=0
+  const char* grid_e = getenv("CTTS_DIT_GRID");
+  const int grid_env = grid_e ? atoi(grid_e) : 1;
+  if (r.mode == 0 && r.x_rows == R && !bf && P == 1 && grid_env != 0 &&
+      ctts::dit_grid_supported(R, NL, r.steps, H, c.n_heads, c.n_kv_heads, c.head_dim, F, L)) {
+    ctts::DitGridArgs ga;
+    ga.R = R; ga.NL = NL; ga.steps = r.steps; ga.H = H; ga.nq = c.n_heads; ga.nkv = c.n_kv_heads;
+    ga.hd = c.head_dim; ga.F = F; ga.L = L; ga.eps = c.rms_eps;
+    for (int i = 0; i < r.steps; i++) ga.dts[i] = r.dts[i];
+    ga.seq = w.seq; ga.qkv = w.qkv; ga.act = w.act; ga.x = r.x;
+    ga.mu = w.mu; ga.temb = w.temb; ga.dtemb = w.dtemb; ga.condh = w.condh; ga.ad = use_ad ? w.ad : nullptr;
+    ga.inv_freq = d->inv_freq; ga.final_norm = d->final_norm;
+    ga.in_w = static_cast<const float*>(d->in_w); ga.in_b = d->in_b;
+    ga.out_w = static_cast<const float*>(d->out_w); ga.out_b = d->out_b;
+    for (int l = 0; l < NL; l++) {
+      const DitLayer& Ly = d->layers[l];
+      ga.wqkv[l] = static_cast<const float*>(Ly.wqkv); ga.wo[l] = static_cast<const float*>(Ly.wo);
+      ga.wgu[l] = static_cast<const float*>(Ly.wgu); ga.wd[l] = static_cast<const float*>(Ly.wd);
+      ga.norm1[l] = Ly.norm1; ga.norm2[l] = Ly.norm2;
+    }
+    ga.bar = w.gbar; ga.err = w.err;
+    CTTS_CK(ctts::launch_dit_grid(ga, s)); nl++;
+    if (launches) *launches += nl;
+    return CTTS_OK;
+  }
   if (r.mode == 0 && r.x_rows == R && dit_cluster_ready(d, r.steps)) {
     ctts::DitClusterArgs ca;
     ca.R = R; ca.NL = NL; ca.steps = r.steps; ca.adaln = use_ad ? 1 : 0; ca.eps = c.rms_eps;
@@ -323,7 +350,7 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
 int dit_read_err(const DitWs& w) {
   int err = 0;
   CTTS_CK(cudaMemcpy(&err, w.err, sizeof(int), cudaMemcpyDeviceToHost));
-  CTTS_REQ(err == 0, CTTS_ERR_TIMEOUT, "a tensor-core linear gave up waiting on its pipeline");
+  CTTS_REQ(err == 0, CTTS_ERR_TIMEOUT, "a DiT kernel gave up waiting on its pipeline or grid barrier");
   return CTTS_OK;
 }
 
@@ -882,7 +909,7 @@ extern "C" int ctts_engine_step(ctts_engine* e, const float* noise, float* laten
     CTTS_CK(cudaMemcpy(&err, g.kv->err, sizeof(int), cudaMemcpyDeviceToHost));
     CTTS_CK(cudaMemcpy(&derr, g.ws->err, sizeof(int), cudaMemcpyDeviceToHost));
     CTTS_REQ(err != 1, CTTS_ERR_RANGE, "device reported a KV position outside capacity");
-    CTTS_REQ(err == 0 && derr == 0, CTTS_ERR_TIMEOUT, "a tensor-core linear gave up waiting on its pipeline");
+    CTTS_REQ(err == 0 && derr == 0, CTTS_ERR_TIMEOUT, "a DiT kernel gave up waiting on its pipeline or grid barrier");
   }
   memcpy(latents_out, e->h_lat, sizeof(float) * B * PL);
   if (stop_out) memcpy(stop_out, e->h_stop, sizeof(float) * B * 2);

@@ -1,0 +1,585 @@
+// dit_grid.cu -- the DiT Euler loop of one frame (every step, every layer,
+// the output/feedback tail) as ONE grid-persistent launch for small batches
+// with fp32 weights (the batch-1 fp32 decode of config[2]).
+//
+// Replaces the per-step launch chain of dit.rs:775-814 predict_cached /
+// euler_sample (dit.rs:819-842) at batch 1..4, where ~200 dependent
+// launches of a few microseconds each dominate the frame.  One CTA per SM
+// (cooperative launch, so every CTA is resident); phases are separated by
+// grid barriers (a global counter per barrier, zeroed again by the last
+// CTA to leave).  Each phase splits its output columns over all CTAs and
+// streams each column's weight row once per step (fp32, 16-byte loads; the
+// weights stay L2-resident across the ten steps), so the work per phase is
+// a few microseconds of L2 bandwidth spread over the whole GPU:
+//   P1  RMSNorm1 + AdaLN modulate (every CTA, all rows, redundant) -> QKV
+//   P2  3-token RoPE attention (every CTA, redundant) -> o-proj -> gated
+//       residual into the CTA's columns of the residual stream
+//   P3  RMSNorm2 + modulate -> gate/up -> SwiGLU
+//   P4  down -> gated residual
+//   T1  final norm -> out_proj -> x += dt * v
+//   T2  in_proj(x) and the next step's sequence rows
+// Intra-kernel data (residual, qkv, SwiGLU output, x) is read with
+// L2-coherent loads (ld.global.cg): L1 is not coherent across SMs.
+#include <cstdio>
+
+#include "common.cuh"
+#include "dit_grid.cuh"
+
+namespace ctts {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr uint32_t kSpinLimit = 1u << 24;
+constexpr int kMaxH4 = 8;  // hidden <= 1024: 16-byte groups per lane of a row
+
+CTTS_DEV float ldcg(const float* p) { return __ldcg(p); }
+CTTS_DEV float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+CTTS_DEV uint32_t ld_acquire(const unsigned* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Optional barrier timeline (build with -DCTTS_GRID_TRACE): thread 0 of
+// CTA 0 records %globaltimer at each barrier's arrival and release.
+#ifdef CTTS_GRID_TRACE
+__device__ long long g_grid_trace[2048];
+CTTS_DEV void grid_trace(int i) {
+  if (blockIdx.x != 0 || i >= 2048) return;
+  long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  g_grid_trace[i] = t;
+}
+#define GRID_TRACE(i) grid_trace(i)
+#else
+#define GRID_TRACE(i)
+#endif
+
+// Grid barrier k: every CTA's writes before it are visible to every CTA
+// after it.  Bounded: a CTA that waits too long records an error and goes on.
+CTTS_DEV void grid_sync(const DitGridArgs& a, int k) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    GRID_TRACE(2 * k);
+    __threadfence();
+    atomicAdd(a.bar + k, 1u);
+    const unsigned n = gridDim.x;
+    uint32_t it = 0;
+    while (ld_acquire(a.bar + k) < n) {
+      if (++it == kSpinLimit) {
+        if (a.err) atomicExch(a.err, 4);
+        break;
+      }
+    }
+    __threadfence();
+    GRID_TRACE(2 * k + 1);
+  }
+  __syncthreads();
+}
+
+// Rows of the residual stream -> RMSNorm (+ AdaLN modulate) into shared
+// memory xs[rows][H]: one warp per row, every load of the row issued before
+// its use (prep/linear_rows semantics: x * inv * gain, then
+// * (1 + scale) + shift).
+CTTS_DEV void norm_rows(const DitGridArgs& a, const float* gain, int l, int shift_k, int scale_k, float* xs) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows = 3 * a.R, H = a.H, nv = H >> 7;
+  const long adld = (long)a.NL * 6 * H;
+  for (int r = warp; r < rows; r += kWarps) {
+    const float* src = a.seq + (size_t)r * H;
+    float* dst = xs + (size_t)r * H;
+    float4 v[kMaxH4];
+#pragma unroll
+    for (int i = 0; i < kMaxH4; i++)
+      if (i < nv) v[i] = ldcg4(src + lane * 4 + 128 * i);
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kMaxH4; i++)
+      if (i < nv) ss = fmaf(v[i].x, v[i].x, fmaf(v[i].y, v[i].y, fmaf(v[i].z, v[i].z, fmaf(v[i].w, v[i].w, ss))));
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)H + a.eps);
+    const float* md = a.ad ? a.ad + (size_t)(r / 3) * adld + (size_t)l * 6 * H : nullptr;
+#pragma unroll
+    for (int i = 0; i < kMaxH4; i++) {
+      if (i >= nv) break;
+      const int k = lane * 4 + 128 * i;
+      float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        e[j] = e[j] * inv * gain[k + j];
+        if (md) e[j] = e[j] * (1.0f + md[scale_k * H + k + j]) + md[shift_k * H + k + j];
+      }
+      *reinterpret_cast<float4*>(dst + k) = make_float4(e[0], e[1], e[2], e[3]);
+    }
+  }
+}
+
+// rows x K floats of global memory -> shared memory (L2-coherent loads,
+// four 16-byte loads in flight per thread)
+CTTS_DEV void load_rows(float* dst, const float* src, int n) {
+  for (int i0 = threadIdx.x * 4; i0 < n; i0 += kThreads * 16) {
+    float4 v[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int i = i0 + q * kThreads * 4;
+      if (i < n) v[q] = ldcg4(src + i);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int i = i0 + q * kThreads * 4;
+      if (i < n) *reinterpret_cast<float4*>(dst + i) = v[q];
+    }
+  }
+}
+
+// One output column for every row: acc[r] = w[:] . xs[r, :] with the weight
+// row already staged in shared memory (warp, lanes over 4-element groups).
+template <int MAXR>
+CTTS_DEV void row_dots(const float* w, int K, const float* xs, int rows, float* acc) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int r = 0; r < MAXR; r++) acc[r] = 0.0f;
+  for (int k = lane * 4; k < K; k += 128) {
+    const float4 wv = *reinterpret_cast<const float4*>(w + k);
+#pragma unroll
+    for (int r = 0; r < MAXR; r++) {
+      if (r >= rows) break;
+      const float4 xv = *reinterpret_cast<const float4*>(xs + (size_t)r * K + k);
+      acc[r] = fmaf(wv.x, xv.x, fmaf(wv.y, xv.y, fmaf(wv.z, xv.z, fmaf(wv.w, xv.w, acc[r]))));
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < MAXR; r++) {
+    if (r >= rows) break;
+    acc[r] = warp_sum(acc[r]);
+  }
+}
+
+// This CTA's share [n0, n1) of N output columns.
+CTTS_DEV void my_cols(int N, int& n0, int& n1) {
+  n0 = (int)(((long)N * blockIdx.x) / gridDim.x);
+  n1 = (int)(((long)N * (blockIdx.x + 1)) / gridDim.x);
+}
+
+// ---- weight staging: before the barrier that opens a phase, thread 0
+// copies the weight rows of this CTA's output columns of that phase into
+// the staging buffer with bulk copies (the weights do not depend on the
+// barrier), completing on one mbarrier; the phase waits on it.
+enum Kind { kQKV, kO, kGU, kD, kOut, kFill };
+
+struct Stage {
+  float* wbuf;
+  uint32_t bar;  // shared address of the mbarrier
+  uint32_t ph;   // uses so far (parity of the next wait)
+};
+
+struct KindGeom {
+  const float* base;
+  int N, K, rows_per;  // output columns, row length, weight rows per column
+};
+CTTS_DEV KindGeom geom(const DitGridArgs& a, int kind, int l) {
+  const int qkvw = (a.nq + 2 * a.nkv) * a.hd, qd = a.nq * a.hd;
+  switch (kind) {
+    case kQKV: return {a.wqkv[l], qkvw, a.H, 1};
+    case kO: return {a.wo[l], a.H, qd, 1};
+    case kGU: return {a.wgu[l], a.F, a.H, 2};
+    case kD: return {a.wd[l], a.H, a.F, 1};
+    case kOut: return {a.out_w, a.R * a.L, a.H, 1};
+    default: return {a.in_w, a.H, a.L, 1};
+  }
+}
+// weight row of output column n (and row j of its rows_per)
+CTTS_DEV int weight_row(const DitGridArgs& a, int kind, int n, int j) {
+  if (kind == kGU) return 128 * (n / 64) + n % 64 + 64 * j;  // gate, then up (tile interleave)
+  if (kind == kOut) return n % a.L;
+  return n;
+}
+
+CTTS_DEV void stage_weights(const DitGridArgs& a, Stage& st, int kind, int l) {
+  if (threadIdx.x == 0) {
+    const KindGeom g = geom(a, kind, l);
+    int n0, n1;
+    my_cols(g.N, n0, n1);
+    const uint32_t row_bytes = (uint32_t)g.K * 4u;
+    const uint32_t bytes = (uint32_t)(n1 - n0) * g.rows_per * row_bytes;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(st.bar), "r"(bytes) : "memory");
+    const uint32_t dst0 = static_cast<uint32_t>(__cvta_generic_to_shared(st.wbuf));
+    for (int n = n0; n < n1; n++)
+      for (int j = 0; j < g.rows_per; j++) {
+        const float* src = g.base + (size_t)weight_row(a, kind, n, j) * g.K;
+        const uint32_t dst = dst0 + (uint32_t)(((n - n0) * g.rows_per + j)) * row_bytes;
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         dst),
+                     "l"(src), "r"(row_bytes), "r"(st.bar)
+                     : "memory");
+      }
+  }
+}
+
+CTTS_DEV void wait_weights(const DitGridArgs& a, Stage& st) {
+  bool done = false;
+  for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
+    uint32_t d;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(d)
+        : "r"(st.bar), "r"(st.ph & 1u)
+        : "memory");
+    done = d != 0;
+  }
+  if (!done && threadIdx.x == 0 && a.err) atomicExch(a.err, 4);
+  st.ph++;
+}
+
+// P1: norm1 (+ modulate) -> this CTA's QKV columns.
+CTTS_DEV void phase_qkv(const DitGridArgs& a, Stage& st, int l, float* sm) {
+  const int rows = 3 * a.R, H = a.H, qkvw = (a.nq + 2 * a.nkv) * a.hd;
+  norm_rows(a, a.norm1[l], l, 0, 1, sm);
+  wait_weights(a, st);
+  __syncthreads();
+  int n0, n1;
+  my_cols(qkvw, n0, n1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int n = n0 + warp; n < n1; n += kWarps) {
+    float acc[DitGridArgs::kMaxRows];
+    row_dots<DitGridArgs::kMaxRows>(st.wbuf + (size_t)(n - n0) * H, H, sm, rows, acc);
+    if (lane == 0)
+      for (int r = 0; r < rows; r++) a.qkv[(size_t)r * qkvw + n] = acc[r];
+  }
+}
+
+// P2: 3-token bidirectional attention with RoPE at positions 0..2 (every
+// CTA, all rows; dit.rs:277-306, 361-405) -> this CTA's o-proj columns ->
+// gated residual (h += (1 + gate) * o).
+CTTS_DEV void phase_attn_o(const DitGridArgs& a, Stage& st, int l, float* sm) {
+  const int rows = 3 * a.R, H = a.H, hd = a.hd, nq = a.nq, nkv = a.nkv;
+  const int qkvw = (nq + 2 * nkv) * hd, qd = nq * hd, G = nq / nkv;
+  float* qs = sm;                         // [rows][qkvw]
+  float* att = sm + (size_t)rows * qkvw;  // [rows][qd]
+  load_rows(qs, a.qkv, rows * qkvw);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float scale = 1.0f / sqrtf((float)hd);
+  for (int job = warp; job < a.R * nq; job += kWarps) {
+    const int u = job / nq, h = job % nq, kh = h / G;
+    float q[3][2], k[3][2], v[3][2];
+#pragma unroll
+    for (int s = 0; s < 3; s++) {
+      const float* row = qs + (size_t)(3 * u + s) * qkvw;
+#pragma unroll
+      for (int j = 0; j < 2; j++) {
+        q[s][j] = row[h * hd + lane + 32 * j];
+        k[s][j] = row[(nq + kh) * hd + lane + 32 * j];
+        v[s][j] = row[(nq + nkv + kh) * hd + lane + 32 * j];
+      }
+      // rotate-half: dim lane pairs with lane + 32 (head_dim 64)
+      float sn, cs;
+      sincosf((float)s * a.inv_freq[lane], &sn, &cs);
+      float a1 = q[s][0], a2 = q[s][1];
+      q[s][0] = a1 * cs - a2 * sn;
+      q[s][1] = a1 * sn + a2 * cs;
+      a1 = k[s][0];
+      a2 = k[s][1];
+      k[s][0] = a1 * cs - a2 * sn;
+      k[s][1] = a1 * sn + a2 * cs;
+    }
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+      float sc[3], m = -INFINITY;
+#pragma unroll
+      for (int j2 = 0; j2 < 3; j2++) {
+        sc[j2] = warp_sum(fmaf(q[i][0], k[j2][0], q[i][1] * k[j2][1])) * scale;
+        m = fmaxf(m, sc[j2]);
+      }
+      float lsum = 0.0f;
+#pragma unroll
+      for (int j2 = 0; j2 < 3; j2++) {
+        sc[j2] = expf(sc[j2] - m);
+        lsum += sc[j2];
+      }
+      const float inv = 1.0f / lsum;
+      float* o = att + (size_t)(3 * u + i) * qd + h * hd;
+#pragma unroll
+      for (int j = 0; j < 2; j++) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int j2 = 0; j2 < 3; j2++) acc = fmaf(sc[j2] * inv, v[j2][j], acc);
+        o[lane + 32 * j] = acc;
+      }
+    }
+  }
+  wait_weights(a, st);
+  __syncthreads();
+  int n0, n1;
+  my_cols(H, n0, n1);
+  const long adld = (long)a.NL * 6 * H;
+  for (int n = n0 + warp; n < n1; n += kWarps) {
+    float acc[DitGridArgs::kMaxRows];
+    row_dots<DitGridArgs::kMaxRows>(st.wbuf + (size_t)(n - n0) * qd, qd, att, rows, acc);
+    if (lane == 0)
+      for (int r = 0; r < rows; r++) {
+        const float coef = a.ad ? 1.0f + a.ad[(size_t)(r / 3) * adld + (size_t)l * 6 * H + 2 * H + n] : 1.0f;
+        float* y = a.seq + (size_t)r * H + n;
+        *y = ldcg(y) + coef * acc[r];
+      }
+  }
+}
+
+// P3: norm2 (+ modulate) -> this CTA's SwiGLU columns (staged as gate row,
+// up row per column).
+CTTS_DEV void phase_gate_up(const DitGridArgs& a, Stage& st, int l, float* sm) {
+  const int rows = 3 * a.R, H = a.H, F = a.F;
+  norm_rows(a, a.norm2[l], l, 3, 4, sm);
+  wait_weights(a, st);
+  __syncthreads();
+  int n0, n1;
+  my_cols(F, n0, n1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int j = n0 + warp; j < n1; j += kWarps) {
+    float g[DitGridArgs::kMaxRows], u[DitGridArgs::kMaxRows];
+    row_dots<DitGridArgs::kMaxRows>(st.wbuf + (size_t)(2 * (j - n0)) * H, H, sm, rows, g);
+    row_dots<DitGridArgs::kMaxRows>(st.wbuf + (size_t)(2 * (j - n0) + 1) * H, H, sm, rows, u);
+    if (lane == 0)
+      for (int r = 0; r < rows; r++) a.act[(size_t)r * F + j] = silu(g[r]) * u[r];
+  }
+}
+
+// P4: down over the SwiGLU rows -> gated residual.
+CTTS_DEV void phase_down(const DitGridArgs& a, Stage& st, int l, float* sm) {
+  const int rows = 3 * a.R, H = a.H, F = a.F;
+  load_rows(sm, a.act, rows * F);
+  wait_weights(a, st);
+  __syncthreads();
+  int n0, n1;
+  my_cols(H, n0, n1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long adld = (long)a.NL * 6 * H;
+  for (int n = n0 + warp; n < n1; n += kWarps) {
+    float acc[DitGridArgs::kMaxRows];
+    row_dots<DitGridArgs::kMaxRows>(st.wbuf + (size_t)(n - n0) * F, F, sm, rows, acc);
+    if (lane == 0)
+      for (int r = 0; r < rows; r++) {
+        const float coef = a.ad ? 1.0f + a.ad[(size_t)(r / 3) * adld + (size_t)l * 6 * H + 5 * H + n] : 1.0f;
+        float* y = a.seq + (size_t)r * H + n;
+        *y = ldcg(y) + coef * acc[r];
+      }
+  }
+}
+
+// T1: final norm of each utterance's x row (token 2), out_proj, Euler
+// update x += dt * (v + b) on this CTA's outputs.
+CTTS_DEV void phase_out(const DitGridArgs& a, Stage& st, int stp, float* sm) {
+  const int H = a.H, L = a.L, R = a.R, nv = H >> 7;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int u = warp; u < R; u += kWarps) {
+    const float* src = a.seq + (size_t)(3 * u + 2) * H;
+    float4 v[kMaxH4];
+#pragma unroll
+    for (int i = 0; i < kMaxH4; i++)
+      if (i < nv) v[i] = ldcg4(src + lane * 4 + 128 * i);
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kMaxH4; i++)
+      if (i < nv) ss = fmaf(v[i].x, v[i].x, fmaf(v[i].y, v[i].y, fmaf(v[i].z, v[i].z, fmaf(v[i].w, v[i].w, ss))));
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)H + a.eps);
+#pragma unroll
+    for (int i = 0; i < kMaxH4; i++) {
+      if (i >= nv) break;
+      const int k = lane * 4 + 128 * i;
+      *reinterpret_cast<float4*>(sm + (size_t)u * H + k) =
+          make_float4(v[i].x * inv * a.final_norm[k], v[i].y * inv * a.final_norm[k + 1],
+                      v[i].z * inv * a.final_norm[k + 2], v[i].w * inv * a.final_norm[k + 3]);
+    }
+  }
+  wait_weights(a, st);
+  __syncthreads();
+  int o0, o1;
+  my_cols(R * L, o0, o1);
+  for (int o = o0 + warp; o < o1; o += kWarps) {
+    const int u = o / L, l = o % L;
+    float acc[1];
+    row_dots<1>(st.wbuf + (size_t)(o - o0) * H, H, sm + (size_t)u * H, 1, acc);
+    if (lane == 0) {
+      float* x = a.x + (size_t)u * L + l;
+      *x = ldcg(x) + a.dts[stp] * (acc[0] + (a.out_b ? a.out_b[l] : 0.0f));
+    }
+  }
+}
+
+// T2: the sequence rows of step stn: [mu + temb + dtemb; cond; in_proj(x)]
+// for this CTA's columns.
+CTTS_DEV void phase_fill(const DitGridArgs& a, Stage& st, int stn, float* sm) {
+  const int H = a.H, L = a.L, R = a.R;
+  for (int i = threadIdx.x; i < R * L; i += kThreads) sm[i] = ldcg(a.x + i);
+  wait_weights(a, st);
+  __syncthreads();
+  int n0, n1;
+  my_cols(H, n0, n1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int n = n0 + warp; n < n1; n += kWarps) {
+    const float* w = st.wbuf + (size_t)(n - n0) * L;
+    for (int u = 0; u < R; u++) {
+      float acc = 0.0f;
+      for (int k = lane; k < L; k += 32) acc = fmaf(w[k], sm[u * L + k], acc);
+      acc = warp_sum(acc);
+      if (lane == 0) {
+        float* row = a.seq + (size_t)(3 * u) * H + n;
+        row[0] = (a.mu[(size_t)u * H + n] + a.temb[(size_t)stn * H + n]) + a.dtemb[n];
+        row[H] = a.condh[(size_t)u * H + n];
+        row[2 * H] = acc + (a.in_b ? a.in_b[n] : 0.0f);
+      }
+    }
+  }
+}
+
+// Shared memory: activations [act_floats], weight staging [w_floats], one
+// mbarrier.  The staging buffer holds the largest per-CTA phase share.
+struct GridSmem {
+  size_t act_floats, w_floats;
+};
+__host__ __device__ inline size_t cdiv_sz(size_t a, size_t b) { return (a + b - 1) / b; }
+__host__ __device__ inline GridSmem grid_smem(int R, int H, int F, int nq, int nkv, int hd, int L, int G) {
+  const size_t rows = 3 * (size_t)R, qkvw = (size_t)(nq + 2 * nkv) * hd, qd = (size_t)nq * hd;
+  GridSmem m;
+  m.act_floats = rows * (size_t)H;
+  if (rows * (size_t)F > m.act_floats) m.act_floats = rows * (size_t)F;
+  if (rows * (qkvw + qd) > m.act_floats) m.act_floats = rows * (qkvw + qd);
+  const size_t w[6] = {(cdiv_sz(qkvw, G) + 1) * H, (cdiv_sz(H, G) + 1) * qd, (cdiv_sz(F, G) + 1) * 2 * H,
+                       (cdiv_sz(H, G) + 1) * F, (cdiv_sz((size_t)R * L, G) + 1) * H, (cdiv_sz(H, G) + 1) * L};
+  m.w_floats = 0;
+  for (size_t v : w) m.w_floats = v > m.w_floats ? v : m.w_floats;
+  return m;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) dit_grid_kernel(const DitGridArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  const GridSmem gs = grid_smem(a.R, a.H, a.F, a.nq, a.nkv, a.hd, a.L, gridDim.x);
+  Stage st;
+  st.wbuf = sm + gs.act_floats;
+  st.bar = static_cast<uint32_t>(__cvta_generic_to_shared(sm + ((gs.act_floats + gs.w_floats + 3) & ~(size_t)3)));
+  st.ph = 0;
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(st.bar));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  int k = 0;  // barrier index
+  // each phase's weights are staged right after the previous phase, before
+  // the barrier that opens it
+  stage_weights(a, st, kFill, 0);
+  phase_fill(a, st, 0, sm);
+  for (int stp = 0; stp < a.steps; stp++) {
+    for (int l = 0; l < a.NL; l++) {
+      __syncthreads();
+      stage_weights(a, st, kQKV, l);
+      grid_sync(a, k++);
+      phase_qkv(a, st, l, sm);
+      __syncthreads();
+      stage_weights(a, st, kO, l);
+      grid_sync(a, k++);
+      phase_attn_o(a, st, l, sm);
+      __syncthreads();
+      stage_weights(a, st, kGU, l);
+      grid_sync(a, k++);
+      phase_gate_up(a, st, l, sm);
+      __syncthreads();
+      stage_weights(a, st, kD, l);
+      grid_sync(a, k++);
+      phase_down(a, st, l, sm);
+    }
+    __syncthreads();
+    stage_weights(a, st, kOut, 0);
+    grid_sync(a, k++);
+    phase_out(a, st, stp, sm);
+    if (stp + 1 < a.steps) {
+      __syncthreads();
+      stage_weights(a, st, kFill, 0);
+      grid_sync(a, k++);
+      phase_fill(a, st, stp + 1, sm);
+    }
+  }
+  // the last CTA to leave zeroes the counters for the next launch
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(a.bar + k, 1u) == gridDim.x - 1) {
+      for (int i = 0; i <= k; i++) a.bar[i] = 0u;
+      __threadfence();
+    }
+  }
+}
+
+size_t grid_smem_bytes(int R, int H, int F, int nq, int nkv, int hd, int L, int G) {
+  const GridSmem m = grid_smem(R, H, F, nq, nkv, hd, L, G);
+  return (((m.act_floats + m.w_floats + 3) & ~(size_t)3) + 4) * sizeof(float);
+}
+
+int grid_ctas() {
+  static int n = -1;
+  if (n < 0) {
+    int dev = 0, sms = 0, coop = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
+    n = coop ? sms : 0;
+  }
+  return n;
+}
+
+}  // namespace
+
+int dit_grid_counters(int NL, int steps) { return 1 + steps * (4 * NL + 2) + 1; }
+
+bool dit_grid_supported(int R, int NL, int steps, int H, int nq, int nkv, int hd, int F, int L) {
+  if (R < 1 || 3 * R > DitGridArgs::kMaxRows || NL < 1 || NL > DitGridArgs::kMaxNL || steps < 1 ||
+      steps > DitGridArgs::kMaxSteps)
+    return false;
+  if (hd != 64 || nkv < 1 || nq % nkv || H % 128 || F % 128 || L > 64 || (nq * hd) % 128 ||
+      ((nq + 2 * nkv) * hd) % 4)
+    return false;
+  if (H > 128 * kMaxH4 || grid_ctas() <= 0) return false;
+  return grid_smem_bytes(R, H, F, nq, nkv, hd, L, grid_ctas()) <= 200 * 1024;
+}
+
+cudaError_t launch_dit_grid(const DitGridArgs& a, cudaStream_t s) {
+  if (!dit_grid_supported(a.R, a.NL, a.steps, a.H, a.nq, a.nkv, a.hd, a.F, a.L) || !a.bar)
+    return cudaErrorInvalidValue;
+  const size_t smem = grid_smem_bytes(a.R, a.H, a.F, a.nq, a.nkv, a.hd, a.L, grid_ctas());
+  static size_t configured = 0;
+  if (smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(dit_grid_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dit_grid_kernel, kThreads, smem);
+  if (e != cudaSuccess || per_sm < 1) return e != cudaSuccess ? e : cudaErrorInvalidConfiguration;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid_ctas());
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the grid barriers need it
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, dit_grid_kernel, a);
+  if (e != cudaSuccess) (void)cudaGetLastError();
+  return e;
+}
+
+}  // namespace ctts
+
+#ifdef CTTS_GRID_TRACE
+extern "C" __attribute__((visibility("default"))) int ctts_grid_trace(long long* out) {
+  return cudaMemcpyFromSymbol(out, ctts::g_grid_trace, sizeof(long long) * 2048) == cudaSuccess ? 0 : -2;
+}
+#endif

@@ -1,0 +1,47 @@
+// dit_grid.cuh -- host interface of the grid-persistent DiT Euler loop for
+// small batches with fp32 weights (dit_grid.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ctts {
+
+struct DitGridArgs {
+  static constexpr int kMaxNL = 8, kMaxSteps = 16, kMaxRows = 12;
+  int R = 0;                      // utterances (3 token rows each: patch 1)
+  int NL = 0, steps = 0;
+  int H = 0, nq = 0, nkv = 0, hd = 0, F = 0, L = 0;
+  float eps = 1e-6f;
+  float dts[kMaxSteps];
+  float* seq = nullptr;           // [3R, H] residual stream (workspace)
+  float* qkv = nullptr;           // [3R, (nq+2nkv)*hd]
+  float* act = nullptr;           // [3R, F]
+  float* x = nullptr;             // [R, L] in: x0, out: x after `steps` Euler steps
+  const float* mu = nullptr;      // [R, H]
+  const float* temb = nullptr;    // [steps, H]
+  const float* dtemb = nullptr;   // [H]
+  const float* condh = nullptr;   // [R, H]
+  const float* ad = nullptr;      // [R, NL*6H] AdaLN or null
+  const float* inv_freq = nullptr;  // [hd/2]
+  const float* final_norm = nullptr;
+  const float *in_w = nullptr, *in_b = nullptr;    // [H, L], [H]
+  const float *out_w = nullptr, *out_b = nullptr;  // [L, H], [L]
+  const float* wqkv[kMaxNL] = {};  // [(nq+2nkv)*hd, H]
+  const float* wo[kMaxNL] = {};    // [H, nq*hd]
+  const float* wgu[kMaxNL] = {};   // [2F, H], 64-row gate/up interleave
+  const float* wd[kMaxNL] = {};    // [H, F]
+  const float* norm1[kMaxNL] = {};
+  const float* norm2[kMaxNL] = {};
+  unsigned* bar = nullptr;        // barrier counters, zero at rest (dit_grid_counters())
+  int* err = nullptr;
+};
+
+// Barrier counters the launch needs (all zero between launches).
+int dit_grid_counters(int NL, int steps);
+// True when the shapes fit the kernel (patch 1, head_dim 64, sizes below
+// the shared-memory budget) and a grid of one CTA per SM can be resident.
+bool dit_grid_supported(int R, int NL, int steps, int H, int nq, int nkv, int hd, int F, int L);
+cudaError_t launch_dit_grid(const DitGridArgs& a, cudaStream_t s);
+
+}  // namespace ctts

@@ -6,6 +6,7 @@
 
 #include "api_common.h"
 #include "dit_cluster.cuh"
+#include "dit_grid.cuh"
 
 // LM stack (replaces QwenW, qwen.rs:26-44).  Weights of a layer are fused
 // into wide matrices at load: [q;k;v] -> wqkv, [gate;up] -> wgu, so one
@@ -65,6 +66,7 @@ struct DitWs {  // workspace for `rows` utterance-branches
   uint16_t *xb = nullptr, *attb = nullptr, *actb = nullptr;
   ctts::TcScratch tc;
   int* err = nullptr;
+  unsigned* gbar = nullptr;  // grid-persistent Euler loop barrier counters (zero at rest)
 };
 
 struct ctts_dit {

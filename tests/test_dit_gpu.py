@@ -120,3 +120,26 @@ def test_cluster_euler_loop_matches_launch_chain(monkeypatch, adaln):
         ref = o.euler_sample(x0[b], z[b], c[b], spk[b] if adaln else None, 10)
         assert cosine(outs["1"][b], ref) >= 0.999, b
         assert rel_err(outs["1"][b], ref) < 2e-3, b
+
+
+@pytest.mark.parametrize("adaln,B", [(True, 1), (False, 3), (True, 4)])
+def test_grid_euler_loop_matches_launch_chain(monkeypatch, adaln, B):
+    """fp32, small batch: the grid-persistent Euler loop (one launch for all
+    10 steps, CTTS_DIT_GRID unset) against the per-step launch chain
+    (CTTS_DIT_GRID=0) and the oracle, twice in a row (its barrier counters
+    must be back at zero after each launch)."""
+    cfg = DiTConfig(adaln=adaln)
+    x0, z, c = rnd(31, (B, 64)), rnd(32, (B, 768)), rnd(33, (B, 64))
+    spk = z if adaln else None
+    outs = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("CTTS_DIT_GRID", flag)
+        m, w = dit_model(cfg, seed=26)
+        outs[flag] = [m.euler_sample(x0, z, c, spk, 10) for _ in range(2)]
+        del m
+    assert np.array_equal(outs["1"][0], outs["1"][1])
+    o = orc.DiT(cfg, w)
+    for b in range(B):
+        assert rel_err(outs["1"][0][b], outs["0"][0][b]) < 1e-5, b
+        ref = o.euler_sample(x0[b], z[b], c[b], spk[b] if adaln else None, 10)
+        assert rel_err(outs["1"][0][b], ref) < 1e-4, b
