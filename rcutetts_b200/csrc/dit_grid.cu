@@ -54,8 +54,21 @@ CTTS_DEV void grid_trace(int i) {
   g_grid_trace[i] = t;
 }
 #define GRID_TRACE(i) grid_trace(i)
+// inside-phase marks: g_grid_sub[kind][mark] accumulates the time from the
+// phase start to the mark (CTA 0, thread 0)
+__device__ long long g_grid_sub[6][4];
+CTTS_DEV long long gtime() {
+  long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define SUB_START() const long long sub_t0 = gtime()
+#define SUB_MARK(kind, m) \
+  if (blockIdx.x == 0 && threadIdx.x == 0) g_grid_sub[kind][m] += gtime() - sub_t0
 #else
 #define GRID_TRACE(i)
+#define SUB_START()
+#define SUB_MARK(kind, m)
 #endif
 
 // Grid barrier k: every CTA's writes before it are visible to every CTA
@@ -84,10 +97,12 @@ CTTS_DEV void grid_sync(const DitGridArgs& a, int k) {
 // memory xs[rows][H]: one warp per row, every load of the row issued before
 // its use (prep/linear_rows semantics: x * inv * gain, then
 // * (1 + scale) + shift).
-CTTS_DEV void norm_rows(const DitGridArgs& a, const float* gain, int l, int shift_k, int scale_k, float* xs) {
+template <int RW>
+CTTS_DEV void norm_rows(const DitGridArgs& a, const float* aux, float* xs) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rows = 3 * a.R, H = a.H, nv = H >> 7;
-  const long adld = (long)a.NL * 6 * H;
+  constexpr int rows = RW;
+  const int H = a.H, nv = H >> 7;
+  const float* gain = aux;  // staged: gain [H], per utterance [shift | scale]
   for (int r = warp; r < rows; r += kWarps) {
     const float* src = a.seq + (size_t)r * H;
     float* dst = xs + (size_t)r * H;
@@ -101,7 +116,7 @@ CTTS_DEV void norm_rows(const DitGridArgs& a, const float* gain, int l, int shif
       if (i < nv) ss = fmaf(v[i].x, v[i].x, fmaf(v[i].y, v[i].y, fmaf(v[i].z, v[i].z, fmaf(v[i].w, v[i].w, ss))));
     ss = warp_sum(ss);
     const float inv = 1.0f / sqrtf(ss / (float)H + a.eps);
-    const float* md = a.ad ? a.ad + (size_t)(r / 3) * adld + (size_t)l * 6 * H : nullptr;
+    const float* md = a.ad ? aux + H + (size_t)(r / 3) * 2 * H : nullptr;
 #pragma unroll
     for (int i = 0; i < kMaxH4; i++) {
       if (i >= nv) break;
@@ -110,7 +125,7 @@ CTTS_DEV void norm_rows(const DitGridArgs& a, const float* gain, int l, int shif
 #pragma unroll
       for (int j = 0; j < 4; j++) {
         e[j] = e[j] * inv * gain[k + j];
-        if (md) e[j] = e[j] * (1.0f + md[scale_k * H + k + j]) + md[shift_k * H + k + j];
+        if (md) e[j] = e[j] * (1.0f + md[H + k + j]) + md[k + j];
       }
       *reinterpret_cast<float4*>(dst + k) = make_float4(e[0], e[1], e[2], e[3]);
     }
@@ -137,25 +152,22 @@ CTTS_DEV void load_rows(float* dst, const float* src, int n) {
 
 // One output column for every row: acc[r] = w[:] . xs[r, :] with the weight
 // row already staged in shared memory (warp, lanes over 4-element groups).
-template <int MAXR>
-CTTS_DEV void row_dots(const float* w, int K, const float* xs, int rows, float* acc) {
+template <int RW>
+CTTS_DEV void row_dots(const float* w, int K, const float* xs, float* acc) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int r = 0; r < MAXR; r++) acc[r] = 0.0f;
+  for (int r = 0; r < RW; r++) acc[r] = 0.0f;
+#pragma unroll 4
   for (int k = lane * 4; k < K; k += 128) {
     const float4 wv = *reinterpret_cast<const float4*>(w + k);
 #pragma unroll
-    for (int r = 0; r < MAXR; r++) {
-      if (r >= rows) break;
+    for (int r = 0; r < RW; r++) {
       const float4 xv = *reinterpret_cast<const float4*>(xs + (size_t)r * K + k);
       acc[r] = fmaf(wv.x, xv.x, fmaf(wv.y, xv.y, fmaf(wv.z, xv.z, fmaf(wv.w, xv.w, acc[r]))));
     }
   }
 #pragma unroll
-  for (int r = 0; r < MAXR; r++) {
-    if (r >= rows) break;
-    acc[r] = warp_sum(acc[r]);
-  }
+  for (int r = 0; r < RW; r++) acc[r] = warp_sum(acc[r]);
 }
 
 // This CTA's share [n0, n1) of N output columns.
@@ -172,9 +184,13 @@ enum Kind { kQKV, kO, kGU, kD, kOut, kFill };
 
 struct Stage {
   float* wbuf;
+  float* aux;    // the phase's small operands: norm gains, AdaLN rows, embeddings
+  float* rope;   // [3 positions][cos 32, sin 32]
+  float* resv;   // [rows][kMaxCols] this CTA's columns of the residual stream
   uint32_t bar;  // shared address of the mbarrier
   uint32_t ph;   // uses so far (parity of the next wait)
 };
+constexpr int kMaxCols = 8;  // residual columns per CTA (hidden / CTAs)
 
 struct KindGeom {
   const float* base;
@@ -198,15 +214,55 @@ CTTS_DEV int weight_row(const DitGridArgs& a, int kind, int n, int j) {
   return n;
 }
 
-CTTS_DEV void stage_weights(const DitGridArgs& a, Stage& st, int kind, int l) {
+CTTS_DEV void bulk_copy(uint32_t dst, const float* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// The phase's small operands into st.aux (all 16-byte aligned vectors):
+//   kQKV/kGU: norm gain [H], then per utterance [shift | scale] [2H]
+//   kO/kD:    per utterance the AdaLN gate [H]
+//   kOut:     final norm [H]
+//   kFill:    mu [R][H], cond [R][H], temb(stn) [H], dtemb [H]
+CTTS_DEV uint32_t stage_aux(const DitGridArgs& a, Stage& st, int kind, int l, int stn, bool issue) {
+  const int H = a.H, R = a.R;
+  const long adld = (long)a.NL * 6 * H;
+  const uint32_t dst0 = static_cast<uint32_t>(__cvta_generic_to_shared(st.aux));
+  const uint32_t hb = (uint32_t)H * 4u;
+  uint32_t bytes = 0;
+  auto cp = [&](const float* src, uint32_t nbytes) {
+    if (issue) bulk_copy(dst0 + bytes, src, nbytes, st.bar);
+    bytes += nbytes;
+  };
+  if (kind == kQKV || kind == kGU) {
+    cp(kind == kQKV ? a.norm1[l] : a.norm2[l], hb);
+    if (a.ad)
+      for (int u = 0; u < R; u++) cp(a.ad + (size_t)u * adld + (size_t)l * 6 * H + (kind == kQKV ? 0 : 3) * H, 2 * hb);
+  } else if (kind == kO || kind == kD) {
+    if (a.ad)
+      for (int u = 0; u < R; u++) cp(a.ad + (size_t)u * adld + (size_t)l * 6 * H + (kind == kO ? 2 : 5) * H, hb);
+  } else if (kind == kOut) {
+    cp(a.final_norm, hb);
+  } else {
+    cp(a.mu, (uint32_t)R * hb);
+    cp(a.condh, (uint32_t)R * hb);
+    cp(a.temb + (size_t)stn * H, hb);
+    cp(a.dtemb, hb);
+  }
+  return bytes;
+}
+
+CTTS_DEV void stage_weights(const DitGridArgs& a, Stage& st, int kind, int l, int stn = 0) {
   if (threadIdx.x == 0) {
     const KindGeom g = geom(a, kind, l);
     int n0, n1;
     my_cols(g.N, n0, n1);
     const uint32_t row_bytes = (uint32_t)g.K * 4u;
-    const uint32_t bytes = (uint32_t)(n1 - n0) * g.rows_per * row_bytes;
+    const uint32_t bytes = (uint32_t)(n1 - n0) * g.rows_per * row_bytes + stage_aux(a, st, kind, l, stn, false);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(st.bar), "r"(bytes) : "memory");
+    stage_aux(a, st, kind, l, stn, true);
     const uint32_t dst0 = static_cast<uint32_t>(__cvta_generic_to_shared(st.wbuf));
     for (int n = n0; n < n1; n++)
       for (int j = 0; j < g.rows_per; j++) {
@@ -238,18 +294,21 @@ CTTS_DEV void wait_weights(const DitGridArgs& a, Stage& st) {
 }
 
 // P1: norm1 (+ modulate) -> this CTA's QKV columns.
+template <int RW>
 CTTS_DEV void phase_qkv(const DitGridArgs& a, Stage& st, int l, float* sm) {
-  const int rows = 3 * a.R, H = a.H, qkvw = (a.nq + 2 * a.nkv) * a.hd;
-  norm_rows(a, a.norm1[l], l, 0, 1, sm);
+  constexpr int rows = RW;
+  const int H = a.H, qkvw = (a.nq + 2 * a.nkv) * a.hd;
   wait_weights(a, st);
+  norm_rows<RW>(a, st.aux, sm);
   __syncthreads();
   int n0, n1;
   my_cols(qkvw, n0, n1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int n = n0 + warp; n < n1; n += kWarps) {
-    float acc[DitGridArgs::kMaxRows];
-    row_dots<DitGridArgs::kMaxRows>(st.wbuf + (size_t)(n - n0) * H, H, sm, rows, acc);
+    float acc[RW];
+    row_dots<RW>(st.wbuf + (size_t)(n - n0) * H, H, sm, acc);
     if (lane == 0)
+#pragma unroll
       for (int r = 0; r < rows; r++) a.qkv[(size_t)r * qkvw + n] = acc[r];
   }
 }
@@ -257,13 +316,17 @@ CTTS_DEV void phase_qkv(const DitGridArgs& a, Stage& st, int l, float* sm) {
 // P2: 3-token bidirectional attention with RoPE at positions 0..2 (every
 // CTA, all rows; dit.rs:277-306, 361-405) -> this CTA's o-proj columns ->
 // gated residual (h += (1 + gate) * o).
+template <int RW>
 CTTS_DEV void phase_attn_o(const DitGridArgs& a, Stage& st, int l, float* sm) {
-  const int rows = 3 * a.R, H = a.H, hd = a.hd, nq = a.nq, nkv = a.nkv;
+  SUB_START();
+  constexpr int rows = RW;
+  const int H = a.H, hd = a.hd, nq = a.nq, nkv = a.nkv;
   const int qkvw = (nq + 2 * nkv) * hd, qd = nq * hd, G = nq / nkv;
   float* qs = sm;                         // [rows][qkvw]
   float* att = sm + (size_t)rows * qkvw;  // [rows][qd]
   load_rows(qs, a.qkv, rows * qkvw);
   __syncthreads();
+  SUB_MARK(kO, 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float scale = 1.0f / sqrtf((float)hd);
   for (int job = warp; job < a.R * nq; job += kWarps) {
@@ -279,8 +342,7 @@ CTTS_DEV void phase_attn_o(const DitGridArgs& a, Stage& st, int l, float* sm) {
         v[s][j] = row[(nq + nkv + kh) * hd + lane + 32 * j];
       }
       // rotate-half: dim lane pairs with lane + 32 (head_dim 64)
-      float sn, cs;
-      sincosf((float)s * a.inv_freq[lane], &sn, &cs);
+      const float cs = st.rope[s * 64 + lane], sn = st.rope[s * 64 + 32 + lane];
       float a1 = q[s][0], a2 = q[s][1];
       q[s][0] = a1 * cs - a2 * sn;
       q[s][1] = a1 * sn + a2 * cs;
@@ -314,60 +376,75 @@ CTTS_DEV void phase_attn_o(const DitGridArgs& a, Stage& st, int l, float* sm) {
       }
     }
   }
+  SUB_MARK(kO, 1);
   wait_weights(a, st);
   __syncthreads();
+  SUB_MARK(kO, 2);
   int n0, n1;
   my_cols(H, n0, n1);
-  const long adld = (long)a.NL * 6 * H;
   for (int n = n0 + warp; n < n1; n += kWarps) {
-    float acc[DitGridArgs::kMaxRows];
-    row_dots<DitGridArgs::kMaxRows>(st.wbuf + (size_t)(n - n0) * qd, qd, att, rows, acc);
+    float acc[RW];
+    row_dots<RW>(st.wbuf + (size_t)(n - n0) * qd, qd, att, acc);
     if (lane == 0)
+#pragma unroll
       for (int r = 0; r < rows; r++) {
-        const float coef = a.ad ? 1.0f + a.ad[(size_t)(r / 3) * adld + (size_t)l * 6 * H + 2 * H + n] : 1.0f;
-        float* y = a.seq + (size_t)r * H + n;
-        *y = ldcg(y) + coef * acc[r];
+        const float coef = a.ad ? 1.0f + st.aux[(size_t)(r / 3) * H + n] : 1.0f;
+        float* rv = st.resv + r * kMaxCols + (n - n0);
+        *rv = *rv + coef * acc[r];
+        a.seq[(size_t)r * H + n] = *rv;
       }
   }
 }
 
 // P3: norm2 (+ modulate) -> this CTA's SwiGLU columns (staged as gate row,
 // up row per column).
+template <int RW>
 CTTS_DEV void phase_gate_up(const DitGridArgs& a, Stage& st, int l, float* sm) {
-  const int rows = 3 * a.R, H = a.H, F = a.F;
-  norm_rows(a, a.norm2[l], l, 3, 4, sm);
+  SUB_START();
+  constexpr int rows = RW;
+  const int H = a.H, F = a.F;
   wait_weights(a, st);
+  SUB_MARK(kGU, 0);
+  norm_rows<RW>(a, st.aux, sm);
   __syncthreads();
+  SUB_MARK(kGU, 1);
   int n0, n1;
   my_cols(F, n0, n1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int j = n0 + warp; j < n1; j += kWarps) {
-    float g[DitGridArgs::kMaxRows], u[DitGridArgs::kMaxRows];
-    row_dots<DitGridArgs::kMaxRows>(st.wbuf + (size_t)(2 * (j - n0)) * H, H, sm, rows, g);
-    row_dots<DitGridArgs::kMaxRows>(st.wbuf + (size_t)(2 * (j - n0) + 1) * H, H, sm, rows, u);
+    float g[RW], u[RW];
+    row_dots<RW>(st.wbuf + (size_t)(2 * (j - n0)) * H, H, sm, g);
+    row_dots<RW>(st.wbuf + (size_t)(2 * (j - n0) + 1) * H, H, sm, u);
     if (lane == 0)
+#pragma unroll
       for (int r = 0; r < rows; r++) a.act[(size_t)r * F + j] = silu(g[r]) * u[r];
   }
+  SUB_MARK(kGU, 2);
+  __syncthreads();
+  SUB_MARK(kGU, 3);
 }
 
 // P4: down over the SwiGLU rows -> gated residual.
+template <int RW>
 CTTS_DEV void phase_down(const DitGridArgs& a, Stage& st, int l, float* sm) {
-  const int rows = 3 * a.R, H = a.H, F = a.F;
+  constexpr int rows = RW;
+  const int H = a.H, F = a.F;
   load_rows(sm, a.act, rows * F);
   wait_weights(a, st);
   __syncthreads();
   int n0, n1;
   my_cols(H, n0, n1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long adld = (long)a.NL * 6 * H;
   for (int n = n0 + warp; n < n1; n += kWarps) {
-    float acc[DitGridArgs::kMaxRows];
-    row_dots<DitGridArgs::kMaxRows>(st.wbuf + (size_t)(n - n0) * F, F, sm, rows, acc);
+    float acc[RW];
+    row_dots<RW>(st.wbuf + (size_t)(n - n0) * F, F, sm, acc);
     if (lane == 0)
+#pragma unroll
       for (int r = 0; r < rows; r++) {
-        const float coef = a.ad ? 1.0f + a.ad[(size_t)(r / 3) * adld + (size_t)l * 6 * H + 5 * H + n] : 1.0f;
-        float* y = a.seq + (size_t)r * H + n;
-        *y = ldcg(y) + coef * acc[r];
+        const float coef = a.ad ? 1.0f + st.aux[(size_t)(r / 3) * H + n] : 1.0f;
+        float* rv = st.resv + r * kMaxCols + (n - n0);
+        *rv = *rv + coef * acc[r];
+        a.seq[(size_t)r * H + n] = *rv;
       }
   }
 }
@@ -377,6 +454,8 @@ CTTS_DEV void phase_down(const DitGridArgs& a, Stage& st, int l, float* sm) {
 CTTS_DEV void phase_out(const DitGridArgs& a, Stage& st, int stp, float* sm) {
   const int H = a.H, L = a.L, R = a.R, nv = H >> 7;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  wait_weights(a, st);
+  const float* fnorm = st.aux;
   for (int u = warp; u < R; u += kWarps) {
     const float* src = a.seq + (size_t)(3 * u + 2) * H;
     float4 v[kMaxH4];
@@ -394,18 +473,17 @@ CTTS_DEV void phase_out(const DitGridArgs& a, Stage& st, int stp, float* sm) {
       if (i >= nv) break;
       const int k = lane * 4 + 128 * i;
       *reinterpret_cast<float4*>(sm + (size_t)u * H + k) =
-          make_float4(v[i].x * inv * a.final_norm[k], v[i].y * inv * a.final_norm[k + 1],
-                      v[i].z * inv * a.final_norm[k + 2], v[i].w * inv * a.final_norm[k + 3]);
+          make_float4(v[i].x * inv * fnorm[k], v[i].y * inv * fnorm[k + 1], v[i].z * inv * fnorm[k + 2],
+                      v[i].w * inv * fnorm[k + 3]);
     }
   }
-  wait_weights(a, st);
   __syncthreads();
   int o0, o1;
   my_cols(R * L, o0, o1);
   for (int o = o0 + warp; o < o1; o += kWarps) {
     const int u = o / L, l = o % L;
     float acc[1];
-    row_dots<1>(st.wbuf + (size_t)(o - o0) * H, H, sm + (size_t)u * H, 1, acc);
+    row_dots<1>(st.wbuf + (size_t)(o - o0) * H, H, sm + (size_t)u * H, acc);
     if (lane == 0) {
       float* x = a.x + (size_t)u * L + l;
       *x = ldcg(x) + a.dts[stp] * (acc[0] + (a.out_b ? a.out_b[l] : 0.0f));
@@ -430,10 +508,18 @@ CTTS_DEV void phase_fill(const DitGridArgs& a, Stage& st, int stn, float* sm) {
       for (int k = lane; k < L; k += 32) acc = fmaf(w[k], sm[u * L + k], acc);
       acc = warp_sum(acc);
       if (lane == 0) {
+        const float* aux = st.aux;  // mu [R][H], cond [R][H], temb [H], dtemb [H]
+        const float v0 = (aux[(size_t)u * H + n] + aux[(size_t)2 * R * H + n]) + aux[(size_t)(2 * R + 1) * H + n];
+        const float v1 = aux[(size_t)(R + u) * H + n];
+        const float v2 = acc + (a.in_b ? a.in_b[n] : 0.0f);
         float* row = a.seq + (size_t)(3 * u) * H + n;
-        row[0] = (a.mu[(size_t)u * H + n] + a.temb[(size_t)stn * H + n]) + a.dtemb[n];
-        row[H] = a.condh[(size_t)u * H + n];
-        row[2 * H] = acc + (a.in_b ? a.in_b[n] : 0.0f);
+        row[0] = v0;
+        row[H] = v1;
+        row[2 * H] = v2;
+        float* rv = st.resv + (3 * u) * kMaxCols + (n - n0);
+        rv[0] = v0;
+        rv[kMaxCols] = v1;
+        rv[2 * kMaxCols] = v2;
       }
     }
   }
@@ -442,7 +528,11 @@ CTTS_DEV void phase_fill(const DitGridArgs& a, Stage& st, int stn, float* sm) {
 // Shared memory: activations [act_floats], weight staging [w_floats], one
 // mbarrier.  The staging buffer holds the largest per-CTA phase share.
 struct GridSmem {
-  size_t act_floats, w_floats;
+  size_t act_floats, w_floats, aux_floats;
+  __host__ __device__ size_t aux_off() const { return act_floats + w_floats; }
+  __host__ __device__ size_t rope_off() const { return aux_off() + aux_floats; }
+  __host__ __device__ size_t resv_off() const { return rope_off() + 192; }
+  __host__ __device__ size_t bar_off() const { return (resv_off() + DitGridArgs::kMaxRows * kMaxCols + 3) & ~(size_t)3; }
 };
 __host__ __device__ inline size_t cdiv_sz(size_t a, size_t b) { return (a + b - 1) / b; }
 __host__ __device__ inline GridSmem grid_smem(int R, int H, int F, int nq, int nkv, int hd, int L, int G) {
@@ -455,16 +545,29 @@ __host__ __device__ inline GridSmem grid_smem(int R, int H, int F, int nq, int n
                        (cdiv_sz(H, G) + 1) * F, (cdiv_sz((size_t)R * L, G) + 1) * H, (cdiv_sz(H, G) + 1) * L};
   m.w_floats = 0;
   for (size_t v : w) m.w_floats = v > m.w_floats ? v : m.w_floats;
+  m.w_floats = (m.w_floats + 3) & ~(size_t)3;  // 16-byte aligned areas
+  m.aux_floats = (size_t)(2 * R + 2) * H;
   return m;
 }
 
+template <int RW>
 __global__ void __launch_bounds__(kThreads, 1) dit_grid_kernel(const DitGridArgs a) {
   extern __shared__ __align__(16) float sm[];
   const GridSmem gs = grid_smem(a.R, a.H, a.F, a.nq, a.nkv, a.hd, a.L, gridDim.x);
   Stage st;
   st.wbuf = sm + gs.act_floats;
-  st.bar = static_cast<uint32_t>(__cvta_generic_to_shared(sm + ((gs.act_floats + gs.w_floats + 3) & ~(size_t)3)));
+  st.aux = sm + gs.aux_off();
+  st.rope = sm + gs.rope_off();
+  st.resv = sm + gs.resv_off();
+  st.bar = static_cast<uint32_t>(__cvta_generic_to_shared(sm + gs.bar_off()));
   st.ph = 0;
+  if (threadIdx.x < 96) {  // RoPE of token positions 0..2 (dit.rs:277-306)
+    const int sp = threadIdx.x / 32, j = threadIdx.x % 32;
+    float sn, cs;
+    sincosf((float)sp * a.inv_freq[j], &sn, &cs);
+    st.rope[sp * 64 + j] = cs;
+    st.rope[sp * 64 + 32 + j] = sn;
+  }
   if (threadIdx.x == 0) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(st.bar));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -473,26 +576,26 @@ __global__ void __launch_bounds__(kThreads, 1) dit_grid_kernel(const DitGridArgs
   int k = 0;  // barrier index
   // each phase's weights are staged right after the previous phase, before
   // the barrier that opens it
-  stage_weights(a, st, kFill, 0);
+  stage_weights(a, st, kFill, 0, 0);
   phase_fill(a, st, 0, sm);
   for (int stp = 0; stp < a.steps; stp++) {
     for (int l = 0; l < a.NL; l++) {
       __syncthreads();
       stage_weights(a, st, kQKV, l);
       grid_sync(a, k++);
-      phase_qkv(a, st, l, sm);
+      phase_qkv<RW>(a, st, l, sm);
       __syncthreads();
       stage_weights(a, st, kO, l);
       grid_sync(a, k++);
-      phase_attn_o(a, st, l, sm);
+      phase_attn_o<RW>(a, st, l, sm);
       __syncthreads();
       stage_weights(a, st, kGU, l);
       grid_sync(a, k++);
-      phase_gate_up(a, st, l, sm);
+      phase_gate_up<RW>(a, st, l, sm);
       __syncthreads();
       stage_weights(a, st, kD, l);
       grid_sync(a, k++);
-      phase_down(a, st, l, sm);
+      phase_down<RW>(a, st, l, sm);
     }
     __syncthreads();
     stage_weights(a, st, kOut, 0);
@@ -500,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1) dit_grid_kernel(const DitGridArgs
     phase_out(a, st, stp, sm);
     if (stp + 1 < a.steps) {
       __syncthreads();
-      stage_weights(a, st, kFill, 0);
+      stage_weights(a, st, kFill, 0, stp + 1);
       grid_sync(a, k++);
       phase_fill(a, st, stp + 1, sm);
     }
@@ -518,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1) dit_grid_kernel(const DitGridArgs
 
 size_t grid_smem_bytes(int R, int H, int F, int nq, int nkv, int hd, int L, int G) {
   const GridSmem m = grid_smem(R, H, F, nq, nkv, hd, L, G);
-  return (((m.act_floats + m.w_floats + 3) & ~(size_t)3) + 4) * sizeof(float);
+  return (m.bar_off() + 4) * sizeof(float);
 }
 
 int grid_ctas() {
@@ -544,22 +647,22 @@ bool dit_grid_supported(int R, int NL, int steps, int H, int nq, int nkv, int hd
   if (hd != 64 || nkv < 1 || nq % nkv || H % 128 || F % 128 || L > 64 || (nq * hd) % 128 ||
       ((nq + 2 * nkv) * hd) % 4)
     return false;
-  if (H > 128 * kMaxH4 || grid_ctas() <= 0) return false;
+  if (H > 128 * kMaxH4 || grid_ctas() <= 0 || (H + grid_ctas() - 1) / grid_ctas() > kMaxCols) return false;
   return grid_smem_bytes(R, H, F, nq, nkv, hd, L, grid_ctas()) <= 200 * 1024;
 }
 
-cudaError_t launch_dit_grid(const DitGridArgs& a, cudaStream_t s) {
-  if (!dit_grid_supported(a.R, a.NL, a.steps, a.H, a.nq, a.nkv, a.hd, a.F, a.L) || !a.bar)
-    return cudaErrorInvalidValue;
-  const size_t smem = grid_smem_bytes(a.R, a.H, a.F, a.nq, a.nkv, a.hd, a.L, grid_ctas());
+namespace {
+
+template <int RW>
+cudaError_t launch_rows(const DitGridArgs& a, size_t smem, cudaStream_t s) {
   static size_t configured = 0;
   if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(dit_grid_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(dit_grid_kernel<RW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     configured = smem;
   }
   int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dit_grid_kernel, kThreads, smem);
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dit_grid_kernel<RW>, kThreads, smem);
   if (e != cudaSuccess || per_sm < 1) return e != cudaSuccess ? e : cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid_ctas());
@@ -571,15 +674,32 @@ cudaError_t launch_dit_grid(const DitGridArgs& a, cudaStream_t s) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, dit_grid_kernel, a);
+  e = cudaLaunchKernelEx(&cfg, dit_grid_kernel<RW>, a);
   if (e != cudaSuccess) (void)cudaGetLastError();
   return e;
+}
+
+}  // namespace
+
+cudaError_t launch_dit_grid(const DitGridArgs& a, cudaStream_t s) {
+  if (!dit_grid_supported(a.R, a.NL, a.steps, a.H, a.nq, a.nkv, a.hd, a.F, a.L) || !a.bar)
+    return cudaErrorInvalidValue;
+  const size_t smem = grid_smem_bytes(a.R, a.H, a.F, a.nq, a.nkv, a.hd, a.L, grid_ctas());
+  switch (a.R) {
+    case 1: return launch_rows<3>(a, smem, s);
+    case 2: return launch_rows<6>(a, smem, s);
+    case 3: return launch_rows<9>(a, smem, s);
+    default: return launch_rows<12>(a, smem, s);
+  }
 }
 
 }  // namespace ctts
 
 #ifdef CTTS_GRID_TRACE
 extern "C" __attribute__((visibility("default"))) int ctts_grid_trace(long long* out) {
+  cudaMemcpyFromSymbol(out + 2048, ctts::g_grid_sub, sizeof(long long) * 24);
+  long long z[24] = {0};
+  cudaMemcpyToSymbol(ctts::g_grid_sub, z, sizeof(z));
   return cudaMemcpyFromSymbol(out, ctts::g_grid_trace, sizeof(long long) * 2048) == cudaSuccess ? 0 : -2;
 }
 #endif
