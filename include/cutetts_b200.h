@@ -217,6 +217,19 @@ CTTS_API int ctts_vae_decode_batch(ctts_vae* v, int batch, const float* latent, 
 CTTS_API int ctts_vae_decode_batch_dev(ctts_vae* v, int batch, const float* latent_dev, int T,
                               float* wav_dev, void* stream);
 
+/* Streaming decoder (replaces rust-codec/src/stream.rs:62 StreamingDecoder::new,
+ * :82 reset, :96 decode_chunk): per-conv left histories carried across
+ * chunks, so decoding an utterance chunk by chunk gives exactly the samples
+ * of the offline decode.  latent [batch, latent, frames] -> wav
+ * [batch, frames*hop]; histories start (and reset) at zero. */
+typedef struct ctts_vae_stream ctts_vae_stream;
+CTTS_API int ctts_vae_stream_create(ctts_vae* v, int batch, ctts_vae_stream** out);
+CTTS_API int ctts_vae_stream_reset(ctts_vae_stream* s);
+CTTS_API int ctts_vae_stream_decode_chunk(ctts_vae_stream* s, const float* latent, int frames, float* wav);
+CTTS_API int ctts_vae_stream_decode_chunk_dev(ctts_vae_stream* s, const float* latent_dev, int frames,
+                              float* wav_dev, void* stream);
+CTTS_API void ctts_vae_stream_free(ctts_vae_stream* s);
+
 /* Exact signatures of rust-codec/src/ffi.rs:19-65 (used by
  * src/cutetts/modeling/rust_vae.py through ctypes).  The handle decodes
  * the shipped topology read from the file (latent 64, rates read from the

@@ -90,6 +90,11 @@ SIGNATURES = {
     "ctts_vae_free": (None, [vp]),
     "ctts_vae_decode_batch": (C.c_int, [vp, C.c_int, fp, C.c_int, fp]),
     "ctts_vae_decode_batch_dev": (C.c_int, [vp, C.c_int, vp, C.c_int, vp, vp]),
+    "ctts_vae_stream_create": (C.c_int, [vp, C.c_int, C.POINTER(vp)]),
+    "ctts_vae_stream_reset": (C.c_int, [vp]),
+    "ctts_vae_stream_decode_chunk": (C.c_int, [vp, fp, C.c_int, fp]),
+    "ctts_vae_stream_decode_chunk_dev": (C.c_int, [vp, vp, C.c_int, vp, vp]),
+    "ctts_vae_stream_free": (None, [vp]),
     "cutetts_vae_load": (vp, [C.c_char_p]),
     "cutetts_vae_free": (None, [vp]),
     "cutetts_vae_decode": (C.c_int, [vp, fp, C.c_ulong, fp]),

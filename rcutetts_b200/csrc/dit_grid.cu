@@ -31,7 +31,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr uint32_t kSpinLimit = 1u << 24;
+constexpr uint32_t kSpinLimit = 1u << 22;  // polls of about 1 us: seconds
 constexpr int kMaxH4 = 8;  // hidden <= 1024: 16-byte groups per lane of a row
 
 CTTS_DEV float ldcg(const float* p) { return __ldcg(p); }
@@ -82,7 +82,8 @@ CTTS_DEV void grid_sync(const DitGridArgs& a, int k) {
     const unsigned n = gridDim.x;
     uint32_t it = 0;
     while (ld_acquire(a.bar + k) < n) {
-      if (++it == kSpinLimit) {
+      // a CTA that already gave up somewhere makes every later wait end at once
+      if (++it == kSpinLimit || ((it & 1023u) == 0 && a.err && *reinterpret_cast<volatile int*>(a.err) != 0)) {
         if (a.err) atomicExch(a.err, 4);
         break;
       }

@@ -165,10 +165,16 @@ struct ConvArgs {
   int B = 0, Cin = 0, Cout = 0, Tin = 0, Tout = 0, k = 1, dil = 1, left = 0;
   int stride = 1;   // transposed conv stride
   int tanh_out = 0;
+  int xoff = 0;     // output position t reads input position t + xoff + j*dil - left
+                    // (streaming: the input carries xoff history columns)
 };
 cudaError_t launch_conv1d(const ConvArgs& a, cudaStream_t s);
 cudaError_t launch_conv_transpose(const ConvArgs& a, cudaStream_t s);
 cudaError_t launch_snake(const float* x, int B, int C, int T, const float* alpha, float* y,
                          cudaStream_t s);
+// Streaming history: ext[b, c, :] = hist_in[b, c, 0:H] ++ x[b, c, 0:T] and
+// hist_out[b, c, :] = the last H columns of ext (hist_out != hist_in).
+cudaError_t launch_stream_ext(const float* hist_in, const float* x, float* ext, float* hist_out, int B, int C,
+                              int H, int T, cudaStream_t s);
 
 }  // namespace ctts

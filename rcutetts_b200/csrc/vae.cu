@@ -66,7 +66,7 @@ __global__ void __launch_bounds__(256) conv_kernel(const ConvArgs a, int Tc, int
       float v = 0.0f;
       if (kidx2 < KK && t0 + tt < Tc) {
         int c = kidx2 / k, j = kidx2 % k;
-        int src = t0 + tt + j * a.dil - a.left;
+        int src = t0 + tt + a.xoff + j * a.dil - a.left;
         if (src >= 0 && src < a.Tin) {
           v = xb[(size_t)c * a.Tin + src];
           if (a.snake_alpha) v = snake1(v, a.snake_alpha[c]);
@@ -117,7 +117,7 @@ __global__ void snake_kernel(const float* x, int C, int T, const float* alpha, f
 }  // namespace
 
 cudaError_t launch_conv1d(const ConvArgs& a, cudaStream_t s) {
-  if (a.Tout != a.Tin) return cudaErrorInvalidValue;
+  if (a.Tout + a.xoff != a.Tin || a.xoff < 0) return cudaErrorInvalidValue;
   dim3 grid((a.Tout + TT - 1) / TT, (a.Cout + TO - 1) / TO, a.B);
   if (a.w_bf16)
     CTTS_LK(launch_k(conv_kernel<true>, dim3(grid), dim3(256), 0, s, a, a.Tout, 1, 1, 0));
@@ -129,13 +129,40 @@ cudaError_t launch_conv1d(const ConvArgs& a, cudaStream_t s) {
 // a.w: repacked [stride][Cout][Cin*2] (tap 0 <- x[i-1], tap 1 <- x[i]);
 // a.k must be 2, a.dil 1, a.left 1; Tout = Tin * stride.
 cudaError_t launch_conv_transpose(const ConvArgs& a, cudaStream_t s) {
-  if (a.k != 2 || a.Tout != a.Tin * a.stride) return cudaErrorInvalidValue;
-  dim3 grid((a.Tin + TT - 1) / TT, (a.Cout + TO - 1) / TO, a.B * a.stride);
+  const int Tc = a.Tin - a.xoff;  // input positions that produce output
+  if (a.k != 2 || a.xoff < 0 || a.Tout != Tc * a.stride) return cudaErrorInvalidValue;
+  dim3 grid((Tc + TT - 1) / TT, (a.Cout + TO - 1) / TO, a.B * a.stride);
   long wphase = (long)a.Cout * a.Cin * 2;
   if (a.w_bf16)
-    CTTS_LK(launch_k(conv_kernel<true>, dim3(grid), dim3(256), 0, s, a, a.Tin, a.stride, a.stride, wphase));
+    CTTS_LK(launch_k(conv_kernel<true>, dim3(grid), dim3(256), 0, s, a, Tc, a.stride, a.stride, wphase));
   else
-    CTTS_LK(launch_k(conv_kernel<false>, dim3(grid), dim3(256), 0, s, a, a.Tin, a.stride, a.stride, wphase));
+    CTTS_LK(launch_k(conv_kernel<false>, dim3(grid), dim3(256), 0, s, a, Tc, a.stride, a.stride, wphase));
+  return cudaGetLastError();
+}
+
+namespace {
+__global__ void stream_ext_kernel(const float* hist_in, const float* x, float* ext, float* hist_out, int H, int T,
+                                  size_t rows) {
+  grid_dep_enter();
+  const size_t row = blockIdx.x;
+  if (row >= rows) return;
+  const float* hi = hist_in + row * H;
+  const float* xi = x + row * T;
+  float* e = ext + row * (H + T);
+  for (int i = threadIdx.x; i < H + T; i += blockDim.x) e[i] = i < H ? hi[i] : xi[i - H];
+  // the last H columns of [hist ++ x]
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const int src = T + i;
+    hist_out[row * H + i] = src < H ? hi[src] : xi[src - H];
+  }
+}
+}  // namespace
+
+cudaError_t launch_stream_ext(const float* hist_in, const float* x, float* ext, float* hist_out, int B, int C,
+                              int H, int T, cudaStream_t s) {
+  const size_t rows = (size_t)B * C;
+  if (!rows || H <= 0 || T <= 0 || hist_in == hist_out) return cudaErrorInvalidValue;
+  CTTS_LK(launch_k(stream_ext_kernel, dim3((unsigned)rows), dim3(128), 0, s, hist_in, x, ext, hist_out, H, T, rows));
   return cudaGetLastError();
 }
 

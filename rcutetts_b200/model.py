@@ -339,6 +339,36 @@ class DecoderW(_Handle):
                                                     _tensor_ptr(wav), _stream(stream)))
 
 
+class StreamingDecoder(_Handle):
+    """Chunked VAE decode with the convs' left histories carried across
+    chunks (StreamingDecoder, stream.rs:62-139): decode_chunk output equals
+    the matching slice of the offline decode."""
+
+    _free = "ctts_vae_stream_free"
+
+    def __init__(self, w: DecoderW, batch: int = 1):
+        super().__init__()
+        self.w = w  # keeps the weights alive
+        self.batch = batch
+        check(_lib.load().ctts_vae_stream_create(w.h, batch, C.byref(self.h)))
+
+    def reset(self) -> None:
+        check(_lib.load().ctts_vae_stream_reset(self.h))
+
+    def decode_chunk(self, latent) -> np.ndarray:
+        """latent [latent, F] or [B, latent, F] -> wav [F*hop] / [B, F*hop]."""
+        lat = _f(latent)
+        single = lat.ndim == 2
+        if single:
+            lat = lat[None]
+        B, _, F = lat.shape
+        if B != self.batch:
+            raise ValueError(f"stream holds {self.batch} utterances, chunk has {B}")
+        wav = np.empty((B, F * self.w.cfg.hop), np.float32)
+        check(_lib.load().ctts_vae_stream_decode_chunk(self.h, _p(lat), F, _p(wav)))
+        return wav[0] if single else wav
+
+
 def load_decoder_weights(path: str, cfg: VAEConfig, dtype="f32", device: int = 0,
                          prefix: str = "decoder.") -> DecoderW:
     return DecoderW(cfg, dtype, device).load(path, prefix)
