@@ -230,6 +230,29 @@ CTTS_API int ctts_vae_stream_decode_chunk_dev(ctts_vae_stream* s, const float* l
                               float* wav_dev, void* stream);
 CTTS_API void ctts_vae_stream_free(ctts_vae_stream* s);
 
+/* ------------------------------------------------------- LocEnc feedback
+ * AudioLocEnc + locenc_to_lm_proj (replaces rust-codec/src/locenc.rs:222
+ * locenc_embed and load_locenc_weights :88; diffusion_head.py:334-378,
+ * model.py:128-130): x [n, patch, latent] (n items = utterance-steps) ->
+ * LM input rows [n, out_dim].  Tensor names are the module's own
+ * (special_token, in_proj.*, encoder.layers.{i}.*, encoder.norm.weight)
+ * plus locenc_to_lm_proj.*; ctts_locenc_load reads a full checkpoint with
+ * prefix "locenc.". */
+typedef struct {
+  int latent, hidden, n_heads, n_kv_heads, head_dim, ffn, n_layers, patch, out_dim;
+  float rms_eps, rope_theta;
+  int weight_dtype;
+} ctts_locenc_config;
+typedef struct ctts_locenc ctts_locenc;
+CTTS_API int ctts_locenc_create(const ctts_locenc_config* cfg, int device, ctts_locenc** out);
+CTTS_API int ctts_locenc_set_tensor(ctts_locenc* l, const char* name, const void* host, int dtype,
+                           const int64_t* shape, int ndim);
+CTTS_API int ctts_locenc_load(ctts_locenc* l, const char* safetensors_path, const char* prefix);
+CTTS_API int ctts_locenc_missing(const ctts_locenc* l);
+CTTS_API void ctts_locenc_free(ctts_locenc* l);
+CTTS_API int ctts_locenc_embed(ctts_locenc* l, const float* x, int n, float* out);
+CTTS_API int ctts_locenc_embed_dev(ctts_locenc* l, const float* x_dev, int n, float* out_dev, void* stream);
+
 /* Exact signatures of rust-codec/src/ffi.rs:19-65 (used by
  * src/cutetts/modeling/rust_vae.py through ctypes).  The handle decodes
  * the shipped topology read from the file (latent 64, rates read from the

@@ -337,6 +337,24 @@ static void dit_layer(const orc_dit_dims* d, const orc_dit_layer_w* lw, float* h
   free(g); free(u); free(qr); free(kr); free(scores);
 }
 
+/* locenc_embed (locenc.rs:222-255): per item the sequence [CLS, in_proj of
+ * the patch frames], plain LocalTransformer layers, final RMSNorm of the CLS
+ * row, then locenc_to_lm_proj (model.py:128-130). */
+void orc_locenc_embed(const orc_dit_dims* d, const orc_locenc_w* w, const float* x, int n, float* out) {
+  const int H = d->hidden, P = d->patch, S = 1 + P, L = d->latent;
+  float* hs = malloc(sizeof(float) * S * H);
+  float* cls = malloc(sizeof(float) * H);
+  for (int it = 0; it < n; it++) {
+    memcpy(hs, w->special, sizeof(float) * H);
+    orc_linear(x + (size_t)it * P * L, P, L, w->in_w, w->in_b, H, hs + H);
+    for (int l = 0; l < d->n_layers; l++) dit_layer(d, &w->layers[l], hs, S, NULL);
+    orc_rms_norm_row(hs, w->final_norm, H, d->eps, cls);
+    orc_linear(cls, 1, H, w->proj_w, w->proj_b, w->out_dim, out + (size_t)it * w->out_dim);
+  }
+  free(hs);
+  free(cls);
+}
+
 /* Per-sample constants (dit.rs:756-772 sample_prologue): dt_emb, the
  * mu token without t_emb (mu_proj(z) + cfg + step), per-layer adaln. */
 typedef struct {

@@ -95,6 +95,18 @@ typedef struct {
   const orc_dit_layer_w* layers;
 } orc_dit_w;
 
+/* LocEnc + locenc_to_lm_proj (locenc.rs:222-255 locenc_embed,
+ * diffusion_head.py:334-378 AudioLocEnc, model.py:128-130): dims use
+ * latent (input), hidden, n_heads, n_kv, head_dim, ffn, n_layers, patch,
+ * eps, rope_theta of orc_dit_dims; layers are plain (adaln NULL). */
+typedef struct {
+  const float *in_w, *in_b, *special, *final_norm, *proj_w, *proj_b;
+  const orc_dit_layer_w* layers;
+  int out_dim;
+} orc_locenc_w;
+/* x [n][patch][latent] -> out [n][out_dim] */
+void orc_locenc_embed(const orc_dit_dims* d, const orc_locenc_w* w, const float* x, int n, float* out);
+
 /* SinusoidalPosEmb (diffusion_head.py:306-320, dit.rs:262-273) */
 void orc_sin_emb(float x, int dim, float* out);
 /* sway_timesteps (dit.rs:846-854) -> steps+1 floats */

@@ -83,6 +83,11 @@ class DiTW(C.Structure):
         [("layers", C.POINTER(DiTLayerW))]
 
 
+class LocEncW(C.Structure):
+    _fields_ = [(n, fp) for n in ("in_w", "in_b", "special", "final_norm", "proj_w", "proj_b")] + \
+               [("layers", C.POINTER(DiTLayerW)), ("out_dim", C.c_int)]
+
+
 class ResW(C.Structure):
     _fields_ = [(n, fp) for n in ("a0", "w0", "b0", "a1", "w1", "b1")]
 
@@ -286,6 +291,39 @@ class DiT:
         lib().orc_dit_euler_sample_cfg(C.byref(self.dims), C.byref(self.W), *[_p(v) for v in a],
                                        _p(spk), steps, C.c_float(coeff), C.c_float(cfg), _p(x))
         return x
+
+
+class LocEnc:
+    """locenc_embed + locenc_to_lm_proj (locenc.rs:222-255, model.py:128-130)."""
+
+    def __init__(self, cfg, weights: dict):
+        self.cfg = cfg
+        self.w = {k: _f(v) for k, v in weights.items()}
+        self.dims = DiTDims(cfg.latent, cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn,
+                            cfg.n_layers, cfg.patch, 0, 0, cfg.rms_eps, cfg.rope_theta)
+        g = lambda n: _p(self.w[n])
+        self.layers = (DiTLayerW * cfg.n_layers)()
+        for i in range(cfg.n_layers):
+            p = f"encoder.layers.{i}."
+            L = self.layers[i]
+            L.norm1, L.norm2 = g(p + "input_layernorm.weight"), g(p + "post_attention_layernorm.weight")
+            L.wq, L.wk = g(p + "self_attn.q_proj.weight"), g(p + "self_attn.k_proj.weight")
+            L.wv, L.wo = g(p + "self_attn.v_proj.weight"), g(p + "self_attn.o_proj.weight")
+            L.wg, L.wu = g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")
+            L.wd, L.adaln = g(p + "mlp.down_proj.weight"), None
+        W = LocEncW()
+        W.in_w, W.in_b, W.special = g("in_proj.weight"), g("in_proj.bias"), g("special_token")
+        W.final_norm, W.proj_w, W.proj_b = g("encoder.norm.weight"), g("locenc_to_lm_proj.weight"), \
+            g("locenc_to_lm_proj.bias")
+        W.layers, W.out_dim = self.layers, cfg.out_dim
+        self.W = W
+
+    def embed(self, x):
+        """x [n, patch, latent] -> [n, out_dim]"""
+        x = _f(x).reshape(-1, self.cfg.patch, self.cfg.latent)
+        out = np.empty((x.shape[0], self.cfg.out_dim), np.float32)
+        lib().orc_locenc_embed(C.byref(self.dims), C.byref(self.W), _p(x), x.shape[0], _p(out))
+        return out
 
 
 # ----------------------------------------------------------------------- VAE

@@ -40,6 +40,12 @@ class EngineConfigC(C.Structure):
                 ("groups", C.c_int)]
 
 
+class LocEncConfigC(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("latent", "hidden", "n_heads", "n_kv_heads", "head_dim", "ffn",
+                                       "n_layers", "patch", "out_dim")] + \
+               [("rms_eps", C.c_float), ("rope_theta", C.c_float), ("weight_dtype", C.c_int)]
+
+
 class VAEConfigC(C.Structure):
     _fields_ = [("latent", C.c_int), ("channels", C.c_int), ("n_stages", C.c_int),
                 ("depthwise", C.c_int), ("strides", C.c_int * 8), ("weight_dtype", C.c_int)]
@@ -95,6 +101,13 @@ SIGNATURES = {
     "ctts_vae_stream_decode_chunk": (C.c_int, [vp, fp, C.c_int, fp]),
     "ctts_vae_stream_decode_chunk_dev": (C.c_int, [vp, vp, C.c_int, vp, vp]),
     "ctts_vae_stream_free": (None, [vp]),
+    "ctts_locenc_create": (C.c_int, [C.POINTER(LocEncConfigC), C.c_int, C.POINTER(vp)]),
+    "ctts_locenc_set_tensor": (C.c_int, [vp, C.c_char_p, vp, C.c_int, i64p, C.c_int]),
+    "ctts_locenc_load": (C.c_int, [vp, C.c_char_p, C.c_char_p]),
+    "ctts_locenc_missing": (C.c_int, [vp]),
+    "ctts_locenc_free": (None, [vp]),
+    "ctts_locenc_embed": (C.c_int, [vp, fp, C.c_int, fp]),
+    "ctts_locenc_embed_dev": (C.c_int, [vp, vp, C.c_int, vp, vp]),
     "cutetts_vae_load": (vp, [C.c_char_p]),
     "cutetts_vae_free": (None, [vp]),
     "cutetts_vae_decode": (C.c_int, [vp, fp, C.c_ulong, fp]),

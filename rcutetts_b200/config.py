@@ -72,6 +72,25 @@ class DiTConfig:
 
 
 @dataclass(frozen=True)
+class LocEncConfig:
+    """AudioLocEnc (diffusion_head.py:334-378) + locenc_to_lm_proj
+    (model.py:55) at generic shape; the shipped model is hidden 1024,
+    ffn 4096, 16 heads / 2 KV heads, 2 layers, patch 2 (locenc.rs:22-24)."""
+
+    latent: int = 64
+    hidden: int = 1024
+    n_heads: int = 16
+    n_kv_heads: int = 2
+    head_dim: int = 64
+    ffn: int = 4096
+    n_layers: int = 2
+    patch: int = 2
+    out_dim: int = 768
+    rms_eps: float = 1e-6
+    rope_theta: float = 1e4
+
+
+@dataclass(frozen=True)
 class VAEConfig:
     """CausalDecoder (audio_vae.py:243-292) at generic shape."""
 

@@ -339,6 +339,50 @@ class DecoderW(_Handle):
                                                     _tensor_ptr(wav), _stream(stream)))
 
 
+class LocEncW(_Handle):
+    """Device-resident LocEnc + locenc_to_lm_proj (LocencW, locenc.rs:36-44;
+    embed = locenc_embed, locenc.rs:222-255 / model.py:128-130)."""
+
+    _free = "ctts_locenc_free"
+
+    def __init__(self, cfg, dtype="f32", device: int = 0):
+        super().__init__()
+        self.cfg = cfg
+        c = _lib.LocEncConfigC(cfg.latent, cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn,
+                               cfg.n_layers, cfg.patch, cfg.out_dim, cfg.rms_eps, cfg.rope_theta,
+                               _dtype_code(dtype))
+        check(_lib.load().ctts_locenc_create(C.byref(c), device, C.byref(self.h)))
+
+    def set_tensor(self, name: str, arr) -> None:
+        _set_tensor(_lib.load().ctts_locenc_set_tensor, self.h, name, arr)
+
+    def set_weights(self, weights: dict) -> "LocEncW":
+        for k, v in weights.items():
+            self.set_tensor(k, v)
+        return self
+
+    def load(self, path: str, prefix: str = "locenc.") -> "LocEncW":
+        check(_lib.load().ctts_locenc_load(self.h, path.encode(), prefix.encode()))
+        return self
+
+    @property
+    def missing(self) -> int:
+        return _lib.load().ctts_locenc_missing(self.h)
+
+    def embed(self, x) -> np.ndarray:
+        """x [n, patch, latent] (or [B, T, patch, latent]) -> [n, out_dim]."""
+        a = _f(x).reshape(-1, self.cfg.patch, self.cfg.latent)
+        out = np.empty((a.shape[0], self.cfg.out_dim), np.float32)
+        check(_lib.load().ctts_locenc_embed(self.h, _p(a), a.shape[0], _p(out)))
+        return out
+
+
+def locenc_embed(w: LocEncW, x, b: int | None = None, t: int | None = None, nth: int = 0) -> np.ndarray:
+    """locenc_embed(w, x, b, t, nth) (locenc.rs:222): x [B, T, patch, 64]
+    flattened -> [B*T, out_dim]; nth is accepted and ignored."""
+    return w.embed(x)
+
+
 class StreamingDecoder(_Handle):
     """Chunked VAE decode with the convs' left histories carried across
     chunks (StreamingDecoder, stream.rs:62-139): decode_chunk output equals

@@ -44,6 +44,31 @@ def lm_weights(cfg: LMConfig, seed: int, with_embed: bool = True) -> dict:
     return w
 
 
+def locenc_weights(cfg, seed: int) -> dict:
+    """AudioLocEnc tensors (names of the module, without `locenc.`) plus
+    locenc_to_lm_proj.*; norm gains 1."""
+    rng = np.random.default_rng(seed)
+    H, F = cfg.hidden, cfg.ffn
+    qd, kvd = cfg.n_heads * cfg.head_dim, cfg.n_kv_heads * cfg.head_dim
+    w = {"special_token": rng.standard_normal((1, 1, 1, H), dtype=np.float32),
+         "in_proj.weight": _normal(rng, (H, cfg.latent)), "in_proj.bias": _normal(rng, (H,))}
+    for i in range(cfg.n_layers):
+        p = f"encoder.layers.{i}."
+        w[p + "input_layernorm.weight"] = np.ones(H, np.float32)
+        w[p + "post_attention_layernorm.weight"] = np.ones(H, np.float32)
+        w[p + "self_attn.q_proj.weight"] = _normal(rng, (qd, H))
+        w[p + "self_attn.k_proj.weight"] = _normal(rng, (kvd, H))
+        w[p + "self_attn.v_proj.weight"] = _normal(rng, (kvd, H))
+        w[p + "self_attn.o_proj.weight"] = _normal(rng, (H, qd))
+        w[p + "mlp.gate_proj.weight"] = _normal(rng, (F, H))
+        w[p + "mlp.up_proj.weight"] = _normal(rng, (F, H))
+        w[p + "mlp.down_proj.weight"] = _normal(rng, (H, F))
+    w["encoder.norm.weight"] = np.ones(H, np.float32)
+    w["locenc_to_lm_proj.weight"] = _normal(rng, (cfg.out_dim, H))
+    w["locenc_to_lm_proj.bias"] = _normal(rng, (cfg.out_dim,))
+    return w
+
+
 def dit_weights(cfg: DiTConfig, seed: int) -> dict:
     """AudioDiTHead tensors, names without the `head.` prefix."""
     rng = np.random.default_rng(seed)

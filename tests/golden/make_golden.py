@@ -25,7 +25,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
 from rcutetts_b200 import synth  # noqa: E402
-from rcutetts_b200.config import DiTConfig, LMConfig, VAEConfig  # noqa: E402
+from rcutetts_b200.config import DiTConfig, LMConfig, LocEncConfig, VAEConfig  # noqa: E402
 
 torch.set_grad_enabled(False)
 
@@ -132,6 +132,39 @@ def torch_vae(av, cfg: VAEConfig, w: dict):
     return m
 
 
+# -------------------------------------------------------------------- LocEnc
+LOCENC_SMALL = LocEncConfig(hidden=256, n_heads=4, n_kv_heads=2, ffn=512, out_dim=128)
+LOCENC_SHIPPED = LocEncConfig()  # hidden 1024, ffn 4096, 16/2 heads, 2 layers, patch 2
+
+
+def torch_locenc(dh, cfg: LocEncConfig, w: dict):
+    """AudioLocEnc (diffusion_head.py:334-378) + locenc_to_lm_proj (model.py:55)."""
+    enc = dh.AudioLocEnc(input_dim=cfg.latent, hidden_dim=cfg.hidden, ffn_dim=cfg.ffn, num_layers=cfg.n_layers,
+                         num_heads=cfg.n_heads, num_kv_heads=cfg.n_kv_heads, patch_size=cfg.patch,
+                         rms_norm_eps=cfg.rms_eps, use_rope=True, rope_theta=cfg.rope_theta).float().eval()
+    enc.load_state_dict({k: torch.from_numpy(v) for k, v in w.items() if not k.startswith("locenc_to_lm_proj")},
+                        strict=True)
+    proj = torch.nn.Linear(cfg.hidden, cfg.out_dim).float().eval()
+    proj.weight.copy_(torch.from_numpy(w["locenc_to_lm_proj.weight"]))
+    proj.bias.copy_(torch.from_numpy(w["locenc_to_lm_proj.bias"]))
+    return lambda x: proj(enc(x))
+
+
+def make_locenc(root):
+    """locenc.npz: x [B, T, patch, 64] and proj(locenc(x)) [B, T, out_dim] for
+    the small config (weights synth.locenc_weights(seed 17)) and the shipped
+    shape (seed 18, one utterance-step pair)."""
+    dh, _ = load_reference(root)
+    out = {}
+    for tag, cfg, seed, shape in (("small", LOCENC_SMALL, 17, (2, 3)), ("shipped", LOCENC_SHIPPED, 18, (1, 2))):
+        w = synth.locenc_weights(cfg, seed)
+        x = rnd(seed + 100, shape + (cfg.patch, cfg.latent))
+        y = torch_locenc(dh, cfg, w)(torch.from_numpy(x)).numpy()
+        out[f"{tag}_x"], out[f"{tag}_out"] = x, y
+    np.savez_compressed(os.path.join(HERE, "locenc.npz"), **out)
+    print({k: v.shape for k, v in out.items()})
+
+
 def main(root):
     dh, av = load_reference(root)
     out = {}
@@ -219,4 +252,10 @@ def main(root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    args = [a for a in sys.argv[1:] if a != "locenc"]
+    root = args[0] if args else "/root/reference"
+    if "locenc" in sys.argv[1:]:
+        make_locenc(root)  # only the LocEnc fixture
+    else:
+        main(root)
+        make_locenc(root)

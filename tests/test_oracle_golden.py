@@ -172,3 +172,19 @@ def test_linear_threads_bitwise():
     assert np.array_equal(a, b)
     ref = (x.astype(np.float64) @ W.T.astype(np.float64))
     assert rel_err(a, ref) < 1e-5
+
+
+def test_locenc_vs_torch_module(golden):
+    """The LocEnc restatement (locenc.rs:222-255 + locenc_to_lm_proj) against
+    the reference's AudioLocEnc torch module (tests/golden/make_golden.py),
+    at a small shape and at the shipped shape (hidden 1024, 16/2 heads)."""
+    from rcutetts_b200 import synth
+    from rcutetts_b200.config import LocEncConfig
+
+    g = golden("locenc.npz")
+    for tag, cfg, seed in (("small", LocEncConfig(hidden=256, n_heads=4, n_kv_heads=2, ffn=512, out_dim=128), 17),
+                           ("shipped", LocEncConfig(), 18)):
+        o = orc.LocEnc(cfg, synth.locenc_weights(cfg, seed))
+        got = o.embed(g[f"{tag}_x"])
+        ref = g[f"{tag}_out"].reshape(got.shape)
+        assert rel_err(got, ref) < 1e-4, tag
