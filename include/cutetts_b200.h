@@ -168,6 +168,11 @@ typedef struct {
   float latent_scale, latent_bias; /* scaled = raw/scale - bias */
   int use_graph;     /* 1: capture the frame step as a CUDA graph */
   int groups;        /* sub-batches run as parallel graph branches (divides batch; <=0 -> 1) */
+  float cfg_strength; /* > 0: base-variant classifier-free guidance (bin/cutetts.rs:440-456,
+                         503-509): a second, unconditional LM branch per utterance (its own KV
+                         cache, prefilled with ctts_engine_prefill_uncond) fed the same latent,
+                         and the CFG Euler sampler v = vc + s*(vc - vu) on the sway grid */
+  float sway_coeff;   /* sway_timesteps coefficient of the CFG grid (dit.rs:846-854) */
 } ctts_engine_config;
 
 CTTS_API int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_config* cfg,
@@ -180,6 +185,9 @@ CTTS_API int ctts_engine_set_heads(ctts_engine* e, const float* stop_w, const fl
  * projected prompt latents) and set its first DiT cond (previous raw
  * latent patch, [patch*latent]). */
 CTTS_API int ctts_engine_prefill(ctts_engine* e, int b, const float* x, int T, const float* cond0);
+/* CFG mode: prefill utterance b's unconditional branch (x [T, hidden]) and
+ * its initial uncond latent condition. */
+CTTS_API int ctts_engine_prefill_uncond(ctts_engine* e, int b, const float* x, int T, const float* cond0);
 /* One frame for every utterance: noise [batch, patch*latent] (host) ->
  * latents_out [batch, patch*latent] (scaled), stop_out [batch, 2] or NULL. */
 CTTS_API int ctts_engine_step(ctts_engine* e, const float* noise, float* latents_out, float* stop_out);

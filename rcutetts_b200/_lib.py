@@ -37,7 +37,7 @@ class DiTConfigC(C.Structure):
 class EngineConfigC(C.Structure):
     _fields_ = [("batch", C.c_int), ("capacity", C.c_int), ("euler_steps", C.c_int),
                 ("latent_scale", C.c_float), ("latent_bias", C.c_float), ("use_graph", C.c_int),
-                ("groups", C.c_int)]
+                ("groups", C.c_int), ("cfg_strength", C.c_float), ("sway_coeff", C.c_float)]
 
 
 class LocEncConfigC(C.Structure):
@@ -84,6 +84,7 @@ SIGNATURES = {
     "ctts_engine_create": (C.c_int, [vp, vp, C.POINTER(EngineConfigC), C.POINTER(vp)]),
     "ctts_engine_set_heads": (C.c_int, [vp, fp, fp, fp, fp]),
     "ctts_engine_prefill": (C.c_int, [vp, C.c_int, fp, C.c_int, fp]),
+    "ctts_engine_prefill_uncond": (C.c_int, [vp, C.c_int, fp, C.c_int, fp]),
     "ctts_engine_step": (C.c_int, [vp, fp, fp, fp]),
     "ctts_engine_step_dev": (C.c_int, [vp, vp, vp, vp, vp]),
     "ctts_engine_launches_per_step": (C.c_int, [vp]),

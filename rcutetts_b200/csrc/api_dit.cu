@@ -664,9 +664,12 @@ int engine_enqueue_group(ctts_engine* e, EngineGroup& g, cudaStream_t s, int* la
   ctts_dit* d = e->dit;
   const int B = g.nb, H = lm->cfg.hidden;
   const int PL = d->cfg.patch * d->cfg.latent;
-  float* z = e->z + (size_t)g.b0 * H;
+  // with CFG a group's LM states and latent conditions are 2B rows:
+  // [conditional B | unconditional B]
+  const int zm = e->cfg_on ? 2 : 1;
+  float* z = e->z + (size_t)zm * g.b0 * H;
   float* x = e->x + (size_t)g.b0 * PL;
-  float* cond = e->cond + (size_t)g.b0 * PL;
+  float* cond = e->cond + (size_t)zm * g.b0 * PL;
   float* lat = e->lat + (size_t)g.b0 * PL;
   float* stop = e->stop + (size_t)g.b0 * 2;
   const float* noise = e->noise + (size_t)g.b0 * PL;
@@ -678,7 +681,7 @@ int engine_enqueue_group(ctts_engine* e, EngineGroup& g, cudaStream_t s, int* la
     CTTS_CK(launch_linear(a, s)); nl++;
   }
   const int steps = e->cfg.euler_steps;
-  std::vector<float> times(steps), dts(steps);
+  std::vector<float> times(steps + 1), dts(steps);
   const float dt = 1.0f / (float)steps;
   for (int i = 0; i < steps; i++) {
     times[i] = (float)i * dt;
@@ -688,16 +691,28 @@ int engine_enqueue_group(ctts_engine* e, EngineGroup& g, cudaStream_t s, int* la
   r.R = B; r.z = z; r.cond = cond; r.spk = d->cfg.adaln ? z : nullptr;
   r.x = x; r.x_rows = B; r.steps = steps; r.times = times.data(); r.dts = dts.data(); r.mode = 0;
   r.step_dt = dt;
+  if (e->cfg_on) {
+    // euler_sample_cfg (dit.rs:862-904) on the sway grid: both branches in
+    // one 2B-row pass, the unconditional rows without AdaLN conditioning
+    int rc0 = ctts_sway_timesteps(steps, e->cfg.sway_coeff, times.data());
+    if (rc0) return rc0;
+    for (int i = 0; i < steps; i++) dts[i] = times[i + 1] - times[i];
+    r.R = 2 * B; r.mode = 2; r.cfg = e->cfg.cfg_strength; r.cfg_w = e->cfg.cfg_strength;
+    r.zero_adaln_from = d->cfg.adaln ? B : -1;
+  }
   int rc = dit_enqueue(d, *g.ws, r, s, &nl);
   if (rc) return rc;
   CTTS_CK(launch_affine(x, B * PL, e->cfg.latent_scale, e->cfg.latent_bias, lat, s)); nl++;
-  CTTS_CK(cudaMemcpyAsync(cond, x, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
+  for (int h = 0; h < zm; h++)  // the raw latent conditions both branches (bin/cutetts.rs:474-480)
+    CTTS_CK(cudaMemcpyAsync(cond + (size_t)h * B * PL, x, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
   {  // feedback projection straight into the LM residual stream
     LinearArgs a; a.x = x; a.x_ld = PL; a.M = B; a.K = PL; a.N = H; a.w = e->proj_w;
     a.bias = e->proj_b; a.y = g.kv->h; a.y_ld = H;
     CTTS_CK(launch_linear(a, s)); nl++;
   }
-  rc = lm_forward_rows(lm, g.kv, B, -1, 0, z, s, &nl);
+  if (e->cfg_on)  // the same acoustic input feeds the unconditional branch (bin/cutetts.rs:503-509)
+    CTTS_CK(cudaMemcpyAsync(g.kv->h + (size_t)B * H, g.kv->h, sizeof(float) * B * H, cudaMemcpyDeviceToDevice, s));
+  rc = lm_forward_rows(lm, g.kv, zm * B, -1, 0, z, s, &nl);
   if (rc) return rc;
   if (launches) *launches += nl;
   return CTTS_OK;
@@ -764,6 +779,9 @@ extern "C" int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_
   rc = dit_check(dit);
   if (rc) return rc;
   CTTS_REQ(!dit->cfg.cfg_emb, CTTS_ERR_ARG, "engine runs the single-branch head (no cfg embedding)");
+  CTTS_REQ(cfg->cfg_strength >= 0.0f, CTTS_ERR_ARG, "cfg_strength must be >= 0");
+  const bool cfg_on = cfg->cfg_strength > 0.0f;
+  const int zm = cfg_on ? 2 : 1;
   CTTS_CK(cudaSetDevice(lm->device));
   auto* e = new ctts_engine();
   e->lm = lm;
@@ -781,8 +799,8 @@ extern "C" int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_
     g.ws = new DitWs();
     cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking);
     cudaEventCreateWithFlags(&g.done, cudaEventDisableTiming);
-    rc = ctts_kv_alloc(lm, per, cfg->capacity, &g.kv);
-    if (!rc) rc = dit_ws_ensure(dit, *g.ws, per, cfg->euler_steps);
+    rc = ctts_kv_alloc(lm, zm * per, cfg->capacity, &g.kv);
+    if (!rc) rc = dit_ws_ensure(dit, *g.ws, zm * per, cfg->euler_steps);
     if (rc) {
       engine_destroy(e);
       return rc;
@@ -795,9 +813,10 @@ extern "C" int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_
   e->stop_b = A.alloc<float>(2);
   e->proj_w = A.alloc<float>((size_t)H * PL);
   e->proj_b = A.alloc<float>(H);
-  e->z = A.alloc<float>((size_t)B * H);
+  e->cfg_on = cfg_on;
+  e->z = A.alloc<float>((size_t)zm * B * H);
   e->x = A.alloc<float>((size_t)B * PL);
-  e->cond = A.alloc<float>((size_t)B * PL);
+  e->cond = A.alloc<float>((size_t)zm * B * PL);
   e->lat = A.alloc<float>((size_t)B * PL);
   e->stop = A.alloc<float>((size_t)B * 2);
   e->noise = A.alloc<float>((size_t)B * PL);
@@ -808,6 +827,7 @@ extern "C" int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_
     return set_error(CTTS_ERR_NOMEM, "engine buffers");
   }
   e->prefilled.assign(B, false);
+  e->prefilled_u.assign(B, !cfg_on);
   *out = e;
   return CTTS_OK;
 }
@@ -826,34 +846,50 @@ extern "C" int ctts_engine_set_heads(ctts_engine* e, const float* stop_w, const 
   return CTTS_OK;
 }
 
-extern "C" int ctts_engine_prefill(ctts_engine* e, int b, const float* x, int T, const float* cond0) {
+namespace {
+// Prefill of utterance b's conditional (unc = false) or unconditional branch.
+int engine_prefill(ctts_engine* e, int b, const float* x, int T, const float* cond0, bool unc) {
   CTTS_REQ(e && x && cond0, CTTS_ERR_ARG, "null argument");
   CTTS_REQ(b >= 0 && b < e->cfg.batch && T > 0, CTTS_ERR_ARG, "bad utterance index or length");
+  CTTS_REQ(!unc || e->cfg_on, CTTS_ERR_STATE, "unconditional prefill needs cfg_strength > 0");
   CTTS_REQ(e->steps_done == 0, CTTS_ERR_STATE, "prefill after the first frame step");
   CTTS_CK(cudaSetDevice(e->lm->device));
   EngineGroup& g = e->groups[b / e->groups[0].nb];
   ctts_kv* kv = g.kv;
-  const int lb = b - g.b0;
+  const int zm = e->cfg_on ? 2 : 1;
+  const int slot = (b - g.b0) + (unc ? g.nb : 0);            // KV slot within the group
+  const size_t row = (size_t)zm * g.b0 + slot;               // z / cond row
   const int H = e->lm->cfg.hidden, PL = e->dit->cfg.patch * e->dit->cfg.latent;
   CTTS_REQ(T <= kv->ws_rows, CTTS_ERR_RANGE, "prefill length outside workspace");
   CTTS_CK(cudaMemcpyAsync(kv->xin, x, sizeof(float) * T * H, cudaMemcpyHostToDevice, e->stream));
-  int rc = ctts_lm_prefill_dev(e->lm, kv, lb, kv->xin, T, kv->xout, e->stream);
+  int rc = ctts_lm_prefill_dev(e->lm, kv, slot, kv->xin, T, kv->xout, e->stream);
   if (rc) return rc;
-  CTTS_CK(cudaMemcpyAsync(e->z + (size_t)b * H, kv->xout + (size_t)(T - 1) * H, sizeof(float) * H,
+  CTTS_CK(cudaMemcpyAsync(e->z + row * H, kv->xout + (size_t)(T - 1) * H, sizeof(float) * H,
                           cudaMemcpyDeviceToDevice, e->stream));
-  CTTS_CK(cudaMemcpyAsync(e->cond + (size_t)b * PL, cond0, sizeof(float) * PL, cudaMemcpyHostToDevice,
-                          e->stream));
+  CTTS_CK(cudaMemcpyAsync(e->cond + row * PL, cond0, sizeof(float) * PL, cudaMemcpyHostToDevice, e->stream));
   CTTS_CK(cudaStreamSynchronize(e->stream));
-  e->prefilled[b] = true;
+  (unc ? e->prefilled_u : e->prefilled)[b] = true;
   return CTTS_OK;
+}
+}  // namespace
+
+extern "C" int ctts_engine_prefill(ctts_engine* e, int b, const float* x, int T, const float* cond0) {
+  return engine_prefill(e, b, x, T, cond0, false);
+}
+
+extern "C" int ctts_engine_prefill_uncond(ctts_engine* e, int b, const float* x, int T, const float* cond0) {
+  return engine_prefill(e, b, x, T, cond0, true);
 }
 
 extern "C" int ctts_engine_step_dev(ctts_engine* e, const float* noise_dev, float* latents_dev,
                                     float* stop_dev, void* stream) {
   CTTS_REQ(e && noise_dev, CTTS_ERR_ARG, "null argument");
   CTTS_REQ(e->heads_set, CTTS_ERR_STATE, "engine heads not set");
-  for (int b = 0; b < e->cfg.batch; b++)
+  for (int b = 0; b < e->cfg.batch; b++) {
     CTTS_REQ(e->prefilled[b], CTTS_ERR_STATE, "utterance " + std::to_string(b) + " not prefilled");
+    CTTS_REQ(e->prefilled_u[b], CTTS_ERR_STATE,
+             "utterance " + std::to_string(b) + ": unconditional branch not prefilled");
+  }
   for (auto& g : e->groups)
     for (int b = 0; b < g.nb; b++) CTTS_REQ(g.kv->pos_host[b] < g.kv->cap, CTTS_ERR_RANGE, "KV cache full");
   CTTS_CK(cudaSetDevice(e->lm->device));

@@ -117,7 +117,8 @@ struct ctts_engine {
         *fb = nullptr, *noise = nullptr;
   float *h_noise = nullptr, *h_lat = nullptr, *h_stop = nullptr;  // pinned staging
   bool heads_set = false;
-  std::vector<bool> prefilled;
+  bool cfg_on = false;  // classifier-free guidance: per-group rows [cond B | uncond B]
+  std::vector<bool> prefilled, prefilled_u;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   int steps_done = 0;

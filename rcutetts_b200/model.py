@@ -255,12 +255,13 @@ class FrameEngine(_Handle):
 
     def __init__(self, lm: QwenW, dit: DitW, heads: dict, batch: int, capacity: int,
                  euler_steps: int = 10, latent_scale: float = 1.0, latent_bias: float = 0.0,
-                 use_graph: bool = True, groups: int = 1):
+                 use_graph: bool = True, groups: int = 1, cfg_strength: float = 0.0,
+                 sway_coeff: float = 0.0):
         super().__init__()
         self.lm, self.dit = lm, dit
         self.batch = batch
         c = _lib.EngineConfigC(batch, capacity, euler_steps, latent_scale, latent_bias, int(use_graph),
-                               groups)
+                               groups, cfg_strength, sway_coeff)
         check(_lib.load().ctts_engine_create(lm.h, dit.h, C.byref(c), C.byref(self.h)))
         sw, sb = _f(heads["stop_predictor.weight"]), _f(heads["stop_predictor.bias"])
         pw, pb = _f(heads["latent_proj.weight"]), _f(heads["latent_proj.bias"])
@@ -270,6 +271,11 @@ class FrameEngine(_Handle):
     def prefill(self, b: int, x, cond0) -> None:
         x, cond0 = _f(x), _f(cond0)
         check(_lib.load().ctts_engine_prefill(self.h, b, _p(x), x.shape[0], _p(cond0)))
+
+    def prefill_uncond(self, b: int, x, cond0) -> None:
+        """CFG mode: the unconditional branch of utterance b."""
+        x, cond0 = _f(x), _f(cond0)
+        check(_lib.load().ctts_engine_prefill_uncond(self.h, b, _p(x), x.shape[0], _p(cond0)))
 
     def step(self, noise):
         noise = _f(noise).reshape(self.batch, self.pl)

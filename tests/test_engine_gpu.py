@@ -200,3 +200,49 @@ def test_cluster_dit_path_is_one_launch(monkeypatch):
     for f in range(2):
         for b in range(B):
             assert cosine(res["1"][0][f, b], res["0"][0][f, b]) >= 0.9999, (f, b)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_cfg_frames_vs_oracle(dtype):
+    """Base-variant CFG frames (bin/cutetts.rs:440-456, 474-509): an
+    unconditional LM branch per utterance with its own KV cache, fed the
+    same latent; the DiT runs euler_sample_cfg on the sway grid with the
+    unconditional rows' AdaLN zeroed.  Against the oracle's composition of
+    the same loop."""
+    from rcutetts_b200.model import DitW, FrameEngine, QwenW
+
+    lcfg, dcfg = LMConfig(n_layers=2), DiTConfig(n_layers=2)
+    lw = synth.lm_weights(lcfg, seed=31, with_embed=False)
+    dw = synth.dit_weights(dcfg, seed=32)
+    hw = synth.frame_weights(lcfg.hidden, dcfg.latent, seed=33)
+    lm = QwenW(lcfg, dtype).set_weights(lw)
+    dit = DitW(dcfg, dtype).set_weights(dw)
+    B, F, cfg_s, coeff = 2, 3, 2.0, -1.0
+    eng = FrameEngine(lm, dit, hw, batch=B, capacity=48, euler_steps=10, cfg_strength=cfg_s, sway_coeff=coeff)
+    pres_c = [rnd(40 + b, (6 + 3 * b, lcfg.hidden)) for b in range(B)]
+    pres_u = [rnd(50 + b, (2 + b, lcfg.hidden)) for b in range(B)]
+    conds = [rnd(60 + b, (64,)) for b in range(B)]
+    unconds = [rnd(70 + b, (64,)) for b in range(B)]
+    for b in range(B):
+        eng.prefill(b, pres_c[b], conds[b])
+        eng.prefill_uncond(b, pres_u[b], unconds[b])
+    noise = rnd(80, (F, B, 64))
+    lat = np.stack([eng.step(noise[f])[0] for f in range(F)])
+    lwo, dwo = (bf16_weights(lw), bf16_weights(dw)) if dtype == "bf16" else (lw, dw)
+    lm_o, dit_o = orc.LM(lcfg, lwo), orc.DiT(dcfg, dwo)
+    for b in range(B):
+        cc, cu = lm_o.new_cache(48), lm_o.new_cache(48)
+        zc = lm_o.forward(pres_c[b], cc)[-1].copy()
+        zu = lm_o.forward(pres_u[b], cu)[-1].copy()
+        cond, uncond = conds[b], unconds[b]
+        for f in range(F):
+            x = dit_o.euler_sample_cfg(noise[f, b], zc, zu, cond, uncond, zc, 10, coeff, cfg_s)
+            if dtype == "f32":
+                assert rel_err(lat[f, b], x) < 1e-4, (b, f)
+            else:
+                assert cosine(lat[f, b], x) >= 0.999, (b, f)
+            x = lat[f, b] if dtype == "bf16" else x  # bf16: follow the device trajectory
+            cond = uncond = x
+            fb = orc.linear(x[None], hw["latent_proj.weight"], hw["latent_proj.bias"])
+            zc = lm_o.forward(fb, cc)[0].copy()
+            zu = lm_o.forward(fb, cu)[0].copy()
