@@ -386,7 +386,9 @@ __global__ void __launch_bounds__(128) attn_step_kernel(const AttnArgs a) {
 // utterance) walks the utterance's keys in 128-key stages through a
 // two-stage ring of bulk copies (the copy of stage s+2 is issued as soon as
 // stage s is consumed) with an online softmax, so there is no split merge
-// and the grid is one wave.  The new key/value row is kept in shared memory
+// and the grid is one wave.  Each warp owns 16 keys of every stage and keeps
+// its own softmax state in registers (one block barrier per stage); the 8
+// warp states merge once at the end, in warp order.  The new key/value row is kept in shared memory
 // and placed into its stage's tile once that stage's copy has landed.
 // grid (nkv, batch), 256 threads, dynamic smem 2 stages x (K, V) x 128 rows.
 template <bool BF, int HD>
@@ -396,18 +398,15 @@ __global__ void __launch_bounds__(256) attn_loop_kernel(const AttnArgs a) {
   constexpr int NC = ROWB / 16;
   constexpr int VPC = 16 / ES;
   constexpr int PER = HD / 32;
-  constexpr int HP = HD / 2;
   constexpr int C = 128;             // keys per stage
   constexpr int NT = 256;
-  constexpr int PARTS = NT / HP;     // key partitions of the P.V pass
   constexpr int NW = NT / 32;
+  constexpr int KPW = C / NW;        // keys of a stage per warp (2 threads per key)
+  constexpr int DPL = HD / 32;       // V dims per lane in the P.V pass
   extern __shared__ __align__(128) uint8_t kv_smem[];  // [2][K|V][C][ROWB]
   __shared__ __align__(16) float qs[kMaxG][HD];
-  __shared__ float ps[kMaxG][C];
-  __shared__ float red[kMaxG][NW];
-  __shared__ float mrun[kMaxG], lrun[kMaxG], fac[kMaxG];
   __shared__ __align__(16) uint8_t newrow[2][ROWB];  // new K, V row in the cache type
-  __shared__ __align__(16) float accs[PARTS][kMaxG][HD];
+  __shared__ float wpart[NW][kMaxG][HD + 2];         // per-warp [m, l, acc[HD]]
   __shared__ __align__(8) uint64_t bars[2];
 
   const int kh = blockIdx.x, b = blockIdx.y;
@@ -503,16 +502,19 @@ __global__ void __launch_bounds__(256) attn_loop_kernel(const AttnArgs a) {
       }
     }
   }
-  if (tid < kMaxG) {
-    mrun[tid] = -INFINITY;
-    lrun[tid] = 0.0f;
-  }
-  __syncthreads();  // queries, the new row and the running statistics are set
+  __syncthreads();  // queries and the new row are set
   const float scale = 1.0f / sqrtf((float)HD);
-  const int dp = tid % HP, pp = tid / HP;
-  float acc[kMaxG][2];
+  // Every warp runs its own online softmax over its 16 keys of each stage
+  // (no block-wide reduction per stage); the 8 warp states merge at the end
+  // in warp order (deterministic).
+  float m_w[kMaxG], l_w[kMaxG], acc[kMaxG][DPL];
 #pragma unroll
-  for (int g = 0; g < kMaxG; g++) acc[g][0] = acc[g][1] = 0.0f;
+  for (int g = 0; g < kMaxG; g++) {
+    m_w[g] = -INFINITY;
+    l_w[g] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < DPL; e++) acc[g][e] = 0.0f;
+  }
   bool ok = true;
   for (int st = 0; st < nst; st++) {
     const int buf = st & 1;
@@ -541,15 +543,19 @@ __global__ void __launch_bounds__(256) attn_loop_kernel(const AttnArgs a) {
     }
     __syncthreads();
     // scores: two threads per key, each half of the 16-byte chunks
-    const int key = tid >> 1, half = tid & 1;
+    const int kbase = warp * KPW;
+    const int key = kbase + (lane >> 1), half = lane & 1;
+    const bool valid = key < rows;
     float sc[kMaxG];
 #pragma unroll
     for (int g = 0; g < kMaxG; g++) sc[g] = 0.0f;
-    if (key < rows) {
+    if (valid) {
       const uint8_t* krow = Ks + (size_t)key * ROWB;
 #pragma unroll
       for (int cc = 0; cc < NC / 2; cc++) {
-        const int c = half * (NC / 2) + (cc + key) % (NC / 2);
+        // rotated per key and half: the 8 lanes of a 16-byte access phase
+        // hit 8 different bank groups
+        const int c = half * (NC / 2) + (cc + key + half * 4) % (NC / 2);
         const uint4 t = *reinterpret_cast<const uint4*>(krow + c * 16);
         float kv[VPC];
         if constexpr (BF) {
@@ -568,84 +574,85 @@ __global__ void __launch_bounds__(256) attn_loop_kernel(const AttnArgs a) {
         }
       }
     }
+    float pr[kMaxG];
 #pragma unroll
     for (int g = 0; g < kMaxG; g++) {
       if (g >= G) break;
       sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], 1);
-      sc[g] = key < rows ? sc[g] * scale : -INFINITY;
-      const float m = warp_max(sc[g]);
-      if (lane == 0) red[g][warp] = m;
-    }
-    __syncthreads();
-    if (tid < G) {
-      float m = red[tid][0];
+      sc[g] = valid ? sc[g] * scale : -INFINITY;
+      const float mn = fmaxf(m_w[g], warp_max(sc[g]));
+      const float f = m_w[g] == -INFINITY ? 0.0f : expf(m_w[g] - mn);
+      pr[g] = valid ? expf(sc[g] - mn) : 0.0f;
+      l_w[g] = l_w[g] * f + warp_sum(half == 0 ? pr[g] : 0.0f);
 #pragma unroll
-      for (int w = 1; w < NW; w++) m = fmaxf(m, red[tid][w]);
-      const float mn = fmaxf(mrun[tid], m);
-      fac[tid] = expf(mrun[tid] - mn);  // 0 on the first stage
-      mrun[tid] = mn;
+      for (int e = 0; e < DPL; e++) acc[g][e] *= f;
+      m_w[g] = mn;
     }
-    __syncthreads();
-#pragma unroll
-    for (int g = 0; g < kMaxG; g++) {
-      if (g >= G) break;
-      const float p = key < rows ? expf(sc[g] - mrun[g]) : 0.0f;
-      if (half == 0) ps[g][key] = p;
-      const float l = warp_sum(half == 0 ? p : 0.0f);
-      if (lane == 0) red[g][warp] = l;
-    }
-    __syncthreads();
-    if (tid < G) {
-      float l = 0.0f;
-#pragma unroll
-      for (int w = 0; w < NW; w++) l += red[tid][w];
-      lrun[tid] = lrun[tid] * fac[tid] + l;
-    }
-    // P.V of this stage, rescaled running accumulators
-#pragma unroll
-    for (int g = 0; g < kMaxG; g++) {
-      if (g >= G) break;
-      acc[g][0] *= fac[g];
-      acc[g][1] *= fac[g];
-    }
-    for (int j = pp; j < rows; j += PARTS) {
-      float v0, v1;
+    // P.V over the warp's keys: lane owns dims [lane*DPL, +DPL)
+    const int nk = min(KPW, rows - kbase);
+#pragma unroll 4
+    for (int kk = 0; kk < KPW; kk++) {
+      if (kk >= nk) break;
+      const uint8_t* vrow = Vs + (size_t)(kbase + kk) * ROWB;
+      float v[DPL];
       if constexpr (BF) {
-        const uint32_t t = reinterpret_cast<const uint32_t*>(Vs + (size_t)j * ROWB)[dp];
-        v0 = bf_lo(t);
-        v1 = bf_hi(t);
+        if constexpr (DPL == 2) {
+          const uint32_t t = reinterpret_cast<const uint32_t*>(vrow)[lane];
+          v[0] = bf_lo(t);
+          v[1] = bf_hi(t);
+        } else {
+          const uint2 t = reinterpret_cast<const uint2*>(vrow)[lane];
+          v[0] = bf_lo(t.x); v[1] = bf_hi(t.x); v[2] = bf_lo(t.y); v[3] = bf_hi(t.y);
+        }
       } else {
-        const float2 t = reinterpret_cast<const float2*>(Vs + (size_t)j * ROWB)[dp];
-        v0 = t.x;
-        v1 = t.y;
+        if constexpr (DPL == 2) {
+          const float2 t = reinterpret_cast<const float2*>(vrow)[lane];
+          v[0] = t.x;
+          v[1] = t.y;
+        } else {
+          const float4 t = reinterpret_cast<const float4*>(vrow)[lane];
+          v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+        }
       }
 #pragma unroll
       for (int g = 0; g < kMaxG; g++) {
         if (g >= G) break;
-        const float p = ps[g][j];
-        acc[g][0] = fmaf(p, v0, acc[g][0]);
-        acc[g][1] = fmaf(p, v1, acc[g][1]);
+        const float pk = __shfl_sync(0xffffffffu, pr[g], 2 * kk);
+#pragma unroll
+        for (int e = 0; e < DPL; e++) acc[g][e] = fmaf(pk, v[e], acc[g][e]);
       }
     }
-    __syncthreads();  // stage buffer and ps consumed
+    __syncthreads();  // stage buffer consumed by every warp
     if (tid == 0 && st + 2 < nst) issue(st + 2);
   }
   if (!ok && a.err && tid == 0) atomicExch(a.err, 3);
   if (bad) return;
-  // partitions summed in order
+  // merge the warp states in warp order
 #pragma unroll
   for (int g = 0; g < kMaxG; g++) {
     if (g >= G) break;
-    accs[pp][g][2 * dp] = acc[g][0];
-    accs[pp][g][2 * dp + 1] = acc[g][1];
+    if (lane == 0) {
+      wpart[warp][g][0] = m_w[g];
+      wpart[warp][g][1] = l_w[g];
+    }
+#pragma unroll
+    for (int e = 0; e < DPL; e++) wpart[warp][g][2 + lane * DPL + e] = acc[g][e];
   }
   __syncthreads();
   for (int i = tid; i < G * HD; i += NT) {
     const int g = i / HD, d = i % HD, h = kh * G + g;
-    float t = 0.0f;
+    float M = -INFINITY;
 #pragma unroll
-    for (int q = 0; q < PARTS; q++) t += accs[q][g][d];
-    const float o = t / lrun[g];
+    for (int w = 0; w < NW; w++) M = fmaxf(M, wpart[w][g][0]);
+    float L = 0.0f, o = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; w++) {
+      const float mw = wpart[w][g][0];
+      const float f = mw == -INFINITY ? 0.0f : expf(mw - M);
+      L = fmaf(wpart[w][g][1], f, L);
+      o = fmaf(wpart[w][g][2 + d], f, o);
+    }
+    o = o / L;
     const size_t oi = (size_t)b * nq * HD + (size_t)h * HD + d;
     if (a.out_b)
       a.out_b[oi] = f2bf(o);

@@ -36,17 +36,21 @@ namespace {
 // Optional phase timeline (build with -DCTTS_TC_TRACE): thread 0 of the
 // first CTA of the grid records (event, %globaltimer) pairs per launch.
 #ifdef CTTS_TC_TRACE
+// Consecutive launches overlap (programmatic dependent launch), so slots are
+// taken atomically and each event carries its launch number: (launch << 8) | ev.
 __device__ long long g_tc_trace[4096];
 __device__ int g_tc_trace_n;
+__device__ int g_tc_launch;
 CTTS_DEV void tc_trace(int ev) {
   if (blockIdx.x != 0 || blockIdx.y != 0 || threadIdx.x != 0) return;
+  __shared__ int lid;
+  if (ev == 0) lid = atomicAdd(&g_tc_launch, 1);
   long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  const int n = g_tc_trace_n;
+  const int n = atomicAdd(&g_tc_trace_n, 1);
   if (n < 2047) {
-    g_tc_trace[2 * n] = ev;
+    g_tc_trace[2 * n] = ((long long)lid << 8) | ev;
     g_tc_trace[2 * n + 1] = t;
-    g_tc_trace_n = n + 1;
   }
 }
 #define TC_TRACE(ev) tc_trace(ev)
@@ -531,8 +535,10 @@ cudaError_t launch_tc_linear(const TcCall& c, cudaStream_t s) {
 // Copies the recorded timeline out and resets it.
 extern "C" __attribute__((visibility("default"))) int ctts_tc_trace(long long* out, int* n) {
   cudaMemcpyFromSymbol(n, ctts::g_tc_trace_n, sizeof(int));
+  if (*n > 2047) *n = 2047;
   cudaMemcpyFromSymbol(out, ctts::g_tc_trace, sizeof(long long) * 4096);
   int z = 0;
+  cudaMemcpyToSymbol(ctts::g_tc_launch, &z, sizeof(int));
   return cudaMemcpyToSymbol(ctts::g_tc_trace_n, &z, sizeof(int)) == cudaSuccess ? 0 : -2;
 }
 #endif
