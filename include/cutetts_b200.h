@@ -202,7 +202,10 @@ CTTS_API void ctts_engine_free(ctts_engine* e);
 
 /* ------------------------------------------------------ VAE decoder
  * Replaces rust-codec/src/decode.rs:decode_nth (94-136), weights.rs
- * load_decoder_weights (98-186) at generic topology. */
+ * load_decoder_weights (98-186) at generic shapes, dense (depthwise = 0,
+ * audio_vae.py CausalDecoder(depthwise=False)) or the shipped depthwise
+ * topology (depthwise = 1: depthwise k7 + pointwise front, depthwise
+ * dilated k7 in every residual unit; decode.rs:97-128). */
 typedef struct {
   int latent, channels, n_stages, depthwise;
   int strides[8];
@@ -300,6 +303,14 @@ CTTS_API int ctts_op_rope(float* x, int M, int heads, int head_dim, const int* p
                  void* stream);
 /* out[M,F] = silu(gu[M, 0:F]) * gu[M, F:2F] */
 CTTS_API int ctts_op_swiglu(const float* gu, int M, int F, float* out, void* stream);
+/* Causal Conv1d, stride 1 (rust-codec/src/conv.rs:36-51 causal_conv1d):
+ * x [batch, c_in, T] -> y [batch, c_out, T], w [c_out, c_in/groups, k]
+ * (weight norm already fused), bias [c_out] or NULL, left pad 2*pad
+ * (the module's padding argument, audio_vae.py CausalConv1d).  groups is 1
+ * (dense) or c_in == c_out (depthwise); other groupings return CTTS_ERR_ARG. */
+CTTS_API int ctts_op_causal_conv1d(const float* x, int batch, int c_in, int T, const void* w, int w_dtype,
+                                   const float* bias, int c_out, int k, int dilation, int groups, int pad,
+                                   float* y, void* stream);
 /* out[n, H] = table[ids[n], :]; ids validated on device, *bad_count (device
  * int, may be NULL) receives the number of out-of-range ids (rows zeroed). */
 CTTS_API int ctts_op_embed_gather(const float* table, int vocab, int H, const int64_t* ids, int n,

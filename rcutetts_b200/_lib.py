@@ -117,6 +117,8 @@ SIGNATURES = {
                                          vp]),
     "ctts_op_rope": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, vp, C.c_float, vp]),
     "ctts_op_swiglu": (C.c_int, [vp, C.c_int, C.c_int, vp, vp]),
+    "ctts_op_causal_conv1d": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, vp, C.c_int, vp, C.c_int, C.c_int,
+                                        C.c_int, C.c_int, C.c_int, vp, vp]),
     "ctts_op_embed_gather": (C.c_int, [vp, C.c_int, C.c_int, vp, C.c_int, vp, vp, vp]),
 }
 

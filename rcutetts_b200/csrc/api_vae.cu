@@ -57,7 +57,6 @@ extern "C" int ctts_vae_create(const ctts_vae_config* cfg, int device, ctts_vae*
   const ctts_vae_config& c = *cfg;
   CTTS_REQ(c.latent > 0 && c.channels > 0 && c.n_stages > 0 && c.n_stages <= 8, CTTS_ERR_ARG, "bad dims");
   CTTS_REQ(c.weight_dtype == CTTS_F32 || c.weight_dtype == CTTS_BF16, CTTS_ERR_ARG, "bad weight dtype");
-  CTTS_REQ(!c.depthwise, CTTS_ERR_ARG, "depthwise decoder topology is not supported by this build");
   for (int i = 0; i < c.n_stages; i++) CTTS_REQ(c.strides[i] > 0, CTTS_ERR_ARG, "bad stride");
   CTTS_REQ((c.channels >> c.n_stages) > 0 && ((c.channels >> c.n_stages) << c.n_stages) == c.channels,
            CTTS_ERR_ARG, "channels must halve cleanly per stage");
@@ -78,8 +77,17 @@ extern "C" int ctts_vae_create(const ctts_vae_config* cfg, int device, ctts_vae*
     v->slots.add(p + ".bias", *b, {o}, false);
   };
   const int C = c.channels, L = c.latent;
-  conv("model.0", &v->front_w, &v->front_b, C, L, 7);
+  // dense: model.0 = Conv(latent -> channels, k7); depthwise (the shipped
+  // topology, audio_vae.py:255-266): model.0 = depthwise k7 on the latent,
+  // model.1 = pointwise latent -> channels (weights.rs:115-121)
   int idx = 1;
+  if (c.depthwise) {
+    conv("model.0", &v->front_w, &v->front_b, L, 1, 7);
+    conv("model.1", &v->front_pw_w, &v->front_pw_b, C, L, 1);
+    idx = 2;
+  } else {
+    conv("model.0", &v->front_w, &v->front_b, C, L, 7);
+  }
   v->hop = 1;
   v->stages.resize(c.n_stages);
   for (int si = 0; si < c.n_stages; si++) {
@@ -107,7 +115,7 @@ extern "C" int ctts_vae_create(const ctts_vae_config* cfg, int device, ctts_vae*
       R.a1 = A.alloc<float>(st.cout);
       v->slots.add(rb + "0.alpha", R.a0, {1, st.cout, 1}, false);
       v->slots.add(rb + "2.alpha", R.a1, {1, st.cout, 1}, false);
-      conv(rb + "1", &R.w0, &R.b0, st.cout, st.cout, 7);
+      conv(rb + "1", &R.w0, &R.b0, st.cout, c.depthwise ? 1 : st.cout, 7);  // depthwise: [C, 1, 7]
       conv(rb + "3", &R.w1, &R.b1, st.cout, st.cout, 1);
     }
   }
@@ -195,7 +203,7 @@ namespace {
 int vae_ws_ensure(ctts_vae* v, int B, int T) {
   size_t need = 0;
   int t = T;
-  need = std::max(need, (size_t)v->cfg.channels * t);
+  need = std::max(need, (size_t)std::max(v->cfg.channels, v->cfg.latent) * t);
   for (auto& st : v->stages) {
     t *= st.stride;
     need = std::max(need, (size_t)st.cout * t);
@@ -221,11 +229,18 @@ int vae_enqueue(ctts_vae* v, int B, const float* lat, int T, float* wav, cudaStr
   float* h = v->buf[0];
   float* h2 = v->buf[1];
   float* r = v->buf[2];
+  const int dw = v->cfg.depthwise;
   ConvArgs a;
-  a.x = lat; a.w = v->front_w; a.w_bf16 = bf; a.bias = v->front_b; a.y = h;
-  a.B = B; a.Cin = v->cfg.latent; a.Cout = v->cfg.channels; a.Tin = T; a.Tout = T; a.k = 7; a.dil = 1;
-  a.left = 6;
+  a.x = lat; a.w = v->front_w; a.w_bf16 = bf; a.bias = v->front_b; a.y = dw ? r : h;
+  a.B = B; a.Cin = v->cfg.latent; a.Cout = dw ? v->cfg.latent : v->cfg.channels; a.Tin = T; a.Tout = T; a.k = 7;
+  a.dil = 1; a.left = 6; a.groups = dw ? v->cfg.latent : 1;
   CTTS_CK(launch_conv1d(a, s));
+  if (dw) {  // pointwise latent -> channels
+    ConvArgs p;
+    p.x = r; p.w = v->front_pw_w; p.w_bf16 = bf; p.bias = v->front_pw_b; p.y = h;
+    p.B = B; p.Cin = v->cfg.latent; p.Cout = v->cfg.channels; p.Tin = T; p.Tout = T; p.k = 1; p.dil = 1; p.left = 0;
+    CTTS_CK(launch_conv1d(p, s));
+  }
   int t = T;
   static const int dils[3] = {1, 3, 9};
   for (auto& st : v->stages) {
@@ -241,7 +256,7 @@ int vae_enqueue(ctts_vae* v, int B, const float* lat, int T, float* wav, cudaStr
       ConvArgs c7;
       c7.x = h; c7.w = R.w0; c7.w_bf16 = bf; c7.bias = R.b0; c7.y = r; c7.snake_alpha = R.a0;
       c7.B = B; c7.Cin = st.cout; c7.Cout = st.cout; c7.Tin = t; c7.Tout = t; c7.k = 7;
-      c7.dil = dils[ri]; c7.left = 6 * dils[ri];
+      c7.dil = dils[ri]; c7.left = 6 * dils[ri]; c7.groups = dw ? st.cout : 1;
       CTTS_CK(launch_conv1d(c7, s));
       ConvArgs c1;
       c1.x = r; c1.w = R.w1; c1.w_bf16 = bf; c1.bias = R.b1; c1.y = h; c1.res = h; c1.snake_alpha = R.a1;
@@ -292,6 +307,22 @@ extern "C" int ctts_vae_decode_batch(ctts_vae* v, int batch, const float* latent
   return CTTS_OK;
 }
 
+extern "C" int ctts_op_causal_conv1d(const float* x, int batch, int c_in, int T, const void* w, int w_dtype,
+                                     const float* bias, int c_out, int k, int dilation, int groups, int pad,
+                                     float* y, void* stream) {
+  CTTS_REQ(x && w && y && batch > 0 && c_in > 0 && c_out > 0 && T > 0 && k > 0 && dilation > 0 && pad >= 0,
+           CTTS_ERR_ARG, "bad argument");
+  CTTS_REQ(w_dtype == CTTS_F32 || w_dtype == CTTS_BF16, CTTS_ERR_ARG, "bad weight dtype");
+  CTTS_REQ(groups == 1 || (groups == c_in && c_in == c_out), CTTS_ERR_ARG,
+           "groups must be 1 or c_in == c_out (depthwise)");
+  ConvArgs a;
+  a.x = x; a.w = w; a.w_bf16 = w_dtype == CTTS_BF16; a.bias = bias; a.y = y;
+  a.B = batch; a.Cin = c_in; a.Cout = c_out; a.Tin = T; a.Tout = T; a.k = k; a.dil = dilation;
+  a.left = 2 * pad; a.groups = groups;
+  CTTS_CK(launch_conv1d(a, as_stream(stream, nullptr)));
+  return CTTS_OK;
+}
+
 // ----------------------------------------------- reference ffi.rs signatures
 
 extern "C" void* cutetts_vae_load(const char* path) {
@@ -305,15 +336,26 @@ extern "C" void* cutetts_vae_load(const char* path) {
     return it->second.shape;
   };
   ctts_vae_config c{};
-  std::vector<int64_t> s0 = shape_of("model.0.weight_v");
-  if (s0.empty()) s0 = shape_of("model.0.weight");
-  if (s0.size() != 3 || s0[1] == 1) return nullptr;  // depthwise front not supported
-  c.channels = (int)s0[0];
-  c.latent = (int)s0[1];
+  auto wshape = [&](const std::string& n) {
+    std::vector<int64_t> r = shape_of(n + ".weight_v");
+    return r.empty() ? shape_of(n + ".weight") : r;
+  };
+  std::vector<int64_t> s0 = wshape("model.0");
+  if (s0.size() != 3) return nullptr;
+  int base = 1;
+  if (s0[1] == 1) {  // depthwise front [latent, 1, 7] + pointwise [channels, latent, 1]
+    std::vector<int64_t> s1 = wshape("model.1");
+    if (s1.size() != 3 || s1[1] != s0[0] || s1[2] != 1) return nullptr;
+    c.depthwise = 1;
+    c.latent = (int)s0[0];
+    c.channels = (int)s1[0];
+    base = 2;
+  } else {
+    c.channels = (int)s0[0];
+    c.latent = (int)s0[1];
+  }
   for (int si = 0; si < 8; si++) {
-    std::string b = "model." + std::to_string(1 + si) + ".block.1.weight";
-    std::vector<int64_t> st = shape_of(b + "_v");
-    if (st.empty()) st = shape_of(b);
+    std::vector<int64_t> st = wshape("model." + std::to_string(base + si) + ".block.1");
     if (st.size() != 3) break;
     c.strides[si] = (int)st[2] / 2;
     c.n_stages = si + 1;

@@ -44,7 +44,7 @@ int stream_ws_ensure(ctts_vae_stream* st, int frames) {
   if (frames <= st->cap_frames) return CTTS_OK;
   ctts_vae* v = st->v;
   const int B = st->batch;
-  size_t act = (size_t)v->cfg.channels * frames, ext = (size_t)v->cfg.latent * (frames + 6);
+  size_t act = (size_t)std::max(v->cfg.channels, v->cfg.latent) * frames, ext = (size_t)v->cfg.latent * (frames + 6);
   int t = frames;
   ext = std::max(ext, (size_t)v->cfg.channels * (t + 1));
   for (auto& s : v->stages) {
@@ -94,11 +94,19 @@ int stream_enqueue(ctts_vae_stream* st, const float* lat, int T, float* wav, cud
   float* r = st->r;
   size_t hi = 0;
   int rc;
+  const int dw = v->cfg.depthwise;
   {
     ConvArgs a;
-    a.w = v->front_w; a.w_bf16 = bf; a.bias = v->front_b; a.y = h;
-    a.B = B; a.Cin = v->cfg.latent; a.Cout = v->cfg.channels; a.k = 7; a.dil = 1; a.left = 6;
+    a.w = v->front_w; a.w_bf16 = bf; a.bias = v->front_b; a.y = dw ? r : h;
+    a.B = B; a.Cin = v->cfg.latent; a.Cout = dw ? v->cfg.latent : v->cfg.channels; a.k = 7; a.dil = 1; a.left = 6;
+    a.groups = dw ? v->cfg.latent : 1;
     if ((rc = conv_streamed(st, hi++, a, lat, T, s, false))) return rc;
+  }
+  if (dw) {  // pointwise latent -> channels: no context
+    ConvArgs p;
+    p.x = r; p.w = v->front_pw_w; p.w_bf16 = bf; p.bias = v->front_pw_b; p.y = h;
+    p.B = B; p.Cin = v->cfg.latent; p.Cout = v->cfg.channels; p.Tin = T; p.Tout = T; p.k = 1; p.dil = 1; p.left = 0;
+    CTTS_CK(launch_conv1d(p, s));
   }
   int t = T;
   static const int dils[3] = {1, 3, 9};
@@ -114,6 +122,7 @@ int stream_enqueue(ctts_vae_stream* st, const float* lat, int T, float* wav, cud
       ConvArgs c7;
       c7.w = R.w0; c7.w_bf16 = bf; c7.bias = R.b0; c7.y = r; c7.snake_alpha = R.a0;
       c7.B = B; c7.Cin = sg.cout; c7.Cout = sg.cout; c7.k = 7; c7.dil = dils[ri]; c7.left = 6 * dils[ri];
+      c7.groups = dw ? sg.cout : 1;
       if ((rc = conv_streamed(st, hi++, c7, h, t, s, false))) return rc;
       ConvArgs c1;  // pointwise: no context
       c1.x = r; c1.w = R.w1; c1.w_bf16 = bf; c1.bias = R.b1; c1.y = h; c1.res = h; c1.snake_alpha = R.a1;

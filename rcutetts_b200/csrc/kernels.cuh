@@ -164,6 +164,7 @@ struct ConvArgs {
   const float* snake_alpha = nullptr;  // Snake applied to x on load (per Cin) or null
   int B = 0, Cin = 0, Cout = 0, Tin = 0, Tout = 0, k = 1, dil = 1, left = 0;
   int stride = 1;   // transposed conv stride
+  int groups = 1;   // 1 (dense) or Cin == Cout (depthwise); conv1d only
   int tanh_out = 0;
   int xoff = 0;     // output position t reads input position t + xoff + j*dil - left
                     // (streaming: the input carries xoff history columns)

@@ -2,7 +2,7 @@
 // decoder (audio_vae.py:43-62,73-79; rust-codec/src/conv.rs, snake.rs,
 // decode.rs).
 //
-// Both convolutions run as an implicit GEMM on CUDA cores:
+// Dense convolutions run as an implicit GEMM on CUDA cores:
 //   y[o, t] = bias[o] + sum_{c, j} W[o, c*k + j] * snake(x[c, t + j*dil - left])
 // The Snake activation of the *input* is applied while the activation tile
 // is staged into shared memory (the reference runs it as a separate pass,
@@ -10,7 +10,9 @@
 // epilogue.  A transposed conv with kernel 2s and stride s is s such
 // convolutions with k = 2, dilation 1, left pad 1 on repacked weights, each
 // writing every s-th output sample (the two-GEMM decomposition of
-// decode.rs:39-80 / weights.rs:133-147).
+// decode.rs:39-80 / weights.rs:133-147).  Depthwise convolutions (the
+// shipped topology's front conv and residual k7 convs) run as a
+// per-channel stencil over a shared-memory window.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -105,6 +107,53 @@ __global__ void __launch_bounds__(256) conv_kernel(const ConvArgs a, int Tc, int
   }
 }
 
+// Depthwise causal conv (groups == Cin == Cout: conv.rs:53-117 with one
+// input channel per group; audio_vae.py CausalResidualUnit with
+// groups = dim):
+//   y[c, t] = bias[c] + sum_j w[c, j] * snake(x[c, t + xoff + j*dil - left])
+// One CTA per (position block, channel, utterance); the input window of the
+// block, Snake applied once per sample, is staged in shared memory.  Memory
+// bound: every input sample is read once per block, every output written once.
+constexpr int kDwT = 1024;  // output positions per CTA
+constexpr int kDwMaxK = 16;
+
+template <bool BF>
+__global__ void __launch_bounds__(256) dw_conv_kernel(const ConvArgs a) {
+  extern __shared__ float xw[];  // [kDwT + (k-1)*dil]
+  grid_dep_enter();
+  const int c = blockIdx.y, b = blockIdx.z, t0 = blockIdx.x * kDwT;
+  const int k = a.k, dil = a.dil, span = (k - 1) * dil;
+  const float* xr = a.x + ((size_t)b * a.Cin + c) * a.Tin;
+  const float al = a.snake_alpha ? a.snake_alpha[c] : 0.0f;
+  // xw[i] holds input position t0 + i + xoff - left
+  for (int i = threadIdx.x; i < kDwT + span; i += blockDim.x) {
+    const int src = t0 + i + a.xoff - a.left;
+    float v = 0.0f;
+    if (src >= 0 && src < a.Tin) {
+      v = xr[src];
+      if (a.snake_alpha) v = snake1(v, al);
+    }
+    xw[i] = v;
+  }
+  float w[kDwMaxK];
+#pragma unroll
+  for (int j = 0; j < kDwMaxK; j++) w[j] = j < k ? ldw<BF>(a.w, (size_t)c * k + j) : 0.0f;
+  const float bo = a.bias ? a.bias[c] : 0.0f;
+  __syncthreads();
+  const size_t orow = ((size_t)b * a.Cout + c) * a.Tout;
+  for (int i = threadIdx.x; i < kDwT; i += blockDim.x) {
+    const int t = t0 + i;
+    if (t >= a.Tout) break;
+    float acc = bo;
+#pragma unroll
+    for (int j = 0; j < kDwMaxK; j++)
+      if (j < k) acc = fmaf(xw[i + j * dil], w[j], acc);
+    if (a.res) acc += a.res[orow + t];
+    if (a.tanh_out) acc = tanhf(acc);
+    a.y[orow + t] = acc;
+  }
+}
+
 __global__ void snake_kernel(const float* x, int C, int T, const float* alpha, float* y,
                              size_t n) {
   grid_dep_enter();
@@ -118,6 +167,17 @@ __global__ void snake_kernel(const float* x, int C, int T, const float* alpha, f
 
 cudaError_t launch_conv1d(const ConvArgs& a, cudaStream_t s) {
   if (a.Tout + a.xoff != a.Tin || a.xoff < 0) return cudaErrorInvalidValue;
+  if (a.groups != 1) {  // depthwise
+    if (a.groups != a.Cin || a.Cin != a.Cout || a.k < 1 || a.k > kDwMaxK || a.dil < 1) return cudaErrorInvalidValue;
+    const size_t smem = sizeof(float) * (size_t)(kDwT + (a.k - 1) * a.dil);
+    if (smem > 48 * 1024) return cudaErrorInvalidValue;
+    dim3 grid((a.Tout + kDwT - 1) / kDwT, a.Cout, a.B);
+    if (a.w_bf16)
+      CTTS_LK(launch_k(dw_conv_kernel<true>, grid, dim3(256), smem, s, a));
+    else
+      CTTS_LK(launch_k(dw_conv_kernel<false>, grid, dim3(256), smem, s, a));
+    return cudaGetLastError();
+  }
   dim3 grid((a.Tout + TT - 1) / TT, (a.Cout + TO - 1) / TO, a.B);
   if (a.w_bf16)
     CTTS_LK(launch_k(conv_kernel<true>, dim3(grid), dim3(256), 0, s, a, a.Tout, 1, 1, 0));

@@ -125,12 +125,20 @@ def frame_weights(lm_hidden: int, latent: int, seed: int) -> dict:
     }
 
 
-def vae_weights(cfg: VAEConfig, seed: int) -> dict:
+def vae_weights(cfg: VAEConfig, seed: int, fan_in: float = 0.0) -> dict:
     """CausalDecoder tensors with weight norm already fused (`.weight`),
     names without the `decoder.` prefix.  Biases are zero, as the
-    reference's init_weights (audio_vae.py:90-95) leaves them."""
+    reference's init_weights (audio_vae.py:90-95) leaves them.  fan_in > 0
+    draws every conv weight with std fan_in / sqrt(in_per_group * k) instead
+    of the fixed init std, so the signal keeps its scale through deep
+    (depthwise) stacks."""
     rng = np.random.default_rng(seed)
     C, L = cfg.channels, cfg.latent
+
+    def _normal(rng, shape):
+        std = fan_in / np.sqrt(shape[1] * shape[2]) if fan_in > 0 else STD
+        return (rng.standard_normal(shape, dtype=np.float32) * np.float32(std)).astype(np.float32)
+
     w = {}
     idx = 0
     if cfg.depthwise:

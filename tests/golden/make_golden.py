@@ -251,11 +251,34 @@ def main(root):
         print(k, v)
 
 
+VAE_DW_GAIN = 0.8  # fan-in weight scale: waveform std well inside tanh's range
+VAE_DW_SMALL = VAEConfig(latent=64, channels=96, strides=(4, 3, 2), depthwise=True)
+VAE_DW_SHIPPED = VAEConfig(latent=64, channels=1536, strides=(16, 8, 5, 3), depthwise=True)
+
+
+def make_vae_dw(root):
+    """Depthwise CausalDecoder (the shipped topology, audio_vae.py:255-280):
+    a small shape and the shipped shape (1536 channels, rates 16/8/5/3,
+    hop 1920), synth weights with fan-in scaling (seed 8 / 9), two short
+    latents each."""
+    _, av = load_reference(root)
+    for name, cfg, seed, T in (("vae_dw_small", VAE_DW_SMALL, 8, 9), ("vae_dw_shipped", VAE_DW_SHIPPED, 9, 3)):
+        w = synth.vae_weights(cfg, seed=seed, fan_in=VAE_DW_GAIN)
+        m = torch_vae(av, cfg, w)
+        lat = rnd(410 + seed, (2, cfg.latent, T))
+        with torch.no_grad():
+            wav = m(torch.from_numpy(lat)).numpy()[:, 0, :]
+        np.savez_compressed(os.path.join(HERE, name + ".npz"), latent=lat, wav=wav)
+        print(name, wav.shape)
+
+
 if __name__ == "__main__":
-    args = [a for a in sys.argv[1:] if a != "locenc"]
+    args = [a for a in sys.argv[1:] if a not in ("locenc", "vae_dw")]
     root = args[0] if args else "/root/reference"
     if "locenc" in sys.argv[1:]:
         make_locenc(root)  # only the LocEnc fixture
+    elif "vae_dw" in sys.argv[1:]:
+        make_vae_dw(root)  # only the depthwise VAE fixtures
     else:
         main(root)
         make_locenc(root)

@@ -149,6 +149,21 @@ def test_vae_config4(golden):
         assert cosine(wav, g["wav"][b]) > 0.9999
 
 
+@pytest.mark.parametrize("name,cfg,seed", [
+    ("vae_dw_small", VAEConfig(latent=64, channels=96, strides=(4, 3, 2), depthwise=True), 8),
+    ("vae_dw_shipped", VAEConfig(latent=64, channels=1536, strides=(16, 8, 5, 3), depthwise=True), 9),
+])
+def test_vae_depthwise(golden, name, cfg, seed):
+    """The shipped depthwise topology (audio_vae.py:255-280, decode.rs:94-136)
+    against the reference CausalDecoder(depthwise=True)."""
+    g = golden(name + ".npz")
+    vae = orc.VAE(cfg, synth.vae_weights(cfg, seed=seed, fan_in=0.8))
+    for b in range(g["latent"].shape[0]):
+        wav = vae.decode(g["latent"][b])
+        assert rel_err(wav, g["wav"][b]) < 1e-4
+        assert cosine(wav, g["wav"][b]) > 0.9999
+
+
 def test_vae_causal_prefix():
     """Causality: the first T1*hop samples depend only on the first T1 frames
     (a size-independent property also used at full size on the GPU)."""
