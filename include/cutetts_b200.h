@@ -185,6 +185,12 @@ CTTS_API int ctts_engine_set_heads(ctts_engine* e, const float* stop_w, const fl
  * projected prompt latents) and set its first DiT cond (previous raw
  * latent patch, [patch*latent]). */
 CTTS_API int ctts_engine_prefill(ctts_engine* e, int b, const float* x, int T, const float* cond0);
+/* AdaLN speaker embedding of utterance b (spk [spk_dim] host floats;
+ * bin/cutetts.rs passes the speaker encoder's vector to every euler_sample).
+ * Required for every utterance when the DiT's spk_dim differs from the LM
+ * hidden width (the shipped model: 256); otherwise the LM state conditions
+ * AdaLN unless speakers are set (the first call before the first step). */
+CTTS_API int ctts_engine_set_speaker(ctts_engine* e, int b, const float* spk);
 /* CFG mode: prefill utterance b's unconditional branch (x [T, hidden]) and
  * its initial uncond latent condition. */
 CTTS_API int ctts_engine_prefill_uncond(ctts_engine* e, int b, const float* x, int T, const float* cond0);

@@ -403,13 +403,14 @@ class VAE:
 
 # ------------------------------------------------------------- frame loop
 def generate(lm: LM, dit: DiT, fw: dict, prefix: np.ndarray, noise: np.ndarray,
-             cond0: np.ndarray, euler_steps: int, capacity: int | None = None):
+             cond0: np.ndarray, euler_steps: int, capacity: int | None = None, spk=None):
     """Per-frame AR loop (bin/cutetts.rs:429-523 / generation.py:931-1087)
     for one utterance: prefill the prefix rows, then for every frame: stop
     logits, Euler-sample the DiT from the supplied noise conditioned on the
     last LM hidden state (AdaLN conditioned on it too), feed the raw latent
     back through latent_proj into one LM decode step.  Returns latents
-    [F, latent], stop logits [F, 2] and the final LM hidden state."""
+    [F, latent], stop logits [F, 2] and the final LM hidden state.  spk, if
+    given, conditions AdaLN instead of the LM state (a speaker embedding)."""
     F = noise.shape[0]
     T = prefix.shape[0]
     cache = lm.new_cache(capacity or (T + F + 1))
@@ -420,7 +421,8 @@ def generate(lm: LM, dit: DiT, fw: dict, prefix: np.ndarray, noise: np.ndarray,
     stops = np.empty((F, 2), np.float32)
     for f in range(F):
         stops[f] = stop_logits(fw["stop_predictor.weight"], fw["stop_predictor.bias"], z)
-        x = dit.euler_sample(noise[f], z, cond, z if dit.cfg.adaln else None, euler_steps)
+        ad = (z if spk is None else _f(spk).reshape(-1)) if dit.cfg.adaln else None
+        x = dit.euler_sample(noise[f], z, cond, ad, euler_steps)
         lat[f] = x
         cond = x
         fb = linear(x[None, :], fw["latent_proj.weight"], fw["latent_proj.bias"])

@@ -85,6 +85,7 @@ SIGNATURES = {
     "ctts_engine_set_heads": (C.c_int, [vp, fp, fp, fp, fp]),
     "ctts_engine_prefill": (C.c_int, [vp, C.c_int, fp, C.c_int, fp]),
     "ctts_engine_prefill_uncond": (C.c_int, [vp, C.c_int, fp, C.c_int, fp]),
+    "ctts_engine_set_speaker": (C.c_int, [vp, C.c_int, fp]),
     "ctts_engine_step": (C.c_int, [vp, fp, fp, fp]),
     "ctts_engine_step_dev": (C.c_int, [vp, vp, vp, vp, vp]),
     "ctts_engine_launches_per_step": (C.c_int, [vp]),

@@ -688,7 +688,8 @@ int engine_enqueue_group(ctts_engine* e, EngineGroup& g, cudaStream_t s, int* la
     dts[i] = dt;
   }
   DitRun r;
-  r.R = B; r.z = z; r.cond = cond; r.spk = d->cfg.adaln ? z : nullptr;
+  const float* spk = !d->cfg.adaln ? nullptr : e->use_spk ? e->spk + (size_t)zm * g.b0 * d->cfg.spk_dim : z;
+  r.R = B; r.z = z; r.cond = cond; r.spk = spk;
   r.x = x; r.x_rows = B; r.steps = steps; r.times = times.data(); r.dts = dts.data(); r.mode = 0;
   r.step_dt = dt;
   if (e->cfg_on) {
@@ -768,8 +769,6 @@ extern "C" int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_
   CTTS_REQ(lm && dit && cfg && out, CTTS_ERR_ARG, "null argument");
   CTTS_REQ(lm->device == dit->device, CTTS_ERR_ARG, "LM and DiT on different devices");
   CTTS_REQ(dit->cfg.cond_dim == lm->cfg.hidden, CTTS_ERR_ARG, "DiT cond_dim must equal LM hidden");
-  CTTS_REQ(!dit->cfg.adaln || dit->cfg.spk_dim == lm->cfg.hidden, CTTS_ERR_ARG,
-           "AdaLN conditioning width must equal LM hidden");
   CTTS_REQ(cfg->batch > 0 && cfg->capacity > 0 && cfg->euler_steps > 0, CTTS_ERR_ARG, "bad config");
   CTTS_REQ(cfg->latent_scale != 0.0f, CTTS_ERR_ARG, "latent_scale must be non-zero");
   const int G = cfg->groups <= 0 ? 1 : cfg->groups;
@@ -828,6 +827,15 @@ extern "C" int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_
   }
   e->prefilled.assign(B, false);
   e->prefilled_u.assign(B, !cfg_on);
+  if (dit->cfg.adaln) {
+    e->spk = A.alloc<float>((size_t)zm * B * dit->cfg.spk_dim);
+    if (!e->spk) {
+      engine_destroy(e);
+      return set_error(CTTS_ERR_NOMEM, "engine speaker buffer");
+    }
+    e->use_spk = dit->cfg.spk_dim != H;
+  }
+  e->spk_set.assign(B, false);
   *out = e;
   return CTTS_OK;
 }
@@ -873,6 +881,28 @@ int engine_prefill(ctts_engine* e, int b, const float* x, int T, const float* co
 }
 }  // namespace
 
+extern "C" int ctts_engine_set_speaker(ctts_engine* e, int b, const float* spk) {
+  CTTS_REQ(e && spk, CTTS_ERR_ARG, "null argument");
+  CTTS_REQ(b >= 0 && b < e->cfg.batch, CTTS_ERR_ARG, "bad utterance index");
+  CTTS_REQ(e->dit->cfg.adaln, CTTS_ERR_STATE, "the DiT head has no AdaLN conditioning");
+  // switching z -> speaker rows changes the captured frame graph: only
+  // before the first step
+  CTTS_REQ(e->use_spk || e->steps_done == 0, CTTS_ERR_STATE, "first speaker embedding after the first frame step");
+  CTTS_CK(cudaSetDevice(e->lm->device));
+  EngineGroup& g = e->groups[b / e->groups[0].nb];
+  const int zm = e->cfg_on ? 2 : 1, S = e->dit->cfg.spk_dim;
+  // the unconditional branch's row gets the same vector (its AdaLN is zeroed)
+  for (int h = 0; h < zm; h++) {
+    const size_t row = (size_t)zm * g.b0 + (b - g.b0) + (size_t)h * g.nb;
+    CTTS_CK(cudaMemcpyAsync(e->spk + row * S, spk, sizeof(float) * S, cudaMemcpyHostToDevice, e->stream));
+  }
+  CTTS_CK(cudaStreamSynchronize(e->stream));
+  if (!e->use_spk) std::fill(e->spk_set.begin(), e->spk_set.end(), false);
+  e->use_spk = true;
+  e->spk_set[b] = true;
+  return CTTS_OK;
+}
+
 extern "C" int ctts_engine_prefill(ctts_engine* e, int b, const float* x, int T, const float* cond0) {
   return engine_prefill(e, b, x, T, cond0, false);
 }
@@ -887,6 +917,8 @@ extern "C" int ctts_engine_step_dev(ctts_engine* e, const float* noise_dev, floa
   CTTS_REQ(e->heads_set, CTTS_ERR_STATE, "engine heads not set");
   for (int b = 0; b < e->cfg.batch; b++) {
     CTTS_REQ(e->prefilled[b], CTTS_ERR_STATE, "utterance " + std::to_string(b) + " not prefilled");
+    CTTS_REQ(!e->use_spk || e->spk_set[b], CTTS_ERR_STATE,
+             "utterance " + std::to_string(b) + ": speaker embedding not set");
     CTTS_REQ(e->prefilled_u[b], CTTS_ERR_STATE,
              "utterance " + std::to_string(b) + ": unconditional branch not prefilled");
   }

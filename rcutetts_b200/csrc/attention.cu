@@ -810,8 +810,10 @@ cudaError_t launch_qk_rope_append(const AttnArgs& a, cudaStream_t s) {
 template <bool BF, int HD>
 cudaError_t launch_attn_step_t(const AttnArgs& a, cudaStream_t s) {
   const size_t smem = (size_t)2 * a.chunk * HD * (BF ? 2 : 4);
+  // opt in whenever the dynamic size grows: the static arrays count against
+  // the 48 KB default as well (fp32, head_dim 128: 32 KB + 16.5 KB)
   static size_t configured = 0;
-  if (smem > 48 * 1024 && smem > configured) {
+  if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(attn_step_kernel<BF, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
@@ -825,7 +827,7 @@ template <bool BF, int HD>
 cudaError_t launch_attn_loop_t(const AttnArgs& a, cudaStream_t s) {
   const size_t smem = (size_t)2 * 2 * 128 * HD * (BF ? 2 : 4);
   static size_t configured = 0;
-  if (smem > 48 * 1024 && smem > configured) {
+  if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(attn_loop_kernel<BF, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;

@@ -119,6 +119,13 @@ struct ctts_engine {
   bool heads_set = false;
   bool cfg_on = false;  // classifier-free guidance: per-group rows [cond B | uncond B]
   std::vector<bool> prefilled, prefilled_u;
+  // AdaLN conditioning: the LM state z (spk_dim == LM hidden, the benchmark
+  // model) or a per-utterance speaker embedding set by ctts_engine_set_speaker
+  // (required when spk_dim differs, the shipped model's 256-wide speaker
+  // vector); rows laid out like z
+  float* spk = nullptr;
+  bool use_spk = false;
+  std::vector<bool> spk_set;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   int steps_done = 0;

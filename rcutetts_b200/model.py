@@ -277,6 +277,12 @@ class FrameEngine(_Handle):
         x, cond0 = _f(x), _f(cond0)
         check(_lib.load().ctts_engine_prefill_uncond(self.h, b, _p(x), x.shape[0], _p(cond0)))
 
+    def set_speaker(self, b: int, spk) -> None:
+        """AdaLN speaker embedding [spk_dim] of utterance b (required when the
+        DiT's spk_dim differs from the LM hidden width)."""
+        spk = np.ascontiguousarray(spk, dtype=np.float32).reshape(-1)
+        check(_lib.load().ctts_engine_set_speaker(self.h, b, _p(spk)))
+
     def step(self, noise):
         noise = _f(noise).reshape(self.batch, self.pl)
         lat = np.empty_like(noise)

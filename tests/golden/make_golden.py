@@ -251,6 +251,44 @@ def main(root):
         print(k, v)
 
 
+# The shipped model's LM and DiT head shapes (qwen.rs:17-24, dit.rs:16-26):
+# LM hidden 1024, 7 layers, 16/8 heads of 128, FFN 3072, vocab 16385; DiT
+# hidden 1024, FFN 4096, 16/2 heads of 64, patch 2, speaker AdaLN width 256,
+# mu_proj Identity (cond_dim == hidden).
+LM_SHIPPED = LMConfig(hidden=1024, n_layers=7, n_heads=16, n_kv_heads=8, head_dim=128, ffn=3072, vocab=16385)
+DIT_SHIPPED = DiTConfig(hidden=1024, n_heads=16, n_kv_heads=2, head_dim=64, ffn=4096, n_layers=4, patch=2,
+                        cond_dim=1024, spk_dim=256)
+
+
+def make_shipped(root):
+    """lm_shipped.npz (synth weights seed 30: 10-row prefill + 3 decodes,
+    final-normed outputs) and dit_shipped.npz (seed 31: predict at t=0.4 and
+    a 10-step Euler sample for 2 utterances with speaker AdaLN)."""
+    dh, _ = load_reference(root)
+    wl = synth.lm_weights(LM_SHIPPED, seed=30, with_embed=False)
+    m = hf_qwen(LM_SHIPPED, LM_SHIPPED.n_layers, wl)
+    xp, xd = rnd(500, (10, LM_SHIPPED.hidden)), rnd(501, (3, LM_SHIPPED.hidden))
+    final, _ = run_hf(m, xp, xd)
+    np.savez_compressed(os.path.join(HERE, "lm_shipped.npz"), x_prefill=xp, x_decode=xd, final_out=final)
+    print("lm_shipped", final.shape)
+    cfg = DIT_SHIPPED
+    wd = synth.dit_weights(cfg, seed=31)
+    md = torch_dit(dh, cfg, wd)
+    B, P = 2, cfg.patch * cfg.latent
+    x0, z = rnd(510, (B, P)), rnd(511, (B, cfg.cond_dim))
+    cond, spk = rnd(512, (B, P)), rnd(513, (B, cfg.spk_dim))
+    tx, tz, tc, ts = (torch.from_numpy(a) for a in (x0, z, cond, spk))
+    with torch.no_grad():
+        # [N, P, D] inputs: a flat [N, P*D] input makes _predict return patch 0 only
+        v3 = md._predict(tx.reshape(B, cfg.patch, cfg.latent), torch.full((B,), 0.4), tz,
+                         tc.reshape(B, cfg.patch, cfg.latent), speaker_embedding=ts)
+        v = v3.reshape(B, P).numpy()
+        xs = md._euler_sample_core(tx, tz, tc, ts, None, 0.0, 10).numpy()
+    np.savez_compressed(os.path.join(HERE, "dit_shipped.npz"), x0=x0, z=z, cond=cond, spk=spk, t=np.float32(0.4),
+                        predict_out=v, euler10_out=xs)
+    print("dit_shipped", xs.shape)
+
+
 VAE_DW_GAIN = 0.8  # fan-in weight scale: waveform std well inside tanh's range
 VAE_DW_SMALL = VAEConfig(latent=64, channels=96, strides=(4, 3, 2), depthwise=True)
 VAE_DW_SHIPPED = VAEConfig(latent=64, channels=1536, strides=(16, 8, 5, 3), depthwise=True)
@@ -273,12 +311,14 @@ def make_vae_dw(root):
 
 
 if __name__ == "__main__":
-    args = [a for a in sys.argv[1:] if a not in ("locenc", "vae_dw")]
+    args = [a for a in sys.argv[1:] if a not in ("locenc", "vae_dw", "shipped")]
     root = args[0] if args else "/root/reference"
     if "locenc" in sys.argv[1:]:
         make_locenc(root)  # only the LocEnc fixture
     elif "vae_dw" in sys.argv[1:]:
         make_vae_dw(root)  # only the depthwise VAE fixtures
+    elif "shipped" in sys.argv[1:]:
+        make_shipped(root)  # only the shipped-shape LM / DiT fixtures
     else:
         main(root)
         make_locenc(root)

@@ -127,6 +127,39 @@ def test_dit_config2(golden):
         assert cosine(x, g["euler10_out"][b]) > 0.9999
 
 
+# The shipped model's shapes (qwen.rs:17-24, dit.rs:16-26)
+LM_SHIPPED = LMConfig(hidden=1024, n_layers=7, n_heads=16, n_kv_heads=8, head_dim=128, ffn=3072, vocab=16385)
+DIT_SHIPPED = DiTConfig(hidden=1024, n_heads=16, n_kv_heads=2, head_dim=64, ffn=4096, n_layers=4, patch=2,
+                        cond_dim=1024, spk_dim=256)
+
+
+def test_lm_shipped_shape(golden):
+    """7 layers, 16/8 heads of 128, FFN 3072 against HF Qwen3Model."""
+    g = golden("lm_shipped.npz")
+    lm = orc.LM(LM_SHIPPED, synth.lm_weights(LM_SHIPPED, seed=30, with_embed=False))
+    cache = lm.new_cache(16)
+    outs = [lm.forward(g["x_prefill"], cache)]
+    for i in range(g["x_decode"].shape[0]):
+        outs.append(lm.forward(g["x_decode"][i:i + 1], cache))
+    got = np.concatenate(outs, 0)
+    for i in range(got.shape[0]):
+        assert rel_err(got[i], g["final_out"][i]) < 1e-4, i
+
+
+def test_dit_shipped_shape(golden):
+    """hidden 1024, 16/2 heads, FFN 4096, patch 2, speaker AdaLN (256),
+    mu_proj Identity: predict and the 10-step Euler sample against the
+    reference AudioDiTHead."""
+    g = golden("dit_shipped.npz")
+    dit = orc.DiT(DIT_SHIPPED, synth.dit_weights(DIT_SHIPPED, seed=31))
+    for b in range(2):
+        v = dit.predict(g["x0"][b], float(g["t"]), g["z"][b], g["cond"][b], spk=g["spk"][b])
+        assert rel_err(v, g["predict_out"][b]) < 1e-4
+        x = dit.euler_sample(g["x0"][b], g["z"][b], g["cond"][b], g["spk"][b], 10)
+        assert rel_err(x, g["euler10_out"][b]) < 1e-4
+        assert cosine(x, g["euler10_out"][b]) > 0.9999
+
+
 def test_dit_plain_and_cfg(golden):
     g, gc = golden("dit_plain.npz"), golden("dit_c2.npz")
     cfg = DiTConfig(adaln=False, n_layers=2)
