@@ -403,14 +403,16 @@ class VAE:
 
 # ------------------------------------------------------------- frame loop
 def generate(lm: LM, dit: DiT, fw: dict, prefix: np.ndarray, noise: np.ndarray,
-             cond0: np.ndarray, euler_steps: int, capacity: int | None = None, spk=None):
+             cond0: np.ndarray, euler_steps: int, capacity: int | None = None, spk=None, cfg_w=0.0):
     """Per-frame AR loop (bin/cutetts.rs:429-523 / generation.py:931-1087)
     for one utterance: prefill the prefix rows, then for every frame: stop
     logits, Euler-sample the DiT from the supplied noise conditioned on the
     last LM hidden state (AdaLN conditioned on it too), feed the raw latent
     back through latent_proj into one LM decode step.  Returns latents
     [F, latent], stop logits [F, 2] and the final LM hidden state.  spk, if
-    given, conditions AdaLN instead of the LM state (a speaker embedding)."""
+    given, conditions AdaLN instead of the LM state (a speaker embedding);
+    cfg_w is the distilled guidance strength of a head with a cfg-strength
+    embedding (bin/cutetts.rs:460-461)."""
     F = noise.shape[0]
     T = prefix.shape[0]
     cache = lm.new_cache(capacity or (T + F + 1))
@@ -422,7 +424,7 @@ def generate(lm: LM, dit: DiT, fw: dict, prefix: np.ndarray, noise: np.ndarray,
     for f in range(F):
         stops[f] = stop_logits(fw["stop_predictor.weight"], fw["stop_predictor.bias"], z)
         ad = (z if spk is None else _f(spk).reshape(-1)) if dit.cfg.adaln else None
-        x = dit.euler_sample(noise[f], z, cond, ad, euler_steps)
+        x = dit.euler_sample(noise[f], z, cond, ad, euler_steps, cfg_w=cfg_w)
         lat[f] = x
         cond = x
         fb = linear(x[None, :], fw["latent_proj.weight"], fw["latent_proj.bias"])

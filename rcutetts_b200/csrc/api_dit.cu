@@ -362,7 +362,8 @@ int dit_check(ctts_dit* d) {
 }
 
 // host-side cfg-strength hidden: silu(cfg0[:,0] * cfg_w / 5) (dit.rs:657-662)
-int dit_upload_cfg_hidden(ctts_dit* d, float cfg_w, cudaStream_t s) {
+// into the first H floats of `hbuf` (a workspace's hbuf)
+int dit_upload_cfg_hidden(ctts_dit* d, float* hbuf, float cfg_w, cudaStream_t s) {
   if (!d->cfg2_w) return CTTS_OK;
   const int H = d->cfg.hidden;
   std::vector<float> w0(H), h(H);
@@ -372,7 +373,7 @@ int dit_upload_cfg_hidden(ctts_dit* d, float cfg_w, cudaStream_t s) {
     float v = fmaf(w0[i], wn, 0.0f);
     h[i] = v / (1.0f + expf(-v));
   }
-  CTTS_CK(cudaMemcpyAsync(d->ws.hbuf, h.data(), H * 4, cudaMemcpyHostToDevice, s));
+  CTTS_CK(cudaMemcpyAsync(hbuf, h.data(), H * 4, cudaMemcpyHostToDevice, s));
   CTTS_CK(cudaStreamSynchronize(s));
   return CTTS_OK;
 }
@@ -540,7 +541,7 @@ extern "C" int ctts_dit_euler_sample_dev(ctts_dit* d, int batch, const float* x0
   rc = dit_ws_ensure(d, d->ws, batch, steps);
   if (rc) return rc;
   cudaStream_t s = as_stream(stream, d->stream);
-  rc = dit_upload_cfg_hidden(d, cfg_w, s);
+  rc = dit_upload_cfg_hidden(d, d->ws.hbuf, cfg_w, s);
   if (rc) return rc;
   const int PL = d->cfg.patch * d->cfg.latent;
   if (x_out_dev != x0_dev)
@@ -597,7 +598,7 @@ extern "C" int ctts_dit_predict(ctts_dit* d, int batch, const float* x, float t,
   if ((rc = copy_in(w.z, z, (size_t)batch * d->cfg.cond_dim, d->stream))) return rc;
   if ((rc = copy_in(w.cond, cond, (size_t)batch * PL, d->stream))) return rc;
   if (spk && (rc = copy_in(w.spk, spk, (size_t)batch * d->cfg.spk_dim, d->stream))) return rc;
-  rc = dit_upload_cfg_hidden(d, cfg_w, d->stream);
+  rc = dit_upload_cfg_hidden(d, d->ws.hbuf, cfg_w, d->stream);
   if (rc) return rc;
   float times[1] = {t};
   DitRun r;
@@ -632,7 +633,7 @@ extern "C" int ctts_dit_euler_sample_cfg(ctts_dit* d, int batch, const float* x0
   if (spk) {
     if ((rc = copy_in(w.spk, spk, (size_t)batch * d->cfg.spk_dim, d->stream))) return rc;
   }
-  rc = dit_upload_cfg_hidden(d, cfg, d->stream);
+  rc = dit_upload_cfg_hidden(d, d->ws.hbuf, cfg, d->stream);
   if (rc) return rc;
   std::vector<float> times(steps + 1), dts(steps);
   rc = ctts_sway_timesteps(steps, coeff, times.data());
@@ -691,7 +692,7 @@ int engine_enqueue_group(ctts_engine* e, EngineGroup& g, cudaStream_t s, int* la
   const float* spk = !d->cfg.adaln ? nullptr : e->use_spk ? e->spk + (size_t)zm * g.b0 * d->cfg.spk_dim : z;
   r.R = B; r.z = z; r.cond = cond; r.spk = spk;
   r.x = x; r.x_rows = B; r.steps = steps; r.times = times.data(); r.dts = dts.data(); r.mode = 0;
-  r.step_dt = dt;
+  r.step_dt = dt; r.cfg_w = d->cfg.cfg_emb ? e->cfg.cfg_strength : 0.0f;
   if (e->cfg_on) {
     // euler_sample_cfg (dit.rs:862-904) on the sway grid: both branches in
     // one 2B-row pass, the unconditional rows without AdaLN conditioning
@@ -777,9 +778,11 @@ extern "C" int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_
   if (rc) return rc;
   rc = dit_check(dit);
   if (rc) return rc;
-  CTTS_REQ(!dit->cfg.cfg_emb, CTTS_ERR_ARG, "engine runs the single-branch head (no cfg embedding)");
   CTTS_REQ(cfg->cfg_strength >= 0.0f, CTTS_ERR_ARG, "cfg_strength must be >= 0");
-  const bool cfg_on = cfg->cfg_strength > 0.0f;
+  // a head with a cfg-strength embedding (the distill checkpoint) takes the
+  // strength as a condition of its single branch (bin/cutetts.rs:460-461);
+  // a base head runs the two-branch CFG when the strength is positive
+  const bool cfg_on = cfg->cfg_strength > 0.0f && !dit->cfg.cfg_emb;
   const int zm = cfg_on ? 2 : 1;
   CTTS_CK(cudaSetDevice(lm->device));
   auto* e = new ctts_engine();
@@ -800,6 +803,7 @@ extern "C" int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_
     cudaEventCreateWithFlags(&g.done, cudaEventDisableTiming);
     rc = ctts_kv_alloc(lm, zm * per, cfg->capacity, &g.kv);
     if (!rc) rc = dit_ws_ensure(dit, *g.ws, zm * per, cfg->euler_steps);
+    if (!rc && dit->cfg.cfg_emb) rc = dit_upload_cfg_hidden(dit, g.ws->hbuf, cfg->cfg_strength, g.stream);
     if (rc) {
       engine_destroy(e);
       return rc;

@@ -86,15 +86,22 @@ def test_dit_shipped_bf16_batch_vs_oracle():
         assert cosine(x[b], ref) >= 0.999, b
 
 
-def test_engine_shipped_frames_vs_oracle():
+@pytest.mark.parametrize("distill", [False, True])
+def test_engine_shipped_frames_vs_oracle(distill):
     """The frame engine at the shipped shapes (7-layer LM, patch-2 DiT whose
     AdaLN is conditioned on a 256-wide speaker vector set per utterance):
     4 utterances x 3 frames in bf16 against the oracle's AR loop on the same
-    bf16 weights."""
+    bf16 weights.  distill: the distill checkpoint's head (step-size and
+    cfg-strength embeddings, dit_manifest.json) sampled in 4 Euler steps with
+    the distilled guidance strength 2.0 as its condition (bin/cutetts.rs:460-461)."""
+    from dataclasses import replace
+
     from rcutetts_b200._lib import ERR_STATE, CttsError
     from rcutetts_b200.model import DitW, FrameEngine, QwenW
 
-    lcfg, dcfg = LM_SHIPPED, DIT_SHIPPED
+    lcfg = LM_SHIPPED
+    dcfg = replace(DIT_SHIPPED, step_emb=True, cfg_emb=True) if distill else DIT_SHIPPED
+    steps, strength = (4, 2.0) if distill else (10, 0.0)
     PL = dcfg.latent * dcfg.patch
     lw = synth.lm_weights(lcfg, seed=34, with_embed=True)
     dw = synth.dit_weights(dcfg, seed=35)
@@ -102,7 +109,7 @@ def test_engine_shipped_frames_vs_oracle():
     lm = QwenW(lcfg, "bf16").set_weights(lw)
     dit = DitW(dcfg, "bf16").set_weights(dw)
     B = 4
-    eng = FrameEngine(lm, dit, hw, batch=B, capacity=64, euler_steps=10)
+    eng = FrameEngine(lm, dit, hw, batch=B, capacity=64, euler_steps=steps, cfg_strength=strength)
     pres = [rnd(800 + b, (6 + 3 * b, lcfg.hidden)) for b in range(B)]
     conds, spks = rnd(810, (B, PL)), rnd(811, (B, dcfg.spk_dim))
     noise = rnd(812, (3, B, PL))
@@ -116,6 +123,7 @@ def test_engine_shipped_frames_vs_oracle():
     lat = np.stack([eng.step(noise[f])[0] for f in range(3)])
     lm_o, dit_o = orc.LM(lcfg, bf16_weights(lw)), orc.DiT(dcfg, bf16_weights(dw))
     for b in (0, 3):
-        ref, _, _ = orc.generate(lm_o, dit_o, hw, pres[b], noise[:, b, :], conds[b], 10, spk=spks[b])
+        ref, _, _ = orc.generate(lm_o, dit_o, hw, pres[b], noise[:, b, :], conds[b], steps, spk=spks[b],
+                                 cfg_w=strength)
         for f in range(3):
             assert cosine(lat[f, b], ref[f]) >= 0.999, (b, f)
