@@ -77,6 +77,10 @@ struct DitRun {
   float cfg_w = 0.0f;            // cfg_strength embedding input (distill)
   float step_dt = 0.0f;          // step-size embedding input (distill)
   float* out = nullptr;          // predict: v [R, P*L]
+  // the time / delta-time / step-size / cfg-strength embeddings already sit
+  // in the workspace from an earlier run with the same grid, dt and
+  // strength (the frame engine: constant across frames)
+  bool consts_cached = false;
 };
 
 // The cluster-resident Euler loop runs when the head has the shapes it is
@@ -152,9 +156,11 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
   for (int i = 0; i < r.steps; i++) g.t[i] = r.times[i];
   g.t[r.steps] = 0.0f;  // delta_time_mlp input (legacy dt = 0)
   if (d->st1_w) g.t[r.steps + 1] = r.step_dt;
-  CTTS_CK(launch_fill_tv(w.tv, g, s)); nl++;
-  CTTS_CK(launch_sin_emb(w.tv, g.n, H, w.se, s)); nl++;
-  {
+  if (!r.consts_cached) {
+    CTTS_CK(launch_fill_tv(w.tv, g, s)); nl++;
+    CTTS_CK(launch_sin_emb(w.tv, g.n, H, w.se, s)); nl++;
+  }
+  if (!r.consts_cached) {
     LinearArgs a; a.x = w.se; a.x_ld = H; a.M = r.steps; a.K = H; a.N = H; a.w = d->t1_w;
     a.bias = d->t1_b; a.act = 1; a.y = w.tmp; a.y_ld = H; RUN(lin(a));
     LinearArgs b; b.x = w.tmp; b.x_ld = H; b.M = r.steps; b.K = H; b.N = H; b.w = d->t2_w;
@@ -166,7 +172,13 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
     c2.w = d->dt2_w; c2.bias = d->dt2_b; c2.y = w.dtemb; c2.y_ld = H; RUN(lin(c2));
   }
   // mu = mu_proj(z) (+ cfg_strength) (+ step_size)   diffusion_head.py:601-627
-  if (d->mu_w) {
+  // (bf16 weights with >= 16 rows: on the tensor cores)
+  if (d->mu_w && bf && R >= 16 && c.cond_dim % 64 == 0) {
+    PrepArgs pa; pa.x = r.z; pa.x_ld = c.cond_dim; pa.y = w.xb; pa.y_ld = c.cond_dim; pa.M = R; pa.K = c.cond_dim;
+    CTTS_CK(launch_prep_bf16(pa, s)); nl++;
+    TcArgs e; e.y = w.mu; e.y_ld = H; e.bias = d->mu_b;
+    RUN(tc_run(w.tc, w.xb, R, c.cond_dim, d->mu_w, H, e, s, &nl));
+  } else if (d->mu_w) {
     LinearArgs a; a.x = r.z; a.x_ld = c.cond_dim; a.M = R; a.K = c.cond_dim; a.N = H; a.w = d->mu_w;
     a.bias = d->mu_b; a.y = w.mu; a.y_ld = H; RUN(lin(a));
   } else {
@@ -174,16 +186,20 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
   }
   if (d->cfg2_w) {
     // silu(cfg0 * cfg_w/5) on the host (a [H,1] x scalar product), then cfg2.
-    LinearArgs a; a.x = w.hbuf; a.x_ld = H; a.M = 1; a.K = H; a.N = H; a.w = d->cfg2_w;
-    a.y = w.hbuf + H; a.y_ld = H; RUN(lin(a));
+    if (!r.consts_cached) {
+      LinearArgs a; a.x = w.hbuf; a.x_ld = H; a.M = 1; a.K = H; a.N = H; a.w = d->cfg2_w;
+      a.y = w.hbuf + H; a.y_ld = H; RUN(lin(a));
+    }
     CTTS_CK(launch_add_rows(w.mu, R, H, w.hbuf + H, s)); nl++;
   }
   if (d->st1_w) {
-    LinearArgs a; a.x = w.se + (size_t)(r.steps + 1) * H; a.x_ld = H; a.M = 1; a.K = H; a.N = H;
-    a.w = d->st1_w; a.bias = d->st1_b; a.act = 1; a.y = w.tmp + (size_t)(r.steps + 1) * H; a.y_ld = H;
-    RUN(lin(a));
-    LinearArgs b; b.x = w.tmp + (size_t)(r.steps + 1) * H; b.x_ld = H; b.M = 1; b.K = H; b.N = H;
-    b.w = d->st2_w; b.bias = d->st2_b; b.y = w.stemb; b.y_ld = H; RUN(lin(b));
+    if (!r.consts_cached) {
+      LinearArgs a; a.x = w.se + (size_t)(r.steps + 1) * H; a.x_ld = H; a.M = 1; a.K = H; a.N = H;
+      a.w = d->st1_w; a.bias = d->st1_b; a.act = 1; a.y = w.tmp + (size_t)(r.steps + 1) * H; a.y_ld = H;
+      RUN(lin(a));
+      LinearArgs b; b.x = w.tmp + (size_t)(r.steps + 1) * H; b.x_ld = H; b.M = 1; b.K = H; b.N = H;
+      b.w = d->st2_w; b.bias = d->st2_b; b.y = w.stemb; b.y_ld = H; RUN(lin(b));
+    }
     CTTS_CK(launch_add_rows(w.mu, R, H, w.stemb, s)); nl++;
   }
   const bool use_ad = c.adaln && r.spk;
@@ -203,7 +219,12 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
     }
     if (rows < R) CTTS_CK(cudaMemsetAsync(w.ad + (size_t)rows * adld, 0, sizeof(float) * (R - rows) * adld, s));
   }
-  {  // cond_proj(cond) rows [R*P, L]
+  if (bf && R * P >= 16 && L % 64 == 0) {  // cond_proj(cond) rows [R*P, L]
+    PrepArgs pa; pa.x = r.cond; pa.x_ld = L; pa.y = w.xb; pa.y_ld = L; pa.M = R * P; pa.K = L;
+    CTTS_CK(launch_prep_bf16(pa, s)); nl++;
+    TcArgs e; e.y = w.condh; e.y_ld = H; e.bias = d->cond_b;
+    RUN(tc_run(w.tc, w.xb, R * P, L, d->cond_w, H, e, s, &nl));
+  } else {
     LinearArgs a; a.x = r.cond; a.x_ld = L; a.M = R * P; a.K = L; a.N = H; a.w = d->cond_w;
     a.bias = d->cond_b; a.y = w.condh; a.y_ld = H; RUN(lin(a));
   }
@@ -693,6 +714,9 @@ int engine_enqueue_group(ctts_engine* e, EngineGroup& g, cudaStream_t s, int* la
   r.R = B; r.z = z; r.cond = cond; r.spk = spk;
   r.x = x; r.x_rows = B; r.steps = steps; r.times = times.data(); r.dts = dts.data(); r.mode = 0;
   r.step_dt = dt; r.cfg_w = d->cfg.cfg_emb ? e->cfg.cfg_strength : 0.0f;
+  // the first (eager) frame computes the frame-constant embeddings into the
+  // group's workspace; later frames (and the captured graph) reuse them
+  r.consts_cached = e->steps_done > 0;
   if (e->cfg_on) {
     // euler_sample_cfg (dit.rs:862-904) on the sway grid: both branches in
     // one 2B-row pass, the unconditional rows without AdaLN conditioning
@@ -935,8 +959,10 @@ extern "C" int ctts_engine_step_dev(ctts_engine* e, const float* noise_dev, floa
     CTTS_CK(cudaMemcpyAsync(e->noise, noise_dev, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
   if (!e->cfg.use_graph || e->steps_done == 0) {
     // first frame runs eagerly (sets kernel attributes outside any capture)
-    int rc = engine_enqueue(e, s, &e->launches);
+    int n = 0;
+    int rc = engine_enqueue(e, s, &n);
     if (rc) return rc;
+    e->launches = n;
   } else {
     if (!e->exec) {
       CTTS_CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
@@ -949,6 +975,7 @@ extern "C" int ctts_engine_step_dev(ctts_engine* e, const float* noise_dev, floa
         return rc;
       }
       CTTS_CK(ce);
+      e->launches = n;  // the steady-state frame (constants computed by the first frame)
       e->graph = gr;
       CTTS_CK(cudaGraphInstantiate(&e->exec, gr, 0));
     }
