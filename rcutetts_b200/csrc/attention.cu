@@ -382,6 +382,30 @@ __global__ void __launch_bounds__(128) attn_step_kernel(const AttnArgs a) {
   }
 }
 
+// Optional phase timeline (build with -DCTTS_ATT_TRACE): thread 0 of CTA
+// (0, 0) of every loop-attention launch records ((launch << 8) | event,
+// %globaltimer) pairs; slots are taken atomically (launches overlap).
+#ifdef CTTS_ATT_TRACE
+__device__ long long g_att_trace[4096];
+__device__ int g_att_trace_n;
+__device__ int g_att_launch;
+CTTS_DEV void att_trace(int ev) {
+  if (blockIdx.x != 0 || blockIdx.y != 0 || threadIdx.x != 0) return;
+  __shared__ int lid;
+  if (ev == 0) lid = atomicAdd(&g_att_launch, 1);
+  long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  const int n = atomicAdd(&g_att_trace_n, 1);
+  if (n < 2047) {
+    g_att_trace[2 * n] = ((long long)lid << 8) | ev;
+    g_att_trace[2 * n + 1] = t;
+  }
+}
+#define ATT_TRACE(ev) att_trace(ev)
+#else
+#define ATT_TRACE(ev)
+#endif
+
 // Large-batch form of the same decode step: one CTA per (kv head,
 // utterance) walks the utterance's keys in 128-key stages through a
 // two-stage ring of bulk copies (the copy of stage s+2 is issued as soon as
@@ -391,7 +415,7 @@ __global__ void __launch_bounds__(128) attn_step_kernel(const AttnArgs a) {
 // warp states merge once at the end, in warp order.  The new key/value row is kept in shared memory
 // and placed into its stage's tile once that stage's copy has landed.
 // grid (nkv, batch), 256 threads, dynamic smem 2 stages x (K, V) x 128 rows.
-template <bool BF, int HD>
+template <bool BF, int HD, int GM>
 __global__ void __launch_bounds__(256) attn_loop_kernel(const AttnArgs a) {
   constexpr int ES = BF ? 2 : 4;
   constexpr int ROWB = HD * ES;
@@ -401,13 +425,17 @@ __global__ void __launch_bounds__(256) attn_loop_kernel(const AttnArgs a) {
   constexpr int C = 128;             // keys per stage
   constexpr int NT = 256;
   constexpr int NW = NT / 32;
-  constexpr int KPW = C / NW;        // keys of a stage per warp (2 threads per key)
+  constexpr int KPW = C / NW;        // keys of a stage per warp
+  constexpr int KPI = 32 / NC;       // keys per warp pass: NC lanes per key, one 16-byte chunk each
+  constexpr int NIT = KPW / KPI;     // passes over the warp's keys
   constexpr int DPL = HD / 32;       // V dims per lane in the P.V pass
+  static_assert(NC == 8 || NC == 16, "one key row is 8 or 16 chunks of 16 bytes");
   extern __shared__ __align__(128) uint8_t kv_smem[];  // [2][K|V][C][ROWB]
   __shared__ __align__(16) float qs[kMaxG][HD];
   __shared__ __align__(16) uint8_t newrow[2][ROWB];  // new K, V row in the cache type
-  __shared__ float wpart[NW][kMaxG][HD + 2];         // per-warp [m, l, acc[HD]]
+  __shared__ float wpart[NW][GM][HD + 2];            // per-warp [m, l, acc[HD]]
   __shared__ __align__(8) uint64_t bars[2];
+  ATT_TRACE(0);
 
   const int kh = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -447,7 +475,9 @@ __global__ void __launch_bounds__(256) attn_loop_kernel(const AttnArgs a) {
     issue(0);
     if (nst > 1) issue(1);
   }
+  ATT_TRACE(1);
   grid_dep_enter();
+  ATT_TRACE(2);
   if (bad && kh == 0 && tid == 0 && a.err) atomicExch(a.err, 1);
 
   // ---- queries and the new key/value row: one warp per job
@@ -503,13 +533,24 @@ __global__ void __launch_bounds__(256) attn_loop_kernel(const AttnArgs a) {
     }
   }
   __syncthreads();  // queries and the new row are set
+  ATT_TRACE(3);
   const float scale = 1.0f / sqrtf((float)HD);
+  // Lane = (key of the pass, 16-byte chunk ch): the lane keeps its chunk of
+  // every query head in registers, so a key row is read once, conflict-free
+  // (the NC lanes of a key cover its contiguous row), and the chunk partial
+  // dot products meet by xor-shuffles inside each key's lane group.
+  const int ch = lane % NC, ksub = lane / NC;
+  float qr[GM][VPC];
+#pragma unroll
+  for (int g = 0; g < GM; g++)
+#pragma unroll
+    for (int e = 0; e < VPC; e++) qr[g][e] = g < G ? qs[g][ch * VPC + e] : 0.0f;
   // Every warp runs its own online softmax over its 16 keys of each stage
   // (no block-wide reduction per stage); the 8 warp states merge at the end
   // in warp order (deterministic).
-  float m_w[kMaxG], l_w[kMaxG], acc[kMaxG][DPL];
+  float m_w[GM], l_w[GM], acc[GM][DPL];
 #pragma unroll
-  for (int g = 0; g < kMaxG; g++) {
+  for (int g = 0; g < GM; g++) {
     m_w[g] = -INFINITY;
     l_w[g] = 0.0f;
 #pragma unroll
@@ -542,22 +583,16 @@ __global__ void __launch_bounds__(256) attn_loop_kernel(const AttnArgs a) {
           reinterpret_cast<const uint4*>(newrow[kv])[cch];
     }
     __syncthreads();
-    // scores: two threads per key, each half of the 16-byte chunks
+    // scores of the warp's keys kbase + it*KPI + ksub
     const int kbase = warp * KPW;
-    const int key = kbase + (lane >> 1), half = lane & 1;
-    const bool valid = key < rows;
-    float sc[kMaxG];
+    float sc[NIT][GM];
 #pragma unroll
-    for (int g = 0; g < kMaxG; g++) sc[g] = 0.0f;
-    if (valid) {
-      const uint8_t* krow = Ks + (size_t)key * ROWB;
-#pragma unroll
-      for (int cc = 0; cc < NC / 2; cc++) {
-        // rotated per key and half: the 8 lanes of a 16-byte access phase
-        // hit 8 different bank groups
-        const int c = half * (NC / 2) + (cc + key + half * 4) % (NC / 2);
-        const uint4 t = *reinterpret_cast<const uint4*>(krow + c * 16);
-        float kv[VPC];
+    for (int it = 0; it < NIT; it++) {
+      const int key = kbase + it * KPI + ksub;
+      const bool valid = key < rows;
+      float kv[VPC];
+      if (valid) {
+        const uint4 t = reinterpret_cast<const uint4*>(Ks + (size_t)key * ROWB)[ch];
         if constexpr (BF) {
           kv[0] = bf_lo(t.x); kv[1] = bf_hi(t.x); kv[2] = bf_lo(t.y); kv[3] = bf_hi(t.y);
           kv[4] = bf_lo(t.z); kv[5] = bf_hi(t.z); kv[6] = bf_lo(t.w); kv[7] = bf_hi(t.w);
@@ -565,32 +600,47 @@ __global__ void __launch_bounds__(256) attn_loop_kernel(const AttnArgs a) {
           kv[0] = __uint_as_float(t.x); kv[1] = __uint_as_float(t.y);
           kv[2] = __uint_as_float(t.z); kv[3] = __uint_as_float(t.w);
         }
+      } else {
 #pragma unroll
-        for (int g = 0; g < kMaxG; g++) {
-          if (g >= G) break;
-          const float* q = qs[g] + c * VPC;
+        for (int e = 0; e < VPC; e++) kv[e] = 0.0f;
+      }
 #pragma unroll
-          for (int e = 0; e < VPC; e++) sc[g] = fmaf(q[e], kv[e], sc[g]);
-        }
+      for (int g = 0; g < GM; g++) {
+        float d = 0.0f;
+#pragma unroll
+        for (int e = 0; e < VPC; e++) d = fmaf(qr[g][e], kv[e], d);
+#pragma unroll
+        for (int o = 1; o < NC; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        sc[it][g] = valid ? d * scale : -INFINITY;
       }
     }
-    float pr[kMaxG];
+    // online softmax update per head over the warp's keys
+    float pr[NIT][GM];
 #pragma unroll
-    for (int g = 0; g < kMaxG; g++) {
-      if (g >= G) break;
-      sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], 1);
-      sc[g] = valid ? sc[g] * scale : -INFINITY;
-      const float mn = fmaxf(m_w[g], warp_max(sc[g]));
+    for (int g = 0; g < GM; g++) {
+      float mx = sc[0][g];
+#pragma unroll
+      for (int it = 1; it < NIT; it++) mx = fmaxf(mx, sc[it][g]);
+#pragma unroll
+      for (int o = NC; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mn = fmaxf(m_w[g], mx);
       const float f = m_w[g] == -INFINITY ? 0.0f : expf(m_w[g] - mn);
-      pr[g] = valid ? expf(sc[g] - mn) : 0.0f;
-      l_w[g] = l_w[g] * f + warp_sum(half == 0 ? pr[g] : 0.0f);
+      float sum = 0.0f;
+#pragma unroll
+      for (int it = 0; it < NIT; it++) {
+        pr[it][g] = sc[it][g] == -INFINITY ? 0.0f : expf(sc[it][g] - mn);
+        sum += pr[it][g];
+      }
+#pragma unroll
+      for (int o = NC; o < 32; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      l_w[g] = l_w[g] * f + sum;
 #pragma unroll
       for (int e = 0; e < DPL; e++) acc[g][e] *= f;
       m_w[g] = mn;
     }
     // P.V over the warp's keys: lane owns dims [lane*DPL, +DPL)
     const int nk = min(KPW, rows - kbase);
-#pragma unroll 4
+#pragma unroll
     for (int kk = 0; kk < KPW; kk++) {
       if (kk >= nk) break;
       const uint8_t* vrow = Vs + (size_t)(kbase + kk) * ROWB;
@@ -615,21 +665,22 @@ __global__ void __launch_bounds__(256) attn_loop_kernel(const AttnArgs a) {
         }
       }
 #pragma unroll
-      for (int g = 0; g < kMaxG; g++) {
-        if (g >= G) break;
-        const float pk = __shfl_sync(0xffffffffu, pr[g], 2 * kk);
+      for (int g = 0; g < GM; g++) {
+        const float pk = __shfl_sync(0xffffffffu, pr[kk / KPI][g], (kk % KPI) * NC);
 #pragma unroll
         for (int e = 0; e < DPL; e++) acc[g][e] = fmaf(pk, v[e], acc[g][e]);
       }
     }
     __syncthreads();  // stage buffer consumed by every warp
     if (tid == 0 && st + 2 < nst) issue(st + 2);
+    ATT_TRACE(4 + min(st, 3));
   }
   if (!ok && a.err && tid == 0) atomicExch(a.err, 3);
+  ATT_TRACE(8);
   if (bad) return;
   // merge the warp states in warp order
 #pragma unroll
-  for (int g = 0; g < kMaxG; g++) {
+  for (int g = 0; g < GM; g++) {
     if (g >= G) break;
     if (lane == 0) {
       wpart[warp][g][0] = m_w[g];
@@ -659,6 +710,7 @@ __global__ void __launch_bounds__(256) attn_loop_kernel(const AttnArgs a) {
     else
       a.out[oi] = o;
   }
+  ATT_TRACE(9);
 }
 
 // causal prefill attention: grid (T, nq), 128 threads, dyn smem n floats
@@ -823,18 +875,26 @@ cudaError_t launch_attn_step_t(const AttnArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-template <bool BF, int HD>
-cudaError_t launch_attn_loop_t(const AttnArgs& a, cudaStream_t s) {
+template <bool BF, int HD, int GM>
+cudaError_t launch_attn_loop_g(const AttnArgs& a, cudaStream_t s) {
   const size_t smem = (size_t)2 * 2 * 128 * HD * (BF ? 2 : 4);
   static size_t configured = 0;
   if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_loop_kernel<BF, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(attn_loop_kernel<BF, HD, GM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
     configured = smem;
   }
-  CTTS_LK(launch_k(attn_loop_kernel<BF, HD>, dim3(a.nkv, a.batch), dim3(256), smem, s, a));
+  CTTS_LK(launch_k(attn_loop_kernel<BF, HD, GM>, dim3(a.nkv, a.batch), dim3(256), smem, s, a));
   return cudaGetLastError();
+}
+// query heads per KV head held in registers: 1, 2 or 4 (G <= 4)
+template <bool BF, int HD>
+cudaError_t launch_attn_loop_t(const AttnArgs& a, cudaStream_t s) {
+  const int G = a.nq / a.nkv;
+  if (G == 1) return launch_attn_loop_g<BF, HD, 1>(a, s);
+  if (G == 2) return launch_attn_loop_g<BF, HD, 2>(a, s);
+  return launch_attn_loop_g<BF, HD, 4>(a, s);
 }
 
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t s) {
@@ -844,9 +904,9 @@ cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t s) {
     return cudaErrorInvalidValue;
   // enough (utterance, kv head) pairs to fill the GPU: one CTA per pair
   // walking all its keys; otherwise split the keys over CTAs
-  if (a.batch * a.nkv >= 128 && (a.kv_bf16 || a.hd == 64)) {
+  if (a.batch * a.nkv >= 128 && (a.kv_bf16 || a.hd == 64) && G <= 4) {
     if (a.kv_bf16) return a.hd == 64 ? launch_attn_loop_t<true, 64>(a, s) : launch_attn_loop_t<true, 128>(a, s);
-    return a.hd == 64 ? launch_attn_loop_t<false, 64>(a, s) : launch_attn_loop_t<false, 128>(a, s);
+    return launch_attn_loop_t<false, 64>(a, s);  // fp32 rows of head_dim 64 only
   }
   if (a.kv_bf16) return a.hd == 64 ? launch_attn_step_t<true, 64>(a, s) : launch_attn_step_t<true, 128>(a, s);
   return a.hd == 64 ? launch_attn_step_t<false, 64>(a, s) : launch_attn_step_t<false, 128>(a, s);
@@ -901,3 +961,15 @@ cudaError_t launch_swiglu(const float* gu, int M, int F, float* out, cudaStream_
 }
 
 }  // namespace ctts
+
+#ifdef CTTS_ATT_TRACE
+// Copies the recorded timeline out and resets it.
+extern "C" __attribute__((visibility("default"))) int ctts_att_trace(long long* out, int* n) {
+  cudaMemcpyFromSymbol(n, ctts::g_att_trace_n, sizeof(int));
+  if (*n > 2047) *n = 2047;
+  cudaMemcpyFromSymbol(out, ctts::g_att_trace, sizeof(long long) * 4096);
+  int z = 0;
+  cudaMemcpyToSymbol(ctts::g_att_launch, &z, sizeof(int));
+  return cudaMemcpyToSymbol(ctts::g_att_trace_n, &z, sizeof(int)) == cudaSuccess ? 0 : -2;
+}
+#endif
