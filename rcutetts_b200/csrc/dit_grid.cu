@@ -77,8 +77,10 @@ CTTS_DEV void grid_sync(const DitGridArgs& a, int k) {
   __syncthreads();
   if (threadIdx.x == 0) {
     GRID_TRACE(2 * k);
-    __threadfence();
-    atomicAdd(a.bar + k, 1u);
+    // release (cumulative over the CTA's writes ordered before it by the
+    // block barrier) fused into the arrival; the acquiring poll orders the
+    // next phase's reads after every CTA's release
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar + k) : "memory");
     const unsigned n = gridDim.x;
     uint32_t it = 0;
     while (ld_acquire(a.bar + k) < n) {
@@ -88,7 +90,6 @@ CTTS_DEV void grid_sync(const DitGridArgs& a, int k) {
         break;
       }
     }
-    __threadfence();
     GRID_TRACE(2 * k + 1);
   }
   __syncthreads();
