@@ -176,10 +176,11 @@ extern "C" int ctts_kv_alloc(const ctts_lm* lm, int batch, int capacity, ctts_kv
   kv->act = kv->arena.alloc<float>((size_t)rows * c.ffn);
   kv->part = kv->arena.alloc<float>((size_t)batch * c.n_heads * kv->nsplit * (c.head_dim + 2));
   kv->cnt = kv->arena.alloc<int>((size_t)batch * c.n_kv_heads);
+  kv->gbar = kv->arena.alloc<unsigned>((size_t)ctts::lm_grid_counters(c.n_layers));
   kv->xin = kv->arena.alloc<float>((size_t)rows * H);
   kv->xout = kv->arena.alloc<float>((size_t)rows * H);
   if (!kv->k || !kv->v || !kv->pos || !kv->h || !kv->qkv || !kv->qrot || !kv->att || !kv->act ||
-      !kv->part || !kv->cnt || !kv->xin || !kv->xout) {
+      !kv->part || !kv->cnt || !kv->xin || !kv->xout || !kv->gbar) {
     delete kv;
     return set_error(CTTS_ERR_NOMEM, "KV cache allocation failed");
   }
@@ -263,6 +264,30 @@ int lm_forward_rows(ctts_lm* lm, ctts_kv* kv, int rows, int prefill_b, int pos0,
   auto fold_out = [&](TcArgs& e, const float* gain) {
     e.yb2 = kv->xb; e.g2 = gain; e.ssp = kv->ssp; e.ssp_ld = kv->ws_rows;
   };
+  // Small decode batches with fp32 weights: the whole step (every layer,
+  // the final norm and the position advance) as one grid-persistent launch
+  // (lm_grid.cu) unless CTTS_LM_GRID=0.
+  const char* grid_e = getenv("CTTS_LM_GRID");
+  if (prefill_b < 0 && !lm->bf16 && rows == kv->batch && (!grid_e || atoi(grid_e) != 0) &&
+      ctts::lm_grid_supported(rows, c.n_layers, H, c.n_heads, c.n_kv_heads, hd, F)) {
+    ctts::LmGridArgs g;
+    g.R = rows; g.NL = c.n_layers; g.H = H; g.nq = c.n_heads; g.nkv = c.n_kv_heads; g.hd = hd; g.F = F;
+    g.cap = kv->cap; g.eps = c.rms_eps;
+    g.h = kv->h; g.qkv = kv->qkv; g.att = kv->att; g.act = kv->act; g.out = out;
+    g.final_norm = lm->final_norm; g.pos = kv->pos; g.inv_freq = lm->inv_freq;
+    g.kcache = static_cast<float*>(kv->k); g.vcache = static_cast<float*>(kv->v); g.layer_elems = kv->layer_elems;
+    for (int l = 0; l < c.n_layers; l++) {
+      const LMLayer& L = lm->layers[l];
+      g.wqkv[l] = static_cast<const float*>(L.wqkv); g.wo[l] = static_cast<const float*>(L.wo);
+      g.wgu[l] = static_cast<const float*>(L.wgu); g.wd[l] = static_cast<const float*>(L.wd);
+      g.norm1[l] = L.norm1; g.norm2[l] = L.norm2;
+      g.qn[l] = c.qk_norm ? L.qn : nullptr; g.kn[l] = c.qk_norm ? L.kn : nullptr;
+    }
+    g.bar = kv->gbar; g.err = kv->err;
+    CTTS_CK(ctts::launch_lm_grid(g, s)); nl++;
+    if (launches) *launches += nl;
+    return CTTS_OK;
+  }
   for (int l = 0; l < c.n_layers; l++) {
     const LMLayer& L = lm->layers[l];
     if (tc) {

@@ -1,0 +1,548 @@
+// lm_grid.cu -- one LM decode step (every layer, the final RMSNorm and the
+// cache-length advance) as ONE grid-persistent launch for small batches
+// with fp32 weights (the batch-1 fp32 decode of config[2]).
+//
+// Replaces the per-layer launch chain of qwen.rs:229-406 decode_step
+// (fused QKV / attention / o-proj / gate-up / down launches, linear.cu and
+// attention.cu) at batch 1..4, where 60 dependent launches of a few
+// microseconds each dominate the step.  One CTA per SM (cooperative launch,
+// so every CTA is resident); phases are separated by grid barriers (a
+// global counter per barrier, zeroed again by the last CTA to leave):
+//   Q  RMSNorm1 (every CTA, all rows, redundant) -> this CTA's QKV columns
+//   A  one CTA per (utterance, query head): QK-Norm + RoPE of its query and
+//      of its KV head's new key, append of the new key/value row (the
+//      head group's first CTA), softmax attention over the cached rows plus
+//      the new one
+//   O  this CTA's o-proj columns + residual
+//   G  RMSNorm2 (redundant) -> this CTA's gate/up columns -> SwiGLU
+//   D  this CTA's down columns + residual
+// then the final RMSNorm and pos += 1.  Each GEMV column's weight row is
+// streamed from HBM into shared memory by bulk copies two phases ahead
+// (double-buffered), so the copies overlap the barriers and the phases in
+// between.  Intra-kernel data is read with L2-coherent loads (ld.global.cg).
+#include <cstdio>
+
+#include "common.cuh"
+#include "lm_grid.cuh"
+
+namespace ctts {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxRows = LmGridArgs::kMaxRows;
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+CTTS_DEV float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+CTTS_DEV uint32_t ld_acquire(const unsigned* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// grid barrier k: arrival as one release reduction (cumulative over this
+// CTA's writes, ordered before it by the block barrier), acquire polling
+CTTS_DEV void grid_sync(const LmGridArgs& a, int k) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar + k) : "memory");
+    const unsigned n = gridDim.x;
+    uint32_t it = 0;
+    while (ld_acquire(a.bar + k) < n) {
+      // a CTA that already gave up waiting somewhere makes every later wait
+      // end at once (a position error, code 1, does not stop the barriers)
+      if (++it == kSpinLimit || ((it & 1023u) == 0 && a.err && *reinterpret_cast<volatile int*>(a.err) == 4)) {
+        if (a.err) atomicExch(a.err, 4);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// ---- GEMV phases: kind, geometry, this CTA's output columns
+enum Kind { kQ = 0, kO = 1, kG = 2, kD = 3 };
+struct Geo {
+  int N, K, rows_per;  // output columns, weight row length, weight rows per column
+};
+CTTS_DEV Geo geo(const LmGridArgs& a, int kind) {
+  const int qkvw = (a.nq + 2 * a.nkv) * a.hd, qd = a.nq * a.hd;
+  switch (kind) {
+    case kQ: return {qkvw, a.H, 1};
+    case kO: return {a.H, qd, 1};
+    case kG: return {a.F, a.H, 2};
+    default: return {a.H, a.F, 1};
+  }
+}
+CTTS_DEV const float* weights(const LmGridArgs& a, int kind, int l) {
+  switch (kind) {
+    case kQ: return a.wqkv[l];
+    case kO: return a.wo[l];
+    case kG: return a.wgu[l];
+    default: return a.wd[l];
+  }
+}
+// weight row of output column n (row j of its rows_per): SwiGLU columns
+// pair gate row 128(n/64) + n%64 with the up row 64 further
+CTTS_DEV int weight_row(int kind, int n, int j) { return kind == kG ? 128 * (n / 64) + n % 64 + 64 * j : n; }
+__host__ __device__ inline void cols_of(int N, int b, int G, int& n0, int& n1) {
+  n0 = (int)(((long)N * b) / G);
+  n1 = (int)(((long)N * (b + 1)) / G);
+}
+
+// Shared memory: two weight staging buffers, the activation rows, the
+// attention scratch, two mbarriers.
+struct Smem {
+  size_t buf_bytes;  // one staging buffer
+  size_t xs_floats;  // activation rows [R][max K]
+  __host__ __device__ size_t xs_off() const { return 2 * buf_bytes; }
+  __host__ __device__ size_t att_off() const { return xs_off() + xs_floats * 4; }
+  // attention: q, new k, new v [3][hd], warp partials [8][hd + 2]
+  __host__ __device__ size_t att_floats(int hd) const { return (size_t)3 * hd + (size_t)kWarps * (hd + 2); }
+  __host__ __device__ size_t bar_off(int hd) const { return (att_off() + att_floats(hd) * 4 + 15) & ~size_t(15); }
+  __host__ __device__ size_t total(int hd) const { return bar_off(hd) + 16; }
+};
+__host__ __device__ inline Smem smem_of(int R, int H, int nq, int nkv, int hd, int F, int G) {
+  const int qkvw = (nq + 2 * nkv) * hd, qd = nq * hd;
+  const int N[4] = {qkvw, H, F, H}, K[4] = {H, qd, H, F}, rp[4] = {1, 1, 2, 1};
+  Smem m;
+  m.buf_bytes = 0;
+  for (int i = 0; i < 4; i++) {
+    const size_t cols = (size_t)(N[i] + G - 1) / G + 1;
+    const size_t b = cols * rp[i] * K[i] * 4;
+    if (b > m.buf_bytes) m.buf_bytes = b;
+  }
+  m.buf_bytes = (m.buf_bytes + 127) & ~size_t(127);
+  int kmax = H > qd ? H : qd;
+  if (F > kmax) kmax = F;
+  m.xs_floats = (size_t)R * kmax;
+  return m;
+}
+
+// Staging: thread 0 copies the weight rows of this CTA's columns of phase
+// `kind` of layer l into buffer b, completing on that buffer's mbarrier.
+struct Stage {
+  uint8_t* buf[2];
+  uint32_t bar[2];  // shared addresses
+  uint32_t ph[2];   // waits so far per buffer (parity of the next)
+};
+CTTS_DEV void stage(const LmGridArgs& a, Stage& st, int kind, int l, int b) {
+  if (threadIdx.x != 0) return;
+  const Geo g = geo(a, kind);
+  int n0, n1;
+  cols_of(g.N, blockIdx.x, gridDim.x, n0, n1);
+  const uint32_t row_bytes = (uint32_t)g.K * 4u;
+  const uint32_t bytes = (uint32_t)(n1 - n0) * g.rows_per * row_bytes;
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(st.bar[b]), "r"(bytes) : "memory");
+  const float* base = weights(a, kind, l);
+  const uint32_t dst0 = static_cast<uint32_t>(__cvta_generic_to_shared(st.buf[b]));
+  for (int n = n0; n < n1; n++)
+    for (int j = 0; j < g.rows_per; j++) {
+      const float* src = base + (size_t)weight_row(kind, n, j) * g.K;
+      const uint32_t dst = dst0 + (uint32_t)((n - n0) * g.rows_per + j) * row_bytes;
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       dst),
+                   "l"(src), "r"(row_bytes), "r"(st.bar[b])
+                   : "memory");
+    }
+}
+CTTS_DEV void wait_stage(const LmGridArgs& a, Stage& st, int b) {
+  bool done = false;
+  for (uint32_t it = 0; it < kSpinLimit && !done; ++it) {
+    uint32_t d;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(d)
+        : "r"(st.bar[b]), "r"(st.ph[b] & 1u)
+        : "memory");
+    done = d != 0;
+  }
+  if (!done && threadIdx.x == 0 && a.err) atomicExch(a.err, 4);
+  st.ph[b]++;
+}
+
+// RMSNorm of the R rows of h (every CTA, one warp per row) -> xs[r][H]
+// (x * inv * gain, prep/linear_rows semantics)
+CTTS_DEV void norm_rows(const LmGridArgs& a, const float* gain, float* xs) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, H = a.H;
+  for (int r = warp; r < a.R; r += kWarps) {
+    const float* src = a.h + (size_t)r * H;
+    float* dst = xs + (size_t)r * H;
+    float ss = 0.0f;
+    for (int k = lane * 4; k < H; k += 128) {
+      const float4 v = ldcg4(src + k);
+      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+      *reinterpret_cast<float4*>(dst + k) = v;
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)H + a.eps);
+    for (int k = lane * 4; k < H; k += 128) {
+      float4 v = *reinterpret_cast<float4*>(dst + k);
+      v.x = v.x * inv * gain[k];
+      v.y = v.y * inv * gain[k + 1];
+      v.z = v.z * inv * gain[k + 2];
+      v.w = v.w * inv * gain[k + 3];
+      *reinterpret_cast<float4*>(dst + k) = v;
+    }
+  }
+}
+
+// n floats of intra-kernel data (global, L2-coherent) -> xs
+CTTS_DEV void load_rows(const float* src, int n, float* xs) {
+  for (int i = threadIdx.x * 4; i < n; i += kThreads * 4)
+    *reinterpret_cast<float4*>(xs + i) = ldcg4(src + i);
+}
+
+// This CTA's output columns of phase `kind`: warp per column, lanes over
+// 4-element groups of K, the R rows of xs [R][K] advancing together.
+CTTS_DEV void gemv(const LmGridArgs& a, Stage& st, int kind, int b, const float* xs) {
+  const Geo g = geo(a, kind);
+  int n0, n1;
+  cols_of(g.N, blockIdx.x, gridDim.x, n0, n1);
+  wait_stage(a, st, b);
+  __syncthreads();  // xs complete
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, K = g.K, R = a.R;
+  for (int n = n0 + warp; n < n1; n += kWarps) {
+    float acc[2][kMaxRows];
+#pragma unroll
+    for (int j = 0; j < 2; j++)
+#pragma unroll
+      for (int r = 0; r < kMaxRows; r++) acc[j][r] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      if (j >= g.rows_per) break;
+      const float* w = reinterpret_cast<const float*>(st.buf[b]) + ((size_t)(n - n0) * g.rows_per + j) * K;
+      for (int k = lane * 4; k < K; k += 128) {
+        const float4 wv = *reinterpret_cast<const float4*>(w + k);
+#pragma unroll
+        for (int r = 0; r < kMaxRows; r++) {
+          if (r >= R) break;
+          const float4 xv = *reinterpret_cast<const float4*>(xs + (size_t)r * K + k);
+          acc[j][r] = fmaf(wv.x, xv.x, fmaf(wv.y, xv.y, fmaf(wv.z, xv.z, fmaf(wv.w, xv.w, acc[j][r]))));
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 2; j++)
+#pragma unroll
+      for (int r = 0; r < kMaxRows; r++)
+        if (j < g.rows_per && r < R) acc[j][r] = warp_sum(acc[j][r]);
+    if (lane == 0) {
+      const int qkvw = (a.nq + 2 * a.nkv) * a.hd;
+#pragma unroll
+      for (int r = 0; r < kMaxRows; r++) {
+        if (r >= R) break;
+        if (kind == kQ) {
+          a.qkv[(size_t)r * qkvw + n] = acc[0][r];
+        } else if (kind == kG) {
+          a.act[(size_t)r * a.F + n] = silu(acc[0][r]) * acc[1][r];
+        } else {  // o-proj / down: residual
+          float* y = a.h + (size_t)r * a.H + n;
+          *y = __ldcg(y) + acc[0][r];
+        }
+      }
+    }
+  }
+}
+
+// Attention of one (utterance, query head) per CTA (CTAs past R * nq idle):
+// warps 0..2 prepare the query and the KV head's new key and value (QK-Norm,
+// RoPE at the utterance's position; the head group's first query head
+// appends key and value to the cache), then warp w walks keys w, w + 8, ...
+// with its own online softmax (lane = HD/32 consecutive dims, scores by warp
+// reduction), the warp states merging in warp order.
+template <int HD>
+CTTS_DEV void attn_phase(const LmGridArgs& a, int l, float* sa) {
+  const int jobs = a.R * a.nq;
+  if ((int)blockIdx.x >= jobs) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x / a.nq, hq = blockIdx.x % a.nq, G = a.nq / a.nkv, kvh = hq / G;
+  const int qd = a.nq * HD, qkvw = (a.nq + 2 * a.nkv) * HD;
+  const int p = a.pos[b];
+  float* att_out = a.att + (size_t)b * qd + (size_t)hq * HD;
+  if (p < 0 || p >= a.cap) {
+    if (threadIdx.x == 0 && a.err) atomicExch(a.err, 1);
+    for (int d = threadIdx.x; d < HD; d += kThreads) att_out[d] = 0.0f;
+    return;
+  }
+  constexpr int PER = HD / 32, DPL = HD / 32;
+  float* qv = sa;
+  float* knew = sa + HD;
+  float* vnew = sa + 2 * HD;
+  float* wpart = sa + 3 * HD;  // [8][HD + 2]
+  const float* kc = a.kcache + (size_t)l * a.layer_elems;
+  const float* vc = a.vcache + (size_t)l * a.layer_elems;
+  const size_t row0 = ((size_t)b * a.nkv + kvh) * a.cap;
+  if (warp < 3) {
+    const float* src =
+        a.qkv + (size_t)b * qkvw + (size_t)(warp == 0 ? hq : warp == 1 ? a.nq + kvh : a.nq + a.nkv + kvh) * HD;
+    float v[PER];
+#pragma unroll
+    for (int j = 0; j < PER; j++) v[j] = __ldcg(src + lane + 32 * j);
+    if (warp < 2) {
+      const float* gn = warp == 0 ? a.qn[l] : a.kn[l];
+      if (gn) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < PER; j++) ss = fmaf(v[j], v[j], ss);
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+#pragma unroll
+        for (int j = 0; j < PER; j++) v[j] = v[j] * inv * gn[lane + 32 * j];
+      }
+#pragma unroll
+      for (int j = 0; j < PER / 2; j++) {  // rotate-half pairs (i, i + HD/2)
+        const int i = lane + 32 * j;
+        float sn, cs;
+        sincosf((float)p * a.inv_freq[i], &sn, &cs);
+        const float x1 = v[j], x2 = v[j + PER / 2];
+        v[j] = x1 * cs - x2 * sn;
+        v[j + PER / 2] = x1 * sn + x2 * cs;
+      }
+    }
+    float* dst = warp == 0 ? qv : warp == 1 ? knew : vnew;
+    float* cache = warp == 1 ? a.kcache : a.vcache;
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+      const int d = lane + 32 * j;
+      if (warp > 0 && hq % G == 0) cache[(size_t)l * a.layer_elems + (row0 + p) * HD + d] = v[j];
+      dst[d] = v[j];
+    }
+  }
+  __syncthreads();
+  float q[DPL];
+#pragma unroll
+  for (int e = 0; e < DPL; e++) q[e] = qv[DPL * lane + e];
+  const float scale = 1.0f / sqrtf((float)HD);
+  float m = -INFINITY, lsum = 0.0f, acc[DPL];
+#pragma unroll
+  for (int e = 0; e < DPL; e++) acc[e] = 0.0f;
+  // key/value row j of this (utterance, KV head): cached rows from global
+  // memory (written by earlier launches), the new row from shared memory
+  auto load_row = [&](const float* cache, const float* fresh, int j, float* out) {
+    if (j == p) {
+#pragma unroll
+      for (int e = 0; e < DPL; e++) out[e] = fresh[DPL * lane + e];
+      return;
+    }
+    const float* rp = cache + (row0 + j) * HD + (size_t)DPL * lane;
+    if constexpr (DPL == 2) {
+      const float2 t = *reinterpret_cast<const float2*>(rp);
+      out[0] = t.x; out[1] = t.y;
+    } else {
+      const float4 t = *reinterpret_cast<const float4*>(rp);
+      out[0] = t.x; out[1] = t.y; out[2] = t.z; out[3] = t.w;
+    }
+  };
+  constexpr int U = 4;  // keys in flight per warp
+  for (int j0 = warp; j0 <= p; j0 += kWarps * U) {
+    float kk[U][DPL], vv[U][DPL], s[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int j = j0 + kWarps * u;
+      if (j <= p) {
+        load_row(kc, knew, j, kk[u]);
+        load_row(vc, vnew, j, vv[u]);
+      } else {  // past the last key: weight 0, and 0 x (stale register) must not be NaN
+#pragma unroll
+        for (int e = 0; e < DPL; e++) kk[u][e] = vv[u][e] = 0.0f;
+      }
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int j = j0 + kWarps * u;
+      float d = 0.0f;
+      if (j <= p) {
+#pragma unroll
+        for (int e = 0; e < DPL; e++) d = fmaf(q[e], kk[u][e], d);
+      }
+      d = warp_sum(d);
+      s[u] = j <= p ? d * scale : -INFINITY;
+      mx = fmaxf(mx, s[u]);
+    }
+    const float mn = fmaxf(m, mx);
+    const float f = m == -INFINITY ? 0.0f : expf(m - mn);
+    lsum *= f;
+#pragma unroll
+    for (int e = 0; e < DPL; e++) acc[e] *= f;
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const float pu = s[u] == -INFINITY ? 0.0f : expf(s[u] - mn);
+      lsum += pu;
+#pragma unroll
+      for (int e = 0; e < DPL; e++) acc[e] = fmaf(pu, vv[u][e], acc[e]);
+    }
+    m = mn;
+  }
+  if (lane == 0) {
+    wpart[warp * (HD + 2)] = m;
+    wpart[warp * (HD + 2) + 1] = lsum;
+  }
+#pragma unroll
+  for (int e = 0; e < DPL; e++) wpart[warp * (HD + 2) + 2 + DPL * lane + e] = acc[e];
+  __syncthreads();
+  for (int d = threadIdx.x; d < HD; d += kThreads) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) M = fmaxf(M, wpart[w * (HD + 2)]);
+    float L = 0.0f, o = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) {
+      const float mw = wpart[w * (HD + 2)];
+      const float fw = mw == -INFINITY ? 0.0f : expf(mw - M);
+      L = fmaf(wpart[w * (HD + 2) + 1], fw, L);
+      o = fmaf(wpart[w * (HD + 2) + 2 + d], fw, o);
+    }
+    att_out[d] = o / L;
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1) lm_grid_kernel(const LmGridArgs a) {
+  extern __shared__ __align__(128) uint8_t smraw[];
+  const Smem m = smem_of(a.R, a.H, a.nq, a.nkv, HD, a.F, gridDim.x);
+  Stage st;
+  st.buf[0] = smraw;
+  st.buf[1] = smraw + m.buf_bytes;
+  float* xs = reinterpret_cast<float*>(smraw + m.xs_off());
+  float* sa = reinterpret_cast<float*>(smraw + m.att_off());
+  st.bar[0] = static_cast<uint32_t>(__cvta_generic_to_shared(smraw + m.bar_off(HD)));
+  st.bar[1] = st.bar[0] + 8u;
+  st.ph[0] = st.ph[1] = 0u;
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(st.bar[0]));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(st.bar[1]));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  // weight phases Q, O, G, D of every layer alternate buffers 0, 1, 0, 1;
+  // each buffer is refilled two weight phases ahead, as soon as its phase
+  // has been computed
+  stage(a, st, kQ, 0, 0);
+  stage(a, st, kO, 0, 1);
+  const int qd = a.nq * HD;
+  int k = 0;
+  for (int l = 0; l < a.NL; l++) {
+    norm_rows(a, a.norm1[l], xs);
+    gemv(a, st, kQ, 0, xs);
+    __syncthreads();
+    stage(a, st, kG, l, 0);
+    grid_sync(a, k++);
+    attn_phase<HD>(a, l, sa);
+    grid_sync(a, k++);
+    load_rows(a.att, a.R * qd, xs);
+    gemv(a, st, kO, 1, xs);
+    __syncthreads();
+    stage(a, st, kD, l, 1);
+    grid_sync(a, k++);
+    norm_rows(a, a.norm2[l], xs);
+    gemv(a, st, kG, 0, xs);
+    __syncthreads();
+    if (l + 1 < a.NL) stage(a, st, kQ, l + 1, 0);
+    grid_sync(a, k++);
+    load_rows(a.act, a.R * a.F, xs);
+    gemv(a, st, kD, 1, xs);
+    __syncthreads();
+    if (l + 1 < a.NL) stage(a, st, kO, l + 1, 1);
+    grid_sync(a, k++);
+  }
+  // final RMSNorm of the last layer's rows and the cache-length advance
+  // (every CTA is past its last attention phase)
+  if (blockIdx.x == 0) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, H = a.H;
+    for (int r = warp; r < a.R; r += kWarps) {
+      const float* src = a.h + (size_t)r * H;
+      float ss = 0.0f;
+      for (int c = lane * 4; c < H; c += 128) {
+        const float4 v = ldcg4(src + c);
+        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+      }
+      ss = warp_sum(ss);
+      const float inv = 1.0f / sqrtf(ss / (float)H + a.eps);
+      for (int c = lane * 4; c < H; c += 128) {
+        const float4 v = ldcg4(src + c);
+        *reinterpret_cast<float4*>(a.out + (size_t)r * H + c) =
+            make_float4(v.x * inv * a.final_norm[c], v.y * inv * a.final_norm[c + 1], v.z * inv * a.final_norm[c + 2],
+                        v.w * inv * a.final_norm[c + 3]);
+      }
+    }
+    if (threadIdx.x < a.R) a.pos[threadIdx.x] += 1;
+  }
+  // the last CTA to leave zeroes the counters for the next launch
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(a.bar + k, 1u) == gridDim.x - 1) {
+      for (int i = 0; i <= k; i++) a.bar[i] = 0u;
+      __threadfence();
+    }
+  }
+}
+
+int grid_ctas() {
+  static int n = -1;
+  if (n < 0) {
+    int dev = 0, sms = 0, coop = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
+    n = coop ? sms : 0;
+  }
+  return n;
+}
+
+template <int HD>
+cudaError_t launch_t(const LmGridArgs& a, size_t smem, cudaStream_t s) {
+  auto kern = lm_grid_kernel<HD>;
+  static size_t configured = 0;
+  if (smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+  if (e != cudaSuccess || per_sm < 1) return e != cudaSuccess ? e : cudaErrorInvalidConfiguration;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid_ctas());
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the grid barriers need it
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (e != cudaSuccess) (void)cudaGetLastError();
+  return e;
+}
+
+}  // namespace
+
+int lm_grid_counters(int NL) { return 5 * NL + 1; }
+
+bool lm_grid_supported(int R, int NL, int H, int nq, int nkv, int hd, int F) {
+  if (R < 1 || R > LmGridArgs::kMaxRows || NL < 1 || NL > LmGridArgs::kMaxNL) return false;
+  if ((hd != 64 && hd != 128) || nkv < 1 || nq % nkv || H % 128 || F % 128 || (nq * hd) % 128 ||
+      ((nq + 2 * nkv) * hd) % 4)
+    return false;
+  const int G = grid_ctas();
+  if (G <= 0 || R * nq > G) return false;
+  return smem_of(R, H, nq, nkv, hd, F, G).total(hd) <= 220 * 1024;
+}
+
+cudaError_t launch_lm_grid(const LmGridArgs& a, cudaStream_t s) {
+  if (!lm_grid_supported(a.R, a.NL, a.H, a.nq, a.nkv, a.hd, a.F) || !a.bar || !a.h || !a.out || !a.pos)
+    return cudaErrorInvalidValue;
+  const size_t smem = smem_of(a.R, a.H, a.nq, a.nkv, a.hd, a.F, grid_ctas()).total(a.hd);
+  return a.hd == 64 ? launch_t<64>(a, smem, s) : launch_t<128>(a, smem, s);
+}
+
+}  // namespace ctts

@@ -7,6 +7,7 @@
 #include "api_common.h"
 #include "dit_cluster.cuh"
 #include "dit_grid.cuh"
+#include "lm_grid.cuh"
 
 // LM stack (replaces QwenW, qwen.rs:26-44).  Weights of a layer are fused
 // into wide matrices at load: [q;k;v] -> wqkv, [gate;up] -> wgu, so one
@@ -36,6 +37,7 @@ struct ctts_kv {
   const ctts_lm* lm = nullptr;
   int batch = 0, cap = 0, nsplit = 0, chunk = 128, ws_rows = 0;
   int* cnt = nullptr;  // decode-attention split tickets [batch][n_kv_heads]
+  unsigned* gbar = nullptr;  // grid-persistent decode step barrier counters (zero at rest)
   float* ssp = nullptr;  // residual-row sum-of-squares partials [hidden/128][ws_rows]
   size_t layer_elems = 0;
   ctts::DevArena arena;

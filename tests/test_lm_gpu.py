@@ -207,3 +207,36 @@ def test_large_batch_decode_stage_boundaries(dtype, B):
                 assert rel_err(outs[s][b], ref[s]) < 1e-4, (b, s)
             else:
                 assert cosine(outs[s][b], ref[s]) >= 0.999, (b, s)
+
+
+@pytest.mark.parametrize("batch,cfg", [
+    (1, LMConfig()),
+    (3, LMConfig(n_layers=4)),
+    (2, LMConfig(hidden=768, n_layers=2, n_heads=8, n_kv_heads=4, head_dim=128, ffn=1536)),
+])
+def test_grid_decode_matches_launch_chain(monkeypatch, batch, cfg):
+    """Small-batch fp32 decode as one grid-persistent launch (lm_grid.cu)
+    against the per-layer launch chain (CTTS_LM_GRID=0): ragged prefills in
+    both length orders, several steps, the cache lengths left behind, and the
+    oracle per utterance."""
+    from rcutetts_b200.model import QwenCache, decode_step, prefill
+
+    m, w = lm_model(cfg, seed=70)
+    for lens in ([4 + 5 * b for b in range(batch)], [14 - 5 * b for b in range(batch)]):
+        pre = [rnd(700 + b, (lens[b], cfg.hidden)) for b in range(batch)]
+        dec = rnd(720, (4, batch, cfg.hidden))
+        outs = {}
+        for grid in ("1", "0"):
+            monkeypatch.setenv("CTTS_LM_GRID", grid)
+            cache = QwenCache(m, batch=batch, capacity=40)
+            for b in range(batch):
+                prefill(m, pre[b], cache, b)
+            outs[grid] = np.stack([decode_step(m, dec[s], cache) for s in range(4)])
+            for b in range(batch):
+                assert cache.len(b) == lens[b] + 4
+        assert np.isfinite(outs["1"]).all()
+        assert rel_err(outs["1"], outs["0"]) < 1e-4
+        for b in range(batch):
+            ref = run_oracle(cfg, w, pre[b], dec[:, b, :], capacity=40)[lens[b]:]
+            for s in range(4):
+                assert rel_err(outs["1"][s, b], ref[s]) < 1e-4, (lens, b, s)
