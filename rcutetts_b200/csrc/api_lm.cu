@@ -177,10 +177,11 @@ extern "C" int ctts_kv_alloc(const ctts_lm* lm, int batch, int capacity, ctts_kv
   kv->part = kv->arena.alloc<float>((size_t)batch * c.n_heads * kv->nsplit * (c.head_dim + 2));
   kv->cnt = kv->arena.alloc<int>((size_t)batch * c.n_kv_heads);
   kv->gbar = kv->arena.alloc<unsigned>((size_t)ctts::lm_grid_counters(c.n_layers));
+  kv->gpart = kv->arena.alloc<float>(ctts::lm_grid_part_floats(c.head_dim));
   kv->xin = kv->arena.alloc<float>((size_t)rows * H);
   kv->xout = kv->arena.alloc<float>((size_t)rows * H);
   if (!kv->k || !kv->v || !kv->pos || !kv->h || !kv->qkv || !kv->qrot || !kv->att || !kv->act ||
-      !kv->part || !kv->cnt || !kv->xin || !kv->xout || !kv->gbar) {
+      !kv->part || !kv->cnt || !kv->xin || !kv->xout || !kv->gbar || !kv->gpart) {
     delete kv;
     return set_error(CTTS_ERR_NOMEM, "KV cache allocation failed");
   }
@@ -273,7 +274,7 @@ int lm_forward_rows(ctts_lm* lm, ctts_kv* kv, int rows, int prefill_b, int pos0,
     ctts::LmGridArgs g;
     g.R = rows; g.NL = c.n_layers; g.H = H; g.nq = c.n_heads; g.nkv = c.n_kv_heads; g.hd = hd; g.F = F;
     g.cap = kv->cap; g.eps = c.rms_eps;
-    g.h = kv->h; g.qkv = kv->qkv; g.att = kv->att; g.act = kv->act; g.out = out;
+    g.h = kv->h; g.qkv = kv->qkv; g.part = kv->gpart; g.act = kv->act; g.out = out;
     g.final_norm = lm->final_norm; g.pos = kv->pos; g.inv_freq = lm->inv_freq;
     g.kcache = static_cast<float*>(kv->k); g.vcache = static_cast<float*>(kv->v); g.layer_elems = kv->layer_elems;
     for (int l = 0; l < c.n_layers; l++) {

@@ -255,26 +255,32 @@ CTTS_DEV uint32_t stage_aux(const DitGridArgs& a, Stage& st, int kind, int l, in
   return bytes;
 }
 
+// warp 0: lane 0 arms the mbarrier with the phase's byte count and copies
+// the small operands, the lanes issue one weight row copy each (a serial
+// issue by one thread delays its barrier arrival by microseconds)
 CTTS_DEV void stage_weights(const DitGridArgs& a, Stage& st, int kind, int l, int stn = 0) {
-  if (threadIdx.x == 0) {
-    const KindGeom g = geom(a, kind, l);
-    int n0, n1;
-    my_cols(g.N, n0, n1);
-    const uint32_t row_bytes = (uint32_t)g.K * 4u;
-    const uint32_t bytes = (uint32_t)(n1 - n0) * g.rows_per * row_bytes + stage_aux(a, st, kind, l, stn, false);
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  const KindGeom g = geom(a, kind, l);
+  int n0, n1;
+  my_cols(g.N, n0, n1);
+  const uint32_t row_bytes = (uint32_t)g.K * 4u;
+  const int rows = (n1 - n0) * g.rows_per;
+  if (lane == 0) {
+    const uint32_t bytes = (uint32_t)rows * row_bytes + stage_aux(a, st, kind, l, stn, false);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(st.bar), "r"(bytes) : "memory");
     stage_aux(a, st, kind, l, stn, true);
-    const uint32_t dst0 = static_cast<uint32_t>(__cvta_generic_to_shared(st.wbuf));
-    for (int n = n0; n < n1; n++)
-      for (int j = 0; j < g.rows_per; j++) {
-        const float* src = g.base + (size_t)weight_row(a, kind, n, j) * g.K;
-        const uint32_t dst = dst0 + (uint32_t)(((n - n0) * g.rows_per + j)) * row_bytes;
-        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                         dst),
-                     "l"(src), "r"(row_bytes), "r"(st.bar)
-                     : "memory");
-      }
+  }
+  __syncwarp();
+  const uint32_t dst0 = static_cast<uint32_t>(__cvta_generic_to_shared(st.wbuf));
+  for (int i = lane; i < rows; i += 32) {
+    const int n = n0 + i / g.rows_per, j = i % g.rows_per;
+    const float* src = g.base + (size_t)weight_row(a, kind, n, j) * g.K;
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     dst0 + (uint32_t)i * row_bytes),
+                 "l"(src), "r"(row_bytes), "r"(st.bar)
+                 : "memory");
   }
 }
 

@@ -9,11 +9,12 @@
 // so every CTA is resident); phases are separated by grid barriers (a
 // global counter per barrier, zeroed again by the last CTA to leave):
 //   Q  RMSNorm1 (every CTA, all rows, redundant) -> this CTA's QKV columns
-//   A  one CTA per (utterance, query head): QK-Norm + RoPE of its query and
-//      of its KV head's new key, append of the new key/value row (the
-//      head group's first CTA), softmax attention over the cached rows plus
-//      the new one
-//   O  this CTA's o-proj columns + residual
+//   A  every (utterance, query head) over gridDim / (R nq) CTAs, each a
+//      contiguous range of the keys: QK-Norm + RoPE of the query and of the
+//      new key, append of the new key/value row (the head group's first
+//      query head), online-softmax partials per range
+//   O  the ranges' partials merged (every CTA) -> this CTA's o-proj
+//      columns + residual
 //   G  RMSNorm2 (redundant) -> this CTA's gate/up columns -> SwiGLU
 //   D  this CTA's down columns + residual
 // then the final RMSNorm and pos += 1.  Each GEMV column's weight row is
@@ -33,6 +34,7 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxRows = LmGridArgs::kMaxRows;
 constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr int kMaxCtas = 1024;  // grid size bound (one CTA per SM)
 
 CTTS_DEV float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
@@ -100,7 +102,11 @@ struct Smem {
   __host__ __device__ size_t xs_off() const { return 2 * buf_bytes; }
   __host__ __device__ size_t att_off() const { return xs_off() + xs_floats * 4; }
   // attention: q, new k, new v [3][hd], warp partials [8][hd + 2]
-  __host__ __device__ size_t att_floats(int hd) const { return (size_t)3 * hd + (size_t)kWarps * (hd + 2); }
+  // (the o-proj phase reuses it for the attention merge factors, one per CTA: kMaxCtas)
+  __host__ __device__ size_t att_floats(int hd) const {
+    const size_t f = (size_t)3 * hd + (size_t)kWarps * (hd + 2);
+    return f > (size_t)kMaxCtas ? f : (size_t)kMaxCtas;
+  }
   __host__ __device__ size_t bar_off(int hd) const { return (att_off() + att_floats(hd) * 4 + 15) & ~size_t(15); }
   __host__ __device__ size_t total(int hd) const { return bar_off(hd) + 16; }
 };
@@ -121,33 +127,47 @@ __host__ __device__ inline Smem smem_of(int R, int H, int nq, int nkv, int hd, i
   return m;
 }
 
-// Staging: thread 0 copies the weight rows of this CTA's columns of phase
-// `kind` of layer l into buffer b, completing on that buffer's mbarrier.
+// Staging: warp 0 copies the weight rows of this CTA's columns of phase
+// `kind` of layer l into buffer b as a few large bulk copies (lane 0 arms
+// the buffer's mbarrier with the byte count), completing on the buffer's
+// mbarrier.  A CTA's columns are consecutive weight rows, except that the
+// gate/up rows of SwiGLU columns sit in 64-row tiles (gate rows
+// 128(n/64) + n%64, up rows 64 further): per 64-column segment one gate and
+// one up copy.  Buffer layout: [j][column - n0][K] (j: gate, up).
 struct Stage {
   uint8_t* buf[2];
   uint32_t bar[2];  // shared addresses
   uint32_t ph[2];   // waits so far per buffer (parity of the next)
 };
 CTTS_DEV void stage(const LmGridArgs& a, Stage& st, int kind, int l, int b) {
-  if (threadIdx.x != 0) return;
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
   const Geo g = geo(a, kind);
   int n0, n1;
   cols_of(g.N, blockIdx.x, gridDim.x, n0, n1);
-  const uint32_t row_bytes = (uint32_t)g.K * 4u;
-  const uint32_t bytes = (uint32_t)(n1 - n0) * g.rows_per * row_bytes;
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(st.bar[b]), "r"(bytes) : "memory");
+  const uint32_t row_bytes = (uint32_t)g.K * 4u, cols = (uint32_t)(n1 - n0);
+  if (lane == 0) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(st.bar[b]),
+                 "r"(cols * g.rows_per * row_bytes)
+                 : "memory");
+  }
+  __syncwarp();
   const float* base = weights(a, kind, l);
   const uint32_t dst0 = static_cast<uint32_t>(__cvta_generic_to_shared(st.buf[b]));
-  for (int n = n0; n < n1; n++)
-    for (int j = 0; j < g.rows_per; j++) {
-      const float* src = base + (size_t)weight_row(kind, n, j) * g.K;
-      const uint32_t dst = dst0 + (uint32_t)((n - n0) * g.rows_per + j) * row_bytes;
-      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                       dst),
-                   "l"(src), "r"(row_bytes), "r"(st.bar[b])
-                   : "memory");
-    }
+  // copy c: segment c / rows_per of the column range, row set j = c % rows_per
+  const int seg0 = kind == kG ? n0 / 64 : 0;
+  const int nseg = kind == kG ? (n1 > n0 ? (n1 - 1) / 64 - seg0 + 1 : 0) : (n1 > n0 ? 1 : 0);
+  for (int c = lane; c < nseg * g.rows_per; c += 32) {
+    const int sg = c / g.rows_per, j = c % g.rows_per;
+    const int a0 = kind == kG ? max(n0, 64 * (seg0 + sg)) : n0;
+    const int a1 = kind == kG ? min(n1, 64 * (seg0 + sg + 1)) : n1;
+    const float* src = base + (size_t)weight_row(kind, a0, j) * g.K;
+    const uint32_t dst = dst0 + ((uint32_t)j * cols + (uint32_t)(a0 - n0)) * row_bytes;
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"((uint32_t)(a1 - a0) * row_bytes), "r"(st.bar[b])
+                 : "memory");
+  }
 }
 CTTS_DEV void wait_stage(const LmGridArgs& a, Stage& st, int b) {
   bool done = false;
@@ -167,27 +187,33 @@ CTTS_DEV void wait_stage(const LmGridArgs& a, Stage& st, int b) {
 }
 
 // RMSNorm of the R rows of h (every CTA, one warp per row) -> xs[r][H]
-// (x * inv * gain, prep/linear_rows semantics)
+// (x * inv * gain, prep/linear_rows semantics); every load of the row is
+// issued before the first use (H <= 128 * kMaxH4)
+constexpr int kMaxH4 = 8;
 CTTS_DEV void norm_rows(const LmGridArgs& a, const float* gain, float* xs) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, H = a.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, H = a.H, nv = H >> 7;
   for (int r = warp; r < a.R; r += kWarps) {
     const float* src = a.h + (size_t)r * H;
     float* dst = xs + (size_t)r * H;
+    float4 v[kMaxH4], gv[kMaxH4];  // the row and the gains, all loads in flight together
+#pragma unroll
+    for (int i = 0; i < kMaxH4; i++)
+      if (i < nv) {
+        v[i] = ldcg4(src + lane * 4 + 128 * i);
+        gv[i] = *reinterpret_cast<const float4*>(gain + lane * 4 + 128 * i);
+      }
     float ss = 0.0f;
-    for (int k = lane * 4; k < H; k += 128) {
-      const float4 v = ldcg4(src + k);
-      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
-      *reinterpret_cast<float4*>(dst + k) = v;
-    }
+#pragma unroll
+    for (int i = 0; i < kMaxH4; i++)
+      if (i < nv) ss = fmaf(v[i].x, v[i].x, fmaf(v[i].y, v[i].y, fmaf(v[i].z, v[i].z, fmaf(v[i].w, v[i].w, ss))));
     ss = warp_sum(ss);
     const float inv = 1.0f / sqrtf(ss / (float)H + a.eps);
-    for (int k = lane * 4; k < H; k += 128) {
-      float4 v = *reinterpret_cast<float4*>(dst + k);
-      v.x = v.x * inv * gain[k];
-      v.y = v.y * inv * gain[k + 1];
-      v.z = v.z * inv * gain[k + 2];
-      v.w = v.w * inv * gain[k + 3];
-      *reinterpret_cast<float4*>(dst + k) = v;
+#pragma unroll
+    for (int i = 0; i < kMaxH4; i++) {
+      if (i >= nv) break;
+      const int k = lane * 4 + 128 * i;
+      *reinterpret_cast<float4*>(dst + k) = make_float4(v[i].x * inv * gv[i].x, v[i].y * inv * gv[i].y,
+                                                        v[i].z * inv * gv[i].z, v[i].w * inv * gv[i].w);
     }
   }
 }
@@ -216,7 +242,7 @@ CTTS_DEV void gemv(const LmGridArgs& a, Stage& st, int kind, int b, const float*
 #pragma unroll
     for (int j = 0; j < 2; j++) {
       if (j >= g.rows_per) break;
-      const float* w = reinterpret_cast<const float*>(st.buf[b]) + ((size_t)(n - n0) * g.rows_per + j) * K;
+      const float* w = reinterpret_cast<const float*>(st.buf[b]) + ((size_t)j * (n1 - n0) + (n - n0)) * K;
       for (int k = lane * 4; k < K; k += 128) {
         const float4 wv = *reinterpret_cast<const float4*>(w + k);
 #pragma unroll
@@ -250,26 +276,39 @@ CTTS_DEV void gemv(const LmGridArgs& a, Stage& st, int kind, int b, const float*
   }
 }
 
-// Attention of one (utterance, query head) per CTA (CTAs past R * nq idle):
-// warps 0..2 prepare the query and the KV head's new key and value (QK-Norm,
-// RoPE at the utterance's position; the head group's first query head
-// appends key and value to the cache), then warp w walks keys w, w + 8, ...
-// with its own online softmax (lane = HD/32 consecutive dims, scores by warp
-// reduction), the warp states merging in warp order.
+// Attention, keys split over CTAs: job = (utterance, query head), S =
+// gridDim / jobs CTAs per job, CTA s of a job walks the contiguous key range
+// s of the job's p + 1 keys (cached rows 0..p-1 and the new row p, which the
+// last range holds).  Warp 0 prepares the query (QK-Norm + RoPE at the
+// utterance's position); in the last range warps 1, 2 prepare the new key
+// and value and the head group's first query head appends them to the
+// cache.  Warp w walks keys j0 + w, j0 + w + 8, ... with its own online
+// softmax (lane = HD/32 consecutive dims, scores by warp reduction); the
+// warp states merge in warp order into this CTA's partial
+// part[cta] = (max, sum, acc[HD]), merged across ranges by merge_attn.
+constexpr int kMaxSplits = 8;  // key ranges per job (the merge reads them all)
+CTTS_DEV int attn_splits(const LmGridArgs& a) {
+  const int jobs = a.R * a.nq;
+  const int S = (int)gridDim.x / jobs;
+  return S < 1 ? 1 : S > kMaxSplits ? kMaxSplits : S;
+}
 template <int HD>
 CTTS_DEV void attn_phase(const LmGridArgs& a, int l, float* sa) {
-  const int jobs = a.R * a.nq;
-  if ((int)blockIdx.x >= jobs) return;
+  const int S = attn_splits(a), jobs = a.R * a.nq;
+  const int job = blockIdx.x / S, sp = blockIdx.x % S;
+  if (job >= jobs) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.x / a.nq, hq = blockIdx.x % a.nq, G = a.nq / a.nkv, kvh = hq / G;
-  const int qd = a.nq * HD, qkvw = (a.nq + 2 * a.nkv) * HD;
+  const int b = job / a.nq, hq = job % a.nq, G = a.nq / a.nkv, kvh = hq / G;
+  const int qkvw = (a.nq + 2 * a.nkv) * HD;
+  float* part = a.part + (size_t)blockIdx.x * (HD + 2);
   const int p = a.pos[b];
-  float* att_out = a.att + (size_t)b * qd + (size_t)hq * HD;
   if (p < 0 || p >= a.cap) {
     if (threadIdx.x == 0 && a.err) atomicExch(a.err, 1);
-    for (int d = threadIdx.x; d < HD; d += kThreads) att_out[d] = 0.0f;
+    for (int d = threadIdx.x; d < HD + 2; d += kThreads) part[d] = d == 0 ? -INFINITY : 0.0f;
     return;
   }
+  const int j0 = (int)(((long)(p + 1) * sp) / S), j1 = (int)(((long)(p + 1) * (sp + 1)) / S);
+  const bool last = j1 == p + 1;  // this range holds the new row
   constexpr int PER = HD / 32, DPL = HD / 32;
   float* qv = sa;
   float* knew = sa + HD;
@@ -278,14 +317,20 @@ CTTS_DEV void attn_phase(const LmGridArgs& a, int l, float* sa) {
   const float* kc = a.kcache + (size_t)l * a.layer_elems;
   const float* vc = a.vcache + (size_t)l * a.layer_elems;
   const size_t row0 = ((size_t)b * a.nkv + kvh) * a.cap;
-  if (warp < 3) {
+  if (warp == 0 || (last && warp < 3)) {
     const float* src =
         a.qkv + (size_t)b * qkvw + (size_t)(warp == 0 ? hq : warp == 1 ? a.nq + kvh : a.nq + a.nkv + kvh) * HD;
-    float v[PER];
+    // the row, its QK-Norm gains and the RoPE frequencies: loads in flight together
+    const float* gn = warp == 0 ? a.qn[l] : warp == 1 ? a.kn[l] : nullptr;
+    float v[PER], gw[PER], fr[PER / 2];
 #pragma unroll
-    for (int j = 0; j < PER; j++) v[j] = __ldcg(src + lane + 32 * j);
+    for (int j = 0; j < PER; j++) {
+      v[j] = __ldcg(src + lane + 32 * j);
+      gw[j] = gn ? gn[lane + 32 * j] : 1.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < PER / 2; j++) fr[j] = warp < 2 ? a.inv_freq[lane + 32 * j] : 0.0f;
     if (warp < 2) {
-      const float* gn = warp == 0 ? a.qn[l] : a.kn[l];
       if (gn) {
         float ss = 0.0f;
 #pragma unroll
@@ -293,13 +338,12 @@ CTTS_DEV void attn_phase(const LmGridArgs& a, int l, float* sa) {
         ss = warp_sum(ss);
         const float inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
 #pragma unroll
-        for (int j = 0; j < PER; j++) v[j] = v[j] * inv * gn[lane + 32 * j];
+        for (int j = 0; j < PER; j++) v[j] = v[j] * inv * gw[j];
       }
 #pragma unroll
       for (int j = 0; j < PER / 2; j++) {  // rotate-half pairs (i, i + HD/2)
-        const int i = lane + 32 * j;
         float sn, cs;
-        sincosf((float)p * a.inv_freq[i], &sn, &cs);
+        sincosf((float)p * fr[j], &sn, &cs);
         const float x1 = v[j], x2 = v[j + PER / 2];
         v[j] = x1 * cs - x2 * sn;
         v[j + PER / 2] = x1 * sn + x2 * cs;
@@ -340,15 +384,15 @@ CTTS_DEV void attn_phase(const LmGridArgs& a, int l, float* sa) {
     }
   };
   constexpr int U = 4;  // keys in flight per warp
-  for (int j0 = warp; j0 <= p; j0 += kWarps * U) {
+  for (int jb = j0 + warp; jb < j1; jb += kWarps * U) {
     float kk[U][DPL], vv[U][DPL], s[U];
 #pragma unroll
     for (int u = 0; u < U; u++) {
-      const int j = j0 + kWarps * u;
-      if (j <= p) {
+      const int j = jb + kWarps * u;
+      if (j < j1) {
         load_row(kc, knew, j, kk[u]);
         load_row(vc, vnew, j, vv[u]);
-      } else {  // past the last key: weight 0, and 0 x (stale register) must not be NaN
+      } else {  // past the range: weight 0, and 0 x (stale register) must not be NaN
 #pragma unroll
         for (int e = 0; e < DPL; e++) kk[u][e] = vv[u][e] = 0.0f;
       }
@@ -356,14 +400,12 @@ CTTS_DEV void attn_phase(const LmGridArgs& a, int l, float* sa) {
     float mx = -INFINITY;
 #pragma unroll
     for (int u = 0; u < U; u++) {
-      const int j = j0 + kWarps * u;
+      const int j = jb + kWarps * u;
       float d = 0.0f;
-      if (j <= p) {
 #pragma unroll
-        for (int e = 0; e < DPL; e++) d = fmaf(q[e], kk[u][e], d);
-      }
+      for (int e = 0; e < DPL; e++) d = fmaf(q[e], kk[u][e], d);
       d = warp_sum(d);
-      s[u] = j <= p ? d * scale : -INFINITY;
+      s[u] = j < j1 ? d * scale : -INFINITY;
       mx = fmaxf(mx, s[u]);
     }
     const float mn = fmaxf(m, mx);
@@ -387,19 +429,58 @@ CTTS_DEV void attn_phase(const LmGridArgs& a, int l, float* sa) {
 #pragma unroll
   for (int e = 0; e < DPL; e++) wpart[warp * (HD + 2) + 2 + DPL * lane + e] = acc[e];
   __syncthreads();
-  for (int d = threadIdx.x; d < HD; d += kThreads) {
-    float M = -INFINITY;
+  // this range's partial (unnormalised, relative to its max), warp order
+  float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kWarps; w++) M = fmaxf(M, wpart[w * (HD + 2)]);
-    float L = 0.0f, o = 0.0f;
+  for (int w = 0; w < kWarps; w++) M = fmaxf(M, wpart[w * (HD + 2)]);
+  for (int d = threadIdx.x; d < HD + 2; d += kThreads) {
+    if (d == 0) {
+      part[0] = M;
+      continue;
+    }
+    float o = 0.0f;
 #pragma unroll
     for (int w = 0; w < kWarps; w++) {
       const float mw = wpart[w * (HD + 2)];
       const float fw = mw == -INFINITY ? 0.0f : expf(mw - M);
-      L = fmaf(wpart[w * (HD + 2) + 1], fw, L);
-      o = fmaf(wpart[w * (HD + 2) + 2 + d], fw, o);
+      o = fmaf(wpart[w * (HD + 2) + d], fw, o);  // d == 1: the sum, d >= 2: acc
     }
-    att_out[d] = o / L;
+    part[d] = o;
+  }
+}
+
+// The o-proj operand: every job's key-range partials merged in range order
+// (every CTA, redundantly) -> xs[r][hq * HD + d] = softmax(.) V.
+template <int HD>
+CTTS_DEV void merge_attn(const LmGridArgs& a, float* xs, float* fac) {
+  const int S = attn_splits(a), jobs = a.R * a.nq, qd = a.nq * HD;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // a warp per job: lane sp holds range sp's (max, sum)
+  for (int job = warp; job < jobs; job += kWarps) {
+    const float* pp = a.part + (size_t)(job * S + lane) * (HD + 2);
+    const float ms = lane < S ? __ldcg(pp) : -INFINITY;
+    const float ls = lane < S ? __ldcg(pp + 1) : 0.0f;
+    float M = ms;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float f = ms == -INFINITY ? 0.0f : expf(ms - M);
+    // the sum in range order (lane 0 gathers), deterministic
+    float L = 0.0f;
+    for (int sp = 0; sp < S; sp++) L = fmaf(__shfl_sync(0xffffffffu, ls, sp), __shfl_sync(0xffffffffu, f, sp), L);
+    if (lane < S) fac[job * S + lane] = f / L;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < a.R * qd; i += kThreads) {
+    const int r = i / qd, hq = (i % qd) / HD, d = i % HD, job = r * a.nq + hq;
+    const float* pp = a.part + (size_t)job * S * (HD + 2) + 2 + d;
+    float v[kMaxSplits];
+#pragma unroll
+    for (int sp = 0; sp < kMaxSplits; sp++) v[sp] = sp < S ? __ldcg(pp + (size_t)sp * (HD + 2)) : 0.0f;
+    float o = 0.0f;
+#pragma unroll
+    for (int sp = 0; sp < kMaxSplits; sp++)
+      if (sp < S) o = fmaf(v[sp], fac[job * S + sp], o);
+    xs[i] = o;
   }
 }
 
@@ -426,7 +507,6 @@ __global__ void __launch_bounds__(kThreads, 1) lm_grid_kernel(const LmGridArgs a
   // has been computed
   stage(a, st, kQ, 0, 0);
   stage(a, st, kO, 0, 1);
-  const int qd = a.nq * HD;
   int k = 0;
   for (int l = 0; l < a.NL; l++) {
     norm_rows(a, a.norm1[l], xs);
@@ -436,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1) lm_grid_kernel(const LmGridArgs a
     grid_sync(a, k++);
     attn_phase<HD>(a, l, sa);
     grid_sync(a, k++);
-    load_rows(a.att, a.R * qd, xs);
+    merge_attn<HD>(a, xs, sa);
     gemv(a, st, kO, 1, xs);
     __syncthreads();
     stage(a, st, kD, l, 1);
@@ -455,23 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1) lm_grid_kernel(const LmGridArgs a
   // final RMSNorm of the last layer's rows and the cache-length advance
   // (every CTA is past its last attention phase)
   if (blockIdx.x == 0) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, H = a.H;
-    for (int r = warp; r < a.R; r += kWarps) {
-      const float* src = a.h + (size_t)r * H;
-      float ss = 0.0f;
-      for (int c = lane * 4; c < H; c += 128) {
-        const float4 v = ldcg4(src + c);
-        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
-      }
-      ss = warp_sum(ss);
-      const float inv = 1.0f / sqrtf(ss / (float)H + a.eps);
-      for (int c = lane * 4; c < H; c += 128) {
-        const float4 v = ldcg4(src + c);
-        *reinterpret_cast<float4*>(a.out + (size_t)r * H + c) =
-            make_float4(v.x * inv * a.final_norm[c], v.y * inv * a.final_norm[c + 1], v.z * inv * a.final_norm[c + 2],
-                        v.w * inv * a.final_norm[c + 3]);
-      }
-    }
+    norm_rows(a, a.final_norm, a.out);
     if (threadIdx.x < a.R) a.pos[threadIdx.x] += 1;
   }
   // the last CTA to leave zeroes the counters for the next launch
@@ -528,18 +592,20 @@ cudaError_t launch_t(const LmGridArgs& a, size_t smem, cudaStream_t s) {
 
 int lm_grid_counters(int NL) { return 5 * NL + 1; }
 
+size_t lm_grid_part_floats(int hd) { return (size_t)(grid_ctas() > 0 ? grid_ctas() : 1) * (hd + 2); }
+
 bool lm_grid_supported(int R, int NL, int H, int nq, int nkv, int hd, int F) {
   if (R < 1 || R > LmGridArgs::kMaxRows || NL < 1 || NL > LmGridArgs::kMaxNL) return false;
-  if ((hd != 64 && hd != 128) || nkv < 1 || nq % nkv || H % 128 || F % 128 || (nq * hd) % 128 ||
+  if ((hd != 64 && hd != 128) || nkv < 1 || nq % nkv || H % 128 || H > 128 * kMaxH4 || F % 128 || (nq * hd) % 128 ||
       ((nq + 2 * nkv) * hd) % 4)
     return false;
   const int G = grid_ctas();
-  if (G <= 0 || R * nq > G) return false;
+  if (G <= 0 || G > kMaxCtas || R * nq > G) return false;
   return smem_of(R, H, nq, nkv, hd, F, G).total(hd) <= 220 * 1024;
 }
 
 cudaError_t launch_lm_grid(const LmGridArgs& a, cudaStream_t s) {
-  if (!lm_grid_supported(a.R, a.NL, a.H, a.nq, a.nkv, a.hd, a.F) || !a.bar || !a.h || !a.out || !a.pos)
+  if (!lm_grid_supported(a.R, a.NL, a.H, a.nq, a.nkv, a.hd, a.F) || !a.bar || !a.h || !a.out || !a.pos || !a.part)
     return cudaErrorInvalidValue;
   const size_t smem = smem_of(a.R, a.H, a.nq, a.nkv, a.hd, a.F, grid_ctas()).total(a.hd);
   return a.hd == 64 ? launch_t<64>(a, smem, s) : launch_t<128>(a, smem, s);

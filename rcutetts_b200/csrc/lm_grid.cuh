@@ -15,7 +15,7 @@ struct LmGridArgs {
   float eps = 1e-6f;
   float* h = nullptr;    // [R, H] residual stream: in the new rows, out the last layer's output
   float* qkv = nullptr;  // [R, (nq + 2 nkv) hd] workspace
-  float* att = nullptr;  // [R, nq hd] workspace
+  float* part = nullptr;  // [grid CTAs][hd + 2] attention partials (lm_grid_part_floats())
   float* act = nullptr;  // [R, F] workspace
   float* out = nullptr;  // [R, H] final RMSNorm of h
   const float* final_norm = nullptr;
@@ -38,6 +38,8 @@ struct LmGridArgs {
 
 // Barrier counters one launch needs (all zero between launches).
 int lm_grid_counters(int NL);
+// Floats of the attention-partial workspace one launch needs.
+size_t lm_grid_part_floats(int hd);
 // True when the shapes fit the kernel's shared memory and a grid of one CTA
 // per SM can be resident (cooperative launch).
 bool lm_grid_supported(int R, int NL, int H, int nq, int nkv, int hd, int F);

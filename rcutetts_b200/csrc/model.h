@@ -38,6 +38,7 @@ struct ctts_kv {
   int batch = 0, cap = 0, nsplit = 0, chunk = 128, ws_rows = 0;
   int* cnt = nullptr;  // decode-attention split tickets [batch][n_kv_heads]
   unsigned* gbar = nullptr;  // grid-persistent decode step barrier counters (zero at rest)
+  float* gpart = nullptr;    // its attention partials
   float* ssp = nullptr;  // residual-row sum-of-squares partials [hidden/128][ws_rows]
   size_t layer_elems = 0;
   ctts::DevArena arena;
