@@ -178,7 +178,7 @@ CTTS_DEV void my_cols(int N, int& n0, int& n1) {
   n1 = (int)(((long)N * (blockIdx.x + 1)) / gridDim.x);
 }
 
-// ---- weight staging: before the barrier that opens a phase, thread 0
+// ---- weight staging: before the barrier that opens a phase, warp 0
 // copies the weight rows of this CTA's output columns of that phase into
 // the staging buffer with bulk copies (the weights do not depend on the
 // barrier), completing on one mbarrier; the phase waits on it.
@@ -256,31 +256,35 @@ CTTS_DEV uint32_t stage_aux(const DitGridArgs& a, Stage& st, int kind, int l, in
 }
 
 // warp 0: lane 0 arms the mbarrier with the phase's byte count and copies
-// the small operands, the lanes issue one weight row copy each (a serial
-// issue by one thread delays its barrier arrival by microseconds)
+// the small operands; the weight rows of this CTA's columns go as a few
+// large bulk copies, one per run of consecutive rows (consecutive columns
+// are consecutive rows except across a 64-column gate/up tile or, for the
+// output projection, across an utterance's latent columns).  Buffer layout:
+// [j][column - n0][K] (j: gate, up for the SwiGLU columns).
 CTTS_DEV void stage_weights(const DitGridArgs& a, Stage& st, int kind, int l, int stn = 0) {
   if (threadIdx.x >= 32) return;
   const int lane = threadIdx.x;
   const KindGeom g = geom(a, kind, l);
   int n0, n1;
   my_cols(g.N, n0, n1);
-  const uint32_t row_bytes = (uint32_t)g.K * 4u;
-  const int rows = (n1 - n0) * g.rows_per;
+  const uint32_t row_bytes = (uint32_t)g.K * 4u, cols = (uint32_t)(n1 - n0);
   if (lane == 0) {
-    const uint32_t bytes = (uint32_t)rows * row_bytes + stage_aux(a, st, kind, l, stn, false);
+    const uint32_t bytes = cols * g.rows_per * row_bytes + stage_aux(a, st, kind, l, stn, false);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(st.bar), "r"(bytes) : "memory");
     stage_aux(a, st, kind, l, stn, true);
   }
   __syncwarp();
+  const int period = kind == kGU ? 64 : kind == kOut ? a.L : 0;
+  const int seg0 = period ? n0 / period : 0;
+  const int nseg = n1 > n0 ? (period ? (n1 - 1) / period - seg0 + 1 : 1) : 0;
   const uint32_t dst0 = static_cast<uint32_t>(__cvta_generic_to_shared(st.wbuf));
-  for (int i = lane; i < rows; i += 32) {
-    const int n = n0 + i / g.rows_per, j = i % g.rows_per;
-    const float* src = g.base + (size_t)weight_row(a, kind, n, j) * g.K;
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     dst0 + (uint32_t)i * row_bytes),
-                 "l"(src), "r"(row_bytes), "r"(st.bar)
-                 : "memory");
+  for (int c = lane; c < nseg * g.rows_per; c += 32) {
+    const int sg = c / g.rows_per, j = c % g.rows_per;
+    const int a0 = period ? max(n0, period * (seg0 + sg)) : n0;
+    const int a1 = period ? min(n1, period * (seg0 + sg + 1)) : n1;
+    bulk_copy(dst0 + ((uint32_t)j * cols + (uint32_t)(a0 - n0)) * row_bytes,
+              g.base + (size_t)weight_row(a, kind, a0, j) * g.K, (uint32_t)(a1 - a0) * row_bytes, st.bar);
   }
 }
 
@@ -404,8 +408,8 @@ CTTS_DEV void phase_attn_o(const DitGridArgs& a, Stage& st, int l, float* sm) {
   }
 }
 
-// P3: norm2 (+ modulate) -> this CTA's SwiGLU columns (staged as gate row,
-// up row per column).
+// P3: norm2 (+ modulate) -> this CTA's SwiGLU columns (staged as the gate
+// rows, then the up rows, of the CTA's columns).
 template <int RW>
 CTTS_DEV void phase_gate_up(const DitGridArgs& a, Stage& st, int l, float* sm) {
   SUB_START();
@@ -421,8 +425,8 @@ CTTS_DEV void phase_gate_up(const DitGridArgs& a, Stage& st, int l, float* sm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int j = n0 + warp; j < n1; j += kWarps) {
     float g[RW], u[RW];
-    row_dots<RW>(st.wbuf + (size_t)(2 * (j - n0)) * H, H, sm, g);
-    row_dots<RW>(st.wbuf + (size_t)(2 * (j - n0) + 1) * H, H, sm, u);
+    row_dots<RW>(st.wbuf + (size_t)(j - n0) * H, H, sm, g);
+    row_dots<RW>(st.wbuf + (size_t)(n1 - n0 + j - n0) * H, H, sm, u);
     if (lane == 0)
 #pragma unroll
       for (int r = 0; r < rows; r++) a.act[(size_t)r * F + j] = silu(g[r]) * u[r];
