@@ -42,7 +42,9 @@ int dit_ws_ensure(ctts_dit* d, DitWs& w, int rows, int steps) {
   w.hbuf = w.arena.alloc<float>((size_t)2 * H);
   w.err = w.arena.alloc<int>(1);
   w.gbar = w.arena.alloc<unsigned>((size_t)dit_grid_counters(c.n_layers, steps));
-  if (!w.seq || !w.qkv || !w.att || !w.act || !w.ad || !w.x || !w.spk || !w.hbuf || !w.err || !w.gbar)
+  w.gll = w.arena.alloc<unsigned long long>(
+      ctts::dit_grid_ll_words(std::min(rows, ctts::DitGridArgs::kMaxRows / 3), H, c.n_heads, c.n_kv_heads, c.head_dim, c.ffn, L));
+  if (!w.seq || !w.qkv || !w.att || !w.act || !w.ad || !w.x || !w.spk || !w.hbuf || !w.err || !w.gbar || !w.gll)
     return set_error(CTTS_ERR_NOMEM, "DiT workspace allocation failed");
   if (d->bf16) {
     const int SR = rows * S;
@@ -251,7 +253,7 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
       ga.wgu[l] = static_cast<const float*>(Ly.wgu); ga.wd[l] = static_cast<const float*>(Ly.wd);
       ga.norm1[l] = Ly.norm1; ga.norm2[l] = Ly.norm2;
     }
-    ga.bar = w.gbar; ga.err = w.err;
+    ga.bar = w.gbar; ga.ll = w.gll; ga.err = w.err;
     CTTS_CK(ctts::launch_dit_grid(ga, s)); nl++;
     if (launches) *launches += nl;
     return CTTS_OK;

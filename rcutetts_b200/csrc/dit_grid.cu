@@ -5,12 +5,11 @@
 // Replaces the per-step launch chain of dit.rs:775-814 predict_cached /
 // euler_sample (dit.rs:819-842) at batch 1..4, where ~200 dependent
 // launches of a few microseconds each dominate the frame.  One CTA per SM
-// (cooperative launch, so every CTA is resident); phases are separated by
-// grid barriers (a global counter per barrier, zeroed again by the last
-// CTA to leave).  Each phase splits its output columns over all CTAs and
-// streams each column's weight row once per step (fp32, 16-byte loads; the
-// weights stay L2-resident across the ten steps), so the work per phase is
-// a few microseconds of L2 bandwidth spread over the whole GPU:
+// (cooperative launch, so every CTA is resident).  Each phase splits its
+// output columns over all CTAs and streams each column's weight row once
+// per step (fp32; the weights stay L2-resident across the ten steps), so
+// the work per phase is a few microseconds of L2 bandwidth spread over the
+// whole GPU:
 //   P1  RMSNorm1 + AdaLN modulate (every CTA, all rows, redundant) -> QKV
 //   P2  3-token RoPE attention (every CTA, redundant) -> o-proj -> gated
 //       residual into the CTA's columns of the residual stream
@@ -18,8 +17,16 @@
 //   P4  down -> gated residual
 //   T1  final norm -> out_proj -> x += dt * v
 //   T2  in_proj(x) and the next step's sequence rows
-// Intra-kernel data (residual, qkv, SwiGLU output, x) is read with
-// L2-coherent loads (ld.global.cg): L1 is not coherent across SMs.
+// Every phase consumes what all CTAs produced in the phase before it, and
+// only that.  The hand-over needs no grid barrier: each value travels as one
+// 64-bit word (tag << 32 | float bits) written with a single store, the tag
+// naming the launch generation and the producing phase, and a consumer
+// polls the words it needs (L2, not L1) until every tag is the one it
+// expects: one L2 round trip per phase instead of a barrier's arrival, its
+// poll and the data load after it.  A word is rewritten only two phases
+// later, by a CTA that has already consumed the next phase's output of
+// every CTA, which each CTA produces after its own reads: no word is
+// overwritten while a consumer may still need it.
 #include <cstdio>
 
 #include "common.cuh"
@@ -37,62 +44,99 @@ constexpr int kMaxH4 = 8;  // hidden <= 1024: 16-byte groups per lane of a row
 CTTS_DEV float ldcg(const float* p) { return __ldcg(p); }
 CTTS_DEV float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
-CTTS_DEV uint32_t ld_acquire(const unsigned* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+// ---- flag-tagged exchange words
+using u64 = unsigned long long;
+CTTS_DEV void ll_put(u64* p, float v, uint32_t tag) {
+  const u64 w = ((u64)tag << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-
-// Optional barrier timeline (build with -DCTTS_GRID_TRACE): thread 0 of
-// CTA 0 records %globaltimer at each barrier's arrival and release.
-#ifdef CTTS_GRID_TRACE
-__device__ long long g_grid_trace[2048];
-CTTS_DEV void grid_trace(int i) {
-  if (blockIdx.x != 0 || i >= 2048) return;
-  long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  g_grid_trace[i] = t;
+CTTS_DEV void ld4(const u64* p, u64 (&w)[4]) {
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(w[0]), "=l"(w[1]) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(w[2]), "=l"(w[3]) : "l"(p + 2) : "memory");
 }
-#define GRID_TRACE(i) grid_trace(i)
-// inside-phase marks: g_grid_sub[kind][mark] accumulates the time from the
-// phase start to the mark (CTA 0, thread 0)
-__device__ long long g_grid_sub[6][4];
-CTTS_DEV long long gtime() {
-  long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
+CTTS_DEV bool tags_are(const u64 (&w)[4], uint32_t tag) {
+  return (uint32_t)(w[0] >> 32) == tag && (uint32_t)(w[1] >> 32) == tag && (uint32_t)(w[2] >> 32) == tag &&
+         (uint32_t)(w[3] >> 32) == tag;
 }
-#define SUB_START() const long long sub_t0 = gtime()
-#define SUB_MARK(kind, m) \
-  if (blockIdx.x == 0 && threadIdx.x == 0) g_grid_sub[kind][m] += gtime() - sub_t0
-#else
-#define GRID_TRACE(i)
-#define SUB_START()
-#define SUB_MARK(kind, m)
-#endif
-
-// Grid barrier k: every CTA's writes before it are visible to every CTA
-// after it.  Bounded: a CTA that waits too long records an error and goes on.
-CTTS_DEV void grid_sync(const DitGridArgs& a, int k) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    GRID_TRACE(2 * k);
-    // release (cumulative over the CTA's writes ordered before it by the
-    // block barrier) fused into the arrival; the acquiring poll orders the
-    // next phase's reads after every CTA's release
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar + k) : "memory");
-    const unsigned n = gridDim.x;
-    uint32_t it = 0;
-    while (ld_acquire(a.bar + k) < n) {
-      // a CTA that already gave up somewhere makes every later wait end at once
-      if (++it == kSpinLimit || ((it & 1023u) == 0 && a.err && *reinterpret_cast<volatile int*>(a.err) != 0)) {
-        if (a.err) atomicExch(a.err, 4);
-        break;
+// Polls groups of four words (group i at p[i]; none where p[i] is null)
+// until every tag equals `tag`; group i's values go to v[i].  Only groups
+// still pending are reloaded.  Bounded: a thread that gives up (or sees
+// that another one did) records error 4 and goes on with what it has.
+// (not inlined: inside the phases its load registers pushed the dot
+// products into local memory)
+template <int NG>
+__device__ __noinline__ void ll_poll(const DitGridArgs& a, const u64* const (&p)[NG], uint32_t tag, float4 (&v)[NG]) {
+  uint32_t pend = 0;
+#pragma unroll
+  for (int i = 0; i < NG; i++)
+    if (p[i]) pend |= 1u << i;
+  for (uint32_t it = 0; pend; ++it) {
+    u64 w[NG][4];
+#pragma unroll
+    for (int i = 0; i < NG; i++)
+      if ((pend >> i) & 1u) ld4(p[i], w[i]);
+#pragma unroll
+    for (int i = 0; i < NG; i++)
+      if (((pend >> i) & 1u) && tags_are(w[i], tag)) {
+        v[i] = make_float4(__uint_as_float((uint32_t)w[i][0]), __uint_as_float((uint32_t)w[i][1]),
+                           __uint_as_float((uint32_t)w[i][2]), __uint_as_float((uint32_t)w[i][3]));
+        pend &= ~(1u << i);
       }
+    if (pend && (it == kSpinLimit || ((it & 255u) == 255u && a.err && *reinterpret_cast<volatile int*>(a.err)))) {
+      if (a.err) atomicExch(a.err, 4);
+      break;
     }
-    GRID_TRACE(2 * k + 1);
   }
-  __syncthreads();
+}
+// One word, polled the same way.
+CTTS_DEV float ll_get1(const DitGridArgs& a, const u64* p, uint32_t tag) {
+  for (uint32_t it = 0;; ++it) {
+    u64 w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
+    if (it == kSpinLimit || ((it & 255u) == 255u && a.err && *reinterpret_cast<volatile int*>(a.err))) {
+      if (a.err) atomicExch(a.err, 4);
+      return 0.0f;
+    }
+  }
+}
+
+// One row of H = 128 nv exchange words for a warp: lane's groups at
+// lane * 4 + 128 i, polled four groups at a time.
+CTTS_DEV void poll_row(const DitGridArgs& a, const u64* src, int nv, uint32_t tag, float4 (&v)[kMaxH4]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int h = 0; h < kMaxH4; h += 4) {
+    if (h < nv) {
+      const u64* ps[4];
+      float4 t[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) ps[q] = h + q < nv ? src + lane * 4 + 128 * (h + q) : nullptr;
+      ll_poll<4>(a, ps, tag, t);
+#pragma unroll
+      for (int q = 0; q < 4; q++) v[h + q] = t[q];
+    }
+  }
+}
+
+// Exchange areas inside a.ll: residual rows [3R][H], QKV rows [3R][qkvw],
+// SwiGLU rows [3R][F], latent x [R][L] (the device code and
+// dit_grid_ll_words() agree on this layout).
+struct LLMap {
+  u64 *seq, *qkv, *act, *x;
+};
+__host__ __device__ inline size_t ll_offsets(int R, int H, int qkvw, int F, size_t (&o)[4]) {
+  const size_t rows = 3 * (size_t)R;
+  o[0] = 0;
+  o[1] = o[0] + rows * H;
+  o[2] = o[1] + rows * qkvw;
+  o[3] = o[2] + rows * F;
+  return o[3] + (size_t)R * 64;
+}
+CTTS_DEV LLMap ll_map(const DitGridArgs& a) {
+  size_t o[4];
+  ll_offsets(a.R, a.H, (a.nq + 2 * a.nkv) * a.hd, a.F, o);
+  return {a.ll + o[0], a.ll + o[1], a.ll + o[2], a.ll + o[3]};
 }
 
 // Rows of the residual stream -> RMSNorm (+ AdaLN modulate) into shared
@@ -100,18 +144,16 @@ CTTS_DEV void grid_sync(const DitGridArgs& a, int k) {
 // its use (prep/linear_rows semantics: x * inv * gain, then
 // * (1 + scale) + shift).
 template <int RW>
-CTTS_DEV void norm_rows(const DitGridArgs& a, const float* aux, float* xs) {
+CTTS_DEV void norm_rows(const DitGridArgs& a, const u64* seq, uint32_t tag, const float* aux, float* xs) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int rows = RW;
   const int H = a.H, nv = H >> 7;
   const float* gain = aux;  // staged: gain [H], per utterance [shift | scale]
   for (int r = warp; r < rows; r += kWarps) {
-    const float* src = a.seq + (size_t)r * H;
+    const u64* src = seq + (size_t)r * H;
     float* dst = xs + (size_t)r * H;
     float4 v[kMaxH4];
-#pragma unroll
-    for (int i = 0; i < kMaxH4; i++)
-      if (i < nv) v[i] = ldcg4(src + lane * 4 + 128 * i);
+    poll_row(a, src, nv, tag, v);
     float ss = 0.0f;
 #pragma unroll
     for (int i = 0; i < kMaxH4; i++)
@@ -134,16 +176,18 @@ CTTS_DEV void norm_rows(const DitGridArgs& a, const float* aux, float* xs) {
   }
 }
 
-// rows x K floats of global memory -> shared memory (L2-coherent loads,
-// four 16-byte loads in flight per thread)
-CTTS_DEV void load_rows(float* dst, const float* src, int n) {
+// n exchange words (n a multiple of 4) -> floats in shared memory, four
+// 16-byte groups per thread and pass
+CTTS_DEV void load_rows(const DitGridArgs& a, float* dst, const u64* src, int n, uint32_t tag) {
   for (int i0 = threadIdx.x * 4; i0 < n; i0 += kThreads * 16) {
     float4 v[4];
+    const u64* ps[4];
 #pragma unroll
     for (int q = 0; q < 4; q++) {
       const int i = i0 + q * kThreads * 4;
-      if (i < n) v[q] = ldcg4(src + i);
+      ps[q] = i < n ? src + i : nullptr;
     }
+    ll_poll<4>(a, ps, tag, v);
 #pragma unroll
     for (int q = 0; q < 4; q++) {
       const int i = i0 + q * kThreads * 4;
@@ -191,6 +235,8 @@ struct Stage {
   float* resv;   // [rows][kMaxCols] this CTA's columns of the residual stream
   uint32_t bar;  // shared address of the mbarrier
   uint32_t ph;   // uses so far (parity of the next wait)
+  LLMap ll;      // exchange areas
+  uint32_t tag;  // tag of the running phase; its inputs carry tag - 1
 };
 constexpr int kMaxCols = 8;  // residual columns per CTA (hidden / CTAs)
 
@@ -305,13 +351,25 @@ CTTS_DEV void wait_weights(const DitGridArgs& a, Stage& st) {
   st.ph++;
 }
 
+// A CTA without output columns in a phase reads none of its inputs (a
+// later phase's producers wait only on the CTAs that produced something)
+// and only retires the phase's staging wait.
+CTTS_DEV bool idle_phase(const DitGridArgs& a, Stage& st, int N) {
+  int n0, n1;
+  my_cols(N, n0, n1);
+  if (n0 < n1) return false;
+  wait_weights(a, st);
+  return true;
+}
+
 // P1: norm1 (+ modulate) -> this CTA's QKV columns.
 template <int RW>
 CTTS_DEV void phase_qkv(const DitGridArgs& a, Stage& st, int l, float* sm) {
   constexpr int rows = RW;
   const int H = a.H, qkvw = (a.nq + 2 * a.nkv) * a.hd;
+  if (idle_phase(a, st, qkvw)) return;
   wait_weights(a, st);
-  norm_rows<RW>(a, st.aux, sm);
+  norm_rows<RW>(a, st.ll.seq, st.tag - 1, st.aux, sm);
   __syncthreads();
   int n0, n1;
   my_cols(qkvw, n0, n1);
@@ -321,7 +379,7 @@ CTTS_DEV void phase_qkv(const DitGridArgs& a, Stage& st, int l, float* sm) {
     row_dots<RW>(st.wbuf + (size_t)(n - n0) * H, H, sm, acc);
     if (lane == 0)
 #pragma unroll
-      for (int r = 0; r < rows; r++) a.qkv[(size_t)r * qkvw + n] = acc[r];
+      for (int r = 0; r < rows; r++) ll_put(st.ll.qkv + (size_t)r * qkvw + n, acc[r], st.tag);
   }
 }
 
@@ -330,15 +388,14 @@ CTTS_DEV void phase_qkv(const DitGridArgs& a, Stage& st, int l, float* sm) {
 // gated residual (h += (1 + gate) * o).
 template <int RW>
 CTTS_DEV void phase_attn_o(const DitGridArgs& a, Stage& st, int l, float* sm) {
-  SUB_START();
   constexpr int rows = RW;
   const int H = a.H, hd = a.hd, nq = a.nq, nkv = a.nkv;
   const int qkvw = (nq + 2 * nkv) * hd, qd = nq * hd, G = nq / nkv;
+  if (idle_phase(a, st, H)) return;
   float* qs = sm;                         // [rows][qkvw]
   float* att = sm + (size_t)rows * qkvw;  // [rows][qd]
-  load_rows(qs, a.qkv, rows * qkvw);
+  load_rows(a, qs, st.ll.qkv, rows * qkvw, st.tag - 1);
   __syncthreads();
-  SUB_MARK(kO, 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float scale = 1.0f / sqrtf((float)hd);
   for (int job = warp; job < a.R * nq; job += kWarps) {
@@ -388,10 +445,8 @@ CTTS_DEV void phase_attn_o(const DitGridArgs& a, Stage& st, int l, float* sm) {
       }
     }
   }
-  SUB_MARK(kO, 1);
   wait_weights(a, st);
   __syncthreads();
-  SUB_MARK(kO, 2);
   int n0, n1;
   my_cols(H, n0, n1);
   for (int n = n0 + warp; n < n1; n += kWarps) {
@@ -403,7 +458,7 @@ CTTS_DEV void phase_attn_o(const DitGridArgs& a, Stage& st, int l, float* sm) {
         const float coef = a.ad ? 1.0f + st.aux[(size_t)(r / 3) * H + n] : 1.0f;
         float* rv = st.resv + r * kMaxCols + (n - n0);
         *rv = *rv + coef * acc[r];
-        a.seq[(size_t)r * H + n] = *rv;
+        ll_put(st.ll.seq + (size_t)r * H + n, *rv, st.tag);
       }
   }
 }
@@ -412,14 +467,12 @@ CTTS_DEV void phase_attn_o(const DitGridArgs& a, Stage& st, int l, float* sm) {
 // rows, then the up rows, of the CTA's columns).
 template <int RW>
 CTTS_DEV void phase_gate_up(const DitGridArgs& a, Stage& st, int l, float* sm) {
-  SUB_START();
   constexpr int rows = RW;
   const int H = a.H, F = a.F;
+  if (idle_phase(a, st, F)) return;
   wait_weights(a, st);
-  SUB_MARK(kGU, 0);
-  norm_rows<RW>(a, st.aux, sm);
+  norm_rows<RW>(a, st.ll.seq, st.tag - 1, st.aux, sm);
   __syncthreads();
-  SUB_MARK(kGU, 1);
   int n0, n1;
   my_cols(F, n0, n1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -429,11 +482,8 @@ CTTS_DEV void phase_gate_up(const DitGridArgs& a, Stage& st, int l, float* sm) {
     row_dots<RW>(st.wbuf + (size_t)(n1 - n0 + j - n0) * H, H, sm, u);
     if (lane == 0)
 #pragma unroll
-      for (int r = 0; r < rows; r++) a.act[(size_t)r * F + j] = silu(g[r]) * u[r];
+      for (int r = 0; r < rows; r++) ll_put(st.ll.act + (size_t)r * F + j, silu(g[r]) * u[r], st.tag);
   }
-  SUB_MARK(kGU, 2);
-  __syncthreads();
-  SUB_MARK(kGU, 3);
 }
 
 // P4: down over the SwiGLU rows -> gated residual.
@@ -441,7 +491,8 @@ template <int RW>
 CTTS_DEV void phase_down(const DitGridArgs& a, Stage& st, int l, float* sm) {
   constexpr int rows = RW;
   const int H = a.H, F = a.F;
-  load_rows(sm, a.act, rows * F);
+  if (idle_phase(a, st, H)) return;
+  load_rows(a, sm, st.ll.act, rows * F, st.tag - 1);
   wait_weights(a, st);
   __syncthreads();
   int n0, n1;
@@ -456,7 +507,7 @@ CTTS_DEV void phase_down(const DitGridArgs& a, Stage& st, int l, float* sm) {
         const float coef = a.ad ? 1.0f + st.aux[(size_t)(r / 3) * H + n] : 1.0f;
         float* rv = st.resv + r * kMaxCols + (n - n0);
         *rv = *rv + coef * acc[r];
-        a.seq[(size_t)r * H + n] = *rv;
+        ll_put(st.ll.seq + (size_t)r * H + n, *rv, st.tag);
       }
   }
 }
@@ -466,14 +517,13 @@ CTTS_DEV void phase_down(const DitGridArgs& a, Stage& st, int l, float* sm) {
 CTTS_DEV void phase_out(const DitGridArgs& a, Stage& st, int stp, float* sm) {
   const int H = a.H, L = a.L, R = a.R, nv = H >> 7;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (idle_phase(a, st, R * L)) return;
   wait_weights(a, st);
   const float* fnorm = st.aux;
   for (int u = warp; u < R; u += kWarps) {
-    const float* src = a.seq + (size_t)(3 * u + 2) * H;
+    const u64* src = st.ll.seq + (size_t)(3 * u + 2) * H;
     float4 v[kMaxH4];
-#pragma unroll
-    for (int i = 0; i < kMaxH4; i++)
-      if (i < nv) v[i] = ldcg4(src + lane * 4 + 128 * i);
+    poll_row(a, src, nv, st.tag - 1, v);
     float ss = 0.0f;
 #pragma unroll
     for (int i = 0; i < kMaxH4; i++)
@@ -497,8 +547,11 @@ CTTS_DEV void phase_out(const DitGridArgs& a, Stage& st, int stp, float* sm) {
     float acc[1];
     row_dots<1>(st.wbuf + (size_t)(o - o0) * H, H, sm + (size_t)u * H, acc);
     if (lane == 0) {
+      // the same thread updates latent column o at every step
       float* x = a.x + (size_t)u * L + l;
-      *x = ldcg(x) + a.dts[stp] * (acc[0] + (a.out_b ? a.out_b[l] : 0.0f));
+      const float xn = ldcg(x) + a.dts[stp] * (acc[0] + (a.out_b ? a.out_b[l] : 0.0f));
+      *x = xn;
+      ll_put(st.ll.x + o, xn, st.tag);
     }
   }
 }
@@ -507,7 +560,10 @@ CTTS_DEV void phase_out(const DitGridArgs& a, Stage& st, int stp, float* sm) {
 // for this CTA's columns.
 CTTS_DEV void phase_fill(const DitGridArgs& a, Stage& st, int stn, float* sm) {
   const int H = a.H, L = a.L, R = a.R;
-  for (int i = threadIdx.x; i < R * L; i += kThreads) sm[i] = ldcg(a.x + i);
+  if (idle_phase(a, st, H)) return;
+  // x0 comes from before the launch; later steps' x from the output phase
+  for (int i = threadIdx.x; i < R * L; i += kThreads)
+    sm[i] = stn == 0 ? ldcg(a.x + i) : ll_get1(a, st.ll.x + i, st.tag - 1);
   wait_weights(a, st);
   __syncthreads();
   int n0, n1;
@@ -524,10 +580,10 @@ CTTS_DEV void phase_fill(const DitGridArgs& a, Stage& st, int stn, float* sm) {
         const float v0 = (aux[(size_t)u * H + n] + aux[(size_t)2 * R * H + n]) + aux[(size_t)(2 * R + 1) * H + n];
         const float v1 = aux[(size_t)(R + u) * H + n];
         const float v2 = acc + (a.in_b ? a.in_b[n] : 0.0f);
-        float* row = a.seq + (size_t)(3 * u) * H + n;
-        row[0] = v0;
-        row[H] = v1;
-        row[2 * H] = v2;
+        u64* row = st.ll.seq + (size_t)(3 * u) * H + n;
+        ll_put(row, v0, st.tag);
+        ll_put(row + H, v1, st.tag);
+        ll_put(row + 2 * H, v2, st.tag);
         float* rv = st.resv + (3 * u) * kMaxCols + (n - n0);
         rv[0] = v0;
         rv[kMaxCols] = v1;
@@ -585,47 +641,51 @@ __global__ void __launch_bounds__(kThreads, 1) dit_grid_kernel(const DitGridArgs
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  int k = 0;  // barrier index
+  // phase tags: launch generation (bar[0], advanced by the last CTA to
+  // leave) and phase number; never 0, the value of a fresh exchange word
+  st.ll = ll_map(a);
+  st.tag = ((__ldcg(a.bar) & 0x3fffffu) << 10) + 1u;
   // each phase's weights are staged right after the previous phase, before
-  // the barrier that opens it
+  // the inputs of the phase are polled
   stage_weights(a, st, kFill, 0, 0);
   phase_fill(a, st, 0, sm);
   for (int stp = 0; stp < a.steps; stp++) {
     for (int l = 0; l < a.NL; l++) {
       __syncthreads();
       stage_weights(a, st, kQKV, l);
-      grid_sync(a, k++);
+      st.tag++;
       phase_qkv<RW>(a, st, l, sm);
       __syncthreads();
       stage_weights(a, st, kO, l);
-      grid_sync(a, k++);
+      st.tag++;
       phase_attn_o<RW>(a, st, l, sm);
       __syncthreads();
       stage_weights(a, st, kGU, l);
-      grid_sync(a, k++);
+      st.tag++;
       phase_gate_up<RW>(a, st, l, sm);
       __syncthreads();
       stage_weights(a, st, kD, l);
-      grid_sync(a, k++);
+      st.tag++;
       phase_down<RW>(a, st, l, sm);
     }
     __syncthreads();
     stage_weights(a, st, kOut, 0);
-    grid_sync(a, k++);
+    st.tag++;
     phase_out(a, st, stp, sm);
     if (stp + 1 < a.steps) {
       __syncthreads();
       stage_weights(a, st, kFill, 0, stp + 1);
-      grid_sync(a, k++);
+      st.tag++;
       phase_fill(a, st, stp + 1, sm);
     }
   }
-  // the last CTA to leave zeroes the counters for the next launch
+  // the last CTA to leave advances the generation for the next launch
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    if (atomicAdd(a.bar + k, 1u) == gridDim.x - 1) {
-      for (int i = 0; i <= k; i++) a.bar[i] = 0u;
+    if (atomicAdd(a.bar + 1, 1u) == gridDim.x - 1) {
+      a.bar[1] = 0u;
+      a.bar[0] = a.bar[0] + 1u;
       __threadfence();
     }
   }
@@ -650,7 +710,12 @@ int grid_ctas() {
 
 }  // namespace
 
-int dit_grid_counters(int NL, int steps) { return 1 + steps * (4 * NL + 2) + 1; }
+int dit_grid_counters(int, int) { return 2; }
+
+size_t dit_grid_ll_words(int R, int H, int nq, int nkv, int hd, int F, int) {
+  size_t o[4];
+  return ll_offsets(R, H, (nq + 2 * nkv) * hd, F, o);
+}
 
 bool dit_grid_supported(int R, int NL, int steps, int H, int nq, int nkv, int hd, int F, int L) {
   if (R < 1 || 3 * R > DitGridArgs::kMaxRows || NL < 1 || NL > DitGridArgs::kMaxNL || steps < 1 ||
@@ -694,7 +759,7 @@ cudaError_t launch_rows(const DitGridArgs& a, size_t smem, cudaStream_t s) {
 }  // namespace
 
 cudaError_t launch_dit_grid(const DitGridArgs& a, cudaStream_t s) {
-  if (!dit_grid_supported(a.R, a.NL, a.steps, a.H, a.nq, a.nkv, a.hd, a.F, a.L) || !a.bar)
+  if (!dit_grid_supported(a.R, a.NL, a.steps, a.H, a.nq, a.nkv, a.hd, a.F, a.L) || !a.bar || !a.ll)
     return cudaErrorInvalidValue;
   const size_t smem = grid_smem_bytes(a.R, a.H, a.F, a.nq, a.nkv, a.hd, a.L, grid_ctas());
   switch (a.R) {
@@ -706,12 +771,3 @@ cudaError_t launch_dit_grid(const DitGridArgs& a, cudaStream_t s) {
 }
 
 }  // namespace ctts
-
-#ifdef CTTS_GRID_TRACE
-extern "C" __attribute__((visibility("default"))) int ctts_grid_trace(long long* out) {
-  cudaMemcpyFromSymbol(out + 2048, ctts::g_grid_sub, sizeof(long long) * 24);
-  long long z[24] = {0};
-  cudaMemcpyToSymbol(ctts::g_grid_sub, z, sizeof(z));
-  return cudaMemcpyFromSymbol(out, ctts::g_grid_trace, sizeof(long long) * 2048) == cudaSuccess ? 0 : -2;
-}
-#endif

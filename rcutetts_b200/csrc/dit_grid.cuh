@@ -33,12 +33,17 @@ struct DitGridArgs {
   const float* wd[kMaxNL] = {};    // [H, F]
   const float* norm1[kMaxNL] = {};
   const float* norm2[kMaxNL] = {};
-  unsigned* bar = nullptr;        // barrier counters, zero at rest (dit_grid_counters())
+  // Flag-tagged exchange words (dit_grid_ll_words(), zero at allocation):
+  // (tag << 32) | float bits, tag = launch generation and phase.
+  unsigned long long* ll = nullptr;
+  unsigned* bar = nullptr;        // [0] launch generation, [1] exit count (dit_grid_counters())
   int* err = nullptr;
 };
 
-// Barrier counters the launch needs (all zero between launches).
+// Counters the launch needs (zero at allocation).
 int dit_grid_counters(int NL, int steps);
+// 64-bit exchange words the launch needs for up to R utterances.
+size_t dit_grid_ll_words(int R, int H, int nq, int nkv, int hd, int F, int L);
 // True when the shapes fit the kernel (patch 1, head_dim 64, sizes below
 // the shared-memory budget) and a grid of one CTA per SM can be resident.
 bool dit_grid_supported(int R, int NL, int steps, int H, int nq, int nkv, int hd, int F, int L);

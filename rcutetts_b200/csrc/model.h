@@ -69,7 +69,8 @@ struct DitWs {  // workspace for `rows` utterance-branches
   uint16_t *xb = nullptr, *attb = nullptr, *actb = nullptr;
   ctts::TcScratch tc;
   int* err = nullptr;
-  unsigned* gbar = nullptr;  // grid-persistent Euler loop barrier counters (zero at rest)
+  unsigned* gbar = nullptr;  // grid-persistent Euler loop: launch generation, exit count
+  unsigned long long* gll = nullptr;  // its flag-tagged exchange words (zero at allocation)
 };
 
 struct ctts_dit {
