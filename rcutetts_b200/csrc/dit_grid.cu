@@ -139,43 +139,6 @@ CTTS_DEV LLMap ll_map(const DitGridArgs& a) {
   return {a.ll + o[0], a.ll + o[1], a.ll + o[2], a.ll + o[3]};
 }
 
-// Rows of the residual stream -> RMSNorm (+ AdaLN modulate) into shared
-// memory xs[rows][H]: one warp per row, every load of the row issued before
-// its use (prep/linear_rows semantics: x * inv * gain, then
-// * (1 + scale) + shift).
-template <int RW>
-CTTS_DEV void norm_rows(const DitGridArgs& a, const u64* seq, uint32_t tag, const float* aux, float* xs) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int rows = RW;
-  const int H = a.H, nv = H >> 7;
-  const float* gain = aux;  // staged: gain [H], per utterance [shift | scale]
-  for (int r = warp; r < rows; r += kWarps) {
-    const u64* src = seq + (size_t)r * H;
-    float* dst = xs + (size_t)r * H;
-    float4 v[kMaxH4];
-    poll_row(a, src, nv, tag, v);
-    float ss = 0.0f;
-#pragma unroll
-    for (int i = 0; i < kMaxH4; i++)
-      if (i < nv) ss = fmaf(v[i].x, v[i].x, fmaf(v[i].y, v[i].y, fmaf(v[i].z, v[i].z, fmaf(v[i].w, v[i].w, ss))));
-    ss = warp_sum(ss);
-    const float inv = 1.0f / sqrtf(ss / (float)H + a.eps);
-    const float* md = a.ad ? aux + H + (size_t)(r / 3) * 2 * H : nullptr;
-#pragma unroll
-    for (int i = 0; i < kMaxH4; i++) {
-      if (i >= nv) break;
-      const int k = lane * 4 + 128 * i;
-      float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        e[j] = e[j] * inv * gain[k + j];
-        if (md) e[j] = e[j] * (1.0f + md[H + k + j]) + md[k + j];
-      }
-      *reinterpret_cast<float4*>(dst + k) = make_float4(e[0], e[1], e[2], e[3]);
-    }
-  }
-}
-
 // n exchange words (n a multiple of 4) -> floats in shared memory, four
 // 16-byte groups per thread and pass
 CTTS_DEV void load_rows(const DitGridArgs& a, float* dst, const u64* src, int n, uint32_t tag) {
@@ -351,6 +314,45 @@ CTTS_DEV void wait_weights(const DitGridArgs& a, Stage& st) {
   st.ph++;
 }
 
+// Rows of the residual stream -> RMSNorm (+ AdaLN modulate) into shared
+// memory xs[rows][H]: one warp per row (prep/linear_rows semantics: x * inv
+// * gain, then * (1 + scale) + shift).  Each warp polls its first row
+// before waiting on the staged gains and weights, so the staging copies
+// complete under the poll.
+template <int RW>
+CTTS_DEV void norm_rows(const DitGridArgs& a, Stage& st, float* xs) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int rows = RW;
+  const int H = a.H, nv = H >> 7;
+  const float* gain = st.aux;  // staged: gain [H], per utterance [shift | scale]
+  float4 v[kMaxH4];
+  if (warp < rows) poll_row(a, st.ll.seq + (size_t)warp * H, nv, st.tag - 1, v);
+  wait_weights(a, st);
+  for (int r = warp; r < rows; r += kWarps) {
+    if (r != warp) poll_row(a, st.ll.seq + (size_t)r * H, nv, st.tag - 1, v);
+    float* dst = xs + (size_t)r * H;
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kMaxH4; i++)
+      if (i < nv) ss = fmaf(v[i].x, v[i].x, fmaf(v[i].y, v[i].y, fmaf(v[i].z, v[i].z, fmaf(v[i].w, v[i].w, ss))));
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)H + a.eps);
+    const float* md = a.ad ? st.aux + H + (size_t)(r / 3) * 2 * H : nullptr;
+#pragma unroll
+    for (int i = 0; i < kMaxH4; i++) {
+      if (i >= nv) break;
+      const int k = lane * 4 + 128 * i;
+      float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        e[j] = e[j] * inv * gain[k + j];
+        if (md) e[j] = e[j] * (1.0f + md[H + k + j]) + md[k + j];
+      }
+      *reinterpret_cast<float4*>(dst + k) = make_float4(e[0], e[1], e[2], e[3]);
+    }
+  }
+}
+
 // A CTA without output columns in a phase reads none of its inputs (a
 // later phase's producers wait only on the CTAs that produced something)
 // and only retires the phase's staging wait.
@@ -368,8 +370,7 @@ CTTS_DEV void phase_qkv(const DitGridArgs& a, Stage& st, int l, float* sm) {
   constexpr int rows = RW;
   const int H = a.H, qkvw = (a.nq + 2 * a.nkv) * a.hd;
   if (idle_phase(a, st, qkvw)) return;
-  wait_weights(a, st);
-  norm_rows<RW>(a, st.ll.seq, st.tag - 1, st.aux, sm);
+  norm_rows<RW>(a, st, sm);
   __syncthreads();
   int n0, n1;
   my_cols(qkvw, n0, n1);
@@ -470,8 +471,7 @@ CTTS_DEV void phase_gate_up(const DitGridArgs& a, Stage& st, int l, float* sm) {
   constexpr int rows = RW;
   const int H = a.H, F = a.F;
   if (idle_phase(a, st, F)) return;
-  wait_weights(a, st);
-  norm_rows<RW>(a, st.ll.seq, st.tag - 1, st.aux, sm);
+  norm_rows<RW>(a, st, sm);
   __syncthreads();
   int n0, n1;
   my_cols(F, n0, n1);
@@ -518,12 +518,14 @@ CTTS_DEV void phase_out(const DitGridArgs& a, Stage& st, int stp, float* sm) {
   const int H = a.H, L = a.L, R = a.R, nv = H >> 7;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (idle_phase(a, st, R * L)) return;
-  wait_weights(a, st);
   const float* fnorm = st.aux;
-  for (int u = warp; u < R; u += kWarps) {
-    const u64* src = st.ll.seq + (size_t)(3 * u + 2) * H;
-    float4 v[kMaxH4];
-    poll_row(a, src, nv, st.tag - 1, v);
+  // warp u < R (<= 4) takes utterance u's x row; polled before the wait
+  // on the staged weights
+  float4 v[kMaxH4];
+  if (warp < R) poll_row(a, st.ll.seq + (size_t)(3 * warp + 2) * H, nv, st.tag - 1, v);
+  wait_weights(a, st);
+  if (warp < R) {
+    const int u = warp;
     float ss = 0.0f;
 #pragma unroll
     for (int i = 0; i < kMaxH4; i++)
