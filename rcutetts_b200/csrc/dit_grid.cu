@@ -40,6 +40,10 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr uint32_t kSpinLimit = 1u << 22;  // polls of about 1 us: seconds
 constexpr int kMaxH4 = 8;  // hidden <= 1024: 16-byte groups per lane of a row
+// The last warp issues the weight staging of the next phase while the
+// others start polling its inputs (no row poll and no bulk poll uses it).
+constexpr int kStageWarp = kWarps - 1;
+constexpr int kPollThreads = kStageWarp * 32;
 
 CTTS_DEV float ldcg(const float* p) { return __ldcg(p); }
 CTTS_DEV float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
@@ -139,21 +143,23 @@ CTTS_DEV LLMap ll_map(const DitGridArgs& a) {
   return {a.ll + o[0], a.ll + o[1], a.ll + o[2], a.ll + o[3]};
 }
 
-// n exchange words (n a multiple of 4) -> floats in shared memory, four
-// 16-byte groups per thread and pass
+// n exchange words (n a multiple of 4) -> floats in shared memory: the
+// threads of every warp but the staging one, eight 16-byte groups each per
+// pass (one pass for the QKV and SwiGLU rows of one utterance).
 CTTS_DEV void load_rows(const DitGridArgs& a, float* dst, const u64* src, int n, uint32_t tag) {
-  for (int i0 = threadIdx.x * 4; i0 < n; i0 += kThreads * 16) {
-    float4 v[4];
-    const u64* ps[4];
+  if (threadIdx.x >= kPollThreads) return;
+  for (int i0 = threadIdx.x * 4; i0 < n; i0 += kPollThreads * 32) {
+    float4 v[8];
+    const u64* ps[8];
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const int i = i0 + q * kThreads * 4;
+    for (int q = 0; q < 8; q++) {
+      const int i = i0 + q * kPollThreads * 4;
       ps[q] = i < n ? src + i : nullptr;
     }
-    ll_poll<4>(a, ps, tag, v);
+    ll_poll<8>(a, ps, tag, v);
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const int i = i0 + q * kThreads * 4;
+    for (int q = 0; q < 8; q++) {
+      const int i = i0 + q * kPollThreads * 4;
       if (i < n) *reinterpret_cast<float4*>(dst + i) = v[q];
     }
   }
@@ -185,7 +191,7 @@ CTTS_DEV void my_cols(int N, int& n0, int& n1) {
   n1 = (int)(((long)N * (blockIdx.x + 1)) / gridDim.x);
 }
 
-// ---- weight staging: before the barrier that opens a phase, warp 0
+// ---- weight staging: before the phase polls its inputs, the staging warp
 // copies the weight rows of this CTA's output columns of that phase into
 // the staging buffer with bulk copies (the weights do not depend on the
 // barrier), completing on one mbarrier; the phase waits on it.
@@ -264,15 +270,15 @@ CTTS_DEV uint32_t stage_aux(const DitGridArgs& a, Stage& st, int kind, int l, in
   return bytes;
 }
 
-// warp 0: lane 0 arms the mbarrier with the phase's byte count and copies
+// staging warp: lane 0 arms the mbarrier with the phase's byte count and copies
 // the small operands; the weight rows of this CTA's columns go as a few
 // large bulk copies, one per run of consecutive rows (consecutive columns
 // are consecutive rows except across a 64-column gate/up tile or, for the
 // output projection, across an utterance's latent columns).  Buffer layout:
 // [j][column - n0][K] (j: gate, up for the SwiGLU columns).
 CTTS_DEV void stage_weights(const DitGridArgs& a, Stage& st, int kind, int l, int stn = 0) {
-  if (threadIdx.x >= 32) return;
-  const int lane = threadIdx.x;
+  if (threadIdx.x < kStageWarp * 32) return;
+  const int lane = threadIdx.x - kStageWarp * 32;
   const KindGeom g = geom(a, kind, l);
   int n0, n1;
   my_cols(g.N, n0, n1);
@@ -315,7 +321,7 @@ CTTS_DEV void wait_weights(const DitGridArgs& a, Stage& st) {
 }
 
 // Rows of the residual stream -> RMSNorm (+ AdaLN modulate) into shared
-// memory xs[rows][H]: one warp per row (prep/linear_rows semantics: x * inv
+// memory xs[rows][H]: one polling warp per row (prep/linear_rows semantics: x * inv
 // * gain, then * (1 + scale) + shift).  Each warp polls its first row
 // before waiting on the staged gains and weights, so the staging copies
 // complete under the poll.
@@ -326,9 +332,9 @@ CTTS_DEV void norm_rows(const DitGridArgs& a, Stage& st, float* xs) {
   const int H = a.H, nv = H >> 7;
   const float* gain = st.aux;  // staged: gain [H], per utterance [shift | scale]
   float4 v[kMaxH4];
-  if (warp < rows) poll_row(a, st.ll.seq + (size_t)warp * H, nv, st.tag - 1, v);
+  if (warp < kStageWarp && warp < rows) poll_row(a, st.ll.seq + (size_t)warp * H, nv, st.tag - 1, v);
   wait_weights(a, st);
-  for (int r = warp; r < rows; r += kWarps) {
+  for (int r = warp; warp < kStageWarp && r < rows; r += kStageWarp) {
     if (r != warp) poll_row(a, st.ll.seq + (size_t)r * H, nv, st.tag - 1, v);
     float* dst = xs + (size_t)r * H;
     float ss = 0.0f;
@@ -564,8 +570,9 @@ CTTS_DEV void phase_fill(const DitGridArgs& a, Stage& st, int stn, float* sm) {
   const int H = a.H, L = a.L, R = a.R;
   if (idle_phase(a, st, H)) return;
   // x0 comes from before the launch; later steps' x from the output phase
-  for (int i = threadIdx.x; i < R * L; i += kThreads)
-    sm[i] = stn == 0 ? ldcg(a.x + i) : ll_get1(a, st.ll.x + i, st.tag - 1);
+  if (threadIdx.x < kPollThreads)
+    for (int i = threadIdx.x; i < R * L; i += kPollThreads)
+      sm[i] = stn == 0 ? ldcg(a.x + i) : ll_get1(a, st.ll.x + i, st.tag - 1);
   wait_weights(a, st);
   __syncthreads();
   int n0, n1;

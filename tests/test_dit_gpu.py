@@ -126,8 +126,8 @@ def test_cluster_euler_loop_matches_launch_chain(monkeypatch, adaln):
 def test_grid_euler_loop_matches_launch_chain(monkeypatch, adaln, B):
     """fp32, small batch: the grid-persistent Euler loop (one launch for all
     10 steps, CTTS_DIT_GRID unset) against the per-step launch chain
-    (CTTS_DIT_GRID=0) and the oracle, twice in a row (its barrier counters
-    must be back at zero after each launch)."""
+    (CTTS_DIT_GRID=0) and the oracle, twice in a row (the second launch
+    must not take the first one's exchange words for its own)."""
     cfg = DiTConfig(adaln=adaln)
     x0, z, c = rnd(31, (B, 64)), rnd(32, (B, 768)), rnd(33, (B, 64))
     spk = z if adaln else None
