@@ -46,7 +46,6 @@ constexpr int kStageWarp = kWarps - 1;
 constexpr int kPollThreads = kStageWarp * 32;
 
 CTTS_DEV float ldcg(const float* p) { return __ldcg(p); }
-CTTS_DEV float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
 // ---- flag-tagged exchange words
 using u64 = unsigned long long;
@@ -183,6 +182,73 @@ CTTS_DEV void row_dots(const float* w, int K, const float* xs, float* acc) {
   }
 #pragma unroll
   for (int r = 0; r < RW; r++) acc[r] = warp_sum(acc[r]);
+}
+
+CTTS_DEV float4 lds4(const float* p) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
+  return v;
+}
+
+// Dot products of NC weight rows w[c] (c < nc; the rest skipped) with RW
+// activation rows xs[r][K], all in shared memory: lanes over 4-element
+// groups of K, each activation group loaded once for every weight row,
+// and the NC x RW warp reductions independent of one another (their
+// shuffles overlap instead of running one reduction after the other).
+template <int RW, int NC>
+CTTS_DEV void warp_dots(const float* const (&w)[NC], int nc, int K, const float* xs, float (&acc)[NC][RW]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int c = 0; c < NC; c++)
+#pragma unroll
+    for (int r = 0; r < RW; r++) acc[c][r] = 0.0f;
+#pragma unroll 2
+  for (int k = lane * 4; k < K; k += 128) {
+    float4 xv[RW];
+#pragma unroll
+    for (int r = 0; r < RW; r++) xv[r] = lds4(xs + (size_t)r * K + k);
+#pragma unroll
+    for (int c = 0; c < NC; c++) {
+      if (c < nc) {
+        const float4 wv = lds4(w[c] + k);
+#pragma unroll
+        for (int r = 0; r < RW; r++)
+          acc[c][r] = fmaf(wv.x, xv[r].x, fmaf(wv.y, xv[r].y, fmaf(wv.z, xv[r].z, fmaf(wv.w, xv[r].w, acc[c][r]))));
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int c = 0; c < NC; c++)
+#pragma unroll
+      for (int r = 0; r < RW; r++) acc[c][r] += __shfl_xor_sync(0xffffffffu, acc[c][r], o);
+}
+
+// This warp's columns n0 + warp + kWarps t of the CTA's share [n0, n1),
+// two at a time.  Column n has PER staged weight rows (row j at
+// wbuf + (j (n1 - n0) + n - n0) K: gate then up for the SwiGLU columns);
+// emit(n, acc of row 0, acc of row PER - 1) runs on every lane.
+template <int RW, int PER, class Emit>
+CTTS_DEV void gemv_cols(const float* wbuf, int K, int n0, int n1, const float* xs, Emit emit) {
+  const int warp = threadIdx.x >> 5;
+  constexpr int NC = 2 * PER;
+  for (int n = n0 + warp; n < n1; n += 2 * kWarps) {
+    const int n2 = n + kWarps;
+    const bool two = n2 < n1;
+    const float* w[NC];
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+      w[j] = wbuf + ((size_t)j * (n1 - n0) + (n - n0)) * K;
+      w[PER + j] = two ? wbuf + ((size_t)j * (n1 - n0) + (n2 - n0)) * K : w[j];
+    }
+    float acc[NC][RW];
+    warp_dots<RW, NC>(w, two ? NC : PER, K, xs, acc);
+    emit(n, acc[0], acc[PER - 1]);
+    if (two) emit(n2, acc[PER], acc[NC - 1]);
+  }
 }
 
 // This CTA's share [n0, n1) of N output columns.
@@ -380,14 +446,12 @@ CTTS_DEV void phase_qkv(const DitGridArgs& a, Stage& st, int l, float* sm) {
   __syncthreads();
   int n0, n1;
   my_cols(qkvw, n0, n1);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int n = n0 + warp; n < n1; n += kWarps) {
-    float acc[RW];
-    row_dots<RW>(st.wbuf + (size_t)(n - n0) * H, H, sm, acc);
+  const int lane = threadIdx.x & 31;
+  gemv_cols<RW, 1>(st.wbuf, H, n0, n1, sm, [&](int n, const float* acc, const float*) {
     if (lane == 0)
 #pragma unroll
       for (int r = 0; r < rows; r++) ll_put(st.ll.qkv + (size_t)r * qkvw + n, acc[r], st.tag);
-  }
+  });
 }
 
 // P2: 3-token bidirectional attention with RoPE at positions 0..2 (every
@@ -456,9 +520,7 @@ CTTS_DEV void phase_attn_o(const DitGridArgs& a, Stage& st, int l, float* sm) {
   __syncthreads();
   int n0, n1;
   my_cols(H, n0, n1);
-  for (int n = n0 + warp; n < n1; n += kWarps) {
-    float acc[RW];
-    row_dots<RW>(st.wbuf + (size_t)(n - n0) * qd, qd, att, acc);
+  gemv_cols<RW, 1>(st.wbuf, qd, n0, n1, att, [&](int n, const float* acc, const float*) {
     if (lane == 0)
 #pragma unroll
       for (int r = 0; r < rows; r++) {
@@ -467,7 +529,7 @@ CTTS_DEV void phase_attn_o(const DitGridArgs& a, Stage& st, int l, float* sm) {
         *rv = *rv + coef * acc[r];
         ll_put(st.ll.seq + (size_t)r * H + n, *rv, st.tag);
       }
-  }
+  });
 }
 
 // P3: norm2 (+ modulate) -> this CTA's SwiGLU columns (staged as the gate
@@ -481,15 +543,12 @@ CTTS_DEV void phase_gate_up(const DitGridArgs& a, Stage& st, int l, float* sm) {
   __syncthreads();
   int n0, n1;
   my_cols(F, n0, n1);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int j = n0 + warp; j < n1; j += kWarps) {
-    float g[RW], u[RW];
-    row_dots<RW>(st.wbuf + (size_t)(j - n0) * H, H, sm, g);
-    row_dots<RW>(st.wbuf + (size_t)(n1 - n0 + j - n0) * H, H, sm, u);
+  const int lane = threadIdx.x & 31;
+  gemv_cols<RW, 2>(st.wbuf, H, n0, n1, sm, [&](int j, const float* g, const float* u) {
     if (lane == 0)
 #pragma unroll
       for (int r = 0; r < rows; r++) ll_put(st.ll.act + (size_t)r * F + j, silu(g[r]) * u[r], st.tag);
-  }
+  });
 }
 
 // P4: down over the SwiGLU rows -> gated residual.
@@ -503,10 +562,8 @@ CTTS_DEV void phase_down(const DitGridArgs& a, Stage& st, int l, float* sm) {
   __syncthreads();
   int n0, n1;
   my_cols(H, n0, n1);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int n = n0 + warp; n < n1; n += kWarps) {
-    float acc[RW];
-    row_dots<RW>(st.wbuf + (size_t)(n - n0) * F, F, sm, acc);
+  const int lane = threadIdx.x & 31;
+  gemv_cols<RW, 1>(st.wbuf, F, n0, n1, sm, [&](int n, const float* acc, const float*) {
     if (lane == 0)
 #pragma unroll
       for (int r = 0; r < rows; r++) {
@@ -515,7 +572,7 @@ CTTS_DEV void phase_down(const DitGridArgs& a, Stage& st, int l, float* sm) {
         *rv = *rv + coef * acc[r];
         ll_put(st.ll.seq + (size_t)r * H + n, *rv, st.tag);
       }
-  }
+  });
 }
 
 // T1: final norm of each utterance's x row (token 2), out_proj, Euler
