@@ -44,6 +44,7 @@ constexpr int kMaxH4 = 8;  // hidden <= 1024: 16-byte groups per lane of a row
 // others start polling its inputs (no row poll and no bulk poll uses it).
 constexpr int kStageWarp = kWarps - 1;
 constexpr int kPollThreads = kStageWarp * 32;
+constexpr int kRedFloats = kWarps * 4 * 12;  // K-split partial sums: warps x 4 columns x rows
 
 CTTS_DEV float ldcg(const float* p) { return __ldcg(p); }
 
@@ -251,10 +252,65 @@ CTTS_DEV void gemv_cols(const float* wbuf, int K, int n0, int n1, const float* x
   }
 }
 
+// The CTA's few output columns [n0, n1) (4 per pass) with K split over all
+// warps: each warp sums its K slice for every column and row, the warp
+// sums go through shared memory `red` and are added in warp order
+// (deterministic); emit(n, r, value) runs once per (column, row).
+template <int RW, class Emit>
+CTTS_DEV void gemv_ksplit(const float* wbuf, int K, int n0, int n1, const float* xs, float* red, Emit emit) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ks = ((K / 4 + kWarps - 1) / kWarps) * 4;
+  const int k0 = warp * ks, k1 = min(K, k0 + ks);
+  for (int c0 = n0; c0 < n1; c0 += 4) {
+    const int nc = min(4, n1 - c0);
+    float acc[4][RW];
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+#pragma unroll
+      for (int r = 0; r < RW; r++) acc[c][r] = 0.0f;
+    for (int k = k0 + lane * 4; k < k1; k += 128) {
+      float4 xv[RW];
+#pragma unroll
+      for (int r = 0; r < RW; r++) xv[r] = lds4(xs + (size_t)r * K + k);
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        if (c < nc) {
+          const float4 wv = lds4(wbuf + (size_t)(c0 - n0 + c) * K + k);
+#pragma unroll
+          for (int r = 0; r < RW; r++)
+            acc[c][r] = fmaf(wv.x, xv[r].x, fmaf(wv.y, xv[r].y, fmaf(wv.z, xv[r].z, fmaf(wv.w, xv[r].w, acc[c][r]))));
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int c = 0; c < 4; c++)
+#pragma unroll
+        for (int r = 0; r < RW; r++) acc[c][r] += __shfl_xor_sync(0xffffffffu, acc[c][r], o);
+    if (lane == 0)
+#pragma unroll
+      for (int c = 0; c < 4; c++)
+#pragma unroll
+        for (int r = 0; r < RW; r++) red[(warp * 4 + c) * RW + r] = acc[c][r];
+    __syncthreads();
+    for (int i = threadIdx.x; i < nc * RW; i += kThreads) {
+      const int c = i / RW, r = i % RW;
+      float v = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kWarps; w++) v += red[(w * 4 + c) * RW + r];
+      emit(c0 + c, r, v);
+    }
+    __syncthreads();
+  }
+}
+
 // This CTA's share [n0, n1) of N output columns.
+// (32-bit arithmetic: N * gridDim.x stays far below 2^32 for the supported
+// shapes, and a 64-bit division costs hundreds of cycles per phase.)
 CTTS_DEV void my_cols(int N, int& n0, int& n1) {
-  n0 = (int)(((long)N * blockIdx.x) / gridDim.x);
-  n1 = (int)(((long)N * (blockIdx.x + 1)) / gridDim.x);
+  n0 = (int)(((uint32_t)N * blockIdx.x) / gridDim.x);
+  n1 = (int)(((uint32_t)N * (blockIdx.x + 1)) / gridDim.x);
 }
 
 // ---- weight staging: before the phase polls its inputs, the staging warp
@@ -268,6 +324,7 @@ struct Stage {
   float* aux;    // the phase's small operands: norm gains, AdaLN rows, embeddings
   float* rope;   // [3 positions][cos 32, sin 32]
   float* resv;   // [rows][kMaxCols] this CTA's columns of the residual stream
+  float* red;    // [kWarps][4][rows] per-warp sums of the K-split GEMVs
   uint32_t bar;  // shared address of the mbarrier
   uint32_t ph;   // uses so far (parity of the next wait)
   LLMap ll;      // exchange areas
@@ -491,12 +548,24 @@ CTTS_DEV void phase_attn_o(const DitGridArgs& a, Stage& st, int l, float* sm) {
       k[s][0] = a1 * cs - a2 * sn;
       k[s][1] = a1 * sn + a2 * cs;
     }
+    // the nine query-key dot products reduced over the warp together
+    float dots[3][3];
+#pragma unroll
+    for (int i = 0; i < 3; i++)
+#pragma unroll
+      for (int j2 = 0; j2 < 3; j2++) dots[i][j2] = fmaf(q[i][0], k[j2][0], q[i][1] * k[j2][1]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int i = 0; i < 3; i++)
+#pragma unroll
+        for (int j2 = 0; j2 < 3; j2++) dots[i][j2] += __shfl_xor_sync(0xffffffffu, dots[i][j2], o);
 #pragma unroll
     for (int i = 0; i < 3; i++) {
       float sc[3], m = -INFINITY;
 #pragma unroll
       for (int j2 = 0; j2 < 3; j2++) {
-        sc[j2] = warp_sum(fmaf(q[i][0], k[j2][0], q[i][1] * k[j2][1])) * scale;
+        sc[j2] = dots[i][j2] * scale;
         m = fmaxf(m, sc[j2]);
       }
       float lsum = 0.0f;
@@ -520,15 +589,11 @@ CTTS_DEV void phase_attn_o(const DitGridArgs& a, Stage& st, int l, float* sm) {
   __syncthreads();
   int n0, n1;
   my_cols(H, n0, n1);
-  gemv_cols<RW, 1>(st.wbuf, qd, n0, n1, att, [&](int n, const float* acc, const float*) {
-    if (lane == 0)
-#pragma unroll
-      for (int r = 0; r < rows; r++) {
-        const float coef = a.ad ? 1.0f + st.aux[(size_t)(r / 3) * H + n] : 1.0f;
-        float* rv = st.resv + r * kMaxCols + (n - n0);
-        *rv = *rv + coef * acc[r];
-        ll_put(st.ll.seq + (size_t)r * H + n, *rv, st.tag);
-      }
+  gemv_ksplit<RW>(st.wbuf, qd, n0, n1, att, st.red, [&](int n, int r, float v) {
+    const float coef = a.ad ? 1.0f + st.aux[(size_t)(r / 3) * H + n] : 1.0f;
+    float* rv = st.resv + r * kMaxCols + (n - n0);
+    *rv = *rv + coef * v;
+    ll_put(st.ll.seq + (size_t)r * H + n, *rv, st.tag);
   });
 }
 
@@ -562,16 +627,11 @@ CTTS_DEV void phase_down(const DitGridArgs& a, Stage& st, int l, float* sm) {
   __syncthreads();
   int n0, n1;
   my_cols(H, n0, n1);
-  const int lane = threadIdx.x & 31;
-  gemv_cols<RW, 1>(st.wbuf, F, n0, n1, sm, [&](int n, const float* acc, const float*) {
-    if (lane == 0)
-#pragma unroll
-      for (int r = 0; r < rows; r++) {
-        const float coef = a.ad ? 1.0f + st.aux[(size_t)(r / 3) * H + n] : 1.0f;
-        float* rv = st.resv + r * kMaxCols + (n - n0);
-        *rv = *rv + coef * acc[r];
-        ll_put(st.ll.seq + (size_t)r * H + n, *rv, st.tag);
-      }
+  gemv_ksplit<RW>(st.wbuf, F, n0, n1, sm, st.red, [&](int n, int r, float v) {
+    const float coef = a.ad ? 1.0f + st.aux[(size_t)(r / 3) * H + n] : 1.0f;
+    float* rv = st.resv + r * kMaxCols + (n - n0);
+    *rv = *rv + coef * v;
+    ll_put(st.ll.seq + (size_t)r * H + n, *rv, st.tag);
   });
 }
 
@@ -666,7 +726,8 @@ struct GridSmem {
   __host__ __device__ size_t aux_off() const { return act_floats + w_floats; }
   __host__ __device__ size_t rope_off() const { return aux_off() + aux_floats; }
   __host__ __device__ size_t resv_off() const { return rope_off() + 192; }
-  __host__ __device__ size_t bar_off() const { return (resv_off() + DitGridArgs::kMaxRows * kMaxCols + 3) & ~(size_t)3; }
+  __host__ __device__ size_t red_off() const { return (resv_off() + DitGridArgs::kMaxRows * kMaxCols + 3) & ~(size_t)3; }
+  __host__ __device__ size_t bar_off() const { return red_off() + kRedFloats; }
 };
 __host__ __device__ inline size_t cdiv_sz(size_t a, size_t b) { return (a + b - 1) / b; }
 __host__ __device__ inline GridSmem grid_smem(int R, int H, int F, int nq, int nkv, int hd, int L, int G) {
@@ -693,6 +754,7 @@ __global__ void __launch_bounds__(kThreads, 1) dit_grid_kernel(const DitGridArgs
   st.aux = sm + gs.aux_off();
   st.rope = sm + gs.rope_off();
   st.resv = sm + gs.resv_off();
+  st.red = sm + gs.red_off();
   st.bar = static_cast<uint32_t>(__cvta_generic_to_shared(sm + gs.bar_off()));
   st.ph = 0;
   if (threadIdx.x < 96) {  // RoPE of token positions 0..2 (dit.rs:277-306)
