@@ -373,7 +373,7 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
 int dit_read_err(const DitWs& w) {
   int err = 0;
   CTTS_CK(cudaMemcpy(&err, w.err, sizeof(int), cudaMemcpyDeviceToHost));
-  CTTS_REQ(err == 0, CTTS_ERR_TIMEOUT, "a DiT kernel gave up waiting on its pipeline or grid barrier");
+  CTTS_REQ(err == 0, CTTS_ERR_TIMEOUT, "a DiT kernel gave up waiting on its pipeline, grid barrier or exchange words");
   return CTTS_OK;
 }
 
@@ -1010,7 +1010,7 @@ extern "C" int ctts_engine_step(ctts_engine* e, const float* noise, float* laten
     CTTS_CK(cudaMemcpy(&err, g.kv->err, sizeof(int), cudaMemcpyDeviceToHost));
     CTTS_CK(cudaMemcpy(&derr, g.ws->err, sizeof(int), cudaMemcpyDeviceToHost));
     CTTS_REQ(err != 1, CTTS_ERR_RANGE, "device reported a KV position outside capacity");
-    CTTS_REQ(err == 0 && derr == 0, CTTS_ERR_TIMEOUT, "a DiT kernel gave up waiting on its pipeline or grid barrier");
+    CTTS_REQ(err == 0 && derr == 0, CTTS_ERR_TIMEOUT, "a DiT kernel gave up waiting on its pipeline, grid barrier or exchange words");
   }
   memcpy(latents_out, e->h_lat, sizeof(float) * B * PL);
   if (stop_out) memcpy(stop_out, e->h_stop, sizeof(float) * B * 2);

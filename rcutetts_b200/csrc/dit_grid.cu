@@ -875,7 +875,7 @@ cudaError_t launch_rows(const DitGridArgs& a, size_t smem, cudaStream_t s) {
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the grid barriers need it
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the polled hand-overs need it
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
