@@ -143,3 +143,21 @@ def test_grid_euler_loop_matches_launch_chain(monkeypatch, adaln, B):
         assert rel_err(outs["1"][0][b], outs["0"][0][b]) < 1e-5, b
         ref = o.euler_sample(x0[b], z[b], c[b], spk[b] if adaln else None, 10)
         assert rel_err(outs["1"][0][b], ref) < 1e-4, b
+
+
+def test_grid_euler_loop_alternating_batches(monkeypatch):
+    """One model, grid-persistent loop launches of batch 3, 1, 3, 2 in turn:
+    each batch size lays out its exchange words differently in the shared
+    workspace, so words left by the previous launch sit where the next one
+    polls; their older generation tag must keep them from being taken.
+    Every launch matches the per-utterance oracle (1e-4)."""
+    monkeypatch.delenv("CTTS_DIT_GRID", raising=False)
+    cfg = DiTConfig(adaln=True)
+    m, w = dit_model(cfg, seed=27)
+    o = orc.DiT(cfg, w)
+    x0, z, c = rnd(41, (3, 64)), rnd(42, (3, 768)), rnd(43, (3, 64))
+    refs = [o.euler_sample(x0[b], z[b], c[b], z[b], 10) for b in range(3)]
+    for B in (3, 1, 3, 2):
+        out = m.euler_sample(x0[:B], z[:B], c[:B], z[:B], 10)
+        for b in range(B):
+            assert rel_err(out[b], refs[b]) < 1e-4, (B, b)
