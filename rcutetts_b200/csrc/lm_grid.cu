@@ -450,37 +450,53 @@ CTTS_DEV void attn_phase(const LmGridArgs& a, int l, float* sa) {
 }
 
 // The o-proj operand: every job's key-range partials merged in range order
-// (every CTA, redundantly) -> xs[r][hq * HD + d] = softmax(.) V.
+// (every CTA, redundantly) -> xs[r][hq * HD + d] = softmax(.) V.  The
+// partials of a thread's elements (kE at a time) are requested before the
+// range factors are computed, so the factors' loads and the values' loads
+// share one L2 round trip.
 template <int HD>
 CTTS_DEV void merge_attn(const LmGridArgs& a, float* xs, float* fac) {
-  const int S = attn_splits(a), jobs = a.R * a.nq, qd = a.nq * HD;
+  const int S = attn_splits(a), jobs = a.R * a.nq, qd = a.nq * HD, n = a.R * qd;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // a warp per job: lane sp holds range sp's (max, sum)
-  for (int job = warp; job < jobs; job += kWarps) {
-    const float* pp = a.part + (size_t)(job * S + lane) * (HD + 2);
-    const float ms = lane < S ? __ldcg(pp) : -INFINITY;
-    const float ls = lane < S ? __ldcg(pp + 1) : 0.0f;
-    float M = ms;
+  constexpr int kE = 4;
+  for (int i0 = 0; i0 < n; i0 += kE * kThreads) {
+    float v[kE][kMaxSplits];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    const float f = ms == -INFINITY ? 0.0f : expf(ms - M);
-    // the sum in range order (lane 0 gathers), deterministic
-    float L = 0.0f;
-    for (int sp = 0; sp < S; sp++) L = fmaf(__shfl_sync(0xffffffffu, ls, sp), __shfl_sync(0xffffffffu, f, sp), L);
-    if (lane < S) fac[job * S + lane] = f / L;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < a.R * qd; i += kThreads) {
-    const int r = i / qd, hq = (i % qd) / HD, d = i % HD, job = r * a.nq + hq;
-    const float* pp = a.part + (size_t)job * S * (HD + 2) + 2 + d;
-    float v[kMaxSplits];
+    for (int e = 0; e < kE; e++) {
+      const int i = i0 + threadIdx.x + e * kThreads;
+      const int r = i / qd, hq = (i % qd) / HD, d = i % HD, job = r * a.nq + hq;
+      const float* pp = a.part + (size_t)job * S * (HD + 2) + 2 + d;
 #pragma unroll
-    for (int sp = 0; sp < kMaxSplits; sp++) v[sp] = sp < S ? __ldcg(pp + (size_t)sp * (HD + 2)) : 0.0f;
-    float o = 0.0f;
+      for (int sp = 0; sp < kMaxSplits; sp++) v[e][sp] = (i < n && sp < S) ? __ldcg(pp + (size_t)sp * (HD + 2)) : 0.0f;
+    }
+    if (i0 == 0) {
+      // a warp per job: lane sp holds range sp's (max, sum)
+      for (int job = warp; job < jobs; job += kWarps) {
+        const float* pp = a.part + (size_t)(job * S + lane) * (HD + 2);
+        const float ms = lane < S ? __ldcg(pp) : -INFINITY;
+        const float ls = lane < S ? __ldcg(pp + 1) : 0.0f;
+        float M = ms;
 #pragma unroll
-    for (int sp = 0; sp < kMaxSplits; sp++)
-      if (sp < S) o = fmaf(v[sp], fac[job * S + sp], o);
-    xs[i] = o;
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float f = ms == -INFINITY ? 0.0f : expf(ms - M);
+        // the sum in range order (lane 0 gathers), deterministic
+        float L = 0.0f;
+        for (int sp = 0; sp < S; sp++) L = fmaf(__shfl_sync(0xffffffffu, ls, sp), __shfl_sync(0xffffffffu, f, sp), L);
+        if (lane < S) fac[job * S + lane] = f / L;
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int e = 0; e < kE; e++) {
+      const int i = i0 + threadIdx.x + e * kThreads;
+      if (i >= n) continue;
+      const int r = i / qd, hq = (i % qd) / HD, job = r * a.nq + hq;
+      float o = 0.0f;
+#pragma unroll
+      for (int sp = 0; sp < kMaxSplits; sp++)
+        if (sp < S) o = fmaf(v[e][sp], fac[job * S + sp], o);
+      xs[i] = o;
+    }
   }
 }
 
