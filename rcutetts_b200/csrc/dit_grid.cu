@@ -669,12 +669,14 @@ CTTS_DEV void phase_out(const DitGridArgs& a, Stage& st, int stp, float* sm) {
   my_cols(R * L, o0, o1);
   for (int o = o0 + warp; o < o1; o += kWarps) {
     const int u = o / L, l = o % L;
+    // the same thread updates latent column o at every step: its current
+    // value is fetched before the dot product instead of after
+    float* x = a.x + (size_t)u * L + l;
+    const float xo = lane == 0 ? ldcg(x) : 0.0f;
     float acc[1];
     row_dots<1>(st.wbuf + (size_t)(o - o0) * H, H, sm + (size_t)u * H, acc);
     if (lane == 0) {
-      // the same thread updates latent column o at every step
-      float* x = a.x + (size_t)u * L + l;
-      const float xn = ldcg(x) + a.dts[stp] * (acc[0] + (a.out_b ? a.out_b[l] : 0.0f));
+      const float xn = xo + a.dts[stp] * (acc[0] + (a.out_b ? a.out_b[l] : 0.0f));
       *x = xn;
       ll_put(st.ll.x + o, xn, st.tag);
     }

@@ -218,10 +218,19 @@ CTTS_DEV void norm_rows(const LmGridArgs& a, const float* gain, float* xs) {
   }
 }
 
-// n floats of intra-kernel data (global, L2-coherent) -> xs
+// n floats of intra-kernel data (global, L2-coherent) -> xs: four 16-byte
+// loads per thread issued before any of their stores (a store through a
+// generic pointer would otherwise hold back the next load)
 CTTS_DEV void load_rows(const float* src, int n, float* xs) {
-  for (int i = threadIdx.x * 4; i < n; i += kThreads * 4)
-    *reinterpret_cast<float4*>(xs + i) = ldcg4(src + i);
+  for (int i0 = threadIdx.x * 4; i0 < n; i0 += kThreads * 16) {
+    float4 v[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+      if (i0 + q * kThreads * 4 < n) v[q] = ldcg4(src + i0 + q * kThreads * 4);
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+      if (i0 + q * kThreads * 4 < n) *reinterpret_cast<float4*>(xs + i0 + q * kThreads * 4) = v[q];
+  }
 }
 
 // This CTA's output columns of phase `kind`: warp per column, lanes over
@@ -233,7 +242,13 @@ CTTS_DEV void gemv(const LmGridArgs& a, Stage& st, int kind, int b, const float*
   wait_stage(a, st, b);
   __syncthreads();  // xs complete
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, K = g.K, R = a.R;
+  const bool resid = kind == kO || kind == kD;
   for (int n = n0 + warp; n < n1; n += kWarps) {
+    // the residual entries this column updates (written by this CTA's own
+    // earlier phases), fetched before the dot products instead of after
+    float yold[kMaxRows];
+#pragma unroll
+    for (int r = 0; r < kMaxRows; r++) yold[r] = (resid && lane == 0 && r < R) ? __ldcg(a.h + (size_t)r * a.H + n) : 0.0f;
     float acc[2][kMaxRows];
 #pragma unroll
     for (int j = 0; j < 2; j++)
@@ -268,8 +283,7 @@ CTTS_DEV void gemv(const LmGridArgs& a, Stage& st, int kind, int b, const float*
         } else if (kind == kG) {
           a.act[(size_t)r * a.F + n] = silu(acc[0][r]) * acc[1][r];
         } else {  // o-proj / down: residual
-          float* y = a.h + (size_t)r * a.H + n;
-          *y = __ldcg(y) + acc[0][r];
+          a.h[(size_t)r * a.H + n] = yold[r] + acc[0][r];
         }
       }
     }
