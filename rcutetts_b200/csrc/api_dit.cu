@@ -242,7 +242,7 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
     ga.R = R; ga.NL = NL; ga.steps = r.steps; ga.H = H; ga.nq = c.n_heads; ga.nkv = c.n_kv_heads;
     ga.hd = c.head_dim; ga.F = F; ga.L = L; ga.eps = c.rms_eps;
     for (int i = 0; i < r.steps; i++) ga.dts[i] = r.dts[i];
-    ga.seq = w.seq; ga.qkv = w.qkv; ga.act = w.act; ga.x = r.x;
+    ga.x = r.x;
     ga.mu = w.mu; ga.temb = w.temb; ga.dtemb = w.dtemb; ga.condh = w.condh; ga.ad = use_ad ? w.ad : nullptr;
     ga.inv_freq = d->inv_freq; ga.final_norm = d->final_norm;
     ga.in_w = static_cast<const float*>(d->in_w); ga.in_b = d->in_b;

@@ -14,9 +14,6 @@ struct DitGridArgs {
   int H = 0, nq = 0, nkv = 0, hd = 0, F = 0, L = 0;
   float eps = 1e-6f;
   float dts[kMaxSteps];
-  float* seq = nullptr;           // [3R, H] residual stream (workspace)
-  float* qkv = nullptr;           // [3R, (nq+2nkv)*hd]
-  float* act = nullptr;           // [3R, F]
   float* x = nullptr;             // [R, L] in: x0, out: x after `steps` Euler steps
   const float* mu = nullptr;      // [R, H]
   const float* temb = nullptr;    // [steps, H]
