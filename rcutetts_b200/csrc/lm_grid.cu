@@ -233,57 +233,80 @@ CTTS_DEV void load_rows(const float* src, int n, float* xs) {
   }
 }
 
-// This CTA's output columns of phase `kind`: warp per column, lanes over
-// 4-element groups of K, the R rows of xs [R][K] advancing together.
+// This CTA's output columns of phase `kind`: each warp takes two columns
+// (n and n + kWarps) per pass, lanes over 4-element groups of K, the RW
+// rows of xs [RW][K] loaded once for both columns; the warp reductions of
+// all (column, weight row, row) sums run interleaved, not one after another.
+// The residual entries an o-proj / down column updates (written by this
+// CTA's own earlier phases) are fetched before the dot products.
+template <int RW>
 CTTS_DEV void gemv(const LmGridArgs& a, Stage& st, int kind, int b, const float* xs) {
   const Geo g = geo(a, kind);
   int n0, n1;
   cols_of(g.N, blockIdx.x, gridDim.x, n0, n1);
   wait_stage(a, st, b);
   __syncthreads();  // xs complete
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, K = g.K, R = a.R;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, K = g.K;
   const bool resid = kind == kO || kind == kD;
-  for (int n = n0 + warp; n < n1; n += kWarps) {
-    // the residual entries this column updates (written by this CTA's own
-    // earlier phases), fetched before the dot products instead of after
-    float yold[kMaxRows];
+  const float* wb = reinterpret_cast<const float*>(st.buf[b]);
+  for (int n = n0 + warp; n < n1; n += 2 * kWarps) {
+    const int nb = n + kWarps;
+    const bool two = nb < n1;
+    float yold[2][RW];
 #pragma unroll
-    for (int r = 0; r < kMaxRows; r++) yold[r] = (resid && lane == 0 && r < R) ? __ldcg(a.h + (size_t)r * a.H + n) : 0.0f;
-    float acc[2][kMaxRows];
+    for (int c = 0; c < 2; c++)
 #pragma unroll
-    for (int j = 0; j < 2; j++)
+      for (int r = 0; r < RW; r++)
+        yold[c][r] = (resid && lane == 0 && (c == 0 || two)) ? __ldcg(a.h + (size_t)r * a.H + (c ? nb : n)) : 0.0f;
+    float acc[2][2][RW];  // [column][weight row j][activation row]
 #pragma unroll
-      for (int r = 0; r < kMaxRows; r++) acc[j][r] = 0.0f;
+    for (int c = 0; c < 2; c++)
 #pragma unroll
-    for (int j = 0; j < 2; j++) {
-      if (j >= g.rows_per) break;
-      const float* w = reinterpret_cast<const float*>(st.buf[b]) + ((size_t)j * (n1 - n0) + (n - n0)) * K;
-      for (int k = lane * 4; k < K; k += 128) {
-        const float4 wv = *reinterpret_cast<const float4*>(w + k);
+      for (int j = 0; j < 2; j++)
 #pragma unroll
-        for (int r = 0; r < kMaxRows; r++) {
-          if (r >= R) break;
-          const float4 xv = *reinterpret_cast<const float4*>(xs + (size_t)r * K + k);
-          acc[j][r] = fmaf(wv.x, xv.x, fmaf(wv.y, xv.y, fmaf(wv.z, xv.z, fmaf(wv.w, xv.w, acc[j][r]))));
+        for (int r = 0; r < RW; r++) acc[c][j][r] = 0.0f;
+    for (int k = lane * 4; k < K; k += 128) {
+      float4 xv[RW];
+#pragma unroll
+      for (int r = 0; r < RW; r++) xv[r] = *reinterpret_cast<const float4*>(xs + (size_t)r * K + k);
+#pragma unroll
+      for (int c = 0; c < 2; c++) {
+        if (c == 1 && !two) break;
+        const int nc = c ? nb : n;
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+          if (j >= g.rows_per) break;
+          const float4 wv = *reinterpret_cast<const float4*>(wb + ((size_t)j * (n1 - n0) + (nc - n0)) * K + k);
+#pragma unroll
+          for (int r = 0; r < RW; r++)
+            acc[c][j][r] = fmaf(wv.x, xv[r].x, fmaf(wv.y, xv[r].y, fmaf(wv.z, xv[r].z, fmaf(wv.w, xv[r].w, acc[c][j][r]))));
         }
       }
     }
 #pragma unroll
-    for (int j = 0; j < 2; j++)
+    for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-      for (int r = 0; r < kMaxRows; r++)
-        if (j < g.rows_per && r < R) acc[j][r] = warp_sum(acc[j][r]);
+      for (int c = 0; c < 2; c++)
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+#pragma unroll
+          for (int r = 0; r < RW; r++)
+            if ((c == 0 || two) && j < g.rows_per) acc[c][j][r] += __shfl_xor_sync(0xffffffffu, acc[c][j][r], o);
     if (lane == 0) {
       const int qkvw = (a.nq + 2 * a.nkv) * a.hd;
 #pragma unroll
-      for (int r = 0; r < kMaxRows; r++) {
-        if (r >= R) break;
-        if (kind == kQ) {
-          a.qkv[(size_t)r * qkvw + n] = acc[0][r];
-        } else if (kind == kG) {
-          a.act[(size_t)r * a.F + n] = silu(acc[0][r]) * acc[1][r];
-        } else {  // o-proj / down: residual
-          a.h[(size_t)r * a.H + n] = yold[r] + acc[0][r];
+      for (int c = 0; c < 2; c++) {
+        if (c == 1 && !two) break;
+        const int nc = c ? nb : n;
+#pragma unroll
+        for (int r = 0; r < RW; r++) {
+          if (kind == kQ) {
+            a.qkv[(size_t)r * qkvw + nc] = acc[c][0][r];
+          } else if (kind == kG) {
+            a.act[(size_t)r * a.F + nc] = silu(acc[c][0][r]) * acc[c][1][r];
+          } else {  // o-proj / down: residual
+            a.h[(size_t)r * a.H + nc] = yold[c][r] + acc[c][0][r];
+          }
         }
       }
     }
@@ -514,7 +537,7 @@ CTTS_DEV void merge_attn(const LmGridArgs& a, float* xs, float* fac) {
   }
 }
 
-template <int HD>
+template <int HD, int RW>
 __global__ void __launch_bounds__(kThreads, 1) lm_grid_kernel(const LmGridArgs a) {
   extern __shared__ __align__(128) uint8_t smraw[];
   const Smem m = smem_of(a.R, a.H, a.nq, a.nkv, HD, a.F, gridDim.x);
@@ -540,24 +563,24 @@ __global__ void __launch_bounds__(kThreads, 1) lm_grid_kernel(const LmGridArgs a
   int k = 0;
   for (int l = 0; l < a.NL; l++) {
     norm_rows(a, a.norm1[l], xs);
-    gemv(a, st, kQ, 0, xs);
+    gemv<RW>(a, st, kQ, 0, xs);
     __syncthreads();
     stage(a, st, kG, l, 0);
     grid_sync(a, k++);
     attn_phase<HD>(a, l, sa);
     grid_sync(a, k++);
     merge_attn<HD>(a, xs, sa);
-    gemv(a, st, kO, 1, xs);
+    gemv<RW>(a, st, kO, 1, xs);
     __syncthreads();
     stage(a, st, kD, l, 1);
     grid_sync(a, k++);
     norm_rows(a, a.norm2[l], xs);
-    gemv(a, st, kG, 0, xs);
+    gemv<RW>(a, st, kG, 0, xs);
     __syncthreads();
     if (l + 1 < a.NL) stage(a, st, kQ, l + 1, 0);
     grid_sync(a, k++);
     load_rows(a.act, a.R * a.F, xs);
-    gemv(a, st, kD, 1, xs);
+    gemv<RW>(a, st, kD, 1, xs);
     __syncthreads();
     if (l + 1 < a.NL) stage(a, st, kO, l + 1, 1);
     grid_sync(a, k++);
@@ -591,9 +614,9 @@ int grid_ctas() {
   return n;
 }
 
-template <int HD>
+template <int HD, int RW>
 cudaError_t launch_t(const LmGridArgs& a, size_t smem, cudaStream_t s) {
-  auto kern = lm_grid_kernel<HD>;
+  auto kern = lm_grid_kernel<HD, RW>;
   static size_t configured = 0;
   if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -638,7 +661,14 @@ cudaError_t launch_lm_grid(const LmGridArgs& a, cudaStream_t s) {
   if (!lm_grid_supported(a.R, a.NL, a.H, a.nq, a.nkv, a.hd, a.F) || !a.bar || !a.h || !a.out || !a.pos || !a.part)
     return cudaErrorInvalidValue;
   const size_t smem = smem_of(a.R, a.H, a.nq, a.nkv, a.hd, a.F, grid_ctas()).total(a.hd);
-  return a.hd == 64 ? launch_t<64>(a, smem, s) : launch_t<128>(a, smem, s);
+  // the utterance count is a template parameter: the GEMV accumulators of
+  // exactly R rows stay in registers
+  switch (a.R) {
+    case 1: return a.hd == 64 ? launch_t<64, 1>(a, smem, s) : launch_t<128, 1>(a, smem, s);
+    case 2: return a.hd == 64 ? launch_t<64, 2>(a, smem, s) : launch_t<128, 2>(a, smem, s);
+    case 3: return a.hd == 64 ? launch_t<64, 3>(a, smem, s) : launch_t<128, 3>(a, smem, s);
+    default: return a.hd == 64 ? launch_t<64, 4>(a, smem, s) : launch_t<128, 4>(a, smem, s);
+  }
 }
 
 }  // namespace ctts
