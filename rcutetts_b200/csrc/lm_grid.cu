@@ -32,7 +32,6 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kMaxRows = LmGridArgs::kMaxRows;
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr int kMaxCtas = 1024;  // grid size bound (one CTA per SM)
 
