@@ -30,10 +30,44 @@ int orc_get_threads(void) { return g_nth; }
  * (micro_8x8_fma): accumulator starts at the bias, then one FMA per k in
  * ascending order.  Threads split output rows like qwen.rs:177-208
  * (disjoint rows => bitwise identical for any thread count). */
+/* Many rows: x transposed to [I][S padded to 16] once, then each output
+ * runs 16 rows side by side (one vector FMA per k); every output still
+ * starts at its bias and takes one fmaf per k in ascending order, so the
+ * result is bitwise the one of the row-by-row loop below. */
+#define ORC_ROWS 16
+static void linear_many_rows(const float* x, int S, int I, const float* W, const float* b, int O,
+                             float* y, int nth) {
+  const int Sp = (S + ORC_ROWS - 1) / ORC_ROWS * ORC_ROWS;
+  float* xt = calloc((size_t)I * Sp, sizeof(float));
+  for (int s = 0; s < S; s++)
+    for (int i = 0; i < I; i++) xt[(size_t)i * Sp + s] = x[(size_t)s * I + i];
+#pragma omp parallel for schedule(static) num_threads(nth) collapse(2)
+  for (int o = 0; o < O; o++) {
+    for (int s0 = 0; s0 < Sp; s0 += ORC_ROWS) {
+      const float* wr = W + (size_t)o * I;
+      const float bias = b ? b[o] : 0.0f;
+      float acc[ORC_ROWS];
+      for (int j = 0; j < ORC_ROWS; j++) acc[j] = bias;
+      for (int i = 0; i < I; i++) {
+        const float wv = wr[i];
+        const float* xr = xt + (size_t)i * Sp + s0;
+        for (int j = 0; j < ORC_ROWS; j++) acc[j] = fmaf(wv, xr[j], acc[j]);
+      }
+      const int ns = S - s0 < ORC_ROWS ? S - s0 : ORC_ROWS;
+      for (int j = 0; j < ns; j++) y[(size_t)(s0 + j) * O + o] = acc[j];
+    }
+  }
+  free(xt);
+}
+
 void orc_linear(const float* x, int S, int I, const float* W, const float* b, int O,
                 float* y) {
   long ops = (long)S * I * O;
   int nth = ops >= 1000000 ? g_nth : 1;
+  if (S >= ORC_ROWS) {
+    linear_many_rows(x, S, I, W, b, O, y, nth);
+    return;
+  }
   const int nblk = (O + 7) / 8;
   /* eight output rows per task, each with its own sequential FMA chain
    * (the gemv8 panel shape); per-output arithmetic is unchanged. */
@@ -171,31 +205,45 @@ void orc_lm_layer(const orc_lm_dims* d, const orc_lm_layer_w* w, const float* h,
   const int group = nq / nkv;
   int ncache = len + T;
   int nth = (long)ncache * T * nq * hd >= 200000 ? g_nth : 1;
+  /* Every score is sum_dd q*k in dd order and every output sum_j p*v in j
+   * order, as in qwen.rs:341-362; the loops run many keys (scores, keys
+   * transposed once per call) or many dims (outputs) side by side. */
+  float* kt = malloc(sizeof(float) * (size_t)nkv * hd * ncache);
+  for (int kh = 0; kh < nkv; kh++)
+    for (int j = 0; j < ncache; j++)
+      for (int dd = 0; dd < hd; dd++)
+        kt[((size_t)kh * hd + dd) * ncache + j] = kc[(size_t)j * kvdim + kh * hd + dd];
 #pragma omp parallel num_threads(nth)
   {
     float* scores = malloc(sizeof(float) * ncache);
+    float* acc = malloc(sizeof(float) * hd);
 #pragma omp for schedule(static) collapse(2)
     for (int hh = 0; hh < nq; hh++) {
       for (int i = 0; i < T; i++) {
         int kh = hh / group;
         int n = len + i + 1;
         const float* qi = q + (size_t)i * qdim + hh * hd;
-        for (int j = 0; j < n; j++) {
-          const float* kj = kc + (size_t)j * kvdim + kh * hd;
-          float acc = 0.0f;
-          for (int dd = 0; dd < hd; dd++) acc += qi[dd] * kj[dd];
-          scores[j] = acc * scale;
-        }
-        orc_softmax_row(scores, n);
+        for (int j = 0; j < n; j++) scores[j] = 0.0f;
         for (int dd = 0; dd < hd; dd++) {
-          float acc = 0.0f;
-          for (int j = 0; j < n; j++) acc += scores[j] * vc[(size_t)j * kvdim + kh * hd + dd];
-          att[(size_t)i * qdim + hh * hd + dd] = acc;
+          const float qv = qi[dd];
+          const float* kr = kt + ((size_t)kh * hd + dd) * ncache;
+          for (int j = 0; j < n; j++) scores[j] += qv * kr[j];
         }
+        for (int j = 0; j < n; j++) scores[j] *= scale;
+        orc_softmax_row(scores, n);
+        for (int dd = 0; dd < hd; dd++) acc[dd] = 0.0f;
+        for (int j = 0; j < n; j++) {
+          const float p = scores[j];
+          const float* vr = vc + (size_t)j * kvdim + kh * hd;
+          for (int dd = 0; dd < hd; dd++) acc[dd] += p * vr[dd];
+        }
+        for (int dd = 0; dd < hd; dd++) att[(size_t)i * qdim + hh * hd + dd] = acc[dd];
       }
     }
     free(scores);
+    free(acc);
   }
+  free(kt);
   orc_linear(att, T, qdim, w->wo, NULL, H, proj);
   float* h2 = out;
   for (size_t i = 0; i < (size_t)T * H; i++) h2[i] = h[i] + proj[i];
@@ -542,17 +590,25 @@ void orc_causal_conv1d(const float* x, int c_in, int T, const float* w, const fl
       }
       continue;
     }
-    for (int t = 0; t < T; t++) {
-      float acc = b[o];
+    /* Each output sample is bias, then + x*w over channels ascending and
+     * taps ascending (taps before the signal start skipped), one rounding
+     * per product and per add.  The loop runs that sequence for a block of
+     * samples at once (time innermost, vectorised); the per-sample order is
+     * the one of conv.rs:53-115. */
+    enum { TB = 2048 };
+    for (int t0 = 0; t0 < T; t0 += TB) {
+      const int t1 = t0 + TB < T ? t0 + TB : T;
+      for (int t = t0; t < t1; t++) orow[t] = b[o];
       for (int ci = 0; ci < cig; ci++) {
         const float* xr = x + (size_t)(c0 + ci) * T;
         const float* wr = w + ((size_t)o * cig + ci) * k;
         for (int kk = 0; kk < k; kk++) {
-          int src = t + kk * dil - left;
-          if (src >= 0) acc += xr[src] * wr[kk];
+          const int off = kk * dil - left;
+          const int ts = t0 > -off ? t0 : -off;
+          const float wv = wr[kk];
+          for (int t = ts; t < t1; t++) orow[t] += xr[t + off] * wv;
         }
       }
-      orow[t] = acc;
     }
   }
 }

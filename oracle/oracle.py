@@ -34,11 +34,19 @@ def lib():
             build()
         _lib = C.CDLL(_LIB_PATH)
         _lib.orc_embed_lookup.restype = C.c_int
+        _lib.orc_get_threads.restype = C.c_int
+        # every output is computed by one thread in a fixed order, so the
+        # results are bitwise the same for any thread count: use them all
+        _lib.orc_set_threads(int(os.cpu_count() or 1))
     return _lib
 
 
 def set_threads(n: int) -> None:
     lib().orc_set_threads(int(n))
+
+
+def get_threads() -> int:
+    return int(lib().orc_get_threads())
 
 
 def _p(a):

@@ -208,18 +208,28 @@ def test_vae_causal_prefix():
     assert np.array_equal(full[:4 * cfg.hop], part)
 
 
-def test_linear_threads_bitwise():
+@pytest.mark.parametrize("rows", [3, 37])
+def test_linear_threads_bitwise(rows):
+    """Few rows (eight-output FMA panels) and many rows (16 rows side by
+    side): bitwise the same for any thread count, and the many-row path
+    bitwise equal to running its rows one at a time."""
     rng = np.random.default_rng(0)
-    x = rng.standard_normal((3, 700), dtype=np.float32)
+    x = rng.standard_normal((rows, 700), dtype=np.float32)
     W = rng.standard_normal((2000, 700), dtype=np.float32)
-    orc.set_threads(1)
-    a = orc.linear(x, W)
-    orc.set_threads(4)
-    b = orc.linear(x, W)
-    orc.set_threads(1)
-    assert np.array_equal(a, b)
-    ref = (x.astype(np.float64) @ W.T.astype(np.float64))
-    assert rel_err(a, ref) < 1e-5
+    b = rng.standard_normal(2000, dtype=np.float32)
+    prev = orc.get_threads()
+    try:
+        orc.set_threads(1)
+        one = orc.linear(x, W, b)
+        orc.set_threads(4)
+        four = orc.linear(x, W, b)
+    finally:
+        orc.set_threads(prev)
+    assert np.array_equal(one, four)
+    by_row = np.concatenate([orc.linear(x[i:i + 1], W, b) for i in range(rows)])
+    assert np.array_equal(one, by_row)
+    ref = (x.astype(np.float64) @ W.T.astype(np.float64)) + b
+    assert rel_err(one, ref) < 1e-5
 
 
 def test_locenc_vs_torch_module(golden):
