@@ -52,6 +52,18 @@ extern "C" {
 
 /* One line describing the last error on this thread ("" if none). */
 CTTS_API const char* ctts_last_error(void);
+/* Error-path testing of the bounded device waits.  The reference's
+ * analogue is the panic -> -1 contract of rust-codec/src/ffi.rs:51-64 (no
+ * direct counterpart).  While `skip` is non-zero, launches of the
+ * small-batch fp32 DiT grid loop enqueued afterwards run with CTA 0 leaving
+ * its QKV outputs unwritten, so the attention phase polls exchange words no
+ * producer writes; every poll gives up after `spin_limit` tries (0 = the
+ * default, about four million).  The kernel records the timeout and runs to
+ * its end; the host call that reads the DiT error word returns
+ * CTTS_ERR_TIMEOUT and clears it, and the device stays usable.
+ * Process-wide, off by default; frames already captured in a CUDA graph
+ * keep the setting they were captured with. */
+CTTS_API int ctts_debug_inject_wait_fault(int skip, unsigned spin_limit);
 /* Library version string. */
 CTTS_API const char* ctts_version(void);
 
@@ -290,9 +302,9 @@ CTTS_API int ctts_op_linear(const float* x, int M, int K, const void* w, int w_d
 /* ctts_op_linear without any device allocation.  No counterpart in the
  * reference (whose CPU kernels allocate host vectors freely): for callers
  * that cannot call cudaMalloc -- a process whose device heap is owned by
- * its own pool, or code that must not allocate after set-up (during a
- * stream capture, or in a serving loop that cannot afford cudaMalloc's
- * implicit synchronization).  Same arguments and results as ctts_op_linear.
+ * its own pool, or a serving loop that must not allocate after set-up
+ * because it cannot afford cudaMalloc's implicit device-wide
+ * synchronization.  Same arguments and results as ctts_op_linear.
  * The bf16 tensor-core path (w_dtype CTTS_BF16, M >= 16, K % 64 == 0) keeps
  * its bf16 activation operand in a static device array of 2^20 elements
  * (2 MiB, held by every GPU that loads this library until exit) instead of
@@ -300,7 +312,9 @@ CTTS_API int ctts_op_linear(const float* x, int M, int K, const void* w, int w_d
  * on a device looks the array's device address up (cudaGetSymbolAddress),
  * so make it before any stream capture.  All calls share the array: calls
  * that overlap on the GPU (different streams, or threads on one device)
- * race on it, so serialize them. */
+ * race on it, so serialize them.  Asynchronous like ctts_op_linear: a
+ * bounded device-side wait that gives up ends the kernel early without a
+ * hang but is not reported in the return code. */
 CTTS_API int ctts_op_linear_noalloc(const float* x, int M, int K, const void* w, int w_dtype, int N,
                                     const float* norm_w, float eps, const float* res, float* y,
                                     void* stream);

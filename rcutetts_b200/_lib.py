@@ -55,6 +55,7 @@ class VAEConfigC(C.Structure):
 SIGNATURES = {
     "ctts_last_error": (C.c_char_p, []),
     "ctts_version": (C.c_char_p, []),
+    "ctts_debug_inject_wait_fault": (C.c_int, [C.c_int, C.c_uint]),
     "ctts_lm_create": (C.c_int, [C.POINTER(LMConfigC), C.c_int, C.POINTER(vp)]),
     "ctts_lm_set_tensor": (C.c_int, [vp, C.c_char_p, vp, C.c_int, i64p, C.c_int]),
     "ctts_lm_load": (C.c_int, [vp, C.c_char_p, C.c_char_p]),

@@ -205,12 +205,9 @@ inline int tc_run(const TcScratch& sc, const uint16_t* x, int M, int K, const vo
   c.counters = sc.counters;
   c.counter_count = sc.ncounters;
   c.err = sc.err;
+  // split-K partials are reduced in the cluster's shared memory: the plan
+  // needs no global scratch, so any K split the planner picks can run
   c.max_splitk = M > 256 ? 1 : 64;
-  while (c.max_splitk > 1) {
-    TcPlan p = tc_plan(M, N, K, tc_num_sms(), c.max_splitk);
-    if (tc_scratch_floats(p) <= sc.part_floats && p.ntiles * p.mtiles <= sc.ncounters) break;
-    c.max_splitk = std::max(1, p.splitk / 2);
-  }
   cudaError_t e = launch_tc_linear(c, s);
   if (e != cudaSuccess) {
     (void)cudaGetLastError();

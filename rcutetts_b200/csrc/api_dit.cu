@@ -1,6 +1,7 @@
 // api_dit.cu -- C ABI: the DiT flow head (dit.rs / diffusion_head.py) and
 // the per-frame engine (bin/cutetts.rs:429-523 loop body) captured as one
 // CUDA graph per frame.
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 
@@ -10,6 +11,11 @@
 using namespace ctts;
 
 namespace {
+
+// Injected wait fault of the small-batch DiT grid loop (error-path tests;
+// ctts_debug_inject_wait_fault), read when a launch is enqueued.
+std::atomic<int> g_fault_skip{0};
+std::atomic<uint32_t> g_fault_spin_limit{0};
 
 int dit_ws_ensure(ctts_dit* d, DitWs& w, int rows, int steps) {
   if (w.rows >= rows && w.steps >= steps) return CTTS_OK;
@@ -254,6 +260,8 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
       ga.norm1[l] = Ly.norm1; ga.norm2[l] = Ly.norm2;
     }
     ga.bar = w.gbar; ga.ll = w.gll; ga.err = w.err;
+    ga.skip_qkv_cta0 = g_fault_skip.load(std::memory_order_relaxed);
+    ga.spin_limit = g_fault_spin_limit.load(std::memory_order_relaxed);
     CTTS_CK(ctts::launch_dit_grid(ga, s)); nl++;
     if (launches) *launches += nl;
     return CTTS_OK;
@@ -369,10 +377,12 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
   return CTTS_OK;
 }
 
-// Reads back the workspace's device error flag after a synchronized run.
+// Reads back the workspace's device error flag after a synchronized run;
+// a reported error is cleared, so the next run starts clean.
 int dit_read_err(const DitWs& w) {
   int err = 0;
   CTTS_CK(cudaMemcpy(&err, w.err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err != 0) CTTS_CK(cudaMemset(w.err, 0, sizeof(int)));
   CTTS_REQ(err == 0, CTTS_ERR_TIMEOUT, "a DiT kernel gave up waiting on its pipeline, grid barrier or exchange words");
   return CTTS_OK;
 }
@@ -1009,6 +1019,8 @@ extern "C" int ctts_engine_step(ctts_engine* e, const float* noise, float* laten
     int err = 0, derr = 0;
     CTTS_CK(cudaMemcpy(&err, g.kv->err, sizeof(int), cudaMemcpyDeviceToHost));
     CTTS_CK(cudaMemcpy(&derr, g.ws->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err != 0) CTTS_CK(cudaMemset(g.kv->err, 0, sizeof(int)));
+    if (derr != 0) CTTS_CK(cudaMemset(g.ws->err, 0, sizeof(int)));
     CTTS_REQ(err != 1, CTTS_ERR_RANGE, "device reported a KV position outside capacity");
     CTTS_REQ(err == 0 && derr == 0, CTTS_ERR_TIMEOUT, "a DiT kernel gave up waiting on its pipeline, grid barrier or exchange words");
   }
@@ -1024,4 +1036,10 @@ extern "C" void* ctts_engine_stream(const ctts_engine* e) { return e ? (void*)e-
 extern "C" void ctts_engine_free(ctts_engine* e) {
   if (!e) return;
   engine_destroy(e);
+}
+
+extern "C" int ctts_debug_inject_wait_fault(int skip, unsigned spin_limit) {
+  g_fault_skip.store(skip ? 1 : 0, std::memory_order_relaxed);
+  g_fault_spin_limit.store(spin_limit, std::memory_order_relaxed);
+  return CTTS_OK;
 }

@@ -6,20 +6,25 @@
 // that operand in a per-device buffer it allocates (cudaMalloc) on first use
 // and grows on demand.  Callers that cannot allocate device memory -- a host
 // process that owns the whole device heap through its own pool or arena, or
-// code that must not allocate once set up (inside a stream capture, or in a
-// latency-critical serving loop where cudaMalloc's implicit synchronization
-// is not acceptable) -- use this variant instead.  Its operand lives in a
-// file-scope __device__ array of fixed size, so each GPU that loads this
-// library holds that array until the process exits.
+// a latency-critical serving loop that must not allocate once set up, where
+// cudaMalloc's implicit device-wide synchronization is not acceptable -- use
+// this variant instead.  Its operand lives in a file-scope __device__ array
+// of fixed size, so each GPU that loads this library holds that array until
+// the process exits.
+//
+// Like ctts_op_linear it is asynchronous on the caller's stream: a bounded
+// wait inside the tensor-core kernel that gives up ends the kernel early
+// (no hang) but is not reported through the return code.
 #include <mutex>
 
 #include "api_common.h"
+#include "launch_state.h"
 
 namespace {
 
 // bf16 elements of the static operand: M * K must not exceed this (2 MiB).
 constexpr size_t kNoAllocMaxElems = (size_t)1 << 20;
-constexpr int kMaxDevices = 64;
+using ctts::kMaxDevices;
 
 static __device__ __align__(256) uint16_t g_noalloc_operand[kNoAllocMaxElems];
 
@@ -73,7 +78,6 @@ extern "C" int ctts_op_linear_noalloc(const float* x, int M, int K, const void* 
     e.y_ld = N;
     e.res = res;
     TcScratch none;  // the split-K partials live in the cluster's shared memory
-    none.ncounters = 1 << 30;
     return tc_run(none, xb, M, K, w, N, e, s, nullptr);
   }
   // CUDA-core path: no operand copy, nothing to hold

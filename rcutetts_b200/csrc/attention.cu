@@ -9,6 +9,7 @@
 // attn_prefill: causal attention of T new rows against the cache
 //   (qwen.rs:273-297).
 #include "common.cuh"
+#include "launch_state.h"
 #include "kernels.cuh"
 
 namespace ctts {
@@ -864,13 +865,8 @@ cudaError_t launch_attn_step_t(const AttnArgs& a, cudaStream_t s) {
   const size_t smem = (size_t)2 * a.chunk * HD * (BF ? 2 : 4);
   // opt in whenever the dynamic size grows: the static arrays count against
   // the 48 KB default as well (fp32, head_dim 128: 32 KB + 16.5 KB)
-  static size_t configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_step_kernel<BF, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  static SmemOptIn opt;
+  if (cudaError_t e = opt.ensure((const void*)attn_step_kernel<BF, HD>, smem)) return e;
   CTTS_LK(launch_k(attn_step_kernel<BF, HD>, dim3(a.nsplit, a.nkv, a.batch), dim3(128), smem, s, a));
   return cudaGetLastError();
 }
@@ -878,13 +874,8 @@ cudaError_t launch_attn_step_t(const AttnArgs& a, cudaStream_t s) {
 template <bool BF, int HD, int GM>
 cudaError_t launch_attn_loop_g(const AttnArgs& a, cudaStream_t s) {
   const size_t smem = (size_t)2 * 2 * 128 * HD * (BF ? 2 : 4);
-  static size_t configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_loop_kernel<BF, HD, GM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  static SmemOptIn opt;
+  if (cudaError_t e = opt.ensure((const void*)attn_loop_kernel<BF, HD, GM>, smem)) return e;
   CTTS_LK(launch_k(attn_loop_kernel<BF, HD, GM>, dim3(a.nkv, a.batch), dim3(256), smem, s, a));
   return cudaGetLastError();
 }

@@ -49,6 +49,7 @@
 #include <vector>
 
 #include "dit_cluster.cuh"
+#include "launch_state.h"
 #include "tc_ptx.cuh"
 
 namespace ctts {
@@ -923,19 +924,8 @@ __global__ void gather_rows_kernel(uint16_t* dst, const uint16_t* src, const int
 }
 
 cudaError_t set_attrs(size_t smem) {
-  static std::mutex mu;
-  std::lock_guard<std::mutex> lk(mu);
-  static size_t configured = 0;
-  if (smem <= configured) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(dit_cluster_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(dit_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) {
-    (void)cudaGetLastError();
-    return e;
-  }
-  configured = smem;
-  return cudaSuccess;
+  static SmemOptIn opt;
+  return opt.ensure((const void*)dit_cluster_kernel, smem, /*nonportable_cluster=*/true);
 }
 
 cudaLaunchConfig_t make_cfg(int nclusters, size_t smem, cudaStream_t s, cudaLaunchAttribute* attr, bool pdl) {

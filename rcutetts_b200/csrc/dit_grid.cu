@@ -30,6 +30,7 @@
 #include <cstdio>
 
 #include "common.cuh"
+#include "launch_state.h"
 #include "dit_grid.cuh"
 
 namespace ctts {
@@ -50,6 +51,8 @@ CTTS_DEV float ldcg(const float* p) { return __ldcg(p); }
 
 // ---- flag-tagged exchange words
 using u64 = unsigned long long;
+// Polls of one exchange word before a consumer gives up.
+CTTS_DEV uint32_t spin_limit(const DitGridArgs& a) { return a.spin_limit ? a.spin_limit : kSpinLimit; }
 CTTS_DEV void ll_put(u64* p, float v, uint32_t tag) {
   const u64 w = ((u64)tag << 32) | __float_as_uint(v);
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
@@ -86,7 +89,7 @@ __device__ __noinline__ void ll_poll(const DitGridArgs& a, const u64* const (&p)
                            __uint_as_float((uint32_t)w[i][2]), __uint_as_float((uint32_t)w[i][3]));
         pend &= ~(1u << i);
       }
-    if (pend && (it == kSpinLimit || ((it & 255u) == 255u && a.err && *reinterpret_cast<volatile int*>(a.err)))) {
+    if (pend && (it == spin_limit(a) || ((it & 255u) == 255u && a.err && *reinterpret_cast<volatile int*>(a.err)))) {
       if (a.err) atomicExch(a.err, 4);
       break;
     }
@@ -98,7 +101,7 @@ CTTS_DEV float ll_get1(const DitGridArgs& a, const u64* p, uint32_t tag) {
     u64 w;
     asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
-    if (it == kSpinLimit || ((it & 255u) == 255u && a.err && *reinterpret_cast<volatile int*>(a.err))) {
+    if (it == spin_limit(a) || ((it & 255u) == 255u && a.err && *reinterpret_cast<volatile int*>(a.err))) {
       if (a.err) atomicExch(a.err, 4);
       return 0.0f;
     }
@@ -504,8 +507,9 @@ CTTS_DEV void phase_qkv(const DitGridArgs& a, Stage& st, int l, float* sm) {
   int n0, n1;
   my_cols(qkvw, n0, n1);
   const int lane = threadIdx.x & 31;
+  const bool skip = a.skip_qkv_cta0 && blockIdx.x == 0;  // injected fault (tests only)
   gemv_cols<RW, 1>(st.wbuf, H, n0, n1, sm, [&](int n, const float* acc, const float*) {
-    if (lane == 0)
+    if (lane == 0 && !skip)
 #pragma unroll
       for (int r = 0; r < rows; r++) ll_put(st.ll.qkv + (size_t)r * qkvw + n, acc[r], st.tag);
   });
@@ -826,17 +830,8 @@ size_t grid_smem_bytes(int R, int H, int F, int nq, int nkv, int hd, int L, int 
   return (m.bar_off() + 4) * sizeof(float);
 }
 
-int grid_ctas() {
-  static int n = -1;
-  if (n < 0) {
-    int dev = 0, sms = 0, coop = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
-    n = coop ? sms : 0;
-  }
-  return n;
-}
+// one CTA per SM of the current device (0: no cooperative launch)
+int grid_ctas() { return device_coop() ? device_sms() : 0; }
 
 }  // namespace
 
@@ -862,12 +857,8 @@ namespace {
 
 template <int RW>
 cudaError_t launch_rows(const DitGridArgs& a, size_t smem, cudaStream_t s) {
-  static size_t configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(dit_grid_kernel<RW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  static SmemOptIn opt;
+  if (cudaError_t e = opt.ensure((const void*)dit_grid_kernel<RW>, smem)) return e;
   int per_sm = 0;
   cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dit_grid_kernel<RW>, kThreads, smem);
   if (e != cudaSuccess || per_sm < 1) return e != cudaSuccess ? e : cudaErrorInvalidConfiguration;

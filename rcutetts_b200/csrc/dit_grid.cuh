@@ -35,6 +35,12 @@ struct DitGridArgs {
   unsigned long long* ll = nullptr;
   unsigned* bar = nullptr;        // [0] launch generation, [1] exit count (dit_grid_counters())
   int* err = nullptr;
+  // Error-path testing (ctts_debug_inject_wait_fault): polls of an exchange
+  // word give up after spin_limit tries (0: the default), and with
+  // skip_qkv_cta0 set CTA 0 leaves its QKV outputs unwritten, so the
+  // attention phase waits on words no producer writes.
+  uint32_t spin_limit = 0;
+  int skip_qkv_cta0 = 0;
 };
 
 // Counters the launch needs (zero at allocation).

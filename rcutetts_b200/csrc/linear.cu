@@ -14,6 +14,7 @@
 #include <cstdlib>
 
 #include "common.cuh"
+#include "launch_state.h"
 #include "kernels.cuh"
 
 namespace ctts {
@@ -233,13 +234,8 @@ template <bool BF16, int MT, int RPW, bool SWIGLU>
 cudaError_t launch_t(const LinearArgs& a, cudaStream_t s) {
   auto kern = linear_rows_kernel<BF16, MT, RPW, SWIGLU>;
   size_t smem = (size_t)MT * a.K * sizeof(float);
-  static int configured = 0;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         200 * 1024);
-    if (e != cudaSuccess) return e;
-    configured = 1;
-  }
+  static SmemOptIn opt;
+  if (cudaError_t e = opt.ensure((const void*)kern, 200 * 1024)) return e;
   dim3 grid((a.N + kWarps * RPW - 1) / (kWarps * RPW), (a.M + MT - 1) / MT);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -289,12 +285,11 @@ int linear_grid_ctas(const LinearArgs& a) {
 }
 
 bool pdl_enabled() {
-  static int v = -1;
-  if (v < 0) {
+  static const bool v = [] {
     const char* e = getenv("CTTS_PDL");
-    v = (e && e[0] == '0') ? 0 : 1;
-  }
-  return v == 1;
+    return !(e && e[0] == '0');
+  }();
+  return v;
 }
 
 cudaError_t launch_prep_bf16(const PrepArgs& a, cudaStream_t s) {

@@ -24,6 +24,7 @@
 #include <cstdio>
 
 #include "common.cuh"
+#include "launch_state.h"
 #include "lm_grid.cuh"
 
 namespace ctts {
@@ -601,27 +602,14 @@ __global__ void __launch_bounds__(kThreads, 1) lm_grid_kernel(const LmGridArgs a
   }
 }
 
-int grid_ctas() {
-  static int n = -1;
-  if (n < 0) {
-    int dev = 0, sms = 0, coop = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
-    n = coop ? sms : 0;
-  }
-  return n;
-}
+// one CTA per SM of the current device (0: no cooperative launch)
+int grid_ctas() { return device_coop() ? device_sms() : 0; }
 
 template <int HD, int RW>
 cudaError_t launch_t(const LmGridArgs& a, size_t smem, cudaStream_t s) {
   auto kern = lm_grid_kernel<HD, RW>;
-  static size_t configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  static SmemOptIn opt;
+  if (cudaError_t e = opt.ensure((const void*)kern, smem)) return e;
   int per_sm = 0;
   cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
   if (e != cudaSuccess || per_sm < 1) return e != cudaSuccess ? e : cudaErrorInvalidConfiguration;

@@ -26,6 +26,7 @@
 #include <cstdlib>
 
 #include "common.cuh"
+#include "launch_state.h"
 #include "tc_linear.cuh"
 #include "tc_ptx.cuh"
 
@@ -398,15 +399,16 @@ __global__ void __launch_bounds__(128)
 
 
 EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
+  static const EncodeTiledFn fn = [] {
     cudaDriverEntryPointQueryResult q;
     void* p = nullptr;
     if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
             cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
+      return reinterpret_cast<EncodeTiledFn>(p);
+    (void)cudaGetLastError();
+    return EncodeTiledFn(nullptr);
+  }();
   return fn;
 }
 
@@ -427,14 +429,8 @@ bool make_map(CUtensorMap* m, const void* base, int rows, int cols, int box_rows
 
 
 int tc_num_sms() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
+  const int n = device_sms();
+  return n > 0 ? n : 148;
 }
 
 TcPlan tc_plan(int M, int N, int K, int num_sms, int max_splitk) {
@@ -445,11 +441,10 @@ TcPlan tc_plan(int M, int N, int K, int num_sms, int max_splitk) {
   p.kblocks = K / kBK;
   // the K splits of one tile form a thread-block cluster (<= 8, portable);
   // aim for about one wave of CTAs.  CTTS_TC_MAX_SPLITK caps the split.
-  static int env_cap = -1;
-  if (env_cap < 0) {
+  static const int env_cap = [] {
     const char* e = getenv("CTTS_TC_MAX_SPLITK");
-    env_cap = e ? std::max(1, atoi(e)) : 8;
-  }
+    return e ? std::max(1, atoi(e)) : 8;
+  }();
   max_splitk = std::min(max_splitk, env_cap);
   const int ctas_per_split = p.ntiles * p.mtiles;
   int sk = std::max(1, num_sms / ctas_per_split);
@@ -481,15 +476,8 @@ cudaError_t launch_tc_linear(const TcCall& c, cudaStream_t s) {
   if ((reinterpret_cast<uintptr_t>(c.w) & 15) || (reinterpret_cast<uintptr_t>(c.x) & 15))
     return cudaErrorInvalidValue;
   TcPlan p = tc_plan(c.M, c.N, c.K, tc_num_sms(), c.max_splitk);
-  static size_t configured = 0;  // dynamic smem opt-in so far (static smem is tiny)
-  if (p.smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(tc_linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
-    if (e != cudaSuccess) {
-      (void)cudaGetLastError();
-      return e;
-    }
-    configured = p.smem;
-  }
+  static SmemOptIn opt;  // dynamic smem opt-in per device (static smem is tiny)
+  if (cudaError_t e = opt.ensure((const void*)tc_linear_kernel, p.smem)) return e;
   CUtensorMap tmW, tmX;
   // distinct codes for the tensor-map failures (diagnostics)
   if (!encode_fn()) return cudaErrorNotSupported;

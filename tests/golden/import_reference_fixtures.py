@@ -59,4 +59,7 @@ def main(root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("RCUTETTS_REFERENCE", "")
+    if not root:
+        sys.exit("usage: import_reference_fixtures.py <RCuteTTS checkout> (or set RCUTETTS_REFERENCE)")
+    main(root)

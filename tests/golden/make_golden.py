@@ -312,7 +312,10 @@ def make_vae_dw(root):
 
 if __name__ == "__main__":
     args = [a for a in sys.argv[1:] if a not in ("locenc", "vae_dw", "shipped")]
-    root = args[0] if args else "/root/reference"
+    root = args[0] if args else os.environ.get("RCUTETTS_REFERENCE", "")
+    if not root:
+        sys.exit("usage: make_golden.py <RCuteTTS checkout> [locenc|vae_dw|shipped] "
+                 "(or set RCUTETTS_REFERENCE)")
     if "locenc" in sys.argv[1:]:
         make_locenc(root)  # only the LocEnc fixture
     elif "vae_dw" in sys.argv[1:]:

@@ -1,10 +1,11 @@
 """ctts_op_linear_noalloc: the op-level linear for callers that cannot
-allocate device memory (their device heap is owned by a pool, or they must
-not allocate after set-up, e.g. while capturing a CUDA graph or inside a
-serving loop).  It keeps the bf16 tensor-core operand in a fixed static
-device array instead of a cudaMalloc'd buffer.  Checked through the C ABI
-against ctts_op_linear, on two calls in a row (the array keeps the previous
-call's contents).  This file is collected last on purpose."""
+allocate device memory (their device heap is owned by a pool, or a serving
+loop must not allocate after set-up because cudaMalloc synchronizes the
+device).  It keeps the bf16 tensor-core operand in a fixed static device
+array instead of a cudaMalloc'd buffer.  Checked through the C ABI against
+ctts_op_linear, on two calls in a row (the array keeps the previous call's
+contents), with the device's free memory unchanged across a repeated call.
+This file is collected last on purpose."""
 import ctypes as C
 
 import numpy as np
@@ -49,6 +50,16 @@ def test_noalloc_matches_allocating_linear_twice():
         for _ in range(2):
             got = _run(lib.ctts_op_linear_noalloc, x, wdev, g, res, M, K, N)
             assert rel_err(got, ref) < 1e-4
+        # a repeated call takes no device memory (the output is allocated
+        # beforehand; the driver's free-memory count must not move)
+        y = torch.empty((M, N), device="cuda")
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
+        rc = lib.ctts_op_linear_noalloc(x.data_ptr(), M, K, wdev.data_ptr(), 1, N, g.data_ptr(), C.c_float(1e-6),
+                                        res.data_ptr(), y.data_ptr(), None)
+        torch.cuda.synchronize()
+        assert rc == 0 and torch.cuda.mem_get_info()[0] == free0
+        assert rel_err(y.cpu().numpy(), ref) < 1e-4
 
 
 def test_noalloc_rejects_oversize():
