@@ -123,7 +123,8 @@ extern "C" int ctts_vae_create(const ctts_vae_config* cfg, int device, ctts_vae*
   v->final_alpha = A.alloc<float>(ch);
   v->slots.add("model." + std::to_string(fi) + ".alpha", v->final_alpha, {1, ch, 1}, false);
   conv("model." + std::to_string(fi + 1), &v->final_w, &v->final_b, 1, ch, 7);
-  if (!v->final_b) {
+  v->err = A.alloc<int>(1);
+  if (!v->final_b || !v->err) {
     delete v;
     return set_error(CTTS_ERR_NOMEM, "device allocation failed");
   }
@@ -165,6 +166,7 @@ extern "C" int ctts_vae_set_tensor(ctts_vae* v, const char* name, const void* ho
       int rc = vae_store(v, s, w);
       if (rc) return rc;
       s.set = true;
+      v->tc_dirty = true;
       s.wn_g.clear();
       s.wn_v.clear();
     }
@@ -178,6 +180,7 @@ extern "C" int ctts_vae_set_tensor(ctts_vae* v, const char* name, const void* ho
   int rc = vae_store(v, s, f);
   if (rc) return rc;
   s.set = true;
+  v->tc_dirty = true;
   return CTTS_OK;
 }
 
@@ -224,6 +227,72 @@ int vae_ws_ensure(ctts_vae* v, int B, int T) {
   return CTTS_OK;
 }
 
+}  // namespace
+
+namespace ctts {
+
+int cout_pad128(int c) { return (c + 127) / 128 * 128; }
+
+// Rebuilds the tensor-core copies of the bf16 dense conv weights after an
+// upload (synchronous; outside any stream capture).
+int vae_tc_prepare(ctts_vae* v) {
+  if (!v->bf16 || !v->tc_dirty) return CTTS_OK;
+  CTTS_CK(cudaDeviceSynchronize());
+  v->tc_arena.~DevArena();
+  new (&v->tc_arena) DevArena();
+  auto make = [&](const void* w, int nphase, int cout, int cin, int k, void** out) -> int {
+    *out = nullptr;
+    ConvArgs probe;
+    probe.w_bf16 = 1; probe.w_tc = w; probe.cout_pad = cout_pad128(cout); probe.Cin = cin; probe.Cout = cout;
+    probe.k = k; probe.dil = 1;
+    if (!conv_tc_supported(probe)) return CTTS_OK;  // stays on the CUDA-core kernel
+    uint16_t* d = v->tc_arena.alloc<uint16_t>((size_t)nphase * k * cin * cout_pad128(cout));
+    if (!d) return set_error(CTTS_ERR_NOMEM, "VAE tensor-core weights");
+    CTTS_CK(repack_conv_tc(d, static_cast<const uint16_t*>(w), nphase, cout, cin, k, cout_pad128(cout), nullptr));
+    *out = d;
+    return CTTS_OK;
+  };
+  const ctts_vae_config& c = v->cfg;
+  int rc = CTTS_OK;
+  if (c.depthwise) {
+    rc = make(v->front_pw_w, 1, c.channels, c.latent, 1, &v->front_pw_tc);
+  } else {
+    rc = make(v->front_w, 1, c.channels, c.latent, 7, &v->front_tc);
+  }
+  for (auto& st : v->stages) {
+    if (!rc) rc = make(st.tw, st.stride, st.cout, st.cin, 2, &st.tw_tc);
+    for (auto& R : st.res) {
+      if (!rc && !c.depthwise) rc = make(R.w0, 1, st.cout, st.cout, 7, &R.w0_tc);
+      if (!rc) rc = make(R.w1, 1, st.cout, st.cout, 1, &R.w1_tc);
+    }
+  }
+  if (rc) return rc;
+  CTTS_CK(cudaDeviceSynchronize());
+  v->tc_dirty = false;
+  return CTTS_OK;
+}
+
+// Points a conv at its tensor-core weights (null: CUDA-core kernel).
+void use_tc(const ctts_vae* v, ConvArgs& a, const void* w_tc) {
+  a.w_tc = w_tc;
+  a.cout_pad = cout_pad128(a.Cout);
+  a.err = v->err;
+}
+
+// Reads back (and clears) the tensor-core convs' error word after a
+// synchronized decode.
+int vae_read_err(ctts_vae* v) {
+  int err = 0;
+  CTTS_CK(cudaMemcpy(&err, v->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err != 0) CTTS_CK(cudaMemset(v->err, 0, sizeof(int)));
+  CTTS_REQ(err == 0, CTTS_ERR_TIMEOUT, "a VAE tensor-core conv gave up waiting on its pipeline");
+  return CTTS_OK;
+}
+
+}  // namespace ctts
+
+namespace {
+
 int vae_enqueue(ctts_vae* v, int B, const float* lat, int T, float* wav, cudaStream_t s) {
   const int bf = v->bf16;
   float* h = v->buf[0];
@@ -234,11 +303,13 @@ int vae_enqueue(ctts_vae* v, int B, const float* lat, int T, float* wav, cudaStr
   a.x = lat; a.w = v->front_w; a.w_bf16 = bf; a.bias = v->front_b; a.y = dw ? r : h;
   a.B = B; a.Cin = v->cfg.latent; a.Cout = dw ? v->cfg.latent : v->cfg.channels; a.Tin = T; a.Tout = T; a.k = 7;
   a.dil = 1; a.left = 6; a.groups = dw ? v->cfg.latent : 1;
+  if (!dw) use_tc(v, a, v->front_tc);
   CTTS_CK(launch_conv1d(a, s));
   if (dw) {  // pointwise latent -> channels
     ConvArgs p;
     p.x = r; p.w = v->front_pw_w; p.w_bf16 = bf; p.bias = v->front_pw_b; p.y = h;
     p.B = B; p.Cin = v->cfg.latent; p.Cout = v->cfg.channels; p.Tin = T; p.Tout = T; p.k = 1; p.dil = 1; p.left = 0;
+    use_tc(v, p, v->front_pw_tc);
     CTTS_CK(launch_conv1d(p, s));
   }
   int t = T;
@@ -248,6 +319,7 @@ int vae_enqueue(ctts_vae* v, int B, const float* lat, int T, float* wav, cudaStr
     tr.x = h; tr.w = st.tw; tr.w_bf16 = bf; tr.bias = st.tb; tr.y = h2; tr.snake_alpha = st.alpha;
     tr.B = B; tr.Cin = st.cin; tr.Cout = st.cout; tr.Tin = t; tr.Tout = t * st.stride; tr.k = 2;
     tr.dil = 1; tr.left = 1; tr.stride = st.stride;
+    use_tc(v, tr, st.tw_tc);
     CTTS_CK(launch_conv_transpose(tr, s));
     t *= st.stride;
     std::swap(h, h2);
@@ -257,11 +329,13 @@ int vae_enqueue(ctts_vae* v, int B, const float* lat, int T, float* wav, cudaStr
       c7.x = h; c7.w = R.w0; c7.w_bf16 = bf; c7.bias = R.b0; c7.y = r; c7.snake_alpha = R.a0;
       c7.B = B; c7.Cin = st.cout; c7.Cout = st.cout; c7.Tin = t; c7.Tout = t; c7.k = 7;
       c7.dil = dils[ri]; c7.left = 6 * dils[ri]; c7.groups = dw ? st.cout : 1;
+      use_tc(v, c7, R.w0_tc);
       CTTS_CK(launch_conv1d(c7, s));
       ConvArgs c1;
       c1.x = r; c1.w = R.w1; c1.w_bf16 = bf; c1.bias = R.b1; c1.y = h; c1.res = h; c1.snake_alpha = R.a1;
       c1.B = B; c1.Cin = st.cout; c1.Cout = st.cout; c1.Tin = t; c1.Tout = t; c1.k = 1; c1.dil = 1;
       c1.left = 0;
+      use_tc(v, c1, R.w1_tc);
       CTTS_CK(launch_conv1d(c1, s));
     }
   }
@@ -282,6 +356,7 @@ extern "C" int ctts_vae_decode_batch_dev(ctts_vae* v, int batch, const float* la
   CTTS_CK(cudaSetDevice(v->device));
   int rc = vae_ws_ensure(v, batch, T);
   if (rc) return rc;
+  if ((rc = vae_tc_prepare(v))) return rc;
   return vae_enqueue(v, batch, latent_dev, T, wav_dev, as_stream(stream, v->stream));
 }
 
@@ -303,6 +378,7 @@ extern "C" int ctts_vae_decode_batch(ctts_vae* v, int batch, const float* latent
   int rc = ctts_vae_decode_batch_dev(v, batch, v->lat_dev, T, v->wav_dev, v->stream);
   if (rc) return rc;
   CTTS_CK(cudaStreamSynchronize(v->stream));
+  if ((rc = vae_read_err(v))) return rc;
   CTTS_CK(cudaMemcpy(wav, v->wav_dev, nw * 4, cudaMemcpyDeviceToHost));
   return CTTS_OK;
 }

@@ -100,12 +100,14 @@ int stream_enqueue(ctts_vae_stream* st, const float* lat, int T, float* wav, cud
     a.w = v->front_w; a.w_bf16 = bf; a.bias = v->front_b; a.y = dw ? r : h;
     a.B = B; a.Cin = v->cfg.latent; a.Cout = dw ? v->cfg.latent : v->cfg.channels; a.k = 7; a.dil = 1; a.left = 6;
     a.groups = dw ? v->cfg.latent : 1;
+    if (!dw) use_tc(v, a, v->front_tc);
     if ((rc = conv_streamed(st, hi++, a, lat, T, s, false))) return rc;
   }
   if (dw) {  // pointwise latent -> channels: no context
     ConvArgs p;
     p.x = r; p.w = v->front_pw_w; p.w_bf16 = bf; p.bias = v->front_pw_b; p.y = h;
     p.B = B; p.Cin = v->cfg.latent; p.Cout = v->cfg.channels; p.Tin = T; p.Tout = T; p.k = 1; p.dil = 1; p.left = 0;
+    use_tc(v, p, v->front_pw_tc);
     CTTS_CK(launch_conv1d(p, s));
   }
   int t = T;
@@ -114,6 +116,7 @@ int stream_enqueue(ctts_vae_stream* st, const float* lat, int T, float* wav, cud
     ConvArgs tr;
     tr.w = sg.tw; tr.w_bf16 = bf; tr.bias = sg.tb; tr.y = h2; tr.snake_alpha = sg.alpha;
     tr.B = B; tr.Cin = sg.cin; tr.Cout = sg.cout; tr.k = 2; tr.dil = 1; tr.left = 1; tr.stride = sg.stride;
+    use_tc(v, tr, sg.tw_tc);
     if ((rc = conv_streamed(st, hi++, tr, h, t, s, true))) return rc;
     t *= sg.stride;
     std::swap(h, h2);
@@ -123,10 +126,12 @@ int stream_enqueue(ctts_vae_stream* st, const float* lat, int T, float* wav, cud
       c7.w = R.w0; c7.w_bf16 = bf; c7.bias = R.b0; c7.y = r; c7.snake_alpha = R.a0;
       c7.B = B; c7.Cin = sg.cout; c7.Cout = sg.cout; c7.k = 7; c7.dil = dils[ri]; c7.left = 6 * dils[ri];
       c7.groups = dw ? sg.cout : 1;
+      use_tc(v, c7, R.w0_tc);
       if ((rc = conv_streamed(st, hi++, c7, h, t, s, false))) return rc;
       ConvArgs c1;  // pointwise: no context
       c1.x = r; c1.w = R.w1; c1.w_bf16 = bf; c1.bias = R.b1; c1.y = h; c1.res = h; c1.snake_alpha = R.a1;
       c1.B = B; c1.Cin = sg.cout; c1.Cout = sg.cout; c1.Tin = t; c1.Tout = t; c1.k = 1; c1.dil = 1; c1.left = 0;
+      use_tc(v, c1, R.w1_tc);
       CTTS_CK(launch_conv1d(c1, s));
     }
   }
@@ -187,6 +192,7 @@ extern "C" int ctts_vae_stream_decode_chunk_dev(ctts_vae_stream* st, const float
   CTTS_CK(cudaSetDevice(st->v->device));
   int rc = stream_ws_ensure(st, frames);
   if (rc) return rc;
+  if ((rc = vae_tc_prepare(st->v))) return rc;
   return stream_enqueue(st, latent_dev, frames, wav_dev, as_stream(stream, st->v->stream));
 }
 
@@ -197,11 +203,13 @@ extern "C" int ctts_vae_stream_decode_chunk(ctts_vae_stream* st, const float* la
   int rc = stream_ws_ensure(st, frames);
   if (rc) return rc;
   const size_t nl = (size_t)st->batch * v->cfg.latent * frames, nw = (size_t)st->batch * frames * v->hop;
+  if ((rc = vae_tc_prepare(v))) return rc;
   CTTS_CK(cudaMemcpyAsync(st->lat_dev, latent, nl * 4, cudaMemcpyHostToDevice, v->stream));
   rc = stream_enqueue(st, st->lat_dev, frames, st->wav_dev, v->stream);
   if (rc) return rc;
   CTTS_CK(cudaMemcpyAsync(wav, st->wav_dev, nw * 4, cudaMemcpyDeviceToHost, v->stream));
   CTTS_CK(cudaStreamSynchronize(v->stream));
+  if ((rc = vae_read_err(v))) return rc;
   return CTTS_OK;
 }
 

@@ -168,9 +168,34 @@ struct ConvArgs {
   int tanh_out = 0;
   int xoff = 0;     // output position t reads input position t + xoff + j*dil - left
                     // (streaming: the input carries xoff history columns)
+  // bf16 tensor-core path (vae_tc.cu): the weights repacked by repack_conv_tc
+  // ([phase][tap][Cin/8][cout_pad][8]); null keeps the CUDA-core kernel
+  const void* w_tc = nullptr;
+  int cout_pad = 0;
+  int* err = nullptr;  // bounded-wait timeouts of the tensor-core path (error 5)
 };
 cudaError_t launch_conv1d(const ConvArgs& a, cudaStream_t s);
 cudaError_t launch_conv_transpose(const ConvArgs& a, cudaStream_t s);
+
+// Arguments of the tensor-core conv kernel (vae_tc.cu).
+struct VaeTcArgs {
+  const float* x = nullptr;
+  const uint16_t* w = nullptr;  // [nphase][k][Cin/8][Cout_pad][8] bf16
+  const float *bias = nullptr, *res = nullptr, *alpha = nullptr;
+  float* y = nullptr;
+  int* err = nullptr;
+  int B = 0, Cin = 0, Cout = 0, Cout_pad = 0, Tin = 0, Tout = 0, Tc = 0;
+  int k = 1, dil = 1, left = 0, xoff = 0, ostride = 1, nphase = 1, tanh_out = 0;
+};
+// True when the dense conv `a` can run on the tensor cores (bf16, repacked
+// weights set, Cin a multiple of 16, Cout >= 64, (k-1)*dil <= 56, k <= 8).
+bool conv_tc_supported(const ConvArgs& a);
+// Tc computed positions, output index t*ostride + phase (blockIdx.z = b*nphase + phase).
+cudaError_t launch_conv_tc(const ConvArgs& a, int Tc, int ostride, int nphase, cudaStream_t s);
+// Repack [nphase][Cout][Cin][k] bf16 conv weights into the tensor-core layout
+// [nphase][k][Cin/8][cout_pad][8] (dst zeroed beforehand: rows >= Cout stay 0).
+cudaError_t repack_conv_tc(uint16_t* dst, const uint16_t* src, int nphase, int Cout, int Cin, int k, int cout_pad,
+                           cudaStream_t s);
 cudaError_t launch_snake(const float* x, int B, int C, int T, const float* alpha, float* y,
                          cudaStream_t s);
 // Streaming history: ext[b, c, :] = hist_in[b, c, 0:H] ++ x[b, c, 0:T] and

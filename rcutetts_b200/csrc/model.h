@@ -140,11 +140,13 @@ struct ctts_engine {
 struct VaeRes {
   float *a0 = nullptr, *b0 = nullptr, *a1 = nullptr, *b1 = nullptr;
   void *w0 = nullptr, *w1 = nullptr;
+  void *w0_tc = nullptr, *w1_tc = nullptr;  // bf16 tensor-core layout (repack_conv_tc) or null
 };
 struct VaeStage {
   int cin = 0, cout = 0, stride = 0;
   float *alpha = nullptr, *tb = nullptr;
   void* tw = nullptr;  // repacked [stride][cout][cin*2]
+  void* tw_tc = nullptr;
   VaeRes res[3];
 };
 struct ctts_vae {
@@ -160,6 +162,12 @@ struct ctts_vae {
   float *final_alpha = nullptr, *final_b = nullptr;
   void* final_w = nullptr;
   int hop = 1;
+  // bf16 weights of the dense convs in the tensor-core layout, rebuilt from
+  // the uploaded weights before the first decode after any upload
+  void *front_tc = nullptr, *front_pw_tc = nullptr;
+  bool tc_dirty = true;
+  ctts::DevArena tc_arena;
+  int* err = nullptr;  // device error word of the tensor-core convs
   // workspace
   size_t ws_elems = 0;
   float *buf[3] = {nullptr, nullptr, nullptr};
@@ -174,4 +182,10 @@ int lm_forward_rows(ctts_lm* lm, ctts_kv* kv, int rows, int prefill_b, int pos0,
 int lm_check_ready(const ctts_lm* lm);
 int lm_decode_dev(ctts_lm* lm, ctts_kv* kv, const float* x_dev, float* out_dev, cudaStream_t s,
                   int* launches);
+// VAE tensor-core convs (api_vae.cu): rebuild the repacked bf16 weights
+// after an upload, point a conv at them, read back the error word.
+struct ConvArgs;
+int vae_tc_prepare(ctts_vae* v);
+void use_tc(const ctts_vae* v, ConvArgs& a, const void* w_tc);
+int vae_read_err(ctts_vae* v);
 }  // namespace ctts

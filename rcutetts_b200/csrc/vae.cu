@@ -178,6 +178,7 @@ cudaError_t launch_conv1d(const ConvArgs& a, cudaStream_t s) {
       CTTS_LK(launch_k(dw_conv_kernel<false>, grid, dim3(256), smem, s, a));
     return cudaGetLastError();
   }
+  if (conv_tc_supported(a)) return launch_conv_tc(a, a.Tout, 1, 1, s);
   dim3 grid((a.Tout + TT - 1) / TT, (a.Cout + TO - 1) / TO, a.B);
   if (a.w_bf16)
     CTTS_LK(launch_k(conv_kernel<true>, dim3(grid), dim3(256), 0, s, a, a.Tout, 1, 1, 0));
@@ -191,6 +192,7 @@ cudaError_t launch_conv1d(const ConvArgs& a, cudaStream_t s) {
 cudaError_t launch_conv_transpose(const ConvArgs& a, cudaStream_t s) {
   const int Tc = a.Tin - a.xoff;  // input positions that produce output
   if (a.k != 2 || a.xoff < 0 || a.Tout != Tc * a.stride) return cudaErrorInvalidValue;
+  if (conv_tc_supported(a)) return launch_conv_tc(a, Tc, a.stride, a.stride, s);
   dim3 grid((Tc + TT - 1) / TT, (a.Cout + TO - 1) / TO, a.B * a.stride);
   long wphase = (long)a.Cout * a.Cin * 2;
   if (a.w_bf16)
