@@ -41,7 +41,13 @@ FRAME_HZ = 75.0  # 24 kHz / hop 320 (config[4] decoder topology)
 B_PER_GPU = 64
 GEN_FRAMES = 500
 PROMPT_FRAMES = 150
-L2_BYTES = 126 * 1024 * 1024
+L2_BYTES = 126 * 1024 * 1024  # fallback when the device does not report its L2 size
+# DRAM bytes (read + write) of one DiT Euler-loop launch at the benchmark
+# shape, from the ncu capture summarised in the file named below (ncu cannot
+# run inside the timed bench; the figure is profile-derived, not measured live)
+DIT_TRAFFIC_BYTES = 31.0e6
+DIT_TRAFFIC_SOURCE = ("profile-derived: profiles/dit_cluster_kernel_b64.md, ncu dram__bytes_read.sum + "
+                      "dram__bytes_write.sum of one launch (weights L2-resident)")
 
 
 def peaks():
@@ -333,12 +339,11 @@ def dit_kernel_roofline(dit, dcfg, lcfg, dev, tc_probe=None):
     flops = 2 * 3 * B * layer_params * steps + 2 * B * (L * 6 * Hd * dcfg.spk_dim + Hd * dcfg.cond_dim)
     tf = flops / t / 1e12
     res = {"bound": "tensor", "achieved": round(tf, 2), "peak": bf16_tf, "unit": "TFLOP/s",
-           "frac": round(tf / bf16_tf, 4), "traffic": 31.0e6, "of": kind,
+           "frac": round(tf / bf16_tf, 4), "traffic": DIT_TRAFFIC_BYTES, "of": kind,
            "kernel": "dit_cluster_kernel (tcgen05, 16-CTA clusters) + DiT prologue via ctts_dit_euler_sample_dev, "
                      "64 utterances x 10 Euler steps",
            "flops_per_launch": flops, "us_per_launch": round(t * 1e6, 2),
-           "traffic_note": "ncu dram__bytes_read+write of one dit_cluster_kernel launch in the bench frame "
-                           "(weights L2-resident; 1.94 GB of L2->SMEM TMA traffic per launch)"}
+           "traffic_source": DIT_TRAFFIC_SOURCE}
     if tc_probe is not None:
         res["others"] = tc_probe
     return res
@@ -367,7 +372,7 @@ def dominant_kernel_roofline(lm, dit, lcfg, dcfg, dev):
         x = torch.randn(M, K, device="cuda")
         g = torch.ones(K, device="cuda")
         y = torch.empty(M, N, device="cuda")
-        flush = torch.empty(2 * L2_BYTES // 4, device="cuda")
+        flush = torch.empty(2 * l2_bytes() // 4, device="cuda")
         st = torch.cuda.current_stream()
         times = []
         torch.cuda.profiler.start()
@@ -394,14 +399,234 @@ def dominant_kernel_roofline(lm, dit, lcfg, dcfg, dev):
             "others": {k: {"us": v["us"], "gbs": round(v["gbs"], 1)} for k, v in out.items()}}
 
 
+# ------------------------------------------- config[0], config[1], config[4]
+def dev_time(fn, n, stream, flush=None):
+    """Mean device time in seconds of fn() over n calls, each bracketed by
+    CUDA events on `stream` (the stream fn launches on); with `flush`, a
+    buffer larger than L2 is rewritten before every call."""
+    import torch
+
+    ts = []
+    for _ in range(n):
+        if flush is not None:
+            flush.add_(1.0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e-3)
+    return statistics.mean(ts)
+
+
+def l2_bytes():
+    import torch
+
+    return int(getattr(torch.cuda.get_device_properties(torch.cuda.current_device()), "L2_cache_size", L2_BYTES))
+
+
+def bench_c0(dev):
+    """config[0]: one fp32 decoder layer at batch 1 -- a 64-row prefill, then
+    32 single-token decode steps against the growing cache, each timed on the
+    device (us per layer step; weights 25.2 MB fp32 streamed per step).  The
+    CPU restatement times the same decode steps beside it."""
+    import torch
+
+    from oracle import oracle as orc
+    from rcutetts_b200 import synth
+    from rcutetts_b200.config import LMConfig
+    from rcutetts_b200.model import QwenCache, QwenW, decode_step_dev, prefill
+
+    cfg = LMConfig(n_layers=1)
+    w = synth.lm_weights(cfg, seed=0)
+    m = QwenW(cfg, "f32", dev).set_weights(w)
+    rng = np.random.default_rng(0)
+    xp = rng.standard_normal((64, cfg.hidden), dtype=np.float32)
+    xd = rng.standard_normal((32, cfg.hidden), dtype=np.float32)
+    cache = QwenCache(m, batch=1, capacity=128)
+    prefill(m, xp, cache)
+    xdd = torch.from_numpy(xd).cuda()
+    out = torch.empty_like(xdd)
+    st = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    flush = torch.empty(2 * l2_bytes() // 4, device="cuda")
+    ts = []
+    for i in range(32):
+        ts.append(dev_time(lambda: decode_step_dev(m, xdd[i:i + 1], cache, out[i:i + 1], st), 1, st, flush))
+    us = statistics.median(ts) * 1e6
+    wbytes = 4 * (cfg.hidden * (cfg.q_dim + 2 * cfg.kv_dim) + cfg.hidden * cfg.q_dim + 3 * cfg.hidden * cfg.ffn)
+    kv = 2 * cfg.kv_dim * 4 * (64 + 16)
+    hbm, _, kind = peaks()
+    lm_o = orc.LM(cfg, w)
+    oc = lm_o.new_cache(128)
+    lm_o.forward(xp, oc)
+    cts = []
+    for i in range(32):
+        t0 = time.perf_counter()
+        lm_o.forward(xd[i:i + 1], oc)
+        cts.append(time.perf_counter() - t0)
+    gbs = (wbytes + kv) / (us * 1e-6) / 1e9
+    return {"workload": "config[0]: one fp32 Qwen3 layer (768, 12/4 heads, FFN 2048), batch 1, 64-row prefill + "
+                        "32 decode steps, L2 flushed before each step",
+            "us_per_layer_step": round(us, 2), "gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4), "of": kind,
+            "bytes_per_step": wbytes + kv,
+            "cpu_us_per_layer_step": round(statistics.median(cts) * 1e6, 1), "cpu_cores": orc.get_threads()}
+
+
+def bench_c1(dev):
+    """config[1]: y = RMSNorm(x) W^T + residual through ctts_op_linear at
+    every (M, K, N, dtype) point, L2 flushed before every launch (device
+    time, CUDA events on the launching stream), the CPU restatement beside
+    each point; plus RoPE on [256, 12, 64] at positions 0..255 + the 4096
+    sweep, SwiGLU on [256, 2x2048] and the 32000x768 embedding gather."""
+    import ctypes as C
+
+    import torch
+
+    from oracle import oracle as orc
+    from rcutetts_b200 import _lib, synth
+
+    lib = _lib.load()
+    hbm, _, kind = peaks()
+    st = torch.cuda.current_stream()
+    flush = torch.empty(2 * l2_bytes() // 4, device="cuda")
+    rows = []
+    rng = np.random.default_rng(1)
+    for dtype in ("f32", "bf16"):
+        for K, N in ((768, 768), (768, 2048), (2048, 768), (768, 2304)):
+            W = rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)
+            if dtype == "bf16":
+                W = synth.bf16_round(W)
+                wd = torch.from_numpy(synth.to_bf16_bits(W).view(np.int16)).cuda()
+            else:
+                wd = torch.from_numpy(W).cuda()
+            g = torch.ones(K, device="cuda")
+            for M in (1, 8, 64, 256):
+                x = rng.standard_normal((M, K), dtype=np.float32)
+                res = rng.standard_normal((M, N), dtype=np.float32)
+                xd, rd = torch.from_numpy(x).cuda(), torch.from_numpy(res).cuda()
+                y = torch.empty((M, N), device="cuda")
+
+                def call():
+                    rc = lib.ctts_op_linear(xd.data_ptr(), M, K, wd.data_ptr(), 1 if dtype == "bf16" else 0, N,
+                                            g.data_ptr(), C.c_float(1e-6), rd.data_ptr(), y.data_ptr(),
+                                            st.cuda_stream)
+                    assert rc == 0, lib.ctts_last_error()
+
+                for _ in range(3):
+                    call()
+                t = dev_time(call, 10, st, flush)
+                algo = N * K * (2 if dtype == "bf16" else 4) + M * K * 4 + 2 * M * N * 4
+                t0 = time.perf_counter()
+                orc.linear(orc.rms_norm(x, np.ones(K, np.float32), 1e-6), W)
+                ct = time.perf_counter() - t0
+                rows.append({"M": M, "K": K, "N": N, "dtype": dtype, "us": round(t * 1e6, 2),
+                             "gbs": round(algo / t / 1e9, 1), "hbm_frac": round(algo / t / 1e9 / hbm, 4),
+                             "cpu_us": round(ct * 1e6, 1)})
+    out = {"workload": "config[1] op sweep: RMSNorm + linear + residual, M x (K,N) x {fp32, bf16 weights}, "
+                       "L2 flushed before every launch", "of": kind, "linear": rows}
+    # RoPE over positions 0..4095, SwiGLU, embedding gather
+    M = 4096
+    xr = torch.randn((M, 12, 64), device="cuda")
+    pos = torch.arange(M, dtype=torch.int32, device="cuda")
+    t = dev_time(lambda: lib.ctts_op_rope(xr.data_ptr(), M, 12, 64, pos.data_ptr(), C.c_float(1e6),
+                                          st.cuda_stream), 10, st, flush)
+    out["rope"] = {"shape": "[4096, 12, 64], positions 0..4095", "us": round(t * 1e6, 2),
+                   "gbs": round(2 * xr.numel() * 4 / t / 1e9, 1)}
+    gu = torch.randn((256, 4096), device="cuda")
+    so = torch.empty((256, 2048), device="cuda")
+    t = dev_time(lambda: lib.ctts_op_swiglu(gu.data_ptr(), 256, 2048, so.data_ptr(), st.cuda_stream), 10, st, flush)
+    out["swiglu"] = {"shape": "[256, 2x2048]", "us": round(t * 1e6, 2),
+                     "gbs": round((gu.numel() + so.numel()) * 4 / t / 1e9, 1)}
+    table = torch.randn((32000, 768), device="cuda")
+    ids = torch.from_numpy(rng.integers(0, 32000, 256)).cuda()
+    eo = torch.empty((256, 768), device="cuda")
+    t = dev_time(lambda: lib.ctts_op_embed_gather(table.data_ptr(), 32000, 768, ids.data_ptr(), 256, eo.data_ptr(),
+                                                  None, st.cuda_stream), 10, st, flush)
+    out["embed_gather"] = {"shape": "32000x768 table, 256 uniform ids", "us": round(t * 1e6, 2),
+                           "gbs": round(2 * eo.numel() * 4 / t / 1e9, 1)}
+    return out
+
+
+def vae_flops(cfg, T):
+    """Dense conv flops of one utterance through the config[4] decoder."""
+    C, L = cfg.channels, cfg.latent
+    f = 2 * C * L * 7 * T
+    t = T
+    for si, s in enumerate(cfg.strides):
+        cin, cout = C >> si, C >> (si + 1)
+        f += 2 * cout * cin * 2 * t * s  # transposed conv: 2 taps per output sample
+        t *= s
+        f += 3 * (2 * cout * cout * 7 * t + 2 * cout * cout * t)
+    f += 2 * (C >> len(cfg.strides)) * 7 * t
+    return f
+
+
+def bench_c4(dev, cpu=True, B=32, T=400, dtypes=("bf16", "f32")):
+    """config[4]: the causal VAE decoder on latents [32, 64, 400] (bf16 on the
+    tensor cores, fp32 on the CUDA cores), ms per batch with CUDA events, RTF
+    against the 170.7 s of audio, TFLOP/s; the CPU restatement decodes one
+    utterance of the batch (extrapolated to 32, stated as such).  Protocol of
+    decode_bench.rs:41-72: warm-up, then repeated timed decodes."""
+    import torch
+
+    from oracle import oracle as orc
+    from rcutetts_b200 import synth
+    from rcutetts_b200.config import VAEConfig
+    from rcutetts_b200.model import DecoderW
+
+    cfg = VAEConfig()
+    w = synth.vae_weights(cfg, seed=4)
+    lat = torch.randn((B, cfg.latent, T), device="cuda", generator=torch.Generator(device="cuda").manual_seed(4))
+    wav = torch.empty((B, T * cfg.hop), device="cuda")
+    audio_s = B * T * cfg.hop / 24000.0
+    flops = vae_flops(cfg, T) * B
+    _, bf16_tf, kind = peaks()
+    out = {"workload": f"config[4]: causal VAE decoder, latents [{B}, 64, {T}] -> {B} x {T * cfg.hop} samples",
+           "flops_per_batch": flops, "audio_s": audio_s}
+    for dtype, n in (("bf16", 5), ("f32", 2)):
+        if dtype not in dtypes:
+            continue
+        m = DecoderW(cfg, dtype, dev).set_weights(w)
+        st = torch.cuda.Stream()
+        m.decode_dev(lat, wav, st)
+        torch.cuda.synchronize()
+        t = dev_time(lambda: m.decode_dev(lat, wav, st), n, st)
+        tf = flops / t / 1e12
+        row = {"ms_per_batch": round(t * 1e3, 2), "rtf": round(t / audio_s, 6), "tflops": round(tf, 1)}
+        if dtype == "bf16":
+            row.update({"tensor_frac": round(tf / bf16_tf, 4), "of": kind,
+                        "kernel": "vae_tc_conv_kernel (tcgen05) for every dense conv; final 64->1 conv on CUDA cores"})
+        else:
+            row["kernel"] = "conv_kernel (CUDA-core FFMA, fp32 weights)"
+        out[dtype] = row
+        del m
+    if cpu:
+        o = orc.VAE(cfg, w)
+        one = lat[0].cpu().numpy()
+        t0 = time.perf_counter()
+        o.decode(one)
+        ct = time.perf_counter() - t0
+        out["cpu"] = {"s_per_utterance": round(ct, 3), "ms_per_batch_extrapolated": round(ct * B * 1e3, 1),
+                      "rtf": round(ct * B / audio_s, 4), "cores": orc.get_threads(),
+                      "sample": f"one utterance of the batch (T={T}, fp32) decoded by the CPU restatement; "
+                                f"batch time extrapolated x{B}"}
+    return out
+
+
 # -------------------------------------------------------------- CPU side
 class CpuRef:
     """The oracle (C restatement of the reference CPU path) on the host
-    cores: one utterance of the config[3] model (bf16-rounded weights widened
-    to fp32, as the reference loads bf16 checkpoints), prefill untimed; run()
-    advances frames for a time budget and returns (frames, seconds)."""
+    cores, on config[3]'s own workload: utterances 0..n-1 of the benchmark
+    batch (bf16-rounded weights widened to fp32, as the reference loads bf16
+    checkpoints), each prefilled untimed with its text + prompt rows and
+    `ctx_frames` feedback rows so the KV context matches the GPU's timed
+    window.  The reference decodes one utterance at a time (decode_step is
+    batch-1, qwen.rs:395-397), so a batch is advanced round-robin, one frame
+    of one utterance per iteration; run() advances frames for a time budget
+    and returns (frames, seconds)."""
 
-    def __init__(self, threads: int | None = None):
+    def __init__(self, threads: int | None = None, n_utts: int = 4, ctx_frames: int | None = None):
         from oracle import oracle as orc
         from rcutetts_b200 import synth
         from rcutetts_b200.config import DiTConfig, LMConfig
@@ -414,39 +639,55 @@ class CpuRef:
         dw = {k: synth.bf16_round(v) if v.ndim > 1 else v for k, v in synth.dit_weights(dcfg, 13).items()}
         self.hw = synth.frame_weights(lcfg.hidden, dcfg.latent, 23)
         self.lm, self.dit = orc.LM(lcfg, lw), orc.DiT(dcfg, dw)
-        ids, prompt = utterances(1, 3, lcfg.vocab)[0]
-        pre = np.concatenate([orc.embed_lookup(lw["embed_tokens.weight"], ids),
-                              orc.linear(prompt, self.hw["latent_proj.weight"], self.hw["latent_proj.bias"])], 0)
-        self.cache = self.lm.new_cache(pre.shape[0] + GEN_FRAMES + 8)
-        self.z = self.lm.forward(pre, self.cache)[-1].copy()
-        self.cond = prompt[-1].copy()
-        self.rng = np.random.default_rng(5)
-        self.frames = 0
+        self.ctx_frames = GEN_FRAMES // 2 - 10 if ctx_frames is None else ctx_frames
+        rng = np.random.default_rng(5)
+        self.rng = rng
+        self.utts = []
+        for ids, prompt in utterances(B_PER_GPU, 3, lcfg.vocab)[:n_utts]:
+            fb = orc.linear(rng.standard_normal((self.ctx_frames, 64), dtype=np.float32),
+                            self.hw["latent_proj.weight"], self.hw["latent_proj.bias"])
+            pre = np.concatenate([orc.embed_lookup(lw["embed_tokens.weight"], ids),
+                                  orc.linear(prompt, self.hw["latent_proj.weight"], self.hw["latent_proj.bias"]),
+                                  fb], 0)
+            cache = self.lm.new_cache(pre.shape[0] + GEN_FRAMES + 8)
+            z = self.lm.forward(pre, cache)[-1].copy()
+            self.utts.append({"cache": cache, "z": z, "cond": prompt[-1].copy(), "frames": 0})
+        self.ctx_mean = float(np.mean([u["cache"]["len"] for u in self.utts]))
+        self.next = 0
 
     def run(self, seconds: float):
         orc, hw = self.orc, self.hw
         n = 0
         t0 = time.perf_counter()
-        while self.frames < GEN_FRAMES:
-            orc.stop_logits(hw["stop_predictor.weight"], hw["stop_predictor.bias"], self.z)
-            x = self.dit.euler_sample(self.rng.standard_normal(64, dtype=np.float32), self.z, self.cond,
-                                      self.z, 10)
-            self.cond = x
+        while True:
+            u = self.utts[self.next % len(self.utts)]
+            self.next += 1
+            if u["frames"] >= GEN_FRAMES // 2:
+                break
+            orc.stop_logits(hw["stop_predictor.weight"], hw["stop_predictor.bias"], u["z"])
+            x = self.dit.euler_sample(self.rng.standard_normal(64, dtype=np.float32), u["z"], u["cond"], u["z"], 10)
+            u["cond"] = x
             fb = orc.linear(x[None], hw["latent_proj.weight"], hw["latent_proj.bias"])
-            self.z = self.lm.forward(fb, self.cache)[0].copy()
+            u["z"] = self.lm.forward(fb, u["cache"])[0].copy()
+            u["frames"] += 1
             n += 1
-            self.frames += 1
             if time.perf_counter() - t0 >= seconds:
                 break
         return n, time.perf_counter() - t0
+
+    def describe(self, frames: int, seconds: float) -> str:
+        return (f"{frames} frames in {seconds:.1f}s: config[3] utterances 0..{len(self.utts) - 1} of the batch "
+                f"advanced round-robin (the reference is batch-1), KV context ~{self.ctx_mean:.0f} like the GPU's "
+                "timed window, untimed prefill; CPU restatement on all host threads (Rust crate unbuildable "
+                "here: no cargo)")
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
     K, W = args.steps, args.warmup
-    # each step: a bounded sample of the workload (about 1 s of frames of one
-    # utterance) on every host core
+    # each step: a bounded sample of the workload (about 1 s of frames of the
+    # round-robin batch sample) on every host core
     budget = float(os.environ.get("CTTS_REF_STEP_S", "1.0"))
     ref = CpuRef()
     frames, secs = 0, 0.0
@@ -459,11 +700,12 @@ def run_reference(args, rank, world):
             "steps": K, "warmup": W, "ms_per_step": round(1e3 / fps, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16-rounded weights)",
             "data": "synthetic (seeded N(0,1) inputs, N(0,0.02) random-init weights)",
-            "config": {"workload": "config[3] model, one utterance, CPU restatement of the reference path",
+            "config": {"workload": "config[3]: batched AR decode, config[2] model, 64 utterances/GPU, "
+                                   "text U[20,120] + 150 prompt frames, 500 frames each",
+                       "utterances_sampled": len(ref.utts), "kv_ctx_mean": round(ref.ctx_mean, 1),
                        "parallelism": "host threads"},
             "cpu_baseline": {"value": round(fps, 3), "unit": UNIT, "cores": ref.threads, "kind": "port",
-                             "sample": f"{frames} frames of one utterance over {K} steps of ~{budget:.0f}s "
-                                       "after an untimed prefill (Rust crate unbuildable here: no cargo)"},
+                             "sample": ref.describe(frames, secs) + f"; {K} steps of ~{budget:.0f}s"},
             "e2e": {"value": round(fps, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -477,9 +719,15 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-b1", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--only", default="", choices=["", "c2", "probe"],
-                    help="c2: only the batch-1 fp32 config[2] measurement; probe: only the roofline probe")
+    ap.add_argument("--only", default="", choices=["", "c2", "probe", "c0", "c1", "c4"],
+                    help="c2: only the batch-1 fp32 config[2] measurement; probe: only the roofline probe; "
+                         "c0 / c1 / c4: only that configuration's measurement")
     ap.add_argument("--b1-frames", type=int, default=197, help="timed frames of the batch-1 run (<= 197)")
+    ap.add_argument("--c4-batch", type=int, default=32, help="config[4] batch (profiling: smaller)")
+    ap.add_argument("--c4-frames", type=int, default=400, help="config[4] latent frames (profiling: fewer)")
+    ap.add_argument("--c4-dtypes", default="bf16,f32", help="config[4] weight dtypes to time")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the config[0] / config[1] / config[4] measurements")
     ap.add_argument("--groups", type=int, default=1,
                     help="sub-batches of the 64 utterances run as parallel branches of the frame graph")
     ap.add_argument("--start-frame", type=int, default=-1,
@@ -497,6 +745,15 @@ def main():
     if args.only == "probe":
         torch.cuda.set_device(local)
         print(json.dumps({"roofline": dominant_kernel_roofline(None, None, None, None, local)}), flush=True)
+        return
+    if args.only in ("c0", "c1", "c4"):
+        torch.cuda.set_device(local)
+        if args.only == "c4":
+            res = bench_c4(local, cpu=not args.no_cpu, B=args.c4_batch, T=args.c4_frames,
+                           dtypes=tuple(args.c4_dtypes.split(",")))
+        else:
+            res = {"c0": bench_c0, "c1": bench_c1}[args.only](local)
+        print(json.dumps({args.only: res}), flush=True)
         return
     if args.only == "c2":
         torch.cuda.set_device(local)
@@ -529,7 +786,7 @@ def main():
                    "sub_batch_groups": args.groups,
                    "timed_frames": f"{res['start'] + W}..{res['start'] + W + K - 1} of 500",
                    "kv_ctx_mean": round(res["ctx_mean"], 1), "parallelism": f"utterance-sharded x{world}",
-                   "l2": "per-step working set (weights+KV) > 126 MB L2; no flush"},
+                   "l2": f"per-step working set (weights+KV) > {l2_bytes() >> 20} MB L2; no flush"},
         "rtf": round((res["ms"] / K * 1e-3) * FRAME_HZ, 4),
         "us_per_step": round(res["ms"] / K * 1e3, 2),
         "step_roofline": {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": hbm, "unit": "GB/s",
@@ -551,13 +808,17 @@ def main():
             out["roofline"] = {"error": repr(ex)}
         if not args.no_b1:
             out["b1"] = run_b1(args, local)
+        if not args.no_configs:
+            for name, fn in (("c0", bench_c0), ("c1", bench_c1), ("c4", bench_c4)):
+                try:
+                    out[name] = fn(local)
+                except Exception as ex:  # report, do not hide
+                    out[name] = {"error": repr(ex)}
         if not args.no_cpu:
             ref = CpuRef()
             n, el = ref.run(15.0)
             out["cpu_baseline"] = {"value": round(n / el, 3), "unit": UNIT, "cores": ref.threads,
-                                   "kind": "port",
-                                   "sample": f"{n} frames of one config[3]-model utterance in {el:.1f}s "
-                                             "after an untimed prefill (CPU restatement, all host threads)"}
+                                   "kind": "port", "sample": ref.describe(n, el)}
     if rank == 0:
         print(json.dumps(out), flush=True)
     if world > 1:
