@@ -154,6 +154,45 @@ __global__ void __launch_bounds__(256) dw_conv_kernel(const ConvArgs a) {
   }
 }
 
+// Dense causal conv with ONE output channel (the decoder's last conv,
+// audio_vae.py:282-292: Snake -> Conv(64 -> 1, k7) -> tanh).  A CTA stages
+// the Snake-applied input window of every input channel for kOutT outputs
+// in shared memory, then each thread sums its output over channels and taps
+// in the (channel, tap) order of conv_kernel (bias, residual, tanh after).
+constexpr int kOutT = 128;
+
+template <bool BF>
+__global__ void __launch_bounds__(kOutT) conv_out1_kernel(const ConvArgs a) {
+  extern __shared__ float win[];  // [Cin][kOutT + span]
+  grid_dep_enter();
+  const int b = blockIdx.y, t0 = blockIdx.x * kOutT;
+  const int k = a.k, dil = a.dil, span = (k - 1) * dil, W = kOutT + span;
+  const float* xb = a.x + (size_t)b * a.Cin * a.Tin;
+  for (int i = threadIdx.x; i < a.Cin * W; i += blockDim.x) {
+    const int c = i / W, r = i - c * W;
+    const int src = t0 + r + a.xoff - a.left;
+    float v = 0.0f;
+    if (src >= 0 && src < a.Tin) {
+      v = xb[(size_t)c * a.Tin + src];
+      if (a.snake_alpha) v = snake1(v, a.snake_alpha[c]);
+    }
+    win[i] = v;
+  }
+  __syncthreads();
+  const int t = t0 + threadIdx.x;
+  if (t >= a.Tout) return;
+  float acc = 0.0f;
+  for (int c = 0; c < a.Cin; c++) {
+    const float* wr = win + (size_t)c * W + threadIdx.x;
+    for (int j = 0; j < k; j++) acc = fmaf(ldw<BF>(a.w, (size_t)c * k + j), wr[j * dil], acc);
+  }
+  const size_t oi = (size_t)b * a.Tout + t;
+  float v = acc + (a.bias ? a.bias[0] : 0.0f);
+  if (a.res) v += a.res[oi];
+  if (a.tanh_out) v = tanhf(v);
+  a.y[oi] = v;
+}
+
 __global__ void snake_kernel(const float* x, int C, int T, const float* alpha, float* y,
                              size_t n) {
   grid_dep_enter();
@@ -179,6 +218,15 @@ cudaError_t launch_conv1d(const ConvArgs& a, cudaStream_t s) {
     return cudaGetLastError();
   }
   if (conv_tc_supported(a)) return launch_conv_tc(a, a.Tout, 1, 1, s);
+  const size_t win = sizeof(float) * (size_t)a.Cin * (kOutT + (a.k - 1) * a.dil);
+  if (a.Cout == 1 && win <= 48 * 1024) {
+    dim3 g1((a.Tout + kOutT - 1) / kOutT, a.B);
+    if (a.w_bf16)
+      CTTS_LK(launch_k(conv_out1_kernel<true>, g1, dim3(kOutT), win, s, a));
+    else
+      CTTS_LK(launch_k(conv_out1_kernel<false>, g1, dim3(kOutT), win, s, a));
+    return cudaGetLastError();
+  }
   dim3 grid((a.Tout + TT - 1) / TT, (a.Cout + TO - 1) / TO, a.B);
   if (a.w_bf16)
     CTTS_LK(launch_k(conv_kernel<true>, dim3(grid), dim3(256), 0, s, a, a.Tout, 1, 1, 0));

@@ -15,8 +15,9 @@
 //    a stage is 2k bulk copies of up to 4 KB into the no-swizzle K-major
 //    layout [tap][chunk][256 rows][16 B];
 //  * activations (B): the window of 256 + (k-1)*dil input positions of the
-//    stage's 16 channels, Snake applied and rounded to bf16 by eight
-//    producer warps while loading, stored [chunk][row][16 B]; tap j reads
+//    stage's 16 channels, Snake applied and rounded to bf16 by four
+//    producer warps while loading (two such groups take alternate stages),
+//    stored [chunk][row][16 B]; tap j reads
 //    rows [j*dil, j*dil + 256) of it -- a row offset of the descriptor's
 //    start address -- so the window is loaded once for all k taps.
 // Epilogue (warps 4..7, TMEM lane quadrant = warp & 3): bias, residual,
@@ -44,7 +45,12 @@ constexpr int kVMaxK = 8;             // taps supported
 constexpr int kVThreads = 320;        // warp 0 weights, warp 1 MMA, warps 2..9 activations
 constexpr int kVProd = 256;           // activation producer threads
 constexpr int kVProd0 = 64;           // first producer thread
+constexpr int kVGroup = 128;          // producer threads per stage (two groups, alternate stages)
+constexpr int kVItems = 5;            // 16-byte chunks per producer thread and stage (2 x 312 rows max)
+constexpr int kVMaxCin = 1024;        // input channels (Snake table in shared memory)
 constexpr size_t kVMinSmem = 120 * 1024;  // one CTA per SM: its 512 TMEM columns
+
+static_assert(kVItems * kVGroup >= 2 * (kVT + kVMaxHalo + 7), "producer items cover the window");
 
 struct VLay {
   uint32_t rows, a_bytes, b_bytes, stage;
@@ -56,7 +62,7 @@ __host__ __device__ inline VLay vlay(int k, int halo) {
   L.a_bytes = (uint32_t)k * 2u * (uint32_t)kVO * 16u;  // [tap][chunk][256 rows][16 B]
   L.b_bytes = 2u * L.rows * 16u;                       // [chunk][rows][16 B]
   L.stage = L.a_bytes + L.b_bytes;
-  L.total = (size_t)kVStages * L.stage + 8 * (2 * kVStages + 2) + 16;
+  L.total = (size_t)kVStages * L.stage + 8 * (2 * kVStages + 2) + 16 + 8 * (size_t)kVMaxCin;
   return L;
 }
 
@@ -100,9 +106,19 @@ CTTS_DEV bool vwait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   return false;
 }
 
-CTTS_DEV float snake_v(float v, float al) {
-  const float s = sinf(v * al);
-  return v + (1.0f / (al + 1e-9f)) * s * s;
+// Snake (snake.rs:26-36) with the per-channel 1/(alpha + 1e-9) precomputed;
+// the sine is the hardware approximation: the result is rounded to bf16
+// for the MMA, whose rounding error (2^-9 relative) dominates its error.
+CTTS_DEV float snake_fast(float v, float al, float inv) {
+  const float s = __sinf(v * al);
+  return v + inv * (s * s);
+}
+
+// two floats -> packed bf16x2 (round to nearest even), lo in the low half
+CTTS_DEV uint32_t pack_bf2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 __global__ void __launch_bounds__(kVThreads, 1) vae_tc_conv_kernel(const VaeTcArgs a) {
@@ -116,6 +132,7 @@ __global__ void __launch_bounds__(kVThreads, 1) vae_tc_conv_kernel(const VaeTcAr
   uint64_t* fin = done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float2* snk = reinterpret_cast<float2*>(smem + (size_t)kVStages * L.stage + 8 * (2 * kVStages + 2) + 16);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = blockIdx.x * kVT, o0 = blockIdx.y * kVO;
@@ -126,7 +143,7 @@ __global__ void __launch_bounds__(kVThreads, 1) vae_tc_conv_kernel(const VaeTcAr
 
   if (tid == 0) {
     for (int s = 0; s < kVStages; s++) {
-      mbar_init(&full[s], 1 + kVProd);
+      mbar_init(&full[s], 1 + kVGroup);
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, 1);
@@ -134,6 +151,12 @@ __global__ void __launch_bounds__(kVThreads, 1) vae_tc_conv_kernel(const VaeTcAr
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // per-channel Snake parameters: (alpha, 1 / (alpha + 1e-9))
+  if (a.alpha)
+    for (int c = tid; c < a.Cin; c += blockDim.x) {
+      const float al = a.alpha[c];
+      snk[c] = make_float2(al, 1.0f / (al + 1e-9f));
+    }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(512));
@@ -204,39 +227,51 @@ __global__ void __launch_bounds__(kVThreads, 1) vae_tc_conv_kernel(const VaeTcAr
     umma_commit(fin);
     vwait(fin, 0, abort);
   } else if (tid >= kVProd0) {
-    // ---- activation producers: Snake(x) window -> bf16 [chunk][row][16 B]
+    // ---- activation producers: Snake(x) window -> bf16 [chunk][row][16 B].
+    // Two groups of 128 threads take alternate stages, so two windows are
+    // in flight; each thread issues every load of its stage before any
+    // Snake arithmetic (the staging is bound by global-load latency).
     const int p = tid - kVProd0;
+    const int grp = p / kVGroup, q = p % kVGroup;
     const int rows = (int)L.rows, span = kVT + halo;
     const float* xb = a.x + (size_t)b * a.Cin * a.Tin;
     const int base_t = t0 + a.xoff - a.left;
-    for (int s = 0; s < nst && ok; s++) {
+    for (int s = grp; s < nst && ok; s += 2) {
       const int slot = s % kVStages;
       if (s >= kVStages && !vwait(&empty[slot], ((s / kVStages) - 1) & 1, abort)) {
         ok = false;
         break;
       }
       const uint32_t bst = sbase + (uint32_t)slot * L.stage + L.a_bytes;
-      for (int item = p; item < 2 * rows; item += kVProd) {
+      float v[kVItems][8];
+#pragma unroll
+      for (int it = 0; it < kVItems; it++) {
+        const int item = q + it * kVGroup;
         const int kc = item / rows, r = item - kc * rows;
-        const int c = 16 * s + 8 * kc;
         const int src = base_t + r;
-        float v[8];
-        if (r < span && src >= 0 && src < a.Tin) {
-          const float* xc = xb + (size_t)c * a.Tin + src;
+        const bool ld = item < 2 * rows && r < span && src >= 0 && src < a.Tin;
+        const float* xc = xb + (size_t)(16 * s + 8 * kc) * a.Tin + src;
 #pragma unroll
-          for (int e = 0; e < 8; e++) v[e] = __ldg(xc + (size_t)e * a.Tin);
-          if (a.alpha) {
+        for (int e = 0; e < 8; e++) v[it][e] = ld ? __ldg(xc + (size_t)e * a.Tin) : 0.0f;
+      }
 #pragma unroll
-            for (int e = 0; e < 8; e++) v[e] = snake_v(v[e], __ldg(a.alpha + c + e));
+      for (int it = 0; it < kVItems; it++) {
+        const int item = q + it * kVGroup;
+        if (item >= 2 * rows) break;
+        const int kc = item / rows, r = item - kc * rows;
+        const int src = base_t + r;
+        if (a.alpha && r < span && src >= 0 && src < a.Tin) {
+          const float2* sk = snk + 16 * s + 8 * kc;
+#pragma unroll
+          for (int e = 0; e < 8; e++) {
+            const float2 t = sk[e];
+            v[it][e] = snake_fast(v[it][e], t.x, t.y);
           }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; e++) v[e] = 0.0f;
         }
-        const uint32_t w0 = (uint32_t)f2bf(v[0]) | ((uint32_t)f2bf(v[1]) << 16);
-        const uint32_t w1 = (uint32_t)f2bf(v[2]) | ((uint32_t)f2bf(v[3]) << 16);
-        const uint32_t w2 = (uint32_t)f2bf(v[4]) | ((uint32_t)f2bf(v[5]) << 16);
-        const uint32_t w3 = (uint32_t)f2bf(v[6]) | ((uint32_t)f2bf(v[7]) << 16);
+        const uint32_t w0 = pack_bf2(v[it][0], v[it][1]);
+        const uint32_t w1 = pack_bf2(v[it][2], v[it][3]);
+        const uint32_t w2 = pack_bf2(v[it][4], v[it][5]);
+        const uint32_t w3 = pack_bf2(v[it][6], v[it][7]);
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(bst + (uint32_t)(kc * rows + r) * 16u),
                      "r"(w0), "r"(w1), "r"(w2), "r"(w3)
                      : "memory");
@@ -348,7 +383,8 @@ __global__ void repack_conv_tc_kernel(uint16_t* dst, const uint16_t* src, int np
 }  // namespace
 
 bool conv_tc_supported(const ConvArgs& a) {
-  return a.w_bf16 && a.w_tc && a.groups == 1 && a.Cin % 16 == 0 && a.Cin >= 16 && a.Cout >= 64 && a.k >= 1 &&
+  return a.w_bf16 && a.w_tc && a.groups == 1 && a.Cin % 16 == 0 && a.Cin >= 16 && a.Cin <= kVMaxCin &&
+         a.Cout >= 64 && a.k >= 1 &&
          a.k <= kVMaxK && (a.k - 1) * a.dil <= kVMaxHalo && a.cout_pad >= a.Cout && a.cout_pad % 128 == 0;
 }
 
