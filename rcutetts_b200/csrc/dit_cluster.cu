@@ -10,39 +10,48 @@
 // Layout.  A cluster owns kU = 10 utterances (30 token rows: row 3u+s is
 // token s of utterance u) for the whole frame.  CTA c of the cluster owns
 // hidden columns [32c, 32c+32) of the residual stream (fp32, in shared
-// memory for all steps) and one contiguous weight slice per GEMM: 96 QKV
-// rows (half of head c/2), 32 o-proj rows, 192 gate/up rows (SwiGLU columns
-// [96c, 96c+96)), 32 down rows.  Each GEMM is one tcgen05.mma chain
-// D[128 x N] = A[128 x K] . B[N x K]^T with the activations as A (rows
-// 0..29 valid; the descriptor's 8-row groups beyond the fourth read the
-// following shared memory and land in accumulator lanes that are never
-// read) and the weight slice as B, streamed by TMA through a 2-slot ring
-// that runs ahead of the activations across layers and steps (the weights
-// do not depend on them), the accumulator in TMEM.
+// memory for all steps).  Every GEMM is a tcgen05.mma chain with the
+// activations as A (rows 0..29 valid; the descriptor's 8-row groups beyond
+// the fourth read the following shared memory and land in accumulator
+// lanes that are never read), a weight slice as B streamed by TMA through
+// a 3-slot ring that runs ahead of the activations across layers and steps
+// (the weights do not depend on them), the accumulator in TMEM:
+//  * QKV and gate/up are split over N: CTA c computes 96 QKV columns (half
+//    of head c/2) and 192 gate/up columns (SwiGLU columns [96c, 96c+96))
+//    from the all-gathered normed operand (K = 512);
+//  * o-proj and down are split over K: CTA c multiplies its own 32
+//    attention dims / 96 SwiGLU columns by all 512 output rows (N = 2 x 256
+//    MMAs), and the fp32 partials are reduce-scattered: each owner sums the
+//    16 partials of its 32 columns in CTA order (deterministic).
 //
 // Exchange.  A operands are stored K-major with the 64-byte swizzle as one
 // contiguous slice per CTA ([32-column atom][row group][8 rows x 64 B]), so
-// each stage ends with the compute warp writing its own slice in place and
-// pushing it to the 15 peers with one bulk copy each
+// the all-gathers end with the compute warps writing their own slice in
+// place and pushing it to the 15 peers with one bulk copy each
 // (cp.async.bulk shared::cta -> shared::cluster), completing on the peer's
 // mbarrier; row statistics, attention score partials, out_proj partials and
-// the new latent go the same way from small staging buffers.  Every
-// mbarrier is armed with its phase's byte count (arrive.expect_tx) by its
-// waiter right after the previous phase completed, which by the stage order
-// is before any peer can push for that phase; consecutive stages never
-// share an mbarrier.  Stages that feed a GEMM (A barriers, two arrivals:
-// the arm and this CTA's own slice) are waited by the MMA thread, the others
-// (B barriers) by the compute warp.  RMSNorm row sums are reduced from the
-// 16 per-CTA partials in CTA order (deterministic), attention scores from
-// the two half-head partials in order, out_proj over the 16 column slices
-// in order.  AdaLN slices of the next layer are prefetched by bulk copies
-// from global memory into a second buffer.
+// the new latent go the same way from small staging buffers.  The
+// reduce-scatter stages the partials in two rounds of eight owners in the
+// all-gathered operand area (idle from the end of its GEMM until the peers'
+// next push, which needs these partials first) and pushes one 4 KB block
+// per owner.  Every mbarrier is armed with its phase's byte count
+// (arrive.expect_tx) by its waiter right after the previous phase
+// completed, which by the stage order is before any peer can push for that
+// phase; consecutive stages never share an mbarrier.  Stages that feed a
+// GEMM (A barriers, two arrivals: the arm and this CTA's own slice) are
+// waited by the MMA thread, the others (B barriers, reduce-scatter) by the
+// compute warps.  RMSNorm row sums are reduced from the 16 per-CTA partials
+// in CTA order (deterministic), attention scores from the two half-head
+// partials in order, out_proj over the 16 column slices in order.  AdaLN
+// slices of the next layer are prefetched by bulk copies from global
+// memory into a second buffer.
 //
-// Roles (128 threads): warp 0 = compute (lane = token row; TMEM lanes
-// 0..31), warp 1 = MMA issuer (lane 0) and TMEM owner, warp 2 = TMA
-// producer (lane 0).  Every wait is bounded; on timeout the CTA records an
-// error code, tells its peers to stop, waits (bounded) for its own copies
-// and MMAs in flight, and leaves through a final cluster barrier.
+// Roles (512 threads): warps 0, 4, 8, 12 = compute (lane = token row; TMEM
+// lanes 0..31, columns split over the four), warp 1 = MMA issuer (lane 0)
+// and TMEM owner, warp 2 = TMA producer (lane 0).  Every wait is bounded;
+// on timeout the CTA records an error code, tells its peers to stop, waits
+// (bounded) for its own copies and MMAs in flight, and leaves through a
+// final cluster barrier.
 #include <algorithm>
 #include <cstdio>
 #include <mutex>
@@ -70,12 +79,21 @@ constexpr int kGuN = 2 * kActOwn;      // 192: gate + up
 // operand is one block it can push to its peers with a single bulk copy.
 constexpr uint32_t kSlice = kGrp * (kOwn / 8) * 128;      // 2 KB: 32 columns
 constexpr uint32_t kActSlice = kGrp * (kActOwn / 8) * 128;  // 6 KB: 96 columns
-constexpr uint32_t kXA = 0;                              // norm outputs, K = 512
-constexpr uint32_t kACT = kXA + kC * kSlice;             // SwiGLU outputs, K = 1536 (attention, K = 512, aliased)
-constexpr uint32_t kRING = kACT + kC * kActSlice;        // weight ring
+constexpr uint32_t kXA = 0;                              // norm outputs, K = 512 (all-gathered)
+constexpr uint32_t kATT = kXA + kC * kSlice;             // own attention slice (o-proj A, K = 32)
+constexpr uint32_t kSWI = kATT + kSlice;                 // own SwiGLU slice (down A, K = 96)
+constexpr uint32_t kPART = kSWI + kActSlice;             // split-K partials from every CTA (o-proj / down)
+constexpr uint32_t kPartBytes = 32 * kOwn * 4;           // 4 KB: [8 column chunks][32 rows][4 floats]
+constexpr uint32_t kRING = kPART + kC * kPartBytes;      // weight ring
 constexpr uint32_t kSlotBytes = kGuN * 128;              // 24 KB: one 192-row, 64-wide K block
-constexpr int kSlots = 2;
+constexpr int kSlots = 3;
 constexpr uint32_t kF32 = kRING + kSlots * kSlotBytes;
+constexpr int kTmemCols = 512;                           // split-K accumulators span all 512 outputs
+// split-K weight blocks (o-proj, down): 256 output rows x 32 K columns,
+// 64-byte swizzle, 16 KB per ring slot
+constexpr uint32_t kHalfBlk = 256 * 64;
+static_assert(kRING % 1024 == 0 && kATT % 512 == 0 && kSWI % 512 == 0 && kPART % 16 == 0,
+              "operand alignment");
 constexpr int kSeqLd = kOwn + 1;
 constexpr int kAdLd = 6 * kOwn + 4;  // 196: 16-byte rows, 2-way banks at most
 // fp32 area, float offsets from kF32 (exchange buffers 16-byte aligned)
@@ -123,7 +141,9 @@ __host__ __device__ inline Lay lay(int NL) {
 
 // mbarrier indices
 constexpr int bFULL = 0, bEMPTY = kSlots, bMMA = 2 * kSlots, bFIN = bMMA + 1, bA = bFIN + 1, bB = bA + 2,
-              bAD = bB + 2;
+              bAD = bB + 2, bRS = bAD + 1;
+static_assert(bRS < 16, "16 mbarrier slots");
+static_assert(8 * kPartBytes <= kPART - kXA, "reduce-scatter staging fits below the partials");
 
 // Optional stage timeline (build with -DCTTS_DIT_TRACE): CTA 0 records
 // (event, %globaltimer) pairs of its compute warp (row 0) and MMA thread.
@@ -147,23 +167,28 @@ CTTS_DEV void dtrace(int role, int ev, int& n) {
 #define DTRACE(role, ev)
 #endif
 
-// per-GEMM geometry: weight rows of the slice (MMA N), 64-wide K blocks,
-// K blocks per ring slot (one TMA box: the packed weights are pre-tiled as
-// [layer][CTA][K block][N rows][64], so a slot is kbps*N contiguous rows),
-// rows of one layer in the row-major slices
+// per-GEMM geometry.  QKV (0) and gate/up (2): the CTA's weight slice is
+// the MMA N (96 / 192 rows), 64-wide K blocks pre-tiled as
+// [layer][CTA][K block][N rows][64] (128-byte swizzle), kbps K blocks per
+// ring slot.  o-proj (1) and down (3) are split over K: the CTA multiplies
+// its own 32 attention dims / 96 SwiGLU columns by all 512 output rows, in
+// blocks of 256 rows x 32 K columns (64-byte swizzle) pre-tiled as
+// [layer][CTA][K atom][half][256][32]; nblk ring slots per GEMM.
 struct Gemm {
-  int N, nkb, kbps, rows_per_layer;
+  int nblk, kbps;
+  uint32_t bytes;  // per ring slot
 };
 CTTS_DEV Gemm gemm(int g) {
   switch (g) {
-    case 0: return {kQkvN, kH / 64, (int)(kSlotBytes / (kQkvN * 128)), kC * kQkvN};
-    case 1: return {kOwn, kH / 64, 4, kH};
-    case 2: return {kGuN, kH / 64, (int)(kSlotBytes / (kGuN * 128)), kC * kGuN};
-    default: return {kOwn, kF / 64, (int)(kSlotBytes / (kOwn * 128)), kH};
+    case 0: return {kH / 64 / 2, 2, 2u * kQkvN * 128u};
+    case 1: return {2, 1, kHalfBlk};
+    case 2: return {kH / 64, 1, kGuN * 128u};
+    default: return {6, 1, kHalfBlk};
   }
 }
-// bytes a CTA receives from its 15 peers for the A stage of GEMM g
-CTTS_DEV uint32_t a_bytes(int g) { return (uint32_t)(kC - 1) * (g == 3 ? kActSlice : kSlice); }
+// bytes a CTA receives from its 15 peers for the A stage of GEMM g (the
+// split-K GEMMs read only this CTA's own slice)
+CTTS_DEV uint32_t a_bytes(int g) { return (g == 0 || g == 2) ? (uint32_t)(kC - 1) * kSlice : 0u; }
 
 // Bytes of B stage b (all senders, self included).  Order: the first fill,
 // then per Euler step [scores, row stats, row stats] per layer, out_proj
@@ -300,16 +325,18 @@ __global__ void __launch_bounds__(kNT, 1)
       mbar_init(&bars[bA + i], 2);
       mbar_init(&bars[bB + i], 1);
     }
+    mbar_init(&bars[bRS], 1);
     *abort = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     arm(bar(bA + 0), a_bytes(0));
     arm(bar(bA + 1), a_bytes(1));
     arm(bar(bB + 0), b_bytes(0, NL));
     arm(bar(bB + 1), b_bytes(1, NL));
+    arm(bar(bRS), kC * kPartBytes);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(256));
+                 "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -325,19 +352,21 @@ __global__ void __launch_bounds__(kNT, 1)
   bool pdone = false;
   auto produce_one = [&]() {
     const Gemm G = gemm(pg);
-    const int n = min(G.kbps, G.nkb - pkb);
     const int slot = (int)(pit % kSlots);
     const uint32_t dst = sb + kRING + (uint32_t)slot * kSlotBytes;
-    mbar_expect_tx(&bars[bFULL + slot], (uint32_t)(n * G.N * 128));
-    const int y = ((pl * kC + c) * G.nkb + pkb) * G.N;
+    mbar_expect_tx(&bars[bFULL + slot], G.bytes);
+    // first row of this slot's box in the tiled matrix
+    int y;
+    if (pg == 0) y = ((pl * kC + c) * (kH / 64) + pkb * G.kbps) * kQkvN;
+    else if (pg == 2) y = ((pl * kC + c) * (kH / 64) + pkb) * kGuN;
+    else y = ((pl * kC + c) * G.nblk + pkb) * 256;
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
             dst),
         "l"(reinterpret_cast<uint64_t>(maps[pg])), "r"(0), "r"(y), "r"(bar(bFULL + slot))
         : "memory");
     pit++;
-    pkb += n;
-    if (pkb >= G.nkb) {
+    if (++pkb >= G.nblk) {
       pkb = 0;
       if (++pg == 4) {
         pg = 0;
@@ -445,16 +474,44 @@ __global__ void __launch_bounds__(kNT, 1)
             DTRACE(1, 5);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t idesc = umma_idesc(G.N);
-            const uint32_t abase = sb + ((g == 0 || g == 2) ? kXA : kACT);
+            if (g == 1 || g == 3) {
+              // split-K: this CTA's own slice (one / three 32-column atoms)
+              // times 256-row weight blocks, accumulators D[:, 256 h + n]
+              const uint32_t idesc = umma_idesc(256);
+              const uint32_t abase = sb + (g == 1 ? kATT : kSWI);
+              for (int blk = 0; blk < G.nblk && ok; blk++) {
+                const int slot = (int)(it % kSlots);
+                if (!wait_local(bar(bFULL + slot), (it / kSlots) & 1, abort)) {
+                  ok = false;
+                  break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                DTRACE(1, 8);
+                const int atom = blk >> 1, half = blk & 1;
+                const uint64_t ad = desc_sw64(abase + (uint32_t)atom * 2048u);
+                const uint64_t bd = desc_sw64(sb + kRING + (uint32_t)slot * kSlotBytes);
+                const uint32_t dcol = tmem + 256u * (uint32_t)half;
+                umma_bf16(dcol, ad, bd, idesc, atom ? 1u : 0u);
+                umma_bf16(dcol, ad + 2, bd + 2, idesc, 1u);
+                umma_commit(&bars[bEMPTY + slot]);
+                it++;
+              }
+              if (ok) umma_commit(&bars[bMMA]);
+              DTRACE(1, 6);
+              continue;
+            }
+            const int GN = g == 0 ? kQkvN : kGuN;
+            const int nkb = kH / 64;
+            const uint32_t idesc = umma_idesc(GN);
+            const uint32_t abase = sb + kXA;
             // Both operands advance by constant descriptor steps (address >> 4
             // in the low bits): the A operand's 32-column atoms are 2 KB apart
             // in column order for every GEMM (one atom per 32-column slice,
             // three per 96-column slice), so K step ks sits at atom ks / 2,
             // +32 bytes for odd ks; a weight K block is G.N rows of 128 bytes.
             uint64_t ad = desc_sw64(abase);
-            const uint64_t bstep = (uint64_t)(G.N * 8);
-            for (int kb0 = 0; kb0 < G.nkb && ok; kb0 += G.kbps) {
+            const uint64_t bstep = (uint64_t)(GN * 8);
+            for (int kb0 = 0; kb0 < nkb && ok; kb0 += G.kbps) {
               const int slot = (int)(it % kSlots);
               if (!wait_local(bar(bFULL + slot), (it / kSlots) & 1, abort)) {
                 ok = false;
@@ -462,7 +519,7 @@ __global__ void __launch_bounds__(kNT, 1)
               }
               asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
               DTRACE(1, 8);
-              const int n = min(G.kbps, G.nkb - kb0);
+              const int n = G.kbps;
               uint64_t bd = umma_desc(sb + kRING + (uint32_t)slot * kSlotBytes);
               for (int q = 0; q < n; q++) {
                 umma_bf16(tmem, ad, bd, idesc, (kb0 | q) ? 1u : 0u);
@@ -544,7 +601,7 @@ __global__ void __launch_bounds__(kNT, 1)
         DTRACE(0, 7);
         const uint32_t ab = bar(bA + (int)(aph & 1));
         if (lane == 0) arrive_local(ab);
-        if (lane < kC && lane != c) push(slice_addr, slice_addr, bytes, ab, (uint32_t)lane);
+        if (bytes && lane < kC && lane != c) push(slice_addr, slice_addr, bytes, ab, (uint32_t)lane);
         __syncwarp();
         DTRACE(0, 1);
       }
@@ -595,20 +652,80 @@ __global__ void __launch_bounds__(kNT, 1)
       st_u4(smem + kXA + c * kSlice + slice_off(r, cw), pk[0], pk[1], pk[2], pk[3]);
       postA(sb + kXA + c * kSlice, kSlice);
     };
-    // gated residual update of own columns [8cw, 8cw+8) from the 32-column
-    // accumulator, and their sum of squares -> pss[cw]
-    auto resid = [&](const float* adb, int gate_k) {
-      uint32_t v[8];
-      tmem_ld8_nowait(tmem + 8 * cw, v);
-      tmem_wait();
+    // Split-K reduce-scatter.  The accumulator holds this CTA's partial of
+    // all 512 outputs for its 32 rows; warp cw sends columns
+    // [128cw, 128cw + 128) -- owner CTAs 4cw..4cw+3 -- each lane its row,
+    // by remote stores into the owner's partial slot of this CTA
+    // ([8 column chunks][32 rows][4 floats]), then an arrive that releases
+    // them.  Warp 0 waits for all 16 x 32 arrivals of the phase.
+    uint32_t rsph = 0;
+    auto rs_exchange = [&]() {
+      // two rounds of eight owners; warp cw stages owners 8*round + 2cw,
+      // 8*round + 2cw + 1 into the staging area (the all-gathered norm
+      // operand, idle until the peers' next push, which needs these
+      // partials first), then warp 0 pushes one 4 KB block per owner
+#pragma unroll 1
+      for (int round = 0; round < 2; round++) {
+#pragma unroll 1
+        for (int k2 = 0; k2 < 2; k2++) {
+          const int slot = 2 * cw + k2;
+          uint32_t v[32];
+          tmem_ld32_nowait(tmem + 32u * (uint32_t)(8 * round + slot), v);
+          tmem_wait();
+          uint8_t* stg = smem + kXA + (uint32_t)slot * kPartBytes + (uint32_t)r * 16u;
+#pragma unroll
+          for (int q = 0; q < 8; q++) st_u4(stg + q * 512, v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        cbar();
+        if (cw == 0) {
+          if (lane < 8) {
+            const uint32_t d = (uint32_t)(8 * round + lane);
+            push(sb + kPART + (uint32_t)c * kPartBytes, sb + kXA + (uint32_t)lane * kPartBytes, kPartBytes,
+                 bar(bRS), d);
+            // the staging is rewritten next round (and by this CTA's next
+            // norm operand): wait until the copy has read it
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+          }
+          __syncwarp();
+          if (round == 0) DTRACE(0, 9);
+        }
+        cbar();
+      }
+      if (cw == 0) DTRACE(0, 10);
+      if (cw == 0) {
+        const uint32_t rb = bar(bRS);
+        if (ok && !wait_cluster(rb, rsph & 1, abort)) ok = false;
+        if (lane == 0) arm(rb, kC * kPartBytes);  // the next exchange's bytes
+        __syncwarp();
+        DTRACE(0, 11);
+      }
+      rsph++;
+      sync_ok();
+    };
+    // gated residual update of own columns [8cw, 8cw+8) from the 16 split-K
+    // partials (summed in CTA order: deterministic), and their sum of
+    // squares -> pss[cw]
+    auto resid_rs = [&](const float* adb, int gate_k) {
       float p = 0.0f;
       if (rv) {
+        const float* part = reinterpret_cast<const float*>(smem + kPART);
+        float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
+#pragma unroll 4
+        for (int q2 = 0; q2 < kC; q2++) {
+          const float4 a0 = *reinterpret_cast<const float4*>(part + q2 * (kPartBytes / 4) + (2 * cw) * 128 + r * 4);
+          const float4 a1 = *reinterpret_cast<const float4*>(part + q2 * (kPartBytes / 4) + (2 * cw + 1) * 128 + r * 4);
+          s0.x += a0.x; s0.y += a0.y; s0.z += a0.z; s0.w += a0.w;
+          s1.x += a1.x; s1.y += a1.y; s1.z += a1.z; s1.w += a1.w;
+        }
+        const float acc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
         const float* gt = adb + u * kAdLd + gate_k * kOwn;
 #pragma unroll
         for (int e = 0; e < 8; e++) {
           const int j = 8 * cw + e;
           const float coef = a.adaln ? 1.0f + gt[j] : 1.0f;
-          const float nv = seq[r * kSeqLd + j] + coef * __uint_as_float(v[e]);
+          const float nv = seq[r * kSeqLd + j] + coef * acc[e];
           seq[r * kSeqLd + j] = nv;
           p = fmaf(nv, nv, p);
         }
@@ -770,15 +887,19 @@ __global__ void __launch_bounds__(kNT, 1)
 #pragma unroll
             for (int i = 0; i < 8; i++) o[i] = fmaf(p, __shfl_sync(0xffffffffu, v[i], src), o[i]);
           }
-          // o-proj weights are column-permuted so this slice is K columns [32c, 32c+32)
-          st_u4(smem + kACT + c * kSlice + slice_off(r, cw), pack_bf(o[0], o[1]), pack_bf(o[2], o[3]),
-                pack_bf(o[4], o[5]), pack_bf(o[6], o[7]));
-          postA(sb + kACT + c * kSlice, kSlice);
+          // the o-proj is split over K: this slice (the CTA's 32 attention
+          // dims) is the whole A operand of its partial product
+          st_u4(smem + kATT + slice_off(r, cw), pack_bf(o[0], o[1]), pack_bf(o[2], o[3]), pack_bf(o[4], o[5]),
+                pack_bf(o[6], o[7]));
+          postA(sb + kATT, 0);
         }
-        // S4: o-proj accumulator -> gated residual -> row statistics
+        // S4: o-proj partials -> owners; the 16 partials of my columns ->
+        // gated residual -> row statistics
         wait_mma();
         if (!ok) break;
-        resid(adb, 2);
+        rs_exchange();
+        if (!ok) break;
+        resid_rs(adb, 2);
         ss_combine_push();
         if (!ok) break;
         // S5: norm2 -> operand
@@ -788,7 +909,7 @@ __global__ void __launch_bounds__(kNT, 1)
         wait_mma();
         if (!ok) break;
         {
-          uint8_t* sl = smem + kACT + c * kActSlice;
+          uint8_t* sl = smem + kSWI;
 #pragma unroll
           for (int t = 0; t < 3; t++) {
             uint32_t gv[8], uv[8];
@@ -804,12 +925,14 @@ __global__ void __launch_bounds__(kNT, 1)
             }
             st_u4(sl + slice_off(r, 3 * cw + t), pk[0], pk[1], pk[2], pk[3]);
           }
-          postA(sb + kACT + c * kActSlice, kActSlice);
+          postA(sb + kSWI, 0);
         }
-        // S7: down accumulator -> gated residual -> row statistics
+        // S7: down partials -> owners -> gated residual -> row statistics
         wait_mma();
         if (!ok) break;
-        resid(adb, 5);
+        rs_exchange();
+        if (!ok) break;
+        resid_rs(adb, 5);
         ss_combine_push();
       }
       if (!ok) break;
@@ -893,13 +1016,7 @@ __global__ void __launch_bounds__(kNT, 1)
   cluster_sync();
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
-}
-
-// dst[row][k] = src[row][perm[k]] (o-proj input columns into CTA order)
-__global__ void permute_cols_kernel(uint16_t* dst, const uint16_t* src, const int* perm, int K) {
-  const size_t row = blockIdx.x;
-  for (int k = threadIdx.x; k < K; k += blockDim.x) dst[row * K + k] = src[row * K + perm[k]];
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
 }
 
 // Pre-tiling: src [blocks*N rows, K] (row-major slices of N rows) ->
@@ -915,12 +1032,43 @@ __global__ void tile_kernel(uint16_t* dst, const uint16_t* src, int N, int K) {
   reinterpret_cast<uint4*>(dst + row * 64)[part] = *s;
 }
 
+// Split-K weight blocks: dst[blk][r][k] (256 rows x 32 columns per block,
+// blocks ordered [CTA c][atom a][half h]) = W[256 h + r][col(c, 32 a + k)]
+// for W [512 rows, K] row-major; col() = the CTA's K columns: the o-proj's
+// attention dims of CTA c (perm[32 c + k]) or the down projection's SwiGLU
+// columns 96 c + k (perm null, 3 atoms per CTA).
+__global__ void splitk_blocks_kernel(uint16_t* dst, const uint16_t* W, int K, int atoms, const int* perm) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t n = (size_t)kC * atoms * 2 * 256 * 32;
+  if (i >= n) return;
+  const int k = (int)(i % 32), r = (int)((i / 32) % 256);
+  const size_t blk = i / (32 * 256);
+  const int h = (int)(blk % 2), a_ = (int)((blk / 2) % atoms), cc = (int)(blk / (2 * atoms));
+  const int kk = cc * atoms * 32 + a_ * 32 + k;
+  const int col = perm ? perm[kk] : kk;
+  dst[i] = W[(size_t)(256 * h + r) * K + col];
+}
+
 // dst row i (K bf16 elements) = src row idx[i]
 __global__ void gather_rows_kernel(uint16_t* dst, const uint16_t* src, const int* idx, int K) {
   const int i = blockIdx.x;
   const uint4* s = reinterpret_cast<const uint4*>(src + (size_t)idx[i] * K);
   uint4* d = reinterpret_cast<uint4*>(dst + (size_t)i * K);
   for (int t = threadIdx.x; t < K / 8; t += blockDim.x) d[t] = s[t];
+}
+
+// 2D bf16 tensor [rows, 32] (64-byte rows), box [256 rows, 32], 64-byte
+// swizzle: the split-K weight blocks.
+bool make_map_sw64(CUtensorMap* m, const void* base, int rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {32, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {64};
+  cuuint32_t box[2] = {32, 256};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 cudaError_t set_attrs(size_t smem) {
@@ -1013,10 +1161,13 @@ cudaError_t dit_cluster_pack(DitClusterW& W, int NL, const void* const* wqkv, co
   for (int l = 0; l < NL && e == cudaSuccess; l++) {
     gather_rows_kernel<<<kC * kQkvN, 64>>>(W.qkv + (size_t)l * kC * kQkvN * kH,
                                            static_cast<const uint16_t*>(wqkv[l]), dq, kH);
-    permute_cols_kernel<<<kH, 128>>>(W.o + (size_t)l * kH * kH, static_cast<const uint16_t*>(wo[l]), dp, kH);
+    const unsigned nob = (unsigned)(((size_t)kC * 1 * 2 * 256 * 32 + 255) / 256);
+    splitk_blocks_kernel<<<nob, 256>>>(W.o + (size_t)l * kH * kH, static_cast<const uint16_t*>(wo[l]), kH, 1, dp);
     gather_rows_kernel<<<kC * kGuN, 64>>>(W.gu + (size_t)l * kC * kGuN * kH,
                                           static_cast<const uint16_t*>(wgu[l]), dg, kH);
-    gather_rows_kernel<<<kH, 64>>>(W.dn + (size_t)l * kH * kF, static_cast<const uint16_t*>(wd[l]), di, kF);
+    const unsigned ndb = (unsigned)(((size_t)kC * 3 * 2 * 256 * 32 + 255) / 256);
+    splitk_blocks_kernel<<<ndb, 256>>>(W.dn + (size_t)l * kH * kF, static_cast<const uint16_t*>(wd[l]), kF, 3,
+                                       nullptr);
     e = cudaGetLastError();
     if (e == cudaSuccess)
       e = cudaMemcpy(W.norms + (size_t)(l * 2) * kH, norm1[l], sizeof(float) * kH, cudaMemcpyDeviceToDevice);
@@ -1033,7 +1184,7 @@ cudaError_t dit_cluster_pack(DitClusterW& W, int NL, const void* const* wqkv, co
     uint16_t* p;
     size_t n;
     int N, K;
-  } mats[4] = {{W.qkv, nq, kQkvN, kH}, {W.o, no, kOwn, kH}, {W.gu, ng, kGuN, kH}, {W.dn, nd, kOwn, kF}};
+  } mats[2] = {{W.qkv, nq, kQkvN, kH}, {W.gu, ng, kGuN, kH}};  // o / down are blocked already
   for (auto& m : mats) {
     if (e == cudaSuccess) e = cudaMemcpy(tmp, m.p, m.n * 2, cudaMemcpyDeviceToDevice);
     if (e == cudaSuccess) {
@@ -1045,8 +1196,8 @@ cudaError_t dit_cluster_pack(DitClusterW& W, int NL, const void* const* wqkv, co
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   cudaFree(tmp);
   if (e != cudaSuccess) return e;
-  if (!make_map(&W.tm_qkv, W.qkv, (int)(nq / 64), 64, 2 * kQkvN) || !make_map(&W.tm_o, W.o, (int)(no / 64), 64, 4 * kOwn) ||
-      !make_map(&W.tm_gu, W.gu, (int)(ng / 64), 64, kGuN) || !make_map(&W.tm_dn, W.dn, (int)(nd / 64), 64, 6 * kOwn))
+  if (!make_map(&W.tm_qkv, W.qkv, (int)(nq / 64), 64, 2 * kQkvN) || !make_map_sw64(&W.tm_o, W.o, (int)(no / 32)) ||
+      !make_map(&W.tm_gu, W.gu, (int)(ng / 64), 64, kGuN) || !make_map_sw64(&W.tm_dn, W.dn, (int)(nd / 32)))
     return cudaErrorInvalidPitchValue;
   return cudaSuccess;
 }

@@ -25,10 +25,11 @@ struct DitClusterShape {
 // Weights repacked so that CTA c of a cluster streams one contiguous slice
 // per GEMM: QKV rows [c*96, c*96+96) of layer l are q, k, v of head c/2 for
 // dims {16(c%2)..+15, 32+16(c%2)..+15}; gate/up rows [c*192, +192) are gate
-// then up of SwiGLU columns [96c, 96c+96); o-proj has its input columns in
-// the same per-CTA order as the QKV slices (columns [32c, 32c+32) are the
-// attention dims CTA c produces); down is the model's own [out, in] matrix.
-// All bf16, layers stacked along rows.
+// then up of SwiGLU columns [96c, 96c+96) (both pre-tiled in 64-column K
+// blocks); o-proj and down are split over K: CTA c's blocks hold all 512
+// output rows against its own input columns (o-proj: the 32 attention dims
+// CTA c produces; down: SwiGLU columns [96c, 96c+96)), as 256-row x
+// 32-column blocks [CTA][K atom][half].  All bf16, layers stacked.
 struct DitClusterW {
   uint16_t *qkv = nullptr, *o = nullptr, *gu = nullptr, *dn = nullptr;
   float* norms = nullptr;  // [NL][2][H]: norm1, norm2
