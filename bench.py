@@ -137,6 +137,15 @@ def shard(n_total: int, rank: int, world: int):
     return range(rank * per, (rank + 1) * per)
 
 
+def rank_workload(rank: int, world: int, vocab: int, seed: int = 3):
+    """The utterances (text ids, prompt latents) rank `rank` decodes: its
+    contiguous shard of the B_PER_GPU * world utterances of the seeded
+    batch, in batch order (every rank draws the same batch, so no data moves
+    between ranks)."""
+    allu = utterances(B_PER_GPU * world, seed=seed, vocab=vocab)
+    return [allu[i] for i in shard(B_PER_GPU * world, rank, world)]
+
+
 def max_over_ranks(values, world: int, device=None):
     """Element-wise max of per-rank timings (the slowest rank defines the
     job's time).  torch.distributed plumbing only."""
@@ -179,14 +188,13 @@ def run_ours(args, rank, world, local):
     hbm, bf16_tf, peak_kind = peaks()
     lcfg, dcfg, lw, dw, hw, lm, dit = make_models("bf16", seed=3, device=dev)
     B = B_PER_GPU
-    allu = utterances(B * world, seed=3, vocab=lcfg.vocab)
-    utts = [allu[i] for i in shard(B * world, rank, world)]
+    utts = rank_workload(rank, world, lcfg.vocab)
     K, W = args.steps, args.warmup
     # timed frames end near the middle of the run unless a start frame is given
     start = args.start_frame if args.start_frame >= 0 else max(0, GEN_FRAMES // 2 - W - K)
     total = start + W + 2 * K + 2
     max_prefix = max(len(ids) for ids, _ in utts) + PROMPT_FRAMES
-    cap = max_prefix + max(total, GEN_FRAMES) + 4
+    cap = max_prefix + max(total, GEN_FRAMES) + 16
     eng = FrameEngine(lm, dit, hw, batch=B, capacity=cap, euler_steps=10, groups=args.groups)
     ctx0 = []
     for b, (ids, prompt) in enumerate(utts):
@@ -232,16 +240,31 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
     ms_e2e = x0.elapsed_time(x1)
     ms, ms_e2e = max_over_ranks([ms, ms_e2e], world, device="cuda")
+    phases = profile_phases(eng, noise[start + W:start + W + 10], lat[start + W:start + W + 10])
     launches = eng.launches_per_step
     ctx_mean = float(np.mean(ctx0)) + start + W + K / 2
     step_bytes = algorithmic_bytes_per_step(lcfg, dcfg, B, ctx_mean, 2, 2)
     res = {
         "ms": ms, "ms_e2e": ms_e2e, "launches": launches, "clocks": clocks, "ctx_mean": ctx_mean,
         "step_bytes": step_bytes, "start": start, "peak": (hbm, bf16_tf, peak_kind),
-        "finite": bool(torch.isfinite(lat[:start + W + K]).all().item()),
+        "finite": bool(torch.isfinite(lat[:start + W + K]).all().item()), "phases": phases,
     }
     del eng
     return res, (lm, dit, lcfg, dcfg, hw)
+
+
+def profile_phases(eng, noise, lat):
+    """Per-phase device times of a few extra frames in the engine's
+    profiling mode (the --profile-steps timers of bin/cutetts.rs:328-350):
+    eager frames with CUDA events between the stop head, DiT sample,
+    feedback projection and LM step (no graph replay, so the phases add up
+    to more than a replayed frame)."""
+    eng.set_profile(True)
+    for f in range(noise.shape[0]):
+        eng.step_dev(noise[f], lat[f], None)
+    st = eng.profile_stats()
+    eng.set_profile(False)
+    return {k: {"p50_ms": round(v["p50_ms"], 4), "p99_ms": round(v["p99_ms"], 4), "n": v["n"]} for k, v in st.items()}
 
 
 def run_b1(args, dev):
@@ -274,6 +297,9 @@ def run_b1(args, dev):
     torch.cuda.synchronize()
     torch.cuda.profiler.stop()
     ms = e0.elapsed_time(e1) / args.b1_frames
+    # five more frames in the profiling mode (the cache has 210 rows past
+    # the prefix; noise rows are reused)
+    phases = profile_phases(eng, noise[:5], lat[:5])
     ctx_mean = 40 + PROMPT_FRAMES + frames / 2
     step_bytes = algorithmic_bytes_per_step(lcfg, dcfg, 1, ctx_mean, 4, 4)
     hbm, _, kind = peaks()
@@ -284,7 +310,7 @@ def run_b1(args, dev):
            "step_roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
                              "frac": round(gbs / hbm, 4), "bytes_per_step": int(step_bytes),
                              "of": kind},
-           "launches_per_step": eng.launches_per_step}
+           "launches_per_step": eng.launches_per_step, "phases": phases}
     del eng
     return out
 
@@ -798,6 +824,7 @@ def main():
         "launches_per_step": res["launches"],
         "clocks": res["clocks"],
         "outputs_finite": res["finite"],
+        "phases": res["phases"],
     }
     if rank == 0 and world == 1:
         lm, dit, lcfg, dcfg, hw = keep

@@ -214,6 +214,18 @@ CTTS_API int ctts_engine_step_dev(ctts_engine* e, const float* noise_dev, float*
                          float* stop_dev, void* stream);
 /* Kernel launches issued by one frame step (for measurement reporting). */
 CTTS_API int ctts_engine_launches_per_step(const ctts_engine* e);
+/* Per-frame phase timers (the --profile-steps instrument of
+ * rust-codec/src/bin/cutetts.rs:328-350,466-478): while on, every frame runs
+ * eagerly with CUDA events between its phases -- 0 stop head, 1 DiT sample,
+ * 2 feedback projection, 3 LM step -- and the step synchronizes its stream.
+ * Switching on or off clears the collected times.  Single sub-batch group
+ * only (CTTS_ERR_STATE otherwise). */
+CTTS_API int ctts_engine_set_profile(ctts_engine* e, int on);
+/* mean, p50, p99 (ms) of one phase over the profiled frames; *n = frames. */
+CTTS_API int ctts_engine_profile_stats(const ctts_engine* e, int phase, float* mean_p50_p99, int* n);
+/* "name: n=N mean=Xms p50=Yms p99=Zms" per phase (profile_report,
+ * bin/cutetts.rs:338-350) into buf; returns the bytes written. */
+CTTS_API int ctts_engine_profile_report(const ctts_engine* e, char* buf, int len);
 /* The engine's stream (cudaStream_t as void*). */
 CTTS_API void* ctts_engine_stream(const ctts_engine* e);
 CTTS_API void ctts_engine_free(ctts_engine* e);

@@ -89,6 +89,9 @@ SIGNATURES = {
     "ctts_engine_set_speaker": (C.c_int, [vp, C.c_int, fp]),
     "ctts_engine_step": (C.c_int, [vp, fp, fp, fp]),
     "ctts_engine_step_dev": (C.c_int, [vp, vp, vp, vp, vp]),
+    "ctts_engine_set_profile": (C.c_int, [vp, C.c_int]),
+    "ctts_engine_profile_stats": (C.c_int, [vp, C.c_int, fp, C.POINTER(C.c_int)]),
+    "ctts_engine_profile_report": (C.c_int, [vp, C.c_char_p, C.c_int]),
     "ctts_engine_launches_per_step": (C.c_int, [vp]),
     "ctts_engine_stream": (vp, [vp]),
     "ctts_engine_free": (None, [vp]),

@@ -1,8 +1,10 @@
 // api_dit.cu -- C ABI: the DiT flow head (dit.rs / diffusion_head.py) and
 // the per-frame engine (bin/cutetts.rs:429-523 loop body) captured as one
 // CUDA graph per frame.
+#include <algorithm>
 #include <atomic>
 #include <cstdio>
+#include <cstring>
 #include <cstdlib>
 
 #include "api_common.h"
@@ -708,6 +710,13 @@ int engine_enqueue_group(ctts_engine* e, EngineGroup& g, cudaStream_t s, int* la
   float* stop = e->stop + (size_t)g.b0 * 2;
   const float* noise = e->noise + (size_t)g.b0 * PL;
   int nl = 0;
+  // phase boundaries of the profiling mode (one sub-batch only)
+  const bool prof = e->profile && e->groups.size() == 1;
+  auto mark = [&](int i) -> int {
+    if (prof) CTTS_CK(cudaEventRecord(e->pev[i], s));
+    return CTTS_OK;
+  };
+  if (int rcm = mark(0)) return rcm;
   CTTS_CK(cudaMemcpyAsync(x, noise, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
   {  // stop logits (e2e.rs:83-92)
     LinearArgs a; a.x = z; a.x_ld = H; a.M = B; a.K = H; a.N = 2; a.w = e->stop_w;
@@ -738,11 +747,13 @@ int engine_enqueue_group(ctts_engine* e, EngineGroup& g, cudaStream_t s, int* la
     r.R = 2 * B; r.mode = 2; r.cfg = e->cfg.cfg_strength; r.cfg_w = e->cfg.cfg_strength;
     r.zero_adaln_from = d->cfg.adaln ? B : -1;
   }
+  if (int rcm = mark(1)) return rcm;
   int rc = dit_enqueue(d, *g.ws, r, s, &nl);
   if (rc) return rc;
   CTTS_CK(launch_affine(x, B * PL, e->cfg.latent_scale, e->cfg.latent_bias, lat, s)); nl++;
   for (int h = 0; h < zm; h++)  // the raw latent conditions both branches (bin/cutetts.rs:474-480)
     CTTS_CK(cudaMemcpyAsync(cond + (size_t)h * B * PL, x, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
+  if (int rcm = mark(2)) return rcm;
   {  // feedback projection straight into the LM residual stream
     LinearArgs a; a.x = x; a.x_ld = PL; a.M = B; a.K = PL; a.N = H; a.w = e->proj_w;
     a.bias = e->proj_b; a.y = g.kv->h; a.y_ld = H;
@@ -750,8 +761,10 @@ int engine_enqueue_group(ctts_engine* e, EngineGroup& g, cudaStream_t s, int* la
   }
   if (e->cfg_on)  // the same acoustic input feeds the unconditional branch (bin/cutetts.rs:503-509)
     CTTS_CK(cudaMemcpyAsync(g.kv->h + (size_t)B * H, g.kv->h, sizeof(float) * B * H, cudaMemcpyDeviceToDevice, s));
+  if (int rcm = mark(3)) return rcm;
   rc = lm_forward_rows(lm, g.kv, zm * B, -1, 0, z, s, &nl);
   if (rc) return rc;
+  if (int rcm = mark(4)) return rcm;
   if (launches) *launches += nl;
   return CTTS_OK;
 }
@@ -785,6 +798,8 @@ void engine_destroy(ctts_engine* e) {
   }
   if (e->exec) cudaGraphExecDestroy(e->exec);
   if (e->graph) cudaGraphDestroy(e->graph);
+  for (auto& ev : e->pev)
+    if (ev) cudaEventDestroy(ev);
   if (e->h_noise) cudaFreeHost(e->h_noise);
   if (e->h_lat) cudaFreeHost(e->h_lat);
   if (e->h_stop) cudaFreeHost(e->h_stop);
@@ -969,12 +984,21 @@ extern "C" int ctts_engine_step_dev(ctts_engine* e, const float* noise_dev, floa
   const int B = e->cfg.batch, PL = e->dit->cfg.patch * e->dit->cfg.latent;
   if (noise_dev != e->noise)
     CTTS_CK(cudaMemcpyAsync(e->noise, noise_dev, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
-  if (!e->cfg.use_graph || e->steps_done == 0) {
-    // first frame runs eagerly (sets kernel attributes outside any capture)
+  if (!e->cfg.use_graph || e->steps_done == 0 || e->profile) {
+    // first frame runs eagerly (sets kernel attributes outside any capture);
+    // so does every frame of the profiling mode (events between phases)
     int n = 0;
     int rc = engine_enqueue(e, s, &n);
     if (rc) return rc;
-    e->launches = n;
+    if (!e->profile) e->launches = n;
+    if (e->profile && e->groups.size() == 1) {
+      CTTS_CK(cudaEventSynchronize(e->pev[ctts_engine::kPhases]));
+      for (int i = 0; i < ctts_engine::kPhases; i++) {
+        float ms = 0.0f;
+        CTTS_CK(cudaEventElapsedTime(&ms, e->pev[i], e->pev[i + 1]));
+        e->ptimes[i].push_back(ms);
+      }
+    }
   } else {
     if (!e->exec) {
       CTTS_CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
@@ -1042,4 +1066,65 @@ extern "C" int ctts_debug_inject_wait_fault(int skip, unsigned spin_limit) {
   g_fault_skip.store(skip ? 1 : 0, std::memory_order_relaxed);
   g_fault_spin_limit.store(spin_limit, std::memory_order_relaxed);
   return CTTS_OK;
+}
+
+// ------------------------------------------------------- phase timers
+// Per-frame phase timers of the frame engine: the --profile-steps
+// instrument of bin/cutetts.rs:328-350,466-478 (dit / locenc / lm phases;
+// here stop head, DiT sample, feedback projection, LM step), measured on
+// the device with CUDA events.  While on, frames run eagerly (not as the
+// captured graph) and each step synchronizes its stream.
+
+static const char* kPhaseNames[ctts_engine::kPhases] = {"stop", "dit", "feedback", "lm"};
+
+extern "C" int ctts_engine_set_profile(ctts_engine* e, int on) {
+  CTTS_REQ(e, CTTS_ERR_ARG, "null engine");
+  CTTS_REQ(!on || e->groups.size() == 1, CTTS_ERR_STATE, "phase timers need a single sub-batch group");
+  CTTS_CK(cudaSetDevice(e->lm->device));
+  if (on && !e->pev[0])
+    for (auto& ev : e->pev) CTTS_CK(cudaEventCreate(&ev));
+  for (auto& v : e->ptimes) v.clear();
+  e->profile = on != 0;
+  return CTTS_OK;
+}
+
+// mean / p50 / p99 (milliseconds) of phase `phase` over the profiled frames;
+// *n receives the frame count
+extern "C" int ctts_engine_profile_stats(const ctts_engine* e, int phase, float* mean_p50_p99, int* n) {
+  CTTS_REQ(e && mean_p50_p99 && phase >= 0 && phase < ctts_engine::kPhases, CTTS_ERR_ARG, "bad argument");
+  std::vector<float> v = e->ptimes[phase];
+  if (n) *n = (int)v.size();
+  mean_p50_p99[0] = mean_p50_p99[1] = mean_p50_p99[2] = 0.0f;
+  if (v.empty()) return CTTS_OK;
+  std::sort(v.begin(), v.end());
+  double sum = 0.0;
+  for (float x : v) sum += x;
+  const size_t k = v.size();
+  mean_p50_p99[0] = (float)(sum / (double)k);
+  mean_p50_p99[1] = v[k / 2];
+  mean_p50_p99[2] = v[std::min(k - 1, k * 99 / 100)];
+  return CTTS_OK;
+}
+
+// One line per phase, "name: n=N mean=Xms p50=Yms p99=Zms" (the format of
+// bin/cutetts.rs:338-350 profile_report); returns the bytes written.
+extern "C" int ctts_engine_profile_report(const ctts_engine* e, char* buf, int len) {
+  CTTS_REQ(e && buf && len > 0, CTTS_ERR_ARG, "bad argument");
+  std::string out;
+  for (int i = 0; i < ctts_engine::kPhases; i++) {
+    float st[3];
+    int n = 0;
+    ctts_engine_profile_stats(e, i, st, &n);
+    char line[160];
+    if (n == 0)
+      snprintf(line, sizeof(line), "%s: n/a\n", kPhaseNames[i]);
+    else
+      snprintf(line, sizeof(line), "%s: n=%d mean=%.3fms p50=%.3fms p99=%.3fms\n", kPhaseNames[i], n, st[0], st[1],
+               st[2]);
+    out += line;
+  }
+  const int w = (int)std::min<size_t>(out.size(), (size_t)len - 1);
+  memcpy(buf, out.data(), (size_t)w);
+  buf[w] = 0;
+  return w;
 }

@@ -1,6 +1,7 @@
 // api_vae.cu -- C ABI: the causal VAE decoder (decode.rs / weights.rs /
 // ffi.rs, audio_vae.py:243-292) at generic topology.
 #include <cstdio>
+#include <cstdlib>
 
 #include "api_common.h"
 #include "model.h"
@@ -293,8 +294,39 @@ int vae_read_err(ctts_vae* v) {
 
 namespace {
 
-int vae_enqueue(ctts_vae* v, int B, const float* lat, int T, float* wav, cudaStream_t s) {
+// Per-stage timing of a host decode under CUTETTS_PROFILE=1 (the "[prof]"
+// lines of decode.rs:12-24): CUDA events recorded between the stages,
+// printed to stderr after the decode synchronizes.
+struct VaeProf {
+  std::vector<std::pair<std::string, cudaEvent_t>> marks;
+  int mark(const std::string& name, cudaStream_t s) {
+    cudaEvent_t ev = nullptr;
+    CTTS_CK(cudaEventCreate(&ev));
+    marks.emplace_back(name, ev);
+    CTTS_CK(cudaEventRecord(ev, s));
+    return CTTS_OK;
+  }
+  void report() {
+    for (size_t i = 1; i < marks.size(); i++) {
+      float ms = 0.0f;
+      if (cudaEventElapsedTime(&ms, marks[i - 1].second, marks[i].second) == cudaSuccess)
+        fprintf(stderr, "[prof] %-24s %8.3fms\n", marks[i].first.c_str(), ms);
+    }
+  }
+  ~VaeProf() {
+    for (auto& m : marks) cudaEventDestroy(m.second);
+  }
+};
+
+bool vae_profile_env() {
+  const char* e = getenv("CUTETTS_PROFILE");
+  return e && e[0] == '1' && e[1] == 0;
+}
+
+int vae_enqueue(ctts_vae* v, int B, const float* lat, int T, float* wav, cudaStream_t s, VaeProf* prof = nullptr) {
   const int bf = v->bf16;
+  auto mark = [&](const std::string& name) -> int { return prof ? prof->mark(name, s) : CTTS_OK; };
+  if (int rc = mark("start")) return rc;
   float* h = v->buf[0];
   float* h2 = v->buf[1];
   float* r = v->buf[2];
@@ -312,6 +344,7 @@ int vae_enqueue(ctts_vae* v, int B, const float* lat, int T, float* wav, cudaStr
     use_tc(v, p, v->front_pw_tc);
     CTTS_CK(launch_conv1d(p, s));
   }
+  if (int rc = mark("front conv")) return rc;
   int t = T;
   static const int dils[3] = {1, 3, 9};
   for (auto& st : v->stages) {
@@ -323,6 +356,8 @@ int vae_enqueue(ctts_vae* v, int B, const float* lat, int T, float* wav, cudaStr
     CTTS_CK(launch_conv_transpose(tr, s));
     t *= st.stride;
     std::swap(h, h2);
+    const std::string sn = "stage " + std::to_string(&st - v->stages.data()) + " ";
+    if (int rc = mark(sn + "snake+transpose")) return rc;
     for (int ri = 0; ri < 3; ri++) {
       const VaeRes& R = st.res[ri];
       ConvArgs c7;
@@ -337,6 +372,7 @@ int vae_enqueue(ctts_vae* v, int B, const float* lat, int T, float* wav, cudaStr
       c1.left = 0;
       use_tc(v, c1, R.w1_tc);
       CTTS_CK(launch_conv1d(c1, s));
+      if (int rc = mark(sn + "resunit d" + std::to_string(dils[ri]))) return rc;
     }
   }
   ConvArgs f;
@@ -344,6 +380,7 @@ int vae_enqueue(ctts_vae* v, int B, const float* lat, int T, float* wav, cudaStr
   f.B = B; f.Cin = v->cfg.channels >> v->cfg.n_stages; f.Cout = 1; f.Tin = t; f.Tout = t; f.k = 7;
   f.dil = 1; f.left = 6; f.tanh_out = 1;
   CTTS_CK(launch_conv1d(f, s));
+  if (int rc = mark("final snake+conv+tanh")) return rc;
   return CTTS_OK;
 }
 
@@ -375,8 +412,19 @@ extern "C" int ctts_vae_decode_batch(ctts_vae* v, int batch, const float* latent
     v->io_wav = nw;
   }
   CTTS_CK(cudaMemcpyAsync(v->lat_dev, latent, nl * 4, cudaMemcpyHostToDevice, v->stream));
-  int rc = ctts_vae_decode_batch_dev(v, batch, v->lat_dev, T, v->wav_dev, v->stream);
-  if (rc) return rc;
+  int rc;
+  if (vae_profile_env()) {
+    if (v->slots.missing()) return set_error(CTTS_ERR_STATE, "VAE weights missing: " + v->slots.first_missing());
+    if ((rc = vae_ws_ensure(v, batch, T))) return rc;
+    if ((rc = vae_tc_prepare(v))) return rc;
+    VaeProf prof;
+    if ((rc = vae_enqueue(v, batch, v->lat_dev, T, v->wav_dev, v->stream, &prof))) return rc;
+    CTTS_CK(cudaStreamSynchronize(v->stream));
+    prof.report();
+  } else {
+    rc = ctts_vae_decode_batch_dev(v, batch, v->lat_dev, T, v->wav_dev, v->stream);
+    if (rc) return rc;
+  }
   CTTS_CK(cudaStreamSynchronize(v->stream));
   if ((rc = vae_read_err(v))) return rc;
   CTTS_CK(cudaMemcpy(wav, v->wav_dev, nw * 4, cudaMemcpyDeviceToHost));

@@ -134,6 +134,12 @@ struct ctts_engine {
   cudaGraphExec_t exec = nullptr;
   int steps_done = 0;
   int launches = 0;
+  // per-phase timers (ctts_engine_set_profile): frames run eagerly with CUDA
+  // events between the phases; per-frame device milliseconds per phase
+  static constexpr int kPhases = 4;  // stop head, DiT sample, feedback, LM step
+  bool profile = false;
+  cudaEvent_t pev[kPhases + 1] = {};
+  std::vector<float> ptimes[kPhases];
 };
 
 // VAE decoder (replaces DecoderW, weights.rs:34-44).

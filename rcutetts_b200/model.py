@@ -299,6 +299,29 @@ class FrameEngine(_Handle):
     def launches_per_step(self) -> int:
         return _lib.load().ctts_engine_launches_per_step(self.h)
 
+    # per-frame phase timers (--profile-steps, bin/cutetts.rs:328-350)
+    PHASES = ("stop", "dit", "feedback", "lm")
+
+    def set_profile(self, on: bool) -> None:
+        check(_lib.load().ctts_engine_set_profile(self.h, int(bool(on))))
+
+    def profile_stats(self) -> dict:
+        """{phase: {"n", "mean_ms", "p50_ms", "p99_ms"}} over the profiled frames."""
+        out = {}
+        for i, name in enumerate(self.PHASES):
+            st = (C.c_float * 3)()
+            n = C.c_int()
+            check(_lib.load().ctts_engine_profile_stats(self.h, i, st, C.byref(n)))
+            out[name] = {"n": n.value, "mean_ms": st[0], "p50_ms": st[1], "p99_ms": st[2]}
+        return out
+
+    def profile_report(self) -> str:
+        buf = C.create_string_buffer(1024)
+        n = _lib.load().ctts_engine_profile_report(self.h, buf, 1024)
+        if n < 0:
+            check(n)
+        return buf.value.decode()
+
     @property
     def stream_ptr(self) -> int:
         return _lib.load().ctts_engine_stream(self.h) or 0

@@ -246,3 +246,30 @@ def test_cfg_frames_vs_oracle(dtype):
             fb = orc.linear(x[None], hw["latent_proj.weight"], hw["latent_proj.bias"])
             zc = lm_o.forward(fb, cc)[0].copy()
             zu = lm_o.forward(fb, cu)[0].copy()
+
+
+def test_phase_timers():
+    """Per-frame phase timers (--profile-steps, bin/cutetts.rs:328-350): the
+    profiled frames produce the same latents as graph replay, and every
+    phase collects one positive device time per frame."""
+    lcfg, dcfg = LMConfig(n_layers=2), DiTConfig(n_layers=2)
+    outs = []
+    for profile in (False, True):
+        eng, keep, lw, dw, hw = build(lcfg, dcfg, seed=9, dtype="f32", batch=2, capacity=64)
+        for b in range(2):
+            eng.prefill(b, rnd(90 + b, (6 + b, lcfg.hidden)), rnd(95 + b, (64,)))
+        noise = rnd(99, (5, 2, 64))
+        lat = [eng.step(noise[0])[0]]  # the first frame runs eagerly in both modes
+        if profile:
+            eng.set_profile(True)
+        lat += [eng.step(noise[f])[0] for f in range(1, 5)]
+        outs.append(np.stack(lat))
+        if profile:
+            st = eng.profile_stats()
+            rep = eng.profile_report()
+        del eng
+    assert np.array_equal(outs[0], outs[1])
+    for name in ("stop", "dit", "feedback", "lm"):
+        assert st[name]["n"] == 4, st
+        assert 0.0 < st[name]["p50_ms"] <= st[name]["p99_ms"] + 1e-9
+        assert f"{name}: n=4 mean=" in rep, rep

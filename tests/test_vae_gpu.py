@@ -88,3 +88,18 @@ def test_reference_ffi_with_weight_norm(tmp_path):
     lib.cutetts_vae_free(h)
     ref = orc.VAE(cfg, fused).decode(lat)
     assert rel_err(wav, ref) < 1e-4
+
+
+def test_stage_profile_env(capfd, monkeypatch):
+    """CUTETTS_PROFILE=1 prints one "[prof]" line per decoder stage
+    (decode.rs:12-24) without changing the waveform."""
+    cfg = VAEConfig(channels=128, strides=(4, 2))
+    m, _ = vae(cfg, 8, "bf16")
+    lat = rnd(9, (2, 64, 6))
+    ref = m.decode(lat)
+    monkeypatch.setenv("CUTETTS_PROFILE", "1")
+    got = m.decode(lat)
+    err = capfd.readouterr().err
+    assert np.array_equal(got, ref)
+    for name in ("front conv", "stage 0 snake+transpose", "stage 1 resunit d9", "final snake+conv+tanh"):
+        assert f"[prof] {name}" in err, err
