@@ -436,6 +436,7 @@ def dev_time(fn, n, stream, flush=None):
     for _ in range(n):
         if flush is not None:
             flush.add_(1.0)
+            torch.cuda.synchronize()  # the flush (torch's stream) ends before the timed call starts
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         fn()
