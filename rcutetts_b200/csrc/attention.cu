@@ -879,12 +879,13 @@ cudaError_t launch_attn_loop_g(const AttnArgs& a, cudaStream_t s) {
   CTTS_LK(launch_k(attn_loop_kernel<BF, HD, GM>, dim3(a.nkv, a.batch), dim3(256), smem, s, a));
   return cudaGetLastError();
 }
-// query heads per KV head held in registers: 1, 2 or 4 (G <= 4)
+// query heads per KV head held in registers: 1, 2, 3 or 4 (G <= 4)
 template <bool BF, int HD>
 cudaError_t launch_attn_loop_t(const AttnArgs& a, cudaStream_t s) {
   const int G = a.nq / a.nkv;
   if (G == 1) return launch_attn_loop_g<BF, HD, 1>(a, s);
   if (G == 2) return launch_attn_loop_g<BF, HD, 2>(a, s);
+  if (G == 3) return launch_attn_loop_g<BF, HD, 3>(a, s);  // the benchmark LM: 12 query / 4 KV heads
   return launch_attn_loop_g<BF, HD, 4>(a, s);
 }
 
