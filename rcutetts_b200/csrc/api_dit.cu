@@ -93,11 +93,52 @@ struct DitRun {
   bool consts_cached = false;
 };
 
+// Packs (or, after a weight upload, repacks in place) the cluster loop's
+// weights from the layer tensors.  Synchronous: waits for the device first,
+// so no launch still reads the buffers being rewritten.
+cudaError_t dit_cluster_pack_all(ctts_dit* d, ctts::DitClusterW& W) {
+  std::vector<const void*> q, o, g, dn;
+  std::vector<const float*> n1, n2;
+  for (const DitLayer& L : d->layers) {
+    q.push_back(L.wqkv);
+    o.push_back(L.wo);
+    g.push_back(L.wgu);
+    dn.push_back(L.wd);
+    n1.push_back(L.norm1);
+    n2.push_back(L.norm2);
+  }
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess)
+    e = ctts::dit_cluster_pack(W, d->cfg.n_layers, q.data(), o.data(), g.data(), dn.data(), n1.data(), n2.data());
+  return e;
+}
+
+// Brings the packed weights up to date after an upload, unless `s` is
+// being captured (the repack is synchronous): returns false then, and the
+// run takes the launch chain, which reads the uploaded tensors directly.
+bool dit_cluster_fresh(ctts_dit* d, cudaStream_t s) {
+  if (d->cl_state != 1) return false;
+  if (!d->cl_dirty) return true;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  if (dit_cluster_pack_all(d, *d->cl) != cudaSuccess) {
+    (void)cudaGetLastError();
+    d->cl_state = -1;
+    return false;
+  }
+  d->cl_dirty = false;
+  return true;
+}
+
 // The cluster-resident Euler loop runs when the head has the shapes it is
-// specialised for, the weights are bf16, 16-CTA clusters fit on the GPU
-// and CTTS_DIT_CLUSTER is not 0.  The first call packs the weights
+// specialised for, the weights are bf16, 16-CTA clusters fit on the GPU,
+// CTTS_DIT_CLUSTER is not 0 and no run of it has reported a split-K partial
+// outside the fp16 exchange range.  The first call packs the weights
 // (synchronous; the engine's first frame runs outside graph capture).
-bool dit_cluster_ready(ctts_dit* d, int steps) {
+bool dit_cluster_ready(ctts_dit* d, int steps, cudaStream_t s) {
   using Sh = ctts::DitClusterShape;
   const ctts_dit_config& c = d->cfg;
   if (!d->bf16 || c.hidden != Sh::kH || c.ffn != Sh::kF || c.n_heads != Sh::kNH || c.n_kv_heads != Sh::kNH ||
@@ -109,20 +150,10 @@ bool dit_cluster_ready(ctts_dit* d, int steps) {
     const char* env = getenv("CTTS_DIT_CLUSTER");
     if ((!env || atoi(env) != 0) && ctts::dit_cluster_max_active() > 0) {
       auto* W = new ctts::DitClusterW();
-      std::vector<const void*> q, o, g, dn;
-      std::vector<const float*> n1, n2;
-      for (const DitLayer& L : d->layers) {
-        q.push_back(L.wqkv);
-        o.push_back(L.wo);
-        g.push_back(L.wgu);
-        dn.push_back(L.wd);
-        n1.push_back(L.norm1);
-        n2.push_back(L.norm2);
-      }
-      if (ctts::dit_cluster_pack(*W, c.n_layers, q.data(), o.data(), g.data(), dn.data(), n1.data(),
-                                 n2.data()) == cudaSuccess) {
+      if (dit_cluster_pack_all(d, *W) == cudaSuccess) {
         d->cl = W;
         d->cl_state = 1;
+        d->cl_dirty = false;
       } else {
         (void)cudaGetLastError();
         ctts::dit_cluster_free(*W);
@@ -130,7 +161,7 @@ bool dit_cluster_ready(ctts_dit* d, int steps) {
       }
     }
   }
-  return d->cl_state == 1;
+  return dit_cluster_fresh(d, s);
 }
 
 // Enqueues one DiT sample / predict on stream s with workspace w (sized by
@@ -268,7 +299,7 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
     if (launches) *launches += nl;
     return CTTS_OK;
   }
-  if (r.mode == 0 && r.x_rows == R && dit_cluster_ready(d, r.steps)) {
+  if (r.mode == 0 && r.x_rows == R && dit_cluster_ready(d, r.steps, s)) {
     ctts::DitClusterArgs ca;
     ca.R = R; ca.NL = NL; ca.steps = r.steps; ca.adaln = use_ad ? 1 : 0; ca.eps = c.rms_eps;
     for (int i = 0; i < r.steps; i++) ca.dts[i] = r.dts[i];
@@ -379,12 +410,23 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
   return CTTS_OK;
 }
 
+// A run of the cluster loop reported a split-K partial outside the fp16
+// exchange range (its output is invalid): later runs of this head take the
+// fp32-partial launch chain.
+int dit_cluster_range_error(ctts_dit* d) {
+  d->cl_state = -1;
+  return set_error(CTTS_ERR_RANGE,
+                   "a DiT split-K partial exceeded the fp16 exchange range (or an input was not finite): the "
+                   "run's output is invalid, and this head now runs the fp32-partial launch chain");
+}
+
 // Reads back the workspace's device error flag after a synchronized run;
 // a reported error is cleared, so the next run starts clean.
-int dit_read_err(const DitWs& w) {
+int dit_read_err(ctts_dit* d, const DitWs& w) {
   int err = 0;
   CTTS_CK(cudaMemcpy(&err, w.err, sizeof(int), cudaMemcpyDeviceToHost));
   if (err != 0) CTTS_CK(cudaMemset(w.err, 0, sizeof(int)));
+  if (err == ctts::kDitClusterErrRange) return dit_cluster_range_error(d);
   CTTS_REQ(err == 0, CTTS_ERR_TIMEOUT, "a DiT kernel gave up waiting on its pipeline, grid barrier or exchange words");
   return CTTS_OK;
 }
@@ -518,7 +560,10 @@ extern "C" int ctts_dit_set_tensor(ctts_dit* d, const char* name, const void* ho
                                    const int64_t* shape, int ndim) {
   CTTS_REQ(d, CTTS_ERR_ARG, "null handle");
   CTTS_CK(cudaSetDevice(d->device));
-  return slot_set(d->slots, name, host, dtype, shape, ndim);
+  const int rc = slot_set(d->slots, name, host, dtype, shape, ndim);
+  // the cluster loop's packed copy is rebuilt before its next run
+  if (rc == CTTS_OK && d->cl) d->cl_dirty = true;
+  return rc;
 }
 
 extern "C" int ctts_dit_load(ctts_dit* d, const char* path, const char* prefix) {
@@ -606,15 +651,22 @@ extern "C" int ctts_dit_euler_sample(ctts_dit* d, int batch, const float* x0, co
   if (rc) return rc;
   DitWs& w = d->ws;
   const int PL = d->cfg.patch * d->cfg.latent;
-  if ((rc = copy_in(w.x, x0, (size_t)batch * PL, d->stream))) return rc;
   if ((rc = copy_in(w.z, z, (size_t)batch * d->cfg.cond_dim, d->stream))) return rc;
   if ((rc = copy_in(w.cond, cond, (size_t)batch * PL, d->stream))) return rc;
   if (spk && (rc = copy_in(w.spk, spk, (size_t)batch * d->cfg.spk_dim, d->stream))) return rc;
-  rc = ctts_dit_euler_sample_dev(d, batch, w.x, w.z, w.cond, spk ? w.spk : nullptr, steps, cfg_w, w.x,
-                                 d->stream);
-  if (rc) return rc;
-  CTTS_CK(cudaStreamSynchronize(d->stream));
-  if ((rc = dit_read_err(w))) return rc;
+  for (int attempt = 0;; attempt++) {
+    if ((rc = copy_in(w.x, x0, (size_t)batch * PL, d->stream))) return rc;
+    rc = ctts_dit_euler_sample_dev(d, batch, w.x, w.z, w.cond, spk ? w.spk : nullptr, steps, cfg_w, w.x,
+                                   d->stream);
+    if (rc) return rc;
+    CTTS_CK(cudaStreamSynchronize(d->stream));
+    rc = dit_read_err(d, w);
+    // the cluster loop gave up on the fp16 partials and is now off: the
+    // rerun takes the fp32-partial launch chain
+    if (rc == CTTS_ERR_RANGE && attempt == 0) continue;
+    if (rc) return rc;
+    break;
+  }
   CTTS_CK(cudaMemcpy(x_out, w.x, sizeof(float) * batch * PL, cudaMemcpyDeviceToHost));
   return CTTS_OK;
 }
@@ -642,7 +694,7 @@ extern "C" int ctts_dit_predict(ctts_dit* d, int batch, const float* x, float t,
   rc = dit_enqueue(d, d->ws, r, d->stream, nullptr);
   if (rc) return rc;
   CTTS_CK(cudaStreamSynchronize(d->stream));
-  if ((rc = dit_read_err(w))) return rc;
+  if ((rc = dit_read_err(d, w))) return rc;
   CTTS_CK(cudaMemcpy(v, w.v, sizeof(float) * batch * PL, cudaMemcpyDeviceToHost));
   return CTTS_OK;
 }
@@ -683,7 +735,7 @@ extern "C" int ctts_dit_euler_sample_cfg(ctts_dit* d, int batch, const float* x0
   rc = dit_enqueue(d, d->ws, r, d->stream, nullptr);
   if (rc) return rc;
   CTTS_CK(cudaStreamSynchronize(d->stream));
-  if ((rc = dit_read_err(w))) return rc;
+  if ((rc = dit_read_err(d, w))) return rc;
   CTTS_CK(cudaMemcpy(x_out, w.x, sizeof(float) * batch * PL, cudaMemcpyDeviceToHost));
   return CTTS_OK;
 }
@@ -966,6 +1018,15 @@ extern "C" int ctts_engine_prefill_uncond(ctts_engine* e, int b, const float* x,
   return engine_prefill(e, b, x, T, cond0, true);
 }
 
+// Releases the captured frame graph: the next graph-mode frame captures
+// again (after the DiT head changed path).
+static void engine_drop_graph(ctts_engine* e) {
+  if (e->exec) cudaGraphExecDestroy(e->exec);
+  if (e->graph) cudaGraphDestroy(e->graph);
+  e->exec = nullptr;
+  e->graph = nullptr;
+}
+
 extern "C" int ctts_engine_step_dev(ctts_engine* e, const float* noise_dev, float* latents_dev,
                                     float* stop_dev, void* stream) {
   CTTS_REQ(e && noise_dev, CTTS_ERR_ARG, "null argument");
@@ -1000,6 +1061,11 @@ extern "C" int ctts_engine_step_dev(ctts_engine* e, const float* noise_dev, floa
       }
     }
   } else {
+    // weights uploaded since the last frame: repack the DiT cluster loop's
+    // copy in place before the graph runs or is captured (the graph's
+    // launch reads the same buffers); a failed repack switches the head to
+    // the launch chain, which needs a new capture
+    if (e->dit->cl_state == 1 && e->dit->cl_dirty && !dit_cluster_fresh(e->dit, s)) engine_drop_graph(e);
     if (!e->exec) {
       CTTS_CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
       int n = 0;
@@ -1046,6 +1112,11 @@ extern "C" int ctts_engine_step(ctts_engine* e, const float* noise, float* laten
     if (err != 0) CTTS_CK(cudaMemset(g.kv->err, 0, sizeof(int)));
     if (derr != 0) CTTS_CK(cudaMemset(g.ws->err, 0, sizeof(int)));
     CTTS_REQ(err != 1, CTTS_ERR_RANGE, "device reported a KV position outside capacity");
+    if (derr == ctts::kDitClusterErrRange) {
+      // the next frame is captured again, on the launch chain
+      engine_drop_graph(e);
+      return dit_cluster_range_error(e->dit);
+    }
     CTTS_REQ(err == 0 && derr == 0, CTTS_ERR_TIMEOUT, "a DiT kernel gave up waiting on its pipeline, grid barrier or exchange words");
   }
   memcpy(latents_out, e->h_lat, sizeof(float) * B * PL);

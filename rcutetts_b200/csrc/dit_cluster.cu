@@ -14,15 +14,17 @@
 // activations as A (rows 0..29 valid; the descriptor's 8-row groups beyond
 // the fourth read the following shared memory and land in accumulator
 // lanes that are never read), a weight slice as B streamed by TMA through
-// a 3-slot ring that runs ahead of the activations across layers and steps
+// a 4-slot ring that runs ahead of the activations across layers and steps
 // (the weights do not depend on them), the accumulator in TMEM:
 //  * QKV and gate/up are split over N: CTA c computes 96 QKV columns (half
 //    of head c/2) and 192 gate/up columns (SwiGLU columns [96c, 96c+96))
 //    from the all-gathered normed operand (K = 512);
 //  * o-proj and down are split over K: CTA c multiplies its own 32
 //    attention dims / 96 SwiGLU columns by all 512 output rows (N = 2 x 256
-//    MMAs), and the fp32 partials are reduce-scattered: each owner sums the
-//    16 partials of its 32 columns in CTA order (deterministic).
+//    MMAs), and the partials (accumulated in fp32, exchanged as fp16: an
+//    11-bit significand, 4x finer than the bf16 operands of these GEMMs)
+//    are reduce-scattered: each owner sums the 16 partials of its 32
+//    columns in fp32, in CTA order (deterministic).
 //
 // Exchange.  A operands are stored K-major with the 64-byte swizzle as one
 // contiguous slice per CTA ([32-column atom][row group][8 rows x 64 B]), so
@@ -31,10 +33,9 @@
 // (cp.async.bulk shared::cta -> shared::cluster), completing on the peer's
 // mbarrier; row statistics, attention score partials, out_proj partials and
 // the new latent go the same way from small staging buffers.  The
-// reduce-scatter stages the partials in two rounds of eight owners in the
-// all-gathered operand area (idle from the end of its GEMM until the peers'
-// next push, which needs these partials first) and pushes one 4 KB block
-// per owner.  Every mbarrier is armed with its phase's byte count
+// reduce-scatter stages the partials of all 16 owners in the all-gathered
+// operand area (idle from the end of its GEMM until the peers' next push,
+// which needs these partials first) and pushes one 2 KB block per owner.  Every mbarrier is armed with its phase's byte count
 // (arrive.expect_tx) by its waiter right after the previous phase
 // completed, which by the stage order is before any peer can push for that
 // phase; consecutive stages never share an mbarrier.  Stages that feed a
@@ -56,6 +57,8 @@
 #include <cstdio>
 #include <mutex>
 #include <vector>
+
+#include <cuda_fp16.h>
 
 #include "dit_cluster.cuh"
 #include "launch_state.h"
@@ -83,10 +86,10 @@ constexpr uint32_t kXA = 0;                              // norm outputs, K = 51
 constexpr uint32_t kATT = kXA + kC * kSlice;             // own attention slice (o-proj A, K = 32)
 constexpr uint32_t kSWI = kATT + kSlice;                 // own SwiGLU slice (down A, K = 96)
 constexpr uint32_t kPART = kSWI + kActSlice;             // split-K partials from every CTA (o-proj / down)
-constexpr uint32_t kPartBytes = 32 * kOwn * 4;           // 4 KB: [8 column chunks][32 rows][4 floats]
+constexpr uint32_t kPartBytes = 32 * kOwn * 2;           // 2 KB: [4 column chunks][32 rows][8 halves]
 constexpr uint32_t kRING = kPART + kC * kPartBytes;      // weight ring
 constexpr uint32_t kSlotBytes = kGuN * 128;              // 24 KB: one 192-row, 64-wide K block
-constexpr int kSlots = 3;
+constexpr int kSlots = 4;
 constexpr uint32_t kF32 = kRING + kSlots * kSlotBytes;
 constexpr int kTmemCols = 512;                           // split-K accumulators span all 512 outputs
 // split-K weight blocks (o-proj, down): 256 output rows x 32 K columns,
@@ -143,7 +146,7 @@ __host__ __device__ inline Lay lay(int NL) {
 constexpr int bFULL = 0, bEMPTY = kSlots, bMMA = 2 * kSlots, bFIN = bMMA + 1, bA = bFIN + 1, bB = bA + 2,
               bAD = bB + 2, bRS = bAD + 1;
 static_assert(bRS < 16, "16 mbarrier slots");
-static_assert(8 * kPartBytes <= kPART - kXA, "reduce-scatter staging fits below the partials");
+static_assert(kC * kPartBytes <= kATT - kXA, "reduce-scatter staging fits the all-gathered operand area");
 
 // Optional stage timeline (build with -DCTTS_DIT_TRACE): CTA 0 records
 // (event, %globaltimer) pairs of its compute warp (row 0) and MMA thread.
@@ -290,7 +293,9 @@ __global__ void __launch_bounds__(kNT, 1)
                        const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmD,
                        const DitClusterArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // aligned by an offset into the shared array (not through an integer
+  // cast), so the compiler keeps every access through it in shared space
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int NL = a.NL, steps = a.steps;
   const Lay LY = lay(NL);
   const uint32_t sb = smem_u32(smem);
@@ -618,8 +623,10 @@ __global__ void __launch_bounds__(kNT, 1)
     // the per-warp row partials pss[cw][r] summed in warp order -> every
     // CTA's ssr[c] (warp 0), then all warps see the 16 CTAs' sums
     auto ss_combine_push = [&]() {
+      if (cw == 0) DTRACE(0, 13);
       cbar();
       if (cw == 0) {
+        DTRACE(0, 14);
         F[oSSO + r] = ((pss[r] + pss[32 + r]) + pss[64 + r]) + pss[96 + r];
         pushB(kF32 + oSSO * 4, kF32 + (oSSR + c * 32) * 4, 128, kC, false);
         waitB();
@@ -660,49 +667,52 @@ __global__ void __launch_bounds__(kNT, 1)
     // them.  Warp 0 waits for all 16 x 32 arrivals of the phase.
     uint32_t rsph = 0;
     auto rs_exchange = [&]() {
-      // two rounds of eight owners; warp cw stages owners 8*round + 2cw,
-      // 8*round + 2cw + 1 into the staging area (the all-gathered norm
-      // operand, idle until the peers' next push, which needs these
-      // partials first), then warp 0 pushes one 4 KB block per owner
+      // warp cw stages owners 4cw..4cw+3 as fp16 (11-bit significand, 4x
+      // finer than the bf16 operands of these GEMMs) into the staging area
+      // (the all-gathered norm operand, idle until the peers' next push,
+      // which needs these partials first); warp 0 pushes one 2 KB block per
+      // owner
 #pragma unroll 1
-      for (int round = 0; round < 2; round++) {
-#pragma unroll 1
-        for (int k2 = 0; k2 < 2; k2++) {
-          const int slot = 2 * cw + k2;
-          uint32_t v[32];
-          tmem_ld32_nowait(tmem + 32u * (uint32_t)(8 * round + slot), v);
-          tmem_wait();
-          uint8_t* stg = smem + kXA + (uint32_t)slot * kPartBytes + (uint32_t)r * 16u;
+      for (int dd = 0; dd < 4; dd++) {
+        const int d = 4 * cw + dd;
+        uint32_t v[32];
+        tmem_ld32_nowait(tmem + 32u * (uint32_t)d, v);
+        tmem_wait();
+        uint8_t* stg = smem + kXA + (uint32_t)d * kPartBytes + (uint32_t)r * 16u;
 #pragma unroll
-          for (int q = 0; q < 8; q++) st_u4(stg + q * 512, v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        cbar();
-        if (cw == 0) {
-          if (lane < 8) {
-            const uint32_t d = (uint32_t)(8 * round + lane);
-            push(sb + kPART + (uint32_t)c * kPartBytes, sb + kXA + (uint32_t)lane * kPartBytes, kPartBytes,
-                 bar(bRS), d);
-            // the staging is rewritten next round (and by this CTA's next
-            // norm operand): wait until the copy has read it
-            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        for (int q = 0; q < 4; q++) {
+          uint32_t h[4];
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const __half2 p2 = __floats2half2_rn(__uint_as_float(v[8 * q + 2 * e]), __uint_as_float(v[8 * q + 2 * e + 1]));
+            h[e] = *reinterpret_cast<const uint32_t*>(&p2);
           }
-          __syncwarp();
-          if (round == 0) DTRACE(0, 9);
+          st_u4(stg + q * 512, h[0], h[1], h[2], h[3]);
         }
-        cbar();
       }
-      if (cw == 0) DTRACE(0, 10);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      cbar();
       if (cw == 0) {
+        if (lane < kC) {
+          push(sb + kPART + (uint32_t)c * kPartBytes, sb + kXA + (uint32_t)lane * kPartBytes, kPartBytes, bar(bRS),
+               (uint32_t)lane);
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        __syncwarp();
+        DTRACE(0, 9);
         const uint32_t rb = bar(bRS);
         if (ok && !wait_cluster(rb, rsph & 1, abort)) ok = false;
         if (lane == 0) arm(rb, kC * kPartBytes);  // the next exchange's bytes
+        // the staging is rewritten by this CTA's next norm operand: every
+        // copy has read it (the peers' own writes to it come after they
+        // received these blocks)
+        if (lane < kC) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
         __syncwarp();
         DTRACE(0, 11);
       }
       rsph++;
       sync_ok();
+      if (cw == 0) DTRACE(0, 12);
     };
     // gated residual update of own columns [8cw, 8cw+8) from the 16 split-K
     // partials (summed in CTA order: deterministic), and their sum of
@@ -710,16 +720,29 @@ __global__ void __launch_bounds__(kNT, 1)
     auto resid_rs = [&](const float* adb, int gate_k) {
       float p = 0.0f;
       if (rv) {
-        const float* part = reinterpret_cast<const float*>(smem + kPART);
-        float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
+        // own columns [8cw, 8cw+8) are chunk cw of every source's block
+        const uint8_t* part = smem + kPART + (uint32_t)cw * 512u + (uint32_t)r * 16u;
+        float acc[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) acc[e] = 0.0f;
 #pragma unroll 4
         for (int q2 = 0; q2 < kC; q2++) {
-          const float4 a0 = *reinterpret_cast<const float4*>(part + q2 * (kPartBytes / 4) + (2 * cw) * 128 + r * 4);
-          const float4 a1 = *reinterpret_cast<const float4*>(part + q2 * (kPartBytes / 4) + (2 * cw + 1) * 128 + r * 4);
-          s0.x += a0.x; s0.y += a0.y; s0.z += a0.z; s0.w += a0.w;
-          s1.x += a1.x; s1.y += a1.y; s1.z += a1.z; s1.w += a1.w;
+          const uint4 w4 = *reinterpret_cast<const uint4*>(part + q2 * kPartBytes);
+          const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+            acc[2 * e] += f2.x;
+            acc[2 * e + 1] += f2.y;
+          }
         }
-        const float acc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        if (cw == 0) DTRACE(0, 15);
+        // a partial outside the fp16 range (or a non-finite input) leaves a
+        // non-finite sum: flagged for the host, which reruns in fp32
+        bool fin = true;
+#pragma unroll
+        for (int e = 0; e < 8; e++) fin = fin && fabsf(acc[e]) <= 3.40282347e38f;
+        if (!fin && a.err) atomicCAS(a.err, 0, kDitClusterErrRange);
         const float* gt = adb + u * kAdLd + gate_k * kOwn;
 #pragma unroll
         for (int e = 0; e < 8; e++) {
@@ -729,6 +752,7 @@ __global__ void __launch_bounds__(kNT, 1)
           seq[r * kSeqLd + j] = nv;
           p = fmaf(nv, nv, p);
         }
+        if (cw == 0) DTRACE(0, 16);
       } else {
 #pragma unroll
         for (int e = 0; e < 8; e++) p = fmaf(seq[r * kSeqLd + 8 * cw + e], seq[r * kSeqLd + 8 * cw + e], p);
@@ -1119,11 +1143,15 @@ cudaError_t dit_cluster_pack(DitClusterW& W, int NL, const void* const* wqkv, co
   const size_t nq = (size_t)NL * kC * kQkvN * kH, no = (size_t)NL * kH * kH;
   const size_t ng = (size_t)NL * kC * kGuN * kH, nd = (size_t)NL * kH * kF;
   cudaError_t e;
-  if ((e = cudaMalloc(&W.qkv, nq * 2)) != cudaSuccess) return e;
-  if ((e = cudaMalloc(&W.o, no * 2)) != cudaSuccess) return e;
-  if ((e = cudaMalloc(&W.gu, ng * 2)) != cudaSuccess) return e;
-  if ((e = cudaMalloc(&W.dn, nd * 2)) != cudaSuccess) return e;
-  if ((e = cudaMalloc(&W.norms, sizeof(float) * NL * 2 * kH)) != cudaSuccess) return e;
+  // a repack (new weights uploaded) reuses the buffers: the addresses, and
+  // the tensor maps built from them, stay what earlier launches captured
+  if (!W.qkv) {
+    if ((e = cudaMalloc(&W.qkv, nq * 2)) != cudaSuccess) return e;
+    if ((e = cudaMalloc(&W.o, no * 2)) != cudaSuccess) return e;
+    if ((e = cudaMalloc(&W.gu, ng * 2)) != cudaSuccess) return e;
+    if ((e = cudaMalloc(&W.dn, nd * 2)) != cudaSuccess) return e;
+    if ((e = cudaMalloc(&W.norms, sizeof(float) * NL * 2 * kH)) != cudaSuccess) return e;
+  }
   // row maps
   std::vector<int> iq(kC * kQkvN), ig(kC * kGuN), iid(kH);
   for (int c = 0; c < kC; c++) {

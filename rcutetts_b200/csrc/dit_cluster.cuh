@@ -59,13 +59,20 @@ struct DitClusterArgs {
   int* err = nullptr;
 };
 
+// Device error word value when an owner's sum of split-K partials (each
+// exchanged as fp16) is not finite: a partial outside the fp16 range or a
+// non-finite input.  The run's output is invalid; the caller reruns on the
+// fp32-partial launch chain.
+constexpr int kDitClusterErrRange = 5;
+
 // Dynamic shared memory of one CTA for NL layers.
 size_t dit_cluster_smem(int NL);
 // Clusters of kC CTAs that fit on this GPU at once (0: the kernel cannot run).
 int dit_cluster_max_active();
 // Packs the layer weights (wqkv [1536,512] as stored, wgu [3072,512] in
 // 64-row gate/up interleave, wo [512,512], wd [512,1536]) into W and builds
-// its tensor maps.  Synchronous.
+// its tensor maps.  Allocates W's buffers on the first call and repacks into
+// the same buffers afterwards.  Synchronous.
 cudaError_t dit_cluster_pack(DitClusterW& W, int NL, const void* const* wqkv, const void* const* wo,
                              const void* const* wgu, const void* const* wd, const float* const* norm1,
                              const float* const* norm2);

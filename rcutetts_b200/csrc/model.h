@@ -94,9 +94,12 @@ struct ctts_dit {
   float* inv_freq = nullptr;
   DitWs ws;
   // cluster-resident Euler loop (dit_cluster.cu): packed weights, state
-  // 0 = not tried, 1 = ready, -1 = shapes/device unsupported or disabled
+  // 0 = not tried, 1 = ready, -1 = shapes/device unsupported, disabled, or
+  // off after a split-K partial left the fp16 exchange range; dirty = a
+  // tensor was uploaded since the weights were packed
   ctts::DitClusterW* cl = nullptr;
   int cl_state = 0;
+  bool cl_dirty = false;
 };
 
 struct EngineGroup {

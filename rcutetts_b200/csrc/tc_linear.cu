@@ -137,8 +137,10 @@ __global__ void __launch_bounds__(128)
                      const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   TC_TRACE(0);
-  // 1024-byte alignment for the swizzled tiles
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte alignment for the swizzled tiles, by an offset into the
+  // shared array (not through an integer cast), so the compiler keeps every
+  // access through it in shared space
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int S = a.stages;
   const int bbytes = a.MT * 128;
   const size_t stage_bytes = 16384 + (size_t)bbytes;

@@ -123,7 +123,9 @@ CTTS_DEV uint32_t pack_bf2(float lo, float hi) {
 
 __global__ void __launch_bounds__(kVThreads, 1) vae_tc_conv_kernel(const VaeTcArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  // aligned by an offset into the shared array (not through an integer
+  // cast), so the compiler keeps every access through it in shared space
+  uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
   const int halo = (a.k - 1) * a.dil;
   const VLay L = vlay(a.k, halo);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)kVStages * L.stage);

@@ -161,3 +161,57 @@ def test_grid_euler_loop_alternating_batches(monkeypatch):
         out = m.euler_sample(x0[:B], z[:B], c[:B], z[:B], 10)
         for b in range(B):
             assert rel_err(out[b], refs[b]) < 1e-4, (B, b)
+
+
+def _scaled_down(cfg, seed, scale):
+    from rcutetts_b200 import synth
+
+    w = synth.dit_weights(cfg, seed=seed)
+    for i in range(cfg.n_layers):
+        w[f"decoder.layers.{i}.mlp.down_proj.weight"] = w[f"decoder.layers.{i}.mlp.down_proj.weight"] * np.float32(scale)
+    return w
+
+
+def test_cluster_fp16_partial_range_falls_back(monkeypatch):
+    """Down-projection weights scaled by 1e8: the split-K partials of the
+    cluster loop (exchanged as fp16) leave the fp16 range.  The loop flags
+    it, the call reruns on the fp32-partial launch chain (bit for bit what
+    a CTTS_DIT_CLUSTER=0 handle gives) and later calls of the handle stay on
+    the chain."""
+    from rcutetts_b200.model import DitW
+
+    cfg = DiTConfig()
+    w = _scaled_down(cfg, 16, 1e8)
+    B = 12
+    x0, z, c = rnd(31, (B, 64)), rnd(32, (B, 768)), rnd(33, (B, 64))
+    monkeypatch.setenv("CTTS_DIT_CLUSTER", "0")
+    ref = DitW(cfg, "bf16").set_weights(w).euler_sample(x0, z, c, z, 10)
+    monkeypatch.setenv("CTTS_DIT_CLUSTER", "1")
+    m = DitW(cfg, "bf16").set_weights(w)
+    out = m.euler_sample(x0, z, c, z, 10)
+    assert np.isfinite(out).all()
+    assert np.array_equal(out, ref)
+    assert np.array_equal(m.euler_sample(x0, z, c, z, 10), ref)
+    o = orc.DiT(cfg, bf16_weights(w))
+    for b in (0, 11):
+        assert rel_err(out[b], o.euler_sample(x0[b], z[b], c[b], z[b], 10)) < 2e-3, b
+
+
+def test_cluster_repacks_after_upload():
+    """New weights uploaded to a handle whose cluster loop already ran (and
+    packed its copy) are what the next run uses: the result equals a fresh
+    handle's, bit for bit."""
+    from rcutetts_b200 import synth
+    from rcutetts_b200.model import DitW
+
+    cfg = DiTConfig()
+    w1, w2 = synth.dit_weights(cfg, seed=16), synth.dit_weights(cfg, seed=17)
+    B = 12
+    x0, z, c = rnd(34, (B, 64)), rnd(35, (B, 768)), rnd(36, (B, 64))
+    m = DitW(cfg, "bf16").set_weights(w1)
+    first = m.euler_sample(x0, z, c, z, 10)
+    m.set_weights(w2)
+    again = m.euler_sample(x0, z, c, z, 10)
+    fresh = DitW(cfg, "bf16").set_weights(w2).euler_sample(x0, z, c, z, 10)
+    assert not np.array_equal(first, again)
+    assert np.array_equal(again, fresh)

@@ -273,3 +273,45 @@ def test_phase_timers():
         assert st[name]["n"] == 4, st
         assert 0.0 < st[name]["p50_ms"] <= st[name]["p99_ms"] + 1e-9
         assert f"{name}: n=4 mean=" in rep, rep
+
+
+def test_dit_fp16_range_error_moves_head_to_launch_chain(monkeypatch):
+    """A DiT head whose split-K partials leave the fp16 exchange range of
+    the cluster loop (down projections scaled by 1e8): the frame step
+    reports CTTS_ERR_RANGE (its latents, and the LM state they fed, are
+    invalid); an engine built again on the same head runs the fp32-partial
+    launch chain, bit for bit like a CTTS_DIT_CLUSTER=0 head."""
+    from rcutetts_b200._lib import ERR_RANGE, CttsError
+    from rcutetts_b200.model import DitW, FrameEngine, QwenW
+
+    lcfg, dcfg = LMConfig(n_layers=1), DiTConfig()
+    B = 16
+    lw = synth.lm_weights(lcfg, seed=11, with_embed=True)
+    dw = synth.dit_weights(dcfg, seed=21)
+    for i in range(dcfg.n_layers):
+        k = f"decoder.layers.{i}.mlp.down_proj.weight"
+        dw[k] = dw[k] * np.float32(1e8)
+    hw = synth.frame_weights(lcfg.hidden, dcfg.latent, seed=31)
+    lm = QwenW(lcfg, "bf16").set_weights(lw)
+
+    def engine(dit):
+        eng = FrameEngine(lm, dit, hw, batch=B, capacity=32, euler_steps=10)
+        for b in range(B):
+            eng.prefill(b, rnd(300 + b, (4 + b % 5, lcfg.hidden)), rnd(400 + b, (64,)))
+        return eng
+
+    noise = rnd(500, (3, B, 64))
+    dit = DitW(dcfg, "bf16").set_weights(dw)
+    eng = engine(dit)
+    with pytest.raises(CttsError) as e:
+        eng.step(noise[0])
+    assert e.value.code == ERR_RANGE
+    del eng
+    eng = engine(dit)
+    lat = np.stack([eng.step(noise[f])[0] for f in range(3)])
+    monkeypatch.setenv("CTTS_DIT_CLUSTER", "0")
+    eng0 = engine(DitW(dcfg, "bf16").set_weights(dw))
+    lat0 = np.stack([eng0.step(noise[f])[0] for f in range(3)])
+    assert np.isfinite(lat).all()
+    assert np.array_equal(lat, lat0)
+    assert eng.launches_per_step == eng0.launches_per_step
