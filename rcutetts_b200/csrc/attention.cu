@@ -6,11 +6,15 @@
 //   query QK-Norm + RoPE, KV append of the new row, GQA attention over each
 //   utterance's ragged cache (qwen.rs:323-362), split over the sequence so
 //   a batch of one still fills the GPU, splits merged by the last CTA.
+// attn_split: the batched decode step: each (utterance, KV head) is split
+//   over the keys into a thread-block cluster of CTAs whose partial softmax
+//   states merge over distributed shared memory (one wave for the batch).
 // attn_prefill: causal attention of T new rows against the cache
 //   (qwen.rs:273-297).
 #include "common.cuh"
-#include "launch_state.h"
 #include "kernels.cuh"
+#include "launch_state.h"
+#include "tc_ptx.cuh"
 
 namespace ctts {
 
@@ -714,6 +718,337 @@ __global__ void __launch_bounds__(256) attn_loop_kernel(const AttnArgs a) {
   ATT_TRACE(9);
 }
 
+// Batched decode step split over the keys: grid (nkv, batch, S), clusters
+// of the S splits of one (KV head, utterance).  Split s walks keys
+// [s*per, min(n, (s+1)*per)) (per = ceil(n / S)) in 64-key stages through a
+// two-stage ring of bulk copies issued before the wait on the previous
+// kernel (the cached rows were written by earlier frames); every split
+// rotates the G queries, the split holding the new position also norms,
+// rotates and appends the new key/value row.  Each warp keeps an online
+// softmax over its 16 keys of every stage; the warp states merge in warp
+// order into the CTA's state (max, sum, unnormalised output), and after a
+// cluster barrier CTA s finishes output elements [s*ceil(G*HD/S), ...) from
+// the S states read over distributed shared memory in split order
+// (deterministic).  Every CTA passes both cluster barriers, also with an
+// out-of-range position (which only raises the error flag).
+template <bool BF, int HD, int GM>
+__global__ void __launch_bounds__(128) attn_split_kernel(const AttnArgs a) {
+  constexpr int ES = BF ? 2 : 4;
+  constexpr int ROWB = HD * ES;
+  constexpr int NC = ROWB / 16;
+  constexpr int VPC = 16 / ES;
+  constexpr int PER = HD / 32;
+  constexpr int C = 64;              // keys per stage
+  constexpr int NT = 128;
+  constexpr int NW = NT / 32;
+  constexpr int KPW = C / NW;        // keys of a stage per warp
+  constexpr int KPI = 32 / NC;       // keys per warp pass: NC lanes per key, one 16-byte chunk each
+  constexpr int NIT = KPW / KPI;     // passes over the warp's keys
+  constexpr int DPL = HD / 32;       // V dims per lane in the P.V pass
+  static_assert(NC == 8 || NC == 16, "one key row is 8 or 16 chunks of 16 bytes");
+  extern __shared__ __align__(128) uint8_t kv_smem[];  // [2][K|V][C][ROWB]
+  __shared__ __align__(16) float qs[GM][HD];
+  __shared__ __align__(16) uint8_t newrow[2][ROWB];  // new K, V row in the cache type
+  __shared__ float wpart[NW][GM][HD + 2];            // per-warp [m, l, acc[HD]]
+  __shared__ __align__(16) float cst[GM][HD + 2];    // this split's [m, l, o[HD]] (read by the cluster)
+  __shared__ __align__(8) uint64_t bars[2];
+
+  const int kh = blockIdx.x, b = blockIdx.y, split = blockIdx.z, S = gridDim.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nq = a.nq, nkv = a.nkv, G = nq / nkv;
+  const int pos = a.pos[b];
+  const bool bad = pos < 0 || pos >= a.cap;
+  const int n = bad ? 0 : pos + 1;
+  const int per = (n + S - 1) / S;
+  const int k0 = min(n, split * per), k1 = min(n, k0 + per);
+  const int nst = (k1 - k0 + C - 1) / C;
+  const bool owns_new = !bad && pos >= k0 && pos < k1;
+  const size_t row0 = ((size_t)b * nkv + kh) * a.cap;
+  auto tile = [&](int buf, int kv) { return kv_smem + ((size_t)(buf * 2 + kv) * C) * ROWB; };
+  auto bar_a = [&](int i) { return static_cast<uint32_t>(__cvta_generic_to_shared(&bars[i])); };
+  // rows of stage st already in the cache (the new row at `pos` is not)
+  auto cached = [&](int st) { return max(0, min(min(k0 + st * C + C, k1), pos) - (k0 + st * C)); };
+  auto issue = [&](int st) {  // thread 0
+    const int rows = cached(st);
+    if (rows <= 0) return;
+    const int buf = st & 1;
+    const uint32_t bytes = (uint32_t)rows * ROWB;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_a(buf)), "r"(2 * bytes)
+                 : "memory");
+#pragma unroll
+    for (int kv = 0; kv < 2; kv++) {
+      const uint8_t* src =
+          reinterpret_cast<const uint8_t*>(kv ? a.vcache : a.kcache) + (row0 + (size_t)k0 + (size_t)st * C) * ROWB;
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       static_cast<uint32_t>(__cvta_generic_to_shared(tile(buf, kv)))),
+                   "l"(src), "r"(bytes), "r"(bar_a(buf))
+                   : "memory");
+    }
+  };
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_a(0)));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_a(1)));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid == 0 && !bad) {  // cached rows were written frames ago
+    issue(0);
+    if (nst > 1) issue(1);
+  }
+  grid_dep_enter();
+  if (bad && kh == 0 && split == 0 && tid == 0 && a.err) atomicExch(a.err, 1);
+
+  // ---- queries (every split) and the new key/value row (its owner): one
+  // warp per job
+  const int width = (nq + 2 * nkv) * HD;
+  const float* src_row = a.qkv + (size_t)b * width;
+  const int jobs = bad ? 0 : (owns_new ? G + 2 : G);
+  for (int job = warp; job < jobs; job += NW) {
+    const bool is_q = job < G, is_v = job == G + 1;
+    const int head = is_q ? kh * G + job : (is_v ? nq + nkv + kh : nq + kh);
+    const float* src = src_row + head * HD;
+    float v[PER];
+#pragma unroll
+    for (int j = 0; j < PER; j++) v[j] = src[lane + 32 * j];
+    if (!is_v) {
+      const float* gn = is_q ? a.qn : a.kn;
+      if (gn) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < PER; j++) ss = fmaf(v[j], v[j], ss);
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+#pragma unroll
+        for (int j = 0; j < PER; j++) v[j] = v[j] * inv * gn[lane + 32 * j];
+      }
+#pragma unroll
+      for (int j = 0; j < PER / 2; j++) {
+        const int i = lane + 32 * j;
+        float sn, cs;
+        sincosf((float)pos * a.inv_freq[i], &sn, &cs);
+        const float x1 = v[j], x2 = v[j + PER / 2];
+        v[j] = x1 * cs - x2 * sn;
+        v[j + PER / 2] = x1 * sn + x2 * cs;
+      }
+    }
+    if (is_q) {
+#pragma unroll
+      for (int j = 0; j < PER; j++) qs[job][lane + 32 * j] = v[j];
+    } else {
+      void* cache = is_v ? a.vcache : a.kcache;
+      uint8_t* nr = newrow[is_v ? 1 : 0];
+#pragma unroll
+      for (int j = 0; j < PER; j++) {
+        const int d = lane + 32 * j;
+        if constexpr (BF) {
+          const uint16_t hb = f2bf(v[j]);
+          reinterpret_cast<uint16_t*>(cache)[(row0 + pos) * HD + d] = hb;
+          reinterpret_cast<uint16_t*>(nr)[d] = hb;
+        } else {
+          reinterpret_cast<float*>(cache)[(row0 + pos) * HD + d] = v[j];
+          reinterpret_cast<float*>(nr)[d] = v[j];
+        }
+      }
+    }
+  }
+  __syncthreads();  // queries and the new row are set
+  const float scale = 1.0f / sqrtf((float)HD);
+  // Lane = (key of the pass, 16-byte chunk ch): the lane keeps its chunk of
+  // every query head in registers, so a key row is read once, conflict-free,
+  // and the chunk partial dot products meet by xor-shuffles inside each
+  // key's lane group.
+  const int ch = lane % NC, ksub = lane / NC;
+  float qr[GM][VPC];
+#pragma unroll
+  for (int g = 0; g < GM; g++)
+#pragma unroll
+    for (int e = 0; e < VPC; e++) qr[g][e] = g < G ? qs[g][ch * VPC + e] : 0.0f;
+  float m_w[GM], l_w[GM], acc[GM][DPL];
+#pragma unroll
+  for (int g = 0; g < GM; g++) {
+    m_w[g] = -INFINITY;
+    l_w[g] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < DPL; e++) acc[g][e] = 0.0f;
+  }
+  bool ok = true;
+  for (int st = 0; st < nst; st++) {
+    const int buf = st & 1;
+    const int kst = k0 + st * C;  // first key of the stage
+    const int rows = min(C, k1 - kst);
+    if (cached(st) > 0) {
+      bool done = false;
+      for (uint32_t it = 0; it < kWaitLimit && !done; ++it) {
+        uint32_t d;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(d)
+            : "r"(bar_a(buf)), "r"((uint32_t)((st >> 1) & 1))
+            : "memory");
+        done = d != 0;
+      }
+      if (!done) ok = false;
+    }
+    uint8_t* Ks = tile(buf, 0);
+    uint8_t* Vs = tile(buf, 1);
+    if (owns_new && pos >= kst && pos < kst + C && tid < 2 * NC) {  // the new row into its stage
+      const int kv = tid / NC, cch = tid % NC;
+      reinterpret_cast<uint4*>((kv ? Vs : Ks) + (size_t)(pos - kst) * ROWB)[cch] =
+          reinterpret_cast<const uint4*>(newrow[kv])[cch];
+    }
+    __syncthreads();
+    const int kbase = warp * KPW;
+    float sc[NIT][GM];
+#pragma unroll
+    for (int it = 0; it < NIT; it++) {
+      const int key = kbase + it * KPI + ksub;
+      const bool valid = key < rows;
+      float kv[VPC];
+      if (valid) {
+        const uint4 t = reinterpret_cast<const uint4*>(Ks + (size_t)key * ROWB)[ch];
+        if constexpr (BF) {
+          kv[0] = bf_lo(t.x); kv[1] = bf_hi(t.x); kv[2] = bf_lo(t.y); kv[3] = bf_hi(t.y);
+          kv[4] = bf_lo(t.z); kv[5] = bf_hi(t.z); kv[6] = bf_lo(t.w); kv[7] = bf_hi(t.w);
+        } else {
+          kv[0] = __uint_as_float(t.x); kv[1] = __uint_as_float(t.y);
+          kv[2] = __uint_as_float(t.z); kv[3] = __uint_as_float(t.w);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < VPC; e++) kv[e] = 0.0f;
+      }
+#pragma unroll
+      for (int g = 0; g < GM; g++) {
+        float d = 0.0f;
+#pragma unroll
+        for (int e = 0; e < VPC; e++) d = fmaf(qr[g][e], kv[e], d);
+#pragma unroll
+        for (int o = 1; o < NC; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        sc[it][g] = valid ? d * scale : -INFINITY;
+      }
+    }
+    float pr[NIT][GM];
+#pragma unroll
+    for (int g = 0; g < GM; g++) {
+      float mx = sc[0][g];
+#pragma unroll
+      for (int it = 1; it < NIT; it++) mx = fmaxf(mx, sc[it][g]);
+#pragma unroll
+      for (int o = NC; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mn = fmaxf(m_w[g], mx);
+      const float f = m_w[g] == -INFINITY ? 0.0f : expf(m_w[g] - mn);
+      float sum = 0.0f;
+#pragma unroll
+      for (int it = 0; it < NIT; it++) {
+        pr[it][g] = sc[it][g] == -INFINITY ? 0.0f : expf(sc[it][g] - mn);
+        sum += pr[it][g];
+      }
+#pragma unroll
+      for (int o = NC; o < 32; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      l_w[g] = l_w[g] * f + sum;
+#pragma unroll
+      for (int e = 0; e < DPL; e++) acc[g][e] *= f;
+      m_w[g] = mn;
+    }
+    const int nk = min(KPW, rows - kbase);
+#pragma unroll
+    for (int kk = 0; kk < KPW; kk++) {
+      if (kk >= nk) break;
+      const uint8_t* vrow = Vs + (size_t)(kbase + kk) * ROWB;
+      float v[DPL];
+      if constexpr (BF) {
+        if constexpr (DPL == 2) {
+          const uint32_t t = reinterpret_cast<const uint32_t*>(vrow)[lane];
+          v[0] = bf_lo(t);
+          v[1] = bf_hi(t);
+        } else {
+          const uint2 t = reinterpret_cast<const uint2*>(vrow)[lane];
+          v[0] = bf_lo(t.x); v[1] = bf_hi(t.x); v[2] = bf_lo(t.y); v[3] = bf_hi(t.y);
+        }
+      } else {
+        if constexpr (DPL == 2) {
+          const float2 t = reinterpret_cast<const float2*>(vrow)[lane];
+          v[0] = t.x;
+          v[1] = t.y;
+        } else {
+          const float4 t = reinterpret_cast<const float4*>(vrow)[lane];
+          v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < GM; g++) {
+        const float pk = __shfl_sync(0xffffffffu, pr[kk / KPI][g], (kk % KPI) * NC);
+#pragma unroll
+        for (int e = 0; e < DPL; e++) acc[g][e] = fmaf(pk, v[e], acc[g][e]);
+      }
+    }
+    __syncthreads();  // stage buffer consumed by every warp
+    if (tid == 0 && st + 2 < nst) issue(st + 2);
+  }
+  if (!ok && a.err && tid == 0) atomicExch(a.err, 3);
+  // ---- this split's state: the warp states merged in warp order
+#pragma unroll
+  for (int g = 0; g < GM; g++) {
+    if (g >= G) break;
+    if (lane == 0) {
+      wpart[warp][g][0] = m_w[g];
+      wpart[warp][g][1] = l_w[g];
+    }
+#pragma unroll
+    for (int e = 0; e < DPL; e++) wpart[warp][g][2 + lane * DPL + e] = acc[g][e];
+  }
+  __syncthreads();
+  for (int i = tid; i < G * (HD + 1); i += NT) {
+    const int g = i / (HD + 1), d = i % (HD + 1);  // d == HD: the row's max and sum
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; w++) M = fmaxf(M, wpart[w][g][0]);
+    float acc_o = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; w++) {
+      const float mw = wpart[w][g][0];
+      const float f = mw == -INFINITY ? 0.0f : expf(mw - M);
+      acc_o = fmaf(d == HD ? wpart[w][g][1] : wpart[w][g][2 + d], f, acc_o);
+    }
+    if (d == HD) {
+      cst[g][0] = M;
+      cst[g][1] = acc_o;
+    } else {
+      cst[g][2 + d] = acc_o;
+    }
+  }
+  // every split's state is written
+  cluster_sync();
+  if (!bad) {
+    const int tot = G * HD, share = (tot + S - 1) / S;
+    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(&cst[0][0]));
+    for (int i = split * share + tid; i < min(tot, split * share + share); i += NT) {
+      const int g = i / HD, d = i % HD, h = kh * G + g;
+      const uint32_t row = base + (uint32_t)(g * (HD + 2)) * 4u;
+      float M = -INFINITY;
+      for (int r = 0; r < S; r++) M = fmaxf(M, __uint_as_float(ld_dsmem_u32(mapa_shared(row, (uint32_t)r))));
+      float L = 0.0f, o = 0.0f;
+      for (int r = 0; r < S; r++) {
+        const uint32_t rr = mapa_shared(row, (uint32_t)r);
+        const float mr = __uint_as_float(ld_dsmem_u32(rr));
+        const float f = mr == -INFINITY ? 0.0f : expf(mr - M);
+        L = fmaf(__uint_as_float(ld_dsmem_u32(rr + 4u)), f, L);
+        o = fmaf(__uint_as_float(ld_dsmem_u32(rr + (uint32_t)(2 + d) * 4u)), f, o);
+      }
+      o = o / L;
+      const size_t oi = (size_t)b * nq * HD + (size_t)h * HD + d;
+      if (a.out_b)
+        a.out_b[oi] = f2bf(o);
+      else
+        a.out[oi] = o;
+    }
+  }
+  // no CTA leaves while a peer may still read its state
+  cluster_sync();
+}
+
 // causal prefill attention: grid (T, nq), 128 threads, dyn smem n floats
 template <bool BF>
 __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnArgs a) {
@@ -879,14 +1214,64 @@ cudaError_t launch_attn_loop_g(const AttnArgs& a, cudaStream_t s) {
   CTTS_LK(launch_k(attn_loop_kernel<BF, HD, GM>, dim3(a.nkv, a.batch), dim3(256), smem, s, a));
   return cudaGetLastError();
 }
+// Splits per (utterance, KV head) for the split kernel: the most (up to 8,
+// a portable cluster) that keep the whole grid resident in one wave.
+template <bool BF, int HD, int GM>
+int attn_splits(const AttnArgs& a, size_t smem) {
+  static PerDeviceInt per_sm;  // resident CTAs per SM of this instance
+  int nb = per_sm.get([&] {
+    int v = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, attn_split_kernel<BF, HD, GM>, 128, smem) != cudaSuccess) {
+      (void)cudaGetLastError();
+      v = 0;
+    }
+    return v;
+  });
+  const int pairs = a.batch * a.nkv;
+  const int slots = nb * device_sms();
+  return std::max(1, std::min(8, pairs > 0 ? slots / pairs : 1));
+}
+
+template <bool BF, int HD, int GM>
+cudaError_t launch_attn_split_g(const AttnArgs& a, int S, size_t smem, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.nkv, a.batch, S);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = S;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  CTTS_LK(cudaLaunchKernelEx(&cfg, attn_split_kernel<BF, HD, GM>, a));
+  return cudaGetLastError();
+}
+
+// Batched decode: the key-split cluster kernel when it takes at least two
+// splits, else one CTA per (utterance, KV head) walking all its keys.
+template <bool BF, int HD, int GM>
+cudaError_t launch_attn_batched_g(const AttnArgs& a, cudaStream_t s) {
+  const size_t smem = (size_t)2 * 2 * 64 * HD * (BF ? 2 : 4);
+  static SmemOptIn opt;
+  if (cudaError_t e = opt.ensure((const void*)attn_split_kernel<BF, HD, GM>, smem)) return e;
+  const int S = attn_splits<BF, HD, GM>(a, smem);
+  if (S >= 2) return launch_attn_split_g<BF, HD, GM>(a, S, smem, s);
+  return launch_attn_loop_g<BF, HD, GM>(a, s);
+}
+
 // query heads per KV head held in registers: 1, 2, 3 or 4 (G <= 4)
 template <bool BF, int HD>
 cudaError_t launch_attn_loop_t(const AttnArgs& a, cudaStream_t s) {
   const int G = a.nq / a.nkv;
-  if (G == 1) return launch_attn_loop_g<BF, HD, 1>(a, s);
-  if (G == 2) return launch_attn_loop_g<BF, HD, 2>(a, s);
-  if (G == 3) return launch_attn_loop_g<BF, HD, 3>(a, s);  // the benchmark LM: 12 query / 4 KV heads
-  return launch_attn_loop_g<BF, HD, 4>(a, s);
+  if (G == 1) return launch_attn_batched_g<BF, HD, 1>(a, s);
+  if (G == 2) return launch_attn_batched_g<BF, HD, 2>(a, s);
+  if (G == 3) return launch_attn_batched_g<BF, HD, 3>(a, s);  // the benchmark LM: 12 query / 4 KV heads
+  return launch_attn_batched_g<BF, HD, 4>(a, s);
 }
 
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t s) {

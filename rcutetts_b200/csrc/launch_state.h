@@ -79,6 +79,26 @@ class DeviceAttrCache {
   std::atomic<int> val_[kMaxDevices] = {};
 };
 
+// An integer computed once per device by the caller's function (an
+// occupancy figure, for instance) and cached; concurrent first calls may
+// both compute it, with the same result.
+class PerDeviceInt {
+ public:
+  template <class F>
+  int get(F&& fn) {
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return fn();
+    int v = val_[dev].load(std::memory_order_acquire);
+    if (v) return v - 1;
+    const int x = fn();
+    val_[dev].store(x + 1, std::memory_order_release);
+    return x;
+  }
+
+ private:
+  std::atomic<int> val_[kMaxDevices] = {};
+};
+
 // SM count of the current device (cached per device).
 inline int device_sms() {
   static DeviceAttrCache c(cudaDevAttrMultiProcessorCount);

@@ -35,24 +35,21 @@ namespace ctts {
 namespace {
 
 // Optional phase timeline (build with -DCTTS_TC_TRACE): thread 0 of the
-// first CTA of the grid records (event, %globaltimer) pairs per launch.
+// first CTA of the grid records %globaltimer per event and launch.
 #ifdef CTTS_TC_TRACE
-// Consecutive launches overlap (programmatic dependent launch), so slots are
-// taken atomically and each event carries its launch number: (launch << 8) | ev.
-__device__ long long g_tc_trace[4096];
-__device__ int g_tc_trace_n;
+// Consecutive launches overlap (programmatic dependent launch): the launch
+// number is taken atomically once, at event 0 (after its timestamp); later
+// events store into their own slot without waiting on memory.
+constexpr int kTcTraceLaunches = 256, kTcTraceEvents = 16;
+__device__ long long g_tc_trace[kTcTraceLaunches * kTcTraceEvents];
 __device__ int g_tc_launch;
 CTTS_DEV void tc_trace(int ev) {
   if (blockIdx.x != 0 || blockIdx.y != 0 || threadIdx.x != 0) return;
   __shared__ int lid;
-  if (ev == 0) lid = atomicAdd(&g_tc_launch, 1);
   long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  const int n = atomicAdd(&g_tc_trace_n, 1);
-  if (n < 2047) {
-    g_tc_trace[2 * n] = ((long long)lid << 8) | ev;
-    g_tc_trace[2 * n + 1] = t;
-  }
+  if (ev == 0) lid = atomicAdd(&g_tc_launch, 1);
+  if (lid < kTcTraceLaunches && ev < kTcTraceEvents) g_tc_trace[lid * kTcTraceEvents + ev] = t;
 }
 #define TC_TRACE(ev) tc_trace(ev)
 #else
@@ -91,10 +88,19 @@ CTTS_DEV float4 epi_gains(const TcArgs& a, int col, int n) {
                      n > 3 ? a.g2[col + 3] : 0.f);
 }
 // 1/rms of activation row m from the folded-norm partial sums (1 without).
+// The first 16 partials are requested together (one round trip to L2 for
+// the usual widths) and summed in tile order like the rest.
 CTTS_DEV float epi_rinv(const TcArgs& a, int m) {
   if (!a.rs_ssp) return 1.0f;
+  constexpr int kBatch = 16;
+  float v[kBatch];
+#pragma unroll
+  for (int t = 0; t < kBatch; t++) v[t] = t < a.rs_nt ? a.rs_ssp[(long)t * a.rs_ld + m] : 0.0f;
   float ss = 0.0f;
-  for (int t = 0; t < a.rs_nt; t++) ss += a.rs_ssp[(long)t * a.rs_ld + m];
+#pragma unroll
+  for (int t = 0; t < kBatch; t++)
+    if (t < a.rs_nt) ss += v[t];
+  for (int t = kBatch; t < a.rs_nt; t++) ss += a.rs_ssp[(long)t * a.rs_ld + m];
   return 1.0f / sqrtf(ss / a.rs_k + a.rs_eps);
 }
 CTTS_DEV void epi_store(const TcArgs& a, int m, int col, int n, const float* val, const Epi4& e, const float4& g,
@@ -336,6 +342,7 @@ __global__ void __launch_bounds__(128)
           }
         }
       }
+      if (u0 == tid) TC_TRACE(8);
       // epilogue: fetch every unit's gate/residual (prefetched in round
       // one), then compute and store
       Epi4 ep[kU];
@@ -522,13 +529,15 @@ cudaError_t launch_tc_linear(const TcCall& c, cudaStream_t s) {
 }  // namespace ctts
 
 #ifdef CTTS_TC_TRACE
-// Copies the recorded timeline out and resets it.
+// Copies the recorded timeline out ([launch][event] timestamps, 0 = not
+// recorded; *n = launches) and resets it.
 extern "C" __attribute__((visibility("default"))) int ctts_tc_trace(long long* out, int* n) {
-  cudaMemcpyFromSymbol(n, ctts::g_tc_trace_n, sizeof(int));
-  if (*n > 2047) *n = 2047;
-  cudaMemcpyFromSymbol(out, ctts::g_tc_trace, sizeof(long long) * 4096);
+  cudaMemcpyFromSymbol(n, ctts::g_tc_launch, sizeof(int));
+  if (*n > ctts::kTcTraceLaunches) *n = ctts::kTcTraceLaunches;
+  cudaMemcpyFromSymbol(out, ctts::g_tc_trace, sizeof(ctts::g_tc_trace));
+  static long long zeros[ctts::kTcTraceLaunches * ctts::kTcTraceEvents] = {};
+  cudaMemcpyToSymbol(ctts::g_tc_trace, zeros, sizeof(zeros));
   int z = 0;
-  cudaMemcpyToSymbol(ctts::g_tc_launch, &z, sizeof(int));
-  return cudaMemcpyToSymbol(ctts::g_tc_trace_n, &z, sizeof(int)) == cudaSuccess ? 0 : -2;
+  return cudaMemcpyToSymbol(ctts::g_tc_launch, &z, sizeof(int)) == cudaSuccess ? 0 : -2;
 }
 #endif
