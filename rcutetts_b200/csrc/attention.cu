@@ -1049,6 +1049,346 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const AttnArgs a) {
   cluster_sync();
 }
 
+// ---- tensor-core form of the split decode step (bf16 cache)
+//
+// Same split, cluster merge and new-row handling as attn_split_kernel; the
+// two products run on mma.sync.m16n8k16 (bf16 in, fp32 accumulate): scores
+// S[q][key] = Q . K^T with the G query heads as the rows of the A operand
+// (rows G..15 zero) and 8-key column tiles read by ldmatrix from the K
+// stage, then O += P . V with P as the A operand and V read transposed.
+// Q and P enter as bf16 pairs hi + lo (hi = bf16(x), lo = bf16(x - hi)), so
+// the products keep about 16 significant bits, close to the fp32 dot
+// products of the CUDA-core form.  Stages of 64 keys arrive by TMA tensor
+// copies with the 128-byte swizzle ([box of 64 dims][64 keys][128 B]), so
+// the ldmatrix rows of a warp fall in distinct banks.  Each warp owns 16
+// keys of a stage and an online softmax over its keys; the merges follow
+// attn_split_kernel.
+CTTS_DEV uint32_t pack_bf2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// x = hi + lo with both parts in bf16 (hi rounded to nearest), packed pairs
+CTTS_DEV void split_bf2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  hi = pack_bf2(x0, x1);
+  lo = pack_bf2(x0 - bf_lo(hi), x1 - bf_hi(hi));
+}
+CTTS_DEV void mma_bf16_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+CTTS_DEV void ldsm_x4(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+CTTS_DEV void ldsm_x4_t(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                       const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+  constexpr int ROWB = HD * 2;
+  constexpr int NB = HD / 64;          // 128-byte boxes per key row
+  constexpr int C = 64;                // keys per stage
+  constexpr int NT = 128, NW = NT / 32;
+  constexpr int KS = HD / 16;          // k-steps of the score product
+  constexpr int NO = HD / 8;           // 8-dim column tiles of the output
+  constexpr uint32_t kBox = C * 128;   // one box: 64 keys x 128 bytes
+  constexpr uint32_t kTile = NB * kBox;  // one K or V stage
+  constexpr int RW = 8;                // query rows held (G <= 8)
+  extern __shared__ __align__(1024) uint8_t dyn_smem[];  // [2][K|V][NB][C][128] swizzled
+  __shared__ __align__(16) float qs[RW][HD];
+  __shared__ __align__(16) uint8_t newrow[2][ROWB];
+  __shared__ __align__(16) float cst[RW][HD + 2];
+  __shared__ __align__(8) uint64_t bars[2];
+  uint8_t* kv_smem = dyn_smem + ((1024u - (static_cast<uint32_t>(__cvta_generic_to_shared(dyn_smem)) & 1023u)) & 1023u);
+  const uint32_t kv_base = static_cast<uint32_t>(__cvta_generic_to_shared(kv_smem));
+
+  const int kh = blockIdx.x, b = blockIdx.y, split = blockIdx.z, S = gridDim.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nq = a.nq, nkv = a.nkv, G = nq / nkv;
+  const int pos = a.pos[b];
+  const bool bad = pos < 0 || pos >= a.cap;
+  const int n = bad ? 0 : pos + 1;
+  const int per = (n + S - 1) / S;
+  const int k0 = min(n, split * per), k1 = min(n, k0 + per);
+  const int nst = (k1 - k0 + C - 1) / C;
+  const bool owns_new = !bad && pos >= k0 && pos < k1;
+  const size_t row0 = ((size_t)b * nkv + kh) * a.cap;
+  auto tile = [&](int buf, int kv) { return kv_base + (uint32_t)(buf * 2 + kv) * kTile; };
+  auto bar_a = [&](int i) { return static_cast<uint32_t>(__cvta_generic_to_shared(&bars[i])); };
+  // byte offset of (key, 16-byte chunk) in a stage tile: 128-byte swizzle
+  auto sw = [](int key, int chunk) {
+    return (uint32_t)(chunk >> 3) * kBox + (uint32_t)key * 128u + (uint32_t)(((chunk & 7) ^ (key & 7)) << 4);
+  };
+  auto issue = [&](int st) {  // thread 0: the stage's K and V boxes (rows past the cache read as stale or zero)
+    const int buf = st & 1;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_a(buf)), "r"(2u * kTile)
+                 : "memory");
+    const int y = (int)(row0 + (size_t)k0 + (size_t)st * C);
+#pragma unroll
+    for (int kv = 0; kv < 2; kv++)
+#pragma unroll
+      for (int bx = 0; bx < NB; bx++)
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+            "[%4];" ::"r"(tile(buf, kv) + (uint32_t)bx * kBox),
+            "l"(reinterpret_cast<uint64_t>(kv ? &tmV : &tmK)), "r"(bx * 64), "r"(y), "r"(bar_a(buf))
+            : "memory");
+  };
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_a(0)));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_a(1)));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid == 0 && !bad) {  // cached rows were written frames ago
+    if (nst > 0) issue(0);
+    if (nst > 1) issue(1);
+  }
+  grid_dep_enter();
+  if (bad && kh == 0 && split == 0 && tid == 0 && a.err) atomicExch(a.err, 1);
+
+  // ---- queries (every split) and the new key/value row (its owner)
+  constexpr int PER = HD / 32;
+  const int width = (nq + 2 * nkv) * HD;
+  const float* src_row = a.qkv + (size_t)b * width;
+  for (int i = tid; i < RW * HD; i += NT) qs[i / HD][i % HD] = 0.0f;
+  __syncthreads();
+  const int jobs = bad ? 0 : (owns_new ? G + 2 : G);
+  for (int job = warp; job < jobs; job += NW) {
+    const bool is_q = job < G, is_v = job == G + 1;
+    const int head = is_q ? kh * G + job : (is_v ? nq + nkv + kh : nq + kh);
+    const float* src = src_row + head * HD;
+    float v[PER];
+#pragma unroll
+    for (int j = 0; j < PER; j++) v[j] = src[lane + 32 * j];
+    if (!is_v) {
+      const float* gn = is_q ? a.qn : a.kn;
+      if (gn) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < PER; j++) ss = fmaf(v[j], v[j], ss);
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+#pragma unroll
+        for (int j = 0; j < PER; j++) v[j] = v[j] * inv * gn[lane + 32 * j];
+      }
+#pragma unroll
+      for (int j = 0; j < PER / 2; j++) {
+        const int i = lane + 32 * j;
+        float sn, cs;
+        sincosf((float)pos * a.inv_freq[i], &sn, &cs);
+        const float x1 = v[j], x2 = v[j + PER / 2];
+        v[j] = x1 * cs - x2 * sn;
+        v[j + PER / 2] = x1 * sn + x2 * cs;
+      }
+    }
+    if (is_q) {
+#pragma unroll
+      for (int j = 0; j < PER; j++) qs[job][lane + 32 * j] = v[j];
+    } else {
+      void* cache = is_v ? a.vcache : a.kcache;
+      uint16_t* nr = reinterpret_cast<uint16_t*>(newrow[is_v ? 1 : 0]);
+#pragma unroll
+      for (int j = 0; j < PER; j++) {
+        const int d = lane + 32 * j;
+        const uint16_t hb = f2bf(v[j]);
+        reinterpret_cast<uint16_t*>(cache)[(row0 + pos) * HD + d] = hb;
+        nr[d] = hb;
+      }
+    }
+  }
+  __syncthreads();  // queries and the new row are set
+
+  // A fragments of Q (rows 0..7 = query heads, rows 8..15 zero), hi and lo
+  const int gq = lane >> 2, tq = lane & 3;
+  uint32_t qa_hi[KS][2], qa_lo[KS][2];
+#pragma unroll
+  for (int ks = 0; ks < KS; ks++) {
+    const float* qrow = qs[gq] + ks * 16 + 2 * tq;
+    split_bf2(qrow[0], qrow[1], qa_hi[ks][0], qa_lo[ks][0]);
+    split_bf2(qrow[8], qrow[9], qa_hi[ks][1], qa_lo[ks][1]);
+  }
+  const float scale = 1.0f / sqrtf((float)HD);
+  float m_w = -INFINITY, l_w = 0.0f;  // row gq of this warp's keys
+  float o[NO][4];
+#pragma unroll
+  for (int t = 0; t < NO; t++) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
+  const int kbase = warp * 16;
+  bool ok = true;
+  for (int st = 0; st < nst; st++) {
+    const int buf = st & 1;
+    const int kst = k0 + st * C;
+    const int rows = min(C, k1 - kst);
+    {
+      bool done = false;
+      for (uint32_t it = 0; it < kWaitLimit && !done; ++it) {
+        uint32_t d;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(d)
+            : "r"(bar_a(buf)), "r"((uint32_t)((st >> 1) & 1))
+            : "memory");
+        done = d != 0;
+      }
+      if (!done) ok = false;
+    }
+    if (owns_new && pos >= kst && pos < kst + C && tid < 2 * (ROWB / 16)) {  // the new row into its stage
+      const int kv = tid / (ROWB / 16), cch = tid % (ROWB / 16);
+      *reinterpret_cast<uint4*>(kv_smem + (tile(buf, kv) - kv_base) + sw(pos - kst, cch)) =
+          reinterpret_cast<const uint4*>(newrow[kv])[cch];
+    }
+    // value rows past the split's keys (stale cache rows or the next
+    // split's) enter P.V with weight 0: make them finite zeros
+    for (int i = tid; i < (C - rows) * (ROWB / 16); i += NT) {
+      const int r = rows + i / (ROWB / 16), cch = i % (ROWB / 16);
+      *reinterpret_cast<uint4*>(kv_smem + (tile(buf, 1) - kv_base) + sw(r, cch)) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    __syncthreads();
+    // scores of the warp's 16 keys: two 8-key column tiles
+    float s[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+    const uint32_t kt = tile(buf, 0), vt = tile(buf, 1);
+#pragma unroll
+    for (int ks = 0; ks < KS; ks++) {
+      // matrices: (keys 0-7, dims lo), (keys 0-7, dims hi), (keys 8-15, lo), (keys 8-15, hi)
+      const int mi = lane >> 3, key = kbase + 8 * (mi >> 1) + (lane & 7);
+      uint32_t kb[4];
+      ldsm_x4(kt + sw(key, 2 * ks + (mi & 1)), kb);
+      const uint32_t ah[4] = {qa_hi[ks][0], 0u, qa_hi[ks][1], 0u};
+      const uint32_t al[4] = {qa_lo[ks][0], 0u, qa_lo[ks][1], 0u};
+      mma_bf16_16816(s[0], ah, kb[0], kb[1]);
+      mma_bf16_16816(s[0], al, kb[0], kb[1]);
+      mma_bf16_16816(s[1], ah, kb[2], kb[3]);
+      mma_bf16_16816(s[1], al, kb[2], kb[3]);
+    }
+    // online softmax of row gq over the warp's keys kbase + 8j + 2tq + e
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 2; j++)
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const int key = kbase + 8 * j + 2 * tq + e;
+        s[j][e] = key < rows ? s[j][e] * scale : -INFINITY;
+        mx = fmaxf(mx, s[j][e]);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mn = fmaxf(m_w, mx);
+    const float f = m_w == -INFINITY ? 0.0f : expf(m_w - mn);
+    float p[2][2], sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 2; j++)
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        p[j][e] = s[j][e] == -INFINITY ? 0.0f : expf(s[j][e] - mn);
+        sum += p[j][e];
+      }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    l_w = l_w * f + sum;
+    m_w = mn;
+#pragma unroll
+    for (int t = 0; t < NO; t++) {
+      o[t][0] *= f;
+      o[t][1] *= f;
+    }
+    // P as the A operand (rows 8..15 zero), hi and lo
+    uint32_t ph[4] = {0u, 0u, 0u, 0u}, pl[4] = {0u, 0u, 0u, 0u};
+    split_bf2(p[0][0], p[0][1], ph[0], pl[0]);
+    split_bf2(p[1][0], p[1][1], ph[2], pl[2]);
+#pragma unroll
+    for (int t = 0; t < NO; t += 2) {
+      // matrices: (keys 0-7, dims 8t..), (keys 8-15, 8t..), (keys 0-7, 8t+8..), (keys 8-15, 8t+8..)
+      const int mi = lane >> 3, key = kbase + 8 * (mi & 1) + (lane & 7);
+      uint32_t vb[4];
+      ldsm_x4_t(vt + sw(key, t + (mi >> 1)), vb);
+      mma_bf16_16816(o[t], ph, vb[0], vb[1]);
+      mma_bf16_16816(o[t], pl, vb[0], vb[1]);
+      mma_bf16_16816(o[t + 1], ph, vb[2], vb[3]);
+      mma_bf16_16816(o[t + 1], pl, vb[2], vb[3]);
+    }
+    __syncthreads();  // stage buffer consumed by every warp
+    if (tid == 0 && st + 2 < nst) issue(st + 2);
+  }
+  if (!ok && a.err && tid == 0) atomicExch(a.err, 3);
+  // ---- this split's state: the warp states merged in warp order (the
+  // per-warp states reuse the stage area: every copy into it was waited on
+  // and every warp passed the last stage's barrier)
+  float (*wpart)[RW][HD + 2] = reinterpret_cast<float (*)[RW][HD + 2]>(kv_smem);
+  static_assert(NW * RW * (HD + 2) * 4 <= 4 * kTile, "warp states fit the stage area");
+  if (gq < G) {
+    if (tq == 0) {
+      wpart[warp][gq][0] = m_w;
+      wpart[warp][gq][1] = l_w;
+    }
+#pragma unroll
+    for (int t = 0; t < NO; t++) {
+      wpart[warp][gq][2 + 8 * t + 2 * tq] = o[t][0];
+      wpart[warp][gq][2 + 8 * t + 2 * tq + 1] = o[t][1];
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < G * (HD + 1); i += NT) {
+    const int g = i / (HD + 1), d = i % (HD + 1);  // d == HD: the row's max and sum
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; w++) M = fmaxf(M, wpart[w][g][0]);
+    float acc_o = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; w++) {
+      const float mw = wpart[w][g][0];
+      const float fw = mw == -INFINITY ? 0.0f : expf(mw - M);
+      acc_o = fmaf(d == HD ? wpart[w][g][1] : wpart[w][g][2 + d], fw, acc_o);
+    }
+    if (d == HD) {
+      cst[g][0] = M;
+      cst[g][1] = acc_o;
+    } else {
+      cst[g][2 + d] = acc_o;
+    }
+  }
+  // every split's state is written
+  cluster_sync();
+  if (!bad) {
+    const int tot = G * HD, share = (tot + S - 1) / S;
+    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(&cst[0][0]));
+    for (int i = split * share + tid; i < min(tot, split * share + share); i += NT) {
+      const int g = i / HD, d = i % HD, h = kh * G + g;
+      const uint32_t row = base + (uint32_t)(g * (HD + 2)) * 4u;
+      float M = -INFINITY;
+      for (int r = 0; r < S; r++) M = fmaxf(M, __uint_as_float(ld_dsmem_u32(mapa_shared(row, (uint32_t)r))));
+      float L = 0.0f, ov = 0.0f;
+      for (int r = 0; r < S; r++) {
+        const uint32_t rr = mapa_shared(row, (uint32_t)r);
+        const float mr = __uint_as_float(ld_dsmem_u32(rr));
+        const float fr = mr == -INFINITY ? 0.0f : expf(mr - M);
+        L = fmaf(__uint_as_float(ld_dsmem_u32(rr + 4u)), fr, L);
+        ov = fmaf(__uint_as_float(ld_dsmem_u32(rr + (uint32_t)(2 + d) * 4u)), fr, ov);
+      }
+      ov = ov / L;
+      const size_t oi = (size_t)b * nq * HD + (size_t)h * HD + d;
+      if (a.out_b)
+        a.out_b[oi] = f2bf(ov);
+      else
+        a.out[oi] = ov;
+    }
+  }
+  // no CTA leaves while a peer may still read its state
+  cluster_sync();
+}
+
 // causal prefill attention: grid (T, nq), 128 threads, dyn smem n floats
 template <bool BF>
 __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnArgs a) {
@@ -1252,6 +1592,48 @@ cudaError_t launch_attn_split_g(const AttnArgs& a, int S, size_t smem, cudaStrea
   return cudaGetLastError();
 }
 
+// Tensor-core decode step (bf16 cache, head_dim 64 or 128, G <= 8): the
+// splits per (utterance, KV head) keep the grid in one wave; tensor maps
+// over this layer's K and V caches ([batch*nkv*cap, hd], 64-key boxes).
+template <int HD>
+cudaError_t launch_attn_mma(const AttnArgs& a, cudaStream_t s) {
+  const size_t smem = (size_t)2 * 2 * (HD / 64) * 64 * 128 + 1024;
+  static SmemOptIn opt;
+  if (cudaError_t e = opt.ensure((const void*)attn_mma_kernel<HD>, smem)) return e;
+  static PerDeviceInt per_sm;
+  const int nb = per_sm.get([&] {
+    int v = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, attn_mma_kernel<HD>, 128, smem) != cudaSuccess) {
+      (void)cudaGetLastError();
+      v = 0;
+    }
+    return v;
+  });
+  const int pairs = a.batch * a.nkv;
+  const int S = std::max(1, std::min(8, pairs > 0 ? nb * device_sms() / pairs : 1));
+  if (!encode_fn()) return cudaErrorNotSupported;
+  const int rows = a.batch * a.nkv * a.cap;
+  CUtensorMap tmK, tmV;
+  if (!make_map(&tmK, a.kcache, rows, HD, 64) || !make_map(&tmV, a.vcache, rows, HD, 64))
+    return cudaErrorInvalidPitchValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.nkv, a.batch, S);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = S;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  CTTS_LK(cudaLaunchKernelEx(&cfg, attn_mma_kernel<HD>, tmK, tmV, a));
+  return cudaGetLastError();
+}
+
 // Batched decode: the key-split cluster kernel when it takes at least two
 // splits, else one CTA per (utterance, KV head) walking all its keys.
 template <bool BF, int HD, int GM>
@@ -1279,6 +1661,8 @@ cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t s) {
   if (G > kMaxG || a.nq % a.nkv != 0 || (a.hd != 64 && a.hd != 128) || a.chunk <= 0 || a.chunk > 128 ||
       a.chunk % 16 != 0 || a.nsplit * a.chunk < a.cap || a.rows != a.batch || !a.cnt)
     return cudaErrorInvalidValue;
+  // bf16 cache: the tensor-core step (any batch; splits fill the GPU)
+  if (a.kv_bf16 && G <= 8) return a.hd == 64 ? launch_attn_mma<64>(a, s) : launch_attn_mma<128>(a, s);
   // enough (utterance, kv head) pairs to fill the GPU: one CTA per pair
   // walking all its keys; otherwise split the keys over CTAs
   if (a.batch * a.nkv >= 128 && (a.kv_bf16 || a.hd == 64) && G <= 4) {
