@@ -60,18 +60,47 @@ def peaks():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons while running."""
+    """SM clocks and throttle reasons sampled while the timed region runs:
+    NVML every ~2 ms from a host thread, with one sample taken before the
+    region starts (the timed region of a short run lasts tens of ms);
+    nvidia-smi -lms 200 when NVML is missing.  Reads only."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, index: int):
         self.index = index
-        self.rows = []
+        self.rows = []  # (sm MHz, max sm MHz, [reason names])
         self.proc = None
+        self.nv = None
+        self.halt = threading.Event()
+
+    def _nvml_handle(self, nv):
+        try:  # the CUDA device's UUID names the same board for NVML
+            import torch
+            u = str(torch.cuda.get_device_properties(self.index).uuid)
+            return nv.nvmlDeviceGetHandleByUUID(u if u.startswith("GPU-") else "GPU-" + u)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.index)
 
     def start(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.h = self._nvml_handle(nv)
+            self.nv = nv
+            self.bits = [getattr(nv, "nvmlClocksEventReason" + n, 0) for n in
+                         ("HwSlowdown", "HwThermalSlowdown", "SwThermalSlowdown", "SwPowerCap")]
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            t0 = time.time()
+            while not self.rows and self.t.is_alive() and time.time() - t0 < 2.0:
+                time.sleep(0.0005)
+            return self
+        except Exception:
+            self.nv = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
@@ -82,30 +111,45 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def _poll(self):
+        nv = self.nv
+        while not self.halt.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                mx = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                return
+            self.rows.append((float(sm), float(mx), [n for n, b in zip(self.NAMES, self.bits) if b and rs & b]))
+            time.sleep(0.002)
+
     def _read(self):
         for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
+            r = [c.strip() for c in line.split(",")]
+            if len(r) >= 9 and r[1].replace(".", "").isdigit() and r[2].replace(".", "").isdigit():
+                self.rows.append((float(r[1]), float(r[2]),
+                                  [n for n, v in zip(self.NAMES, r[5:9]) if v.strip().lower() == "active"]))
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.t.join(timeout=2)
-        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = set()
-        for r in self.rows:
-            if len(r) >= 9:
-                for n, v in zip(names, r[5:9]):
-                    if v.strip().lower() == "active":
-                        reasons.add(n)
+        if self.nv is not None:
+            self.halt.set()
+            self.t.join(timeout=2)
+            src = "nvml"
+        elif self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=2)
+            src = "nvidia-smi"
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml and nvidia-smi unavailable"], "samples": 0}
+        sm = [r[0] for r in self.rows]
+        mx = [r[1] for r in self.rows]
+        reasons = sorted({n for r in self.rows for n in r[2]})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": reasons, "samples": len(sm), "source": src}
 
 
 # ----------------------------------------------------------------- workload

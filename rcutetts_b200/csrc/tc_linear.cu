@@ -254,20 +254,33 @@ __global__ void __launch_bounds__(128)
     ec = sw ? tile * 64 + c : n0 + c;
     en = u < nunits ? (sw ? 4 : max(0, min(4, a.N - (n0 + c)))) : 0;
   };
-  Epi4 pre_ep[kU];
-  float pre_rinv[kU];
-  float4 pre_g[kU];
+  // the operands of round r + 1 are requested at the start of round r
+  auto fetch_round = [&](int u0, Epi4* ep, float* rinv, float4* g) {
 #pragma unroll
-  for (int q = 0; q < kU; q++) {
-    int em, ec, en;
-    unit_geom(tid + q * 128, em, ec, en);
-    pre_rinv[q] = 1.0f;
-    pre_g[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (en > 0) {
-      epi_fetch(a, em, ec, en, pre_ep[q]);
-      pre_rinv[q] = epi_rinv(a, em);
-      pre_g[q] = epi_gains(a, ec, en);
+    for (int q = 0; q < kU; q++) {
+      int em, ec, en;
+      unit_geom(u0 + q * 128, em, ec, en);
+      rinv[q] = 1.0f;
+      g[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (en > 0) {
+        epi_fetch(a, em, ec, en, ep[q]);
+        rinv[q] = epi_rinv(a, em);
+        g[q] = epi_gains(a, ec, en);
+      }
     }
+  };
+  Epi4 cur_ep[kU];
+  float cur_rinv[kU];
+  float4 cur_g[kU];
+  fetch_round(tid, cur_ep, cur_rinv, cur_g);
+  // a thread's column group is the same in every round (the round and unit
+  // strides are multiples of the group count): its bias, loaded once
+  const int cb = (tid % groups) * 4;
+  float bias_g[4], bias_u[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    bias_g[j] = (a.bias && (sw || n0 + cb + j < a.N)) ? a.bias[n0 + cb + j] : 0.0f;
+    bias_u[j] = (a.bias && sw) ? a.bias[n0 + 64 + cb + j] : 0.0f;
   }
 
   // ---- epilogue: every warp waits for the accumulator
@@ -315,6 +328,10 @@ __global__ void __launch_bounds__(128)
     // is requested before the first sum, and the epilogue's global loads of
     // the round are issued before its stores (prefetched for round one).
     for (int u0 = tid; u0 < nunits; u0 += 128 * kU) {
+      Epi4 nxt_ep[kU];
+      float nxt_rinv[kU];
+      float4 nxt_g[kU];
+      fetch_round(u0 + 128 * kU, nxt_ep, nxt_rinv, nxt_g);
       float acc[kU][4], accu[kU][4];
 #pragma unroll
       for (int q = 0; q < kU; q++) {
@@ -325,9 +342,14 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
         for (int s0 = 0; s0 < 8; s0++) {
           if (u < nunits && s0 < a.splitk) {
-            const uint32_t remote = mapa_shared(my_base + off, (uint32_t)s0);
-            tg[s0] = ld_dsmem_f4(remote);
-            if (sw) tu[s0] = ld_dsmem_f4(remote + 64u * 4u);
+            if (s0 == split) {  // this CTA's own partial: a local read
+              tg[s0] = *reinterpret_cast<const float4*>(part + m * kTileN + c);
+              if (sw) tu[s0] = *reinterpret_cast<const float4*>(part + m * kTileN + c + 64);
+            } else {
+              const uint32_t remote = mapa_shared(my_base + off, (uint32_t)s0);
+              tg[s0] = ld_dsmem_f4(remote);
+              if (sw) tu[s0] = ld_dsmem_f4(remote + 64u * 4u);
+            }
           }
         }
 #pragma unroll
@@ -343,42 +365,26 @@ __global__ void __launch_bounds__(128)
         }
       }
       if (u0 == tid) TC_TRACE(8);
-      // epilogue: fetch every unit's gate/residual (prefetched in round
-      // one), then compute and store
-      Epi4 ep[kU];
+      // epilogue with the operands fetched a round ago (during the
+      // mainloop for round one)
       int em[kU], ec[kU], en[kU];
-      float rinv[kU];
-      float4 gv[kU];
 #pragma unroll
-      for (int q = 0; q < kU; q++) {
-        unit_geom(u0 + q * 128, em[q], ec[q], en[q]);
-        if (u0 == tid) {
-          ep[q] = pre_ep[q];
-          rinv[q] = pre_rinv[q];
-          gv[q] = pre_g[q];
-        } else if (en[q] > 0) {
-          epi_fetch(a, em[q], ec[q], en[q], ep[q]);
-          rinv[q] = epi_rinv(a, em[q]);
-          gv[q] = epi_gains(a, ec[q], en[q]);
-        }
-      }
+      for (int q = 0; q < kU; q++) unit_geom(u0 + q * 128, em[q], ec[q], en[q]);
 #pragma unroll
       for (int q = 0; q < kU; q++) {
         const int u = u0 + q * 128;
-        const int c = (u % groups) * 4;
         float sq = 0.0f;
         if (en[q] > 0) {  // rinv: folded RMSNorm of activation row em[q]
+          const float rinv = cur_rinv[q];
           float val[4], out[4];
 #pragma unroll
           for (int j = 0; j < 4; j++) {
-            if (sw) {
-              const float bg = a.bias ? a.bias[n0 + c + j] : 0.0f, bu = a.bias ? a.bias[n0 + 64 + c + j] : 0.0f;
-              val[j] = silu(acc[q][j] * rinv[q] + bg) * (accu[q][j] * rinv[q] + bu);
-            } else {
-              val[j] = acc[q][j] * rinv[q] + ((a.bias && j < en[q]) ? a.bias[n0 + c + j] : 0.0f);
-            }
+            if (sw)
+              val[j] = silu(acc[q][j] * rinv + bias_g[j]) * (accu[q][j] * rinv + bias_u[j]);
+            else
+              val[j] = acc[q][j] * rinv + (j < en[q] ? bias_g[j] : 0.0f);
           }
-          epi_store(a, em[q], ec[q], en[q], val, ep[q], gv[q], out);
+          epi_store(a, em[q], ec[q], en[q], val, cur_ep[q], cur_g[q], out);
           for (int j = 0; j < en[q]; j++) sq = fmaf(out[j], out[j], sq);
         }
         // one warp covers one output row of the tile (32 groups of 4
@@ -387,6 +393,12 @@ __global__ void __launch_bounds__(128)
           sq = warp_sum(sq);
           if (lane == 0 && u < nunits) a.ssp[(long)tile * a.ssp_ld + em[q]] = sq;
         }
+      }
+#pragma unroll
+      for (int q = 0; q < kU; q++) {
+        cur_ep[q] = nxt_ep[q];
+        cur_rinv[q] = nxt_rinv[q];
+        cur_g[q] = nxt_g[q];
       }
     }
   } else if (tid == 0 && a.err) {

@@ -315,3 +315,63 @@ def test_dit_fp16_range_error_moves_head_to_launch_chain(monkeypatch):
     assert np.isfinite(lat).all()
     assert np.array_equal(lat, lat0)
     assert eng.launches_per_step == eng0.launches_per_step
+
+
+def test_two_engines_from_two_host_threads():
+    """Two bf16 engines (own handles, streams and workspaces; the benchmark
+    DiT shape) stepped at the same time from two host threads -- the C calls
+    release the GIL.  Each gives bit for bit what the same engine gives
+    stepped alone, and matches the oracle."""
+    import threading
+
+    lcfg, dcfg = LMConfig(n_layers=2), DiTConfig()
+    B, F = 16, 3
+
+    def setup(k):
+        eng, keep, lw, dw, hw = build(lcfg, dcfg, seed=40 + k, dtype="bf16", batch=B, capacity=48)
+        rng = np.random.default_rng(40 + k)
+        lwb = bf16_weights(lw)
+        pres, conds = [], []
+        for b in range(B):
+            ids = rng.integers(0, lcfg.vocab, 8 + b % 5)
+            prompt = rng.standard_normal((4, 64), dtype=np.float32)
+            pres.append(prefix_rows(lwb, hw, ids, prompt))
+            conds.append(prompt[-1])
+            eng.prefill(b, pres[-1], conds[-1])
+        noise = rng.standard_normal((F, B, 64), dtype=np.float32)
+        return dict(eng=eng, keep=keep, lw=lw, dw=dw, hw=hw, pres=pres, conds=conds, noise=noise)
+
+    def frames(st):
+        return np.stack([st["eng"].step(st["noise"][f])[0] for f in range(F)])
+
+    alone = []
+    for k in range(2):
+        st = setup(k)
+        alone.append(frames(st))
+        del st
+    setups = [setup(k) for k in range(2)]
+    out, errs = [None, None], []
+    start = threading.Barrier(2)
+
+    def run(k):
+        try:
+            start.wait(timeout=60)
+            out[k] = frames(setups[k])
+        except Exception as e:  # reported below
+            errs.append(e)
+
+    th = [threading.Thread(target=run, args=(k,)) for k in range(2)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join(300)
+    assert not any(t.is_alive() for t in th)
+    assert not errs, errs
+    for k in range(2):
+        st = setups[k]
+        assert np.array_equal(out[k], alone[k]), k
+        lm_o, dit_o = orc.LM(lcfg, bf16_weights(st["lw"])), orc.DiT(dcfg, bf16_weights(st["dw"]))
+        for b in (0, B - 1):
+            ref, _, _ = orc.generate(lm_o, dit_o, st["hw"], st["pres"][b], st["noise"][:, b, :], st["conds"][b], 10)
+            for f in range(F):
+                assert cosine(out[k][f, b], ref[f]) >= 0.999, (k, b, f)
