@@ -1059,10 +1059,13 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const AttnArgs a) {
 // Q and P enter as bf16 pairs hi + lo (hi = bf16(x), lo = bf16(x - hi)), so
 // the products keep about 16 significant bits, close to the fp32 dot
 // products of the CUDA-core form.  Stages of 64 keys arrive by TMA tensor
-// copies with the 128-byte swizzle ([box of 64 dims][64 keys][128 B]), so
-// the ldmatrix rows of a warp fall in distinct banks.  Each warp owns 16
+// copies with the 128-byte swizzle ([box of 64 dims][64 keys][128 B]; the
+// ldmatrix rows of a warp fall in distinct banks), kAttnRing stages in
+// flight per CTA.  Each warp owns 16
 // keys of a stage and an online softmax over its keys; the merges follow
 // attn_split_kernel.
+constexpr int kAttnRing = 3;  // attn_mma_kernel: 64-key stages in flight per CTA
+
 CTTS_DEV uint32_t pack_bf2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -1103,11 +1106,12 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
   constexpr uint32_t kBox = C * 128;   // one box: 64 keys x 128 bytes
   constexpr uint32_t kTile = NB * kBox;  // one K or V stage
   constexpr int RW = 8;                // query rows held (G <= 8)
-  extern __shared__ __align__(1024) uint8_t dyn_smem[];  // [2][K|V][NB][C][128] swizzled
+  constexpr int NS = kAttnRing;        // stages in flight
+  extern __shared__ __align__(1024) uint8_t dyn_smem[];  // [NS][K|V][NB][C][128] swizzled
   __shared__ __align__(16) float qs[RW][HD];
   __shared__ __align__(16) uint8_t newrow[2][ROWB];
   __shared__ __align__(16) float cst[RW][HD + 2];
-  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ __align__(8) uint64_t bars[NS];
   uint8_t* kv_smem = dyn_smem + ((1024u - (static_cast<uint32_t>(__cvta_generic_to_shared(dyn_smem)) & 1023u)) & 1023u);
   const uint32_t kv_base = static_cast<uint32_t>(__cvta_generic_to_shared(kv_smem));
 
@@ -1129,7 +1133,7 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
     return (uint32_t)(chunk >> 3) * kBox + (uint32_t)key * 128u + (uint32_t)(((chunk & 7) ^ (key & 7)) << 4);
   };
   auto issue = [&](int st) {  // thread 0: the stage's K and V boxes (rows past the cache read as stale or zero)
-    const int buf = st & 1;
+    const int buf = st % NS;
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_a(buf)), "r"(2u * kTile)
                  : "memory");
     const int y = (int)(row0 + (size_t)k0 + (size_t)st * C);
@@ -1144,15 +1148,12 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
             : "memory");
   };
   if (tid == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_a(0)));
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_a(1)));
+    for (int i = 0; i < NS; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_a(i)));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  if (tid == 0 && !bad) {  // cached rows were written frames ago
-    if (nst > 0) issue(0);
-    if (nst > 1) issue(1);
-  }
+  if (tid == 0 && !bad)  // cached rows were written frames ago
+    for (int st = 0; st < min(nst, NS); st++) issue(st);
   grid_dep_enter();
   if (bad && kh == 0 && split == 0 && tid == 0 && a.err) atomicExch(a.err, 1);
 
@@ -1225,7 +1226,7 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
   const int kbase = warp * 16;
   bool ok = true;
   for (int st = 0; st < nst; st++) {
-    const int buf = st & 1;
+    const int buf = st % NS;
     const int kst = k0 + st * C;
     const int rows = min(C, k1 - kst);
     {
@@ -1237,7 +1238,7 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
             "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
             "selp.u32 %0, 1, 0, p;\n\t}"
             : "=r"(d)
-            : "r"(bar_a(buf)), "r"((uint32_t)((st >> 1) & 1))
+            : "r"(bar_a(buf)), "r"((uint32_t)((st / NS) & 1))
             : "memory");
         done = d != 0;
       }
@@ -1320,14 +1321,14 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
       mma_bf16_16816(o[t + 1], pl, vb[2], vb[3]);
     }
     __syncthreads();  // stage buffer consumed by every warp
-    if (tid == 0 && st + 2 < nst) issue(st + 2);
+    if (tid == 0 && st + NS < nst) issue(st + NS);
   }
   if (!ok && a.err && tid == 0) atomicExch(a.err, 3);
   // ---- this split's state: the warp states merged in warp order (the
   // per-warp states reuse the stage area: every copy into it was waited on
   // and every warp passed the last stage's barrier)
   float (*wpart)[RW][HD + 2] = reinterpret_cast<float (*)[RW][HD + 2]>(kv_smem);
-  static_assert(NW * RW * (HD + 2) * 4 <= 4 * kTile, "warp states fit the stage area");
+  static_assert(NW * RW * (HD + 2) * 4 <= 2 * NS * kTile, "warp states fit the stage area");
   if (gq < G) {
     if (tq == 0) {
       wpart[warp][gq][0] = m_w;
@@ -1597,7 +1598,7 @@ cudaError_t launch_attn_split_g(const AttnArgs& a, int S, size_t smem, cudaStrea
 // over this layer's K and V caches ([batch*nkv*cap, hd], 64-key boxes).
 template <int HD>
 cudaError_t launch_attn_mma(const AttnArgs& a, cudaStream_t s) {
-  const size_t smem = (size_t)2 * 2 * (HD / 64) * 64 * 128 + 1024;
+  const size_t smem = (size_t)kAttnRing * 2 * (HD / 64) * 64 * 128 + 1024;
   static SmemOptIn opt;
   if (cudaError_t e = opt.ensure((const void*)attn_mma_kernel<HD>, smem)) return e;
   static PerDeviceInt per_sm;
