@@ -731,9 +731,14 @@ __global__ void __launch_bounds__(kNT, 1)
           const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
           for (int e = 0; e < 4; e++) {
-            const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
-            acc[2 * e] += f2.x;
-            acc[2 * e + 1] += f2.y;
+            // fp32 += fp16 in one instruction (the fp16 value converts
+            // exactly; one rounding, as with a convert and an add)
+            asm("{\n\t.reg .f16 lo, hi;\n\t"
+                "mov.b32 {lo, hi}, %2;\n\t"
+                "add.rn.f32.f16 %0, lo, %0;\n\t"
+                "add.rn.f32.f16 %1, hi, %1;\n\t}"
+                : "+f"(acc[2 * e]), "+f"(acc[2 * e + 1])
+                : "r"(w[e]));
           }
         }
         if (cw == 0) DTRACE(0, 15);
