@@ -672,23 +672,33 @@ __global__ void __launch_bounds__(kNT, 1)
       // (the all-gathered norm operand, idle until the peers' next push,
       // which needs these partials first); warp 0 pushes one 2 KB block per
       // owner
-#pragma unroll 1
-      for (int dd = 0; dd < 4; dd++) {
-        const int d = 4 * cw + dd;
-        uint32_t v[32];
-        tmem_ld32_nowait(tmem + 32u * (uint32_t)d, v);
-        tmem_wait();
+      // 16-column halves through two register buffers: the TMEM load of
+      // half i + 1 is in flight while half i is converted and stored
+      auto stage_half = [&](const uint32_t* v, int i) {
+        const int d = 4 * cw + (i >> 1);
         uint8_t* stg = smem + kXA + (uint32_t)d * kPartBytes + (uint32_t)r * 16u;
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
+        for (int q = 0; q < 2; q++) {
           uint32_t h[4];
 #pragma unroll
           for (int e = 0; e < 4; e++) {
             const __half2 p2 = __floats2half2_rn(__uint_as_float(v[8 * q + 2 * e]), __uint_as_float(v[8 * q + 2 * e + 1]));
             h[e] = *reinterpret_cast<const uint32_t*>(&p2);
           }
-          st_u4(stg + q * 512, h[0], h[1], h[2], h[3]);
+          st_u4(stg + (2 * (i & 1) + q) * 512, h[0], h[1], h[2], h[3]);
         }
+      };
+      auto half_addr = [&](int i) { return tmem + 32u * (uint32_t)(4 * cw + (i >> 1)) + 16u * (uint32_t)(i & 1); };
+      uint32_t va[16], vb[16];
+      tmem_ld16_nowait(half_addr(0), va);
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        tmem_wait16(va);
+        tmem_ld16_nowait(half_addr(i + 1), vb);
+        stage_half(va, i);
+        tmem_wait16(vb);
+        if (i + 2 < 8) tmem_ld16_nowait(half_addr(i + 2), va);
+        stage_half(vb, i + 1);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       cbar();
@@ -939,21 +949,32 @@ __global__ void __launch_bounds__(kNT, 1)
         if (!ok) break;
         {
           uint8_t* sl = smem + kSWI;
-#pragma unroll
-          for (int t = 0; t < 3; t++) {
-            uint32_t gv[8], uv[8];
-            tmem_ld8_nowait(tmem + 24 * cw + 8 * t, gv);
-            tmem_ld8_nowait(tmem + kActOwn + 24 * cw + 8 * t, uv);
-            tmem_wait();
+          // chunk t = 8 gate + 8 up columns in one 16-register buffer; the
+          // TMEM loads of chunk t + 1 are in flight while chunk t is computed
+          auto load_chunk = [&](int t, uint32_t* c) {
+            tmem_ld8_nowait(tmem + 24 * cw + 8 * t, c);
+            tmem_ld8_nowait(tmem + kActOwn + 24 * cw + 8 * t, c + 8);
+          };
+          auto swiglu_chunk = [&](const uint32_t* c, int t) {
             uint32_t pk[4];
 #pragma unroll
             for (int e = 0; e < 8; e += 2) {
-              const float g0 = __uint_as_float(gv[e]), g1 = __uint_as_float(gv[e + 1]);
-              pk[e >> 1] = pack_bf(__fdividef(g0, 1.0f + __expf(-g0)) * __uint_as_float(uv[e]),
-                                   __fdividef(g1, 1.0f + __expf(-g1)) * __uint_as_float(uv[e + 1]));
+              const float g0 = __uint_as_float(c[e]), g1 = __uint_as_float(c[e + 1]);
+              pk[e >> 1] = pack_bf(__fdividef(g0, 1.0f + __expf(-g0)) * __uint_as_float(c[8 + e]),
+                                   __fdividef(g1, 1.0f + __expf(-g1)) * __uint_as_float(c[8 + e + 1]));
             }
             st_u4(sl + slice_off(r, 3 * cw + t), pk[0], pk[1], pk[2], pk[3]);
-          }
+          };
+          uint32_t ca[16], cb[16];
+          load_chunk(0, ca);
+          tmem_wait16(ca);
+          load_chunk(1, cb);
+          swiglu_chunk(ca, 0);
+          tmem_wait16(cb);
+          load_chunk(2, ca);
+          swiglu_chunk(cb, 1);
+          tmem_wait16(ca);
+          swiglu_chunk(ca, 2);
           postA(sb + kSWI, 0);
         }
         // S7: down partials -> owners -> gated residual -> row statistics

@@ -184,6 +184,68 @@ __global__ void __launch_bounds__(kWarps * 32) linear_rows_kernel(const LinearAr
   }
 }
 
+// Short contractions (K <= 128, fp32 weights, no prologue, no SwiGLU): the
+// latent-sized projections of a frame (the feedback projection has K = 64).
+// The form above splits K over the lanes and shuffle-reduces RPW x MT
+// accumulators per warp, which at such K leaves half the lanes idle and
+// runs a large unrolled body.  Here a thread owns one output column for MT
+// activation rows and walks K in order with fmaf from zero; the CTA's 128
+// weight rows are staged transposed in shared memory ([K][129], a warp
+// reads 32 consecutive columns) and its activation rows as [MT][K]
+// (broadcast reads).  grid (ceil(N / 128), ceil(M / MT)), 128 threads.
+constexpr int kSkCols = 128, kSkLd = kSkCols + 1;
+
+template <int MT>
+__global__ void __launch_bounds__(kSkCols) linear_smallk_kernel(const LinearArgs a) {
+  extern __shared__ __align__(16) float sk[];
+  const int K = a.K, K4 = K / 4;
+  float* xs = sk;           // [MT][K]
+  float* wt = sk + MT * K;  // [K][kSkLd]
+  const int n0 = blockIdx.x * kSkCols, m0 = blockIdx.y * MT;
+  const int mt = min(MT, a.M - m0);
+  const int tid = threadIdx.x;
+  grid_dep_enter();
+  const float* W = static_cast<const float*>(a.w);
+  for (int i = tid; i < kSkCols * K4; i += kSkCols) {
+    const int n = i / K4, k = (i % K4) * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (n0 + n < a.N) v = *reinterpret_cast<const float4*>(W + (size_t)(n0 + n) * K + k);
+    wt[(k + 0) * kSkLd + n] = v.x;
+    wt[(k + 1) * kSkLd + n] = v.y;
+    wt[(k + 2) * kSkLd + n] = v.z;
+    wt[(k + 3) * kSkLd + n] = v.w;
+  }
+  for (int i = tid; i < MT * K; i += kSkCols) {
+    const int r = i / K, k = i % K;
+    xs[i] = r < mt ? row_in(a.x, m0 + r, a.x_div, a.x_ld, a.x_ld_outer)[k] : 0.0f;
+  }
+  __syncthreads();
+  const int n = n0 + tid;
+  if (n >= a.N) return;
+  float acc[MT];
+#pragma unroll
+  for (int m = 0; m < MT; m++) acc[m] = 0.0f;
+#pragma unroll 4
+  for (int k = 0; k < K; k++) {
+    const float w = wt[k * kSkLd + tid];
+#pragma unroll
+    for (int m = 0; m < MT; m++) acc[m] = fmaf(w, xs[m * K + k], acc[m]);
+  }
+  const float b = a.bias ? a.bias[n] : 0.0f;
+#pragma unroll
+  for (int m = 0; m < MT; m++) {
+    if (m >= mt) break;
+    const int mm = m0 + m;
+    float val = acc[m] + b;
+    if (a.act == 1) val = silu(val);
+    const float coef = a.gate ? 1.0f + a.gate[(long)(mm / a.gate_div) * a.gate_ld + a.gate_off + n] : a.scale;
+    float* yr = const_cast<float*>(row_in(a.y, mm, a.y_div, a.y_ld, a.y_ld_outer));
+    float out = coef * val;
+    if (a.res) out = row_in(a.res, mm, a.y_div, a.y_ld, a.y_ld_outer)[n] + out;
+    yr[n] = out;
+  }
+}
+
 // One warp per row: y = bf16( modulate( RMSNorm(x) ) ), the tensor-core
 // path's activation operand.
 __global__ void __launch_bounds__(128) prep_bf16_kernel(const PrepArgs a) {
@@ -251,6 +313,35 @@ cudaError_t launch_t(const LinearArgs& a, cudaStream_t s) {
 }
 
 int pick_mt(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
+// a handful of output columns (a stop head: N = 2): one activation row per
+// CTA, so the rows spread over the GPU instead of idling most warps of few CTAs
+int pick_mt(const LinearArgs& a) { return a.N <= 16 ? 1 : pick_mt(a.M); }
+
+// (from 8 activation rows: with fewer, the long-K form's 1-4 rows per CTA
+// spread the columns over more CTAs than 128-column tiles do)
+bool smallk(const LinearArgs& a) {
+  return !a.w_bf16 && a.act != 2 && !a.norm_w && !a.mod && a.K <= 128 && a.K % 4 == 0 && a.M >= 8;
+}
+
+template <int MT>
+cudaError_t launch_smallk_t(const LinearArgs& a, cudaStream_t s) {
+  const size_t smem = ((size_t)MT * a.K + (size_t)a.K * kSkLd) * sizeof(float);
+  static SmemOptIn opt;
+  if (cudaError_t e = opt.ensure((const void*)linear_smallk_kernel<MT>, smem)) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.N + kSkCols - 1) / kSkCols, (a.M + MT - 1) / MT);
+  cfg.blockDim = dim3(kSkCols);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, linear_smallk_kernel<MT>, a);
+}
+
+cudaError_t launch_smallk(const LinearArgs& a, cudaStream_t s) { return launch_smallk_t<8>(a, s); }
 
 int pick_rpw(const LinearArgs& a, int mt) {
   int gy = (a.M + mt - 1) / mt;
@@ -263,7 +354,7 @@ int pick_rpw(const LinearArgs& a, int mt) {
 
 template <bool BF16, bool SW>
 cudaError_t dispatch_mt(const LinearArgs& a, cudaStream_t s) {
-  int mt = pick_mt(a.M);
+  int mt = pick_mt(a);
   int rpw = pick_rpw(a, mt);
 #define CTTS_L(MT_)                                                     \
   if (mt == MT_) {                                                      \
@@ -279,7 +370,8 @@ cudaError_t dispatch_mt(const LinearArgs& a, cudaStream_t s) {
 }  // namespace
 
 int linear_grid_ctas(const LinearArgs& a) {
-  int mt = pick_mt(a.M);
+  if (smallk(a)) return ((a.N + kSkCols - 1) / kSkCols) * ((a.M + 7) / 8);
+  int mt = pick_mt(a);
   int rpw = pick_rpw(a, mt);
   return ((a.N + kWarps * rpw - 1) / (kWarps * rpw)) * ((a.M + mt - 1) / mt);
 }
@@ -304,6 +396,7 @@ cudaError_t launch_linear(const LinearArgs& a, cudaStream_t s) {
   if (a.K <= 0 || a.K % vec != 0 || (size_t)8 * a.K * sizeof(float) > 200 * 1024)
     return cudaErrorInvalidValue;
   const bool sw = a.act == 2;
+  if (smallk(a)) return launch_smallk(a, s);
   if (a.w_bf16) return sw ? dispatch_mt<true, true>(a, s) : dispatch_mt<true, false>(a, s);
   return sw ? dispatch_mt<false, true>(a, s) : dispatch_mt<false, false>(a, s);
 }

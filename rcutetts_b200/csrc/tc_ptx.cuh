@@ -121,6 +121,16 @@ CTTS_DEV void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 CTTS_DEV void tmem_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// The same wait, naming the 16 destination registers of the load it waits
+// for as operands: their uses cannot be scheduled before it (a load's
+// outputs land only at the wait), while another load may be in flight.
+CTTS_DEV void tmem_wait16(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
 
 CTTS_DEV void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
