@@ -214,9 +214,11 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
   }
   // mu = mu_proj(z) (+ cfg_strength) (+ step_size)   diffusion_head.py:601-627
   // (bf16 weights with >= 16 rows: on the tensor cores)
+  bool xb_holds_z = false;  // w.xb = bf16(z) rows [0, R)
   if (d->mu_w && bf && R >= 16 && c.cond_dim % 64 == 0) {
     PrepArgs pa; pa.x = r.z; pa.x_ld = c.cond_dim; pa.y = w.xb; pa.y_ld = c.cond_dim; pa.M = R; pa.K = c.cond_dim;
     CTTS_CK(launch_prep_bf16(pa, s)); nl++;
+    xb_holds_z = true;
     TcArgs e; e.y = w.mu; e.y_ld = H; e.bias = d->mu_b;
     RUN(tc_run(w.tc, w.xb, R, c.cond_dim, d->mu_w, H, e, s, &nl));
   } else if (d->mu_w) {
@@ -249,9 +251,13 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
   if (use_ad) {
     int rows = r.zero_adaln_from >= 0 ? r.zero_adaln_from : R;
     if (bf && rows >= 16 && c.spk_dim % 64 == 0) {
-      PrepArgs pa; pa.x = r.spk; pa.x_ld = c.spk_dim; pa.y = w.xb; pa.y_ld = c.spk_dim; pa.M = rows;
-      pa.K = c.spk_dim;
-      CTTS_CK(launch_prep_bf16(pa, s)); nl++;
+      // AdaLN conditioned on the LM state itself: its bf16 rows are already
+      // the mu_proj operand
+      if (!(xb_holds_z && r.spk == r.z && c.spk_dim == c.cond_dim)) {
+        PrepArgs pa; pa.x = r.spk; pa.x_ld = c.spk_dim; pa.y = w.xb; pa.y_ld = c.spk_dim; pa.M = rows;
+        pa.K = c.spk_dim;
+        CTTS_CK(launch_prep_bf16(pa, s)); nl++;
+      }
       TcArgs e; e.y = w.ad; e.y_ld = adld;
       RUN(tc_run(w.tc, w.xb, rows, c.spk_dim, d->adaln, (int)adld, e, s, &nl));
     } else {
@@ -260,7 +266,9 @@ int dit_enqueue(ctts_dit* d, DitWs& w, const DitRun& r, cudaStream_t s, int* lau
     }
     if (rows < R) CTTS_CK(cudaMemsetAsync(w.ad + (size_t)rows * adld, 0, sizeof(float) * (R - rows) * adld, s));
   }
-  if (bf && R * P >= 16 && L % 64 == 0) {  // cond_proj(cond) rows [R*P, L]
+  // cond_proj(cond) rows [R*P, L]: tensor cores for a long contraction; the
+  // latent-sized one (L <= 128) on the short-contraction CUDA-core linear
+  if (bf && R * P >= 16 && L % 64 == 0 && L > 128) {
     PrepArgs pa; pa.x = r.cond; pa.x_ld = L; pa.y = w.xb; pa.y_ld = L; pa.M = R * P; pa.K = L;
     CTTS_CK(launch_prep_bf16(pa, s)); nl++;
     TcArgs e; e.y = w.condh; e.y_ld = H; e.bias = d->cond_b;

@@ -184,8 +184,9 @@ __global__ void __launch_bounds__(kWarps * 32) linear_rows_kernel(const LinearAr
   }
 }
 
-// Short contractions (K <= 128, fp32 weights, no prologue, no SwiGLU): the
-// latent-sized projections of a frame (the feedback projection has K = 64).
+// Short contractions (K <= 128, fp32 or bf16 weights, no prologue, no
+// SwiGLU): the latent-sized projections of a frame (the feedback and the
+// DiT condition projections have K = 64).
 // The form above splits K over the lanes and shuffle-reduces RPW x MT
 // accumulators per warp, which at such K leaves half the lanes idle and
 // runs a large unrolled body.  Here a thread owns one output column for MT
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(kWarps * 32) linear_rows_kernel(const LinearAr
 // (broadcast reads).  grid (ceil(N / 128), ceil(M / MT)), 128 threads.
 constexpr int kSkCols = 128, kSkLd = kSkCols + 1;
 
-template <int MT>
+template <int MT, bool BF16>
 __global__ void __launch_bounds__(kSkCols) linear_smallk_kernel(const LinearArgs a) {
   extern __shared__ __align__(16) float sk[];
   const int K = a.K, K4 = K / 4;
@@ -205,15 +206,31 @@ __global__ void __launch_bounds__(kSkCols) linear_smallk_kernel(const LinearArgs
   const int mt = min(MT, a.M - m0);
   const int tid = threadIdx.x;
   grid_dep_enter();
-  const float* W = static_cast<const float*>(a.w);
-  for (int i = tid; i < kSkCols * K4; i += kSkCols) {
-    const int n = i / K4, k = (i % K4) * 4;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (n0 + n < a.N) v = *reinterpret_cast<const float4*>(W + (size_t)(n0 + n) * K + k);
-    wt[(k + 0) * kSkLd + n] = v.x;
-    wt[(k + 1) * kSkLd + n] = v.y;
-    wt[(k + 2) * kSkLd + n] = v.z;
-    wt[(k + 3) * kSkLd + n] = v.w;
+  if constexpr (BF16) {  // 8 weights per 16-byte load, widened exactly
+    const uint16_t* W = static_cast<const uint16_t*>(a.w);
+    const int K8 = K / 8;
+    for (int i = tid; i < kSkCols * K8; i += kSkCols) {
+      const int n = i / K8, k = (i % K8) * 8;
+      uint4 t = make_uint4(0u, 0u, 0u, 0u);
+      if (n0 + n < a.N) t = *reinterpret_cast<const uint4*>(W + (size_t)(n0 + n) * K + k);
+      const uint32_t u[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        wt[(k + 2 * j) * kSkLd + n] = bf_lo(u[j]);
+        wt[(k + 2 * j + 1) * kSkLd + n] = bf_hi(u[j]);
+      }
+    }
+  } else {
+    const float* W = static_cast<const float*>(a.w);
+    for (int i = tid; i < kSkCols * K4; i += kSkCols) {
+      const int n = i / K4, k = (i % K4) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (n0 + n < a.N) v = *reinterpret_cast<const float4*>(W + (size_t)(n0 + n) * K + k);
+      wt[(k + 0) * kSkLd + n] = v.x;
+      wt[(k + 1) * kSkLd + n] = v.y;
+      wt[(k + 2) * kSkLd + n] = v.z;
+      wt[(k + 3) * kSkLd + n] = v.w;
+    }
   }
   for (int i = tid; i < MT * K; i += kSkCols) {
     const int r = i / K, k = i % K;
@@ -320,14 +337,14 @@ int pick_mt(const LinearArgs& a) { return a.N <= 16 ? 1 : pick_mt(a.M); }
 // (from 8 activation rows: with fewer, the long-K form's 1-4 rows per CTA
 // spread the columns over more CTAs than 128-column tiles do)
 bool smallk(const LinearArgs& a) {
-  return !a.w_bf16 && a.act != 2 && !a.norm_w && !a.mod && a.K <= 128 && a.K % 4 == 0 && a.M >= 8;
+  return a.act != 2 && !a.norm_w && !a.mod && a.K <= 128 && a.K % (a.w_bf16 ? 8 : 4) == 0 && a.M >= 8;
 }
 
-template <int MT>
+template <int MT, bool BF16>
 cudaError_t launch_smallk_t(const LinearArgs& a, cudaStream_t s) {
   const size_t smem = ((size_t)MT * a.K + (size_t)a.K * kSkLd) * sizeof(float);
   static SmemOptIn opt;
-  if (cudaError_t e = opt.ensure((const void*)linear_smallk_kernel<MT>, smem)) return e;
+  if (cudaError_t e = opt.ensure((const void*)linear_smallk_kernel<MT, BF16>, smem)) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((a.N + kSkCols - 1) / kSkCols, (a.M + MT - 1) / MT);
   cfg.blockDim = dim3(kSkCols);
@@ -338,10 +355,12 @@ cudaError_t launch_smallk_t(const LinearArgs& a, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, linear_smallk_kernel<MT>, a);
+  return cudaLaunchKernelEx(&cfg, linear_smallk_kernel<MT, BF16>, a);
 }
 
-cudaError_t launch_smallk(const LinearArgs& a, cudaStream_t s) { return launch_smallk_t<8>(a, s); }
+cudaError_t launch_smallk(const LinearArgs& a, cudaStream_t s) {
+  return a.w_bf16 ? launch_smallk_t<8, true>(a, s) : launch_smallk_t<8, false>(a, s);
+}
 
 int pick_rpw(const LinearArgs& a, int mt) {
   int gy = (a.M + mt - 1) / mt;
