@@ -387,24 +387,21 @@ __global__ void __launch_bounds__(128) attn_step_kernel(const AttnArgs a) {
   }
 }
 
-// Optional phase timeline (build with -DCTTS_ATT_TRACE): thread 0 of CTA
-// (0, 0) of every loop-attention launch records ((launch << 8) | event,
-// %globaltimer) pairs; slots are taken atomically (launches overlap).
+// Optional phase timeline (build with -DCTTS_ATT_TRACE): thread 0 of the
+// first CTA of every decode-attention launch records %globaltimer per event.
 #ifdef CTTS_ATT_TRACE
-__device__ long long g_att_trace[4096];
-__device__ int g_att_trace_n;
+// The launch number is taken atomically once, at event 0 (after its
+// timestamp); later events store into their own [launch][event] slot.
+constexpr int kAttTraceLaunches = 128, kAttTraceEvents = 16;
+__device__ long long g_att_trace[kAttTraceLaunches * kAttTraceEvents];
 __device__ int g_att_launch;
 CTTS_DEV void att_trace(int ev) {
-  if (blockIdx.x != 0 || blockIdx.y != 0 || threadIdx.x != 0) return;
+  if (blockIdx.x != 0 || blockIdx.y != 0 || blockIdx.z != 0 || threadIdx.x != 0) return;
   __shared__ int lid;
-  if (ev == 0) lid = atomicAdd(&g_att_launch, 1);
   long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  const int n = atomicAdd(&g_att_trace_n, 1);
-  if (n < 2047) {
-    g_att_trace[2 * n] = ((long long)lid << 8) | ev;
-    g_att_trace[2 * n + 1] = t;
-  }
+  if (ev == 0) lid = atomicAdd(&g_att_launch, 1);
+  if (lid < kAttTraceLaunches && ev < kAttTraceEvents) g_att_trace[lid * kAttTraceEvents + ev] = t;
 }
 #define ATT_TRACE(ev) att_trace(ev)
 #else
@@ -1056,9 +1053,10 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const AttnArgs a) {
 // S[q][key] = Q . K^T with the G query heads as the rows of the A operand
 // (rows G..15 zero) and 8-key column tiles read by ldmatrix from the K
 // stage, then O += P . V with P as the A operand and V read transposed.
-// Q and P enter as bf16 pairs hi + lo (hi = bf16(x), lo = bf16(x - hi)), so
-// the products keep about 16 significant bits, close to the fp32 dot
-// products of the CUDA-core form.  Stages of 64 keys arrive by TMA tensor
+// Q enters as a bf16 pair hi + lo (hi = bf16(x), lo = bf16(x - hi)), so the
+// scores keep about 16 significant bits (the exponential amplifies their
+// error); P, in [0, 1], enters in bf16 with the products accumulated in
+// fp32.  Stages of 64 keys arrive by TMA tensor
 // copies with the 128-byte swizzle ([box of 64 dims][64 keys][128 B]; the
 // ldmatrix rows of a warp fall in distinct banks), kAttnRing stages in
 // flight per CTA.  Each warp owns 16
@@ -1076,8 +1074,9 @@ CTTS_DEV void split_bf2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
   hi = pack_bf2(x0, x1);
   lo = pack_bf2(x0 - bf_lo(hi), x1 - bf_hi(hi));
 }
+// (register operands only: not volatile, so independent MMAs interleave)
 CTTS_DEV void mma_bf16_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -1112,6 +1111,7 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
   __shared__ __align__(16) uint8_t newrow[2][ROWB];
   __shared__ __align__(16) float cst[RW][HD + 2];
   __shared__ __align__(8) uint64_t bars[NS];
+  ATT_TRACE(0);
   uint8_t* kv_smem = dyn_smem + ((1024u - (static_cast<uint32_t>(__cvta_generic_to_shared(dyn_smem)) & 1023u)) & 1023u);
   const uint32_t kv_base = static_cast<uint32_t>(__cvta_generic_to_shared(kv_smem));
 
@@ -1151,56 +1151,71 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
     for (int i = 0; i < NS; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_a(i)));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  for (int i = tid; i < RW * HD; i += NT) qs[i / HD][i % HD] = 0.0f;
   __syncthreads();
   if (tid == 0 && !bad)  // cached rows were written frames ago
     for (int st = 0; st < min(nst, NS); st++) issue(st);
+  // what the prologue needs besides the new q/k/v rows depends on weights
+  // and the position only: the RoPE angles of this position and the
+  // QK-Norm gains of this lane's dims, ready before the wait
+  constexpr int PH = HD / 16;
+  const int hl = lane & 15;
+  float rcs[PH / 2], rsn[PH / 2], gnq[PH], gnk[PH];
+#pragma unroll
+  for (int j = 0; j < PH / 2; j++) sincosf((float)(bad ? 0 : pos) * a.inv_freq[hl + 16 * j], &rsn[j], &rcs[j]);
+#pragma unroll
+  for (int j = 0; j < PH; j++) {
+    gnq[j] = a.qn ? a.qn[hl + 16 * j] : 1.0f;
+    gnk[j] = a.kn ? a.kn[hl + 16 * j] : 1.0f;
+  }
+  ATT_TRACE(1);
   grid_dep_enter();
+  ATT_TRACE(2);
   if (bad && kh == 0 && split == 0 && tid == 0 && a.err) atomicExch(a.err, 1);
 
-  // ---- queries (every split) and the new key/value row (its owner)
-  constexpr int PER = HD / 32;
+  // ---- queries (every split) and the new key/value row (its owner): one
+  // job per half-warp (lanes 16h..16h+15 of warp w take job 2w + h), a lane
+  // holding dims l, l + 16, ...; the RoPE pairs (d, d + HD/2) stay in the
+  // lane and every lane takes part in the half-warp norm reduction
   const int width = (nq + 2 * nkv) * HD;
   const float* src_row = a.qkv + (size_t)b * width;
-  for (int i = tid; i < RW * HD; i += NT) qs[i / HD][i % HD] = 0.0f;
-  __syncthreads();
   const int jobs = bad ? 0 : (owns_new ? G + 2 : G);
-  for (int job = warp; job < jobs; job += NW) {
+  for (int j0 = 2 * warp; j0 < jobs; j0 += 2 * NW) {
+    const int job = j0 + (lane >> 4);
+    const bool act = job < jobs;
     const bool is_q = job < G, is_v = job == G + 1;
     const int head = is_q ? kh * G + job : (is_v ? nq + nkv + kh : nq + kh);
     const float* src = src_row + head * HD;
-    float v[PER];
+    float v[PH];
 #pragma unroll
-    for (int j = 0; j < PER; j++) v[j] = src[lane + 32 * j];
-    if (!is_v) {
-      const float* gn = is_q ? a.qn : a.kn;
-      if (gn) {
-        float ss = 0.0f;
+    for (int j = 0; j < PH; j++) v[j] = act ? src[hl + 16 * j] : 0.0f;
+    float ss = 0.0f;
 #pragma unroll
-        for (int j = 0; j < PER; j++) ss = fmaf(v[j], v[j], ss);
-        ss = warp_sum(ss);
+    for (int j = 0; j < PH; j++) ss = fmaf(v[j], v[j], ss);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (act && !is_v) {
+      if (is_q ? a.qn != nullptr : a.kn != nullptr) {
         const float inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
 #pragma unroll
-        for (int j = 0; j < PER; j++) v[j] = v[j] * inv * gn[lane + 32 * j];
+        for (int j = 0; j < PH; j++) v[j] = v[j] * inv * (is_q ? gnq[j] : gnk[j]);
       }
 #pragma unroll
-      for (int j = 0; j < PER / 2; j++) {
-        const int i = lane + 32 * j;
-        float sn, cs;
-        sincosf((float)pos * a.inv_freq[i], &sn, &cs);
-        const float x1 = v[j], x2 = v[j + PER / 2];
-        v[j] = x1 * cs - x2 * sn;
-        v[j + PER / 2] = x1 * sn + x2 * cs;
+      for (int j = 0; j < PH / 2; j++) {
+        const float x1 = v[j], x2 = v[j + PH / 2];
+        v[j] = x1 * rcs[j] - x2 * rsn[j];
+        v[j + PH / 2] = x1 * rsn[j] + x2 * rcs[j];
       }
     }
-    if (is_q) {
+    if (act && is_q) {
 #pragma unroll
-      for (int j = 0; j < PER; j++) qs[job][lane + 32 * j] = v[j];
-    } else {
+      for (int j = 0; j < PH; j++) qs[job][hl + 16 * j] = v[j];
+    } else if (act) {
       void* cache = is_v ? a.vcache : a.kcache;
       uint16_t* nr = reinterpret_cast<uint16_t*>(newrow[is_v ? 1 : 0]);
 #pragma unroll
-      for (int j = 0; j < PER; j++) {
-        const int d = lane + 32 * j;
+      for (int j = 0; j < PH; j++) {
+        const int d = hl + 16 * j;
         const uint16_t hb = f2bf(v[j]);
         reinterpret_cast<uint16_t*>(cache)[(row0 + pos) * HD + d] = hb;
         nr[d] = hb;
@@ -1208,6 +1223,7 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
     }
   }
   __syncthreads();  // queries and the new row are set
+  ATT_TRACE(3);
 
   // A fragments of Q (rows 0..7 = query heads, rows 8..15 zero), hi and lo
   const int gq = lane >> 2, tq = lane & 3;
@@ -1244,6 +1260,7 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
       }
       if (!done) ok = false;
     }
+    ATT_TRACE(4 + 2 * min(st, 3));
     if (owns_new && pos >= kst && pos < kst + C && tid < 2 * (ROWB / 16)) {  // the new row into its stage
       const int kv = tid / (ROWB / 16), cch = tid % (ROWB / 16);
       *reinterpret_cast<uint4*>(kv_smem + (tile(buf, kv) - kv_base) + sw(pos - kst, cch)) =
@@ -1257,9 +1274,14 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
     }
     __syncthreads();
     // scores of the warp's 16 keys: two 8-key column tiles
-    float s[2][4];
+    // the hi and lo products accumulate separately (four independent MMA
+    // chains instead of two), summed once
+    float s[2][4], sl[2][4];
 #pragma unroll
-    for (int j = 0; j < 2; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+    for (int j = 0; j < 2; j++) {
+      s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+      sl[j][0] = sl[j][1] = sl[j][2] = sl[j][3] = 0.0f;
+    }
     const uint32_t kt = tile(buf, 0), vt = tile(buf, 1);
 #pragma unroll
     for (int ks = 0; ks < KS; ks++) {
@@ -1270,10 +1292,14 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
       const uint32_t ah[4] = {qa_hi[ks][0], 0u, qa_hi[ks][1], 0u};
       const uint32_t al[4] = {qa_lo[ks][0], 0u, qa_lo[ks][1], 0u};
       mma_bf16_16816(s[0], ah, kb[0], kb[1]);
-      mma_bf16_16816(s[0], al, kb[0], kb[1]);
+      mma_bf16_16816(sl[0], al, kb[0], kb[1]);
       mma_bf16_16816(s[1], ah, kb[2], kb[3]);
-      mma_bf16_16816(s[1], al, kb[2], kb[3]);
+      mma_bf16_16816(sl[1], al, kb[2], kb[3]);
     }
+#pragma unroll
+    for (int j = 0; j < 2; j++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) s[j][e] += sl[j][e];
     // online softmax of row gq over the warp's keys kbase + 8j + 2tq + e
     float mx = -INFINITY;
 #pragma unroll
@@ -1305,10 +1331,11 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
       o[t][0] *= f;
       o[t][1] *= f;
     }
-    // P as the A operand (rows 8..15 zero), hi and lo
-    uint32_t ph[4] = {0u, 0u, 0u, 0u}, pl[4] = {0u, 0u, 0u, 0u};
-    split_bf2(p[0][0], p[0][1], ph[0], pl[0]);
-    split_bf2(p[1][0], p[1][1], ph[2], pl[2]);
+    // P as the A operand in bf16 (rows 8..15 zero): probabilities in
+    // [0, 1], products accumulated in fp32
+    uint32_t ph[4] = {0u, 0u, 0u, 0u};
+    ph[0] = pack_bf2(p[0][0], p[0][1]);
+    ph[2] = pack_bf2(p[1][0], p[1][1]);
 #pragma unroll
     for (int t = 0; t < NO; t += 2) {
       // matrices: (keys 0-7, dims 8t..), (keys 8-15, 8t..), (keys 0-7, 8t+8..), (keys 8-15, 8t+8..)
@@ -1316,11 +1343,10 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
       uint32_t vb[4];
       ldsm_x4_t(vt + sw(key, t + (mi >> 1)), vb);
       mma_bf16_16816(o[t], ph, vb[0], vb[1]);
-      mma_bf16_16816(o[t], pl, vb[0], vb[1]);
       mma_bf16_16816(o[t + 1], ph, vb[2], vb[3]);
-      mma_bf16_16816(o[t + 1], pl, vb[2], vb[3]);
     }
     __syncthreads();  // stage buffer consumed by every warp
+    ATT_TRACE(5 + 2 * min(st, 3));
     if (tid == 0 && st + NS < nst) issue(st + NS);
   }
   if (!ok && a.err && tid == 0) atomicExch(a.err, 3);
@@ -1361,7 +1387,9 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
     }
   }
   // every split's state is written
+  ATT_TRACE(12);
   cluster_sync();
+  ATT_TRACE(13);
   if (!bad) {
     const int tot = G * HD, share = (tot + S - 1) / S;
     const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(&cst[0][0]));
@@ -1386,8 +1414,10 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __grid_constant__ C
         a.out[oi] = ov;
     }
   }
+  ATT_TRACE(14);
   // no CTA leaves while a peer may still read its state
   cluster_sync();
+  ATT_TRACE(15);
 }
 
 // causal prefill attention: grid (T, nq), 128 threads, dyn smem n floats
@@ -1725,13 +1755,15 @@ cudaError_t launch_swiglu(const float* gu, int M, int F, float* out, cudaStream_
 }  // namespace ctts
 
 #ifdef CTTS_ATT_TRACE
-// Copies the recorded timeline out and resets it.
+// Copies the recorded timeline out ([launch][event] timestamps, 0 = not
+// recorded; *n = launches) and resets it.
 extern "C" __attribute__((visibility("default"))) int ctts_att_trace(long long* out, int* n) {
-  cudaMemcpyFromSymbol(n, ctts::g_att_trace_n, sizeof(int));
-  if (*n > 2047) *n = 2047;
-  cudaMemcpyFromSymbol(out, ctts::g_att_trace, sizeof(long long) * 4096);
+  cudaMemcpyFromSymbol(n, ctts::g_att_launch, sizeof(int));
+  if (*n > ctts::kAttTraceLaunches) *n = ctts::kAttTraceLaunches;
+  cudaMemcpyFromSymbol(out, ctts::g_att_trace, sizeof(ctts::g_att_trace));
+  static long long zeros[ctts::kAttTraceLaunches * ctts::kAttTraceEvents] = {};
+  cudaMemcpyToSymbol(ctts::g_att_trace, zeros, sizeof(zeros));
   int z = 0;
-  cudaMemcpyToSymbol(ctts::g_att_launch, &z, sizeof(int));
-  return cudaMemcpyToSymbol(ctts::g_att_trace_n, &z, sizeof(int)) == cudaSuccess ? 0 : -2;
+  return cudaMemcpyToSymbol(ctts::g_att_launch, &z, sizeof(int)) == cudaSuccess ? 0 : -2;
 }
 #endif
