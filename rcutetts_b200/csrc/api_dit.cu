@@ -778,11 +778,20 @@ int engine_enqueue_group(ctts_engine* e, EngineGroup& g, cudaStream_t s, int* la
   };
   if (int rcm = mark(0)) return rcm;
   CTTS_CK(cudaMemcpyAsync(x, noise, sizeof(float) * B * PL, cudaMemcpyDeviceToDevice, s));
-  {  // stop logits (e2e.rs:83-92)
+  // stop logits (e2e.rs:83-92) read z like the DiT prologue; outside the
+  // profiling mode they run on the group's side stream, concurrently with
+  // the DiT, joined before the LM step rewrites z
+  const bool side = !prof && g.side;
+  if (side) {
+    CTTS_CK(cudaEventRecord(g.side_fork, s));
+    CTTS_CK(cudaStreamWaitEvent(g.side, g.side_fork, 0));
+  }
+  {
     LinearArgs a; a.x = z; a.x_ld = H; a.M = B; a.K = H; a.N = 2; a.w = e->stop_w;
     a.bias = e->stop_b; a.y = stop; a.y_ld = 2;
-    CTTS_CK(launch_linear(a, s)); nl++;
+    CTTS_CK(launch_linear(a, side ? g.side : s)); nl++;
   }
+  if (side) CTTS_CK(cudaEventRecord(g.side_join, g.side));
   const int steps = e->cfg.euler_steps;
   std::vector<float> times(steps + 1), dts(steps);
   const float dt = 1.0f / (float)steps;
@@ -822,6 +831,7 @@ int engine_enqueue_group(ctts_engine* e, EngineGroup& g, cudaStream_t s, int* la
   if (e->cfg_on)  // the same acoustic input feeds the unconditional branch (bin/cutetts.rs:503-509)
     CTTS_CK(cudaMemcpyAsync(g.kv->h + (size_t)B * H, g.kv->h, sizeof(float) * B * H, cudaMemcpyDeviceToDevice, s));
   if (int rcm = mark(3)) return rcm;
+  if (side) CTTS_CK(cudaStreamWaitEvent(s, g.side_join, 0));
   rc = lm_forward_rows(lm, g.kv, zm * B, -1, 0, z, s, &nl);
   if (rc) return rc;
   if (int rcm = mark(4)) return rcm;
@@ -868,6 +878,12 @@ void engine_destroy(ctts_engine* e) {
     delete g.ws;
     if (g.done) cudaEventDestroy(g.done);
     if (g.stream) cudaStreamDestroy(g.stream);
+    if (g.side) {
+      cudaStreamSynchronize(g.side);
+      cudaStreamDestroy(g.side);
+    }
+    if (g.side_fork) cudaEventDestroy(g.side_fork);
+    if (g.side_join) cudaEventDestroy(g.side_join);
   }
   if (e->fork) cudaEventDestroy(e->fork);
   if (e->stream) cudaStreamDestroy(e->stream);
@@ -912,6 +928,9 @@ extern "C" int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_
     g.ws = new DitWs();
     cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking);
     cudaEventCreateWithFlags(&g.done, cudaEventDisableTiming);
+    cudaStreamCreateWithFlags(&g.side, cudaStreamNonBlocking);
+    cudaEventCreateWithFlags(&g.side_fork, cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&g.side_join, cudaEventDisableTiming);
     rc = ctts_kv_alloc(lm, zm * per, cfg->capacity, &g.kv);
     if (!rc) rc = dit_ws_ensure(dit, *g.ws, zm * per, cfg->euler_steps);
     if (!rc && dit->cfg.cfg_emb) rc = dit_upload_cfg_hidden(dit, g.ws->hbuf, cfg->cfg_strength, g.stream);

@@ -108,6 +108,9 @@ struct EngineGroup {
   DitWs* ws = nullptr;         // their DiT workspace (owned)
   cudaStream_t stream = nullptr;
   cudaEvent_t done = nullptr;
+  // side branch of a frame: the stop head, concurrent with the DiT
+  cudaStream_t side = nullptr;
+  cudaEvent_t side_fork = nullptr, side_join = nullptr;
 };
 
 struct ctts_engine {

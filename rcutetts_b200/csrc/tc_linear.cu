@@ -67,7 +67,7 @@ struct Epi4 {
 CTTS_DEV void epi_fetch(const TcArgs& a, int m, int col, int n, Epi4& e) {
   const long yo = (long)m * a.y_ld + col;
   const float* gp = a.gate ? a.gate + (long)(m / a.gate_div) * a.gate_ld + a.gate_off + col : nullptr;
-  if (n == 4 && (yo % 4 == 0) && (!gp || ((reinterpret_cast<uintptr_t>(gp) & 15) == 0))) {
+  if (n == 4 && (yo & 3) == 0 && (!gp || ((reinterpret_cast<uintptr_t>(gp) & 15) == 0))) {
     float4 gv = gp ? *reinterpret_cast<const float4*>(gp) : make_float4(0.f, 0.f, 0.f, 0.f);
     float4 rv = a.res ? *reinterpret_cast<const float4*>(a.res + yo) : make_float4(0.f, 0.f, 0.f, 0.f);
     e.g[0] = gv.x; e.g[1] = gv.y; e.g[2] = gv.z; e.g[3] = gv.w;
@@ -109,7 +109,7 @@ CTTS_DEV void epi_store(const TcArgs& a, int m, int col, int n, const float* val
 #pragma unroll
   for (int j = 0; j < 4; j++) out[j] = e.r[j] + (a.gate ? 1.0f + e.g[j] : a.scale) * val[j];
   if (a.yb2) {  // the next RMSNorm's operand, gain applied, scale folded downstream
-    if (n == 4 && (yo % 4 == 0)) {
+    if (n == 4 && (yo & 3) == 0) {
       uint2 pk;
       pk.x = (uint32_t)f2bf(out[0] * g.x) | ((uint32_t)f2bf(out[1] * g.y) << 16);
       pk.y = (uint32_t)f2bf(out[2] * g.z) | ((uint32_t)f2bf(out[3] * g.w) << 16);
@@ -119,7 +119,7 @@ CTTS_DEV void epi_store(const TcArgs& a, int m, int col, int n, const float* val
       for (int j = 0; j < n; j++) a.yb2[yo + j] = f2bf(out[j] * gg[j]);
     }
   }
-  if (n == 4 && (yo % 4 == 0)) {
+  if (n == 4 && (yo & 3) == 0) {
     if (a.yb) {
       uint2 pk;
       pk.x = (uint32_t)f2bf(out[0]) | ((uint32_t)f2bf(out[1]) << 16);
@@ -138,6 +138,11 @@ CTTS_DEV void epi_store(const TcArgs& a, int m, int col, int n, const float* val
   }
 }
 
+// SW: the SwiGLU epilogue (act 2); SPLIT: K split over a cluster (else the
+// CTA's own accumulator is the whole sum).  The epilogue runs several
+// rounds of output units per thread for wide tiles (a 64-row tile of a
+// 12288-column AdaLN projection: 8), so its dead paths are compiled out.
+template <bool SW, bool SPLIT>
 __global__ void __launch_bounds__(128)
     tc_linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                      const TcArgs a) {
@@ -244,12 +249,13 @@ __global__ void __launch_bounds__(128)
   const int mcount = min(a.MT, a.M - a.m0);
   const int rows_per = (mcount + a.splitk - 1) / a.splitk;
   const int m_lo = split * rows_per, m_hi = min(mcount, m_lo + rows_per);
-  const bool sw = a.act == 2;
-  const int groups = sw ? 16 : 32;
+  constexpr bool sw = SW;
+  constexpr int groups = sw ? 16 : 32;
+  constexpr int gshift = sw ? 4 : 5;  // log2(groups)
   const int nunits = max(0, m_hi - m_lo) * groups;
   constexpr int kU = 2;
   auto unit_geom = [&](int u, int& em, int& ec, int& en) {
-    const int m = m_lo + u / groups, c = (u % groups) * 4;
+    const int m = m_lo + (u >> gshift), c = (u & (groups - 1)) * 4;
     em = a.m0 + m;
     ec = sw ? tile * 64 + c : n0 + c;
     en = u < nunits ? (sw ? 4 : max(0, min(4, a.N - (n0 + c)))) : 0;
@@ -320,7 +326,8 @@ __global__ void __launch_bounds__(128)
   // splits, in split order (deterministic), reading peers over DSMEM, and
   // runs the epilogue on float4 column groups.
   // a failed peer leaves a garbage partial: lane s reads split s's flag
-  const uint32_t peer_flag = lane < a.splitk ? ld_dsmem_u32(mapa_shared(smem_u32(flag), (uint32_t)lane)) : 0u;
+  const uint32_t peer_flag =
+      (SPLIT && lane < a.splitk) ? ld_dsmem_u32(mapa_shared(smem_u32(flag), (uint32_t)lane)) : 0u;
   const bool any_failed = failed || __any_sync(0xffffffffu, peer_flag != 0u);
   if (!any_failed) {
     const uint32_t my_base = smem_u32(part);
@@ -337,12 +344,12 @@ __global__ void __launch_bounds__(128)
       for (int q = 0; q < kU; q++) {
         const int u = u0 + q * 128;
         float4 tg[8], tu[8];
-        const int m = m_lo + u / groups, c = (u % groups) * 4;
+        const int m = m_lo + (u >> gshift), c = (u & (groups - 1)) * 4;
         const uint32_t off = (uint32_t)(m * kTileN + c) * 4u;
 #pragma unroll
-        for (int s0 = 0; s0 < 8; s0++) {
+        for (int s0 = 0; s0 < (SPLIT ? 8 : 1); s0++) {
           if (u < nunits && s0 < a.splitk) {
-            if (s0 == split) {  // this CTA's own partial: a local read
+            if (!SPLIT || s0 == split) {  // this CTA's own partial: a local read
               tg[s0] = *reinterpret_cast<const float4*>(part + m * kTileN + c);
               if (sw) tu[s0] = *reinterpret_cast<const float4*>(part + m * kTileN + c + 64);
             } else {
@@ -355,7 +362,7 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[q][j] = accu[q][j] = 0.0f;
 #pragma unroll
-        for (int s0 = 0; s0 < 8; s0++) {
+        for (int s0 = 0; s0 < (SPLIT ? 8 : 1); s0++) {
           if (u < nunits && s0 < a.splitk) {
             acc[q][0] += tg[s0].x; acc[q][1] += tg[s0].y; acc[q][2] += tg[s0].z; acc[q][3] += tg[s0].w;
             if (sw) {
@@ -497,8 +504,11 @@ cudaError_t launch_tc_linear(const TcCall& c, cudaStream_t s) {
   if ((reinterpret_cast<uintptr_t>(c.w) & 15) || (reinterpret_cast<uintptr_t>(c.x) & 15))
     return cudaErrorInvalidValue;
   TcPlan p = tc_plan(c.M, c.N, c.K, tc_num_sms(), c.max_splitk);
-  static SmemOptIn opt;  // dynamic smem opt-in per device (static smem is tiny)
-  if (cudaError_t e = opt.ensure((const void*)tc_linear_kernel, p.smem)) return e;
+  const bool sw = c.epi.act == 2, ksplit = p.splitk > 1;
+  auto kern = sw ? (ksplit ? tc_linear_kernel<true, true> : tc_linear_kernel<true, false>)
+                 : (ksplit ? tc_linear_kernel<false, true> : tc_linear_kernel<false, false>);
+  static SmemOptIn opts[4];  // dynamic smem opt-in per device and instance (static smem is tiny)
+  if (cudaError_t e = opts[(sw ? 2 : 0) + (ksplit ? 1 : 0)].ensure((const void*)kern, p.smem)) return e;
   CUtensorMap tmW, tmX;
   // distinct codes for the tensor-map failures (diagnostics)
   if (!encode_fn()) return cudaErrorNotSupported;
@@ -529,7 +539,7 @@ cudaError_t launch_tc_linear(const TcCall& c, cudaStream_t s) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, tc_linear_kernel, tmW, tmX, a);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmW, tmX, a);
     if (e != cudaSuccess) {
       (void)cudaGetLastError();
       return e;
