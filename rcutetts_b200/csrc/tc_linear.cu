@@ -474,12 +474,20 @@ TcPlan tc_plan(int M, int N, int K, int num_sms, int max_splitk) {
     return e ? std::max(1, atoi(e)) : 8;
   }();
   max_splitk = std::min(max_splitk, env_cap);
+  // a power of two, one CTA per SM; where that leaves the K unsplit (tiles
+  // beyond the SM count: a tile's epilogue then covers all its rows, e.g. 8
+  // rounds for the 96 tiles of the DiT's AdaLN projection), two CTAs per SM
+  // and a split of 2 when the tile's partial (MT x 128 floats) leaves room
+  // (a larger split of tiles that already split measured slower)
   const int ctas_per_split = p.ntiles * p.mtiles;
-  int sk = std::max(1, num_sms / ctas_per_split);
-  p.splitk = std::max(1, std::min(std::min(std::min(sk, p.kblocks), max_splitk), 8));
+  const int per_sm = (num_sms / ctas_per_split < 2 && p.MT <= 128) ? 2 : 1;
+  int sk = std::max(1, std::min(std::min(std::min(per_sm * num_sms / ctas_per_split, p.kblocks), max_splitk), 8));
+  while (sk & (sk - 1)) sk &= sk - 1;
+  p.splitk = sk;
   const int kb_per = (p.kblocks + p.splitk - 1) / p.splitk;
   const size_t stage = 16384 + (size_t)p.MT * 128;
-  const size_t budget = 200 * 1024;
+  // a grid beyond one CTA per SM keeps two CTAs per SM resident
+  const size_t budget = ctas_per_split * p.splitk > num_sms ? 100 * 1024 : 200 * 1024;
   p.stages = std::max(1, std::min(kb_per, (int)(budget / stage)));
   p.stages = std::min(p.stages, 8);
   size_t pipe = (size_t)p.stages * stage;
