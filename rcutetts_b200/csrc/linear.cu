@@ -190,14 +190,15 @@ __global__ void __launch_bounds__(kWarps * 32) linear_rows_kernel(const LinearAr
 // The form above splits K over the lanes and shuffle-reduces RPW x MT
 // accumulators per warp, which at such K leaves half the lanes idle and
 // runs a large unrolled body.  Here a thread owns one output column for MT
-// activation rows and walks K in order with fmaf from zero; the CTA's 128
-// weight rows are staged transposed in shared memory ([K][129], a warp
-// reads 32 consecutive columns) and its activation rows as [MT][K]
-// (broadcast reads).  grid (ceil(N / 128), ceil(M / MT)), 128 threads.
-constexpr int kSkCols = 128, kSkLd = kSkCols + 1;
-
-template <int MT, bool BF16>
-__global__ void __launch_bounds__(kSkCols) linear_smallk_kernel(const LinearArgs a) {
+// activation rows and walks K in order with fmaf from zero -- the same
+// order for every batch size, so a row's result does not depend on the
+// batch it runs in; the CTA's NC weight rows are staged transposed in
+// shared memory ([K][NC + 1], a warp reads 32 consecutive columns) and its
+// activation rows as [MT][K] (broadcast reads).  NC = 128 from 8 rows, 32
+// (one warp per CTA, more CTAs) below.  grid (ceil(N / NC), ceil(M / MT)).
+template <int MT, int NC, bool BF16>
+__global__ void __launch_bounds__(NC) linear_smallk_kernel(const LinearArgs a) {
+  constexpr int kSkCols = NC, kSkLd = NC + 1;
   extern __shared__ __align__(16) float sk[];
   const int K = a.K, K4 = K / 4;
   float* xs = sk;           // [MT][K]
@@ -334,20 +335,18 @@ int pick_mt(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
 // CTA, so the rows spread over the GPU instead of idling most warps of few CTAs
 int pick_mt(const LinearArgs& a) { return a.N <= 16 ? 1 : pick_mt(a.M); }
 
-// (from 8 activation rows: with fewer, the long-K form's 1-4 rows per CTA
-// spread the columns over more CTAs than 128-column tiles do)
 bool smallk(const LinearArgs& a) {
-  return a.act != 2 && !a.norm_w && !a.mod && a.K <= 128 && a.K % (a.w_bf16 ? 8 : 4) == 0 && a.M >= 8;
+  return a.act != 2 && !a.norm_w && !a.mod && a.K <= 128 && a.K % (a.w_bf16 ? 8 : 4) == 0;
 }
 
-template <int MT, bool BF16>
+template <int MT, int NC, bool BF16>
 cudaError_t launch_smallk_t(const LinearArgs& a, cudaStream_t s) {
-  const size_t smem = ((size_t)MT * a.K + (size_t)a.K * kSkLd) * sizeof(float);
+  const size_t smem = ((size_t)MT * a.K + (size_t)a.K * (NC + 1)) * sizeof(float);
   static SmemOptIn opt;
-  if (cudaError_t e = opt.ensure((const void*)linear_smallk_kernel<MT, BF16>, smem)) return e;
+  if (cudaError_t e = opt.ensure((const void*)linear_smallk_kernel<MT, NC, BF16>, smem)) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.N + kSkCols - 1) / kSkCols, (a.M + MT - 1) / MT);
-  cfg.blockDim = dim3(kSkCols);
+  cfg.gridDim = dim3((a.N + NC - 1) / NC, (a.M + MT - 1) / MT);
+  cfg.blockDim = dim3(NC);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -355,11 +354,21 @@ cudaError_t launch_smallk_t(const LinearArgs& a, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, linear_smallk_kernel<MT, BF16>, a);
+  return cudaLaunchKernelEx(&cfg, linear_smallk_kernel<MT, NC, BF16>, a);
+}
+
+template <bool BF16>
+cudaError_t launch_smallk_b(const LinearArgs& a, cudaStream_t s) {
+  switch (pick_mt(a.M)) {
+    case 1: return launch_smallk_t<1, 32, BF16>(a, s);
+    case 2: return launch_smallk_t<2, 32, BF16>(a, s);
+    case 4: return launch_smallk_t<4, 32, BF16>(a, s);
+    default: return launch_smallk_t<8, 128, BF16>(a, s);
+  }
 }
 
 cudaError_t launch_smallk(const LinearArgs& a, cudaStream_t s) {
-  return a.w_bf16 ? launch_smallk_t<8, true>(a, s) : launch_smallk_t<8, false>(a, s);
+  return a.w_bf16 ? launch_smallk_b<true>(a, s) : launch_smallk_b<false>(a, s);
 }
 
 int pick_rpw(const LinearArgs& a, int mt) {
@@ -389,7 +398,10 @@ cudaError_t dispatch_mt(const LinearArgs& a, cudaStream_t s) {
 }  // namespace
 
 int linear_grid_ctas(const LinearArgs& a) {
-  if (smallk(a)) return ((a.N + kSkCols - 1) / kSkCols) * ((a.M + 7) / 8);
+  if (smallk(a)) {
+    const int mt = pick_mt(a.M), nc = mt < 8 ? 32 : 128;
+    return ((a.N + nc - 1) / nc) * ((a.M + mt - 1) / mt);
+  }
   int mt = pick_mt(a);
   int rpw = pick_rpw(a, mt);
   return ((a.N + kWarps * rpw - 1) / (kWarps * rpw)) * ((a.M + mt - 1) / mt);
