@@ -873,6 +873,7 @@ void engine_destroy(ctts_engine* e) {
   if (e->h_noise) cudaFreeHost(e->h_noise);
   if (e->h_lat) cudaFreeHost(e->h_lat);
   if (e->h_stop) cudaFreeHost(e->h_stop);
+  if (e->h_err) cudaFreeHost(e->h_err);
   for (auto& g : e->groups) {
     if (g.kv) ctts_kv_free(g.kv);
     delete g.ws;
@@ -955,7 +956,8 @@ extern "C" int ctts_engine_create(ctts_lm* lm, ctts_dit* dit, const ctts_engine_
   e->noise = A.alloc<float>((size_t)B * PL);
   if (cudaMallocHost(&e->h_noise, sizeof(float) * B * PL) != cudaSuccess ||
       cudaMallocHost(&e->h_lat, sizeof(float) * B * PL) != cudaSuccess ||
-      cudaMallocHost(&e->h_stop, sizeof(float) * B * 2) != cudaSuccess || !e->noise) {
+      cudaMallocHost(&e->h_stop, sizeof(float) * B * 2) != cudaSuccess ||
+      cudaMallocHost(&e->h_err, sizeof(int) * 2 * e->groups.size()) != cudaSuccess || !e->noise) {
     engine_destroy(e);
     return set_error(CTTS_ERR_NOMEM, "engine buffers");
   }
@@ -1131,11 +1133,16 @@ extern "C" int ctts_engine_step(ctts_engine* e, const float* noise, float* laten
   CTTS_CK(cudaMemcpyAsync(e->h_lat, e->lat, sizeof(float) * B * PL, cudaMemcpyDeviceToHost, e->stream));
   if (stop_out)
     CTTS_CK(cudaMemcpyAsync(e->h_stop, e->stop, sizeof(float) * B * 2, cudaMemcpyDeviceToHost, e->stream));
+  // the groups' error words come back with the latents: one sync per step
+  for (size_t gi = 0; gi < e->groups.size(); gi++) {
+    CTTS_CK(cudaMemcpyAsync(e->h_err + 2 * gi, e->groups[gi].kv->err, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+    CTTS_CK(cudaMemcpyAsync(e->h_err + 2 * gi + 1, e->groups[gi].ws->err, sizeof(int), cudaMemcpyDeviceToHost,
+                            e->stream));
+  }
   CTTS_CK(cudaStreamSynchronize(e->stream));
-  for (auto& g : e->groups) {
-    int err = 0, derr = 0;
-    CTTS_CK(cudaMemcpy(&err, g.kv->err, sizeof(int), cudaMemcpyDeviceToHost));
-    CTTS_CK(cudaMemcpy(&derr, g.ws->err, sizeof(int), cudaMemcpyDeviceToHost));
+  for (size_t gi = 0; gi < e->groups.size(); gi++) {
+    EngineGroup& g = e->groups[gi];
+    const int err = e->h_err[2 * gi], derr = e->h_err[2 * gi + 1];
     if (err != 0) CTTS_CK(cudaMemset(g.kv->err, 0, sizeof(int)));
     if (derr != 0) CTTS_CK(cudaMemset(g.ws->err, 0, sizeof(int)));
     CTTS_REQ(err != 1, CTTS_ERR_RANGE, "device reported a KV position outside capacity");

@@ -126,6 +126,7 @@ struct ctts_engine {
   float *z = nullptr, *x = nullptr, *cond = nullptr, *lat = nullptr, *stop = nullptr,
         *fb = nullptr, *noise = nullptr;
   float *h_noise = nullptr, *h_lat = nullptr, *h_stop = nullptr;  // pinned staging
+  int* h_err = nullptr;  // pinned: each group's KV and DiT error words, read with the latents
   bool heads_set = false;
   bool cfg_on = false;  // classifier-free guidance: per-group rows [cond B | uncond B]
   std::vector<bool> prefilled, prefilled_u;
