@@ -31,11 +31,14 @@
 // the all-gathers end with the compute warps writing their own slice in
 // place and pushing it to the 15 peers with one bulk copy each
 // (cp.async.bulk shared::cta -> shared::cluster), completing on the peer's
-// mbarrier; row statistics, attention score partials, out_proj partials and
-// the new latent go the same way from small staging buffers.  The
-// reduce-scatter stages the partials of all 16 owners in the all-gathered
-// operand area (idle from the end of its GEMM until the peers' next push,
-// which needs these partials first) and pushes one 2 KB block per owner.  Every mbarrier is armed with its phase's byte count
+// mbarrier; the per-step out_proj partials and the new latent go the same
+// way from small staging buffers.  The other per-layer exchanges leave
+// straight from the compute threads' registers as remote stores that
+// complete on the receiver's mbarrier (st.async ... mbarrier::complete_tx),
+// a warp's 32 stores filling one contiguous span: each thread its row's
+// fp16 split-K partials into the 16 owners' partial blocks (the
+// reduce-scatter), warp 0 its row statistics and attention score partials.
+// Every mbarrier is armed with its phase's byte count
 // (arrive.expect_tx) by its waiter right after the previous phase
 // completed, which by the stage order is before any peer can push for that
 // phase; consecutive stages never share an mbarrier.  Stages that feed a
@@ -102,10 +105,8 @@ constexpr int kAdLd = 6 * kOwn + 4;  // 196: 16-byte rows, 2-way banks at most
 // fp32 area, float offsets from kF32 (exchange buffers 16-byte aligned)
 constexpr int oSEQ = 0;                          // [32][33] residual stream, own columns
 constexpr int oSSR = 1056;                       // [16][32] row sum-of-squares partials, by source CTA
-constexpr int oSSO = oSSR + kC * 32;             // [32] my partials (push source)
-constexpr int oSCR = oSSO + 32;                  // [2][32][3] attention score partials, by half
-constexpr int oSCO = oSCR + 2 * 32 * 3;          // [32][3] my partials
-constexpr int oVR = oSCO + 32 * 3;               // [16][10][4] out_proj partials of my 4 latent columns, by source
+constexpr int oSCR = oSSR + kC * 32;             // [2][3][32] attention score partials, by half, key token, row
+constexpr int oVR = oSCR + 2 * 32 * 3;           // [16][10][4] out_proj partials of my 4 latent columns, by source
 constexpr int oVRO = oVR + kC * kU * 4;          // [16][10][4] my partials, by owner
 constexpr int oXS = oVRO + kC * kU * 4;          // [16][10][4] latent x, by owner: x[u][4c+i]
 constexpr int oXO = oXS + kC * kU * 4;           // [10][4] my updated latent columns
@@ -124,7 +125,7 @@ __host__ __device__ constexpr int oPSC(int NL) { return oAD(NL) + 2 * kU * kAdLd
 __host__ __device__ constexpr int oPSS(int NL) { return oPSC(NL) + 4 * 32 * 3; }     // [4][32] row ss partials
 __host__ __device__ constexpr int f32_floats(int NL) { return oPSS(NL) + 4 * 32; }
 static_assert(oSSR >= 32 * kSeqLd && oSSR % 4 == 0 && oSCR % 4 == 0 && oVR % 4 == 0 && oXS % 4 == 0 &&
-                  oXO % 4 == 0 && oVRO % 4 == 0 && oSSO % 4 == 0 && oSCO % 4 == 0 && oNRM % 4 == 0,
+                  oXO % 4 == 0 && oVRO % 4 == 0 && oNRM % 4 == 0,
               "exchange buffers must be 16-byte aligned");
 
 // byte offsets of the bf16 tail tables and the barriers
@@ -146,7 +147,6 @@ __host__ __device__ inline Lay lay(int NL) {
 constexpr int bFULL = 0, bEMPTY = kSlots, bMMA = 2 * kSlots, bFIN = bMMA + 1, bA = bFIN + 1, bB = bA + 2,
               bAD = bB + 2, bRS = bAD + 1;
 static_assert(bRS < 16, "16 mbarrier slots");
-static_assert(kC * kPartBytes <= kATT - kXA, "reduce-scatter staging fits the all-gathered operand area");
 
 // Optional stage timeline (build with -DCTTS_DIT_TRACE): CTA 0 records
 // (event, %globaltimer) pairs of its compute warp (row 0) and MMA thread.
@@ -251,6 +251,21 @@ CTTS_DEV void push(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar, uin
           mapa_shared(dst, rank)),
       "r"(src), "r"(bytes), "r"(mapa_shared(bar, rank))
       : "memory");
+}
+// remote stores from registers into CTA `rank`'s shared memory at the same
+// offset, completing (their bytes) on that CTA's mbarrier at `bar`: they
+// leave straight from the thread, not through the CTA's bulk-copy queue
+CTTS_DEV void sta_v4(uint32_t dst, uint32_t x, uint32_t y, uint32_t z, uint32_t w, uint32_t bar, uint32_t rank) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   mapa_shared(dst, rank)),
+               "r"(x), "r"(y), "r"(z), "r"(w), "r"(mapa_shared(bar, rank))
+               : "memory");
+}
+CTTS_DEV void sta_f32(uint32_t dst, float v, uint32_t bar, uint32_t rank) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(
+                   mapa_shared(dst, rank)),
+               "r"(__float_as_uint(v)), "r"(mapa_shared(bar, rank))
+               : "memory");
 }
 CTTS_DEV void st_rc_u32(uint32_t a, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
@@ -576,17 +591,15 @@ __global__ void __launch_bounds__(kNT, 1)
       ok = cok[nsync & 1] != 0u;
       nsync++;
     };
-    // B stage (warp 0): staging writes visible to the bulk copies, lanes
-    // issue the pushes; then wait and re-arm for two stages later
-    auto pushB = [&](uint32_t src_off, uint32_t dst_off, uint32_t bytes, int ndst, bool pair) {
+    // B stage (warp 0) from a staging buffer: its writes visible to the
+    // bulk copies, lane d pushes to CTA d; then wait and re-arm for two
+    // stages later
+    auto pushB = [&](uint32_t src_off, uint32_t dst_off, uint32_t bytes) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       DTRACE(0, 7);
       const uint32_t bb = bar(bB + (int)(bph & 1));
-      if (lane < ndst) {
-        const uint32_t d = pair ? (uint32_t)(c ^ lane) : (uint32_t)lane;
-        push(sb + dst_off, sb + src_off, bytes, bb, d);
-      }
+      if (lane < kC) push(sb + dst_off, sb + src_off, bytes, bb, (uint32_t)lane);
     };
     auto waitB = [&]() {
       const uint32_t bb = bar(bB + (int)(bph & 1));
@@ -597,7 +610,9 @@ __global__ void __launch_bounds__(kNT, 1)
       DTRACE(0, 3);
     };
     // A stage (all compute warps): this CTA's slice, written in place by the
-    // four warps, to the 15 peers (warp 0 pushes)
+    // four warps, to the 15 peers (warp 0 pushes; a contiguous 2 KB block
+    // per peer as one bulk copy -- the slice's 64-byte row stride would
+    // scatter per-thread remote stores)
     auto postA = [&](uint32_t slice_addr, uint32_t bytes) {
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -620,6 +635,15 @@ __global__ void __launch_bounds__(kNT, 1)
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       if (cw == 0) DTRACE(0, 4);
     };
+    // warp 0: this CTA's partial of row r's sum of squares -> ssr[c][r] of
+    // every CTA (itself included), by remote stores
+    auto push_row_stat = [&](float v) {
+      DTRACE(0, 7);
+      const uint32_t bb = bar(bB + (int)(bph & 1));
+      const uint32_t dst = fb + (uint32_t)(oSSR + c * 32 + r) * 4u;
+#pragma unroll 4
+      for (int i = 0; i < kC; i++) sta_f32(dst, v, bb, (uint32_t)((c + i) & (kC - 1)));
+    };
     // the per-warp row partials pss[cw][r] summed in warp order -> every
     // CTA's ssr[c] (warp 0), then all warps see the 16 CTAs' sums
     auto ss_combine_push = [&]() {
@@ -627,8 +651,7 @@ __global__ void __launch_bounds__(kNT, 1)
       cbar();
       if (cw == 0) {
         DTRACE(0, 14);
-        F[oSSO + r] = ((pss[r] + pss[32 + r]) + pss[64 + r]) + pss[96 + r];
-        pushB(kF32 + oSSO * 4, kF32 + (oSSR + c * 32) * 4, 128, kC, false);
+        push_row_stat(((pss[r] + pss[32 + r]) + pss[64 + r]) + pss[96 + r]);
         waitB();
       }
       sync_ok();
@@ -661,22 +684,19 @@ __global__ void __launch_bounds__(kNT, 1)
     };
     // Split-K reduce-scatter.  The accumulator holds this CTA's partial of
     // all 512 outputs for its 32 rows; warp cw sends columns
-    // [128cw, 128cw + 128) -- owner CTAs 4cw..4cw+3 -- each lane its row,
-    // by remote stores into the owner's partial slot of this CTA
-    // ([8 column chunks][32 rows][4 floats]), then an arrive that releases
-    // them.  Warp 0 waits for all 16 x 32 arrivals of the phase.
+    // [128cw, 128cw + 128) -- owner CTAs 4cw..4cw+3 -- as fp16 (11-bit
+    // significand, 4x finer than the bf16 operands of these GEMMs), each
+    // lane its row, by remote stores into the owner's partial block of this
+    // CTA ([4 column chunks][32 rows][8 halves]) that complete on the
+    // owner's bRS.  Warp 0 waits for all 16 blocks of the phase.
     uint32_t rsph = 0;
     auto rs_exchange = [&]() {
-      // warp cw stages owners 4cw..4cw+3 as fp16 (11-bit significand, 4x
-      // finer than the bf16 operands of these GEMMs) into the staging area
-      // (the all-gathered norm operand, idle until the peers' next push,
-      // which needs these partials first); warp 0 pushes one 2 KB block per
-      // owner
       // 16-column halves through two register buffers: the TMEM load of
-      // half i + 1 is in flight while half i is converted and stored
+      // half i + 1 is in flight while half i is converted and sent
+      const uint32_t dst = sb + kPART + (uint32_t)c * kPartBytes + (uint32_t)r * 16u;
+      const uint32_t rb = bar(bRS);
       auto stage_half = [&](const uint32_t* v, int i) {
-        const int d = 4 * cw + (i >> 1);
-        uint8_t* stg = smem + kXA + (uint32_t)d * kPartBytes + (uint32_t)r * 16u;
+        const uint32_t d = (uint32_t)(4 * cw + (i >> 1));
 #pragma unroll
         for (int q = 0; q < 2; q++) {
           uint32_t h[4];
@@ -685,7 +705,7 @@ __global__ void __launch_bounds__(kNT, 1)
             const __half2 p2 = __floats2half2_rn(__uint_as_float(v[8 * q + 2 * e]), __uint_as_float(v[8 * q + 2 * e + 1]));
             h[e] = *reinterpret_cast<const uint32_t*>(&p2);
           }
-          st_u4(stg + (2 * (i & 1) + q) * 512, h[0], h[1], h[2], h[3]);
+          sta_v4(dst + (uint32_t)(2 * (i & 1) + q) * 512u, h[0], h[1], h[2], h[3], rb, d);
         }
       };
       auto half_addr = [&](int i) { return tmem + 32u * (uint32_t)(4 * cw + (i >> 1)) + 16u * (uint32_t)(i & 1); };
@@ -700,23 +720,10 @@ __global__ void __launch_bounds__(kNT, 1)
         if (i + 2 < 8) tmem_ld16_nowait(half_addr(i + 2), va);
         stage_half(vb, i + 1);
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      cbar();
       if (cw == 0) {
-        if (lane < kC) {
-          push(sb + kPART + (uint32_t)c * kPartBytes, sb + kXA + (uint32_t)lane * kPartBytes, kPartBytes, bar(bRS),
-               (uint32_t)lane);
-          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        }
-        __syncwarp();
         DTRACE(0, 9);
-        const uint32_t rb = bar(bRS);
         if (ok && !wait_cluster(rb, rsph & 1, abort)) ok = false;
         if (lane == 0) arm(rb, kC * kPartBytes);  // the next exchange's bytes
-        // the staging is rewritten by this CTA's next norm operand: every
-        // copy has read it (the peers' own writes to it come after they
-        // received these blocks)
-        if (lane < kC) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
         __syncwarp();
         DTRACE(0, 11);
       }
@@ -806,8 +813,7 @@ __global__ void __launch_bounds__(kNT, 1)
       float p = 0.0f;
 #pragma unroll 8
       for (int jj = 0; jj < kOwn; jj++) p = fmaf(seq[r * kSeqLd + jj], seq[r * kSeqLd + jj], p);
-      F[oSSO + r] = p;
-      pushB(kF32 + oSSO * 4, kF32 + (oSSR + c * 32) * 4, 128, kC, false);
+      push_row_stat(p);
       waitB();
     };
 
@@ -890,11 +896,18 @@ __global__ void __launch_bounds__(kNT, 1)
         }
         cbar();
         if (cw == 0) {
+          // my half-head score partials -> scr[c & 1] of this CTA and its
+          // partner (the other half of the head)
+          DTRACE(0, 7);
+          const uint32_t bb = bar(bB + (int)(bph & 1));
+          const uint32_t dst = fb + (uint32_t)(oSCR + (c & 1) * 96 + r) * 4u;
 #pragma unroll
-          for (int jt = 0; jt < 3; jt++)
-            F[oSCO + r * 3 + jt] = ((psc[r * 3 + jt] + psc[(32 + r) * 3 + jt]) + psc[(64 + r) * 3 + jt]) +
-                                   psc[(96 + r) * 3 + jt];
-          pushB(kF32 + oSCO * 4, kF32 + (oSCR + (c & 1) * 96) * 4, 384, 2, true);
+          for (int jt = 0; jt < 3; jt++) {
+            const float v = ((psc[r * 3 + jt] + psc[(32 + r) * 3 + jt]) + psc[(64 + r) * 3 + jt]) +
+                            psc[(96 + r) * 3 + jt];
+            sta_f32(dst + 128u * (uint32_t)jt, v, bb, (uint32_t)c);
+            sta_f32(dst + 128u * (uint32_t)jt, v, bb, (uint32_t)(c ^ 1));
+          }
           waitB();
         }
         sync_ok();
@@ -906,7 +919,7 @@ __global__ void __launch_bounds__(kNT, 1)
           const float scale = 1.0f / sqrtf((float)kHD);
 #pragma unroll
           for (int jt = 0; jt < 3; jt++) {
-            sc[jt] = (scr[r * 3 + jt] + scr[96 + r * 3 + jt]) * scale;
+            sc[jt] = (scr[jt * 32 + r] + scr[96 + jt * 32 + r]) * scale;
             m = fmaxf(m, sc[jt]);
           }
           float lsum = 0.0f;
@@ -1040,7 +1053,7 @@ __global__ void __launch_bounds__(kNT, 1)
             }
           }
           if (st + 1 < steps) {
-            pushB(kF32 + oXO * 4, kF32 + (oXS + c * kU * 4) * 4, kU * 16, kC, false);
+            pushB(kF32 + oXO * 4, kF32 + (oXS + c * kU * 4) * 4, kU * 16);
             waitB();
             // T3: the next step's sequence
             if (ok) fill(st + 1);
