@@ -668,16 +668,16 @@ __global__ void __launch_bounds__(kNT, 1)
       }
       sync_ok();
     };
-    auto row_inv = [&]() {
+    auto row_inv = [&](int row) {
       float ss = 0.0f;
 #pragma unroll
-      for (int q = 0; q < kC; q++) ss += ssr[q * 32 + r];
+      for (int q = 0; q < kC; q++) ss += ssr[q * 32 + row];
       return 1.0f / sqrtf(ss / (float)kH + eps);
     };
     // RMSNorm (+ AdaLN modulate) of own columns [8cw, 8cw+8) -> chunk cw of
     // my slice of the K=512 operand
     auto norm_slice = [&](const float* adb, int l, int which) {
-      const float inv = row_inv();
+      const float inv = row_inv(r);
       const float* nw = nrm + (l * 2 + which) * kOwn;
       const float* md = adb + min(u, kU - 1) * kAdLd + which * 3 * kOwn;  // shift, scale
       uint32_t pk[4];
@@ -796,40 +796,49 @@ __global__ void __launch_bounds__(kNT, 1)
     // seq rows of step stn: [mu + temb + dtemb; cond; in_proj(x)] (warp 0,
     // lane = column), then the rows' sums of squares to every CTA
     auto fill = [&](int stn) {
+      // all compute warps: lane = own column, warp cw the utterances cw,
+      // cw + 4, cw + 8; in_proj's dot products of a warp's utterances advance
+      // together (independent chains), each in latent order
       const int j = lane;
-      float acc[kU];
-#pragma unroll
-      for (int uu = 0; uu < kU; uu++) acc[uu] = 0.0f;
-      // in_proj: the utterances' dot products advance together (independent chains)
+      float acc[3] = {0.0f, 0.0f, 0.0f};
 #pragma unroll 4
       for (int i4 = 0; i4 < kL / 4; i4++) {
         float w4[4];
 #pragma unroll
         for (int e = 0; e < 4; e++) w4[e] = bf2f(inw_t[(4 * i4 + e) * kOwn + j]);
 #pragma unroll
-        for (int uu = 0; uu < kU; uu++) {
-          const float4 xv = *reinterpret_cast<const float4*>(&xs[(i4 * kU + uu) * 4]);
-          acc[uu] = fmaf(w4[0], xv.x, acc[uu]);
-          acc[uu] = fmaf(w4[1], xv.y, acc[uu]);
-          acc[uu] = fmaf(w4[2], xv.z, acc[uu]);
-          acc[uu] = fmaf(w4[3], xv.w, acc[uu]);
+        for (int k = 0; k < 3; k++) {
+          const int uu = cw + 4 * k;
+          if (uu < kU) {
+            const float4 xv = *reinterpret_cast<const float4*>(&xs[(i4 * kU + uu) * 4]);
+            acc[k] = fmaf(w4[0], xv.x, acc[k]);
+            acc[k] = fmaf(w4[1], xv.y, acc[k]);
+            acc[k] = fmaf(w4[2], xv.z, acc[k]);
+            acc[k] = fmaf(w4[3], xv.w, acc[k]);
+          }
         }
       }
 #pragma unroll
-      for (int uu = 0; uu < kU; uu++) {
-        seq[(3 * uu) * kSeqLd + j] = (F[oMU + uu * kOwn + j] + F[oTEMB + stn * kOwn + j]) + F[oDT + j];
-        seq[(3 * uu + 1) * kSeqLd + j] = F[oCH + uu * kOwn + j];
-        seq[(3 * uu + 2) * kSeqLd + j] = acc[uu] + F[oINB + j];
+      for (int k = 0; k < 3; k++) {
+        const int uu = cw + 4 * k;
+        if (uu < kU) {
+          seq[(3 * uu) * kSeqLd + j] = (F[oMU + uu * kOwn + j] + F[oTEMB + stn * kOwn + j]) + F[oDT + j];
+          seq[(3 * uu + 1) * kSeqLd + j] = F[oCH + uu * kOwn + j];
+          seq[(3 * uu + 2) * kSeqLd + j] = acc[k] + F[oINB + j];
+        }
       }
-      __syncwarp();
-      float p = 0.0f;
+      cbar();
+      // warp 0: the rows' sums of squares to every CTA
+      if (cw == 0) {
+        float p = 0.0f;
 #pragma unroll 8
-      for (int jj = 0; jj < kOwn; jj++) p = fmaf(seq[r * kSeqLd + jj], seq[r * kSeqLd + jj], p);
-      push_row_stat(p);
-      waitB();
+        for (int jj = 0; jj < kOwn; jj++) p = fmaf(seq[r * kSeqLd + jj], seq[r * kSeqLd + jj], p);
+        push_row_stat(p);
+        waitB();
+      }
     };
 
-    if (cw == 0) fill(0);
+    fill(0);
     sync_ok();
     for (int st = 0; st < steps && ok; st++) {
       for (int l = 0; l < NL && ok; l++) {
@@ -1010,39 +1019,39 @@ __global__ void __launch_bounds__(kNT, 1)
         ss_combine_push();
       }
       if (!ok) break;
-      if (cw == 0) {
-        // T1: final norm of the x rows, out_proj partial over the own columns,
-        // 4 latent columns to each owner CTA
-        if (rv && s == 2) {
-          const float inv = row_inv();
-#pragma unroll 8
-          for (int j = 0; j < kOwn; j++) xn[u * kOwn + j] = seq[r * kSeqLd + j] * inv * F[oFN + j];
-        }
-        __syncwarp();
-        {
-          float a0[kU], a1[kU];
+      // T1: final norm of the x rows (row 3u + 2 of utterance u; lane = own
+      // column, warp cw the utterances cw, cw + 4, cw + 8), then the out_proj
+      // partial over the own columns (warp cw latent outputs [16cw, 16cw+16),
+      // half-warp h utterances [5h, 5h+5), each sum in column order), 4
+      // latent columns to each owner CTA
 #pragma unroll
-          for (int uu = 0; uu < kU; uu++) a0[uu] = a1[uu] = 0.0f;
+      for (int k = 0; k < 3; k++) {
+        const int uu = cw + 4 * k;
+        if (uu < kU) {
+          const float inv = row_inv(3 * uu + 2);
+          xn[uu * kOwn + lane] = seq[(3 * uu + 2) * kSeqLd + lane] * inv * F[oFN + lane];
+        }
+      }
+      cbar();
+      {
+        const int o = 16 * cw + (lane & 15), u5 = 5 * (lane >> 4);
+        float ac[5];
+#pragma unroll
+        for (int k = 0; k < 5; k++) ac[k] = 0.0f;
 #pragma unroll 4
-          for (int j = 0; j < kOwn; j++) {
-            const float w0 = bf2f(outw_t[j * kL + lane]), w1 = bf2f(outw_t[j * kL + lane + 32]);
+        for (int j = 0; j < kOwn; j++) {
+          const float w = bf2f(outw_t[j * kL + o]);
 #pragma unroll
-            for (int uu = 0; uu < kU; uu++) {
-              const float xv = xn[uu * kOwn + j];
-              a0[uu] = fmaf(w0, xv, a0[uu]);
-              a1[uu] = fmaf(w1, xv, a1[uu]);
-            }
-          }
-          // owner of latent column o is CTA o/4; vro[owner][uu][o%4]
-#pragma unroll
-          for (int uu = 0; uu < kU; uu++) {
-            F[oVRO + ((lane >> 2) * kU + uu) * 4 + (lane & 3)] = a0[uu];
-            F[oVRO + (((lane + 32) >> 2) * kU + uu) * 4 + (lane & 3)] = a1[uu];
-          }
+          for (int k = 0; k < 5; k++) ac[k] = fmaf(w, xn[(u5 + k) * kOwn + j], ac[k]);
         }
+        // owner of latent column o is CTA o/4; vro[owner][uu][o%4]
+#pragma unroll
+        for (int k = 0; k < 5; k++) F[oVRO + ((o >> 2) * kU + u5 + k) * 4 + (o & 3)] = ac[k];
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      cbar();
+      if (cw == 0) {
         {
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          __syncwarp();
           const uint32_t bb = bar(bB + (int)(bph & 1));
           if (lane < kC)
             push(sb + kF32 + (oVR + c * kU * 4) * 4, sb + kF32 + (oVRO + lane * kU * 4) * 4, kU * 16, bb,
@@ -1066,12 +1075,15 @@ __global__ void __launch_bounds__(kNT, 1)
           if (st + 1 < steps) {
             pushB(kF32 + oXO * 4, kF32 + (oXS + c * kU * 4) * 4, kU * 16);
             waitB();
-            // T3: the next step's sequence
-            if (ok) fill(st + 1);
           }
         }
       }
       sync_ok();
+      if (ok && st + 1 < steps) {
+        // T3: the next step's sequence
+        fill(st + 1);
+        sync_ok();
+      }
     }
     if (cw == 0 && !ok) fail(3);
   }
